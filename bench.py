@@ -1,0 +1,323 @@
+"""Benchmark: one Qwen3-30B-A3B-shaped MoE layer decode step.
+
+A step = router GEMV + softmax/top-8/renorm + fused 4-bit (AFFINE-Q4) SwiGLU
+FFN of the 8 routed experts + weighted combine, batch 1, x bf16[2048] ->
+y bf16[2048], all through the C ABI (libsmoe_cuda.so).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+`value`: algorithmic HBM bytes of the layer step (router 524,288 + x 4,096 +
+8 experts x 2,654,208 + y 4,096 = 21,762,144 B) / device time, inputs
+resident. L2 is defeated by cycling through 8 distinct resident layers
+(8 x 340 MB) with a fresh x per step: each step's experts were last touched
+7 steps (>= 150 MB of other traffic) earlier. `e2e`: the same step with x
+copied from pinned host memory and y read back to the host inside the timed
+region. N > 1: every rank runs its own replica of the layer step (the layer
+is not sharded), timed as the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "s-moe_b200"))
+
+D, DFF, E, K = 2048, 768, 128, 8
+N_LAYERS = 8
+LAYER_BYTES = 524_288 + 4_096 + 8 * 2_654_208 + 4_096      # 21,762,144
+FFN_BYTES = 8 * 2_654_208                                    # 21,233,664
+METRIC = "expert-FFN HBM GB/s, Qwen3-30B-A3B MoE layer decode step, batch 1"
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clocks / throttle reasons during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_init(n_gpus):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=None)
+    return rank, world, local
+
+
+def max_over_ranks(v, world):
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ------------------------------------------------------------------ data
+def make_inputs(seed=1234):
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import oracle as O
+    layers = []
+    for l in range(N_LAYERS):
+        arena, stride, off = O.make_experts(O.FMT_AFFINE_Q4, E, D, DFF, seed=seed + l)
+        rw = O.normal_bf16(seed + l, 6, E * D, 0.0, 0.02)
+        layers.append((arena, stride, off, rw))
+    xs = np.stack([O.normal_bf16(seed + 7919 + i, 5, D) for i in range(64)])
+    return layers, xs
+
+
+# ------------------------------------------------------------ CPU legs
+def cpu_layer_time(layers, xs, budget_s, threads):
+    """Reference router (compiled sampler/top-k/matvec of the reference) +
+    the oracle's restated Q4 FFN (there is no reference CPU FFN) + combine."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import oracle as O
+    used = O.set_threads(threads)
+    R = O.ref()
+    n, t0 = 0, time.perf_counter()
+    while True:
+        arena, stride, off, rw = layers[n % len(layers)]
+        x = O.bf16_to_f32(xs[n % len(xs)])
+        if R is not None:
+            lg = np.empty(E, np.float32)
+            ids = np.zeros(K, np.uint32)
+            w = np.zeros(K, np.float32)
+            R.ref_route(x, rw, E, D, K, 1, lg, ids, w)
+            y = np.zeros(D, np.float32)
+            for j in range(K):
+                y = y + w[j] * O.expert_ffn(O.FMT_AFFINE_Q4, arena[ids[j]], D, DFF, x, precise=False)
+        else:
+            O.moe_layer(O.FMT_AFFINE_Q4, x, rw, arena, stride, E, D, DFF, K, precise=False)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    kind = "reference" if R is not None else "port"
+    return n, el, used, kind
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    layers, xs = make_inputs()
+    threads = os.cpu_count() or 1
+    n_total, el_total = 0, 0.0
+    for i in range(args.warmup):
+        cpu_layer_time(layers, xs, 0.0, threads)
+    for i in range(args.steps):
+        n, el, used, kind = cpu_layer_time(layers, xs, 2.0, threads)
+        n_total += n
+        el_total += el
+    gbs = LAYER_BYTES * n_total / el_total / 1e9
+    line = {"impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(1e3 * el_total / n_total, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config1: Qwen3-30B-A3B MoE layer (d 2048, 128 experts, top-8, "
+                                   "AFFINE-Q4 g64), batch 1", "layers_cycled": N_LAYERS},
+            "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": used, "kind": kind,
+                             "sample": f"{n_total} layer steps in {el_total:.1f} s: reference "
+                                       "router (sampler/top-k/matvec compiled from the reference) "
+                                       "+ restated Q4 FFN, OpenMP"},
+            "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# -------------------------------------------------------------- GPU arm
+def run_ours(args, rank, world, local):
+    import numpy as np
+    import torch
+    import smoe_cuda as S
+
+    torch.cuda.set_device(local)
+    layers, xs = make_inputs()
+    ctx = S.Context(local)
+    stream = torch.cuda.Stream()
+    ctx.set_stream(stream.cuda_stream)
+    descs, keep = [], []
+    for arena, stride, off, rw in layers:
+        da = torch.from_numpy(arena).cuda()
+        dr = torch.from_numpy(rw.view(np.int16)).cuda()
+        keep += [da, dr]
+        descs.append(S.make_layer(da, stride, off, E, D, DFF, S.FMT_AFFINE_Q4, dr))
+    d_x = torch.from_numpy(xs.view(np.int16)).cuda()          # [64, D] bf16
+    d_y = torch.zeros(D, dtype=torch.bfloat16, device="cuda")
+    ids = torch.zeros(K, dtype=torch.int32, device="cuda")
+    wts = torch.zeros(K, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+
+    def step(i, ev=None):
+        L = descs[i % N_LAYERS]
+        x = d_x[i % 64]
+        ctx.router_topk(L.router_w, x.data_ptr(), S.DTYPE_BF16, E, D, 1, K, True, ids, wts)
+        if ev is not None:
+            ev[0].record(stream)
+        ctx.moe_ffn(L, x.data_ptr(), S.DTYPE_BF16, ids, wts, K, 1, d_y, S.DTYPE_BF16)
+        if ev is not None:
+            ev[1].record(stream)
+
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    ctx.synchronize()
+
+    # ---- device-resident timing
+    clocks = Clocks(local)
+    clocks.start()
+    time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    d0 = ctx.dispatches()
+    ffn_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(args.steps):
+        step(1000 + i, ffn_ev[i])
+    t1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = t0.elapsed_time(t1)
+    launches = ctx.dispatches() - d0
+    ffn_ms = sum(a.elapsed_time(b) for a, b in ffn_ev) / args.steps
+    ck = clocks.stop()
+    ctx.synchronize()
+    ms = max_over_ranks(ms, world)
+    per_step = ms / args.steps
+    value = LAYER_BYTES * args.steps * world / (ms * 1e-3) / 1e9
+
+    # ---- end to end through the C ABI with host buffers
+    hx = torch.from_numpy(xs.view(np.int16)).pin_memory()
+    hy = torch.zeros(D, dtype=torch.bfloat16).pin_memory()
+    stage_x = torch.zeros(D, dtype=torch.bfloat16, device="cuda")
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    with torch.cuda.stream(stream):
+        for i in range(args.steps):
+            stage_x.view(torch.int16).copy_(hx[(2000 + i) % 64], non_blocking=True)
+            L = descs[(2000 + i) % N_LAYERS]
+            ctx.moe_layer(L, stage_x, S.DTYPE_BF16, 1, K, True, d_y, S.DTYPE_BF16)
+            hy.copy_(d_y, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ctx.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    e2e = LAYER_BYTES * args.steps * world / (e2e_ms * 1e-3) / 1e9
+
+    if rank == 0:
+        peak, peak_kind = peaks()
+        ach = FFN_BYTES / (ffn_ms * 1e-3) / 1e9
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded; BASELINE config-1 distributions)",
+            "config": {"workload": "config1: Qwen3-30B-A3B MoE layer (d 2048, 128 experts, "
+                                   "top-8, d_ff 768, AFFINE-Q4 g64), batch 1, bf16 in/out",
+                       "layers_cycled": N_LAYERS, "l2": "inputs larger than L2 (8 resident "
+                       "layers x 340 MB cycled, fresh x per step)",
+                       "parallelism": f"replicas x{world}"},
+            "layer_us": round(per_step * 1e3, 3),
+            "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(ach / peak, 4), "traffic": None,
+                         "kernel": "expert FFN (gate_up + down_combine), 21,233,664 B per launch "
+                                   f"pair, {ffn_ms * 1e3:.2f} us avg", "peak_kind": peak_kind},
+            "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": D * 2,
+                    "d2h_bytes_per_step": D * 2},
+            "gpu_launches": int(launches),
+            "clocks": ck,
+        }
+        if world == 1 and not args.no_cpu:
+            n, el, used, kind = cpu_layer_time(layers, xs, args.cpu_seconds, os.cpu_count() or 1)
+            line["cpu_baseline"] = {
+                "value": round(LAYER_BYTES * n / el / 1e9, 4), "unit": "GB/s", "cores": used,
+                "kind": kind, "sample": f"{n} layer steps in {el:.1f} s (reference router + "
+                                        "restated Q4 FFN, OpenMP)"}
+        print(json.dumps(line), flush=True)
+    ctx.close()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    rank, world, local = dist_init(args.gpus)
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+    else:
+        run_ours(args, rank, world, local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,216 @@
+/*
+ * smoe_cuda.h - C ABI of the B200 (sm_100a) decode hot path of S-MoE.
+ *
+ * Drop-in for the reference's compute interface src/compute/metal_bridge.h:
+ * every smoe_metal_X there has a smoe_cuda_X here with the same argument
+ * meaning (see smoe_cuda_compat.h for the name shim), plus native entries for
+ * the router (decode.cpp:280-303 -> scout.cpp:77-123, host code in the
+ * reference), the whole MoE layer and the token sampler (sampler.hpp:33-157,
+ * host code in the reference).
+ *
+ * Conventions
+ *   - Pure C, <stdint.h>/<stddef.h>/<stdbool.h> only; no CUDA types.
+ *   - Weight pointers are DEVICE pointers into a resident expert arena (the
+ *     reference passes unified-memory host pointers).
+ *   - Activation pointers of the mirrored entries may be host or device
+ *     memory (detected per call); the native entries take device pointers
+ *     and run asynchronously on the context's stream.
+ *   - int-returning entries give an SMOE_* status; pointer-returning mirrored
+ *     entries keep the reference's NULL-on-failure contract. The message of
+ *     the last failure is in smoe_cuda_last_error().
+ *   - One context per (thread, device). No allocation after init: all
+ *     scratch is sized by SmoeCudaInitArgs.
+ *   - Every host wait is bounded by timeout_ms and returns SMOE_ERR_TIMEOUT.
+ */
+#pragma once
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#include <stdbool.h>
+#include <stddef.h>
+#include <stdint.h>
+
+/* ---------------------------------------------------------------- status */
+#define SMOE_OK               0
+#define SMOE_ERR_ARG          1   /* bad argument / unsupported shape        */
+#define SMOE_ERR_CUDA         2   /* CUDA runtime error                      */
+#define SMOE_ERR_TIMEOUT      3   /* bounded host or device wait ran out     */
+#define SMOE_ERR_NCCL         4
+#define SMOE_ERR_DEVICE       5   /* a kernel raised its error flag          */
+#define SMOE_ERR_UNSUPPORTED  6
+
+/* ----------------------------------------------------------- formats */
+/* SMOE-Q4 (vault format, shatter_moe.py:331-387): w = (q - 7.5)/7.5 * s,
+ * fp16 s per group of 64, no bias. AFFINE-Q4: w = scale*q + bias, bf16 scale
+ * and bf16 bias per group of 64. Both: 2 codes per byte, LSB first,
+ * row-major, K (input dim) contiguous. */
+#define SMOE_FMT_SMOE_Q4   0
+#define SMOE_FMT_AFFINE_Q4 1
+
+#define SMOE_DTYPE_F32  0
+#define SMOE_DTYPE_BF16 1
+
+#define SMOE_MAX_ACTIVE        16     /* scout.hpp:32 MAX_ACTIVE            */
+#define SMOE_MAX_FFN_BATCH     64     /* metal_bridge.h:134                 */
+#define SMOE_MAX_FFN_BATCH_DIM 16384  /* metal_bridge.h:135                 */
+#define SMOE_MAX_TOP_K_SAMPLE  1024   /* main.cpp:323 TOP_K_PROTOCOL_CAP    */
+
+typedef struct SmoeCudaCtx SmoeCudaCtx;
+
+/* ------------------------------------------------------------ lifecycle */
+typedef struct {
+    int      device;        /* CUDA ordinal                                 */
+    uint32_t max_d_model;   /* 0 -> 8192                                    */
+    uint32_t max_d_ff;      /* 0 -> 4096                                    */
+    uint32_t max_experts;   /* router width, 0 -> 512                       */
+    uint32_t max_batch;     /* tokens per call, 0 -> 256                    */
+    uint32_t max_vocab;     /* sampler rows, 0 -> 262144                    */
+    uint32_t timeout_ms;    /* host waits, 0 -> 10000                       */
+} SmoeCudaInitArgs;
+
+/* Mirror of smoe_metal_init (metal_bridge.h:47): defaults, current device.
+ * slot_bytes is accepted for signature compatibility. NULL on failure. */
+SmoeCudaCtx* smoe_cuda_init(size_t slot_bytes);
+SmoeCudaCtx* smoe_cuda_init_ex(const SmoeCudaInitArgs* args);
+/* metal_bridge.h:50. NULL-safe. */
+void smoe_cuda_destroy(SmoeCudaCtx* ctx);
+/* Message of the last failure on this thread ("" if none). */
+const char* smoe_cuda_last_error(void);
+/* Run subsequent work on an external cudaStream_t (NULL -> own stream). */
+int smoe_cuda_set_stream(SmoeCudaCtx* ctx, void* cuda_stream);
+void* smoe_cuda_get_stream(SmoeCudaCtx* ctx);
+/* Bounded wait for all work on the context's stream; also reports a device
+ * error flag raised by any kernel since the previous call. */
+int smoe_cuda_synchronize(SmoeCudaCtx* ctx);
+
+/* ------------------------------------------------ mirrored FFN entries */
+/* metal_bridge.h:74-90. One expert, returns a wait handle (NULL on error).
+ * hidden_vec is accepted for compatibility; the context owns its scratch. */
+void* smoe_cuda_fused_ffn(SmoeCudaCtx* ctx,
+                          const uint8_t* packed_gate, const uint16_t* scales_gate,
+                          const uint8_t* packed_up, const uint16_t* scales_up,
+                          const uint8_t* packed_down, const uint16_t* scales_down,
+                          const float* input_vec, float* hidden_vec, float* output_vec,
+                          uint32_t gate_rows, uint32_t gate_cols,
+                          uint32_t down_rows, uint32_t down_cols,
+                          uint32_t group_size, uint32_t bits, uint32_t expert_index);
+
+/* metal_bridge.h:92. Waits for `handle` then copies slot `expert_index`'s
+ * output (cols floats) into output_vec (host or device). */
+void smoe_cuda_wait(SmoeCudaCtx* ctx, void* handle, float* output_vec,
+                    uint32_t expert_index, uint32_t cols);
+
+/* metal_bridge.h:106-114 */
+typedef struct {
+    const uint8_t*  packed_gate;
+    const uint16_t* scales_gate;
+    const uint8_t*  packed_up;
+    const uint16_t* scales_up;
+    const uint8_t*  packed_down;
+    const uint16_t* scales_down;
+    uint32_t        slot;
+} SmoeExpertBlob;
+
+/* metal_bridge.h:116-125. n_experts <= SMOE_MAX_ACTIVE same-shape SMOE-Q4
+ * experts on one input vector; fetch each with smoe_cuda_wait(slot). */
+void* smoe_cuda_fused_ffn_group(SmoeCudaCtx* ctx, const SmoeExpertBlob* experts,
+                                uint32_t n_experts, const float* input_vec,
+                                uint32_t gate_rows, uint32_t gate_cols,
+                                uint32_t down_rows, uint32_t down_cols,
+                                uint32_t group_size, uint32_t bits);
+
+/* metal_bridge.h:137-151. One expert over `batch` <= SMOE_MAX_FFN_BATCH rows
+ * of input_mat [batch x gate_cols]; NULL when batch/dims exceed the limits. */
+void* smoe_cuda_fused_ffn_batch(SmoeCudaCtx* ctx,
+                                const uint8_t* packed_gate, const uint16_t* scales_gate,
+                                const uint8_t* packed_up, const uint16_t* scales_up,
+                                const uint8_t* packed_down, const uint16_t* scales_down,
+                                const float* input_mat, uint32_t batch,
+                                uint32_t gate_rows, uint32_t gate_cols,
+                                uint32_t down_rows, uint32_t down_cols,
+                                uint32_t group_size, uint32_t bits);
+
+/* metal_bridge.h:153-154: out_mat [batch x cols] (host or device). */
+void smoe_cuda_wait_ffn_batch(SmoeCudaCtx* ctx, void* handle, float* out_mat,
+                              uint32_t batch, uint32_t cols);
+
+/* metal_bridge.h:157-162: bf16 W [rows x cols] . fp32 x, synchronous. */
+void smoe_cuda_scout_matvec_bf16(SmoeCudaCtx* ctx, const uint16_t* weight,
+                                 const float* input_vec, float* output_vec,
+                                 uint32_t rows, uint32_t cols);
+
+/* metal_bridge.h:221. Pins a host buffer (cudaHostRegister); device
+ * pointers are accepted and ignored. */
+void smoe_cuda_register_buffer(SmoeCudaCtx* ctx, const void* ptr, size_t size_in_bytes);
+
+/* metal_bridge.h:224. Number of kernels this context has launched. */
+uint64_t smoe_cuda_kernel_dispatches(const SmoeCudaCtx* ctx);
+
+/* ------------------------------------------------------ native entries */
+/* A layer's resident experts: expert e's blob at base + e * expert_stride,
+ * matrix m (0 gate [d_ff x d_model], 1 up, 2 down [d_model x d_ff]) with its
+ * nibbles / scales / biases at offsets off[3m+0..2] inside the blob
+ * (biases ignored for SMOE-Q4). All offsets and the stride 16-byte aligned. */
+typedef struct {
+    const uint8_t*  base;
+    uint64_t        expert_stride;
+    uint64_t        off[9];
+    uint32_t        n_experts;
+    uint32_t        d_model;
+    uint32_t        d_ff;
+    uint32_t        fmt;          /* SMOE_FMT_*                              */
+    const uint16_t* router_w;     /* bf16 [n_experts x d_model]              */
+} SmoeMoeLayer;
+
+/* Router of decode.cpp:280-303 for `batch` tokens: logits = W . x (bf16 W,
+ * fp32 accumulate), softmax over n_experts, top-k by probability (lowest
+ * index wins ties), renormalised over the k when norm_topk. Outputs (device):
+ * ids [batch x k] u32 in rank order, weights [batch x k] f32, logits
+ * [batch x n_experts] (optional, may be NULL). x: [batch x d_model]. */
+int smoe_cuda_router_topk(SmoeCudaCtx* ctx, const uint16_t* router_w, const void* x,
+                          int x_dtype, uint32_t n_experts, uint32_t d_model,
+                          uint32_t batch, uint32_t k, int norm_topk,
+                          uint32_t* ids, float* weights, float* logits);
+
+/* Expert FFN + weighted combine for `batch` tokens whose routing is already
+ * on the device (ids/weights [batch x k]): y[t] = sum_j w[t,j] * FFN_{ids[t,j]}(x[t])
+ * accumulated in rank order j = 0..k-1 (decode.cpp:485-499).
+ * y: [batch x d_model] in y_dtype. */
+int smoe_cuda_moe_ffn(SmoeCudaCtx* ctx, const SmoeMoeLayer* layer, const void* x,
+                      int x_dtype, const uint32_t* ids, const float* weights,
+                      uint32_t k, uint32_t batch, void* y, int y_dtype);
+
+/* Router + expert FFN + combine, all on the device. ids_out / w_out
+ * (optional, device, [batch x k]) receive the routing. */
+int smoe_cuda_moe_layer(SmoeCudaCtx* ctx, const SmoeMoeLayer* layer, const void* x,
+                        int x_dtype, uint32_t batch, uint32_t k, int norm_topk,
+                        void* y, int y_dtype, uint32_t* ids_out, float* w_out);
+
+/* ------------------------------------------------------------- sampler */
+/* One row of sampler state (sampler.hpp:11-17 SamplerConfig + the draw). */
+typedef struct {
+    float    temperature;   /* < 1e-4 -> greedy                             */
+    float    top_p;
+    uint32_t top_k;         /* 0..SMOE_MAX_TOP_K_SAMPLE                     */
+    float    rep_penalty;   /* 1.0 -> none                                  */
+    float    u;             /* generate_canonical<float,24> draw in [0,1)   */
+    uint32_t history_len;   /* entries of this row's history                */
+} SmoeSamplerRow;
+
+/* sampler.hpp:33-157 for `batch` rows. logits: device [batch x vocab] fp32,
+ * mutated in place by the repetition penalty exactly as the reference does.
+ * rows: device [batch]. history: device [batch x history_stride] u32.
+ * tokens: device [batch] u32. */
+int smoe_cuda_sample(SmoeCudaCtx* ctx, float* logits, uint32_t vocab, uint32_t batch,
+                     const SmoeSamplerRow* rows, const uint32_t* history,
+                     uint32_t history_stride, uint32_t* tokens);
+
+/* Host helper: the float libstdc++'s generate_canonical<float,24> makes of
+ * one 32-bit std::mt19937 word (what sample_token consumes per call). */
+float smoe_cuda_canonical_from_u32(uint32_t word);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif

@@ -1,0 +1,149 @@
+// router.cuh - exact router gate + softmax + top-k + renorm, and the plain
+// bf16 GEMV of metal_bridge.h:157 (sm_100a).
+//
+// Router (decode.cpp:280-303 -> common.hpp:294-306, scout.cpp:77-123):
+//   logits[e] = sum_j bf16(W[e,j]) * x[j]           fp32 accumulate
+//   p = softmax(logits)  (max-subtracted exp, index-order sum, * 1/sum)
+//   top-k by p, descending, lowest expert index wins ties
+//   w_j = p_j * (1 / sum_{rank order} p)   when norm_topk
+// One warp per expert row; the last CTA of a token (atomic ticket) finishes
+// the softmax/selection in one warp, so there is no second launch.
+#pragma once
+#include "smoe_common.cuh"
+
+namespace smoe {
+
+struct RouterArgs {
+    const uint16_t* w;        // [E x d] bf16
+    const void*     x;        // [batch x d]
+    int             x_dtype;
+    uint32_t        E, d, k;
+    int             norm;
+    float*          logits;   // [batch x E] (scratch or caller's)
+    uint32_t*       ids;      // [batch x k]
+    float*          wts;      // [batch x k]
+    uint32_t*       ticket;   // [batch] zero on entry, left zero on exit
+    uint32_t*       err;
+};
+
+constexpr int kRouterRowsPerCta = 8;
+constexpr int kRouterMaxE = 512;
+
+// Warp dot of one bf16 row with the smem fp32 vector (16-byte loads).
+SMOE_DEVINL float warp_row_dot_bf16(const uint16_t* row, const float* xs, int d, int lane) {
+    float acc = 0.f;
+    const uint4* rp = reinterpret_cast<const uint4*>(row);
+    for (int c = lane; c < d / 8; c += 32) {
+        const uint4 v = __ldg(rp + c);
+        const float* xv = xs + c * 8;
+        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            acc = fmaf(__uint_as_float(u[q] << 16), xv[2 * q], acc);
+            acc = fmaf(__uint_as_float(u[q] & 0xffff0000u), xv[2 * q + 1], acc);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    return acc;
+}
+
+template <typename T>
+SMOE_DEVINL void stage_vec(const void* src, int x_dtype, size_t off, int d, float* xs) {
+    if (x_dtype == 0) {
+        const float* s = static_cast<const float*>(src) + off;
+        for (int i = threadIdx.x; i < d; i += blockDim.x) xs[i] = s[i];
+    } else {
+        const uint16_t* s = static_cast<const uint16_t*>(src) + off;
+        for (int i = threadIdx.x; i < d; i += blockDim.x) xs[i] = bf16_bits_to_f32(s[i]);
+    }
+}
+
+// grid (ceil(E/8), batch), 256 threads, smem d floats + selection scratch.
+__global__ void __launch_bounds__(256) k_router(RouterArgs a) {
+    extern __shared__ __align__(16) float xs[];
+    __shared__ float ps[kRouterMaxE];
+    __shared__ uint32_t last_flag;
+    const int tok = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    stage_vec<float>(a.x, a.x_dtype, size_t(tok) * a.d, a.d, xs);
+    __syncthreads();
+    const int e = blockIdx.x * kRouterRowsPerCta + warp;
+    float* lg = a.logits + size_t(tok) * a.E;
+    if (e < (int)a.E) {
+        const float v = warp_row_dot_bf16(a.w + size_t(e) * a.d, xs, a.d, lane);
+        if (lane == 0) lg[e] = v;
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const uint32_t old = atomicAdd(a.ticket + tok, 1u);
+        last_flag = (old == gridDim.x - 1) ? 1u : 0u;
+    }
+    __syncthreads();
+    if (!last_flag) return;
+    __threadfence();
+    if (warp != 0) return;
+    // ---- last CTA, warp 0: softmax + top-k + renorm (scout.cpp:77-123)
+    const int E = a.E;
+    float mx = -INFINITY;
+    for (int i = lane; i < E; i += 32) {
+        const float v = __ldcg(lg + i);
+        ps[i] = v;
+        mx = fmaxf(mx, v);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    for (int i = lane; i < E; i += 32) ps[i] = expf(ps[i] - mx);
+    __syncwarp();
+    float se = 0.f;
+    if (lane == 0)
+        for (int i = 0; i < E; ++i) se += ps[i];       // index-order sum, as the reference
+    se = __shfl_sync(0xffffffffu, se, 0);
+    const float inv = se > 0.f ? 1.0f / se : 0.f;
+    for (int i = lane; i < E; i += 32) ps[i] *= inv;
+    __syncwarp();
+    const uint32_t k = a.k < (uint32_t)E ? a.k : (uint32_t)E;
+    float wsel = 0.f;
+    uint32_t idsel = 0;
+    for (uint32_t s = 0; s < k; ++s) {
+        float bv = -1.f;
+        int bi = 0x7fffffff;
+        for (int i = lane; i < E; i += 32) {
+            const float v = ps[i];
+            if (v > bv) { bv = v; bi = i; }          // ascending i: first max per lane
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+        }
+        if (lane == (int)s) { wsel = bv; idsel = bi; }
+        if (lane == 0) ps[bi] = -2.f;                 // removed
+        __syncwarp();
+    }
+    // renorm over the k in rank order (decode.cpp:296-303)
+    float ws = 0.f;
+    for (uint32_t s = 0; s < k; ++s) ws += __shfl_sync(0xffffffffu, wsel, s);
+    const float winv = (a.norm && ws > 0.f) ? 1.0f / ws : 1.0f;
+    if (lane < (int)k) {
+        a.ids[size_t(tok) * a.k + lane] = idsel;
+        a.wts[size_t(tok) * a.k + lane] = wsel * winv;
+    }
+    if (lane == 0) a.ticket[tok] = 0;                 // ready for the next call
+}
+
+// Plain bf16 GEMV y = W . x (metal_bridge.h:157), one warp per row.
+__global__ void __launch_bounds__(256) k_gemv_bf16(const uint16_t* w, const float* x, float* y,
+                                                   uint32_t rows, uint32_t cols) {
+    extern __shared__ __align__(16) float xs[];
+    for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x) xs[i] = x[i];
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (uint32_t r = blockIdx.x * 8 + warp; r < rows; r += gridDim.x * 8) {
+        const float v = warp_row_dot_bf16(w + size_t(r) * cols, xs, cols, lane);
+        if (lane == 0) y[r] = v;
+    }
+}
+
+}  // namespace smoe

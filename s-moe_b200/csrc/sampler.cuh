@@ -1,0 +1,342 @@
+// sampler.cuh - token sampler of sampler.hpp:33-157 on sm_100a.
+//
+// One thread-block cluster of 8 CTAs x 1024 threads per row; each CTA keeps
+// its eighth of the vocabulary in shared memory for all passes, and the
+// cluster exchanges partial results through distributed shared memory:
+//   1. repetition penalty over the last 256 history ids, each distinct
+//      non-exempt id once, in place (sampler.hpp:42-70), written back;
+//   2. greedy argmax when T < 1e-4, lowest index on ties (sampler.hpp:73-83);
+//   3. max, then sum of exp((s - max)/T) (sampler.hpp:86-129);
+//   4. top-K candidates by penalised score via a 4 x 8-bit radix select
+//      (K = max(top_k,1) <= 1024; the score order is the probability order),
+//      ties at the threshold taken lowest index first;
+//   5. CTA 0 sorts the K candidates (score desc, index asc), evaluates their
+//      probabilities with a double-precision exp rounded to float, and walks
+//      the top-p / top-k cutoff and the draw with the reference's float
+//      operations (sampler.hpp:132-156).
+#pragma once
+#include <cooperative_groups.h>
+#include "smoe_common.cuh"
+
+namespace smoe {
+namespace cg = cooperative_groups;
+
+struct SamplerRowDev {      // layout of SmoeSamplerRow
+    float temperature, top_p;
+    uint32_t top_k;
+    float rep_penalty, u;
+    uint32_t history_len;
+};
+
+struct SamplerArgs {
+    float* logits;
+    uint32_t V;
+    const SamplerRowDev* rows;
+    const uint32_t* hist;
+    uint32_t hstride;
+    uint32_t* tokens;
+};
+
+constexpr int kSampCluster = 8;
+constexpr int kSampThreads = 1024;
+constexpr int kSampCand = 1024;
+
+// exp(x) for x <= 0 in double: Cody-Waite reduction x = k ln2 + r with ln 2
+// split into a 32-significant-bit head and its remainder, |r| <= ln2/2, then
+// the Taylor series of e^r to degree 13 (truncation < 5e-18), scaled by 2^k.
+SMOE_DEVINL double exp_neg_d(double x) {
+    if (x < -745.0) return 0.0;
+    const double k = rint(x * 1.4426950408889634);
+    const double r = fma(-k, 1.9082149292705877e-10, fma(-k, 0.6931471803691238, x));
+    double p = 1.0 / 6227020800.0;                       // 1/13!
+    const double inv_fact[13] = {1.0 / 479001600.0, 1.0 / 39916800.0, 1.0 / 3628800.0,
+                                 1.0 / 362880.0, 1.0 / 40320.0, 1.0 / 5040.0, 1.0 / 720.0,
+                                 1.0 / 120.0, 1.0 / 24.0, 1.0 / 6.0, 0.5, 1.0, 1.0};
+#pragma unroll
+    for (int i = 0; i < 13; ++i) p = fma(p, r, inv_fact[i]);
+    return scalbn(p, int(k));
+}
+
+SMOE_DEVINL uint32_t score_key(float s) {
+    uint32_t u = __float_as_uint(s);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return 0u;        // NaN: never a candidate
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+SMOE_DEVINL float key_score(uint32_t k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+template <typename T, typename Op>
+SMOE_DEVINL T block_reduce(T v, T* red, Op op) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = op(v, __shfl_xor_sync(0xffffffffu, v, o));
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    v = red[0];
+    for (int i = 1; i < (int)(blockDim.x >> 5); ++i) v = op(v, red[i]);
+    return v;
+}
+
+// exclusive block scan of a u32 (1024 threads)
+SMOE_DEVINL uint32_t block_exscan(uint32_t v, uint32_t* red, uint32_t* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint32_t inc = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t t = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += t;
+    }
+    __syncthreads();
+    if (lane == 31) red[warp] = inc;
+    __syncthreads();
+    uint32_t base = 0, tot = 0;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) {
+        if (i < warp) base += red[i];
+        tot += red[i];
+    }
+    *total = tot;
+    return base + inc - v;
+}
+
+struct SampPub {            // per-CTA values read by the cluster
+    float fval;
+    uint32_t uidx;
+    double dsum;
+    uint32_t n_gt, n_eq;
+};
+
+__global__ void __cluster_dims__(kSampCluster, 1, 1) __launch_bounds__(kSampThreads, 1)
+k_sample(SamplerArgs a) {
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    __shared__ uint32_t hist[2][256];
+    __shared__ uint32_t tot[256];
+    __shared__ unsigned long long cand[kSampCand];
+    __shared__ float probs[kSampCand];
+    __shared__ float redf[32];
+    __shared__ double redd[32];
+    __shared__ uint32_t redu[32];
+    __shared__ SampPub pub;
+    __shared__ uint32_t sel_prefix, sel_krem;
+
+    cg::cluster_group cl = cg::this_cluster();
+    const int rank = (int)cl.block_rank();
+    const int tid = threadIdx.x;
+    const uint32_t row = blockIdx.y;
+    const SamplerRowDev P = a.rows[row];
+    const uint32_t V = a.V;
+    const uint32_t L = (((V + kSampCluster - 1) / kSampCluster) + 3u) & ~3u;
+    const uint32_t lo = min(V, rank * L);
+    const uint32_t n = min(V - lo, L);
+    float* s = reinterpret_cast<float*>(smem_raw);
+    float* lg = a.logits + size_t(row) * V;
+
+    for (uint32_t i = tid; i < n; i += kSampThreads) s[i] = lg[lo + i];
+    __syncthreads();
+
+    // ---- 1. repetition penalty (sampler.hpp:42-70)
+    if (P.rep_penalty != 1.0f) {
+        const uint32_t hl = P.history_len;
+        const uint32_t start = hl > 256u ? hl - 256u : 0u;
+        const uint32_t* h = a.hist + size_t(row) * a.hstride;
+        const uint32_t i = start + tid;
+        if (tid < 256 && i < hl) {
+            const uint32_t t = h[i];
+            bool skip = (t == 13 || t == 11 || t == 198 || t == 271 || t == 30 || t == 0 ||
+                         t == 151643 || t == 151645);
+            for (uint32_t j = start; j < i && !skip; ++j)
+                if (h[j] == t) skip = true;
+            if (!skip && t >= lo && t < lo + n) {
+                float v = s[t - lo];
+                v = (v <= 0.0f) ? __fmul_rn(v, P.rep_penalty) : __fdiv_rn(v, P.rep_penalty);
+                s[t - lo] = v;
+                lg[t] = v;
+            }
+        }
+        __syncthreads();
+    }
+
+    // ---- 2. greedy (sampler.hpp:73-83)
+    if (P.temperature < 1e-4f) {
+        float best = -1e38f;
+        uint32_t bi = 0xffffffffu;
+        for (uint32_t i = tid; i < n; i += kSampThreads)
+            if (s[i] > best) { best = s[i]; bi = lo + i; }
+        // (value, index): larger value, then smaller index
+        const int lane = tid & 31, warp = tid >> 5;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+            const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+        }
+        if (lane == 0) { redf[warp] = best; redu[warp] = bi; }
+        __syncthreads();
+        if (tid == 0) {
+            for (int w = 1; w < 32; ++w)
+                if (redf[w] > best || (redf[w] == best && redu[w] < bi)) { best = redf[w]; bi = redu[w]; }
+            pub.fval = best;
+            pub.uidx = bi;
+        }
+        cl.sync();
+        if (rank == 0 && tid == 0) {
+            for (int r = 1; r < kSampCluster; ++r) {
+                const SampPub* o = cl.map_shared_rank(&pub, r);
+                if (o->fval > best || (o->fval == best && o->uidx < bi)) { best = o->fval; bi = o->uidx; }
+            }
+            a.tokens[row] = (bi == 0xffffffffu) ? 0u : bi;
+        }
+        cl.sync();
+        return;
+    }
+
+    // ---- 3. max and softmax denominator
+    float mx = -INFINITY;
+    for (uint32_t i = tid; i < n; i += kSampThreads) mx = fmaxf(mx, s[i]);
+    mx = block_reduce(mx, redf, [](float x, float y) { return fmaxf(x, y); });
+    if (tid == 0) pub.fval = mx;
+    cl.sync();
+    mx = -INFINITY;
+    for (int r = 0; r < kSampCluster; ++r) mx = fmaxf(mx, cl.map_shared_rank(&pub, r)->fval);
+    {   // the reference's max starts from scores[0]: a NaN there poisons it
+        const float s0 = *cl.map_shared_rank(s, 0);
+        if (s0 != s0) mx = s0;
+    }
+    const float T = P.temperature;
+    double dsum = 0.0;
+    for (uint32_t i = tid; i < n; i += kSampThreads)
+        dsum += (double)expf(__fdiv_rn(__fsub_rn(s[i], mx), T));
+    dsum = block_reduce(dsum, redd, [](double x, double y) { return x + y; });
+    if (tid == 0) pub.dsum = dsum;
+
+    // ---- 4. radix select of the K-th largest score key
+    uint32_t K = P.top_k < 1u ? 1u : P.top_k;
+    if (K > (uint32_t)kSampCand) K = kSampCand;
+    if (K > V) K = V;
+    uint32_t prefix = 0, mask = 0, krem = K;
+    for (int pass = 0; pass < 4; ++pass) {
+        const int shift = 24 - 8 * pass;
+        uint32_t* hh = hist[pass & 1];
+        if (tid < 256) hh[tid] = 0;
+        __syncthreads();
+        for (uint32_t i = tid; i < n; i += kSampThreads) {
+            const uint32_t key = score_key(s[i]);
+            if ((key & mask) == prefix) atomicAdd(&hh[(key >> shift) & 255u], 1u);
+        }
+        cl.sync();
+        if (tid < 256) {
+            uint32_t t = 0;
+            for (int r = 0; r < kSampCluster; ++r) t += cl.map_shared_rank(hh, r)[tid];
+            tot[tid] = t;
+        }
+        __syncthreads();
+        if (tid == 0) {
+            uint32_t cum = 0;
+            int b = 255;
+            for (; b > 0; --b) {
+                if (cum + tot[b] >= krem) break;
+                cum += tot[b];
+            }
+            sel_krem = krem - cum;
+            sel_prefix = prefix | (uint32_t(b) << shift);
+        }
+        __syncthreads();
+        krem = sel_krem;
+        prefix = sel_prefix;
+        mask |= 255u << shift;
+    }
+    const uint32_t thr = prefix;   // key of the K-th largest; krem ties to take
+
+    // ---- collect candidates into CTA 0 (contiguous chunk per thread keeps
+    // the tie order = index order)
+    const uint32_t chunk = (n + kSampThreads - 1) / kSampThreads;
+    const uint32_t b0 = min(n, tid * chunk), b1 = min(n, b0 + chunk);
+    uint32_t ngt = 0, neq = 0;
+    for (uint32_t i = b0; i < b1; ++i) {
+        const uint32_t key = score_key(s[i]);
+        ngt += key > thr;
+        neq += key == thr;
+    }
+    uint32_t cta_gt, cta_eq;
+    const uint32_t off_gt = block_exscan(ngt, redu, &cta_gt);
+    const uint32_t off_eq = block_exscan(neq, redu, &cta_eq);
+    if (tid == 0) { pub.n_gt = cta_gt; pub.n_eq = cta_eq; }
+    cl.sync();
+    uint32_t all_gt = 0, gt_before = 0, eq_before = 0;
+    double total = 0.0;
+    for (int r = 0; r < kSampCluster; ++r) {
+        const SampPub* o = cl.map_shared_rank(&pub, r);
+        all_gt += o->n_gt;
+        total += o->dsum;
+        if (r < rank) { gt_before += o->n_gt; eq_before += o->n_eq; }
+    }
+    unsigned long long* cand0 = cl.map_shared_rank(cand, 0);
+    {
+        uint32_t pg = gt_before + off_gt, pe = eq_before + off_eq;
+        for (uint32_t i = b0; i < b1; ++i) {
+            const uint32_t key = score_key(s[i]);
+            const unsigned long long packed =
+                (static_cast<unsigned long long>(key) << 32) | (~(lo + i) & 0xffffffffu);
+            if (key > thr) cand0[pg++] = packed;
+            else if (key == thr) {
+                if (pe < krem) cand0[all_gt + pe] = packed;
+                ++pe;
+            }
+        }
+    }
+    cl.sync();
+    if (rank != 0) return;       // CTA 0's shared memory is no longer read remotely
+
+    // ---- 5. sort (score desc, index asc) and walk
+    uint32_t N2 = 1;
+    while (N2 < K) N2 <<= 1;
+    for (uint32_t i = K + tid; i < N2; i += kSampThreads) cand[i] = 0ull;
+    __syncthreads();
+    for (uint32_t size = 2; size <= N2; size <<= 1) {
+        for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
+            for (uint32_t i = tid; i < N2; i += kSampThreads) {
+                const uint32_t j = i ^ stride;
+                if (j > i) {
+                    const bool desc = (i & size) == 0;
+                    const unsigned long long x = cand[i], y = cand[j];
+                    if (desc ? (x < y) : (x > y)) { cand[i] = y; cand[j] = x; }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    const float sum_exp = (float)total;
+    const float inv_sum = 1.0f / sum_exp;
+    for (uint32_t i = tid; i < K; i += kSampThreads) {
+        const float sc = key_score(uint32_t(cand[i] >> 32));
+        const float arg = __fdiv_rn(__fsub_rn(sc, mx), T);
+        const float e = (float)exp_neg_d((double)arg);
+        probs[i] = __fmul_rn(e, inv_sum);
+    }
+    __syncthreads();
+    if (tid == 0) {
+        float cum = 0.0f;
+        uint32_t tl = 0;
+        for (uint32_t i = 0; i < K; ++i) {
+            cum = __fadd_rn(cum, probs[i]);
+            ++tl;
+            if (cum >= P.top_p || tl >= P.top_k) break;
+        }
+        const float rv = __fmul_rn(P.u, cum);
+        float run = 0.0f;
+        uint32_t tok = ~uint32_t(cand[tl - 1] & 0xffffffffu);
+        for (uint32_t i = 0; i < tl; ++i) {
+            run = __fadd_rn(run, probs[i]);
+            if (rv <= run) { tok = ~uint32_t(cand[i] & 0xffffffffu); break; }
+        }
+        a.tokens[row] = tok;
+    }
+}
+
+inline size_t sampler_smem_bytes(uint32_t V) {
+    const uint32_t L = (((V + kSampCluster - 1) / kSampCluster) + 3u) & ~3u;
+    return size_t(L) * 4;
+}
+
+}  // namespace smoe

@@ -1,0 +1,94 @@
+// smoe_common.cuh - PTX helpers shared by the sm_100a kernels.
+#pragma once
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#define SMOE_DEVINL __device__ __forceinline__
+
+// Device-side error codes written into the context's error word.
+enum : uint32_t {
+    SMOE_DEVERR_NONE = 0,
+    SMOE_DEVERR_MBAR_TIMEOUT = 1,   // a bulk copy never completed
+    SMOE_DEVERR_SPIN_TIMEOUT = 2,   // a cross-CTA wait ran out
+};
+
+// Bounded spins: ~2^24 polls with back-off is far beyond any legitimate wait
+// (a few microseconds) and far below a watchdog.
+#define SMOE_SPIN_LIMIT (1u << 24)
+
+SMOE_DEVINL uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+SMOE_DEVINL uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {
+    // (a & b) | c
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// D += A(16x16, f16, row) * B(16x8, f16, col), fp32 accumulate.
+SMOE_DEVINL void mma_f16_16816(float d[4], const uint32_t a[4], const uint32_t b[2]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+// ------------------------------------------------------------- mbarrier
+SMOE_DEVINL void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(smem_u32(bar)), "r"(count));
+}
+SMOE_DEVINL void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+SMOE_DEVINL void fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+SMOE_DEVINL void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+                 :: "r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+SMOE_DEVINL void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(smem_u32(bar)) : "memory");
+}
+SMOE_DEVINL bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+// Bounded wait; returns false (and the caller raises the error flag) when
+// the phase never completes.
+SMOE_DEVINL bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+    for (uint32_t i = 0; i < SMOE_SPIN_LIMIT; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (i > 64) __nanosleep(64);
+    }
+    return false;
+}
+
+// 1-D bulk copy global -> shared, completion counted on `bar` (bytes).
+// dst, src 16-byte aligned; bytes a multiple of 16. No multicast.
+SMOE_DEVINL void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+
+// ----------------------------------------------------------- conversions
+SMOE_DEVINL float bf16_bits_to_f32(uint16_t b) { return __uint_as_float(uint32_t(b) << 16); }
+SMOE_DEVINL float f16_bits_to_f32(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+
+SMOE_DEVINL uint32_t pack_half2(__half lo, __half hi) {
+    return uint32_t(__half_as_ushort(lo)) | (uint32_t(__half_as_ushort(hi)) << 16);
+}
+
+SMOE_DEVINL uint32_t ld_volatile_u32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.volatile.global.u32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}

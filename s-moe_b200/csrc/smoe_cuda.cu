@@ -1,0 +1,567 @@
+// smoe_cuda.cu - the C ABI of include/smoe_cuda.h: context, scratch,
+// launches and bounded waits. Kernels live in the *.cuh files.
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <chrono>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <thread>
+
+#include "../../include/smoe_cuda.h"
+#include "ffn_q4.cuh"
+#include "router.cuh"
+#include "sampler.cuh"
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+void set_err(const char* fmt, const char* a = "", long b = 0) {
+    std::snprintf(g_err, sizeof(g_err), fmt, a, b);
+}
+
+#define CK(call)                                                                      \
+    do {                                                                              \
+        cudaError_t e_ = (call);                                                      \
+        if (e_ != cudaSuccess) {                                                      \
+            set_err("CUDA error %s (line %ld)", cudaGetErrorString(e_), (long)__LINE__); \
+            return SMOE_ERR_CUDA;                                                     \
+        }                                                                             \
+    } while (0)
+
+constexpr int kEventRing = 64;
+
+}  // namespace
+
+struct SmoeCudaCtx {
+    int device = 0;
+    SmoeCudaInitArgs cfg{};
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;
+    // scratch (device)
+    float* hidden = nullptr;        // [max_batch * 16][max_d_ff]
+    float* slot_out = nullptr;      // [max(16, 64)][max_d_model]  mirror outputs
+    float* in_stage = nullptr;      // [64][max_d_model]           mirror inputs
+    float* batch_out = nullptr;     // [64][max_d_model]           token-batch outputs
+    float* logits = nullptr;        // [max_batch][max_experts]
+    uint32_t* ids = nullptr;        // [max_batch][16]
+    float* wts = nullptr;           // [max_batch][16]
+    uint32_t* ticket = nullptr;     // [max_batch]
+    uint32_t* err = nullptr;        // device error word
+    float* gemv_out = nullptr;      // staging for the mirrored matvec
+    float* gemv_in = nullptr;
+    size_t gemv_cap = 0;
+    // waits
+    cudaEvent_t events[kEventRing] = {};
+    uint64_t seq = 0;
+    std::atomic<uint64_t> dispatches{0};
+    size_t smem_optin = 0;
+};
+
+namespace {
+
+bool is_device_ptr(const void* p) {
+    cudaPointerAttributes at{};
+    if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged;
+}
+
+int check_device_err(SmoeCudaCtx* c) {
+    uint32_t e = 0;
+    CK(cudaMemcpyAsync(&e, c->err, 4, cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    if (e != 0) {
+        cudaMemsetAsync(c->err, 0, 4, c->stream);
+        set_err("device error flag %s%ld raised by a kernel", "", (long)e);
+        return SMOE_ERR_DEVICE;
+    }
+    return SMOE_OK;
+}
+
+int wait_event_bounded(SmoeCudaCtx* c, cudaEvent_t ev) {
+    auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        cudaError_t q = cudaEventQuery(ev);
+        if (q == cudaSuccess) return SMOE_OK;
+        if (q != cudaErrorNotReady) {
+            set_err("CUDA error %s while waiting (%ld)", cudaGetErrorString(q), 0);
+            return SMOE_ERR_CUDA;
+        }
+        auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
+                      std::chrono::steady_clock::now() - t0).count();
+        if (ms > (long)c->cfg.timeout_ms) {
+            set_err("wait timed out after %s%ld ms", "", (long)ms);
+            return SMOE_ERR_TIMEOUT;
+        }
+        std::this_thread::yield();
+    }
+}
+
+template <typename K>
+int prep_kernel(SmoeCudaCtx* c, K kern, size_t smem) {
+    if (smem > 48 * 1024) {
+        if (smem > c->smem_optin) {
+            set_err("kernel needs %s%ld bytes of shared memory", "", (long)smem);
+            return SMOE_ERR_ARG;
+        }
+        CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    }
+    return SMOE_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_ffn_dims(SmoeCudaCtx* c, uint32_t d, uint32_t dff) {
+    if (d == 0 || dff == 0 || d % 64 || dff % 64 || d > c->cfg.max_d_model || dff > c->cfg.max_d_ff) {
+        set_err("unsupported FFN dims (need multiples of 64 within the context limits) %s%ld", "",
+                (long)d);
+        return SMOE_ERR_ARG;
+    }
+    return SMOE_OK;
+}
+
+// Launch gate_up then down/combine for a prepared FfnArgs.
+int launch_ffn(SmoeCudaCtx* c, smoe::FfnArgs& a, int fmt) {
+    const uint32_t nslots = a.ntok * a.k;
+    if (nslots == 0) return SMOE_OK;
+    if (nslots > c->cfg.max_batch * 16u) {
+        set_err("too many (token, expert) slots %s%ld", "", (long)nslots);
+        return SMOE_ERR_ARG;
+    }
+    a.hidden = c->hidden;
+    a.err = c->err;
+    const size_t s1 = smoe::gate_up_smem_bytes(a.d_model), s2 = smoe::down_smem_bytes(a.d_ff);
+    int rc;
+    dim3 g1(a.d_ff / 16, nslots), g2(a.d_model / 16, a.ntok);
+    if (fmt == SMOE_FMT_AFFINE_Q4) {
+        if ((rc = prep_kernel(c, smoe::k_gate_up<smoe::kFmtAffine>, s1))) return rc;
+        if ((rc = prep_kernel(c, smoe::k_down_combine<smoe::kFmtAffine>, s2))) return rc;
+        smoe::k_gate_up<smoe::kFmtAffine><<<g1, 256, s1, c->stream>>>(a);
+        smoe::k_down_combine<smoe::kFmtAffine><<<g2, 256, s2, c->stream>>>(a);
+    } else {
+        if ((rc = prep_kernel(c, smoe::k_gate_up<smoe::kFmtSmoe>, s1))) return rc;
+        if ((rc = prep_kernel(c, smoe::k_down_combine<smoe::kFmtSmoe>, s2))) return rc;
+        smoe::k_gate_up<smoe::kFmtSmoe><<<g1, 256, s1, c->stream>>>(a);
+        smoe::k_down_combine<smoe::kFmtSmoe><<<g2, 256, s2, c->stream>>>(a);
+    }
+    CK(cudaGetLastError());
+    c->dispatches += 2;
+    return SMOE_OK;
+}
+
+void* record_handle(SmoeCudaCtx* c) {
+    const uint64_t s = ++c->seq;
+    if (cudaEventRecord(c->events[s % kEventRing], c->stream) != cudaSuccess) {
+        set_err("cudaEventRecord failed %s%ld", "", 0);
+        return nullptr;
+    }
+    return reinterpret_cast<void*>(static_cast<uintptr_t>(s));
+}
+
+int wait_handle(SmoeCudaCtx* c, void* h) {
+    const uint64_t s = reinterpret_cast<uintptr_t>(h);
+    if (s == 0 || s > c->seq || c->seq - s >= (uint64_t)kEventRing) {
+        set_err("stale or invalid wait handle %s%ld", "", (long)s);
+        return SMOE_ERR_ARG;
+    }
+    return wait_event_bounded(c, c->events[s % kEventRing]);
+}
+
+// Copy an activation the caller passed (host or device) into device memory.
+const float* stage_input(SmoeCudaCtx* c, const float* in, size_t n) {
+    if (is_device_ptr(in)) return in;
+    if (cudaMemcpyAsync(c->in_stage, in, n * 4, cudaMemcpyHostToDevice, c->stream) != cudaSuccess)
+        return nullptr;
+    return c->in_stage;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* smoe_cuda_last_error(void) { return g_err; }
+
+float smoe_cuda_canonical_from_u32(uint32_t w) {
+    float r = (float)w / 4294967296.0f;
+    if (r >= 1.0f) r = std::nextafter(1.0f, 0.0f);
+    return r;
+}
+
+SmoeCudaCtx* smoe_cuda_init_ex(const SmoeCudaInitArgs* args) {
+    SmoeCudaInitArgs a = args ? *args : SmoeCudaInitArgs{};
+    if (!args) cudaGetDevice(&a.device);
+    if (!a.max_d_model) a.max_d_model = 8192;
+    if (!a.max_d_ff) a.max_d_ff = 4096;
+    if (!a.max_experts) a.max_experts = 512;
+    if (!a.max_batch) a.max_batch = 256;
+    if (!a.max_vocab) a.max_vocab = 262144;
+    if (!a.timeout_ms) a.timeout_ms = 10000;
+    if (a.max_experts > (uint32_t)smoe::kRouterMaxE) {
+        set_err("max_experts above %s%ld", "", (long)smoe::kRouterMaxE);
+        return nullptr;
+    }
+    auto* c = new (std::nothrow) SmoeCudaCtx();
+    if (!c) return nullptr;
+    c->device = a.device;
+    c->cfg = a;
+    auto fail = [&](cudaError_t e) {
+        set_err("init failed: %s (%ld)", cudaGetErrorString(e), 0);
+        smoe_cuda_destroy(c);
+        return (SmoeCudaCtx*)nullptr;
+    };
+    cudaError_t e;
+    if ((e = cudaSetDevice(a.device)) != cudaSuccess) return fail(e);
+    int optin = 0;
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, a.device);
+    c->smem_optin = (size_t)optin;
+    if ((e = cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking)) != cudaSuccess) return fail(e);
+    c->stream = c->own_stream;
+    const size_t slots = size_t(a.max_batch) * 16;
+    if ((e = cudaMalloc(&c->hidden, slots * a.max_d_ff * 4)) != cudaSuccess) return fail(e);
+    if ((e = cudaMalloc(&c->slot_out, size_t(SMOE_MAX_FFN_BATCH) * a.max_d_model * 4)) != cudaSuccess) return fail(e);
+    if ((e = cudaMalloc(&c->batch_out, size_t(SMOE_MAX_FFN_BATCH) * a.max_d_model * 4)) != cudaSuccess) return fail(e);
+    if ((e = cudaMalloc(&c->in_stage, size_t(SMOE_MAX_FFN_BATCH) * a.max_d_model * 4)) != cudaSuccess) return fail(e);
+    if ((e = cudaMalloc(&c->logits, size_t(a.max_batch) * a.max_experts * 4)) != cudaSuccess) return fail(e);
+    if ((e = cudaMalloc(&c->ids, size_t(a.max_batch) * 16 * 4)) != cudaSuccess) return fail(e);
+    if ((e = cudaMalloc(&c->wts, size_t(a.max_batch) * 16 * 4)) != cudaSuccess) return fail(e);
+    if ((e = cudaMalloc(&c->ticket, size_t(a.max_batch) * 4)) != cudaSuccess) return fail(e);
+    if ((e = cudaMalloc(&c->err, 4)) != cudaSuccess) return fail(e);
+    c->gemv_cap = a.max_vocab > a.max_d_model ? a.max_vocab : a.max_d_model;
+    if ((e = cudaMalloc(&c->gemv_out, c->gemv_cap * 4)) != cudaSuccess) return fail(e);
+    if ((e = cudaMalloc(&c->gemv_in, size_t(a.max_d_model) * 4)) != cudaSuccess) return fail(e);
+    cudaMemsetAsync(c->ticket, 0, size_t(a.max_batch) * 4, c->stream);
+    cudaMemsetAsync(c->err, 0, 4, c->stream);
+    for (auto& ev : c->events)
+        if ((e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming)) != cudaSuccess) return fail(e);
+    if ((e = cudaStreamSynchronize(c->stream)) != cudaSuccess) return fail(e);
+    return c;
+}
+
+SmoeCudaCtx* smoe_cuda_init(size_t slot_bytes) {
+    (void)slot_bytes;
+    SmoeCudaInitArgs a{};
+    cudaGetDevice(&a.device);
+    return smoe_cuda_init_ex(&a);
+}
+
+void smoe_cuda_destroy(SmoeCudaCtx* c) {
+    if (!c) return;
+    cudaSetDevice(c->device);
+    if (c->own_stream) cudaStreamSynchronize(c->own_stream);
+    for (auto& ev : c->events)
+        if (ev) cudaEventDestroy(ev);
+    void* bufs[] = {c->hidden, c->slot_out, c->in_stage, c->batch_out, c->logits, c->ids,
+                    c->wts, c->ticket, c->err, c->gemv_out, c->gemv_in};
+    for (void* b : bufs)
+        if (b) cudaFree(b);
+    if (c->own_stream) cudaStreamDestroy(c->own_stream);
+    delete c;
+}
+
+int smoe_cuda_set_stream(SmoeCudaCtx* c, void* s) {
+    if (!c) return SMOE_ERR_ARG;
+    c->stream = s ? static_cast<cudaStream_t>(s) : c->own_stream;
+    return SMOE_OK;
+}
+
+void* smoe_cuda_get_stream(SmoeCudaCtx* c) { return c ? c->stream : nullptr; }
+
+int smoe_cuda_synchronize(SmoeCudaCtx* c) {
+    if (!c) return SMOE_ERR_ARG;
+    cudaEvent_t ev = c->events[(c->seq + 1) % kEventRing];
+    ++c->seq;
+    CK(cudaEventRecord(ev, c->stream));
+    int rc = wait_event_bounded(c, ev);
+    if (rc) return rc;
+    return check_device_err(c);
+}
+
+uint64_t smoe_cuda_kernel_dispatches(const SmoeCudaCtx* c) { return c ? c->dispatches.load() : 0; }
+
+void smoe_cuda_register_buffer(SmoeCudaCtx* c, const void* p, size_t n) {
+    if (!c || !p || !n || is_device_ptr(p)) return;
+    if (cudaHostRegister(const_cast<void*>(p), n, cudaHostRegisterDefault) != cudaSuccess)
+        cudaGetLastError();   // already registered or not registrable: copies still work
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------ mirrored entries
+namespace {
+
+// Pointer-mode FfnArgs for SMOE-Q4 expert column j.
+bool set_ptr_expert(smoe::FfnArgs& a, int j, const uint8_t* pg, const uint16_t* sg,
+                    const uint8_t* pu, const uint16_t* su, const uint8_t* pd, const uint16_t* sd) {
+    const void* ps[6] = {pg, sg, pu, su, pd, sd};
+    for (const void* p : ps)
+        if (!p || !aligned16(p)) return false;
+    a.p_nib[j][0] = pg; a.p_sc[j][0] = sg; a.p_bi[j][0] = sg;
+    a.p_nib[j][1] = pu; a.p_sc[j][1] = su; a.p_bi[j][1] = su;
+    a.p_nib[j][2] = pd; a.p_sc[j][2] = sd; a.p_bi[j][2] = sd;
+    return true;
+}
+
+int mirror_check(SmoeCudaCtx* c, uint32_t gate_rows, uint32_t gate_cols, uint32_t down_rows,
+                 uint32_t down_cols, uint32_t group_size, uint32_t bits) {
+    if (!c) { set_err("null context %s%ld", "", 0); return SMOE_ERR_ARG; }
+    if (bits != 4 || group_size != 64) {
+        set_err("only SMOE-Q4 with group 64 is implemented (bits %s%ld)", "", (long)bits);
+        return SMOE_ERR_UNSUPPORTED;
+    }
+    if (down_rows != gate_cols || down_cols != gate_rows) {
+        set_err("inconsistent FFN dims %s%ld", "", (long)down_rows);
+        return SMOE_ERR_ARG;
+    }
+    return check_ffn_dims(c, gate_cols, gate_rows);
+}
+
+}  // namespace
+
+extern "C" {
+
+void* smoe_cuda_fused_ffn(SmoeCudaCtx* c, const uint8_t* pg, const uint16_t* sg,
+                          const uint8_t* pu, const uint16_t* su, const uint8_t* pd,
+                          const uint16_t* sd, const float* input_vec, float* hidden_vec,
+                          float* output_vec, uint32_t gate_rows, uint32_t gate_cols,
+                          uint32_t down_rows, uint32_t down_cols, uint32_t group_size,
+                          uint32_t bits, uint32_t expert_index) {
+    (void)hidden_vec;
+    (void)output_vec;   // fetched by smoe_cuda_wait, as the reference does
+    SmoeExpertBlob b{pg, sg, pu, su, pd, sd, expert_index};
+    return smoe_cuda_fused_ffn_group(c, &b, 1, input_vec, gate_rows, gate_cols, down_rows,
+                                     down_cols, group_size, bits);
+}
+
+void* smoe_cuda_fused_ffn_group(SmoeCudaCtx* c, const SmoeExpertBlob* ex, uint32_t n,
+                                const float* input_vec, uint32_t gate_rows, uint32_t gate_cols,
+                                uint32_t down_rows, uint32_t down_cols, uint32_t group_size,
+                                uint32_t bits) {
+    if (mirror_check(c, gate_rows, gate_cols, down_rows, down_cols, group_size, bits)) return nullptr;
+    if (!ex || n == 0 || n > SMOE_MAX_ACTIVE) {
+        set_err("bad expert group size %s%ld", "", (long)n);
+        return nullptr;
+    }
+    smoe::FfnArgs a{};
+    // slots are laid out by column; the per-slot output goes to slot_out[slot]
+    // so the caller's `slot` numbering is honoured by a final scatter.
+    uint32_t maxslot = 0;
+    for (uint32_t j = 0; j < n; ++j) {
+        if (!set_ptr_expert(a, j, ex[j].packed_gate, ex[j].scales_gate, ex[j].packed_up,
+                            ex[j].scales_up, ex[j].packed_down, ex[j].scales_down)) {
+            set_err("null or unaligned expert pointer (expert %s%ld)", "", (long)j);
+            return nullptr;
+        }
+        if (ex[j].slot >= SMOE_MAX_FFN_BATCH - SMOE_MAX_ACTIVE) {
+            set_err("slot out of range %s%ld", "", (long)ex[j].slot);
+            return nullptr;
+        }
+        if (ex[j].slot > maxslot) maxslot = ex[j].slot;
+    }
+    const float* x = stage_input(c, input_vec, gate_cols);
+    if (!x) { set_err("input copy failed %s%ld", "", 0); return nullptr; }
+    a.x = x;
+    a.x_dtype = SMOE_DTYPE_F32;
+    a.per_slot = 1;
+    a.d_model = gate_cols;
+    a.d_ff = gate_rows;
+    a.k = n;
+    a.ntok = 1;
+    // kernel writes column j to slot_out + (64 - 16 + j) rows region, then we
+    // move each to the caller's slot (device-to-device, tiny).
+    float* tmp = c->slot_out + size_t(SMOE_MAX_FFN_BATCH - SMOE_MAX_ACTIVE) * c->cfg.max_d_model;
+    a.y = tmp;
+    // per-slot output rows are d_model apart
+    if (launch_ffn(c, a, SMOE_FMT_SMOE_Q4)) return nullptr;
+    for (uint32_t j = 0; j < n; ++j) {
+        if (cudaMemcpyAsync(c->slot_out + size_t(ex[j].slot) * c->cfg.max_d_model,
+                            tmp + size_t(j) * gate_cols, size_t(gate_cols) * 4,
+                            cudaMemcpyDeviceToDevice, c->stream) != cudaSuccess) {
+            set_err("slot scatter failed %s%ld", "", 0);
+            return nullptr;
+        }
+    }
+    return record_handle(c);
+}
+
+void smoe_cuda_wait(SmoeCudaCtx* c, void* h, float* out, uint32_t slot, uint32_t cols) {
+    if (!c || !out || slot >= SMOE_MAX_FFN_BATCH - SMOE_MAX_ACTIVE || cols > c->cfg.max_d_model) {
+        set_err("bad wait arguments %s%ld", "", (long)slot);
+        return;
+    }
+    if (wait_handle(c, h)) return;
+    if (cudaMemcpy(out, c->slot_out + size_t(slot) * c->cfg.max_d_model, size_t(cols) * 4,
+                   cudaMemcpyDefault) != cudaSuccess)
+        set_err("output copy failed %s%ld", "", 0);
+}
+
+void* smoe_cuda_fused_ffn_batch(SmoeCudaCtx* c, const uint8_t* pg, const uint16_t* sg,
+                                const uint8_t* pu, const uint16_t* su, const uint8_t* pd,
+                                const uint16_t* sd, const float* input_mat, uint32_t batch,
+                                uint32_t gate_rows, uint32_t gate_cols, uint32_t down_rows,
+                                uint32_t down_cols, uint32_t group_size, uint32_t bits) {
+    if (mirror_check(c, gate_rows, gate_cols, down_rows, down_cols, group_size, bits)) return nullptr;
+    if (batch == 0 || batch > SMOE_MAX_FFN_BATCH || gate_cols > SMOE_MAX_FFN_BATCH_DIM ||
+        gate_rows > SMOE_MAX_FFN_BATCH_DIM) {
+        set_err("batch/dims exceed the staging limits %s%ld", "", (long)batch);
+        return nullptr;
+    }
+    smoe::FfnArgs a{};
+    if (!set_ptr_expert(a, 0, pg, sg, pu, su, pd, sd)) {
+        set_err("null or unaligned expert pointer %s%ld", "", 0);
+        return nullptr;
+    }
+    const float* x = stage_input(c, input_mat, size_t(batch) * gate_cols);
+    if (!x) { set_err("input copy failed %s%ld", "", 0); return nullptr; }
+    a.x = x;
+    a.x_dtype = SMOE_DTYPE_F32;
+    a.per_slot = 1;
+    a.d_model = gate_cols;
+    a.d_ff = gate_rows;
+    a.k = 1;
+    a.ntok = batch;
+    a.y = c->batch_out;           // [batch x d_model], contiguous
+    if (launch_ffn(c, a, SMOE_FMT_SMOE_Q4)) return nullptr;
+    return record_handle(c);
+}
+
+void smoe_cuda_wait_ffn_batch(SmoeCudaCtx* c, void* h, float* out, uint32_t batch, uint32_t cols) {
+    if (!c || !out || batch > SMOE_MAX_FFN_BATCH || cols > c->cfg.max_d_model) {
+        set_err("bad wait arguments %s%ld", "", (long)batch);
+        return;
+    }
+    if (wait_handle(c, h)) return;
+    if (cudaMemcpy(out, c->batch_out, size_t(batch) * cols * 4, cudaMemcpyDefault) != cudaSuccess)
+        set_err("output copy failed %s%ld", "", 0);
+}
+
+void smoe_cuda_scout_matvec_bf16(SmoeCudaCtx* c, const uint16_t* w, const float* in, float* out,
+                                 uint32_t rows, uint32_t cols) {
+    if (!c || !w || !in || !out || cols % 8 || cols > c->cfg.max_d_model || !aligned16(w)) {
+        set_err("bad matvec arguments %s%ld", "", (long)cols);
+        return;
+    }
+    const bool out_dev = is_device_ptr(out);
+    if (!out_dev && rows > c->gemv_cap) {
+        set_err("matvec rows exceed staging %s%ld", "", (long)rows);
+        return;
+    }
+    const float* x = in;
+    if (!is_device_ptr(in)) {
+        if (cudaMemcpyAsync(c->gemv_in, in, size_t(cols) * 4, cudaMemcpyHostToDevice, c->stream)) return;
+        x = c->gemv_in;
+    }
+    float* y = out_dev ? out : c->gemv_out;
+    const uint32_t blocks = (rows + 7) / 8 < 148u * 8u ? (rows + 7) / 8 : 148u * 8u;
+    const size_t smem = size_t(cols) * 4;
+    if (prep_kernel(c, smoe::k_gemv_bf16, smem)) return;
+    smoe::k_gemv_bf16<<<blocks, 256, smem, c->stream>>>(w, x, y, rows, cols);
+    c->dispatches += 1;
+    if (!out_dev)
+        cudaMemcpyAsync(out, y, size_t(rows) * 4, cudaMemcpyDeviceToHost, c->stream);
+    smoe_cuda_synchronize(c);   // synchronous, as metal_bridge.h:157
+}
+
+// ------------------------------------------------------- native entries
+int smoe_cuda_router_topk(SmoeCudaCtx* c, const uint16_t* w, const void* x, int x_dtype,
+                          uint32_t E, uint32_t d, uint32_t batch, uint32_t k, int norm,
+                          uint32_t* ids, float* wts, float* logits) {
+    if (!c || !w || !x || !ids || !wts) { set_err("null argument %s%ld", "", 0); return SMOE_ERR_ARG; }
+    if (E == 0 || E > c->cfg.max_experts || d % 8 || d > c->cfg.max_d_model || k == 0 ||
+        k > SMOE_MAX_ACTIVE || k > E || batch == 0 || batch > c->cfg.max_batch ||
+        (x_dtype != 0 && x_dtype != 1) || !aligned16(w)) {
+        set_err("bad router arguments %s%ld", "", (long)E);
+        return SMOE_ERR_ARG;
+    }
+    smoe::RouterArgs a{w, x, x_dtype, E, d, k, norm, logits ? logits : c->logits, ids, wts,
+                       c->ticket, c->err};
+    const size_t smem = size_t(d) * 4;
+    int rc = prep_kernel(c, smoe::k_router, smem);
+    if (rc) return rc;
+    dim3 g((E + smoe::kRouterRowsPerCta - 1) / smoe::kRouterRowsPerCta, batch);
+    smoe::k_router<<<g, 256, smem, c->stream>>>(a);
+    CK(cudaGetLastError());
+    c->dispatches += 1;
+    return SMOE_OK;
+}
+
+static int layer_args(SmoeCudaCtx* c, const SmoeMoeLayer* L, smoe::FfnArgs& a) {
+    if (!L || !L->base || (L->fmt != SMOE_FMT_SMOE_Q4 && L->fmt != SMOE_FMT_AFFINE_Q4) ||
+        L->expert_stride % 16 || !aligned16(L->base)) {
+        set_err("bad layer descriptor %s%ld", "", 0);
+        return SMOE_ERR_ARG;
+    }
+    for (int i = 0; i < 9; ++i)
+        if (L->off[i] % 16) { set_err("unaligned blob offset %s%ld", "", (long)i); return SMOE_ERR_ARG; }
+    int rc = check_ffn_dims(c, L->d_model, L->d_ff);
+    if (rc) return rc;
+    a.base = L->base;
+    a.stride = L->expert_stride;
+    for (int i = 0; i < 9; ++i) a.off[i] = L->off[i];
+    a.d_model = L->d_model;
+    a.d_ff = L->d_ff;
+    return SMOE_OK;
+}
+
+int smoe_cuda_moe_ffn(SmoeCudaCtx* c, const SmoeMoeLayer* L, const void* x, int x_dtype,
+                      const uint32_t* ids, const float* wts, uint32_t k, uint32_t batch,
+                      void* y, int y_dtype) {
+    if (!c || !x || !ids || !wts || !y) { set_err("null argument %s%ld", "", 0); return SMOE_ERR_ARG; }
+    smoe::FfnArgs a{};
+    int rc = layer_args(c, L, a);
+    if (rc) return rc;
+    if (k == 0 || k > SMOE_MAX_ACTIVE || batch == 0 || batch > c->cfg.max_batch ||
+        (x_dtype != 0 && x_dtype != 1) || (y_dtype != 0 && y_dtype != 1)) {
+        set_err("bad moe_ffn arguments %s%ld", "", (long)k);
+        return SMOE_ERR_ARG;
+    }
+    a.ids = ids;
+    a.wts = wts;
+    a.x = x;
+    a.x_dtype = x_dtype;
+    a.y = y;
+    a.y_dtype = y_dtype;
+    a.per_slot = 0;
+    a.k = k;
+    a.ntok = batch;
+    return launch_ffn(c, a, (int)L->fmt);
+}
+
+int smoe_cuda_moe_layer(SmoeCudaCtx* c, const SmoeMoeLayer* L, const void* x, int x_dtype,
+                        uint32_t batch, uint32_t k, int norm, void* y, int y_dtype,
+                        uint32_t* ids_out, float* w_out) {
+    if (!c || !L) { set_err("null argument %s%ld", "", 0); return SMOE_ERR_ARG; }
+    uint32_t* ids = ids_out ? ids_out : c->ids;
+    float* wts = w_out ? w_out : c->wts;
+    int rc = smoe_cuda_router_topk(c, L->router_w, x, x_dtype, L->n_experts, L->d_model, batch,
+                                   k, norm, ids, wts, nullptr);
+    if (rc) return rc;
+    return smoe_cuda_moe_ffn(c, L, x, x_dtype, ids, wts, k, batch, y, y_dtype);
+}
+
+int smoe_cuda_sample(SmoeCudaCtx* c, float* logits, uint32_t vocab, uint32_t batch,
+                     const SmoeSamplerRow* rows, const uint32_t* history, uint32_t hstride,
+                     uint32_t* tokens) {
+    if (!c || !logits || !rows || !tokens || vocab == 0 || vocab > c->cfg.max_vocab || batch == 0 ||
+        batch > 65535u || (hstride && !history)) {
+        set_err("bad sampler arguments %s%ld", "", (long)vocab);
+        return SMOE_ERR_ARG;
+    }
+    static_assert(sizeof(SmoeSamplerRow) == sizeof(smoe::SamplerRowDev), "row layout");
+    smoe::SamplerArgs a{logits, vocab, reinterpret_cast<const smoe::SamplerRowDev*>(rows),
+                        history, hstride, tokens};
+    const size_t smem = smoe::sampler_smem_bytes(vocab);
+    int rc = prep_kernel(c, smoe::k_sample, smem);
+    if (rc) return rc;
+    dim3 g(smoe::kSampCluster, batch);
+    smoe::k_sample<<<g, smoe::kSampThreads, smem, c->stream>>>(a);
+    CK(cudaGetLastError());
+    c->dispatches += 1;
+    return SMOE_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,238 @@
+"""Python host binding of the C ABI in include/smoe_cuda.h (ctypes).
+
+Mirrors the reference's compute interface (src/compute/metal_bridge.h) name
+for name with the ``smoe_cuda_`` prefix, plus the native router / MoE-layer /
+sampler entries. Device buffers are passed as integer addresses or as
+objects with ``data_ptr()`` (torch tensors). There is no CPU fallback: if
+libsmoe_cuda.so is missing or no GPU is present, calls raise.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libsmoe_cuda.so")
+
+SMOE_OK = 0
+STATUS = {0: "OK", 1: "ERR_ARG", 2: "ERR_CUDA", 3: "ERR_TIMEOUT", 4: "ERR_NCCL",
+          5: "ERR_DEVICE", 6: "ERR_UNSUPPORTED"}
+FMT_SMOE_Q4 = 0
+FMT_AFFINE_Q4 = 1
+DTYPE_F32 = 0
+DTYPE_BF16 = 1
+MAX_ACTIVE = 16
+MAX_FFN_BATCH = 64
+
+# Every symbol include/smoe_cuda.h declares (checked by the CPU tests).
+EXPORTS = [
+    "smoe_cuda_init", "smoe_cuda_init_ex", "smoe_cuda_destroy", "smoe_cuda_last_error",
+    "smoe_cuda_set_stream", "smoe_cuda_get_stream", "smoe_cuda_synchronize",
+    "smoe_cuda_fused_ffn", "smoe_cuda_wait", "smoe_cuda_fused_ffn_group",
+    "smoe_cuda_fused_ffn_batch", "smoe_cuda_wait_ffn_batch", "smoe_cuda_scout_matvec_bf16",
+    "smoe_cuda_register_buffer", "smoe_cuda_kernel_dispatches", "smoe_cuda_router_topk",
+    "smoe_cuda_moe_ffn", "smoe_cuda_moe_layer", "smoe_cuda_sample",
+    "smoe_cuda_canonical_from_u32",
+]
+
+
+class SmoeCudaError(RuntimeError):
+    pass
+
+
+class InitArgs(C.Structure):
+    _fields_ = [("device", C.c_int), ("max_d_model", C.c_uint32), ("max_d_ff", C.c_uint32),
+                ("max_experts", C.c_uint32), ("max_batch", C.c_uint32),
+                ("max_vocab", C.c_uint32), ("timeout_ms", C.c_uint32)]
+
+
+class ExpertBlob(C.Structure):
+    _fields_ = [("packed_gate", C.c_void_p), ("scales_gate", C.c_void_p),
+                ("packed_up", C.c_void_p), ("scales_up", C.c_void_p),
+                ("packed_down", C.c_void_p), ("scales_down", C.c_void_p),
+                ("slot", C.c_uint32)]
+
+
+class MoeLayer(C.Structure):
+    _fields_ = [("base", C.c_void_p), ("expert_stride", C.c_uint64), ("off", C.c_uint64 * 9),
+                ("n_experts", C.c_uint32), ("d_model", C.c_uint32), ("d_ff", C.c_uint32),
+                ("fmt", C.c_uint32), ("router_w", C.c_void_p)]
+
+
+class SamplerRow(C.Structure):
+    _fields_ = [("temperature", C.c_float), ("top_p", C.c_float), ("top_k", C.c_uint32),
+                ("rep_penalty", C.c_float), ("u", C.c_float), ("history_len", C.c_uint32)]
+
+
+_lib = None
+
+
+def lib():
+    """Load libsmoe_cuda.so (raises if it was not built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise SmoeCudaError(f"{LIB_PATH} not built (python s-moe_b200/build.py)")
+        L = C.CDLL(LIB_PATH)
+        vp, u32, u64, i32, f32 = C.c_void_p, C.c_uint32, C.c_uint64, C.c_int, C.c_float
+        L.smoe_cuda_init.argtypes = [C.c_size_t]
+        L.smoe_cuda_init.restype = vp
+        L.smoe_cuda_init_ex.argtypes = [C.POINTER(InitArgs)]
+        L.smoe_cuda_init_ex.restype = vp
+        L.smoe_cuda_destroy.argtypes = [vp]
+        L.smoe_cuda_last_error.restype = C.c_char_p
+        L.smoe_cuda_set_stream.argtypes = [vp, vp]
+        L.smoe_cuda_get_stream.argtypes = [vp]
+        L.smoe_cuda_get_stream.restype = vp
+        L.smoe_cuda_synchronize.argtypes = [vp]
+        L.smoe_cuda_fused_ffn.argtypes = [vp] * 10 + [u32] * 7
+        L.smoe_cuda_fused_ffn.restype = vp
+        L.smoe_cuda_wait.argtypes = [vp, vp, vp, u32, u32]
+        L.smoe_cuda_fused_ffn_group.argtypes = [vp, C.POINTER(ExpertBlob), u32, vp] + [u32] * 6
+        L.smoe_cuda_fused_ffn_group.restype = vp
+        L.smoe_cuda_fused_ffn_batch.argtypes = [vp] * 8 + [u32] * 7
+        L.smoe_cuda_fused_ffn_batch.restype = vp
+        L.smoe_cuda_wait_ffn_batch.argtypes = [vp, vp, vp, u32, u32]
+        L.smoe_cuda_scout_matvec_bf16.argtypes = [vp, vp, vp, vp, u32, u32]
+        L.smoe_cuda_register_buffer.argtypes = [vp, vp, C.c_size_t]
+        L.smoe_cuda_kernel_dispatches.argtypes = [vp]
+        L.smoe_cuda_kernel_dispatches.restype = u64
+        L.smoe_cuda_router_topk.argtypes = [vp, vp, vp, i32, u32, u32, u32, u32, i32, vp, vp, vp]
+        L.smoe_cuda_moe_ffn.argtypes = [vp, C.POINTER(MoeLayer), vp, i32, vp, vp, u32, u32, vp, i32]
+        L.smoe_cuda_moe_layer.argtypes = [vp, C.POINTER(MoeLayer), vp, i32, u32, u32, i32, vp,
+                                          i32, vp, vp]
+        L.smoe_cuda_sample.argtypes = [vp, vp, u32, u32, vp, vp, u32, vp]
+        L.smoe_cuda_canonical_from_u32.argtypes = [u32]
+        L.smoe_cuda_canonical_from_u32.restype = f32
+        _lib = L
+    return _lib
+
+
+def ptr(x) -> int | None:
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    if hasattr(x, "data_ptr"):
+        return x.data_ptr()
+    if hasattr(x, "ctypes"):          # numpy (host memory)
+        return x.ctypes.data
+    raise TypeError(f"cannot take the address of {type(x)}")
+
+
+def last_error() -> str:
+    return lib().smoe_cuda_last_error().decode()
+
+
+def check(rc: int, what: str = "") -> None:
+    if rc != SMOE_OK:
+        raise SmoeCudaError(f"{what}: {STATUS.get(rc, rc)}: {last_error()}")
+
+
+def canonical_from_u32(word: int) -> float:
+    return float(lib().smoe_cuda_canonical_from_u32(word))
+
+
+class Context:
+    """One smoe_cuda context (scratch, stream, event ring) on one device."""
+
+    def __init__(self, device: int = 0, max_d_model=0, max_d_ff=0, max_experts=0,
+                 max_batch=0, max_vocab=0, timeout_ms=0):
+        a = InitArgs(device, max_d_model, max_d_ff, max_experts, max_batch, max_vocab, timeout_ms)
+        self.L = lib()
+        self.h = self.L.smoe_cuda_init_ex(C.byref(a))
+        if not self.h:
+            raise SmoeCudaError(f"smoe_cuda_init_ex failed: {last_error()}")
+
+    def close(self):
+        if self.h:
+            self.L.smoe_cuda_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # -------------------------------------------------------------- plumbing
+    def set_stream(self, stream_handle: int | None):
+        check(self.L.smoe_cuda_set_stream(self.h, stream_handle), "set_stream")
+
+    def synchronize(self):
+        check(self.L.smoe_cuda_synchronize(self.h), "synchronize")
+
+    def dispatches(self) -> int:
+        return int(self.L.smoe_cuda_kernel_dispatches(self.h))
+
+    # ------------------------------------------------------------ mirrored
+    def fused_ffn_group(self, blobs, input_vec, gate_rows, gate_cols, group_size=64, bits=4):
+        arr = (ExpertBlob * len(blobs))(*blobs)
+        h = self.L.smoe_cuda_fused_ffn_group(self.h, arr, len(blobs), ptr(input_vec), gate_rows,
+                                             gate_cols, gate_cols, gate_rows, group_size, bits)
+        if not h:
+            raise SmoeCudaError(f"fused_ffn_group: {last_error()}")
+        return h
+
+    def fused_ffn(self, pg, sg, pu, su, pd, sd, input_vec, gate_rows, gate_cols, expert_index,
+                  group_size=64, bits=4):
+        h = self.L.smoe_cuda_fused_ffn(self.h, ptr(pg), ptr(sg), ptr(pu), ptr(su), ptr(pd), ptr(sd),
+                                       ptr(input_vec), None, None, gate_rows, gate_cols, gate_cols,
+                                       gate_rows, group_size, bits, expert_index)
+        if not h:
+            raise SmoeCudaError(f"fused_ffn: {last_error()}")
+        return h
+
+    def wait(self, handle, output_vec, slot, cols):
+        self.L.smoe_cuda_wait(self.h, handle, ptr(output_vec), slot, cols)
+
+    def fused_ffn_batch(self, pg, sg, pu, su, pd, sd, input_mat, batch, gate_rows, gate_cols,
+                        group_size=64, bits=4):
+        h = self.L.smoe_cuda_fused_ffn_batch(self.h, ptr(pg), ptr(sg), ptr(pu), ptr(su), ptr(pd),
+                                             ptr(sd), ptr(input_mat), batch, gate_rows, gate_cols,
+                                             gate_cols, gate_rows, group_size, bits)
+        if not h:
+            raise SmoeCudaError(f"fused_ffn_batch: {last_error()}")
+        return h
+
+    def wait_ffn_batch(self, handle, out_mat, batch, cols):
+        self.L.smoe_cuda_wait_ffn_batch(self.h, handle, ptr(out_mat), batch, cols)
+
+    def scout_matvec_bf16(self, weight, input_vec, output_vec, rows, cols):
+        self.L.smoe_cuda_scout_matvec_bf16(self.h, ptr(weight), ptr(input_vec), ptr(output_vec),
+                                           rows, cols)
+
+    # -------------------------------------------------------------- native
+    def router_topk(self, router_w, x, x_dtype, n_experts, d_model, batch, k, norm, ids, weights,
+                    logits=None):
+        check(self.L.smoe_cuda_router_topk(self.h, ptr(router_w), ptr(x), x_dtype, n_experts,
+                                           d_model, batch, k, int(norm), ptr(ids), ptr(weights),
+                                           ptr(logits)), "router_topk")
+
+    def moe_ffn(self, layer: MoeLayer, x, x_dtype, ids, weights, k, batch, y, y_dtype):
+        check(self.L.smoe_cuda_moe_ffn(self.h, C.byref(layer), ptr(x), x_dtype, ptr(ids),
+                                       ptr(weights), k, batch, ptr(y), y_dtype), "moe_ffn")
+
+    def moe_layer(self, layer: MoeLayer, x, x_dtype, batch, k, norm, y, y_dtype, ids=None,
+                  weights=None):
+        check(self.L.smoe_cuda_moe_layer(self.h, C.byref(layer), ptr(x), x_dtype, batch, k,
+                                         int(norm), ptr(y), y_dtype, ptr(ids), ptr(weights)),
+              "moe_layer")
+
+    def sample(self, logits, vocab, batch, rows, history, history_stride, tokens):
+        check(self.L.smoe_cuda_sample(self.h, ptr(logits), vocab, batch, ptr(rows), ptr(history),
+                                      history_stride, ptr(tokens)), "sample")
+
+
+def make_layer(base, stride, off, n_experts, d_model, d_ff, fmt, router_w) -> MoeLayer:
+    L = MoeLayer()
+    L.base = ptr(base)
+    L.expert_stride = stride
+    for i in range(9):
+        L.off[i] = off[i]
+    L.n_experts = n_experts
+    L.d_model = d_model
+    L.d_ff = d_ff
+    L.fmt = fmt
+    L.router_w = ptr(router_w)
+    return L
