@@ -204,48 +204,69 @@ def run_ours(args, rank, world, local):
         descs.append(S.make_layer(da, stride, off, E, D, DFF, S.FMT_AFFINE_Q4, dr))
     d_x = torch.from_numpy(xs.view(np.int16)).cuda()          # [64, D] bf16
     d_y = torch.zeros(D, dtype=torch.bfloat16, device="cuda")
-    ids = torch.zeros(K, dtype=torch.int32, device="cuda")
-    wts = torch.zeros(K, dtype=torch.float32, device="cuda")
+    ids = torch.zeros(N_LAYERS, K, dtype=torch.int32, device="cuda")
+    wts = torch.zeros(N_LAYERS, K, dtype=torch.float32, device="cuda")
     torch.cuda.synchronize()
 
-    def step(i, ev=None):
-        L = descs[i % N_LAYERS]
-        x = d_x[i % 64]
-        ctx.router_topk(L.router_w, x.data_ptr(), S.DTYPE_BF16, E, D, 1, K, True, ids, wts)
-        if ev is not None:
-            ev[0].record(stream)
-        ctx.moe_ffn(L, x.data_ptr(), S.DTYPE_BF16, ids, wts, K, 1, d_y, S.DTYPE_BF16)
-        if ev is not None:
-            ev[1].record(stream)
+    def router(l):
+        L = descs[l]
+        ctx.router_topk(L.router_w, d_x[l].data_ptr(), S.DTYPE_BF16, E, D, 1, K, True,
+                        ids[l], wts[l])
 
+    def ffn(l):
+        ctx.moe_ffn(descs[l], d_x[l].data_ptr(), S.DTYPE_BF16, ids[l], wts[l], K, 1, d_y,
+                    S.DTYPE_BF16)
+
+    # eager warm-up (also sets kernel attributes before capture)
     for i in range(max(args.warmup, 3)):
-        step(i)
+        for l in range(N_LAYERS):
+            router(l)
+            ffn(l)
     ctx.synchronize()
+    # One graph = one MoE layer step on each of the 8 resident layers.
+    g_step, g_ffn = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_step, stream=stream):
+        for l in range(N_LAYERS):
+            router(l)
+            ffn(l)
+    with torch.cuda.graph(g_ffn, stream=stream):
+        for l in range(N_LAYERS):
+            ffn(l)
+    reps = max(1, args.steps // N_LAYERS)
+    steps = reps * N_LAYERS
+    for _ in range(max(args.warmup, 3)):
+        g_step.replay()
+        g_ffn.replay()
+    torch.cuda.synchronize()
 
-    # ---- device-resident timing
+    def timed(graph):
+        barrier(world)
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        t1.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        return t0.elapsed_time(t1)
+
+    # ---- device-resident timing (CUDA graph replays)
     clocks = Clocks(local)
     clocks.start()
     time.sleep(0.3)
-    barrier(world)
-    torch.cuda.synchronize()
     d0 = ctx.dispatches()
-    ffn_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-              for _ in range(args.steps)]
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0.record(stream)
-    for i in range(args.steps):
-        step(1000 + i, ffn_ev[i])
-    t1.record(stream)
-    torch.cuda.synchronize()
-    barrier(world)
-    ms = t0.elapsed_time(t1)
-    launches = ctx.dispatches() - d0
-    ffn_ms = sum(a.elapsed_time(b) for a, b in ffn_ev) / args.steps
+    ms = timed(g_step)
+    ffn_ms_total = timed(g_ffn)
     ck = clocks.stop()
+    launches = steps * 3           # router + gate_up + down_combine per step (graph replays)
     ctx.synchronize()
     ms = max_over_ranks(ms, world)
-    per_step = ms / args.steps
-    value = LAYER_BYTES * args.steps * world / (ms * 1e-3) / 1e9
+    per_step = ms / steps
+    ffn_ms = ffn_ms_total / steps
+    value = LAYER_BYTES * steps * world / (ms * 1e-3) / 1e9
+    args.steps = steps
+    del d0
 
     # ---- end to end through the C ABI with host buffers
     hx = torch.from_numpy(xs.view(np.int16)).pin_memory()
@@ -258,7 +279,7 @@ def run_ours(args, rank, world, local):
     with torch.cuda.stream(stream):
         for i in range(args.steps):
             stage_x.view(torch.int16).copy_(hx[(2000 + i) % 64], non_blocking=True)
-            L = descs[(2000 + i) % N_LAYERS]
+            L = descs[i % N_LAYERS]
             ctx.moe_layer(L, stage_x, S.DTYPE_BF16, 1, K, True, d_y, S.DTYPE_BF16)
             hy.copy_(d_y, non_blocking=True)
     e1.record(stream)

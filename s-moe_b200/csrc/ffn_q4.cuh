@@ -8,13 +8,13 @@
 //
 // Arithmetic. A 4-bit code q is turned into an fp16 operand by one LOP3
 // that ORs it into the mantissa of 1024.0 (0x6400): codes at bits 0-3 of a
-// half word become 1024+q, codes at bits 4-7 become 1024+16q. The matching
-// activation slots of the B operand carry x or x/16, so the tensor core sums
-// q.x plus a per-group constant (1024 * sum of x at even positions + 64 * sum
-// at odd positions) that the epilogue subtracts. The activation is split
+// half word become 1024+q, codes at bits 4-7 become 1024+16q; one packed
+// fp16 subtraction of 1024 leaves the exact q or 16q, so no large offset is
+// left to cancel inside the fp32 accumulator. The matching activation slots
+// of the B operand carry x or x/16, so the tensor core sums q.x. The activation is split
 // into two fp16 halves x = hi + lo held in two B columns, so the product is
 // accumulated at ~fp32 quality in fp32. Per 64-element group g:
-//     sum_k w_k x_k = scale_g * (D_g - corr_g) + bias_g * sum_g(x)
+//     sum_k w_k x_k = scale_g * D_g + bias_g * sum_g(x)
 // with (scale, bias) = (bf16 scale, bf16 bias) for AFFINE-Q4 and
 // (s/7.5, -s) for SMOE-Q4 (the same identity kernels.metal:136-143 uses).
 //
@@ -83,7 +83,8 @@ SMOE_DEVINL SlotW slot_weights(const FfnArgs& a, uint32_t slot) {
 // ---------------------------------------------------------------- B table
 // For a K-vector v: btab[(grp*4 + s)*8 + lane8] (uint2 = the two B regs of
 // lanes 0..7 of the MMA at k-step s of group grp; lanes 0-3 hold the hi
-// column, 4-7 the lo column), and gsum[grp] = (corr, sum x_eff).
+// column, 4-7 the lo column), and gsum[grp].y = sum of x_eff over the group
+// (x_eff = hi + lo as the MMA sees it; .x unused).
 // `part` scratch: K/4 float2. Must be followed by __syncthreads() (inside).
 template <typename Load>
 SMOE_DEVINL void build_btab(Load ld, int K, uint2* btab, float2* gsum, float2* part) {
@@ -106,7 +107,7 @@ SMOE_DEVINL void build_btab(Load ld, int K, uint2* btab, float2* gsum, float2* p
         float x4 = __half2float(he4) + __half2float(le4);
         float x1 = 16.0f * (__half2float(ho1) + __half2float(lo1));
         float x5 = 16.0f * (__half2float(ho5) + __half2float(lo5));
-        part[t] = make_float2(1024.0f * (x0 + x4) + 64.0f * (x1 + x5), (x0 + x4) + (x1 + x5));
+        part[t] = make_float2(0.0f, (x0 + x4) + (x1 + x5));
     }
     __syncthreads();
     for (int grp = threadIdx.x; grp < K / 64; grp += blockDim.x) {
@@ -139,10 +140,10 @@ SMOE_DEVINL void group_mma(const uint8_t* rowp, int rs, int grp, const uint2* bt
         for (int h = 0; h < 2; ++h) {
             const uint32_t g8 = h ? (wg >> 8) : wg, h8 = h ? (wh >> 8) : wh;
             uint32_t a[4];
-            a[0] = lop3_and_or(g8, M0, OR);
-            a[1] = lop3_and_or(h8, M0, OR);
-            a[2] = lop3_and_or(g8, M1, OR);
-            a[3] = lop3_and_or(h8, M1, OR);
+            a[0] = hsub_1024(lop3_and_or(g8, M0, OR));
+            a[1] = hsub_1024(lop3_and_or(h8, M0, OR));
+            a[2] = hsub_1024(lop3_and_or(g8, M1, OR));
+            a[3] = hsub_1024(lop3_and_or(h8, M1, OR));
             uint2 b = make_uint2(0u, 0u);
             if (lane < 8) b = btab[(grp * 4 + i * 2 + h) * 8 + lane];
             uint32_t bb[2] = {b.x, b.y};
@@ -158,10 +159,10 @@ SMOE_DEVINL float group_epilogue(float dsum, float2 gs, const uint16_t* sc, cons
                                  int idx) {
     if (FMT == kFmtAffine) {
         const float s = bf16_bits_to_f32(sc[idx]), b = bf16_bits_to_f32(bi[idx]);
-        return s * (dsum - gs.x) + b * gs.y;
+        return s * dsum + b * gs.y;
     } else {
         const float s = f16_bits_to_f32(sc[idx]);
-        return s * ((dsum - gs.x) * (1.0f / 7.5f) - gs.y);
+        return s * (dsum * (1.0f / 7.5f) - gs.y);
     }
 }
 

@@ -28,6 +28,13 @@ SMOE_DEVINL uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {
     return d;
 }
 
+// Packed fp16 a - (1024, 1024): exact for the 1024+q / 1024+16q operands.
+SMOE_DEVINL uint32_t hsub_1024(uint32_t a) {
+    uint32_t d;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(0x64006400u));
+    return d;
+}
+
 // D += A(16x16, f16, row) * B(16x8, f16, col), fp32 accumulate.
 SMOE_DEVINL void mma_f16_16816(float d[4], const uint32_t a[4], const uint32_t b[2]) {
     asm volatile(

@@ -109,7 +109,15 @@ int prep_kernel(SmoeCudaCtx* c, K kern, size_t smem) {
             set_err("kernel needs %s%ld bytes of shared memory", "", (long)smem);
             return SMOE_ERR_ARG;
         }
+        // Raise the limit once per (kernel, device, size): later calls, including
+        // calls made while a stream is being captured, then issue no attribute call.
+        static thread_local struct { const void* f; int dev; size_t smem; } seen[32];
+        static thread_local int nseen = 0;
+        for (int i = 0; i < nseen; ++i)
+            if (seen[i].f == (const void*)kern && seen[i].dev == c->device && seen[i].smem >= smem)
+                return SMOE_OK;
         CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        if (nseen < 32) seen[nseen++] = {(const void*)kern, c->device, smem};
     }
     return SMOE_OK;
 }

@@ -31,7 +31,7 @@ def test_router_golden(ctx):
         W = O.normal_bf16(s, 6, 128 * 2048, 0.0, 0.02)
         ids, w, lg = run_router(ctx, W, r["x"][s], 128, 2048, 8)
         assert (ids[0] == r["ids"][s]).all(), s
-        np.testing.assert_allclose(w[0], r["weights"][s], rtol=2e-6, atol=1e-8)
+        np.testing.assert_allclose(w[0], r["weights"][s], rtol=2e-5, atol=1e-8)
         np.testing.assert_allclose(lg[0], r["logits"][s], rtol=1e-4, atol=1e-5)
 
 
@@ -50,7 +50,7 @@ def test_router_many_seeds_bf16_input_batched(ctx):
                 assert near_tie, (rep, t)
                 mism += 1
             else:
-                np.testing.assert_allclose(w[t], rw, rtol=2e-6, atol=1e-8)
+                np.testing.assert_allclose(w[t], rw, rtol=2e-5, atol=1e-8)
     assert mism == 0
 
 
@@ -62,7 +62,7 @@ def test_router_shapes_and_no_norm(ctx):
             ids, w, _ = run_router(ctx, W, x, E, d, k, norm=norm)
             rids, rw, _ = O.route(x, W, E, d, k, norm=norm)
             assert (ids[0] == rids).all()
-            np.testing.assert_allclose(w[0], rw, rtol=2e-6, atol=1e-8)
+            np.testing.assert_allclose(w[0], rw, rtol=2e-5, atol=1e-8)
 
 
 def test_router_ties_lowest_index(ctx):
