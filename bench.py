@@ -234,19 +234,21 @@ def run_ours(args, rank, world, local):
             ffn(l)
     reps = max(1, args.steps // N_LAYERS)
     steps = reps * N_LAYERS
-    for _ in range(max(args.warmup, 3)):
-        g_step.replay()
-        g_ffn.replay()
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            g_step.replay()
+            g_ffn.replay()
     torch.cuda.synchronize()
 
     def timed(graph):
         barrier(world)
         torch.cuda.synchronize()
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        t0.record(stream)
-        for _ in range(reps):
-            graph.replay()
-        t1.record(stream)
+        with torch.cuda.stream(stream):      # replay() launches on the current stream
+            t0.record(stream)
+            for _ in range(reps):
+                graph.replay()
+            t1.record(stream)
         torch.cuda.synchronize()
         barrier(world)
         return t0.elapsed_time(t1)

@@ -83,17 +83,37 @@ SMOE_DEVINL SlotW slot_weights(const FfnArgs& a, uint32_t slot) {
 // ---------------------------------------------------------------- B table
 // For a K-vector v: btab[(grp*4 + s)*8 + lane8] (uint2 = the two B regs of
 // lanes 0..7 of the MMA at k-step s of group grp; lanes 0-3 hold the hi
-// column, 4-7 the lo column), and gsum[grp].y = sum of x_eff over the group
-// (x_eff = hi + lo as the MMA sees it; .x unused).
+// column, 4-7 the lo column), and gsum[grp] = (1/scale, sum of scale*x over
+// the group as the MMA sees it, hi + lo). The vector is multiplied by a power
+// of two `scale` first; the epilogue multiplies the group result by 1/scale.
 // `part` scratch: K/4 float2. Must be followed by __syncthreads() (inside).
+// Power-of-two factor that brings max|v| to [2^13, 2^14): keeps the fp16
+// halves of small vectors (e.g. SiLU outputs ~1e-3) out of the subnormals.
+SMOE_DEVINL float pow2_scale_for(float amax) {
+    if (!(amax > 0.0f) || !isfinite(amax)) return 1.0f;
+    int e;
+    frexpf(amax, &e);                        // amax in [2^(e-1), 2^e)
+    return ldexpf(1.0f, 14 - e);
+}
+
 template <typename Load>
 SMOE_DEVINL void build_btab(Load ld, int K, uint2* btab, float2* gsum, float2* part) {
+    // max |v| over the vector (block reduction through `part`)
+    float amax = 0.0f;
+    for (int i = threadIdx.x; i < K; i += blockDim.x) amax = fmaxf(amax, fabsf(ld(i)));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5].x = amax;
+    __syncthreads();
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) amax = fmaxf(amax, part[w].x);
+    __syncthreads();
+    const float sc = pow2_scale_for(amax), inv = 1.0f / sc;
     const int ntup = K / 4;
     for (int t = threadIdx.x; t < ntup; t += blockDim.x) {
         const int grp = t >> 4, r = t & 15, s = r >> 2, c = r & 3;
         const int base = grp * 64 + c * 16 + (s >> 1) * 8 + (s & 1) * 2;
-        float e0 = ld(base), e4 = ld(base + 4);
-        float o1 = ld(base + 1) * 0.0625f, o5 = ld(base + 5) * 0.0625f;
+        float e0 = ld(base) * sc, e4 = ld(base + 4) * sc;
+        float o1 = ld(base + 1) * (sc * 0.0625f), o5 = ld(base + 5) * (sc * 0.0625f);
         __half he0 = __float2half_rn(e0), he4 = __float2half_rn(e4);
         __half le0 = __float2half_rn(e0 - __half2float(he0));
         __half le4 = __float2half_rn(e4 - __half2float(he4));
@@ -117,7 +137,7 @@ SMOE_DEVINL void build_btab(Load ld, int K, uint2* btab, float2* gsum, float2* p
             cs += p.x;
             xs += p.y;
         }
-        gsum[grp] = make_float2(cs, xs);
+        gsum[grp] = make_float2(inv, xs);
     }
     __syncthreads();
 }
@@ -159,10 +179,10 @@ SMOE_DEVINL float group_epilogue(float dsum, float2 gs, const uint16_t* sc, cons
                                  int idx) {
     if (FMT == kFmtAffine) {
         const float s = bf16_bits_to_f32(sc[idx]), b = bf16_bits_to_f32(bi[idx]);
-        return s * dsum + b * gs.y;
+        return (s * dsum + b * gs.y) * gs.x;
     } else {
         const float s = f16_bits_to_f32(sc[idx]);
-        return s * (dsum * (1.0f / 7.5f) - gs.y);
+        return s * (dsum * (1.0f / 7.5f) - gs.y) * gs.x;
     }
 }
 
