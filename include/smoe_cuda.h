@@ -188,6 +188,23 @@ int smoe_cuda_moe_layer(SmoeCudaCtx* ctx, const SmoeMoeLayer* layer, const void*
                         int x_dtype, uint32_t batch, uint32_t k, int norm_topk,
                         void* y, int y_dtype, uint32_t* ids_out, float* w_out);
 
+/* No counterpart in the reference. For callers that cannot call cudaMalloc -
+ * engines whose device memory is all reserved by their own pool, code run
+ * inside callbacks where allocation is forbidden - this is smoe_cuda_moe_ffn
+ * (same arguments and results, device pointers, asynchronous on `stream`, a
+ * cudaStream_t or NULL) without a context: it allocates nothing. Its only
+ * scratch is one fixed array compiled into the library, which every GPU that
+ * loads the library holds until the process exits. Limits: batch * k * d_ff
+ * <= 65536 (256 KiB of hidden vectors); larger calls return SMOE_ERR_ARG.
+ * The first call on each device looks up the array's device address, so make
+ * that call before any stream capture. All calls share the array: calls that
+ * overlap on the GPU (different streams, or different host threads) race.
+ * The message of a failure is in smoe_cuda_noalloc_last_error(). */
+int smoe_cuda_moe_ffn_noalloc(const SmoeMoeLayer* layer, const void* x, int x_dtype,
+                              const uint32_t* ids, const float* weights, uint32_t k,
+                              uint32_t batch, void* y, int y_dtype, void* stream);
+const char* smoe_cuda_noalloc_last_error(void);
+
 /* ------------------------------------------------------------- sampler */
 /* One row of sampler state (sampler.hpp:11-17 SamplerConfig + the draw). */
 typedef struct {

@@ -11,7 +11,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 LIB = os.path.join(HERE, "libsmoe_cuda.so")
-SOURCES = [os.path.join(HERE, "csrc", "smoe_cuda.cu")]
+SOURCES = [os.path.join(HERE, "csrc", "smoe_cuda.cu"), os.path.join(HERE, "csrc", "smoe_noalloc.cu")]
 DEPS = SOURCES + [os.path.join(HERE, "csrc", f) for f in os.listdir(os.path.join(HERE, "csrc"))] + [
     os.path.join(ROOT, "include", "smoe_cuda.h")]
 

@@ -32,7 +32,7 @@ EXPORTS = [
     "smoe_cuda_fused_ffn_batch", "smoe_cuda_wait_ffn_batch", "smoe_cuda_scout_matvec_bf16",
     "smoe_cuda_register_buffer", "smoe_cuda_kernel_dispatches", "smoe_cuda_router_topk",
     "smoe_cuda_moe_ffn", "smoe_cuda_moe_layer", "smoe_cuda_sample",
-    "smoe_cuda_canonical_from_u32",
+    "smoe_cuda_canonical_from_u32", "smoe_cuda_moe_ffn_noalloc", "smoe_cuda_noalloc_last_error",
 ]
 
 
@@ -102,6 +102,9 @@ def lib():
         L.smoe_cuda_moe_layer.argtypes = [vp, C.POINTER(MoeLayer), vp, i32, u32, u32, i32, vp,
                                           i32, vp, vp]
         L.smoe_cuda_sample.argtypes = [vp, vp, u32, u32, vp, vp, u32, vp]
+        L.smoe_cuda_moe_ffn_noalloc.argtypes = [C.POINTER(MoeLayer), vp, i32, vp, vp, u32, u32, vp,
+                                                i32, vp]
+        L.smoe_cuda_noalloc_last_error.restype = C.c_char_p
         L.smoe_cuda_canonical_from_u32.argtypes = [u32]
         L.smoe_cuda_canonical_from_u32.restype = f32
         _lib = L
