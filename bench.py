@@ -201,34 +201,39 @@ def run_ours(args, rank, world, local):
         da = torch.from_numpy(arena).cuda()
         dr = torch.from_numpy(rw.view(np.int16)).cuda()
         keep += [da, dr]
-        descs.append(S.make_layer(da, stride, off, E, D, DFF, S.FMT_AFFINE_Q4, dr))
+        vault = S.make_layer(da, stride, off, E, D, DFF, S.FMT_AFFINE_Q4, dr)
+        # one-time load-time re-layout into the tiled device format (the
+        # vault-layout copy is dropped afterwards)
+        tstride = S.tiled_stride(S.FMT_AFFINE_Q4, D, DFF)
+        tb = torch.empty(E * tstride, dtype=torch.uint8, device="cuda")
+        descs.append(ctx.prepack_layer(vault, tb, tstride))
+        ctx.synchronize()
+        keep[-2] = tb
     d_x = torch.from_numpy(xs.view(np.int16)).cuda()          # [64, D] bf16
     d_y = torch.zeros(D, dtype=torch.bfloat16, device="cuda")
     ids = torch.zeros(N_LAYERS, K, dtype=torch.int32, device="cuda")
     wts = torch.zeros(N_LAYERS, K, dtype=torch.float32, device="cuda")
     torch.cuda.synchronize()
 
-    def router(l):
-        L = descs[l]
-        ctx.router_topk(L.router_w, d_x[l].data_ptr(), S.DTYPE_BF16, E, D, 1, K, True,
-                        ids[l], wts[l])
+    def layer(l):      # router + top-k + expert FFN + combine: one fused launch
+        ctx.moe_layer(descs[l], d_x[l].data_ptr(), S.DTYPE_BF16, 1, K, True, d_y, S.DTYPE_BF16,
+                      ids[l], wts[l])
 
-    def ffn(l):
+    def ffn(l):        # the same with the routing already on the device
         ctx.moe_ffn(descs[l], d_x[l].data_ptr(), S.DTYPE_BF16, ids[l], wts[l], K, 1, d_y,
                     S.DTYPE_BF16)
 
     # eager warm-up (also sets kernel attributes before capture)
     for i in range(max(args.warmup, 3)):
         for l in range(N_LAYERS):
-            router(l)
+            layer(l)
             ffn(l)
     ctx.synchronize()
     # One graph = one MoE layer step on each of the 8 resident layers.
     g_step, g_ffn = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
     with torch.cuda.graph(g_step, stream=stream):
         for l in range(N_LAYERS):
-            router(l)
-            ffn(l)
+            layer(l)
     with torch.cuda.graph(g_ffn, stream=stream):
         for l in range(N_LAYERS):
             ffn(l)
@@ -261,7 +266,7 @@ def run_ours(args, rank, world, local):
     ms = timed(g_step)
     ffn_ms_total = timed(g_ffn)
     ck = clocks.stop()
-    launches = steps * 3           # router + gate_up + down_combine per step (graph replays)
+    launches = steps * 1           # one fused MoE-layer kernel per step (graph replays)
     ctx.synchronize()
     ms = max_over_ranks(ms, world)
     per_step = ms / steps
@@ -306,8 +311,8 @@ def run_ours(args, rank, world, local):
             "layer_us": round(per_step * 1e3, 3),
             "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(ach / peak, 4), "traffic": None,
-                         "kernel": "expert FFN (gate_up + down_combine), 21,233,664 B per launch "
-                                   f"pair, {ffn_ms * 1e3:.2f} us avg", "peak_kind": peak_kind},
+                         "kernel": "k_moe_fused (expert FFN + combine, routing given), 21,233,664 B "
+                                   f"per launch, {ffn_ms * 1e3:.2f} us avg", "peak_kind": peak_kind},
             "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": D * 2,
                     "d2h_bytes_per_step": D * 2},
             "gpu_launches": int(launches),

@@ -164,6 +164,25 @@ typedef struct {
     const uint16_t* router_w;     /* bf16 [n_experts x d_model]              */
 } SmoeMoeLayer;
 
+/* Tiled device layout of a layer's experts, made once at load time by
+ * smoe_cuda_prepack_layer (no counterpart in the reference, whose experts
+ * stay in the vault layout). Set as a flag in SmoeMoeLayer.fmt: the fused
+ * single-launch MoE path needs it; the vault layout is served by the
+ * two-kernel path. Per expert: d_ff/16 gate+up tiles then d_model/16 down
+ * tiles, each tile one contiguous block (nibbles in MMA-fragment order,
+ * then transposed scales, then biases). Same byte count as the vault layout. */
+#define SMOE_LAYOUT_TILED 0x100
+
+/* Bytes of one expert in the tiled layout (0 for unsupported shapes). */
+uint64_t smoe_cuda_tiled_expert_bytes(uint32_t fmt, uint32_t d_model, uint32_t d_ff);
+
+/* Re-lay out every expert of `src` (vault layout, device) into `dst`
+ * (device, n_experts * dst_stride bytes, dst_stride >= the tiled size and a
+ * multiple of 256) and describe the result in *out (base dst, fmt |
+ * SMOE_LAYOUT_TILED, router_w copied). Asynchronous on the context stream. */
+int smoe_cuda_prepack_layer(SmoeCudaCtx* ctx, const SmoeMoeLayer* src, void* dst,
+                            uint64_t dst_stride, SmoeMoeLayer* out);
+
 /* Router of decode.cpp:280-303 for `batch` tokens: logits = W . x (bf16 W,
  * fp32 accumulate), softmax over n_experts, top-k by probability (lowest
  * index wins ties), renormalised over the k when norm_topk. Outputs (device):

@@ -3,7 +3,7 @@
 //
 // Router (decode.cpp:280-303 -> common.hpp:294-306, scout.cpp:77-123):
 //   logits[e] = sum_j bf16(W[e,j]) * x[j]           fp32 accumulate
-//   p = softmax(logits)  (max-subtracted exp, index-order sum, * 1/sum)
+//   p = softmax(logits)  (max-subtracted exp, * 1/sum)
 //   top-k by p, descending, lowest expert index wins ties
 //   w_j = p_j * (1 / sum_{rank order} p)   when norm_topk
 // One warp per expert row; the last CTA of a token (atomic ticket) finishes
@@ -33,14 +33,22 @@ constexpr int kRouterMaxE = 512;
 SMOE_DEVINL float warp_row_dot_bf16(const uint16_t* row, const float* xs, int d, int lane) {
     float acc = 0.f;
     const uint4* rp = reinterpret_cast<const uint4*>(row);
-    for (int c = lane; c < d / 8; c += 32) {
-        const uint4 v = __ldg(rp + c);
-        const float* xv = xs + c * 8;
-        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+    const int n = d / 8;
+    for (int c0 = lane; c0 < n; c0 += 32 * 8) {
+        uint4 v[8];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            acc = fmaf(__uint_as_float(u[q] << 16), xv[2 * q], acc);
-            acc = fmaf(__uint_as_float(u[q] & 0xffff0000u), xv[2 * q + 1], acc);
+        for (int q = 0; q < 8; ++q)              // all loads in flight before any use
+            if (c0 + q * 32 < n) v[q] = __ldg(rp + c0 + q * 32);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            if (c0 + q * 32 >= n) break;
+            const float* xv = xs + (c0 + q * 32) * 8;
+            const uint32_t u[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                acc = fmaf(__uint_as_float(u[r] << 16), xv[2 * r], acc);
+                acc = fmaf(__uint_as_float(u[r] & 0xffff0000u), xv[2 * r + 1], acc);
+            }
         }
     }
 #pragma unroll
@@ -56,6 +64,63 @@ SMOE_DEVINL void stage_vec(const void* src, int x_dtype, size_t off, int d, floa
     } else {
         const uint16_t* s = static_cast<const uint16_t*>(src) + off;
         for (int i = threadIdx.x; i < d; i += blockDim.x) xs[i] = bf16_bits_to_f32(s[i]);
+    }
+}
+
+// One warp: softmax over E logits (read from global, bypassing L1), top-k
+// by probability with the lowest index winning ties, renormalised over the k
+// in rank order when `norm` (scout.cpp:77-123, decode.cpp:296-303). The
+// denominator is a warp tree sum; expert ids do not depend on it.
+// ps: shared scratch of E floats. ids/wts: k outputs (global or shared).
+SMOE_DEVINL void warp_topk(const float* lg, uint32_t E_, uint32_t k_, int norm, float* ps,
+                           uint32_t* ids, float* wts, int lane) {
+    const int E = (int)E_;
+    float mx = -INFINITY;
+    for (int i = lane; i < E; i += 32) {
+        const float v = __ldcg(lg + i);
+        ps[i] = v;
+        mx = fmaxf(mx, v);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float se = 0.f;
+    for (int i = lane; i < E; i += 32) {
+        const float e = expf(ps[i] - mx);
+        ps[i] = e;
+        se += e;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) se += __shfl_xor_sync(0xffffffffu, se, o);
+    const float inv = se > 0.f ? 1.0f / se : 0.f;
+    __syncwarp();
+    for (int i = lane; i < E; i += 32) ps[i] *= inv;
+    __syncwarp();
+    const uint32_t k = k_ < E_ ? k_ : E_;
+    float wsel = 0.f;
+    uint32_t idsel = 0;
+    for (uint32_t s = 0; s < k; ++s) {
+        float bv = -1.f;
+        int bi = 0x7fffffff;
+        for (int i = lane; i < E; i += 32) {
+            const float v = ps[i];
+            if (v > bv) { bv = v; bi = i; }          // ascending i: first max per lane
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+        }
+        if (lane == (int)s) { wsel = bv; idsel = bi; }
+        if (lane == 0) ps[bi] = -2.f;                 // removed
+        __syncwarp();
+    }
+    float ws = 0.f;                                   // rank-order sum (decode.cpp:296-303)
+    for (uint32_t s = 0; s < k; ++s) ws += __shfl_sync(0xffffffffu, wsel, s);
+    const float winv = (norm && ws > 0.f) ? 1.0f / ws : 1.0f;
+    if (lane < (int)k) {
+        ids[lane] = idsel;
+        wts[lane] = wsel * winv;
     }
 }
 
@@ -83,53 +148,7 @@ __global__ void __launch_bounds__(256) k_router(RouterArgs a) {
     if (!last_flag) return;
     __threadfence();
     if (warp != 0) return;
-    // ---- last CTA, warp 0: softmax + top-k + renorm (scout.cpp:77-123)
-    const int E = a.E;
-    float mx = -INFINITY;
-    for (int i = lane; i < E; i += 32) {
-        const float v = __ldcg(lg + i);
-        ps[i] = v;
-        mx = fmaxf(mx, v);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    for (int i = lane; i < E; i += 32) ps[i] = expf(ps[i] - mx);
-    __syncwarp();
-    float se = 0.f;
-    if (lane == 0)
-        for (int i = 0; i < E; ++i) se += ps[i];       // index-order sum, as the reference
-    se = __shfl_sync(0xffffffffu, se, 0);
-    const float inv = se > 0.f ? 1.0f / se : 0.f;
-    for (int i = lane; i < E; i += 32) ps[i] *= inv;
-    __syncwarp();
-    const uint32_t k = a.k < (uint32_t)E ? a.k : (uint32_t)E;
-    float wsel = 0.f;
-    uint32_t idsel = 0;
-    for (uint32_t s = 0; s < k; ++s) {
-        float bv = -1.f;
-        int bi = 0x7fffffff;
-        for (int i = lane; i < E; i += 32) {
-            const float v = ps[i];
-            if (v > bv) { bv = v; bi = i; }          // ascending i: first max per lane
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-        }
-        if (lane == (int)s) { wsel = bv; idsel = bi; }
-        if (lane == 0) ps[bi] = -2.f;                 // removed
-        __syncwarp();
-    }
-    // renorm over the k in rank order (decode.cpp:296-303)
-    float ws = 0.f;
-    for (uint32_t s = 0; s < k; ++s) ws += __shfl_sync(0xffffffffu, wsel, s);
-    const float winv = (a.norm && ws > 0.f) ? 1.0f / ws : 1.0f;
-    if (lane < (int)k) {
-        a.ids[size_t(tok) * a.k + lane] = idsel;
-        a.wts[size_t(tok) * a.k + lane] = wsel * winv;
-    }
+    warp_topk(lg, a.E, a.k, a.norm, ps, a.ids + size_t(tok) * a.k, a.wts + size_t(tok) * a.k, lane);
     if (lane == 0) a.ticket[tok] = 0;                 // ready for the next call
 }
 

@@ -35,6 +35,27 @@ SMOE_DEVINL uint32_t hsub_1024(uint32_t a) {
     return d;
 }
 
+// Packed bf16 a - (128, 128): exact for the 128+q operands.
+SMOE_DEVINL uint32_t bsub_128(uint32_t a) {
+    uint32_t d;
+    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(0x43004300u));
+    return d;
+}
+
+// D += A(16x16, bf16, row) * B(16x8, bf16, col), fp32 accumulate.
+SMOE_DEVINL void mma_bf16_16816(float d[4], const uint32_t a[4], const uint32_t b[2]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+SMOE_DEVINL uint32_t pack_bf16x2(float lo, float hi) {
+    const __nv_bfloat16 a = __float2bfloat16_rn(lo), b = __float2bfloat16_rn(hi);
+    return uint32_t(__bfloat16_as_ushort(a)) | (uint32_t(__bfloat16_as_ushort(b)) << 16);
+}
+
 // D += A(16x16, f16, row) * B(16x8, f16, col), fp32 accumulate.
 SMOE_DEVINL void mma_f16_16816(float d[4], const uint32_t a[4], const uint32_t b[2]) {
     asm volatile(
@@ -72,8 +93,8 @@ SMOE_DEVINL bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // the phase never completes.
 SMOE_DEVINL bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
     for (uint32_t i = 0; i < SMOE_SPIN_LIMIT; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if (i > 64) __nanosleep(64);
+        if (mbar_try_wait(bar, parity)) return true;   // try_wait itself suspends a while
+        if (i > 4096) __nanosleep(64);
     }
     return false;
 }

@@ -5,12 +5,14 @@
 #include <atomic>
 #include <chrono>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 #include <thread>
 
 #include "../../include/smoe_cuda.h"
 #include "ffn_q4.cuh"
+#include "ffn_fused_kernel.cuh"
 #include "router.cuh"
 #include "sampler.cuh"
 
@@ -58,6 +60,9 @@ struct SmoeCudaCtx {
     uint64_t seq = 0;
     std::atomic<uint64_t> dispatches{0};
     size_t smem_optin = 0;
+    int num_sms = 0;
+    smoe::FusedState* fstate = nullptr;
+    unsigned long long* trace = nullptr;   // phase timestamps of the fused kernel (profiling aid)
 };
 
 namespace {
@@ -162,6 +167,45 @@ int launch_ffn(SmoeCudaCtx* c, smoe::FfnArgs& a, int fmt) {
     return SMOE_OK;
 }
 
+// The persistent fused layer kernel: one CTA per SM, cooperative launch so
+// that all CTAs are co-resident (phase B waits on phase-A results of other
+// CTAs). Returns SMOE_ERR_UNSUPPORTED when the shape does not fit, so the
+// caller can use the two-kernel path.
+int launch_fused(SmoeCudaCtx* c, smoe::FfnArgs& f, int fmt, const uint16_t* rw, uint32_t E,
+                 int norm) {
+    if (f.ntok > (uint32_t)smoe::kFusedMaxTok || f.k > (uint32_t)smoe::kFusedMaxK ||
+        (rw && E > (uint32_t)smoe::kRouterMaxE) || (rw && f.d_model % 8))
+        return SMOE_ERR_UNSUPPORTED;
+    smoe::FusedArgs A{};
+    A.g.init(fmt, (int)f.d_model, (int)f.d_ff, (int)f.k, (int)f.ntok, (int)c->smem_optin);
+    if (A.g.nstages < 2) return SMOE_ERR_UNSUPPORTED;
+    f.hidden = c->hidden;
+    f.err = c->err;
+    A.f = f;
+    A.st = c->fstate;
+    A.rw = rw;
+    A.E = E;
+    A.norm = norm;
+    A.logits = c->logits;
+    A.htab_g = reinterpret_cast<uint2*>(c->hidden);      // [slots][dff/16][8] uint2 = 4*dff B per slot
+    A.hsum_g = c->hidden + size_t(smoe::kFusedMaxTok) * smoe::kFusedMaxK * c->cfg.max_d_ff;
+    A.trace = c->trace;
+    A.dbg_skip = (c->trace && std::getenv("SMOE_DEBUG_MODE")) ? std::atoi(std::getenv("SMOE_DEBUG_MODE")) : 0;
+    if (c->num_sms > smoe::kFusedMaxGrid) return SMOE_ERR_UNSUPPORTED;
+    smoe::fused_partition(A.g, c->num_sms, A.a_bound);
+    const size_t smem = (size_t)A.g.total;
+    void* kern = fmt == SMOE_FMT_AFFINE_Q4 ? (void*)smoe::k_moe_fused<smoe::kFmtAffine>
+                                           : (void*)smoe::k_moe_fused<smoe::kFmtSmoe>;
+    int rc = fmt == SMOE_FMT_AFFINE_Q4 ? prep_kernel(c, smoe::k_moe_fused<smoe::kFmtAffine>, smem)
+                                       : prep_kernel(c, smoe::k_moe_fused<smoe::kFmtSmoe>, smem);
+    if (rc) return rc;
+    void* args[] = {&A};
+    CK(cudaLaunchCooperativeKernel(kern, dim3(c->num_sms), dim3(smoe::kFusedThreads), args, smem,
+                                   c->stream));
+    c->dispatches += 1;
+    return SMOE_OK;
+}
+
 void* record_handle(SmoeCudaCtx* c) {
     const uint64_t s = ++c->seq;
     if (cudaEventRecord(c->events[s % kEventRing], c->stream) != cudaSuccess) {
@@ -227,6 +271,7 @@ SmoeCudaCtx* smoe_cuda_init_ex(const SmoeCudaInitArgs* args) {
     int optin = 0;
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, a.device);
     c->smem_optin = (size_t)optin;
+    cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, a.device);
     if ((e = cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking)) != cudaSuccess) return fail(e);
     c->stream = c->own_stream;
     const size_t slots = size_t(a.max_batch) * 16;
@@ -239,6 +284,8 @@ SmoeCudaCtx* smoe_cuda_init_ex(const SmoeCudaInitArgs* args) {
     if ((e = cudaMalloc(&c->wts, size_t(a.max_batch) * 16 * 4)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->ticket, size_t(a.max_batch) * 4)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->err, 4)) != cudaSuccess) return fail(e);
+    if ((e = cudaMalloc(&c->fstate, sizeof(smoe::FusedState))) != cudaSuccess) return fail(e);
+    cudaMemsetAsync(c->fstate, 0, sizeof(smoe::FusedState), c->stream);
     c->gemv_cap = a.max_vocab > a.max_d_model ? a.max_vocab : a.max_d_model;
     if ((e = cudaMalloc(&c->gemv_out, c->gemv_cap * 4)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->gemv_in, size_t(a.max_d_model) * 4)) != cudaSuccess) return fail(e);
@@ -263,7 +310,7 @@ void smoe_cuda_destroy(SmoeCudaCtx* c) {
     if (c->own_stream) cudaStreamSynchronize(c->own_stream);
     for (auto& ev : c->events)
         if (ev) cudaEventDestroy(ev);
-    void* bufs[] = {c->hidden, c->slot_out, c->in_stage, c->batch_out, c->logits, c->ids,
+    void* bufs[] = {c->fstate, c->hidden, c->slot_out, c->in_stage, c->batch_out, c->logits, c->ids,
                     c->wts, c->ticket, c->err, c->gemv_out, c->gemv_in};
     for (void* b : bufs)
         if (b) cudaFree(b);
@@ -290,6 +337,15 @@ int smoe_cuda_synchronize(SmoeCudaCtx* c) {
 }
 
 uint64_t smoe_cuda_kernel_dispatches(const SmoeCudaCtx* c) { return c ? c->dispatches.load() : 0; }
+
+// Profiling aid, not part of the public header: record per-CTA phase
+// timestamps of the fused layer kernel into `buf` ([num_SMs x 8] u64, device;
+// NULL turns it off).
+int smoe_cuda_debug_trace(SmoeCudaCtx* c, void* buf) {
+    if (!c) return SMOE_ERR_ARG;
+    c->trace = static_cast<unsigned long long*>(buf);
+    return SMOE_OK;
+}
 
 void smoe_cuda_register_buffer(SmoeCudaCtx* c, const void* p, size_t n) {
     if (!c || !p || !n || is_device_ptr(p)) return;
@@ -498,7 +554,8 @@ int smoe_cuda_router_topk(SmoeCudaCtx* c, const uint16_t* w, const void* x, int 
 }
 
 static int layer_args(SmoeCudaCtx* c, const SmoeMoeLayer* L, smoe::FfnArgs& a) {
-    if (!L || !L->base || (L->fmt != SMOE_FMT_SMOE_Q4 && L->fmt != SMOE_FMT_AFFINE_Q4) ||
+    const uint32_t fmt = L ? (L->fmt & ~uint32_t(SMOE_LAYOUT_TILED)) : 99u;
+    if (!L || !L->base || (fmt != SMOE_FMT_SMOE_Q4 && fmt != SMOE_FMT_AFFINE_Q4) ||
         L->expert_stride % 16 || !aligned16(L->base)) {
         set_err("bad layer descriptor %s%ld", "", 0);
         return SMOE_ERR_ARG;
@@ -536,7 +593,14 @@ int smoe_cuda_moe_ffn(SmoeCudaCtx* c, const SmoeMoeLayer* L, const void* x, int 
     a.per_slot = 0;
     a.k = k;
     a.ntok = batch;
-    return launch_ffn(c, a, (int)L->fmt);
+    const int fmt = int(L->fmt & ~uint32_t(SMOE_LAYOUT_TILED));
+    if (L->fmt & SMOE_LAYOUT_TILED) {
+        rc = launch_fused(c, a, fmt, nullptr, 0, 0);
+        if (rc == SMOE_ERR_UNSUPPORTED)
+            set_err("tiled layout needs batch <= 4 and a shape whose tiles fit shared memory %s%ld", "", (long)batch);
+        return rc;
+    }
+    return launch_ffn(c, a, fmt);
 }
 
 int smoe_cuda_moe_layer(SmoeCudaCtx* c, const SmoeMoeLayer* L, const void* x, int x_dtype,
@@ -545,6 +609,26 @@ int smoe_cuda_moe_layer(SmoeCudaCtx* c, const SmoeMoeLayer* L, const void* x, in
     if (!c || !L) { set_err("null argument %s%ld", "", 0); return SMOE_ERR_ARG; }
     uint32_t* ids = ids_out ? ids_out : c->ids;
     float* wts = w_out ? w_out : c->wts;
+    if ((L->fmt & SMOE_LAYOUT_TILED) && L->router_w && x && y &&
+        aligned16(L->router_w) && L->n_experts >= k && k > 0 && k <= SMOE_MAX_ACTIVE &&
+        L->n_experts <= c->cfg.max_experts && (x_dtype == 0 || x_dtype == 1) &&
+        (y_dtype == 0 || y_dtype == 1)) {
+        smoe::FfnArgs a{};
+        int rc = layer_args(c, L, a);
+        if (rc) return rc;
+        a.ids = ids;
+        a.wts = wts;
+        a.x = x;
+        a.x_dtype = x_dtype;
+        a.y = y;
+        a.y_dtype = y_dtype;
+        a.k = k;
+        a.ntok = batch;
+        rc = launch_fused(c, a, int(L->fmt & ~uint32_t(SMOE_LAYOUT_TILED)), L->router_w, L->n_experts, norm);
+        if (rc == SMOE_ERR_UNSUPPORTED)
+            set_err("tiled layout needs batch <= 4 and a shape whose tiles fit shared memory %s%ld", "", (long)batch);
+        return rc;
+    }
     int rc = smoe_cuda_router_topk(c, L->router_w, x, x_dtype, L->n_experts, L->d_model, batch,
                                    k, norm, ids, wts, nullptr);
     if (rc) return rc;
@@ -569,6 +653,50 @@ int smoe_cuda_sample(SmoeCudaCtx* c, float* logits, uint32_t vocab, uint32_t bat
     smoe::k_sample<<<g, smoe::kSampThreads, smem, c->stream>>>(a);
     CK(cudaGetLastError());
     c->dispatches += 1;
+    return SMOE_OK;
+}
+
+}  // extern "C"
+
+extern "C" {
+
+uint64_t smoe_cuda_tiled_expert_bytes(uint32_t fmt, uint32_t d, uint32_t dff) {
+    fmt &= ~uint32_t(SMOE_LAYOUT_TILED);
+    if ((fmt != SMOE_FMT_SMOE_Q4 && fmt != SMOE_FMT_AFFINE_Q4) || !d || !dff || d % 64 || dff % 64) return 0;
+    smoe::TiledGeom t;
+    t.init((int)fmt, d, dff);
+    return t.expert;
+}
+
+int smoe_cuda_prepack_layer(SmoeCudaCtx* c, const SmoeMoeLayer* src, void* dst, uint64_t dst_stride,
+                            SmoeMoeLayer* out) {
+    if (!c || !src || !dst || !out) { set_err("null argument %s%ld", "", 0); return SMOE_ERR_ARG; }
+    if (src->fmt & SMOE_LAYOUT_TILED) { set_err("layer is already tiled %s%ld", "", 0); return SMOE_ERR_ARG; }
+    smoe::FfnArgs a{};
+    int rc = layer_args(c, src, a);
+    if (rc) return rc;
+    const uint64_t need = smoe_cuda_tiled_expert_bytes(src->fmt, src->d_model, src->d_ff);
+    if (dst_stride < need || dst_stride % 256 || !aligned16(dst)) {
+        set_err("dst_stride below the tiled expert size or not a multiple of 256 (%s%ld)", "", (long)need);
+        return SMOE_ERR_ARG;
+    }
+    smoe::PrepackArgs p{};
+    p.src = src->base;
+    p.src_stride = src->expert_stride;
+    for (int i = 0; i < 9; ++i) p.off[i] = src->off[i];
+    p.dst = static_cast<uint8_t*>(dst);
+    p.dst_stride = dst_stride;
+    p.fmt = (int)src->fmt;
+    p.tg.init((int)src->fmt, src->d_model, src->d_ff);
+    dim3 grid(src->d_ff / 16 + src->d_model / 16, src->n_experts);
+    smoe::k_prepack<<<grid, 256, 0, c->stream>>>(p);
+    CK(cudaGetLastError());
+    c->dispatches += 1;
+    *out = *src;
+    out->base = static_cast<const uint8_t*>(dst);
+    out->expert_stride = dst_stride;
+    for (int i = 0; i < 9; ++i) out->off[i] = 0;
+    out->fmt = src->fmt | SMOE_LAYOUT_TILED;
     return SMOE_OK;
 }
 

@@ -19,6 +19,7 @@ STATUS = {0: "OK", 1: "ERR_ARG", 2: "ERR_CUDA", 3: "ERR_TIMEOUT", 4: "ERR_NCCL",
           5: "ERR_DEVICE", 6: "ERR_UNSUPPORTED"}
 FMT_SMOE_Q4 = 0
 FMT_AFFINE_Q4 = 1
+LAYOUT_TILED = 0x100
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
 MAX_ACTIVE = 16
@@ -33,6 +34,7 @@ EXPORTS = [
     "smoe_cuda_register_buffer", "smoe_cuda_kernel_dispatches", "smoe_cuda_router_topk",
     "smoe_cuda_moe_ffn", "smoe_cuda_moe_layer", "smoe_cuda_sample",
     "smoe_cuda_canonical_from_u32", "smoe_cuda_moe_ffn_noalloc", "smoe_cuda_noalloc_last_error",
+    "smoe_cuda_tiled_expert_bytes", "smoe_cuda_prepack_layer",
 ]
 
 
@@ -105,6 +107,9 @@ def lib():
         L.smoe_cuda_moe_ffn_noalloc.argtypes = [C.POINTER(MoeLayer), vp, i32, vp, vp, u32, u32, vp,
                                                 i32, vp]
         L.smoe_cuda_noalloc_last_error.restype = C.c_char_p
+        L.smoe_cuda_tiled_expert_bytes.argtypes = [u32, u32, u32]
+        L.smoe_cuda_tiled_expert_bytes.restype = u64
+        L.smoe_cuda_prepack_layer.argtypes = [vp, C.POINTER(MoeLayer), vp, u64, C.POINTER(MoeLayer)]
         L.smoe_cuda_canonical_from_u32.argtypes = [u32]
         L.smoe_cuda_canonical_from_u32.restype = f32
         _lib = L
@@ -222,6 +227,14 @@ class Context:
                                          int(norm), ptr(y), y_dtype, ptr(ids), ptr(weights)),
               "moe_layer")
 
+    def prepack_layer(self, layer: MoeLayer, dst, dst_stride: int) -> MoeLayer:
+        """Tiled copy of a vault-layout layer (dst: device buffer of
+        n_experts * dst_stride bytes, kept alive by the caller)."""
+        out = MoeLayer()
+        check(self.L.smoe_cuda_prepack_layer(self.h, C.byref(layer), ptr(dst), dst_stride,
+                                             C.byref(out)), "prepack_layer")
+        return out
+
     def sample(self, logits, vocab, batch, rows, history, history_stride, tokens):
         check(self.L.smoe_cuda_sample(self.h, ptr(logits), vocab, batch, ptr(rows), ptr(history),
                                       history_stride, ptr(tokens)), "sample")
@@ -239,3 +252,11 @@ def make_layer(base, stride, off, n_experts, d_model, d_ff, fmt, router_w) -> Mo
     L.fmt = fmt
     L.router_w = ptr(router_w)
     return L
+
+
+def tiled_stride(fmt: int, d_model: int, d_ff: int) -> int:
+    """Per-expert stride (bytes, 256-aligned) of the tiled layout."""
+    b = int(lib().smoe_cuda_tiled_expert_bytes(fmt, d_model, d_ff))
+    if b == 0:
+        raise SmoeCudaError("unsupported shape for the tiled layout")
+    return (b + 255) // 256 * 256

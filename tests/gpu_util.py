@@ -39,3 +39,12 @@ class Layer:
         self.d_router = dev(self.router_w)
         self.desc = S.make_layer(self.d_arena, self.stride, self.off, n_experts, d, dff, fmt,
                                  self.d_router)
+
+
+def tiled(ctx, layer: "Layer"):
+    """Prepack a Layer into the tiled device layout; returns (desc, buffer)."""
+    stride = S.tiled_stride(layer.fmt, layer.d, layer.dff)
+    buf = torch.empty(layer.E * stride, dtype=torch.uint8, device="cuda")
+    desc = ctx.prepack_layer(layer.desc, buf, stride)
+    ctx.synchronize()
+    return desc, buf

@@ -10,7 +10,7 @@ import torch
 
 import oracle as O
 import smoe_cuda as S
-from gpu_util import Layer, bf16_dev_to_f32, dev, rel_err
+from gpu_util import Layer, bf16_dev_to_f32, dev, rel_err, tiled
 
 pytestmark = pytest.mark.gpu
 GOLD = os.path.join(os.path.dirname(__file__), "golden")
@@ -71,11 +71,15 @@ def test_token_batch_mirror(ctx):
         assert rel_err(out[t], O.expert_ffn(O.FMT_SMOE_Q4, L.arena[1], d, dff, X[t])) < TIGHT
 
 
+@pytest.mark.parametrize("layout", ["vault", "tiled"])
 @pytest.mark.parametrize("fmt", [O.FMT_AFFINE_Q4, O.FMT_SMOE_Q4])
-def test_moe_layer_config1(ctx, fmt):
-    """Config 1: Qwen3-30B-A3B MoE layer, x bf16[2048], 128 experts, top-8."""
+def test_moe_layer_config1(ctx, fmt, layout):
+    """Config 1: Qwen3-30B-A3B MoE layer, x bf16[2048], 128 experts, top-8.
+    vault layout -> two-kernel path; tiled layout -> single persistent launch."""
     d, dff, E, k = 2048, 768, 128, 8
     L = Layer(fmt, E, d, dff, seed=21 + fmt)
+    if layout == "tiled":
+        L.desc, L._tiled_buf = tiled(ctx, L)
     for s in range(3):
         xb = O.normal_bf16(100 + s, 5, d)
         x = O.bf16_to_f32(xb)
@@ -143,3 +147,45 @@ def test_bad_arguments_rejected(ctx):
     with pytest.raises(S.SmoeCudaError):
         ctx.moe_ffn(bad, x, S.DTYPE_F32, ids, w, 1, 1, y, S.DTYPE_F32)        # d % 64
     ctx.synchronize()
+
+
+@pytest.mark.parametrize("B,k,fmt", [(2, 8, O.FMT_AFFINE_Q4), (4, 16, O.FMT_SMOE_Q4), (3, 6, O.FMT_AFFINE_Q4)])
+def test_moe_layer_fused_small_batch(ctx, B, k, fmt):
+    """The persistent single-launch path (batch <= 4), called twice in a row so
+    the in-kernel counters must have been reset by the previous launch."""
+    d, dff, E = 1024, 512, 64
+    L = Layer(fmt, E, d, dff, seed=60 + B)
+    L.desc, L._tiled_buf = tiled(ctx, L)
+    for call in range(2):
+        X = O.normal_bf16(70 + 10 * B + call, 5, B * d)
+        y = torch.zeros(B, d, dtype=torch.float32, device="cuda")
+        ids = torch.zeros(B, k, dtype=torch.int32, device="cuda")
+        w = torch.zeros(B, k, dtype=torch.float32, device="cuda")
+        ctx.moe_layer(L.desc, dev(X), S.DTYPE_BF16, B, k, True, y, S.DTYPE_F32, ids, w)
+        ctx.synchronize()
+        got = y.cpu().numpy()
+        gid = ids.cpu().numpy().view(np.uint32)
+        for t in range(B):
+            x = O.bf16_to_f32(X[t * d:(t + 1) * d])
+            ref, rids, rw = O.moe_layer(fmt, x, L.router_w, L.arena, L.stride, E, d, dff, k)
+            assert (gid[t] == rids).all()
+            assert rel_err(got[t], ref) < TIGHT
+
+
+def test_tiled_moe_ffn_given_routing(ctx):
+    """moe_ffn on the tiled layout (routing supplied), two fp32 tokens."""
+    d, dff, E, k, B = 2048, 1024, 16, 8, 2
+    L = Layer(O.FMT_AFFINE_Q4, E, d, dff, seed=33)
+    desc, buf = tiled(ctx, L)
+    X = O.normal_f32(33, 9, B * d).reshape(B, d)
+    ids = np.stack([np.random.default_rng(t).permutation(E)[:k] for t in range(B)]).astype(np.uint32)
+    w = np.random.default_rng(9).random((B, k)).astype(np.float32)
+    y = torch.zeros(B, d, dtype=torch.float32, device="cuda")
+    ctx.moe_ffn(desc, dev(X), S.DTYPE_F32, dev(ids), dev(w), k, B, y, S.DTYPE_F32)
+    ctx.synchronize()
+    got = y.cpu().numpy()
+    for t in range(B):
+        ref = np.zeros(d, np.float32)
+        for j in range(k):
+            ref = ref + w[t, j] * O.expert_ffn(O.FMT_AFFINE_Q4, L.arena[ids[t, j]], d, dff, X[t])
+        assert rel_err(got[t], ref) < TIGHT
