@@ -49,11 +49,12 @@ constexpr int kFusedSlotsPerB = 4;                 // slots per phase-B stage
 constexpr int kFusedMaxK = 16;
 constexpr int kFusedMaxGrid = 256;
 
-struct FusedState {          // device scratch, zero on entry, zero on exit
-    uint32_t hdone[kFusedMaxTok];   // phase-A units finished, per token
-    uint32_t rdone;                 // router logit rows finished
-    uint32_t done;                  // CTAs finished
-    uint32_t pad[2];
+struct FusedState {          // device scratch, zero at context creation
+    uint32_t rdone;                 // router logit rows finished (reset at exit)
+    uint32_t done;                  // CTAs finished (reset at exit)
+    uint32_t epoch;                 // launches completed: tags this launch's h tables
+    uint32_t hcount[kFusedMaxTok];  // phase-A units written, per token (relaxed; reset at exit)
+    uint32_t pad[1];
 };
 
 struct FusedGeom {           // shared by host (smem sizing) and device
@@ -91,7 +92,7 @@ struct FusedGeom {           // shared by host (smem sizing) and device
         o_ids = take(ntok * k * 4);
         o_w = take(ntok * k * 4);
         o_ps = take(kFusedMaxTok * kRouterMaxE * 4);
-        o_vst = take(4 * ntok * d);                     // staged x (fp32)
+        o_vst = take(4 * (ntok * d > k * dff / 16 ? ntok * d : k * dff / 16));   // staged x / quarter sums
         off = (off + 1023) & ~1023;
         o_ring = off;
         nstages = (max_smem - off) / stage;
@@ -168,6 +169,50 @@ SMOE_DEVINL void group_mma_bf16(const uint8_t* frag, int grp, const uint2* btab,
 }
 
 // dsum = sum (128+q).v from the MMA, vsum = sum v: sum q.v = dsum - 128 vsum.
+// N independent 64-groups at once (same arithmetic as group_mma_bf16): the
+// 4N loads are issued first and the 4 k-steps of all N groups interleaved,
+// so a warp has 2N accumulator chains in flight instead of 2.
+template <int N>
+SMOE_DEVINL void group_mma_n(const uint8_t* const* frag, const int* grp, const uint2* const* btab,
+                             int lane, float* r0, float* r8) {
+    uint2 w[N], v[N];
+#pragma unroll
+    for (int q = 0; q < N; ++q) {
+        w[q] = *reinterpret_cast<const uint2*>(frag[q] + grp[q] * 512 + lane * 8);
+        v[q] = *reinterpret_cast<const uint2*>(frag[q] + grp[q] * 512 + 256 + lane * 8);
+    }
+    float d[N][2][4];
+#pragma unroll
+    for (int q = 0; q < N; ++q)
+#pragma unroll
+        for (int z = 0; z < 4; ++z) d[q][0][z] = d[q][1][z] = 0.f;
+    const uint32_t M = 0x000F000Fu, OR = 0x43004300u;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+#pragma unroll
+            for (int q = 0; q < N; ++q) {
+                const uint32_t g8 = (i ? w[q].y : w[q].x) >> (8 * h), h8 = (i ? v[q].y : v[q].x) >> (8 * h);
+                uint32_t a[4];
+                a[0] = lop3_and_or(g8, M, OR);
+                a[1] = lop3_and_or(h8, M, OR);
+                a[2] = lop3_and_or(g8 >> 4, M, OR);
+                a[3] = lop3_and_or(h8 >> 4, M, OR);
+                uint2 b = make_uint2(0u, 0u);
+                if (lane < 8) b = btab[q][(grp[q] * 4 + i * 2 + h) * 8 + lane];
+                const uint32_t bb[2] = {b.x, b.y};
+                mma_bf16_16816(d[q][h], a, bb);
+            }
+        }
+    }
+#pragma unroll
+    for (int q = 0; q < N; ++q) {
+        r0[q] = (d[q][0][0] + d[q][0][1]) + (d[q][1][0] + d[q][1][1]);
+        r8[q] = (d[q][0][2] + d[q][0][3]) + (d[q][1][2] + d[q][1][3]);
+    }
+}
+
 template <int FMT>
 SMOE_DEVINL float group_epi(float dsum, float vsum, const uint16_t* sc, const uint16_t* bi, int idx) {
     const float qv = fmaf(-128.0f, vsum, dsum);
@@ -254,8 +299,8 @@ struct FusedArgs {
     uint32_t E;
     int norm;
     float* logits;             // scratch [ntok x E]
-    uint2* htab_g;             // scratch: h B-tables [ntok*k][dff/16][8]
-    float* hsum_g;             // scratch: quarter sums [ntok*k][dff/64][4]
+    uint4* htab_g;             // scratch: tagged h B-tables [ntok*k][dff/16][8] {w0,tag,w1,tag}
+    uint2* hsum_g;             // scratch: tagged quarter sums [ntok*k][dff/64][4] {sum,tag}
     unsigned long long* trace; // optional [grid x 8] phase timestamps (ns), null in production
     int dbg_skip;              // profiling experiment: 1 = consumers skip the phase-A math
     int a_bound[kFusedMaxGrid + 1];   // CTA c owns A units [a_bound[c], a_bound[c+1])
@@ -267,8 +312,8 @@ inline void fused_partition(const FusedGeom& g, int G, int* a_bound) {
     a_bound[G] = g.nA;
 }
 
-SMOE_DEVINL void trace_mark(unsigned long long* tr, int i) {
-    if (tr && threadIdx.x == 0) {
+SMOE_DEVINL void trace_mark(unsigned long long* tr, int i, bool who = threadIdx.x == 0) {
+    if (tr && who) {
         unsigned long long t;
         asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
         tr[blockIdx.x * 8 + i] = t;
@@ -287,10 +332,32 @@ SMOE_DEVINL SlotW expert_ptrs(const FfnArgs& a, uint32_t e) {
     return w;
 }
 
+// Tagged 8-byte stores/loads: each 64-bit word {data, tag} is written and
+// read in one single-copy-atomic access, so a reader that sees the current
+// tag also sees the data, with no fence on the writer side (the scheme of
+// NCCL's LL protocol).
+SMOE_DEVINL void st_tagged2(uint4* p, uint2 v, uint32_t tag) {
+    asm volatile("st.global.v2.u64 [%0], {%1, %2};" ::"l"(p),
+                 "l"((uint64_t(tag) << 32) | v.x), "l"((uint64_t(tag) << 32) | v.y) : "memory");
+}
+SMOE_DEVINL void st_tagged1(uint2* p, float v, uint32_t tag) {
+    asm volatile("st.global.u64 [%0], %1;" ::"l"(p), "l"((uint64_t(tag) << 32) | __float_as_uint(v)) : "memory");
+}
+SMOE_DEVINL uint4 ld_tagged2(const uint4* p) {
+    uint64_t a, b;
+    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p));
+    return make_uint4(uint32_t(a), uint32_t(a >> 32), uint32_t(b), uint32_t(b >> 32));
+}
+SMOE_DEVINL uint2 ld_tagged1(const uint2* p) {
+    uint64_t a;
+    asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(a) : "l"(p));
+    return make_uint2(uint32_t(a), uint32_t(a >> 32));
+}
+
 SMOE_DEVINL bool spin_until_geq(const uint32_t* p, uint32_t target) {
     for (uint32_t i = 0; i < SMOE_SPIN_LIMIT; ++i) {
         if (ld_volatile_u32(p) >= target) return true;
-        if (i > 32) __nanosleep(32);
+        if (i > 32) __nanosleep(i > 256 ? 256 : 64);
     }
     return false;
 }

@@ -70,6 +70,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
     const uint32_t nslots = uint32_t(g.ntok * k);
 
     trace_mark(A.trace, 0);
+    const uint32_t tag = ld_volatile_u32(&A.st->epoch) + 1u;    // this launch's h-table tag
     if (tid == 0) {
         for (int i = 0; i < NS; ++i) {
             mbar_init(full + i, 1);
@@ -162,28 +163,12 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
         }
     } else if (warp == kFusedPubWarp) {
         // ---------------------------------------------------- publisher
-        // Reduces each phase-A unit over the 16 consumer warps, writes its
-        // 16 h rows as B-table entries + quarter sum; publishes a token's
-        // units with one fence and one counter update once they are all
-        // written (phase B needs every unit of the token anyway).
-        uint32_t pending = 0;
-        int pending_tok = -1;
-        auto publish = [&]() {
-            __syncwarp();
-            if (pending && lane == 0) {
-                if (A.dbg_skip != 2) __threadfence();
-                atomicAdd(&A.st->hdone[pending_tok], pending);
-            }
-            __syncwarp();
-            pending = 0;
-        };
+        // Reduces each phase-A unit over the 16 consumer warps and writes its
+        // 16 h rows as tagged B-table entries + tagged quarter sum. Readers
+        // validate the tags, so no fence or counter is needed.
         for (int u = sh.a0; u < sh.a1; ++u) {
             const int i = u - sh.a0, b = i % kFusedRedBufs;
-            const int slot = u / g.tilesA, tile = u % g.tilesA, tok = slot / k;
-            if (tok != pending_tok) {
-                publish();
-                pending_tok = tok;
-            }
+            const int slot = u / g.tilesA, tile = u % g.tilesA;
             if (!mbar_wait_bounded(pub_full + b, (i / kFusedRedBufs) & 1))
                 atomicExch(f.err, SMOE_DEVERR_MBAR_TIMEOUT);
             const float* rb = red + b * kFusedConsumers * 32;
@@ -198,7 +183,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
             const int grp = tile >> 2, c = tile & 3;                  // rows = lane quarter c of grp
             if (lane < 8) {
                 const int s = lane >> 1, col = lane & 1;
-                A.htab_g[(size_t(slot) * (dff / 16) + grp * 4 + s) * 8 + col * 4 + c] = btab_entry(hq, s, col);
+                st_tagged2(A.htab_g + (size_t(slot) * (dff / 16) + grp * 4 + s) * 8 + col * 4 + c,
+                           btab_entry(hq, s, col), tag);
             }
             float qs = 0.f;                                           // quarter sum of hi + lo
             if (lane < 16) {
@@ -208,10 +194,12 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
             }
 #pragma unroll
             for (int o = 8; o > 0; o >>= 1) qs += __shfl_xor_sync(0xffffffffu, qs, o);
-            if (lane == 0) A.hsum_g[(size_t(slot) * g.Gd + grp) * 4 + c] = qs;
-            ++pending;
+            if (lane == 0) {
+                st_tagged1(A.hsum_g + (size_t(slot) * g.Gd + grp) * 4 + c, qs, tag);
+                atomicAdd(&A.st->hcount[slot / k], 1u);   // a hint for readers, no ordering implied
+            }
+            __syncwarp();
         }
-        publish();
     } else {
         // ----------------------------------------------------- consumers
         const int ctid = tid, gr = lane >> 2;
@@ -229,18 +217,33 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
             const int nsc = tg.scA / 2;
             const uint2* bt = xtab + tok * (d / 16) * 8;
             float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
-#pragma unroll 2
-            for (int grp = warp; grp < (A.dbg_skip == 1 ? 0 : g.G); grp += kFusedConsumers) {
+            const int ng = (A.dbg_skip == 1) ? 0 : g.G;
+            int grp = warp;
+            for (; grp + kFusedConsumers < ng; grp += 2 * kFusedConsumers) {      // 4 group-mats at once
+                const uint8_t* fr[4] = {sp, sp + tg.fragA, sp, sp + tg.fragA};
+                const int gp[4] = {grp, grp, grp + kFusedConsumers, grp + kFusedConsumers};
+                const uint2* bts[4] = {bt, bt, bt, bt};
+                float r0[4], r8[4];
+                group_mma_n<4>(fr, gp, bts, lane, r0, r8);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int m = q & 1, gq = gp[q];
+                    const float xs = xg[tok * g.G + gq];
+                    acc[m][0] += group_epi<FMT>(r0[q], xs, sb + m * nsc, sb + (2 + m) * nsc, gq * 16 + gr);
+                    acc[m][1] += group_epi<FMT>(r8[q], xs, sb + m * nsc, sb + (2 + m) * nsc, gq * 16 + gr + 8);
+                }
+            }
+            for (; grp < ng; grp += kFusedConsumers) {                              // remainder
+                const uint8_t* fr[2] = {sp, sp + tg.fragA};
+                const int gp[2] = {grp, grp};
+                const uint2* bts[2] = {bt, bt};
+                float r0[2], r8[2];
+                group_mma_n<2>(fr, gp, bts, lane, r0, r8);
                 const float xs = xg[tok * g.G + grp];
-                float r[2][2];
-                group_mma_bf16(sp, grp, bt, lane, r[0][0], r[0][1]);
-                group_mma_bf16(sp + tg.fragA, grp, bt, lane, r[1][0], r[1][1]);
 #pragma unroll
                 for (int m = 0; m < 2; ++m) {
-                    const uint16_t* sc = sb + m * nsc;
-                    const uint16_t* bi = sb + (2 + m) * nsc;
-                    acc[m][0] += group_epi<FMT>(r[m][0], xs, sc, bi, grp * 16 + gr);
-                    acc[m][1] += group_epi<FMT>(r[m][1], xs, sc, bi, grp * 16 + gr + 8);
+                    acc[m][0] += group_epi<FMT>(r0[m], xs, sb + m * nsc, sb + (2 + m) * nsc, grp * 16 + gr);
+                    acc[m][1] += group_epi<FMT>(r8[m], xs, sb + m * nsc, sb + (2 + m) * nsc, grp * 16 + gr + 8);
                 }
             }
             __syncwarp();
@@ -261,34 +264,58 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
         // phase B: down projection of the token's k slots + combine
         for (int v = sh.b0; v < sh.b1; ++v) {
             const int tok = v / g.tilesB, tile = v % g.tilesB;
-            if (ctid == 0 && !spin_until_geq(&A.st->hdone[tok], uint32_t(k * g.tilesA)))
+            // cheap gate: one thread polls the token's counter; the tags below
+            // remain the proof that each entry is this launch's data
+            if (ctid == 0 && !spin_until_geq(&A.st->hcount[tok], uint32_t(k * g.tilesA)))
                 atomicExch(f.err, SMOE_DEVERR_SPIN_TIMEOUT);
             consumer_sync();
             trace_mark(A.trace, 4);
-            {   // finished h tables of this token's k slots: one round of wide loads
-                const uint4* src = reinterpret_cast<const uint4*>(A.htab_g + size_t(tok) * k * (dff / 16) * 8);
-                uint4* dst = reinterpret_cast<uint4*>(htab);
-                const int n16 = k * (dff / 16) * 4;                 // uint4 count
-                uint4 tmp[6];
+            {   // h tables of the token's k slots, tag-validated, into shared memory
+                const int sl0 = tok * k;
+                const uint4* src = A.htab_g + size_t(sl0) * (dff / 16) * 8;
+                const int n16 = k * (dff / 16) * 8;
+                uint4 t[6];
 #pragma unroll
                 for (int q = 0; q < 6; ++q) {
                     const int ii = ctid + q * kFusedCThreads;
-                    if (ii < n16) tmp[q] = __ldcg(src + ii);
+                    if (ii < n16) t[q] = ld_tagged2(src + ii);
                 }
-                float hs[4] = {0.f, 0.f, 0.f, 0.f};
-                const int ng = k * g.Gd;
-                if (ctid < ng) {
-                    const float4 qq = __ldcg(reinterpret_cast<const float4*>(A.hsum_g) + size_t(tok) * ng + ctid);
-                    hs[0] = qq.x; hs[1] = qq.y; hs[2] = qq.z; hs[3] = qq.w;
-                }
+                const int ngs = k * g.Gd * 4;
+                uint2 hsv = make_uint2(0u, tag);
+                if (ctid < ngs) hsv = ld_tagged1(A.hsum_g + size_t(sl0) * g.Gd * 4 + ctid);
 #pragma unroll
                 for (int q = 0; q < 6; ++q) {
                     const int ii = ctid + q * kFusedCThreads;
-                    if (ii < n16) dst[ii] = tmp[q];
+                    if (ii < n16) {
+                        for (uint32_t it = 0; (t[q].y != tag || t[q].w != tag); ++it) {
+                            if (it > SMOE_SPIN_LIMIT) { atomicExch(f.err, SMOE_DEVERR_SPIN_TIMEOUT); break; }
+                            if (it > 32) __nanosleep(32);
+                            t[q] = ld_tagged2(src + ii);
+                        }
+                        htab[ii] = make_uint2(t[q].x, t[q].z);
+                    }
                 }
-                for (int ii = ctid + 6 * kFusedCThreads; ii < n16; ii += kFusedCThreads) dst[ii] = __ldcg(src + ii);
-                if (ctid < ng) hg[ctid] = (hs[0] + hs[1]) + (hs[2] + hs[3]);
+                for (int ii = ctid + 6 * kFusedCThreads; ii < n16; ii += kFusedCThreads) {
+                    uint4 tt = ld_tagged2(src + ii);
+                    for (uint32_t it = 0; (tt.y != tag || tt.w != tag); ++it) {
+                        if (it > SMOE_SPIN_LIMIT) { atomicExch(f.err, SMOE_DEVERR_SPIN_TIMEOUT); break; }
+                        if (it > 32) __nanosleep(32);
+                        tt = ld_tagged2(src + ii);
+                    }
+                    htab[ii] = make_uint2(tt.x, tt.z);
+                }
+                for (int ii = ctid; ii < ngs; ii += kFusedCThreads) {
+                    if (ii != ctid) hsv = ld_tagged1(A.hsum_g + size_t(sl0) * g.Gd * 4 + ii);
+                    for (uint32_t it = 0; hsv.y != tag; ++it) {
+                        if (it > SMOE_SPIN_LIMIT) { atomicExch(f.err, SMOE_DEVERR_SPIN_TIMEOUT); break; }
+                        if (it > 32) __nanosleep(32);
+                        hsv = ld_tagged1(A.hsum_g + size_t(sl0) * g.Gd * 4 + ii);
+                    }
+                    vst[ii] = __uint_as_float(hsv.x);       // quarter sums (x staging is free now)
+                }
             }
+            consumer_sync();
+            if (ctid < k * g.Gd) hg[ctid] = (vst[4 * ctid] + vst[4 * ctid + 1]) + (vst[4 * ctid + 2] + vst[4 * ctid + 3]);
             consumer_sync();
             trace_mark(A.trace, 5);
             for (int ch = 0; ch < g.chunksB; ++ch, ++n) {
@@ -304,13 +331,30 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
                     const uint8_t* tp = sp + jj * tg.tileB;
                     const uint16_t* sc = reinterpret_cast<const uint16_t*>(tp + tg.fragB);
                     const uint16_t* bi = sc + tg.scB / 2;
-#pragma unroll 3
-                    for (int grp = quarter; grp < g.Gd; grp += 4) {
-                        float r0, r8;
-                        group_mma_bf16(tp, grp, htab + j * (dff / 16) * 8, lane, r0, r8);
+                    const uint2* hb = htab + j * (dff / 16) * 8;
+                    int grp = quarter;
+                    for (; grp + 8 < g.Gd; grp += 12) {                     // 3 groups at once
+                        const uint8_t* fr[3] = {tp, tp, tp};
+                        const int gp[3] = {grp, grp + 4, grp + 8};
+                        const uint2* bts[3] = {hb, hb, hb};
+                        float r0[3], r8[3];
+                        group_mma_n<3>(fr, gp, bts, lane, r0, r8);
+#pragma unroll
+                        for (int q = 0; q < 3; ++q) {
+                            const float hs = hg[j * g.Gd + gp[q]];
+                            y0 += group_epi<FMT>(r0[q], hs, sc, bi, gp[q] * 16 + gr);
+                            y8 += group_epi<FMT>(r8[q], hs, sc, bi, gp[q] * 16 + gr + 8);
+                        }
+                    }
+                    for (; grp < g.Gd; grp += 4) {
+                        const uint8_t* fr[1] = {tp};
+                        const int gp[1] = {grp};
+                        const uint2* bts[1] = {hb};
+                        float r0[1], r8[1];
+                        group_mma_n<1>(fr, gp, bts, lane, r0, r8);
                         const float hs = hg[j * g.Gd + grp];
-                        y0 += group_epi<FMT>(r0, hs, sc, bi, grp * 16 + gr);
-                        y8 += group_epi<FMT>(r8, hs, sc, bi, grp * 16 + gr + 8);
+                        y0 += group_epi<FMT>(r0[0], hs, sc, bi, grp * 16 + gr);
+                        y8 += group_epi<FMT>(r8[0], hs, sc, bi, grp * 16 + gr + 8);
                     }
                 }
                 if (ch == 0) trace_mark(A.trace, 2);
@@ -343,9 +387,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
         __threadfence();
         const uint32_t old = atomicAdd(&A.st->done, 1u);
         if (old == gridDim.x - 1) {
-            for (int t = 0; t < kFusedMaxTok; ++t) A.st->hdone[t] = 0;
             A.st->rdone = 0;
             A.st->done = 0;
+            for (int t = 0; t < kFusedMaxTok; ++t) A.st->hcount[t] = 0;
+            A.st->epoch = tag;                   // next launch tags with tag + 1
             __threadfence();
         }
     }

@@ -187,8 +187,9 @@ int launch_fused(SmoeCudaCtx* c, smoe::FfnArgs& f, int fmt, const uint16_t* rw, 
     A.E = E;
     A.norm = norm;
     A.logits = c->logits;
-    A.htab_g = reinterpret_cast<uint2*>(c->hidden);      // [slots][dff/16][8] uint2 = 4*dff B per slot
-    A.hsum_g = c->hidden + size_t(smoe::kFusedMaxTok) * smoe::kFusedMaxK * c->cfg.max_d_ff;
+    // tagged tables: 8*dff bytes per slot, then tagged sums (zeroed at init: tag 0 never matches)
+    A.htab_g = reinterpret_cast<uint4*>(c->hidden);
+    A.hsum_g = reinterpret_cast<uint2*>(c->hidden + size_t(smoe::kFusedMaxTok) * smoe::kFusedMaxK * 2 * c->cfg.max_d_ff);
     A.trace = c->trace;
     A.dbg_skip = (c->trace && std::getenv("SMOE_DEBUG_MODE")) ? std::atoi(std::getenv("SMOE_DEBUG_MODE")) : 0;
     if (c->num_sms > smoe::kFusedMaxGrid) return SMOE_ERR_UNSUPPORTED;
@@ -290,6 +291,7 @@ SmoeCudaCtx* smoe_cuda_init_ex(const SmoeCudaInitArgs* args) {
     if ((e = cudaMalloc(&c->gemv_out, c->gemv_cap * 4)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->gemv_in, size_t(a.max_d_model) * 4)) != cudaSuccess) return fail(e);
     cudaMemsetAsync(c->ticket, 0, size_t(a.max_batch) * 4, c->stream);
+    cudaMemsetAsync(c->hidden, 0, slots * a.max_d_ff * 4, c->stream);
     cudaMemsetAsync(c->err, 0, 4, c->stream);
     for (auto& ev : c->events)
         if ((e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming)) != cudaSuccess) return fail(e);
