@@ -6,17 +6,23 @@
 //   1. repetition penalty over the last 256 history ids, each distinct
 //      non-exempt id once, in place (sampler.hpp:42-70), written back;
 //   2. greedy argmax when T < 1e-4, lowest index on ties (sampler.hpp:73-83);
-//   3. max, then sum of exp((s - max)/T) (sampler.hpp:86-129);
-//   4. top-K candidates by penalised score via a 4 x 8-bit radix select
-//      (K = max(top_k,1) <= 1024; the score order is the probability order),
-//      ties at the threshold taken lowest index first;
-//   5. CTA 0 sorts the K candidates (score desc, index asc), evaluates their
-//      probabilities with a double-precision exp rounded to float, and walks
-//      the top-p / top-k cutoff and the draw with the reference's float
-//      operations (sampler.hpp:132-156).
+//   3. max, then e = exp((s - max)/T) for every entry, correctly rounded
+//      (double-precision evaluation), and the reference's sequential fp32
+//      sum of all e reproduced exactly (seqsum.cuh) (sampler.hpp:86-129);
+//   4. top-K candidates by e via a 4 x 8-bit radix select (K = max(top_k,1)
+//      <= 1024), ties at the threshold taken lowest index first;
+//   5. CTA 0 sorts the K candidates (e desc, index asc) and walks the top-p /
+//      top-k cutoff and the draw with the reference's float operations
+//      (sampler.hpp:132-156).
+// Bit-exactness: token ids equal the reference's whenever each e equals
+// glibc's expf result; glibc's expf is within 0.502 ulp (measured here:
+// it differs from the correctly rounded value on 6.3e-4 of random inputs),
+// and ties between equal e values are ordered by index here and unspecified
+// in the reference's heap + sort.
 #pragma once
 #include <cooperative_groups.h>
 #include "smoe_common.cuh"
+#include "seqsum.cuh"
 
 namespace smoe {
 namespace cg = cooperative_groups;
@@ -35,7 +41,16 @@ struct SamplerArgs {
     const uint32_t* hist;
     uint32_t hstride;
     uint32_t* tokens;
+    unsigned long long* trace;   // optional [8 x 8] phase timestamps of row 0 (profiling aid)
 };
+
+SMOE_DEVINL void samp_mark(unsigned long long* tr, int i) {
+    if (tr && threadIdx.x == 0 && blockIdx.y == 0) {
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        tr[blockIdx.x * 8 + i] = t;
+    }
+}
 
 constexpr int kSampCluster = 8;
 constexpr int kSampThreads = 1024;
@@ -118,6 +133,7 @@ k_sample(SamplerArgs a) {
     __shared__ double redd[32];
     __shared__ uint32_t redu[32];
     __shared__ SampPub pub;
+    __shared__ SeqShared seqsh;
     __shared__ uint32_t sel_prefix, sel_krem;
 
     cg::cluster_group cl = cg::this_cluster();
@@ -130,10 +146,14 @@ k_sample(SamplerArgs a) {
     const uint32_t lo = min(V, rank * L);
     const uint32_t n = min(V - lo, L);
     float* s = reinterpret_cast<float*>(smem_raw);
+    // per-warp radix histograms [32][256] after the slice
+    uint32_t (*whist)[256] = reinterpret_cast<uint32_t (*)[256]>(smem_raw + size_t(L) * 4);
     float* lg = a.logits + size_t(row) * V;
 
+    samp_mark(a.trace, 0);
     for (uint32_t i = tid; i < n; i += kSampThreads) s[i] = lg[lo + i];
     __syncthreads();
+    samp_mark(a.trace, 1);
 
     // ---- 1. repetition penalty (sampler.hpp:42-70)
     if (P.rep_penalty != 1.0f) {
@@ -203,12 +223,25 @@ k_sample(SamplerArgs a) {
         const float s0 = *cl.map_shared_rank(s, 0);
         if (s0 != s0) mx = s0;
     }
+    cl.sync();     // every CTA has read rank 0's s[0] before any e overwrites it
     const float T = P.temperature;
-    double dsum = 0.0;
-    for (uint32_t i = tid; i < n; i += kSampThreads)
-        dsum += (double)expf(__fdiv_rn(__fsub_rn(s[i], mx), T));
-    dsum = block_reduce(dsum, redd, [](double x, double y) { return x + y; });
-    if (tid == 0) pub.dsum = dsum;
+    // e_v = exp((s_v - max) / T), correctly rounded, in place of s; then the
+    // reference's sequential fp32 sum of all e_v, reproduced exactly
+    const uint32_t C = (L + kSampThreads - 1) / kSampThreads;
+    {
+        const uint32_t c0 = min(n, tid * C), cnt = min(n, c0 + C) - c0;
+        float v[kSeqMaxC];                       // independent evaluations, unrolled for ILP
+#pragma unroll
+        for (int q = 0; q < kSeqMaxC; ++q)
+            if (q < (int)cnt) v[q] = (float)exp_neg_d((double)__fdiv_rn(__fsub_rn(s[c0 + q], mx), T));
+#pragma unroll
+        for (int q = 0; q < kSeqMaxC; ++q)
+            if (q < (int)cnt) s[c0 + q] = v[q];
+    }
+    __syncthreads();
+    samp_mark(a.trace, 2);
+    seq_sum_cluster(cl, s, n, L, V, C, &seqsh, a.trace);
+    samp_mark(a.trace, 3);
 
     // ---- 4. radix select of the K-th largest score key
     uint32_t K = P.top_k < 1u ? 1u : P.top_k;
@@ -218,11 +251,18 @@ k_sample(SamplerArgs a) {
     for (int pass = 0; pass < 4; ++pass) {
         const int shift = 24 - 8 * pass;
         uint32_t* hh = hist[pass & 1];
-        if (tid < 256) hh[tid] = 0;
-        __syncthreads();
+        uint32_t* wh = whist[tid >> 5];
+        for (int b = tid & 31; b < 256; b += 32) wh[b] = 0;
+        __syncwarp();
         for (uint32_t i = tid; i < n; i += kSampThreads) {
             const uint32_t key = score_key(s[i]);
-            if ((key & mask) == prefix) atomicAdd(&hh[(key >> shift) & 255u], 1u);
+            if ((key & mask) == prefix) atomicAdd(&wh[(key >> shift) & 255u], 1u);
+        }
+        __syncthreads();
+        if (tid < 256) {
+            uint32_t t = 0;
+            for (int w = 0; w < kSampThreads / 32; ++w) t += whist[w][tid];
+            hh[tid] = t;
         }
         cl.sync();
         if (tid < 256) {
@@ -247,6 +287,7 @@ k_sample(SamplerArgs a) {
         mask |= 255u << shift;
     }
     const uint32_t thr = prefix;   // key of the K-th largest; krem ties to take
+    samp_mark(a.trace, 4);
 
     // ---- collect candidates into CTA 0 (contiguous chunk per thread keeps
     // the tie order = index order)
@@ -264,11 +305,9 @@ k_sample(SamplerArgs a) {
     if (tid == 0) { pub.n_gt = cta_gt; pub.n_eq = cta_eq; }
     cl.sync();
     uint32_t all_gt = 0, gt_before = 0, eq_before = 0;
-    double total = 0.0;
     for (int r = 0; r < kSampCluster; ++r) {
         const SampPub* o = cl.map_shared_rank(&pub, r);
         all_gt += o->n_gt;
-        total += o->dsum;
         if (r < rank) { gt_before += o->n_gt; eq_before += o->n_eq; }
     }
     unsigned long long* cand0 = cl.map_shared_rank(cand, 0);
@@ -286,6 +325,7 @@ k_sample(SamplerArgs a) {
         }
     }
     cl.sync();
+    samp_mark(a.trace, 5);
     if (rank != 0) return;       // CTA 0's shared memory is no longer read remotely
 
     // ---- 5. sort (score desc, index asc) and walk
@@ -306,12 +346,10 @@ k_sample(SamplerArgs a) {
             __syncthreads();
         }
     }
-    const float sum_exp = (float)total;
-    const float inv_sum = 1.0f / sum_exp;
+    samp_mark(a.trace, 6);
+    const float inv_sum = __fdiv_rn(1.0f, seqsh.result);
     for (uint32_t i = tid; i < K; i += kSampThreads) {
-        const float sc = key_score(uint32_t(cand[i] >> 32));
-        const float arg = __fdiv_rn(__fsub_rn(sc, mx), T);
-        const float e = (float)exp_neg_d((double)arg);
+        const float e = key_score(uint32_t(cand[i] >> 32));    // keys are the e values
         probs[i] = __fmul_rn(e, inv_sum);
     }
     __syncthreads();
@@ -332,11 +370,12 @@ k_sample(SamplerArgs a) {
         }
         a.tokens[row] = tok;
     }
+    samp_mark(a.trace, 7);
 }
 
 inline size_t sampler_smem_bytes(uint32_t V) {
     const uint32_t L = (((V + kSampCluster - 1) / kSampCluster) + 3u) & ~3u;
-    return size_t(L) * 4;
+    return size_t(L) * 4 + size_t(kSampThreads / 32) * 256 * 4;
 }
 
 }  // namespace smoe

@@ -640,14 +640,15 @@ int smoe_cuda_moe_layer(SmoeCudaCtx* c, const SmoeMoeLayer* L, const void* x, in
 int smoe_cuda_sample(SmoeCudaCtx* c, float* logits, uint32_t vocab, uint32_t batch,
                      const SmoeSamplerRow* rows, const uint32_t* history, uint32_t hstride,
                      uint32_t* tokens) {
-    if (!c || !logits || !rows || !tokens || vocab == 0 || vocab > c->cfg.max_vocab || batch == 0 ||
+    if (!c || !logits || !rows || !tokens || vocab == 0 || vocab > c->cfg.max_vocab ||
+        vocab > uint32_t(smoe::kSampCluster) * smoe::kSampThreads * smoe::kSeqMaxC || batch == 0 ||
         batch > 65535u || (hstride && !history)) {
         set_err("bad sampler arguments %s%ld", "", (long)vocab);
         return SMOE_ERR_ARG;
     }
     static_assert(sizeof(SmoeSamplerRow) == sizeof(smoe::SamplerRowDev), "row layout");
     smoe::SamplerArgs a{logits, vocab, reinterpret_cast<const smoe::SamplerRowDev*>(rows),
-                        history, hstride, tokens};
+                        history, hstride, tokens, c->trace};
     const size_t smem = smoe::sampler_smem_bytes(vocab);
     int rc = prep_kernel(c, smoe::k_sample, smem);
     if (rc) return rc;
