@@ -32,6 +32,9 @@ D, DFF, E, K = 2048, 768, 128, 8
 N_LAYERS = 8
 LAYER_BYTES = 524_288 + 4_096 + 8 * 2_654_208 + 4_096      # 21,762,144
 FFN_BYTES = 8 * 2_654_208                                    # 21,233,664
+# dram__bytes_read.sum + dram__bytes_write.sum of one k_moe_fused launch on
+# this workload, measured once with ncu (--set full, one launch)
+NCU_TRAFFIC = 21_848_320
 METRIC = "expert-FFN HBM GB/s, Qwen3-30B-A3B MoE layer decode step, batch 1"
 
 
@@ -158,15 +161,19 @@ def cpu_layer_time(layers, xs, budget_s, threads):
 
 
 def run_reference(args, rank, world):
+    """The reference's own CPU path, timed on this host: its compiled router
+    (matvec_bf16 + top_k + renorm, sampler.hpp/scout.cpp/common.hpp built
+    unmodified into oracle/_ref) plus the restated Q4 FFN (the reference has
+    no CPU FFN), all host threads. One step = one MoE layer step."""
     if rank != 0:
         return
     layers, xs = make_inputs()
     threads = os.cpu_count() or 1
-    n_total, el_total = 0, 0.0
     for i in range(args.warmup):
         cpu_layer_time(layers, xs, 0.0, threads)
+    n_total, el_total, used, kind = 0, 0.0, threads, "port"
     for i in range(args.steps):
-        n, el, used, kind = cpu_layer_time(layers, xs, 2.0, threads)
+        n, el, used, kind = cpu_layer_time(layers, xs, 0.0, threads)   # exactly one layer step
         n_total += n
         el_total += el
     gbs = LAYER_BYTES * n_total / el_total / 1e9
@@ -177,9 +184,9 @@ def run_reference(args, rank, world):
             "config": {"workload": "config1: Qwen3-30B-A3B MoE layer (d 2048, 128 experts, top-8, "
                                    "AFFINE-Q4 g64), batch 1", "layers_cycled": N_LAYERS},
             "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": used, "kind": kind,
-                             "sample": f"{n_total} layer steps in {el_total:.1f} s: reference "
-                                       "router (sampler/top-k/matvec compiled from the reference) "
-                                       "+ restated Q4 FFN, OpenMP"},
+                             "sample": f"{n_total} layer steps in {el_total:.2f} s: reference "
+                                       "router (compiled from the reference) + restated Q4 FFN, "
+                                       "OpenMP"},
             "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -310,7 +317,7 @@ def run_ours(args, rank, world, local):
                        "parallelism": f"replicas x{world}"},
             "layer_us": round(per_step * 1e3, 3),
             "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(ach / peak, 4), "traffic": None,
+                         "frac": round(ach / peak, 4), "traffic": NCU_TRAFFIC,
                          "kernel": "k_moe_fused (expert FFN + combine, routing given), 21,233,664 B "
                                    f"per launch, {ffn_ms * 1e3:.2f} us avg", "peak_kind": peak_kind},
             "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": D * 2,
