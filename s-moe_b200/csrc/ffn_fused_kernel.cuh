@@ -1,7 +1,35 @@
-// ffn_fused_kernel.cuh - the persistent MoE-layer kernel (design notes in
-// ffn_fused.cuh).
+// ffn_fused_kernel.cuh - the persistent fused MoE-layer kernel (sm_100a).
+//
+// One launch, one CTA per SM, does a whole MoE layer of a decode
+// step for up to kFusedMaxTok tokens:
+//   routing (optional): router logit rows spread over the grid, then every
+//     CTA runs the softmax / top-k / renorm of router.cuh on all logits;
+//   units (slot j, hidden rows 16t..16t+15) split evenly over the CTAs, each
+//     computing  h = silu(Wg.x) * (Wu.x) * w_j  for its 16 rows and at once
+//     its share of the down projection, W_down[:, 16t..16t+15] . h, into a
+//     per-CTA fp32 partial output in shared memory (split-K down: no unit
+//     waits for another CTA);
+//   each CTA adds its partial outputs to a global fp32 accumulator with
+//   vector reductions; the last CTA to finish writes y and clears the
+//   accumulator, so consecutive launches need no host work.
+// Warp 17 (producer) streams every byte the CTA will use - each unit is one
+// contiguous block of the tiled layout (tiled.cuh), plus the down scales of
+// a 64-row group when the unit starts one - into a ring of shared-memory
+// stages with 1-D bulk copies, the first ones before the CTA's first barrier;
+// sixteen consumer warps run the gate/up dots as integer MMAs on the raw
+// codes and the down slice as bf16 MMAs (arithmetic in ffn_fused.cuh); warp
+// 16 turns each unit's partial sums into h.
+// Note: the fp32 reductions make the sum over units order-dependent in its
+// last bits (results within 1e-6 relative of each other run to run).
 #pragma once
 #include "ffn_fused.cuh"
+
+// cycle counters of the phases, for profiling builds only (-DSMOE_FUSED_PROFILE)
+#ifdef SMOE_FUSED_PROFILE
+#define SMOE_PROF(...) __VA_ARGS__
+#else
+#define SMOE_PROF(...)
+#endif
 
 namespace smoe {
 
@@ -42,7 +70,14 @@ SMOE_DEVINL float router_row(const FusedArgs& A, uint32_t t, uint32_t e, int cti
     return acc;
 }
 
-template <int FMT>
+SMOE_DEVINL void red_add_v4(float* p, float4 v) {
+    asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(v.x), "f"(v.y),
+                 "f"(v.z), "f"(v.w)
+                 : "memory");
+}
+
+// GW: 64-groups of the gate/up rows per consumer warp, ceil(d_model / 1024)
+template <int FMT, int GW>
 __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
     extern __shared__ __align__(1024) uint8_t sm[];
     const FusedGeom& g = A.g;
@@ -51,38 +86,66 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const bool consumer = warp < kFusedConsumers;
     uint8_t* ring = sm + g.o_ring;
-    uint2* xtab = reinterpret_cast<uint2*>(sm + g.o_xtab);
-    float* xg = reinterpret_cast<float*>(sm + g.o_xg);
-    uint2* htab = reinterpret_cast<uint2*>(sm + g.o_htab);
-    float* hg = reinterpret_cast<float*>(sm + g.o_hg);
-    float* red = reinterpret_cast<float*>(sm + g.o_red);       // [kFusedRedBufs][16 warps][32]
-    float* redB = reinterpret_cast<float*>(sm + g.o_yslot);    // [4 chunks][16 warps][32]
-    float* hq = reinterpret_cast<float*>(sm + g.o_hq);
+    uint4* xtab = reinterpret_cast<uint4*>(sm + g.o_xtab);
+    float2* xg = reinterpret_cast<float2*>(sm + g.o_xg);
+    float* ysum = reinterpret_cast<float*>(sm + g.o_ysum);     // [ntok][d]; earlier x staging / softmax scratch
+    uint16_t* sbc0 = reinterpret_cast<uint16_t*>(sm + g.o_sbc); // [2][down sc[d] (+ bias[d])] by group parity
+    float* red0 = reinterpret_cast<float*>(sm + g.o_red);       // [2][16 warps][32]
     uint64_t* full = reinterpret_cast<uint64_t*>(sm + g.o_bar);
     uint64_t* empty = full + 16;
-    uint64_t* pub_full = full + 32;
-    uint64_t* pub_empty = pub_full + kFusedRedBufs;
+    uint64_t* redF = full + 32;                                 // [2] partial sums written (16 arrivals)
+    uint64_t* hR = full + 34;                                   // [2] h ready (1 arrival)
     uint32_t* s_ids = reinterpret_cast<uint32_t*>(sm + g.o_ids);
     float* s_w = reinterpret_cast<float*>(sm + g.o_w);
-    float* ps = reinterpret_cast<float*>(sm + g.o_ps);
-    float* vst = reinterpret_cast<float*>(sm + g.o_vst);
-    const int NS = g.nstages, k = g.k, d = g.d, dff = g.dff;
+    float* red = red0;                                          // routing uses buffer 0
+    const int NS = g.nstages, k = g.k, d = g.d;
     const uint32_t nslots = uint32_t(g.ntok * k);
+    __shared__ uint32_t last_cta;
 
     trace_mark(A.trace, 0);
-    const uint32_t tag = ld_volatile_u32(&A.st->epoch) + 1u;    // this launch's h-table tag
+    SMOE_PROF(if (A.trace && tid == 0) A.trace[gridDim.x * 32 + blockIdx.x * 8 + 4] = clock64();)
+    // inputs (x, routing) may come from the previous kernel in the stream
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int u0 = int(blockIdx.x * uint32_t(g.nU) / gridDim.x);          // nU * grid < 2^31
+    const int u1 = int((blockIdx.x + 1) * uint32_t(g.nU) / gridDim.x);
+    auto needs_sb = [&](int u) { return u == u0 || (u % g.tilesU) % 4 == 0; };
+    // copy of unit u (the n-th of this CTA) into its stage: one bulk copy, plus
+    // the down scales of the 64-row group it starts (producer lane 0)
+    auto issue = [&](int u, int n) {
+        const int st = n % NS, slot = u / g.tilesU, t = u % g.tilesU;
+        const bool sb = needs_sb(u);
+        const uint8_t* ex = f.base + uint64_t(s_ids[slot]) * f.stride;
+        mbar_arrive_expect_tx(full + st, tg.unit + (sb ? tg.dgroup : 0));
+        bulk_g2s(ring + size_t(st) * g.stage, ex + tg.unit_off(t), tg.unit, full + st);
+        if (sb) bulk_g2s(sbc0 + ((u / 4) & 1) * (tg.dgroup / 2), ex + tg.group_off(t / 4), tg.dgroup, full + st);
+        if (n < 3) trace_mark(A.trace, 25 + n, true);
+    };
     if (tid == 0) {
         for (int i = 0; i < NS; ++i) {
             mbar_init(full + i, 1);
             mbar_init(empty + i, kFusedConsumers);
         }
-        for (int i = 0; i < kFusedRedBufs; ++i) {
-            mbar_init(pub_full + i, kFusedConsumers);
-            mbar_init(pub_empty + i, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(redF + b, kFusedConsumers);
+            mbar_init(hR + b, 1);
         }
         fence_mbar_init();
     }
     __syncthreads();
+    int pre = 0;                                                // units issued ahead of the main loop
+    if (!A.rw && warp == kFusedProdWarp) {
+        // routing given: read it and start the weight stream at once
+        for (uint32_t i = lane; i < nslots; i += 32) s_ids[i] = f.ids[i];
+        __syncwarp();
+        pre = min(NS, u1 - u0);
+        if (lane == 0)
+            for (int n = 0; n < pre; ++n) issue(u0 + n, n);
+        __syncwarp();
+    } else if (!A.rw && warp == kFusedHWarp) {
+        for (uint32_t i = lane; i < nslots; i += 32) s_w[i] = f.wts[i];
+        __syncwarp();
+    }
+    trace_mark(A.trace, 8);
 
     // ---------------------------------------------------------- routing
     if (A.rw) {
@@ -102,17 +165,22 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
             __syncthreads();
         }
     }
-    // x: one round of wide loads, finished before any weight copy is issued
-    // (loads issued behind this SM's bulk traffic would wait for all of it)
+    // x table (consumers): one round of wide loads, then the table in shared memory
     if (consumer) {
-        if (f.x_dtype == 0) stage_vec_smem<false>(f.x, g.ntok * d, vst, tid);
-        else stage_vec_smem<true>(f.x, g.ntok * d, vst, tid);
+        if (f.x_dtype == 0) stage_vec_smem<false>(f.x, g.ntok * d, ysum, tid);
+        else stage_vec_smem<true>(f.x, g.ntok * d, ysum, tid);
+        consumer_sync();
+        trace_mark(A.trace, 9);
+        build_xplanes<FMT>(ysum, g.ntok, d, xtab, xg, tid);
+
+        consumer_sync();
+        trace_mark(A.trace, 10);                             // x staging (ysum) is reused below
     }
     if (A.rw) {
         if (tid == 0 && !spin_until_geq(&A.st->rdone, A.E * g.ntok)) atomicExch(f.err, SMOE_DEVERR_SPIN_TIMEOUT);
-        __syncthreads();
+        __syncthreads();      // (x tables are complete here too)
         if (warp < g.ntok) {
-            warp_topk(A.logits + size_t(warp) * A.E, A.E, k, A.norm, ps + warp * kRouterMaxE,
+            warp_topk(A.logits + size_t(warp) * A.E, A.E, k, A.norm, ysum + warp * kRouterMaxE,
                       s_ids + warp * k, s_w + warp * k, lane);
             __syncwarp();
             if (blockIdx.x == 0 && lane < k) {
@@ -120,280 +188,292 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
                 const_cast<float*>(f.wts)[warp * k + lane] = s_w[warp * k + lane];
             }
         }
-    } else {
-        for (uint32_t i = tid; i < nslots; i += blockDim.x) {
-            s_ids[i] = f.ids[i];
-            s_w[i] = f.wts[i];
-        }
+        __syncthreads();
     }
-    __syncthreads();
     trace_mark(A.trace, 1);
-
-    const FusedShare sh{A.a_bound[blockIdx.x], A.a_bound[blockIdx.x + 1],
-                        int(blockIdx.x * g.nB / gridDim.x), int((blockIdx.x + 1) * g.nB / gridDim.x)};
 
     if (warp == kFusedProdWarp) {
         // ------------------------------------------------------ producer
-        int n = 0;
-        auto acquire = [&](int stage_n, uint32_t bytes) -> uint8_t* {
-            const int st = stage_n % NS, round = stage_n / NS;
+        for (int u = u0 + pre, n = pre; u < u1; ++u, ++n) {
+            const int st = n % NS, round = n / NS;
             if (round > 0 && lane == 0 && !mbar_wait_bounded(empty + st, (round - 1) & 1))
                 atomicExch(f.err, SMOE_DEVERR_MBAR_TIMEOUT);
+            if (lane == 0) issue(u, n);
             __syncwarp();
-            if (lane == 0) mbar_arrive_expect_tx(full + st, bytes);
-            __syncwarp();
-            return ring + size_t(st) * g.stage;
-        };
-        for (int u = sh.a0; u < sh.a1; ++u, ++n) {
-            const int slot = u / g.tilesA, tile = u % g.tilesA;
-            uint8_t* sp = acquire(n, tg.tileA);
-            if (lane == 0)
-                bulk_g2s(sp, f.base + uint64_t(s_ids[slot]) * f.stride + tg.a_tile(tile), tg.tileA, full + n % NS);
         }
-        for (int v = sh.b0; v < sh.b1; ++v) {
-            const int tok = v / g.tilesB, tile = v % g.tilesB;
-            for (int ch = 0; ch < g.chunksB; ++ch, ++n) {
-                const int j0 = ch * kFusedSlotsPerB, nj = min(kFusedSlotsPerB, k - j0);
-                uint8_t* sp = acquire(n, nj * tg.tileB);
-                if (lane < nj)
-                    bulk_g2s(sp + lane * tg.tileB,
-                             f.base + uint64_t(s_ids[tok * k + j0 + lane]) * f.stride + tg.b_tile(tile), tg.tileB,
-                             full + n % NS);
-            }
-        }
-    } else if (warp == kFusedPubWarp) {
-        // ---------------------------------------------------- publisher
-        // Reduces each phase-A unit over the 16 consumer warps and writes its
-        // 16 h rows as tagged B-table entries + tagged quarter sum. Readers
-        // validate the tags, so no fence or counter is needed.
-        for (int u = sh.a0; u < sh.a1; ++u) {
-            const int i = u - sh.a0, b = i % kFusedRedBufs;
-            const int slot = u / g.tilesA, tile = u % g.tilesA;
-            if (!mbar_wait_bounded(pub_full + b, (i / kFusedRedBufs) & 1))
-                atomicExch(f.err, SMOE_DEVERR_MBAR_TIMEOUT);
-            const float* rb = red + b * kFusedConsumers * 32;
-            float acc = 0.f;                                          // lane = (matrix, row)
+    } else if (warp == kFusedHWarp) {
+        // ---------------------------------------------------------- h warp
+        SMOE_PROF(if (A.trace) for (int n = 0; n < 3 && n < u1 - u0; ++n) { mbar_wait_bounded(full + n, 0); trace_mark(A.trace, 28 + n, lane == 0); })
+        for (int u = u0, n = 0; u < u1; ++u, ++n) {
+            const int b = n & 1, slot = u / g.tilesU;
+            if (!mbar_wait_bounded(redF + b, (n >> 1) & 1)) atomicExch(f.err, SMOE_DEVERR_MBAR_TIMEOUT);
+            const float* rb = red0 + b * kFusedConsumers * 32;
+            float* hq = reinterpret_cast<float*>(sm + g.o_hq + b * 256);
+            uint2* dB = reinterpret_cast<uint2*>(sm + g.o_hq + b * 256 + 64);
+            float* hsum = reinterpret_cast<float*>(sm + g.o_hq + b * 256 + 128);
+            float v = 0.f;                                        // lane = (matrix, row)
 #pragma unroll
-            for (int w = 0; w < kFusedConsumers; ++w) acc += rb[w * 32 + lane];
+            for (int w = 0; w < kFusedConsumers; ++w) v += rb[w * 32 + lane];
+            const float up = __shfl_down_sync(0xffffffffu, v, 16);
+            if (lane < 16) hq[lane] = v * (1.0f / (1.0f + expf(-v))) * up * s_w[slot];   // kernels.metal:61-63
             __syncwarp();
-            if (lane == 0) mbar_arrive(pub_empty + b);                // red buffer b is free again
-            const float up = __shfl_down_sync(0xffffffffu, acc, 16);
-            if (lane < 16) hq[lane] = acc * (1.0f / (1.0f + expf(-acc))) * up;   // kernels.metal:61-63
-            __syncwarp();
-            const int grp = tile >> 2, c = tile & 3;                  // rows = lane quarter c of grp
-            if (lane < 8) {
-                const int s = lane >> 1, col = lane & 1;
-                st_tagged2(A.htab_g + (size_t(slot) * (dff / 16) + grp * 4 + s) * 8 + col * 4 + c,
-                           btab_entry(hq, s, col), tag);
-            }
-            float qs = 0.f;                                           // quarter sum of hi + lo
+            float part = 0.f;
             if (lane < 16) {
                 const float hv = hq[lane];
                 const float hi = __bfloat162float(__float2bfloat16_rn(hv));
-                qs = hi + __bfloat162float(__float2bfloat16_rn(hv - hi));
+                part = hi + __bfloat162float(__float2bfloat16_rn(hv - hi));
             }
 #pragma unroll
-            for (int o = 8; o > 0; o >>= 1) qs += __shfl_xor_sync(0xffffffffu, qs, o);
-            if (lane == 0) {
-                st_tagged1(A.hsum_g + (size_t(slot) * g.Gd + grp) * 4 + c, qs, tag);
-                atomicAdd(&A.st->hcount[slot / k], 1u);   // a hint for readers, no ordering implied
+            for (int o = 8; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+            if (lane == 0) *hsum = part;
+            if (lane < 8) {                                       // standard B layout: k 2c,2c+1 / 2c+8,2c+9
+                const int c = lane & 3, col = lane >> 2;
+                float e[4] = {hq[2 * c], hq[2 * c + 1], hq[2 * c + 8], hq[2 * c + 9]};
+                if (col) {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) e[q] -= __bfloat162float(__float2bfloat16_rn(e[q]));
+                }
+                dB[lane] = make_uint2(pack_bf16x2(e[0], e[1]), pack_bf16x2(e[2], e[3]));
             }
             __syncwarp();
+            if (lane == 0) mbar_arrive(hR + b);
+            if (n == 0) trace_mark(A.trace, 12, lane == 0);
         }
     } else {
         // ----------------------------------------------------- consumers
-        const int ctid = tid, gr = lane >> 2;
-        build_btab_bf16(vst, g.ntok, d, xtab, xg, ctid);
+        // step n: gate/up of unit n, then the down slice of unit n-1 (whose h
+        // the h warp computed meanwhile)
+        const int gr = lane >> 2;
+        for (int i = tid; i < g.ntok * d; i += kFusedCThreads) ysum[i] = 0.f;
         consumer_sync();
-        int n = 0;
-        // phase A: gate/up dots of each unit -> reduction buffer -> publisher
-        for (int u = sh.a0; u < sh.a1; ++u, ++n) {
-            const int i = u - sh.a0, b = i % kFusedRedBufs;
-            const int st = n % NS;
-            const int slot = u / g.tilesA, tok = slot / k;
-            if (!mbar_wait_bounded(full + st, (n / NS) & 1)) atomicExch(f.err, SMOE_DEVERR_MBAR_TIMEOUT);
-            const uint8_t* sp = ring + size_t(st) * g.stage;
-            const uint16_t* sb = reinterpret_cast<const uint16_t*>(sp + 2 * tg.fragA);   // [gsc][usc][gbi][ubi]
-            const int nsc = tg.scA / 2;
-            const uint2* bt = xtab + tok * (d / 16) * 8;
-            float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
-            const int ng = (A.dbg_skip == 1) ? 0 : g.G;
-            int grp = warp;
-            for (; grp + kFusedConsumers < ng; grp += 2 * kFusedConsumers) {      // 4 group-mats at once
-                const uint8_t* fr[4] = {sp, sp + tg.fragA, sp, sp + tg.fragA};
-                const int gp[4] = {grp, grp, grp + kFusedConsumers, grp + kFusedConsumers};
-                const uint2* bts[4] = {bt, bt, bt, bt};
-                float r0[4], r8[4];
-                group_mma_n<4>(fr, gp, bts, lane, r0, r8);
+        trace_mark(A.trace, 2);
+        const int cq = lane & 3;                         // token whose results this lane holds
+        // Down projection, split-K: this CTA's units are consecutive (slot,
+        // 16 hidden rows) blocks, so four of them in a row share one 64-column
+        // quantisation group of W_down. Warp w owns output tiles w + 16q; for
+        // q < kDownRegTiles the raw MMA sums stay in registers for the whole
+        // group (the epilogue is linear in the dot and the h sum) and are
+        // scaled into the token's shared-memory partial output once per
+        // group. Tiles beyond those (d_model > 2048) take the scale per unit.
+        float dacc[kDownRegTiles][4], hsg = 0.f;
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const int m = q & 1, gq = gp[q];
-                    const float xs = xg[tok * g.G + gq];
-                    acc[m][0] += group_epi<FMT>(r0[q], xs, sb + m * nsc, sb + (2 + m) * nsc, gq * 16 + gr);
-                    acc[m][1] += group_epi<FMT>(r8[q], xs, sb + m * nsc, sb + (2 + m) * nsc, gq * 16 + gr + 8);
+        for (int q = 0; q < kDownRegTiles; ++q) dacc[q][0] = dacc[q][1] = dacc[q][2] = dacc[q][3] = 0.f;
+        const uint32_t M = 0x000F000Fu, OR = 0x43004300u;
+        SMOE_PROF(long long cy_wait = 0, cy_gu = 0, cy_hw = 0, cy_dn = 0, cy_t = 0;)
+        auto down = [&](int u, int n) {
+            const int b = n & 1, st = n % NS, tok = (u / g.tilesU) / k, t = u % g.tilesU;
+            SMOE_PROF(cy_t = clock64();)
+            if (!mbar_wait_bounded(hR + b, (n >> 1) & 1)) atomicExch(f.err, SMOE_DEVERR_MBAR_TIMEOUT);
+            SMOE_PROF(cy_hw += clock64() - cy_t; cy_t = clock64();)
+            const uint8_t* sp = ring + size_t(st) * g.stage;
+            const uint32_t* sl = reinterpret_cast<const uint32_t*>(sp + tg.gateup);
+            const uint2* dB = reinterpret_cast<const uint2*>(sm + g.o_hq + b * 256 + 64);
+            const uint2 bv = lane < 8 ? dB[lane] : make_uint2(0u, 0u);
+            const uint32_t bb[2] = {bv.x, bv.y};
+            const float hs = *reinterpret_cast<const float*>(sm + g.o_hq + b * 256 + 128);
+            const uint16_t* dsc = sbc0 + ((u / 4) & 1) * (tg.dgroup / 2);
+            const uint16_t* dbi = dsc + d;
+            float* yt = ysum + tok * d;
+#pragma unroll
+            for (int q = 0; q < kDownRegTiles; ++q) {
+                const int o = warp + q * kFusedConsumers;
+                if (o < g.outTiles) {
+                    const uint32_t w = sl[o * 32 + lane];
+                    uint32_t a[4];
+                    a[0] = lop3_and_or(w, M, OR);
+                    a[1] = lop3_and_or(w >> 4, M, OR);
+                    a[2] = lop3_and_or(w >> 8, M, OR);
+                    a[3] = lop3_and_or(w >> 12, M, OR);
+                    mma_bf16_16816(dacc[q], a, bb);
                 }
             }
-            for (; grp < ng; grp += kFusedConsumers) {                              // remainder
-                const uint8_t* fr[2] = {sp, sp + tg.fragA};
-                const int gp[2] = {grp, grp};
-                const uint2* bts[2] = {bt, bt};
-                float r0[2], r8[2];
-                group_mma_n<2>(fr, gp, bts, lane, r0, r8);
-                const float xs = xg[tok * g.G + grp];
-#pragma unroll
-                for (int m = 0; m < 2; ++m) {
-                    acc[m][0] += group_epi<FMT>(r0[m], xs, sb + m * nsc, sb + (2 + m) * nsc, grp * 16 + gr);
-                    acc[m][1] += group_epi<FMT>(r8[m], xs, sb + m * nsc, sb + (2 + m) * nsc, grp * 16 + gr + 8);
+            for (int o = warp + kDownRegTiles * kFusedConsumers; o < g.outTiles; o += kFusedConsumers) {
+                float dd[4] = {0.f, 0.f, 0.f, 0.f};
+                const uint32_t w = sl[o * 32 + lane];
+                uint32_t a[4];
+                a[0] = lop3_and_or(w, M, OR);
+                a[1] = lop3_and_or(w >> 4, M, OR);
+                a[2] = lop3_and_or(w >> 8, M, OR);
+                a[3] = lop3_and_or(w >> 12, M, OR);
+                mma_bf16_16816(dd, a, bb);
+                if ((lane & 3) == 0) {
+                    const int r0 = o * 16 + gr, r8 = r0 + 8;
+                    yt[r0] += group_epi<FMT>(dd[0] + dd[1], hs, dsc, dbi, r0);
+                    yt[r8] += group_epi<FMT>(dd[2] + dd[3], hs, dsc, dbi, r8);
                 }
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(empty + st);
-            if (i >= kFusedRedBufs && !mbar_wait_bounded(pub_empty + b, ((i / kFusedRedBufs) - 1) & 1))
-                atomicExch(f.err, SMOE_DEVERR_MBAR_TIMEOUT);
-            float* rb = red + (b * kFusedConsumers + warp) * 32;
-            if ((lane & 3) == 0) {
+            if (lane == 0) mbar_arrive(empty + st);           // stage of unit n fully consumed
+            if (n < 3) trace_mark(A.trace, 22 + n);
+            hsg += hs;
+            SMOE_PROF(cy_dn += clock64() - cy_t;)
+            const bool last = (u + 1 == u1);
+            if (last || (t & 3) == 3) {
+                // group ends: scale once per group and add into the token's
+                // partial output. All shared-memory loads of the flush are
+                // issued before any store (the compiler cannot prove that the
+                // stores to yt do not alias the scale loads).
+                if ((lane & 3) == 0) {
+#pragma unroll
+                    for (int q0 = 0; q0 < kDownRegTiles; q0 += 4) {      // 4 tiles: 24 loads in flight
+                        float sv[4][2], bi[4][2], yv[4][2];
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            const int o = min(warp + (q0 + q) * kFusedConsumers, g.outTiles - 1);
+                            const int r0 = o * 16 + gr;
+#pragma unroll
+                            for (int h = 0; h < 2; ++h) {
+                                if (FMT == kFmtAffine) {
+                                    sv[q][h] = bf16_bits_to_f32(dsc[r0 + 8 * h]);
+                                    bi[q][h] = bf16_bits_to_f32(dbi[r0 + 8 * h]);
+                                } else {
+                                    sv[q][h] = f16_bits_to_f32(dsc[r0 + 8 * h]);
+                                    bi[q][h] = 0.f;
+                                }
+                                yv[q][h] = yt[r0 + 8 * h];
+                            }
+                        }
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            const int o = warp + (q0 + q) * kFusedConsumers;
+                            if (o < g.outTiles) {
+#pragma unroll
+                                for (int h = 0; h < 2; ++h) {
+                                    const float dsum = dacc[q0 + q][2 * h] + dacc[q0 + q][2 * h + 1];
+                                    const float qv = fmaf(-128.0f, hsg, dsum);
+                                    const float v = (FMT == kFmtAffine) ? sv[q][h] * qv + bi[q][h] * hsg
+                                                                        : sv[q][h] * (qv * (1.0f / 7.5f) - hsg);
+                                    yt[o * 16 + gr + 8 * h] = yv[q][h] + v;
+                                }
+                            }
+                        }
+                    }
+                }
+#pragma unroll
+                for (int q = 0; q < kDownRegTiles; ++q) dacc[q][0] = dacc[q][1] = dacc[q][2] = dacc[q][3] = 0.f;
+                hsg = 0.f;
+            }
+        };
+        for (int u = u0, n = 0; u < u1; ++u, ++n) {
+            const int st = n % NS, b = n & 1;
+            const int slot = u / g.tilesU, tok = slot / k;
+            SMOE_PROF(cy_t = clock64();)
+            if (!mbar_wait_bounded(full + st, (n / NS) & 1)) atomicExch(f.err, SMOE_DEVERR_MBAR_TIMEOUT);
+            SMOE_PROF(cy_wait += clock64() - cy_t; cy_t = clock64();)
+            if (n < 3) trace_mark(A.trace, 16 + n);
+            const uint8_t* sp = ring + size_t(st) * g.stage;
+            // -- gate / up dots of the unit's 16 rows: groups warp + 16j
+            const uint8_t* sbp = sp + 2 * tg.fragA;              // [gate sb][up sb]
+            float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+            uint4 w[GW][2];
+#pragma unroll
+            for (int j = 0; j < GW; ++j) {
+                const int grp = min(warp + j * kFusedConsumers, g.G - 1);
+#pragma unroll
+                for (int m = 0; m < 2; ++m)
+                    w[j][m] = *reinterpret_cast<const uint4*>(sp + m * tg.fragA + (grp * 32 + lane) * 16);
+            }
+#pragma unroll
+            for (int j = 0; j < GW; ++j) {
+                const int grp = warp + j * kFusedConsumers;
+                if (grp < g.G) {
+                    const float2 xv = xg[grp * 4 + cq];
+                    const uint4 bA = xtab[(grp * 2) * 32 + lane], bB = xtab[(grp * 2 + 1) * 32 + lane];
+                    const uint32_t be[2] = {bA.x, bA.y}, bo[2] = {bA.z, bA.w};
+                    const uint32_t be2[2] = {bB.x, bB.y}, bo2[2] = {bB.z, bB.w};
+#pragma unroll
+                    for (int m = 0; m < 2; ++m) {
+                        const uint32_t ae[4] = {w[j][m].x & 0x0F0F0F0Fu, w[j][m].y & 0x0F0F0F0Fu,
+                                                w[j][m].z & 0x0F0F0F0Fu, w[j][m].w & 0x0F0F0F0Fu};
+                        const uint32_t ao[4] = {w[j][m].x & 0xF0F0F0F0u, w[j][m].y & 0xF0F0F0F0u,
+                                                w[j][m].z & 0xF0F0F0F0u, w[j][m].w & 0xF0F0F0F0u};
+                        int de[4] = {0, 0, 0, 0}, dO[4] = {0, 0, 0, 0}, de2[4] = {0, 0, 0, 0}, dO2[4] = {0, 0, 0, 0};
+                        mma_u8s8_16832(de, ae, be);
+                        mma_u8s8_16832(dO, ao, bo);
+                        mma_u8s8_16832(de2, ae, be2);
+                        mma_u8s8_16832(dO2, ao, bo2);
+                        const float v0 = fmaf(float(16 * de2[0] + dO2[0]), 65536.0f,
+                                              float((16 * de[0] + dO[0]) + 256 * (16 * de[1] + dO[1])));
+                        const float v8 = fmaf(float(16 * de2[2] + dO2[2]), 65536.0f,
+                                              float((16 * de[2] + dO[2]) + 256 * (16 * de[3] + dO[3])));
+                        if (FMT == kFmtAffine) {
+                            const uint32_t* sbw = reinterpret_cast<const uint32_t*>(sbp + m * tg.sbA) + grp * 16 + gr;
+                            const uint32_t s0 = sbw[0], s8 = sbw[8];
+                            acc[m][0] += fmaf(bf16_bits_to_f32(uint16_t(s0)), v0 * xv.x,
+                                              bf16_bits_to_f32(uint16_t(s0 >> 16)) * xv.y);
+                            acc[m][1] += fmaf(bf16_bits_to_f32(uint16_t(s8)), v8 * xv.x,
+                                              bf16_bits_to_f32(uint16_t(s8 >> 16)) * xv.y);
+                        } else {
+                            const uint16_t* sbh = reinterpret_cast<const uint16_t*>(sbp + m * tg.sbA) + grp * 16 + gr;
+                            acc[m][0] += f16_bits_to_f32(sbh[0]) * fmaf(v0, xv.x, -xv.y);
+                            acc[m][1] += f16_bits_to_f32(sbh[8]) * fmaf(v8, xv.x, -xv.y);
+                        }
+                    }
+                }
+            }
+            float* rb = red0 + (b * kFusedConsumers + warp) * 32;
+            if (cq == tok) {
                 rb[gr] = acc[0][0];
                 rb[gr + 8] = acc[0][1];
                 rb[16 + gr] = acc[1][0];
                 rb[16 + gr + 8] = acc[1][1];
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(pub_full + b);
+            if (lane == 0) mbar_arrive(redF + b);
+            SMOE_PROF(cy_gu += clock64() - cy_t;)
+            if (n < 3) trace_mark(A.trace, 19 + n);
+            if (n > 0) down(u - 1, n - 1);
         }
+        if (u1 > u0) down(u1 - 1, u1 - u0 - 1);
         trace_mark(A.trace, 3);
-        // phase B: down projection of the token's k slots + combine
-        for (int v = sh.b0; v < sh.b1; ++v) {
-            const int tok = v / g.tilesB, tile = v % g.tilesB;
-            // cheap gate: one thread polls the token's counter; the tags below
-            // remain the proof that each entry is this launch's data
-            if (ctid == 0 && !spin_until_geq(&A.st->hcount[tok], uint32_t(k * g.tilesA)))
-                atomicExch(f.err, SMOE_DEVERR_SPIN_TIMEOUT);
-            consumer_sync();
-            trace_mark(A.trace, 4);
-            {   // h tables of the token's k slots, tag-validated, into shared memory
-                const int sl0 = tok * k;
-                const uint4* src = A.htab_g + size_t(sl0) * (dff / 16) * 8;
-                const int n16 = k * (dff / 16) * 8;
-                uint4 t[6];
-#pragma unroll
-                for (int q = 0; q < 6; ++q) {
-                    const int ii = ctid + q * kFusedCThreads;
-                    if (ii < n16) t[q] = ld_tagged2(src + ii);
-                }
-                const int ngs = k * g.Gd * 4;
-                uint2 hsv = make_uint2(0u, tag);
-                if (ctid < ngs) hsv = ld_tagged1(A.hsum_g + size_t(sl0) * g.Gd * 4 + ctid);
-#pragma unroll
-                for (int q = 0; q < 6; ++q) {
-                    const int ii = ctid + q * kFusedCThreads;
-                    if (ii < n16) {
-                        for (uint32_t it = 0; (t[q].y != tag || t[q].w != tag); ++it) {
-                            if (it > SMOE_SPIN_LIMIT) { atomicExch(f.err, SMOE_DEVERR_SPIN_TIMEOUT); break; }
-                            if (it > 32) __nanosleep(32);
-                            t[q] = ld_tagged2(src + ii);
-                        }
-                        htab[ii] = make_uint2(t[q].x, t[q].z);
-                    }
-                }
-                for (int ii = ctid + 6 * kFusedCThreads; ii < n16; ii += kFusedCThreads) {
-                    uint4 tt = ld_tagged2(src + ii);
-                    for (uint32_t it = 0; (tt.y != tag || tt.w != tag); ++it) {
-                        if (it > SMOE_SPIN_LIMIT) { atomicExch(f.err, SMOE_DEVERR_SPIN_TIMEOUT); break; }
-                        if (it > 32) __nanosleep(32);
-                        tt = ld_tagged2(src + ii);
-                    }
-                    htab[ii] = make_uint2(tt.x, tt.z);
-                }
-                for (int ii = ctid; ii < ngs; ii += kFusedCThreads) {
-                    if (ii != ctid) hsv = ld_tagged1(A.hsum_g + size_t(sl0) * g.Gd * 4 + ii);
-                    for (uint32_t it = 0; hsv.y != tag; ++it) {
-                        if (it > SMOE_SPIN_LIMIT) { atomicExch(f.err, SMOE_DEVERR_SPIN_TIMEOUT); break; }
-                        if (it > 32) __nanosleep(32);
-                        hsv = ld_tagged1(A.hsum_g + size_t(sl0) * g.Gd * 4 + ii);
-                    }
-                    vst[ii] = __uint_as_float(hsv.x);       // quarter sums (x staging is free now)
-                }
-            }
-            consumer_sync();
-            if (ctid < k * g.Gd) hg[ctid] = (vst[4 * ctid] + vst[4 * ctid + 1]) + (vst[4 * ctid + 2] + vst[4 * ctid + 3]);
-            consumer_sync();
-            trace_mark(A.trace, 5);
-            for (int ch = 0; ch < g.chunksB; ++ch, ++n) {
-                const int st = n % NS;
-                const int j0 = ch * kFusedSlotsPerB, nj = min(kFusedSlotsPerB, k - j0);
-                if (!mbar_wait_bounded(full + st, (n / NS) & 1)) atomicExch(f.err, SMOE_DEVERR_MBAR_TIMEOUT);
-                if (ch == 0) trace_mark(A.trace, 7);
-                const uint8_t* sp = ring + size_t(st) * g.stage;
-                const int jj = warp >> 2, quarter = warp & 3;
-                float y0 = 0.f, y8 = 0.f;
-                if (jj < nj) {
-                    const int j = j0 + jj;
-                    const uint8_t* tp = sp + jj * tg.tileB;
-                    const uint16_t* sc = reinterpret_cast<const uint16_t*>(tp + tg.fragB);
-                    const uint16_t* bi = sc + tg.scB / 2;
-                    const uint2* hb = htab + j * (dff / 16) * 8;
-                    int grp = quarter;
-                    for (; grp + 8 < g.Gd; grp += 12) {                     // 3 groups at once
-                        const uint8_t* fr[3] = {tp, tp, tp};
-                        const int gp[3] = {grp, grp + 4, grp + 8};
-                        const uint2* bts[3] = {hb, hb, hb};
-                        float r0[3], r8[3];
-                        group_mma_n<3>(fr, gp, bts, lane, r0, r8);
-#pragma unroll
-                        for (int q = 0; q < 3; ++q) {
-                            const float hs = hg[j * g.Gd + gp[q]];
-                            y0 += group_epi<FMT>(r0[q], hs, sc, bi, gp[q] * 16 + gr);
-                            y8 += group_epi<FMT>(r8[q], hs, sc, bi, gp[q] * 16 + gr + 8);
-                        }
-                    }
-                    for (; grp < g.Gd; grp += 4) {
-                        const uint8_t* fr[1] = {tp};
-                        const int gp[1] = {grp};
-                        const uint2* bts[1] = {hb};
-                        float r0[1], r8[1];
-                        group_mma_n<1>(fr, gp, bts, lane, r0, r8);
-                        const float hs = hg[j * g.Gd + grp];
-                        y0 += group_epi<FMT>(r0[0], hs, sc, bi, grp * 16 + gr);
-                        y8 += group_epi<FMT>(r8[0], hs, sc, bi, grp * 16 + gr + 8);
-                    }
-                }
-                if (ch == 0) trace_mark(A.trace, 2);
-                __syncwarp();
-                if (lane == 0) mbar_arrive(empty + st);
-                if ((lane & 3) == 0) {
-                    redB[(ch * kFusedConsumers + warp) * 32 + gr] = y0;
-                    redB[(ch * kFusedConsumers + warp) * 32 + gr + 8] = y8;
-                }
-            }
-            consumer_sync();
-            if (ctid < 16) {
-                float o = 0.f;     // routed[i] += w * y[i]: product then sum, no FMA (axpy_f32)
-                for (int j = 0; j < k; ++j) {
-                    const float* rj = redB + ((j / kFusedSlotsPerB) * kFusedConsumers + (j % kFusedSlotsPerB) * 4) * 32;
-                    const float yj = (rj[ctid] + rj[32 + ctid]) + (rj[64 + ctid] + rj[96 + ctid]);
-                    o = __fadd_rn(o, __fmul_rn(s_w[tok * k + j], yj));
-                }
-                const size_t oi = size_t(tok) * d + tile * 16 + ctid;
-                if (f.y_dtype == 0) static_cast<float*>(f.y)[oi] = o;
-                else static_cast<__nv_bfloat16*>(f.y)[oi] = __float2bfloat16_rn(o);
-            }
+        if (A.trace && lane == 0 && (warp == 0 || warp == 15)) {
+            SMOE_PROF(long long* cy = reinterpret_cast<long long*>(A.trace) + gridDim.x * 40 + blockIdx.x * 8 + (warp ? 4 : 0);)
+            SMOE_PROF(cy[0] = cy_wait; cy[1] = cy_gu; cy[2] = cy_hw; cy[3] = cy_dn;)
         }
     }
 
-    // ------------------------------------------------ finish: reset counters
+    // the next kernel in the stream may start its launch now
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // ---------------- partial outputs: vector reductions into the accumulator
+    if (consumer) {
+        consumer_sync();                             // every warp's share of ysum is written
+        for (int i = tid; i < g.ntok * d / 4; i += kFusedCThreads)
+            red_add_v4(A.acc + 4 * i, reinterpret_cast<const float4*>(ysum)[i]);
+    }
     trace_mark(A.trace, 6);
+
+    // ------------------------------------- last CTA: write y, clear scratch
     __syncthreads();
     if (tid == 0) {
         __threadfence();
-        const uint32_t old = atomicAdd(&A.st->done, 1u);
-        if (old == gridDim.x - 1) {
+        trace_mark(A.trace, 14);
+        last_cta = (atomicAdd(&A.st->done, 1u) == gridDim.x - 1) ? 1u : 0u;
+        trace_mark(A.trace, 15);
+    }
+    __syncthreads();
+    if (last_cta) {
+        __threadfence();
+        for (int i = tid; i < g.ntok * d / 4; i += blockDim.x) {      // d % 64 == 0: whole float4s
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(A.acc) + i);
+            reinterpret_cast<float4*>(A.acc)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (f.y_dtype == 0) {
+                reinterpret_cast<float4*>(f.y)[i] = v;
+            } else {
+                __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+                uint2 o;
+                o.x = *reinterpret_cast<uint32_t*>(&lo);
+                o.y = *reinterpret_cast<uint32_t*>(&hi);
+                reinterpret_cast<uint2*>(f.y)[i] = o;
+            }
+        }
+        if (tid == 0) {
             A.st->rdone = 0;
             A.st->done = 0;
-            for (int t = 0; t < kFusedMaxTok; ++t) A.st->hcount[t] = 0;
-            A.st->epoch = tag;                   // next launch tags with tag + 1
-            __threadfence();
         }
+        __threadfence();
     }
+    trace_mark(A.trace, 7);
+    SMOE_PROF(if (A.trace && tid == 0) A.trace[gridDim.x * 32 + blockIdx.x * 8 + 5] = clock64();)
 }
 
 }  // namespace smoe

@@ -130,7 +130,6 @@ k_sample(SamplerArgs a) {
     __shared__ unsigned long long cand[kSampCand];
     __shared__ float probs[kSampCand];
     __shared__ float redf[32];
-    __shared__ double redd[32];
     __shared__ uint32_t redu[32];
     __shared__ SampPub pub;
     __shared__ SeqShared seqsh;

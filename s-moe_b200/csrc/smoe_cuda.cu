@@ -62,6 +62,9 @@ struct SmoeCudaCtx {
     size_t smem_optin = 0;
     int num_sms = 0;
     smoe::FusedState* fstate = nullptr;
+    float* acc = nullptr;            // fused kernel's output accumulator [kFusedMaxTok][max_d_model]
+    int fused_grid[2][3] = {};       // fused kernel grid per (format, groups per warp)
+    size_t fused_smem_seen[2][3] = {};
     unsigned long long* trace = nullptr;   // phase timestamps of the fused kernel (profiling aid)
 };
 
@@ -173,11 +176,15 @@ int launch_ffn(SmoeCudaCtx* c, smoe::FfnArgs& a, int fmt) {
 // caller can use the two-kernel path.
 int launch_fused(SmoeCudaCtx* c, smoe::FfnArgs& f, int fmt, const uint16_t* rw, uint32_t E,
                  int norm) {
-    if (f.ntok > (uint32_t)smoe::kFusedMaxTok || f.k > (uint32_t)smoe::kFusedMaxK ||
+    if (f.ntok > (uint32_t)smoe::kFusedMaxTok || f.k > (uint32_t)smoe::kFusedMaxK || f.d_model > 4096 ||
         (rw && E > (uint32_t)smoe::kRouterMaxE) || (rw && f.d_model % 8))
         return SMOE_ERR_UNSUPPORTED;
+    if (!aligned16(f.x) || !aligned16(f.y)) {            // whole-vector loads and stores
+        set_err("fused layer kernel needs 16-byte aligned x and y %s%ld", "", 0);
+        return SMOE_ERR_ARG;
+    }
     smoe::FusedArgs A{};
-    A.g.init(fmt, (int)f.d_model, (int)f.d_ff, (int)f.k, (int)f.ntok, (int)c->smem_optin);
+    A.g.init(fmt, (int)f.d_model, (int)f.d_ff, (int)f.k, (int)f.ntok, (int)c->smem_optin - 2048);
     if (A.g.nstages < 2) return SMOE_ERR_UNSUPPORTED;
     f.hidden = c->hidden;
     f.err = c->err;
@@ -187,22 +194,51 @@ int launch_fused(SmoeCudaCtx* c, smoe::FfnArgs& f, int fmt, const uint16_t* rw, 
     A.E = E;
     A.norm = norm;
     A.logits = c->logits;
-    // tagged tables: 8*dff bytes per slot, then tagged sums (zeroed at init: tag 0 never matches)
-    A.htab_g = reinterpret_cast<uint4*>(c->hidden);
-    A.hsum_g = reinterpret_cast<uint2*>(c->hidden + size_t(smoe::kFusedMaxTok) * smoe::kFusedMaxK * 2 * c->cfg.max_d_ff);
+    A.acc = c->acc;                       // [ntok x d] fp32, zeroed at init and by each launch's last CTA
     A.trace = c->trace;
-    A.dbg_skip = (c->trace && std::getenv("SMOE_DEBUG_MODE")) ? std::atoi(std::getenv("SMOE_DEBUG_MODE")) : 0;
-    if (c->num_sms > smoe::kFusedMaxGrid) return SMOE_ERR_UNSUPPORTED;
-    smoe::fused_partition(A.g, c->num_sms, A.a_bound);
     const size_t smem = (size_t)A.g.total;
-    void* kern = fmt == SMOE_FMT_AFFINE_Q4 ? (void*)smoe::k_moe_fused<smoe::kFmtAffine>
-                                           : (void*)smoe::k_moe_fused<smoe::kFmtSmoe>;
-    int rc = fmt == SMOE_FMT_AFFINE_Q4 ? prep_kernel(c, smoe::k_moe_fused<smoe::kFmtAffine>, smem)
-                                       : prep_kernel(c, smoe::k_moe_fused<smoe::kFmtSmoe>, smem);
+    // gate/up groups per consumer warp: d_model <= 1024, 2048, 4096
+    const int gwi = A.g.G <= 16 ? 0 : A.g.G <= 32 ? 1 : 2;
+    using smoe::k_moe_fused;
+    using smoe::kFmtAffine;
+    using smoe::kFmtSmoe;
+    static void* const kerns[2][3] = {
+        {(void*)k_moe_fused<kFmtSmoe, 1>, (void*)k_moe_fused<kFmtSmoe, 2>, (void*)k_moe_fused<kFmtSmoe, 4>},
+        {(void*)k_moe_fused<kFmtAffine, 1>, (void*)k_moe_fused<kFmtAffine, 2>, (void*)k_moe_fused<kFmtAffine, 4>}};
+    const int fi = fmt == SMOE_FMT_AFFINE_Q4 ? 1 : 0;
+    void* kern = kerns[fi][gwi];
+    int rc = prep_kernel(c, kern, smem);
     if (rc) return rc;
+    cudaLaunchConfig_t lc{};
+    lc.blockDim = dim3(smoe::kFusedThreads);
+    lc.dynamicSmemBytes = smem;
+    lc.stream = c->stream;
+    // With a router phase CTAs wait on each other's logits: cooperative
+    // launch (co-residency guaranteed). With the routing given nothing waits,
+    // so a plain launch, marked for programmatic dependent launch so that its
+    // setup overlaps the previous kernel's tail.
+    cudaLaunchAttribute at[1];
+    if (rw) {
+        at[0].id = cudaLaunchAttributeCooperative;
+        at[0].val.cooperative = 1;
+    } else {
+        at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[0].val.programmaticStreamSerializationAllowed = 1;
+    }
+    lc.attrs = at;
+    lc.numAttrs = 1;
+    // one CTA per SM (the shared-memory ring fills an SM); cached per kernel and size
+    int& best = c->fused_grid[fi][gwi];
+    if (best == 0 || c->fused_smem_seen[fi][gwi] != smem) {
+        int per_sm = 0;
+        CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, smoe::kFusedThreads, smem));
+        if (per_sm < 1) { set_err("fused kernel does not fit an SM with %s%ld bytes", "", (long)smem); return SMOE_ERR_CUDA; }
+        best = c->num_sms;
+        c->fused_smem_seen[fi][gwi] = smem;
+    }
+    lc.gridDim = dim3(best);
     void* args[] = {&A};
-    CK(cudaLaunchCooperativeKernel(kern, dim3(c->num_sms), dim3(smoe::kFusedThreads), args, smem,
-                                   c->stream));
+    CK(cudaLaunchKernelExC(&lc, kern, args));
     c->dispatches += 1;
     return SMOE_OK;
 }
@@ -286,6 +322,8 @@ SmoeCudaCtx* smoe_cuda_init_ex(const SmoeCudaInitArgs* args) {
     if ((e = cudaMalloc(&c->ticket, size_t(a.max_batch) * 4)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->err, 4)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->fstate, sizeof(smoe::FusedState))) != cudaSuccess) return fail(e);
+    if ((e = cudaMalloc(&c->acc, size_t(smoe::kFusedMaxTok) * a.max_d_model * 4)) != cudaSuccess) return fail(e);
+    cudaMemsetAsync(c->acc, 0, size_t(smoe::kFusedMaxTok) * a.max_d_model * 4, c->stream);
     cudaMemsetAsync(c->fstate, 0, sizeof(smoe::FusedState), c->stream);
     c->gemv_cap = a.max_vocab > a.max_d_model ? a.max_vocab : a.max_d_model;
     if ((e = cudaMalloc(&c->gemv_out, c->gemv_cap * 4)) != cudaSuccess) return fail(e);
@@ -312,7 +350,7 @@ void smoe_cuda_destroy(SmoeCudaCtx* c) {
     if (c->own_stream) cudaStreamSynchronize(c->own_stream);
     for (auto& ev : c->events)
         if (ev) cudaEventDestroy(ev);
-    void* bufs[] = {c->fstate, c->hidden, c->slot_out, c->in_stage, c->batch_out, c->logits, c->ids,
+    void* bufs[] = {c->fstate, c->acc, c->hidden, c->slot_out, c->in_stage, c->batch_out, c->logits, c->ids,
                     c->wts, c->ticket, c->err, c->gemv_out, c->gemv_in};
     for (void* b : bufs)
         if (b) cudaFree(b);
@@ -691,7 +729,7 @@ int smoe_cuda_prepack_layer(SmoeCudaCtx* c, const SmoeMoeLayer* src, void* dst, 
     p.dst_stride = dst_stride;
     p.fmt = (int)src->fmt;
     p.tg.init((int)src->fmt, src->d_model, src->d_ff);
-    dim3 grid(src->d_ff / 16 + src->d_model / 16, src->n_experts);
+    dim3 grid(src->d_ff / 16 + src->d_ff / 64, src->n_experts);
     smoe::k_prepack<<<grid, 256, 0, c->stream>>>(p);
     CK(cudaGetLastError());
     c->dispatches += 1;

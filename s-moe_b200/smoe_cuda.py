@@ -12,7 +12,7 @@ import ctypes as C
 import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libsmoe_cuda.so")
+LIB_PATH = os.environ.get("SMOE_CUDA_LIB") or os.path.join(HERE, "libsmoe_cuda.so")   # override: another build of the library
 
 SMOE_OK = 0
 STATUS = {0: "OK", 1: "ERR_ARG", 2: "ERR_CUDA", 3: "ERR_TIMEOUT", 4: "ERR_NCCL",
