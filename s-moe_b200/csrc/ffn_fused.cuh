@@ -25,14 +25,20 @@
 
 namespace smoe {
 
-constexpr int kFusedConsumers = 16;                // consumer warps
+#ifndef SMOE_FUSED_CONSUMERS
+#define SMOE_FUSED_CONSUMERS 16
+#endif
+constexpr int kFusedConsumers = SMOE_FUSED_CONSUMERS;   // consumer warps
 constexpr int kFusedCThreads = kFusedConsumers * 32;
 constexpr int kFusedHWarp = kFusedConsumers;        // turns each unit's partial sums into h
 constexpr int kFusedProdWarp = kFusedConsumers + 1; // issues the bulk copies
 constexpr int kFusedThreads = kFusedCThreads + 64;
 constexpr int kFusedMaxTok = 4;
 constexpr int kFusedMaxK = 16;
-constexpr int kDownRegTiles = 8;       // down output tiles per consumer warp kept in registers (d_model <= 2048)
+#ifndef SMOE_DOWN_REG_TILES
+#define SMOE_DOWN_REG_TILES (128 / SMOE_FUSED_CONSUMERS)
+#endif
+constexpr int kDownRegTiles = SMOE_DOWN_REG_TILES;       // down output tiles per consumer warp kept in registers (d_model <= 2048)
 constexpr int kFusedCluster = 4;                   // CTAs that pre-reduce partial outputs together
 
 struct FusedState {          // device scratch, zero at context creation and on exit

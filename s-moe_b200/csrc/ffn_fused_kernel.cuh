@@ -277,7 +277,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
 #pragma unroll
             for (int q = 0; q < kDownRegTiles; ++q) {
                 const int o = warp + q * kFusedConsumers;
+#ifdef SMOE_EXP_NODOWN
+                if (false) {
+#else
                 if (o < g.outTiles) {
+#endif
                     const uint32_t w = sl[o * 32 + lane];
                     uint32_t a[4];
                     a[0] = lop3_and_or(w, M, OR);
@@ -306,7 +310,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
             if (lane == 0) mbar_arrive(empty + st);           // stage of unit n fully consumed
             if (n < 3) trace_mark(A.trace, 22 + n);
             hsg += hs;
-            SMOE_PROF(cy_dn += clock64() - cy_t;)
+            SMOE_PROF(cy_dn += clock64() - cy_t; if (n < 3 && A.trace && lane == 0 && warp == 0) reinterpret_cast<long long*>(A.trace)[gridDim.x * 48 + blockIdx.x * 8 + 4 + n] = clock64() - cy_t;)
             const bool last = (u + 1 == u1);
             if (last || (t & 3) == 3) {
                 // group ends: scale once per group and add into the token's
@@ -354,7 +358,12 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
                 hsg = 0.f;
             }
         };
-        for (int u = u0, n = 0; u < u1; ++u, ++n) {
+        // step n: gate/up of unit n (if any), then the down slice of unit n-1;
+        // one call site each keeps the loop body small (instruction cache)
+        const int nun = u1 - u0;
+        for (int n = 0; n <= nun; ++n) {
+          if (n < nun) {
+            const int u = u0 + n;
             const int st = n % NS, b = n & 1;
             const int slot = u / g.tilesU, tok = slot / k;
             SMOE_PROF(cy_t = clock64();)
@@ -420,11 +429,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(redF + b);
-            SMOE_PROF(cy_gu += clock64() - cy_t;)
+            SMOE_PROF(cy_gu += clock64() - cy_t; if (n < 3 && A.trace && lane == 0 && warp == 0) reinterpret_cast<long long*>(A.trace)[gridDim.x * 48 + blockIdx.x * 8 + n] = clock64() - cy_t;)
             if (n < 3) trace_mark(A.trace, 19 + n);
-            if (n > 0) down(u - 1, n - 1);
+          }
+          if (n > 0) down(u0 + n - 1, n - 1);
         }
-        if (u1 > u0) down(u1 - 1, u1 - u0 - 1);
         trace_mark(A.trace, 3);
         if (A.trace && lane == 0 && (warp == 0 || warp == 15)) {
             SMOE_PROF(long long* cy = reinterpret_cast<long long*>(A.trace) + gridDim.x * 40 + blockIdx.x * 8 + (warp ? 4 : 0);)

@@ -100,12 +100,17 @@ SMOE_DEVINL bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 // Bounded wait; returns false (and the caller raises the error flag) when
 // the phase never completes.
-SMOE_DEVINL bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+// The loop is kept out of line: the many wait sites then add one try_wait
+// and a call each to the hot code instead of a copy of the loop.
+static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity) {
     for (uint32_t i = 0; i < SMOE_SPIN_LIMIT; ++i) {
         if (mbar_try_wait(bar, parity)) return true;   // try_wait itself suspends a while
         if (i > 4096) __nanosleep(64);
     }
     return false;
+}
+SMOE_DEVINL bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+    return mbar_try_wait(bar, parity) || mbar_wait_slow(bar, parity);
 }
 
 // 1-D bulk copy global -> shared, completion counted on `bar` (bytes).

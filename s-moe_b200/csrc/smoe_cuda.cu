@@ -63,8 +63,8 @@ struct SmoeCudaCtx {
     int num_sms = 0;
     smoe::FusedState* fstate = nullptr;
     float* acc = nullptr;            // fused kernel's output accumulator [kFusedMaxTok][max_d_model]
-    int fused_grid[2][3] = {};       // fused kernel grid per (format, groups per warp)
-    size_t fused_smem_seen[2][3] = {};
+    int fused_grid[2][4] = {};       // fused kernel grid per (format, groups per warp)
+    size_t fused_smem_seen[2][4] = {};
     unsigned long long* trace = nullptr;   // phase timestamps of the fused kernel (profiling aid)
 };
 
@@ -197,14 +197,18 @@ int launch_fused(SmoeCudaCtx* c, smoe::FfnArgs& f, int fmt, const uint16_t* rw, 
     A.acc = c->acc;                       // [ntok x d] fp32, zeroed at init and by each launch's last CTA
     A.trace = c->trace;
     const size_t smem = (size_t)A.g.total;
-    // gate/up groups per consumer warp: d_model <= 1024, 2048, 4096
-    const int gwi = A.g.G <= 16 ? 0 : A.g.G <= 32 ? 1 : 2;
+    // gate/up groups per consumer warp (GW = 1, 2, 4, 8)
+    const int gw_need = (A.g.G + smoe::kFusedConsumers - 1) / smoe::kFusedConsumers;
+    const int gwi = gw_need <= 1 ? 0 : gw_need <= 2 ? 1 : gw_need <= 4 ? 2 : 3;
+    if (gw_need > 8) return SMOE_ERR_UNSUPPORTED;
     using smoe::k_moe_fused;
     using smoe::kFmtAffine;
     using smoe::kFmtSmoe;
-    static void* const kerns[2][3] = {
-        {(void*)k_moe_fused<kFmtSmoe, 1>, (void*)k_moe_fused<kFmtSmoe, 2>, (void*)k_moe_fused<kFmtSmoe, 4>},
-        {(void*)k_moe_fused<kFmtAffine, 1>, (void*)k_moe_fused<kFmtAffine, 2>, (void*)k_moe_fused<kFmtAffine, 4>}};
+    static void* const kerns[2][4] = {
+        {(void*)k_moe_fused<kFmtSmoe, 1>, (void*)k_moe_fused<kFmtSmoe, 2>, (void*)k_moe_fused<kFmtSmoe, 4>,
+         (void*)k_moe_fused<kFmtSmoe, 8>},
+        {(void*)k_moe_fused<kFmtAffine, 1>, (void*)k_moe_fused<kFmtAffine, 2>, (void*)k_moe_fused<kFmtAffine, 4>,
+         (void*)k_moe_fused<kFmtAffine, 8>}};
     const int fi = fmt == SMOE_FMT_AFFINE_Q4 ? 1 : 0;
     void* kern = kerns[fi][gwi];
     int rc = prep_kernel(c, kern, smem);
