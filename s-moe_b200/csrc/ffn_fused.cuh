@@ -171,7 +171,7 @@ struct FusedGeom {
     TiledGeom tg;
     int stage, nstages;
     int nU, tilesU, outTiles;       // units (slot, 16 hidden rows), units per slot, 16-row output tiles
-    int o_xtab, o_xg, o_ysum, o_sbc, o_red, o_hq, o_bar, o_ids, o_w, o_ring, total;
+    int o_xtab, o_xg, o_ysum, o_sbc, o_red, o_hq, o_bar, o_ids, o_w, o_scr, o_ring, total;
 
     __host__ __device__ void init(int fmt, int d_, int dff_, int k_, int ntok_, int max_smem) {
         d = d_; dff = dff_; k = k_; ntok = ntok_;
@@ -190,9 +190,10 @@ struct FusedGeom {
         o_sbc = take(2 * int(tg.dgroup));                // two groups' down scales
         o_red = take(2 * kFusedConsumers * 32 * 4);      // double-buffered partial sums
         o_hq = take(2 * 256);                            // per buffer: h[16], B regs[8], sum
-        o_bar = take((2 * 16 + 4) * 8);
+        o_bar = take((2 * 16 + 5) * 8);                 // full[16] empty[16] redF[2] hR[2] routed
         o_ids = take(ntok * k * 4);
         o_w = take(ntok * k * 4);
+        o_scr = take(2 * kFusedMaxK * 4);                // throw-away outputs (instruction warm-up)
         off = (off + 1023) & ~1023;
         o_ring = off;
         nstages = (max_smem - off) / stage;

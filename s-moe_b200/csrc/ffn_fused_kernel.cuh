@@ -95,6 +95,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
     uint64_t* empty = full + 16;
     uint64_t* redF = full + 32;                                 // [2] partial sums written (16 arrivals)
     uint64_t* hR = full + 34;                                   // [2] h ready (1 arrival)
+    uint64_t* routedB = full + 36;                              // routing in s_ids / s_w (1 arrival)
     uint32_t* s_ids = reinterpret_cast<uint32_t*>(sm + g.o_ids);
     float* s_w = reinterpret_cast<float*>(sm + g.o_w);
     float* red = red0;                                          // routing uses buffer 0
@@ -129,6 +130,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
             mbar_init(redF + b, kFusedConsumers);
             mbar_init(hR + b, 1);
         }
+        mbar_init(routedB, 1);
         fence_mbar_init();
     }
     __syncthreads();
@@ -164,6 +166,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
             }
             __syncthreads();
         }
+        trace_mark(A.trace, 11);
     }
     // x table (consumers): one round of wide loads, then the table in shared memory
     if (consumer) {
@@ -176,24 +179,51 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
         consumer_sync();
         trace_mark(A.trace, 10);                             // x staging (ysum) is reused below
     }
-    if (A.rw) {
-        if (tid == 0 && !spin_until_geq(&A.st->rdone, A.E * g.ntok)) atomicExch(f.err, SMOE_DEVERR_SPIN_TIMEOUT);
-        __syncthreads();      // (x tables are complete here too)
-        if (warp < g.ntok) {
-            warp_topk(A.logits + size_t(warp) * A.E, A.E, k, A.norm, ysum + warp * kRouterMaxE,
-                      s_ids + warp * k, s_w + warp * k, lane);
+    if (A.rw && warp == kFusedProdWarp) {
+        // The selection code runs once per launch and would be fetched cold
+        // on the routing critical path; the otherwise idle producer runs it
+        // once on last launch's logits (outputs discarded) to bring it into
+        // the SM's instruction cache before the h warp needs it.
+        uint32_t* scr = reinterpret_cast<uint32_t*>(sm + g.o_scr);
+        SMOE_PROF(long long c0 = clock64();)
+        warp_topk(A.logits, A.E, k, A.norm, scr, reinterpret_cast<float*>(scr + kFusedMaxK), lane);
+        SMOE_PROF(if (A.trace && lane == 0) reinterpret_cast<long long*>(A.trace)[gridDim.x * 56 + blockIdx.x * 8 + 0] = clock64() - c0;)
+    }
+    if (A.rw && warp == kFusedHWarp) {
+        // routing (h warp, while the consumers build the x table): wait for
+        // every logit row of the grid, then softmax / top-k / renorm per token
+        if (lane == 0 && !spin_until_geq(&A.st->rdone, A.E * g.ntok)) atomicExch(f.err, SMOE_DEVERR_SPIN_TIMEOUT);
+        __syncwarp();
+        trace_mark(A.trace, 13, lane == 0);
+        SMOE_PROF(long long c0 = clock64();)
+        for (int t = 0; t < g.ntok; ++t) {
+            warp_topk(A.logits + size_t(t) * A.E, A.E, k, A.norm, s_ids + t * k, s_w + t * k, lane);
+            SMOE_PROF(if (A.trace && lane == 0 && t == 0) reinterpret_cast<long long*>(A.trace)[gridDim.x * 56 + blockIdx.x * 8 + 1] = clock64() - c0;)
             __syncwarp();
             if (blockIdx.x == 0 && lane < k) {
-                const_cast<uint32_t*>(f.ids)[warp * k + lane] = s_ids[warp * k + lane];
-                const_cast<float*>(f.wts)[warp * k + lane] = s_w[warp * k + lane];
+                const_cast<uint32_t*>(f.ids)[t * k + lane] = s_ids[t * k + lane];
+                const_cast<float*>(f.wts)[t * k + lane] = s_w[t * k + lane];
             }
         }
-        __syncthreads();
+        __syncwarp();
+        // start the weight stream from here: no hand-off to the producer,
+        // which takes over from unit `pre` once routedB completes
+        pre = min(NS, u1 - u0);
+        if (lane == 0) {
+            for (int n = 0; n < pre; ++n) issue(u0 + n, n);
+            mbar_arrive(routedB);
+        }
+        SMOE_PROF(if (A.trace && lane == 0) reinterpret_cast<long long*>(A.trace)[gridDim.x * 56 + blockIdx.x * 8 + 2] = clock64() - c0;)
+        trace_mark(A.trace, 1, lane == 0);
     }
-    trace_mark(A.trace, 1);
 
     if (warp == kFusedProdWarp) {
         // ------------------------------------------------------ producer
+        if (A.rw) {                                  // expert ids (and the first units) come from the h warp
+            if (lane == 0 && !mbar_wait_bounded(routedB, 0)) atomicExch(f.err, SMOE_DEVERR_MBAR_TIMEOUT);
+            __syncwarp();
+            pre = min(NS, u1 - u0);
+        }
         for (int u = u0 + pre, n = pre; u < u1; ++u, ++n) {
             const int st = n % NS, round = n / NS;
             if (round > 0 && lane == 0 && !mbar_wait_bounded(empty + st, (round - 1) & 1))

@@ -71,49 +71,52 @@ SMOE_DEVINL void stage_vec(const void* src, int x_dtype, size_t off, int d, floa
 // by probability with the lowest index winning ties, renormalised over the k
 // in rank order when `norm` (scout.cpp:77-123, decode.cpp:296-303). The
 // denominator is a warp tree sum; expert ids do not depend on it.
-// ps: shared scratch of E floats. ids/wts: k outputs (global or shared).
-SMOE_DEVINL void warp_topk(const float* lg, uint32_t E_, uint32_t k_, int norm, float* ps,
-                           uint32_t* ids, float* wts, int lane) {
-    const int E = (int)E_;
+// ids/wts: k outputs (global or shared).
+template <int NV>
+SMOE_DEVINL void warp_topk_n(const float* lg, int E, uint32_t k, int norm, uint32_t* ids, float* wts,
+                             int lane) {
+    // Lane l holds entries l + 32j. Selection keys: bits(p) + 1 for a live
+    // probability (p >= 0, so the order of the keys is the order of p), 0 for
+    // removed or absent entries. Each round is two warp reductions: the
+    // largest key, then the lowest index among the lanes holding it.
+    float p[NV];
     float mx = -INFINITY;
-    for (int i = lane; i < E; i += 32) {
-        const float v = __ldcg(lg + i);
-        ps[i] = v;
-        mx = fmaxf(mx, v);
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+        const int i = lane + 32 * j;
+        p[j] = i < E ? __ldcg(lg + i) : -INFINITY;
+        mx = fmaxf(mx, p[j]);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     float se = 0.f;
-    for (int i = lane; i < E; i += 32) {
-        const float e = expf(ps[i] - mx);
-        ps[i] = e;
-        se += e;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+        if (lane + 32 * j < E) {
+            p[j] = expf(p[j] - mx);
+            se += p[j];
+        }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) se += __shfl_xor_sync(0xffffffffu, se, o);
     const float inv = se > 0.f ? 1.0f / se : 0.f;
-    __syncwarp();
-    for (int i = lane; i < E; i += 32) ps[i] *= inv;
-    __syncwarp();
-    const uint32_t k = k_ < E_ ? k_ : E_;
+    uint32_t key[NV];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) key[j] = lane + 32 * j < E ? __float_as_uint(p[j] * inv) + 1u : 0u;
     float wsel = 0.f;
     uint32_t idsel = 0;
     for (uint32_t s = 0; s < k; ++s) {
-        float bv = -1.f;
-        int bi = 0x7fffffff;
-        for (int i = lane; i < E; i += 32) {
-            const float v = ps[i];
-            if (v > bv) { bv = v; bi = i; }          // ascending i: first max per lane
-        }
+        uint32_t lb = 0u;
+        int lj = 0;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-        }
-        if (lane == (int)s) { wsel = bv; idsel = bi; }
-        if (lane == 0) ps[bi] = -2.f;                 // removed
-        __syncwarp();
+        for (int j = 0; j < NV; ++j)
+            if (key[j] > lb) { lb = key[j]; lj = j; }               // ascending index: first max per lane
+        const uint32_t gm = __reduce_max_sync(0xffffffffu, lb);
+        const uint32_t win = __reduce_min_sync(0xffffffffu, lb == gm ? uint32_t(lane + 32 * lj) : 0xffffffffu);
+        if (lane == (int)s) { wsel = __uint_as_float(gm - 1u); idsel = win; }
+#pragma unroll
+        for (int j = 0; j < NV; ++j)                                // remove the winner
+            if (win == uint32_t(lane + 32 * j)) key[j] = 0u;
     }
     float ws = 0.f;                                   // rank-order sum (decode.cpp:296-303)
     for (uint32_t s = 0; s < k; ++s) ws += __shfl_sync(0xffffffffu, wsel, s);
@@ -124,10 +127,16 @@ SMOE_DEVINL void warp_topk(const float* lg, uint32_t E_, uint32_t k_, int norm, 
     }
 }
 
+SMOE_DEVINL void warp_topk(const float* lg, uint32_t E_, uint32_t k_, int norm, uint32_t* ids, float* wts,
+                           int lane) {
+    const uint32_t k = k_ < E_ ? k_ : E_;
+    if (E_ <= 128) warp_topk_n<4>(lg, (int)E_, k, norm, ids, wts, lane);
+    else warp_topk_n<kRouterMaxE / 32>(lg, (int)E_, k, norm, ids, wts, lane);
+}
+
 // grid (ceil(E/8), batch), 256 threads, smem d floats + selection scratch.
 __global__ void __launch_bounds__(256) k_router(RouterArgs a) {
     extern __shared__ __align__(16) float xs[];
-    __shared__ float ps[kRouterMaxE];
     __shared__ uint32_t last_flag;
     const int tok = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     stage_vec<float>(a.x, a.x_dtype, size_t(tok) * a.d, a.d, xs);
@@ -148,7 +157,7 @@ __global__ void __launch_bounds__(256) k_router(RouterArgs a) {
     if (!last_flag) return;
     __threadfence();
     if (warp != 0) return;
-    warp_topk(lg, a.E, a.k, a.norm, ps, a.ids + size_t(tok) * a.k, a.wts + size_t(tok) * a.k, lane);
+    warp_topk(lg, a.E, a.k, a.norm, a.ids + size_t(tok) * a.k, a.wts + size_t(tok) * a.k, lane);
     if (lane == 0) a.ticket[tok] = 0;                 // ready for the next call
 }
 
