@@ -207,6 +207,38 @@ int smoe_cuda_moe_layer(SmoeCudaCtx* ctx, const SmoeMoeLayer* layer, const void*
                         int x_dtype, uint32_t batch, uint32_t k, int norm_topk,
                         void* y, int y_dtype, uint32_t* ids_out, float* w_out);
 
+/* ---- Expert parallel over the GPUs of one node (one process per GPU).
+ * Replaces the per-GPU partial-sum combine that the reference leaves to
+ * NCCL (the 235B EP layout: experts [r*E/G, (r+1)*E/G) on rank r, x and y on
+ * rank 0). No counterpart in metal_bridge.h, which is single-GPU.
+ *
+ * Set-up, once per context: every rank calls smoe_cuda_ep_export, the host
+ * gathers the handles in rank order by any means (e.g. an all-gather of
+ * the 64-byte blobs), and every rank calls smoe_cuda_ep_attach with all of
+ * them. The exchange then runs inside the layer kernel over NVLink: rank 0
+ * publishes x, the other ranks read it with peer loads, every rank routes
+ * (identical ids), runs the experts it holds and stores its fp32 partial
+ * output into rank 0's window; rank 0 sums the partials in rank order.
+ * All ranks must make the same sequence of smoe_cuda_moe_layer_ep calls.
+ * Waits on other GPUs are bounded (a rank that never arrives raises
+ * SMOE_ERR_DEVICE at the next synchronize instead of hanging). */
+typedef struct SmoeEpHandle {
+    uint8_t bytes[64];
+} SmoeEpHandle;
+
+int smoe_cuda_ep_export(SmoeCudaCtx* ctx, SmoeEpHandle* out);
+int smoe_cuda_ep_attach(SmoeCudaCtx* ctx, int rank, int world, const SmoeEpHandle* handles);
+
+/* One MoE layer, expert parallel. shard: this rank's experts
+ * [expert_base, expert_base + shard->n_experts) in the tiled layout, with
+ * the full router (n_experts_total rows) in shard->router_w. x, y: device
+ * buffers on rank 0 (ignored, may be NULL, on other ranks); ids_out / w_out
+ * (optional) receive the routing on every rank. */
+int smoe_cuda_moe_layer_ep(SmoeCudaCtx* ctx, const SmoeMoeLayer* shard, uint32_t n_experts_total,
+                           uint32_t expert_base, const void* x, int x_dtype, uint32_t batch,
+                           uint32_t k, int norm_topk, void* y, int y_dtype, uint32_t* ids_out,
+                           float* w_out);
+
 /* No counterpart in the reference. For callers that cannot call cudaMalloc -
  * engines whose device memory is all reserved by their own pool, code run
  * inside callbacks where allocation is forbidden - this is smoe_cuda_moe_ffn

@@ -157,6 +157,23 @@ SMOE_DEVINL SlotW expert_ptrs(const FfnArgs& a, uint32_t e) {
     return w;
 }
 
+SMOE_DEVINL uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+SMOE_DEVINL void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
+}
+// Bounded wait on a word another GPU writes (system scope).
+SMOE_DEVINL bool spin_sys_until_geq(const uint32_t* p, uint32_t target) {
+    for (uint32_t i = 0; i < SMOE_SPIN_LIMIT; ++i) {
+        if (ld_acquire_sys(p) >= target) return true;
+        if (i > 32) __nanosleep(i > 256 ? 256 : 64);
+    }
+    return false;
+}
+
 SMOE_DEVINL bool spin_until_geq(const uint32_t* p, uint32_t target) {
     for (uint32_t i = 0; i < SMOE_SPIN_LIMIT; ++i) {
         if (ld_volatile_u32(p) >= target) return true;
@@ -171,7 +188,7 @@ struct FusedGeom {
     TiledGeom tg;
     int stage, nstages;
     int nU, tilesU, outTiles;       // units (slot, 16 hidden rows), units per slot, 16-row output tiles
-    int o_xtab, o_xg, o_ysum, o_sbc, o_red, o_hq, o_bar, o_ids, o_w, o_scr, o_ring, total;
+    int o_xtab, o_xg, o_ysum, o_sbc, o_red, o_hq, o_bar, o_ids, o_w, o_loc, o_ring, total;
 
     __host__ __device__ void init(int fmt, int d_, int dff_, int k_, int ntok_, int max_smem) {
         d = d_; dff = dff_; k = k_; ntok = ntok_;
@@ -193,7 +210,7 @@ struct FusedGeom {
         o_bar = take((2 * 16 + 5) * 8);                 // full[16] empty[16] redF[2] hR[2] routed
         o_ids = take(ntok * k * 4);
         o_w = take(ntok * k * 4);
-        o_scr = take(2 * kFusedMaxK * 4);                // throw-away outputs (instruction warm-up)
+        o_loc = take(4 * (kFusedMaxTok * kFusedMaxK + 1)); // expert parallel: local slot list + count
         off = (off + 1023) & ~1023;
         o_ring = off;
         nstages = (max_smem - off) / stage;
@@ -203,6 +220,29 @@ struct FusedGeom {
         if (nstages > 4) nstages = 4;
         total = off + nstages * stage;
     }
+};
+
+// Expert-parallel exchange (world > 1), one process per GPU. Every rank runs
+// the same launch sequence; rank 0 owns x and y. Each rank has a window of
+// device memory exported over CUDA IPC; ranks > 0 map rank 0's:
+//   flag0  rank 0's x epoch: rank 0 copies x into x0, then releases it;
+//   x0     that copy, read by the other ranks with peer loads over NVLink;
+//   part0  [world][kFusedMaxTok * d] fp32: rank r's partial output,
+//          written by rank r's last CTA with peer stores;
+//   done0  ranks whose partial has arrived (system-scope atomics); rank 0's
+//          last CTA waits for world - 1, sums, writes y and resets it.
+// Routing is computed on every rank (same weights, same x, same code: the
+// same ids); each rank runs the units of the slots whose expert it holds.
+constexpr int kEpMaxWorld = 8;
+struct FusedEp {
+    int world, rank;
+    uint32_t base, nlocal;     // global id of this rank's first expert, experts held
+    uint32_t epoch;            // launch number, equal on every rank
+    uint8_t* x0;
+    uint32_t* flag0;
+    float* part0;
+    uint32_t* done0;
+    uint32_t part_stride;      // floats per rank in part0
 };
 
 struct FusedArgs {
@@ -215,6 +255,7 @@ struct FusedArgs {
     float* logits;             // scratch [ntok x E]
     float* acc;                // scratch [ntok x d] fp32, zero on entry and on exit
     unsigned long long* trace; // optional [grid x 8] phase timestamps (ns), null in production
+    FusedEp ep;                // world 0/1: single GPU
 };
 
 }  // namespace smoe

@@ -34,7 +34,7 @@
 namespace smoe {
 
 // Phase R: logit row r = (token, expert) by all consumer warps of this CTA.
-SMOE_DEVINL float router_row(const FusedArgs& A, uint32_t t, uint32_t e, int ctid) {
+SMOE_DEVINL float router_row(const FusedArgs& A, const void* xsrc, uint32_t t, uint32_t e, int ctid) {
     const FfnArgs& f = A.f;
     const int d = A.g.d;
     float acc = 0.f;
@@ -45,13 +45,13 @@ SMOE_DEVINL float router_row(const FusedArgs& A, uint32_t t, uint32_t e, int cti
         float xv[8];
         if (f.x_dtype == 0) {
             const float4* xp =
-                reinterpret_cast<const float4*>(static_cast<const float*>(f.x) + size_t(t) * d + c * 8);
+                reinterpret_cast<const float4*>(static_cast<const float*>(xsrc) + size_t(t) * d + c * 8);
             const float4 a0 = xp[0], a1 = xp[1];
             xv[0] = a0.x; xv[1] = a0.y; xv[2] = a0.z; xv[3] = a0.w;
             xv[4] = a1.x; xv[5] = a1.y; xv[6] = a1.z; xv[7] = a1.w;
         } else {
             const uint4 b =
-                *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(f.x) + size_t(t) * d + c * 8);
+                *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(xsrc) + size_t(t) * d + c * 8);
             const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
@@ -107,15 +107,37 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
     SMOE_PROF(if (A.trace && tid == 0) A.trace[gridDim.x * 32 + blockIdx.x * 8 + 4] = clock64();)
     // inputs (x, routing) may come from the previous kernel in the stream
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    const int u0 = int(blockIdx.x * uint32_t(g.nU) / gridDim.x);          // nU * grid < 2^31
-    const int u1 = int((blockIdx.x + 1) * uint32_t(g.nU) / gridDim.x);
+    const FusedEp& ep = A.ep;
+    const bool epm = ep.world > 1;
+    uint32_t* s_loc = reinterpret_cast<uint32_t*>(sm + g.o_loc);     // expert parallel: local slots, count
+    // this CTA's units [u0, u1) of nU: every unit of every slot, or (expert
+    // parallel) of the slots whose expert this rank holds, known after routing
+    int u0 = 0, u1 = 0;
+    auto set_range = [&](int nU) {
+        u0 = int(blockIdx.x * uint32_t(nU) / gridDim.x);                 // nU * grid < 2^31
+        u1 = int((blockIdx.x + 1) * uint32_t(nU) / gridDim.x);
+    };
+    if (!epm) set_range(g.nU);
+    auto slot_of = [&](int u) { return epm ? int(s_loc[u / g.tilesU]) : u / g.tilesU; };
     auto needs_sb = [&](int u) { return u == u0 || (u % g.tilesU) % 4 == 0; };
+    // x: the caller's, or on ranks > 0 rank 0's published copy (peer memory)
+    const void* xsrc = f.x;
+    if (epm) {
+        const size_t xbytes = size_t(g.ntok) * d * (f.x_dtype == 0 ? 4 : 2);
+        if (ep.rank == 0 && blockIdx.x == 0) {
+            for (size_t i = tid; i < xbytes / 16; i += blockDim.x)
+                reinterpret_cast<uint4*>(ep.x0)[i] = reinterpret_cast<const uint4*>(f.x)[i];
+        } else if (ep.rank > 0) {
+            if (tid == 0 && !spin_sys_until_geq(ep.flag0, ep.epoch)) atomicExch(f.err, SMOE_DEVERR_SPIN_TIMEOUT);
+            xsrc = ep.x0;
+        }
+    }
     // copy of unit u (the n-th of this CTA) into its stage: one bulk copy, plus
     // the down scales of the 64-row group it starts (producer lane 0)
     auto issue = [&](int u, int n) {
-        const int st = n % NS, slot = u / g.tilesU, t = u % g.tilesU;
+        const int st = n % NS, slot = slot_of(u), t = u % g.tilesU;
         const bool sb = needs_sb(u);
-        const uint8_t* ex = f.base + uint64_t(s_ids[slot]) * f.stride;
+        const uint8_t* ex = f.base + uint64_t(s_ids[slot] - (epm ? ep.base : 0u)) * f.stride;
         mbar_arrive_expect_tx(full + st, tg.unit + (sb ? tg.dgroup : 0));
         bulk_g2s(ring + size_t(st) * g.stage, ex + tg.unit_off(t), tg.unit, full + st);
         if (sb) bulk_g2s(sbc0 + ((u / 4) & 1) * (tg.dgroup / 2), ex + tg.group_off(t / 4), tg.dgroup, full + st);
@@ -133,7 +155,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
         mbar_init(routedB, 1);
         fence_mbar_init();
     }
-    __syncthreads();
+    __syncthreads();              // (ranks > 0: rank 0's x is published; rank 0 CTA 0: x0 is written)
+    if (epm && ep.rank == 0 && blockIdx.x == 0 && tid == 0) {
+        __threadfence_system();
+        st_release_sys(ep.flag0, ep.epoch);
+    }
     int pre = 0;                                                // units issued ahead of the main loop
     if (!A.rw && warp == kFusedProdWarp) {
         // routing given: read it and start the weight stream at once
@@ -154,7 +180,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
         const uint32_t rows = A.E * g.ntok;
         for (uint32_t r = blockIdx.x; r < rows; r += gridDim.x) {
             float v = 0.f;
-            if (consumer) v = router_row(A, r / A.E, r % A.E, tid);
+            if (consumer) v = router_row(A, xsrc, r / A.E, r % A.E, tid);
             if (consumer && lane == 0) red[warp] = v;
             __syncthreads();
             if (tid == 0) {
@@ -170,24 +196,14 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
     }
     // x table (consumers): one round of wide loads, then the table in shared memory
     if (consumer) {
-        if (f.x_dtype == 0) stage_vec_smem<false>(f.x, g.ntok * d, ysum, tid);
-        else stage_vec_smem<true>(f.x, g.ntok * d, ysum, tid);
+        if (f.x_dtype == 0) stage_vec_smem<false>(xsrc, g.ntok * d, ysum, tid);
+        else stage_vec_smem<true>(xsrc, g.ntok * d, ysum, tid);
         consumer_sync();
         trace_mark(A.trace, 9);
         build_xplanes<FMT>(ysum, g.ntok, d, xtab, xg, tid);
 
         consumer_sync();
         trace_mark(A.trace, 10);                             // x staging (ysum) is reused below
-    }
-    if (A.rw && warp == kFusedProdWarp) {
-        // The selection code runs once per launch and would be fetched cold
-        // on the routing critical path; the otherwise idle producer runs it
-        // once on last launch's logits (outputs discarded) to bring it into
-        // the SM's instruction cache before the h warp needs it.
-        uint32_t* scr = reinterpret_cast<uint32_t*>(sm + g.o_scr);
-        SMOE_PROF(long long c0 = clock64();)
-        warp_topk(A.logits, A.E, k, A.norm, scr, reinterpret_cast<float*>(scr + kFusedMaxK), lane);
-        SMOE_PROF(if (A.trace && lane == 0) reinterpret_cast<long long*>(A.trace)[gridDim.x * 56 + blockIdx.x * 8 + 0] = clock64() - c0;)
     }
     if (A.rw && warp == kFusedHWarp) {
         // routing (h warp, while the consumers build the x table): wait for
@@ -206,6 +222,19 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
             }
         }
         __syncwarp();
+        if (epm) {                                   // slots whose expert this rank holds, in slot order
+            uint32_t cnt = 0;
+            for (uint32_t s0 = 0; s0 < nslots; s0 += 32) {
+                const uint32_t sl = s0 + lane;
+                const bool loc = sl < nslots && s_ids[sl] - ep.base < ep.nlocal;
+                const uint32_t m = __ballot_sync(0xffffffffu, loc);
+                if (loc) s_loc[cnt + __popc(m & ((1u << lane) - 1u))] = sl;
+                cnt += __popc(m);
+            }
+            if (lane == 0) s_loc[kFusedMaxTok * kFusedMaxK] = cnt;
+            __syncwarp();
+            set_range(int(cnt) * g.tilesU);
+        }
         // start the weight stream from here: no hand-off to the producer,
         // which takes over from unit `pre` once routedB completes
         pre = min(NS, u1 - u0);
@@ -222,6 +251,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
         if (A.rw) {                                  // expert ids (and the first units) come from the h warp
             if (lane == 0 && !mbar_wait_bounded(routedB, 0)) atomicExch(f.err, SMOE_DEVERR_MBAR_TIMEOUT);
             __syncwarp();
+            if (epm) set_range(int(s_loc[kFusedMaxTok * kFusedMaxK]) * g.tilesU);
             pre = min(NS, u1 - u0);
         }
         for (int u = u0 + pre, n = pre; u < u1; ++u, ++n) {
@@ -235,7 +265,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
         // ---------------------------------------------------------- h warp
         SMOE_PROF(if (A.trace) for (int n = 0; n < 3 && n < u1 - u0; ++n) { mbar_wait_bounded(full + n, 0); trace_mark(A.trace, 28 + n, lane == 0); })
         for (int u = u0, n = 0; u < u1; ++u, ++n) {
-            const int b = n & 1, slot = u / g.tilesU;
+            const int b = n & 1, slot = slot_of(u);
             if (!mbar_wait_bounded(redF + b, (n >> 1) & 1)) atomicExch(f.err, SMOE_DEVERR_MBAR_TIMEOUT);
             const float* rb = red0 + b * kFusedConsumers * 32;
             float* hq = reinterpret_cast<float*>(sm + g.o_hq + b * 256);
@@ -276,6 +306,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
         const int gr = lane >> 2;
         for (int i = tid; i < g.ntok * d; i += kFusedCThreads) ysum[i] = 0.f;
         consumer_sync();
+        if (epm) {                                   // the unit list depends on the routing
+            if (!mbar_wait_bounded(routedB, 0)) atomicExch(f.err, SMOE_DEVERR_MBAR_TIMEOUT);
+            set_range(int(s_loc[kFusedMaxTok * kFusedMaxK]) * g.tilesU);
+        }
         trace_mark(A.trace, 2);
         const int cq = lane & 3;                         // token whose results this lane holds
         // Down projection, split-K: this CTA's units are consecutive (slot,
@@ -291,7 +325,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
         const uint32_t M = 0x000F000Fu, OR = 0x43004300u;
         SMOE_PROF(long long cy_wait = 0, cy_gu = 0, cy_hw = 0, cy_dn = 0, cy_t = 0;)
         auto down = [&](int u, int n) {
-            const int b = n & 1, st = n % NS, tok = (u / g.tilesU) / k, t = u % g.tilesU;
+            const int b = n & 1, st = n % NS, tok = slot_of(u) / k, t = u % g.tilesU;
             SMOE_PROF(cy_t = clock64();)
             if (!mbar_wait_bounded(hR + b, (n >> 1) & 1)) atomicExch(f.err, SMOE_DEVERR_MBAR_TIMEOUT);
             SMOE_PROF(cy_hw += clock64() - cy_t; cy_t = clock64();)
@@ -395,7 +429,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
           if (n < nun) {
             const int u = u0 + n;
             const int st = n % NS, b = n & 1;
-            const int slot = u / g.tilesU, tok = slot / k;
+            const int slot = slot_of(u), tok = slot / k;
             SMOE_PROF(cy_t = clock64();)
             if (!mbar_wait_bounded(full + st, (n / NS) & 1)) atomicExch(f.err, SMOE_DEVERR_MBAR_TIMEOUT);
             SMOE_PROF(cy_wait += clock64() - cy_t; cy_t = clock64();)
@@ -492,18 +526,45 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
     __syncthreads();
     if (last_cta) {
         __threadfence();
-        for (int i = tid; i < g.ntok * d / 4; i += blockDim.x) {      // d % 64 == 0: whole float4s
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(A.acc) + i);
-            reinterpret_cast<float4*>(A.acc)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (f.y_dtype == 0) {
-                reinterpret_cast<float4*>(f.y)[i] = v;
-            } else {
-                __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
-                uint2 o;
-                o.x = *reinterpret_cast<uint32_t*>(&lo);
-                o.y = *reinterpret_cast<uint32_t*>(&hi);
-                reinterpret_cast<uint2*>(f.y)[i] = o;
+        const int n4 = g.ntok * d / 4;                               // d % 64 == 0: whole float4s
+        float4* acc4 = reinterpret_cast<float4*>(A.acc);
+        if (epm && ep.rank > 0) {
+            // this rank's partial output -> rank 0 (peer stores), then count it
+            float4* dst = reinterpret_cast<float4*>(ep.part0 + size_t(ep.rank) * ep.part_stride);
+            for (int i = tid; i < n4; i += blockDim.x) {
+                dst[i] = __ldcg(acc4 + i);
+                acc4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
             }
+            __syncthreads();
+            if (tid == 0) {
+                __threadfence_system();
+                atomicAdd_system(ep.done0, 1u);
+            }
+        } else {
+            if (epm) {                                               // wait for every other rank's partial
+                if (tid == 0 && !spin_sys_until_geq(ep.done0, uint32_t(ep.world - 1)))
+                    atomicExch(f.err, SMOE_DEVERR_SPIN_TIMEOUT);
+                __syncthreads();
+            }
+            for (int i = tid; i < n4; i += blockDim.x) {
+                float4 v = __ldcg(acc4 + i);
+                for (int r = 1; r < (epm ? ep.world : 1); ++r) {       // rank order
+                    const float4 p = __ldcg(reinterpret_cast<const float4*>(ep.part0 + size_t(r) * ep.part_stride) + i);
+                    v.x += p.x; v.y += p.y; v.z += p.z; v.w += p.w;
+                }
+                acc4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (f.y_dtype == 0) {
+                    reinterpret_cast<float4*>(f.y)[i] = v;
+                } else {
+                    __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+                    uint2 o;
+                    o.x = *reinterpret_cast<uint32_t*>(&lo);
+                    o.y = *reinterpret_cast<uint32_t*>(&hi);
+                    reinterpret_cast<uint2*>(f.y)[i] = o;
+                }
+            }
+            // the other ranks' next partials come only after the next x epoch
+            if (epm && tid == 0) *ep.done0 = 0u;
         }
         if (tid == 0) {
             A.st->rdone = 0;

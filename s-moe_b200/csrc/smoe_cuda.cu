@@ -66,6 +66,12 @@ struct SmoeCudaCtx {
     int fused_grid[2][4] = {};       // fused kernel grid per (format, groups per warp)
     size_t fused_smem_seen[2][4] = {};
     unsigned long long* trace = nullptr;   // phase timestamps of the fused kernel (profiling aid)
+    // expert parallel: this rank's exchange window (IPC-exported) and rank 0's, mapped
+    uint8_t* ep_win = nullptr;
+    size_t ep_win_bytes = 0;
+    uint8_t* ep_peer0 = nullptr;
+    int ep_world = 0, ep_rank = 0;
+    uint32_t ep_epoch = 0;
 };
 
 namespace {
@@ -175,7 +181,7 @@ int launch_ffn(SmoeCudaCtx* c, smoe::FfnArgs& a, int fmt) {
 // CTAs). Returns SMOE_ERR_UNSUPPORTED when the shape does not fit, so the
 // caller can use the two-kernel path.
 int launch_fused(SmoeCudaCtx* c, smoe::FfnArgs& f, int fmt, const uint16_t* rw, uint32_t E,
-                 int norm) {
+                 int norm, const smoe::FusedEp* ep = nullptr) {
     if (f.ntok > (uint32_t)smoe::kFusedMaxTok || f.k > (uint32_t)smoe::kFusedMaxK || f.d_model > 4096 ||
         (rw && E > (uint32_t)smoe::kRouterMaxE) || (rw && f.d_model % 8))
         return SMOE_ERR_UNSUPPORTED;
@@ -196,6 +202,7 @@ int launch_fused(SmoeCudaCtx* c, smoe::FfnArgs& f, int fmt, const uint16_t* rw, 
     A.logits = c->logits;
     A.acc = c->acc;                       // [ntok x d] fp32, zeroed at init and by each launch's last CTA
     A.trace = c->trace;
+    if (ep) A.ep = *ep;
     const size_t smem = (size_t)A.g.total;
     // gate/up groups per consumer warp (GW = 1, 2, 4, 8)
     const int gw_need = (A.g.G + smoe::kFusedConsumers - 1) / smoe::kFusedConsumers;
@@ -352,6 +359,8 @@ void smoe_cuda_destroy(SmoeCudaCtx* c) {
     if (!c) return;
     cudaSetDevice(c->device);
     if (c->own_stream) cudaStreamSynchronize(c->own_stream);
+    if (c->ep_peer0 && c->ep_peer0 != c->ep_win) cudaIpcCloseMemHandle(c->ep_peer0);
+    if (c->ep_win) cudaFree(c->ep_win);
     for (auto& ev : c->events)
         if (ev) cudaEventDestroy(ev);
     void* bufs[] = {c->fstate, c->acc, c->hidden, c->slot_out, c->in_stage, c->batch_out, c->logits, c->ids,
@@ -677,6 +686,91 @@ int smoe_cuda_moe_layer(SmoeCudaCtx* c, const SmoeMoeLayer* L, const void* x, in
                                    k, norm, ids, wts, nullptr);
     if (rc) return rc;
     return smoe_cuda_moe_ffn(c, L, x, x_dtype, ids, wts, k, batch, y, y_dtype);
+}
+
+// ----------------------------------------------------------- expert parallel
+namespace {
+constexpr size_t kEpFlagOff = 0, kEpDoneOff = 128, kEpXOff = 256;
+size_t ep_x_bytes(const SmoeCudaCtx* c) { return size_t(smoe::kFusedMaxTok) * c->cfg.max_d_model * 4; }
+size_t ep_part_stride(const SmoeCudaCtx* c) { return size_t(smoe::kFusedMaxTok) * c->cfg.max_d_model; }
+}  // namespace
+
+int smoe_cuda_ep_export(SmoeCudaCtx* c, SmoeEpHandle* out) {
+    if (!c || !out) { set_err("null argument %s%ld", "", 0); return SMOE_ERR_ARG; }
+    if (!c->ep_win) {
+        c->ep_win_bytes = kEpXOff + ep_x_bytes(c) + size_t(smoe::kEpMaxWorld) * ep_part_stride(c) * 4;
+        CK(cudaMalloc(&c->ep_win, c->ep_win_bytes));
+        CK(cudaMemset(c->ep_win, 0, c->ep_win_bytes));
+    }
+    cudaIpcMemHandle_t h;
+    static_assert(sizeof(h) <= sizeof(out->bytes), "IPC handle size");
+    CK(cudaIpcGetMemHandle(&h, c->ep_win));
+    memset(out->bytes, 0, sizeof(out->bytes));
+    memcpy(out->bytes, &h, sizeof(h));
+    return SMOE_OK;
+}
+
+int smoe_cuda_ep_attach(SmoeCudaCtx* c, int rank, int world, const SmoeEpHandle* handles) {
+    if (!c || !handles || world < 1 || world > smoe::kEpMaxWorld || rank < 0 || rank >= world || !c->ep_win) {
+        set_err("bad expert-parallel attach (rank %s%ld)", "", (long)rank);
+        return SMOE_ERR_ARG;
+    }
+    if (c->ep_peer0 && c->ep_peer0 != c->ep_win) cudaIpcCloseMemHandle(c->ep_peer0);
+    c->ep_peer0 = nullptr;
+    if (rank == 0) {
+        c->ep_peer0 = c->ep_win;
+    } else {
+        cudaIpcMemHandle_t h;
+        memcpy(&h, handles[0].bytes, sizeof(h));
+        void* p = nullptr;
+        CK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+        c->ep_peer0 = static_cast<uint8_t*>(p);
+    }
+    c->ep_rank = rank;
+    c->ep_world = world;
+    c->ep_epoch = 0;
+    return SMOE_OK;
+}
+
+int smoe_cuda_moe_layer_ep(SmoeCudaCtx* c, const SmoeMoeLayer* shard, uint32_t n_experts_total,
+                           uint32_t expert_base, const void* x, int x_dtype, uint32_t batch, uint32_t k,
+                           int norm, void* y, int y_dtype, uint32_t* ids_out, float* w_out) {
+    if (!c || !shard || !c->ep_peer0) { set_err("expert parallel not attached %s%ld", "", 0); return SMOE_ERR_ARG; }
+    const bool r0 = c->ep_rank == 0;
+    if (!(shard->fmt & SMOE_LAYOUT_TILED) || !shard->router_w || !aligned16(shard->router_w) ||
+        n_experts_total < k || k == 0 || k > SMOE_MAX_ACTIVE || n_experts_total > c->cfg.max_experts ||
+        expert_base + shard->n_experts > n_experts_total || (x_dtype != 0 && x_dtype != 1) ||
+        (y_dtype != 0 && y_dtype != 1) || (r0 && (!x || !y))) {
+        set_err("bad expert-parallel layer arguments %s%ld", "", (long)k);
+        return SMOE_ERR_ARG;
+    }
+    smoe::FfnArgs a{};
+    int rc = layer_args(c, shard, a);
+    if (rc) return rc;
+    a.ids = ids_out ? ids_out : c->ids;
+    a.wts = w_out ? w_out : c->wts;
+    a.x = r0 ? x : c->ep_peer0 + kEpXOff;            // ranks > 0 read rank 0's published copy
+    a.x_dtype = x_dtype;
+    a.y = r0 ? y : c->acc;                           // (not written on ranks > 0)
+    a.y_dtype = y_dtype;
+    a.k = k;
+    a.ntok = batch;
+    smoe::FusedEp ep{};
+    ep.world = c->ep_world;
+    ep.rank = c->ep_rank;
+    ep.base = expert_base;
+    ep.nlocal = shard->n_experts;
+    ep.epoch = ++c->ep_epoch;
+    ep.x0 = c->ep_peer0 + kEpXOff;
+    ep.flag0 = reinterpret_cast<uint32_t*>(c->ep_peer0 + kEpFlagOff);
+    ep.done0 = reinterpret_cast<uint32_t*>(c->ep_peer0 + kEpDoneOff);
+    ep.part0 = reinterpret_cast<float*>(c->ep_peer0 + kEpXOff + ep_x_bytes(c));
+    ep.part_stride = uint32_t(ep_part_stride(c));
+    const int fmt = int(shard->fmt & ~uint32_t(SMOE_LAYOUT_TILED));
+    rc = launch_fused(c, a, fmt, shard->router_w, n_experts_total, norm, c->ep_world > 1 ? &ep : nullptr);
+    if (rc == SMOE_ERR_UNSUPPORTED)
+        set_err("tiled layout needs batch <= 4 and a shape whose tiles fit shared memory %s%ld", "", (long)batch);
+    return rc;
 }
 
 int smoe_cuda_sample(SmoeCudaCtx* c, float* logits, uint32_t vocab, uint32_t batch,

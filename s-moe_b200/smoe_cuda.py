@@ -35,7 +35,21 @@ EXPORTS = [
     "smoe_cuda_moe_ffn", "smoe_cuda_moe_layer", "smoe_cuda_sample",
     "smoe_cuda_canonical_from_u32", "smoe_cuda_moe_ffn_noalloc", "smoe_cuda_noalloc_last_error",
     "smoe_cuda_tiled_expert_bytes", "smoe_cuda_prepack_layer",
+    "smoe_cuda_ep_export", "smoe_cuda_ep_attach", "smoe_cuda_moe_layer_ep",
 ]
+
+
+class EpHandle(C.Structure):
+    _fields_ = [("bytes", C.c_uint8 * 64)]
+
+
+def ep_partition(n_experts: int, world: int, rank: int):
+    """Experts held by `rank`: [base, base + count) of an even split (the
+    235B layout: 128 experts over 8 GPUs -> 16 each)."""
+    if world < 1 or not 0 <= rank < world or n_experts % world:
+        raise ValueError(f"{n_experts} experts do not split over {world} ranks")
+    per = n_experts // world
+    return rank * per, per
 
 
 class SmoeCudaError(RuntimeError):
@@ -104,6 +118,10 @@ def lib():
         L.smoe_cuda_moe_layer.argtypes = [vp, C.POINTER(MoeLayer), vp, i32, u32, u32, i32, vp,
                                           i32, vp, vp]
         L.smoe_cuda_sample.argtypes = [vp, vp, u32, u32, vp, vp, u32, vp]
+        L.smoe_cuda_ep_export.argtypes = [vp, C.POINTER(EpHandle)]
+        L.smoe_cuda_ep_attach.argtypes = [vp, i32, i32, C.POINTER(EpHandle)]
+        L.smoe_cuda_moe_layer_ep.argtypes = [vp, C.POINTER(MoeLayer), u32, u32, vp, i32, u32, u32, i32,
+                                             vp, i32, vp, vp]
         L.smoe_cuda_moe_ffn_noalloc.argtypes = [C.POINTER(MoeLayer), vp, i32, vp, vp, u32, u32, vp,
                                                 i32, vp]
         L.smoe_cuda_noalloc_last_error.restype = C.c_char_p
@@ -226,6 +244,24 @@ class Context:
         check(self.L.smoe_cuda_moe_layer(self.h, C.byref(layer), ptr(x), x_dtype, batch, k,
                                          int(norm), ptr(y), y_dtype, ptr(ids), ptr(weights)),
               "moe_layer")
+
+    # ---- expert parallel (one process per GPU)
+    def ep_export(self) -> bytes:
+        h = EpHandle()
+        check(self.L.smoe_cuda_ep_export(self.h, C.byref(h)), "ep_export")
+        return bytes(h.bytes)
+
+    def ep_attach(self, rank: int, world: int, handles):
+        arr = (EpHandle * world)()
+        for r, b in enumerate(handles):
+            C.memmove(arr[r].bytes, bytes(b), 64)
+        check(self.L.smoe_cuda_ep_attach(self.h, rank, world, arr), "ep_attach")
+
+    def moe_layer_ep(self, shard: MoeLayer, n_experts_total, expert_base, x, x_dtype, batch, k, norm,
+                     y, y_dtype, ids=None, weights=None):
+        check(self.L.smoe_cuda_moe_layer_ep(self.h, C.byref(shard), n_experts_total, expert_base,
+                                            ptr(x), x_dtype, batch, k, int(norm), ptr(y), y_dtype,
+                                            ptr(ids), ptr(weights)), "moe_layer_ep")
 
     def prepack_layer(self, layer: MoeLayer, dst, dst_stride: int) -> MoeLayer:
         """Tiled copy of a vault-layout layer (dst: device buffer of

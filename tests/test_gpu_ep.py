@@ -1,0 +1,47 @@
+"""GPU parity of the expert-parallel layer (smoe_cuda_moe_layer_ep): one
+process per GPU over 2 GPUs (and 4 when present), exchange inside the layer
+kernel over NVLink, results against the CPU oracle of the whole layer.
+Skipped on a box with a single GPU (ranks that wait on each other never run
+as processes sharing one GPU)."""
+import os
+import socket
+import subprocess
+import sys
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _gpus() -> int:
+    import torch
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("world,fmt", [(2, 1), (2, 0), (4, 1)])
+def test_moe_layer_expert_parallel(world, fmt):
+    if _gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    port = _free_port()
+    procs = [subprocess.Popen([sys.executable, os.path.join(HERE, "ep_worker.py"), str(r), str(world),
+                               str(port), str(fmt)], stdout=subprocess.PIPE, stderr=subprocess.STDOUT,
+                              text=True, env={**os.environ, "NCCL_NVLS_ENABLE": "0"})
+             for r in range(world)]
+    outs = []
+    for p in procs:
+        try:
+            out, _ = p.communicate(timeout=240)
+        except subprocess.TimeoutExpired:
+            for q in procs:
+                q.kill()
+            pytest.fail("expert-parallel ranks did not finish")
+        outs.append((p.returncode, out))
+    for r, (rc, out) in enumerate(outs):
+        assert rc == 0, f"rank {r} failed:\n{out[-3000:]}"
