@@ -12,8 +12,10 @@ resident. L2 is defeated by cycling through 8 distinct resident layers
 (8 x 340 MB) with a fresh x per step: each step's experts were last touched
 7 steps (>= 150 MB of other traffic) earlier. `e2e`: the same step with x
 copied from pinned host memory and y read back to the host inside the timed
-region. N > 1: every rank runs its own replica of the layer step (the layer
-is not sharded), timed as the max over ranks.
+region. N > 1 (torchrun, one rank per GPU): the same layer step expert-
+parallel - rank r holds experts [r*128/N, (r+1)*128/N) of every layer, x and
+y live on rank 0, and the exchange runs inside the layer kernel over NVLink
+(smoe_cuda_moe_layer_ep); strong scaling, timed as the max over ranks.
 """
 from __future__ import annotations
 
@@ -203,19 +205,28 @@ def run_ours(args, rank, world, local):
     ctx = S.Context(local)
     stream = torch.cuda.Stream()
     ctx.set_stream(stream.cuda_stream)
+    ep = world > 1
+    base, per = S.ep_partition(E, world, rank) if ep else (0, E)
     descs, keep = [], []
     for arena, stride, off, rw in layers:
-        da = torch.from_numpy(arena).cuda()
+        da = torch.from_numpy(np.ascontiguousarray(arena[base:base + per])).cuda()
         dr = torch.from_numpy(rw.view(np.int16)).cuda()
         keep += [da, dr]
-        vault = S.make_layer(da, stride, off, E, D, DFF, S.FMT_AFFINE_Q4, dr)
+        vault = S.make_layer(da, stride, off, per, D, DFF, S.FMT_AFFINE_Q4, dr)
         # one-time load-time re-layout into the tiled device format (the
         # vault-layout copy is dropped afterwards)
         tstride = S.tiled_stride(S.FMT_AFFINE_Q4, D, DFF)
-        tb = torch.empty(E * tstride, dtype=torch.uint8, device="cuda")
+        tb = torch.empty(per * tstride, dtype=torch.uint8, device="cuda")
         descs.append(ctx.prepack_layer(vault, tb, tstride))
         ctx.synchronize()
         keep[-2] = tb
+    if ep:
+        import torch.distributed as dist
+        grp = dist.new_group(backend="gloo")
+        handles = [None] * world
+        dist.all_gather_object(handles, ctx.ep_export(), group=grp)
+        ctx.ep_attach(rank, world, handles)
+        barrier(world)
     d_x = torch.from_numpy(xs.view(np.int16)).cuda()          # [64, D] bf16
     d_y = torch.zeros(D, dtype=torch.bfloat16, device="cuda")
     ids = torch.zeros(N_LAYERS, K, dtype=torch.int32, device="cuda")
@@ -223,8 +234,13 @@ def run_ours(args, rank, world, local):
     torch.cuda.synchronize()
 
     def layer(l):      # router + top-k + expert FFN + combine: one fused launch
-        ctx.moe_layer(descs[l], d_x[l].data_ptr(), S.DTYPE_BF16, 1, K, True, d_y, S.DTYPE_BF16,
-                      ids[l], wts[l])
+        if ep:
+            ctx.moe_layer_ep(descs[l], E, base, d_x[l].data_ptr() if rank == 0 else None,
+                             S.DTYPE_BF16, 1, K, True, d_y if rank == 0 else None, S.DTYPE_BF16,
+                             ids[l], wts[l])
+        else:
+            ctx.moe_layer(descs[l], d_x[l].data_ptr(), S.DTYPE_BF16, 1, K, True, d_y, S.DTYPE_BF16,
+                          ids[l], wts[l])
 
     def ffn(l):        # the same with the routing already on the device
         ctx.moe_ffn(descs[l], d_x[l].data_ptr(), S.DTYPE_BF16, ids[l], wts[l], K, 1, d_y,
@@ -234,7 +250,8 @@ def run_ours(args, rank, world, local):
     for i in range(max(args.warmup, 3)):
         for l in range(N_LAYERS):
             layer(l)
-            ffn(l)
+            if not ep:
+                ffn(l)
     ctx.synchronize()
     # One graph = one MoE layer step on each of the 8 resident layers.
     g_step, g_ffn = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
@@ -243,7 +260,10 @@ def run_ours(args, rank, world, local):
             layer(l)
     with torch.cuda.graph(g_ffn, stream=stream):
         for l in range(N_LAYERS):
-            ffn(l)
+            if ep:
+                layer(l)           # routing-given mode is single-GPU: time the layer again
+            else:
+                ffn(l)
     reps = max(1, args.steps // N_LAYERS)
     steps = reps * N_LAYERS
     with torch.cuda.stream(stream):
@@ -251,6 +271,7 @@ def run_ours(args, rank, world, local):
             g_step.replay()
             g_ffn.replay()
     torch.cuda.synchronize()
+    barrier(world)
 
     def timed(graph):
         barrier(world)
@@ -278,7 +299,8 @@ def run_ours(args, rank, world, local):
     ms = max_over_ranks(ms, world)
     per_step = ms / steps
     ffn_ms = ffn_ms_total / steps
-    value = LAYER_BYTES * steps * world / (ms * 1e-3) / 1e9
+    # replicas would be weak scaling; expert parallel splits one layer step
+    value = LAYER_BYTES * steps / (ms * 1e-3) / 1e9
     args.steps = steps
     del d0
 
@@ -292,34 +314,47 @@ def run_ours(args, rank, world, local):
     e0.record(stream)
     with torch.cuda.stream(stream):
         for i in range(args.steps):
-            stage_x.view(torch.int16).copy_(hx[(2000 + i) % 64], non_blocking=True)
             L = descs[i % N_LAYERS]
-            ctx.moe_layer(L, stage_x, S.DTYPE_BF16, 1, K, True, d_y, S.DTYPE_BF16)
-            hy.copy_(d_y, non_blocking=True)
+            if not ep:
+                stage_x.view(torch.int16).copy_(hx[(2000 + i) % 64], non_blocking=True)
+                ctx.moe_layer(L, stage_x, S.DTYPE_BF16, 1, K, True, d_y, S.DTYPE_BF16)
+                hy.copy_(d_y, non_blocking=True)
+            elif rank == 0:
+                stage_x.view(torch.int16).copy_(hx[(2000 + i) % 64], non_blocking=True)
+                ctx.moe_layer_ep(L, E, base, stage_x, S.DTYPE_BF16, 1, K, True, d_y, S.DTYPE_BF16)
+                hy.copy_(d_y, non_blocking=True)
+            else:
+                ctx.moe_layer_ep(L, E, base, None, S.DTYPE_BF16, 1, K, True, None, S.DTYPE_BF16)
     e1.record(stream)
     torch.cuda.synchronize()
     ctx.synchronize()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
-    e2e = LAYER_BYTES * args.steps * world / (e2e_ms * 1e-3) / 1e9
+    e2e = LAYER_BYTES * args.steps / (e2e_ms * 1e-3) / 1e9
 
     if rank == 0:
         peak, peak_kind = peaks()
-        ach = FFN_BYTES / (ffn_ms * 1e-3) / 1e9
+        # per GPU: the fused kernel's share of the expert bytes / its time
+        ach = FFN_BYTES / world / (ffn_ms * 1e-3) / 1e9
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step, 5),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "higher_is_better": True, "scaling": "strong" if ep else "weak", "vs_baseline": None,
+            "dtype": "bf16",
             "data": "synthetic (seeded; BASELINE config-1 distributions)",
             "config": {"workload": "config1: Qwen3-30B-A3B MoE layer (d 2048, 128 experts, "
                                    "top-8, d_ff 768, AFFINE-Q4 g64), batch 1, bf16 in/out",
                        "layers_cycled": N_LAYERS, "l2": "inputs larger than L2 (8 resident "
                        "layers x 340 MB cycled, fresh x per step)",
-                       "parallelism": f"replicas x{world}"},
+                       "parallelism": (f"expert parallel x{world} ({per} experts per GPU, exchange "
+                                       "in-kernel over NVLink)") if ep else "single GPU"},
             "layer_us": round(per_step * 1e3, 3),
             "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(ach / peak, 4), "traffic": NCU_TRAFFIC,
-                         "kernel": "k_moe_fused (expert FFN + combine, routing given), 21,233,664 B "
-                                   f"per launch, {ffn_ms * 1e3:.2f} us avg", "peak_kind": peak_kind},
+                         "frac": round(ach / peak, 4), "traffic": None if ep else NCU_TRAFFIC,
+                         "kernel": (f"k_moe_fused expert parallel (layer incl. routing and NVLink "
+                                    f"exchange), {FFN_BYTES // world:,} B of experts per GPU per launch, "
+                                    f"{ffn_ms * 1e3:.2f} us avg") if ep else
+                                   ("k_moe_fused (expert FFN + combine, routing given), 21,233,664 B "
+                                    f"per launch, {ffn_ms * 1e3:.2f} us avg"), "peak_kind": peak_kind},
             "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": D * 2,
                     "d2h_bytes_per_step": D * 2},
             "gpu_launches": int(launches),

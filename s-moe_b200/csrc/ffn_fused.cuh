@@ -44,7 +44,8 @@ constexpr int kFusedCluster = 4;                   // CTAs that pre-reduce parti
 struct FusedState {          // device scratch, zero at context creation and on exit
     uint32_t rdone;                 // router logit rows finished
     uint32_t done;                  // CTAs finished
-    uint32_t pad[6];
+    uint32_t epoch;                 // expert-parallel launches completed (advanced by the last CTA)
+    uint32_t pad[5];
 };
 
 SMOE_DEVINL void consumer_sync() {
@@ -231,13 +232,15 @@ struct FusedGeom {
 //          written by rank r's last CTA with peer stores;
 //   done0  ranks whose partial has arrived (system-scope atomics); rank 0's
 //          last CTA waits for world - 1, sums, writes y and resets it.
+// The epoch of a launch is the rank's count of completed expert-parallel
+// launches + 1, kept on the device (so graph replays advance it); every rank
+// runs the same launch sequence, so the epochs agree.
 // Routing is computed on every rank (same weights, same x, same code: the
 // same ids); each rank runs the units of the slots whose expert it holds.
 constexpr int kEpMaxWorld = 8;
 struct FusedEp {
     int world, rank;
     uint32_t base, nlocal;     // global id of this rank's first expert, experts held
-    uint32_t epoch;            // launch number, equal on every rank
     uint8_t* x0;
     uint32_t* flag0;
     float* part0;

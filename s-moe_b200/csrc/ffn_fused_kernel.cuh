@@ -109,6 +109,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const FusedEp& ep = A.ep;
     const bool epm = ep.world > 1;
+    const uint32_t epoch = epm ? A.st->epoch + 1u : 0u;            // written by the previous launch only
     uint32_t* s_loc = reinterpret_cast<uint32_t*>(sm + g.o_loc);     // expert parallel: local slots, count
     // this CTA's units [u0, u1) of nU: every unit of every slot, or (expert
     // parallel) of the slots whose expert this rank holds, known after routing
@@ -128,7 +129,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
             for (size_t i = tid; i < xbytes / 16; i += blockDim.x)
                 reinterpret_cast<uint4*>(ep.x0)[i] = reinterpret_cast<const uint4*>(f.x)[i];
         } else if (ep.rank > 0) {
-            if (tid == 0 && !spin_sys_until_geq(ep.flag0, ep.epoch)) atomicExch(f.err, SMOE_DEVERR_SPIN_TIMEOUT);
+            if (tid == 0 && !spin_sys_until_geq(ep.flag0, epoch)) atomicExch(f.err, SMOE_DEVERR_SPIN_TIMEOUT);
             xsrc = ep.x0;
         }
     }
@@ -158,7 +159,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
     __syncthreads();              // (ranks > 0: rank 0's x is published; rank 0 CTA 0: x0 is written)
     if (epm && ep.rank == 0 && blockIdx.x == 0 && tid == 0) {
         __threadfence_system();
-        st_release_sys(ep.flag0, ep.epoch);
+        st_release_sys(ep.flag0, epoch);
     }
     int pre = 0;                                                // units issued ahead of the main loop
     if (!A.rw && warp == kFusedProdWarp) {
@@ -569,6 +570,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
         if (tid == 0) {
             A.st->rdone = 0;
             A.st->done = 0;
+            if (epm) A.st->epoch = epoch;
         }
         __threadfence();
     }

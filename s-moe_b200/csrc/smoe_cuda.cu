@@ -71,7 +71,6 @@ struct SmoeCudaCtx {
     size_t ep_win_bytes = 0;
     uint8_t* ep_peer0 = nullptr;
     int ep_world = 0, ep_rank = 0;
-    uint32_t ep_epoch = 0;
 };
 
 namespace {
@@ -728,7 +727,11 @@ int smoe_cuda_ep_attach(SmoeCudaCtx* c, int rank, int world, const SmoeEpHandle*
     }
     c->ep_rank = rank;
     c->ep_world = world;
-    c->ep_epoch = 0;
+    // a fresh exchange: window and this rank's epoch count start at 0 (every
+    // rank attaches before any rank launches an expert-parallel layer)
+    CK(cudaMemsetAsync(c->ep_win, 0, c->ep_win_bytes, c->stream));
+    CK(cudaMemsetAsync(&c->fstate->epoch, 0, sizeof(uint32_t), c->stream));
+    CK(cudaStreamSynchronize(c->stream));
     return SMOE_OK;
 }
 
@@ -760,7 +763,6 @@ int smoe_cuda_moe_layer_ep(SmoeCudaCtx* c, const SmoeMoeLayer* shard, uint32_t n
     ep.rank = c->ep_rank;
     ep.base = expert_base;
     ep.nlocal = shard->n_experts;
-    ep.epoch = ++c->ep_epoch;
     ep.x0 = c->ep_peer0 + kEpXOff;
     ep.flag0 = reinterpret_cast<uint32_t*>(c->ep_peer0 + kEpFlagOff);
     ep.done0 = reinterpret_cast<uint32_t*>(c->ep_peer0 + kEpDoneOff);

@@ -52,6 +52,7 @@ def main():
     handles = [None] * world
     dist.all_gather_object(handles, mine)
     ctx.ep_attach(rank, world, handles)
+    dist.barrier()                           # every rank attached before any launch
 
     failures = []
     for call in range(3):
