@@ -217,6 +217,7 @@ def run_ours(args, rank, world, local):
         # vault-layout copy is dropped afterwards)
         tstride = S.tiled_stride(S.FMT_AFFINE_Q4, D, DFF)
         tb = torch.empty(per * tstride, dtype=torch.uint8, device="cuda")
+        torch.cuda.synchronize()             # the arena was copied on torch's stream
         descs.append(ctx.prepack_layer(vault, tb, tstride))
         ctx.synchronize()
         keep[-2] = tb

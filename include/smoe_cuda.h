@@ -279,6 +279,67 @@ int smoe_cuda_sample(SmoeCudaCtx* ctx, float* logits, uint32_t vocab, uint32_t b
  * one 32-bit std::mt19937 word (what sample_token consumes per call). */
 float smoe_cuda_canonical_from_u32(uint32_t word);
 
+/* ---- Dense trunk of a decode step around the MoE layer. All pointers are
+ * device pointers; calls are asynchronous on the context stream unless
+ * stated (so a whole decode step can be captured in one CUDA graph).
+ * Not bit-exact with the reference's CPU loops (tree reductions, CUDA
+ * exp/cos/sin), like the reference's own Metal attention. */
+
+/* Mirror of SmoeAttnLayerArgs (metal_bridge.h:171-194), same fields. */
+typedef struct SmoeCudaAttnLayerArgs {
+    const uint16_t* w_q;        /* [q_dim x d_model] bf16 */
+    const uint16_t* w_k;        /* [kv_dim x d_model] bf16 */
+    const uint16_t* w_v;        /* [kv_dim x d_model] bf16 */
+    const uint16_t* w_o;        /* [d_model x q_dim] bf16 */
+    const uint16_t* q_norm_w;   /* [head_dim] bf16, NULL: no QK norm */
+    const uint16_t* k_norm_w;
+    const float*    rope_cos;   /* [head_dim/2] for this token's position */
+    const float*    rope_sin;
+    const float*    normed_in;  /* [d_model] post input-norm hidden */
+    float*          qbuf;       /* [q_dim] scratch (normed + roped Q on exit) */
+    float*          kbuf;       /* [kv_dim] */
+    float*          vbuf;       /* [kv_dim] */
+    float*          k_cache;    /* layer base of the KV ring [attn_ctx x kv_dim] */
+    float*          v_cache;
+    float*          attn_out;   /* [q_dim] scratch */
+    float*          o_out;      /* [d_model] result */
+    uint32_t d_model, q_dim, kv_dim, head_dim, num_heads, num_kv_heads;
+    uint32_t slot;              /* ring write slot (ctx_pos % attn_ctx) */
+    uint32_t valid;             /* attended positions incl. current */
+    uint32_t attn_ctx;          /* ring capacity (<= 8192) */
+    float    attn_scale;        /* 1/sqrt(head_dim) */
+} SmoeCudaAttnLayerArgs;
+
+/* smoe_metal_attention_layer (metal_bridge.h:196): QKV -> per-head QK
+ * RMSNorm -> RoPE -> ring append -> GQA attention -> O. Synchronous. */
+int smoe_cuda_attention_layer(SmoeCudaCtx* ctx, const SmoeCudaAttnLayerArgs* args);
+/* The same, asynchronous. pos (device, optional): the token's position;
+ * when given it overrides slot/valid (slot = pos % attn_ctx, valid =
+ * min(pos + 1, attn_ctx)) so graph replays follow the position. */
+int smoe_cuda_attention_layer_async(SmoeCudaCtx* ctx, const SmoeCudaAttnLayerArgs* args,
+                                    const uint32_t* pos);
+
+/* y[r] = sum_j W[r, j] x[j] (matvec_bf16, common.hpp:293-306), device
+ * pointers, asynchronous; cols % 8 == 0, cols <= 16384. */
+int smoe_cuda_matvec_bf16(SmoeCudaCtx* ctx, const uint16_t* w, const float* x, float* y,
+                          uint32_t rows, uint32_t cols);
+/* For each of `rows` rows: hidden += delta (delta may be NULL), then
+ * normed = rms_norm_bf16(hidden, w) (common.hpp:245-256, eps 1e-6). */
+int smoe_cuda_rms_norm(SmoeCudaCtx* ctx, float* hidden, const float* delta, const uint16_t* w,
+                       float* normed, uint32_t n, uint32_t rows);
+/* out[t] = bf16 embedding row tokens[t] as fp32 (decode.cpp:103-107). */
+int smoe_cuda_embed_bf16(SmoeCudaCtx* ctx, const uint16_t* table, const uint32_t* tokens,
+                         uint32_t n_tokens, uint32_t d_model, float* out);
+/* cos/sin of float(*pos) * inv_freq[i], i < half (decode.cpp:113-118). */
+int smoe_cuda_rope_table(SmoeCudaCtx* ctx, const uint32_t* pos, const float* inv_freq,
+                         float* cos_out, float* sin_out, uint32_t half);
+/* End of a decode step on the device: append *token to the row's history
+ * (history_len < hcap), ++*pos, and row->u = u_seq[*pos % u_len] when
+ * u_seq is given. */
+int smoe_cuda_decode_advance(SmoeCudaCtx* ctx, SmoeSamplerRow* row, uint32_t* history,
+                             uint32_t hcap, const uint32_t* token, uint32_t* pos,
+                             const float* u_seq, uint32_t u_len);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -15,6 +15,7 @@
 #include "ffn_fused_kernel.cuh"
 #include "router.cuh"
 #include "sampler.cuh"
+#include "decode.cuh"
 
 namespace {
 
@@ -117,7 +118,9 @@ int wait_event_bounded(SmoeCudaCtx* c, cudaEvent_t ev) {
 
 template <typename K>
 int prep_kernel(SmoeCudaCtx* c, K kern, size_t smem) {
-    if (smem > 48 * 1024) {
+    // (also below 48 KB of dynamic memory: with the kernel's static shared
+    // memory the total may still exceed the default limit)
+    if (smem > 0) {
         if (smem > c->smem_optin) {
             set_err("kernel needs %s%ld bytes of shared memory", "", (long)smem);
             return SMOE_ERR_ARG;
@@ -685,6 +688,122 @@ int smoe_cuda_moe_layer(SmoeCudaCtx* c, const SmoeMoeLayer* L, const void* x, in
                                    k, norm, ids, wts, nullptr);
     if (rc) return rc;
     return smoe_cuda_moe_ffn(c, L, x, x_dtype, ids, wts, k, batch, y, y_dtype);
+}
+
+// ------------------------------------------------------- dense trunk (decode)
+namespace {
+int gemv_set(SmoeCudaCtx* c, const smoe::GemvSet& g) {
+    uint32_t total = 0;
+    for (uint32_t m = 0; m < g.nmat; ++m) {
+        if (!g.w[m] || !g.y[m] || !aligned16(g.w[m])) { set_err("bad matvec operand %s%ld", "", (long)m); return SMOE_ERR_ARG; }
+        total += g.rows[m];
+    }
+    if (!g.x || g.cols == 0 || g.cols % 8 || g.cols > 16384) { set_err("bad matvec cols %s%ld", "", (long)g.cols); return SMOE_ERR_ARG; }
+    const size_t smem = size_t(g.cols) * 4;
+    int rc = prep_kernel(c, smoe::k_gemv_set, smem);
+    if (rc) return rc;
+    smoe::k_gemv_set<<<(total + smoe::kGemvRowsPerCta - 1) / smoe::kGemvRowsPerCta, 256, smem, c->stream>>>(g);
+    c->dispatches += 1;
+    return cudaGetLastError() == cudaSuccess ? SMOE_OK : SMOE_ERR_CUDA;
+}
+}  // namespace
+
+int smoe_cuda_matvec_bf16(SmoeCudaCtx* c, const uint16_t* w, const float* x, float* y, uint32_t rows,
+                          uint32_t cols) {
+    if (!c) { set_err("null context %s%ld", "", 0); return SMOE_ERR_ARG; }
+    smoe::GemvSet g{};
+    g.w[0] = w;
+    g.y[0] = y;
+    g.rows[0] = rows;
+    g.nmat = 1;
+    g.cols = cols;
+    g.x = x;
+    return gemv_set(c, g);
+}
+
+int smoe_cuda_rms_norm(SmoeCudaCtx* c, float* hidden, const float* delta, const uint16_t* w, float* normed,
+                       uint32_t n, uint32_t rows) {
+    if (!c || !hidden || !w || !normed || n == 0 || rows == 0) { set_err("bad rms_norm arguments %s%ld", "", (long)n); return SMOE_ERR_ARG; }
+    smoe::k_add_rms_norm<<<rows, 1024, 0, c->stream>>>(hidden, delta, w, normed, n);
+    c->dispatches += 1;
+    return cudaGetLastError() == cudaSuccess ? SMOE_OK : SMOE_ERR_CUDA;
+}
+
+int smoe_cuda_embed_bf16(SmoeCudaCtx* c, const uint16_t* table, const uint32_t* tokens, uint32_t n_tokens,
+                         uint32_t d_model, float* out) {
+    if (!c || !table || !tokens || !out || n_tokens == 0 || d_model == 0) { set_err("bad embed arguments %s%ld", "", 0); return SMOE_ERR_ARG; }
+    smoe::k_embed<<<dim3((d_model + 255) / 256, n_tokens), 256, 0, c->stream>>>(table, tokens, d_model, out);
+    c->dispatches += 1;
+    return cudaGetLastError() == cudaSuccess ? SMOE_OK : SMOE_ERR_CUDA;
+}
+
+int smoe_cuda_rope_table(SmoeCudaCtx* c, const uint32_t* pos, const float* inv_freq, float* cos_out,
+                         float* sin_out, uint32_t half) {
+    if (!c || !pos || !inv_freq || !cos_out || !sin_out || half == 0) { set_err("bad rope arguments %s%ld", "", 0); return SMOE_ERR_ARG; }
+    smoe::k_rope_table<<<(half + 127) / 128, 128, 0, c->stream>>>(pos, inv_freq, cos_out, sin_out, half);
+    c->dispatches += 1;
+    return cudaGetLastError() == cudaSuccess ? SMOE_OK : SMOE_ERR_CUDA;
+}
+
+int smoe_cuda_decode_advance(SmoeCudaCtx* c, SmoeSamplerRow* row, uint32_t* history, uint32_t hcap,
+                             const uint32_t* token, uint32_t* pos, const float* u_seq, uint32_t u_len) {
+    if (!c || !row || !token || !pos || (hcap && !history)) { set_err("bad decode_advance arguments %s%ld", "", 0); return SMOE_ERR_ARG; }
+    static_assert(sizeof(SmoeSamplerRow) == sizeof(smoe::SamplerRowDevMut), "row layout");
+    smoe::k_decode_advance<<<1, 32, 0, c->stream>>>(reinterpret_cast<smoe::SamplerRowDevMut*>(row), history,
+                                                     hcap, token, pos, u_seq, u_len);
+    c->dispatches += 1;
+    return cudaGetLastError() == cudaSuccess ? SMOE_OK : SMOE_ERR_CUDA;
+}
+
+int smoe_cuda_attention_layer_async(SmoeCudaCtx* c, const SmoeCudaAttnLayerArgs* a, const uint32_t* pos) {
+    if (!c || !a || !a->w_q || !a->w_k || !a->w_v || !a->w_o || !a->rope_cos || !a->rope_sin ||
+        !a->normed_in || !a->qbuf || !a->kbuf || !a->vbuf || !a->k_cache || !a->v_cache || !a->attn_out ||
+        !a->o_out || a->head_dim == 0 || a->head_dim > 256 || a->head_dim % 32 || a->num_kv_heads == 0 ||
+        a->num_heads % a->num_kv_heads || a->q_dim != a->num_heads * a->head_dim ||
+        a->kv_dim != a->num_kv_heads * a->head_dim || a->attn_ctx == 0 || a->attn_ctx > smoe::kAttnMaxCtx ||
+        (!pos && (a->valid == 0 || a->valid > a->attn_ctx || a->slot >= a->attn_ctx))) {
+        set_err("bad attention-layer arguments %s%ld", "", 0);
+        return SMOE_ERR_ARG;
+    }
+    // 1. Q, K, V projections of the normed input (one launch)
+    smoe::GemvSet g{};
+    g.w[0] = a->w_q; g.y[0] = a->qbuf; g.rows[0] = a->q_dim;
+    g.w[1] = a->w_k; g.y[1] = a->kbuf; g.rows[1] = a->kv_dim;
+    g.w[2] = a->w_v; g.y[2] = a->vbuf; g.rows[2] = a->kv_dim;
+    g.nmat = 3;
+    g.cols = a->d_model;
+    g.x = a->normed_in;
+    int rc = gemv_set(c, g);
+    if (rc) return rc;
+    // 2. per-head QK norm + RoPE, ring append; 3. attention
+    smoe::AttnArgs t{};
+    t.q = a->qbuf; t.k = a->kbuf; t.v = a->vbuf;
+    t.q_norm_w = a->q_norm_w; t.k_norm_w = a->k_norm_w;
+    t.rope_cos = a->rope_cos; t.rope_sin = a->rope_sin;
+    t.qbuf = a->qbuf; t.kbuf = a->kbuf; t.vbuf = a->vbuf;
+    t.k_cache = a->k_cache; t.v_cache = a->v_cache;
+    t.attn_out = a->attn_out;
+    t.q_dim = a->q_dim; t.kv_dim = a->kv_dim; t.head_dim = a->head_dim;
+    t.num_heads = a->num_heads; t.num_kv_heads = a->num_kv_heads;
+    t.slot = a->slot; t.valid = a->valid; t.attn_ctx = a->attn_ctx;
+    t.pos = pos;
+    t.scale = a->attn_scale;
+    smoe::k_qk_rope_append<<<a->num_heads + 2 * a->num_kv_heads, a->head_dim, 0, c->stream>>>(t);
+    smoe::k_attn_decode<<<a->num_heads, smoe::kAttnThreads, 0, c->stream>>>(t);
+    c->dispatches += 2;
+    // 4. O projection
+    smoe::GemvSet o{};
+    o.w[0] = a->w_o; o.y[0] = a->o_out; o.rows[0] = a->d_model;
+    o.nmat = 1;
+    o.cols = a->q_dim;
+    o.x = a->attn_out;
+    return gemv_set(c, o);
+}
+
+int smoe_cuda_attention_layer(SmoeCudaCtx* c, const SmoeCudaAttnLayerArgs* a) {
+    int rc = smoe_cuda_attention_layer_async(c, a, nullptr);
+    if (rc) return rc;
+    return smoe_cuda_synchronize(c);      // o_out valid on return, as metal_bridge.h:163-169
 }
 
 // ----------------------------------------------------------- expert parallel

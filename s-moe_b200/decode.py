@@ -1,0 +1,286 @@
+"""Batch-1 decode of a Qwen3-MoE-shaped model through libsmoe_cuda.
+
+Host-side restatement of the reference's token step (decode.cpp:103-231 and
+the MoE block that follows it, main.cpp:621-641 for the final norm, LM head
+and sampler) over the C ABI: every operation is a kernel of the library,
+and one whole step - embedding, L x (input norm, attention layer, post norm,
+fused MoE layer), final norm, LM head, sampler, bookkeeping - is captured
+once as a CUDA graph. The token, its position, the sampler row (history
+length, uniform draw) and the history live on the device, so a replay needs
+no host work; prompt tokens are written into the token slot before their
+step. (During the prompt the sampled token is discarded but still appended
+to the device history, which the repetition penalty reads.)
+
+    python s-moe_b200/decode.py --layers 48 --gen 256     # 30B-shaped decode timing
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import sys
+import time
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+import smoe_cuda as S  # noqa: E402
+
+
+@dataclass
+class Shape:
+    layers: int = 48
+    d_model: int = 2048
+    num_heads: int = 32
+    num_kv_heads: int = 4
+    head_dim: int = 128
+    n_experts: int = 128
+    top_k: int = 8
+    d_ff: int = 768
+    vocab: int = 151_936
+    rope_theta: float = 1_000_000.0
+    norm_topk: bool = True
+    attn_ctx: int = 4096
+    fmt: int = S.FMT_AFFINE_Q4
+
+    @property
+    def q_dim(self):
+        return self.num_heads * self.head_dim
+
+    @property
+    def kv_dim(self):
+        return self.num_kv_heads * self.head_dim
+
+
+def rope_inv_freq(shape: Shape) -> np.ndarray:
+    """engine.cpp:351-356: 1 / theta^(2d / head_dim), in fp32."""
+    half = shape.head_dim // 2
+    return np.array([1.0 / math.pow(shape.rope_theta, float(2 * d) / float(shape.head_dim))
+                     for d in range(half)], np.float32)
+
+
+def _bf16(t: torch.Tensor) -> torch.Tensor:
+    return t.to(torch.bfloat16).contiguous()
+
+
+class Model:
+    """Device-resident weights. `weights` (numpy, for tests): dict with
+    embed [V*d] u16, lm_head [V*d] u16, model_norm [d] u16, and per layer
+    lists in_norm, post_norm [d] u16, q_norm, k_norm [hd] u16, w_q, w_k, w_v,
+    w_o u16, router [E*d] u16, experts (arena [E, stride] u8, stride, off)
+    in the vault layout. Without `weights`, random weights with the
+    benchmark's distributions are generated on the device (seeded)."""
+
+    def __init__(self, ctx: "S.Context", shape: Shape, weights=None, seed: int = 7):
+        self.ctx, self.shape = ctx, shape
+        sh = shape
+        dev = "cuda"
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+
+        def from_np(a):
+            return torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).to(dev)
+
+        def randn_bf16(n, std):
+            return _bf16(torch.randn(n, generator=g, device=dev) * std).view(torch.int16)
+
+        def ones_bf16(n):
+            return _bf16(torch.ones(n, device=dev)).view(torch.int16)
+
+        W = weights
+        self.embed = from_np(W["embed"]) if W else randn_bf16(sh.vocab * sh.d_model, 0.02)
+        self.lm_head = from_np(W["lm_head"]) if W else randn_bf16(sh.vocab * sh.d_model, 0.02)
+        self.model_norm = from_np(W["model_norm"]) if W else ones_bf16(sh.d_model)
+        self.layers = []
+        tstride = S.tiled_stride(sh.fmt, sh.d_model, sh.d_ff)
+        for l in range(sh.layers):
+            L = {}
+            for name, n in (("w_q", sh.q_dim * sh.d_model), ("w_k", sh.kv_dim * sh.d_model),
+                            ("w_v", sh.kv_dim * sh.d_model), ("w_o", sh.d_model * sh.q_dim),
+                            ("router", sh.n_experts * sh.d_model)):
+                L[name] = from_np(W[name][l]) if W else randn_bf16(n, 0.02)
+            for name, n in (("in_norm", sh.d_model), ("post_norm", sh.d_model), ("q_norm", sh.head_dim),
+                            ("k_norm", sh.head_dim)):
+                L[name] = from_np(W[name][l]) if W else ones_bf16(n)
+            if W:
+                arena, stride, off = W["experts"][l]
+                varena = torch.from_numpy(np.ascontiguousarray(arena)).to(dev)
+            else:
+                varena, stride, off = self._random_experts(g)
+            vault = S.make_layer(varena, stride, off, sh.n_experts, sh.d_model, sh.d_ff, sh.fmt, L["router"])
+            tb = torch.empty(sh.n_experts * tstride, dtype=torch.uint8, device=dev)
+            # the arena was written on torch's stream, the prepack runs on the
+            # context's: finish the former first, the latter before the arena
+            # goes back to torch's allocator
+            torch.cuda.synchronize()
+            L["tiled"] = ctx.prepack_layer(vault, tb, tstride)
+            ctx.synchronize()
+            L["tiled_buf"] = tb
+            del varena, vault
+            self.layers.append(L)
+        torch.cuda.synchronize()
+
+    def _random_experts(self, g):
+        """Vault-layout arena on the device: codes U{0..15}, AFFINE scale
+        bf16 ~ U(0.001, 0.01), bias bf16 ~ N(0, 0.01^2), group 64."""
+        sh = self.shape
+        off, total = S.blob_layout(sh.fmt, sh.d_model, sh.d_ff)
+        stride = (total + 255) // 256 * 256
+        arena = torch.zeros(sh.n_experts, stride, dtype=torch.uint8, device="cuda")
+        for m in range(3):
+            rows, cols = (sh.d_ff, sh.d_model) if m < 2 else (sh.d_model, sh.d_ff)
+            nb, ng = rows * cols // 2, rows * cols // 64
+            arena[:, off[3 * m]:off[3 * m] + nb] = torch.randint(0, 256, (sh.n_experts, nb), generator=g,
+                                                                   device="cuda", dtype=torch.int32).to(torch.uint8)
+            sc = _bf16(torch.rand(sh.n_experts, ng, generator=g, device="cuda") * 0.009 + 0.001)
+            arena[:, off[3 * m + 1]:off[3 * m + 1] + 2 * ng] = sc.view(torch.uint8).view(sh.n_experts, 2 * ng)
+            if sh.fmt == S.FMT_AFFINE_Q4:
+                bi = _bf16(torch.randn(sh.n_experts, ng, generator=g, device="cuda") * 0.01)
+                arena[:, off[3 * m + 2]:off[3 * m + 2] + 2 * ng] = bi.view(torch.uint8).view(sh.n_experts, 2 * ng)
+        return arena, stride, off
+
+
+class Decoder:
+    """One sequence, batch 1. Step graph: see the module docstring."""
+
+    def __init__(self, model: Model, temperature=0.7, top_p=0.8, top_k=20, rep_penalty=1.1,
+                 uniforms: np.ndarray | None = None, hcap: int = 8192):
+        self.m, self.ctx = model, model.ctx
+        sh = model.shape
+        f32 = dict(dtype=torch.float32, device="cuda")
+        self.hidden = torch.zeros(sh.d_model, **f32)
+        self.normed = torch.zeros(sh.d_model, **f32)
+        self.attn_o = torch.zeros(sh.d_model, **f32)
+        self.ffn_out = torch.zeros(sh.d_model, **f32)
+        self.qbuf = torch.zeros(sh.q_dim, **f32)
+        self.kbuf = torch.zeros(sh.kv_dim, **f32)
+        self.vbuf = torch.zeros(sh.kv_dim, **f32)
+        self.attn_out = torch.zeros(sh.q_dim, **f32)
+        self.kv = torch.zeros(sh.layers, 2, sh.attn_ctx, sh.kv_dim, **f32)
+        self.rope_cos = torch.zeros(sh.head_dim // 2, **f32)
+        self.rope_sin = torch.zeros(sh.head_dim // 2, **f32)
+        self.inv_freq = torch.from_numpy(rope_inv_freq(sh)).cuda()
+        self.logits = torch.zeros(sh.vocab, **f32)
+        self.token = torch.zeros(1, dtype=torch.int32, device="cuda")
+        self.pos = torch.zeros(1, dtype=torch.int32, device="cuda")
+        self.hcap = hcap
+        self.history = torch.zeros(hcap, dtype=torch.int32, device="cuda")
+        row = np.zeros(6, np.float32)
+        row[0:2] = (temperature, top_p)
+        row.view(np.uint32)[2] = top_k
+        row[3:5] = (rep_penalty, 0.5)
+        row.view(np.uint32)[5] = 0
+        self.row = torch.from_numpy(row.view(np.int32)).cuda()
+        self.u_seq = torch.from_numpy((uniforms if uniforms is not None else np.full(1, 0.5)).astype(np.float32)).cuda()
+        torch.cuda.synchronize()
+        self.args = []
+        for l, L in enumerate(model.layers):
+            a = S.AttnLayerArgs()
+            for name in ("w_q", "w_k", "w_v", "w_o"):
+                setattr(a, name, L[name].data_ptr())
+            a.q_norm_w, a.k_norm_w = L["q_norm"].data_ptr(), L["k_norm"].data_ptr()
+            a.rope_cos, a.rope_sin = self.rope_cos.data_ptr(), self.rope_sin.data_ptr()
+            a.normed_in = self.normed.data_ptr()
+            a.qbuf, a.kbuf, a.vbuf = self.qbuf.data_ptr(), self.kbuf.data_ptr(), self.vbuf.data_ptr()
+            a.k_cache, a.v_cache = self.kv[l, 0].data_ptr(), self.kv[l, 1].data_ptr()
+            a.attn_out, a.o_out = self.attn_out.data_ptr(), self.attn_o.data_ptr()
+            a.d_model, a.q_dim, a.kv_dim = sh.d_model, sh.q_dim, sh.kv_dim
+            a.head_dim, a.num_heads, a.num_kv_heads = sh.head_dim, sh.num_heads, sh.num_kv_heads
+            a.slot, a.valid, a.attn_ctx = 0, 1, sh.attn_ctx
+            a.attn_scale = 1.0 / math.sqrt(sh.head_dim)
+            self.args.append(a)
+        self.graph = None
+
+    def _step(self):
+        """One token step, all on the context stream (decode.cpp:103-231 +
+        MoE block, main.cpp:621-641)."""
+        c, sh = self.ctx, self.m.shape
+        c.embed_bf16(self.m.embed, self.token, 1, sh.d_model, self.hidden)
+        c.rope_table(self.pos, self.inv_freq, self.rope_cos, self.rope_sin, sh.head_dim // 2)
+        for l, L in enumerate(self.m.layers):
+            c.rms_norm(self.hidden, self.ffn_out if l > 0 else None, L["in_norm"], self.normed, sh.d_model)
+            c.attention_layer(self.args[l], pos=self.pos)
+            c.rms_norm(self.hidden, self.attn_o, L["post_norm"], self.normed, sh.d_model)
+            c.moe_layer(L["tiled"], self.normed, S.DTYPE_F32, 1, sh.top_k, sh.norm_topk, self.ffn_out, S.DTYPE_F32)
+        c.rms_norm(self.hidden, self.ffn_out, self.m.model_norm, self.normed, sh.d_model)
+        c.matvec_bf16(self.m.lm_head, self.normed, self.logits, sh.vocab, sh.d_model)
+        c.sample(self.logits, sh.vocab, 1, self.row, self.history, self.hcap, self.token)
+        c.decode_advance(self.row, self.history, self.hcap, self.token, self.pos, self.u_seq, self.u_seq.numel())
+
+    def capture(self, stream: torch.cuda.Stream):
+        self.stream = stream
+        self.ctx.set_stream(stream.cuda_stream)
+        with torch.cuda.stream(stream):
+            self._step()                  # eager once: kernel attributes set before capture
+        torch.cuda.synchronize()
+        self.reset()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=stream):
+            self._step()
+        torch.cuda.synchronize()
+
+    def reset(self):
+        torch.cuda.synchronize()
+        self.kv.zero_()
+        self.pos.zero_()
+        self.history.zero_()
+        self.row[5] = 0
+        torch.cuda.synchronize()
+
+    def run(self, prompt: list[int], n_gen: int):
+        """Prompt tokens then n_gen sampled tokens (graph replays); returns
+        (generated ids, seconds spent generating, device time)."""
+        assert self.graph is not None
+        with torch.cuda.stream(self.stream):
+            for tok in prompt:
+                self.token.fill_(int(tok))
+                self.graph.replay()
+            toks = torch.zeros(n_gen, dtype=torch.int32, device="cuda")
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(self.stream)
+            for i in range(n_gen):
+                self.graph.replay()
+                toks[i:i + 1].copy_(self.token)
+            e1.record(self.stream)
+            torch.cuda.synchronize()
+        return toks.cpu().numpy().tolist(), e0.elapsed_time(e1) / 1e3
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--layers", type=int, default=48)
+    ap.add_argument("--prompt", type=int, default=45)
+    ap.add_argument("--gen", type=int, default=256)
+    args = ap.parse_args()
+    sh = Shape(layers=args.layers)
+    ctx = S.Context(0)
+    t0 = time.time()
+    model = Model(ctx, sh)
+    t_load = time.time() - t0
+    rng = np.random.default_rng(11)
+    dec = Decoder(model, uniforms=rng.integers(0, 1 << 24, 4096).astype(np.float64) / (1 << 24))
+    dec.capture(torch.cuda.Stream())
+    prompt = rng.integers(0, sh.vocab, args.prompt).tolist()
+    dec.run(prompt, 8)                                   # warm-up
+    dec.reset()
+    toks, t = dec.run(prompt, args.gen)
+    ctx.synchronize()
+    attn = (2 * sh.q_dim + 2 * sh.kv_dim) * sh.d_model * 2           # q, k, v, o bf16
+    per_token_bytes = (sh.layers * (sh.top_k * S.expert_bytes(sh.fmt, sh.d_model, sh.d_ff) + attn
+                                    + sh.n_experts * sh.d_model * 2) + sh.vocab * sh.d_model * 2)
+    print(json.dumps({"workload": f"Qwen3-30B-A3B-shaped decode, {sh.layers} layers, batch 1, prompt "
+                                  f"{args.prompt}, {args.gen} generated (random weights)",
+                      "tok_per_s": round(args.gen / t, 2), "ms_per_token": round(1e3 * t / args.gen, 4),
+                      "load_s": round(t_load, 1), "weights_gb_per_token": round(per_token_bytes / 1e9, 3),
+                      "achieved_gbs": round(per_token_bytes * args.gen / t / 1e9, 1),
+                      "first_tokens": toks[:8]}))
+    ctx.close()
+
+
+if __name__ == "__main__":
+    main()

@@ -36,7 +36,19 @@ EXPORTS = [
     "smoe_cuda_canonical_from_u32", "smoe_cuda_moe_ffn_noalloc", "smoe_cuda_noalloc_last_error",
     "smoe_cuda_tiled_expert_bytes", "smoe_cuda_prepack_layer",
     "smoe_cuda_ep_export", "smoe_cuda_ep_attach", "smoe_cuda_moe_layer_ep",
+    "smoe_cuda_attention_layer", "smoe_cuda_attention_layer_async", "smoe_cuda_matvec_bf16",
+    "smoe_cuda_rms_norm", "smoe_cuda_embed_bf16", "smoe_cuda_rope_table", "smoe_cuda_decode_advance",
 ]
+
+
+class AttnLayerArgs(C.Structure):
+    """SmoeCudaAttnLayerArgs (device pointers)."""
+    _fields_ = [(n, C.c_void_p) for n in ("w_q", "w_k", "w_v", "w_o", "q_norm_w", "k_norm_w", "rope_cos",
+                                          "rope_sin", "normed_in", "qbuf", "kbuf", "vbuf", "k_cache",
+                                          "v_cache", "attn_out", "o_out")] + \
+              [(n, C.c_uint32) for n in ("d_model", "q_dim", "kv_dim", "head_dim", "num_heads",
+                                         "num_kv_heads", "slot", "valid", "attn_ctx")] + \
+              [("attn_scale", C.c_float)]
 
 
 class EpHandle(C.Structure):
@@ -119,6 +131,13 @@ def lib():
                                           i32, vp, vp]
         L.smoe_cuda_sample.argtypes = [vp, vp, u32, u32, vp, vp, u32, vp]
         L.smoe_cuda_ep_export.argtypes = [vp, C.POINTER(EpHandle)]
+        L.smoe_cuda_attention_layer.argtypes = [vp, C.POINTER(AttnLayerArgs)]
+        L.smoe_cuda_attention_layer_async.argtypes = [vp, C.POINTER(AttnLayerArgs), vp]
+        L.smoe_cuda_matvec_bf16.argtypes = [vp, vp, vp, vp, u32, u32]
+        L.smoe_cuda_rms_norm.argtypes = [vp, vp, vp, vp, vp, u32, u32]
+        L.smoe_cuda_embed_bf16.argtypes = [vp, vp, vp, u32, u32, vp]
+        L.smoe_cuda_rope_table.argtypes = [vp, vp, vp, vp, vp, u32]
+        L.smoe_cuda_decode_advance.argtypes = [vp, vp, vp, u32, vp, vp, vp, u32]
         L.smoe_cuda_ep_attach.argtypes = [vp, i32, i32, C.POINTER(EpHandle)]
         L.smoe_cuda_moe_layer_ep.argtypes = [vp, C.POINTER(MoeLayer), u32, u32, vp, i32, u32, u32, i32,
                                              vp, i32, vp, vp]
@@ -271,6 +290,31 @@ class Context:
                                              C.byref(out)), "prepack_layer")
         return out
 
+    # ---- dense trunk
+    def attention_layer(self, args: AttnLayerArgs, pos=None, sync=False):
+        if sync:
+            check(self.L.smoe_cuda_attention_layer(self.h, C.byref(args)), "attention_layer")
+        else:
+            check(self.L.smoe_cuda_attention_layer_async(self.h, C.byref(args), ptr(pos)), "attention_layer")
+
+    def matvec_bf16(self, w, x, y, rows, cols):
+        check(self.L.smoe_cuda_matvec_bf16(self.h, ptr(w), ptr(x), ptr(y), rows, cols), "matvec_bf16")
+
+    def rms_norm(self, hidden, delta, w, normed, n, rows=1):
+        check(self.L.smoe_cuda_rms_norm(self.h, ptr(hidden), ptr(delta), ptr(w), ptr(normed), n, rows), "rms_norm")
+
+    def embed_bf16(self, table, tokens, n_tokens, d_model, out):
+        check(self.L.smoe_cuda_embed_bf16(self.h, ptr(table), ptr(tokens), n_tokens, d_model, ptr(out)),
+              "embed_bf16")
+
+    def rope_table(self, pos, inv_freq, cos_out, sin_out, half):
+        check(self.L.smoe_cuda_rope_table(self.h, ptr(pos), ptr(inv_freq), ptr(cos_out), ptr(sin_out), half),
+              "rope_table")
+
+    def decode_advance(self, row, history, hcap, token, pos, u_seq=None, u_len=0):
+        check(self.L.smoe_cuda_decode_advance(self.h, ptr(row), ptr(history), hcap, ptr(token), ptr(pos),
+                                              ptr(u_seq), u_len), "decode_advance")
+
     def sample(self, logits, vocab, batch, rows, history, history_stride, tokens):
         check(self.L.smoe_cuda_sample(self.h, ptr(logits), vocab, batch, ptr(rows), ptr(history),
                                       history_stride, ptr(tokens)), "sample")
@@ -288,6 +332,29 @@ def make_layer(base, stride, off, n_experts, d_model, d_ff, fmt, router_w) -> Mo
     L.fmt = fmt
     L.router_w = ptr(router_w)
     return L
+
+
+def blob_layout(fmt: int, d_model: int, d_ff: int):
+    """Byte offsets of the 9 tensors of one vault expert blob - per matrix
+    (gate [d_ff x d_model], up, down [d_model x d_ff]) nibbles, scales (one
+    16-bit value per 64 weights), biases (AFFINE-Q4 only) - and the blob's
+    byte count without padding (shatter_moe.py:627-674)."""
+    off, cur = [], 0
+    for rows, cols in ((d_ff, d_model), (d_ff, d_model), (d_model, d_ff)):
+        nib, sc = rows * cols // 2, rows * cols // 64 * 2
+        off.append(cur)
+        cur += nib
+        off.append(cur)
+        cur += sc
+        off.append(cur)
+        if fmt == FMT_AFFINE_Q4:
+            cur += sc
+    return off, cur
+
+
+def expert_bytes(fmt: int, d_model: int, d_ff: int) -> int:
+    """Bytes one expert's FFN reads (the vault blob without padding)."""
+    return blob_layout(fmt, d_model, d_ff)[1]
 
 
 def tiled_stride(fmt: int, d_model: int, d_ff: int) -> int:

@@ -45,6 +45,7 @@ def main():
     vault = S.make_layer(d_shard, stride, off, per, d, dff, fmt, d_router)
     tstride = S.tiled_stride(fmt, d, dff)
     tbuf = torch.empty(per * tstride, dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()                 # the shard was copied on torch's stream
     shard = ctx.prepack_layer(vault, tbuf, tstride)
     ctx.synchronize()
 

@@ -45,6 +45,7 @@ def tiled(ctx, layer: "Layer"):
     """Prepack a Layer into the tiled device layout; returns (desc, buffer)."""
     stride = S.tiled_stride(layer.fmt, layer.d, layer.dff)
     buf = torch.empty(layer.E * stride, dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()          # the arena was copied on torch's stream
     desc = ctx.prepack_layer(layer.desc, buf, stride)
     ctx.synchronize()
     return desc, buf
