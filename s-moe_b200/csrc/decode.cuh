@@ -76,6 +76,10 @@ __global__ void k_add_rms_norm(float* hidden, const float* delta, const uint16_t
 
 // Up to 3 bf16 GEMVs over the same fp32 input, one warp per output row:
 // y_m[r] = sum_j W_m[r, j] x[j] (matvec_bf16, common.hpp:293-306).
+// Grid-stride over row pairs: a lane keeps 2 x 8 16-byte weight loads in
+// flight (both rows' chunks, issued before any use) and reads x through L1
+// (the same few KB for every warp), so no staging barrier sits in front of
+// the weight stream. cols % 8 == 0.
 struct GemvSet {
     const uint16_t* w[3];
     float* y[3];
@@ -83,20 +87,76 @@ struct GemvSet {
     uint32_t nmat, cols;
     const float* x;
 };
-constexpr int kGemvRowsPerCta = 8;
-__global__ void __launch_bounds__(256) k_gemv_set(GemvSet a) {
-    extern __shared__ __align__(16) float xs[];
-    for (uint32_t i = threadIdx.x; i < a.cols; i += blockDim.x) xs[i] = a.x[i];
-    __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    uint32_t r = blockIdx.x * kGemvRowsPerCta + warp;
+constexpr int kGemvThreads = 256;
+
+SMOE_DEVINL void gemv_locate(const GemvSet& a, uint32_t r, const uint16_t*& w, float*& y) {
     for (uint32_t m = 0; m < a.nmat; ++m) {
         if (r < a.rows[m]) {
-            const float v = warp_row_dot_bf16(a.w[m] + size_t(r) * a.cols, xs, a.cols, lane);
-            if (lane == 0) a.y[m][r] = v;
+            w = a.w[m] + size_t(r) * a.cols;
+            y = a.y[m] + r;
             return;
         }
         r -= a.rows[m];
+    }
+    w = nullptr;
+    y = nullptr;
+}
+
+SMOE_DEVINL float dot8_bf16(uint4 v, const float4* xp) {
+    const float4 a = __ldg(xp), b = __ldg(xp + 1);
+    float s = __uint_as_float(v.x << 16) * a.x;
+    s = fmaf(__uint_as_float(v.x & 0xffff0000u), a.y, s);
+    s = fmaf(__uint_as_float(v.y << 16), a.z, s);
+    s = fmaf(__uint_as_float(v.y & 0xffff0000u), a.w, s);
+    s = fmaf(__uint_as_float(v.z << 16), b.x, s);
+    s = fmaf(__uint_as_float(v.z & 0xffff0000u), b.y, s);
+    s = fmaf(__uint_as_float(v.w << 16), b.z, s);
+    s = fmaf(__uint_as_float(v.w & 0xffff0000u), b.w, s);
+    return s;
+}
+
+__global__ void __launch_bounds__(kGemvThreads) k_gemv_set(GemvSet a, uint32_t total) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t nwarp = gridDim.x * (kGemvThreads / 32);
+    const uint32_t n = a.cols / 8;                                   // 16-byte chunks per row
+    const float4* x4 = reinterpret_cast<const float4*>(a.x);
+    for (uint32_t r0 = (blockIdx.x * (kGemvThreads / 32) + (threadIdx.x >> 5)) * 2; r0 < total; r0 += nwarp * 2) {
+        const uint16_t *w0, *w1;
+        float *y0, *y1;
+        gemv_locate(a, r0, w0, y0);
+        gemv_locate(a, r0 + 1 < total ? r0 + 1 : r0, w1, y1);
+        if (r0 + 1 >= total) y1 = nullptr;
+        const uint4* p0 = reinterpret_cast<const uint4*>(w0);
+        const uint4* p1 = reinterpret_cast<const uint4*>(w1);
+        float s0 = 0.f, s1 = 0.f;
+        for (uint32_t c0 = lane; c0 < n; c0 += 32 * 8) {
+            uint4 v0[8], v1[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const uint32_t c = c0 + q * 32;
+                if (c < n) {
+                    v0[q] = __ldcs(p0 + c);                          // streamed once: do not keep in L2
+                    v1[q] = __ldcs(p1 + c);
+                }
+            }
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const uint32_t c = c0 + q * 32;
+                if (c < n) {
+                    s0 += dot8_bf16(v0[q], x4 + 2 * c);
+                    s1 += dot8_bf16(v1[q], x4 + 2 * c);
+                }
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+            s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+        }
+        if (lane == 0) {
+            *y0 = s0;
+            if (y1) *y1 = s1;
+        }
     }
 }
 
@@ -135,71 +195,98 @@ SMOE_DEVINL void attn_slot_valid(const AttnArgs& a, uint32_t& slot, uint32_t& va
     }
 }
 
-// One CTA per head: Q heads (QK norm + RoPE -> qbuf), K heads (QK norm +
-// RoPE -> kbuf and the ring slot), V heads (-> vbuf and the ring slot)
-// (decode.cpp:159-195). blockDim = head_dim (<= 1024, multiple of 32). Each
-// thread reads and writes only its own element of q/k/v, so they may alias
-// qbuf/kbuf/vbuf.
-__global__ void k_qk_rope_append(AttnArgs a) {
-    __shared__ float red32[32];
-    __shared__ float row[1024];
-    const uint32_t b = blockIdx.x, t = threadIdx.x, hd = a.head_dim, half = hd / 2;
-    uint32_t slot, valid;
-    attn_slot_valid(a, slot, valid);
-    const bool isq = b < a.num_heads, isk = !isq && b < a.num_heads + a.num_kv_heads;
-    const uint32_t h = isq ? b : isk ? b - a.num_heads : b - a.num_heads - a.num_kv_heads;
-    const float* src = (isq ? a.q : isk ? a.k : a.v) + size_t(h) * hd;
-    float v = src[t];
-    if (isq || isk) {
-        const uint16_t* nw = isq ? a.q_norm_w : a.k_norm_w;
-        if (nw) {
-            const float ss = block_sum(v * v, red32);
-            const float inv = 1.0f / sqrtf(ss / float(hd) + 1e-6f);
-            v = (v * inv) * bf16_bits_to_f32(nw[t]);
-        }
-        row[t] = v;
-        __syncthreads();
+// QK RMSNorm (when w) + half-split RoPE of one head held in x[0..hd) of
+// shared memory, in place; every thread of the CTA calls it (decode.cpp:159-195).
+SMOE_DEVINL void head_norm_rope(float* x, const uint16_t* w, const float* cs, const float* sn, uint32_t hd,
+                                float* red32) {
+    const uint32_t t = threadIdx.x, half = hd / 2;
+    float v = t < hd ? x[t] : 0.f;
+    if (w) {
+        const float ss = block_sum(v * v, red32);
+        const float inv = 1.0f / sqrtf(ss / float(hd) + 1e-6f);
+        if (t < hd) v = (v * inv) * bf16_bits_to_f32(w[t]);
+    }
+    __syncthreads();
+    if (t < hd) x[t] = v;
+    __syncthreads();
+    float r = 0.f;
+    if (t < hd) {
         const uint32_t d = t < half ? t : t - half;
-        const float c = a.rope_cos[d], s = a.rope_sin[d];
-        v = t < half ? row[t] * c - row[t + half] * s : row[t - half] * s + row[t] * c;
+        r = t < half ? x[t] * cs[d] - x[t + half] * sn[d] : x[t - half] * sn[d] + x[t] * cs[d];
     }
-    if (isq) {
-        a.qbuf[size_t(h) * hd + t] = v;
-    } else {
-        (isk ? a.kbuf : a.vbuf)[size_t(h) * hd + t] = v;
-        (isk ? a.k_cache : a.v_cache)[size_t(slot) * a.kv_dim + size_t(h) * hd + t] = v;
-    }
+    __syncthreads();
+    if (t < hd) x[t] = r;
+    __syncthreads();
 }
 
-// GQA decode attention, one CTA per query head: scores against the `valid`
-// newest ring entries (i = 0 is this step's slot), softmax, weighted sum of
-// V (decode.cpp:197-226). head_dim <= 256.
+// One CTA per query head (decode.cpp:159-226): QK norm + RoPE of its Q head
+// (-> qbuf) and of its KV head's K, the V head as is; the first Q head of
+// each KV group appends K and V to the ring slot. Scores against the
+// `valid` newest positions (i = 0: this step, taken from shared memory, the
+// others from the ring, written by earlier steps), softmax, weighted sum of
+// V. Scores: a warp takes 8 positions per round, 4 lanes per position with
+// all their loads issued before the reduction. head_dim % 16 == 0, <= 256.
 __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(AttnArgs a) {
     __shared__ float red32[32];
-    __shared__ float qs[256];
+    __shared__ __align__(16) float qs[256];
+    __shared__ __align__(16) float ks[256];
+    __shared__ __align__(16) float vs[256];
     __shared__ float sc[kAttnMaxCtx];
     __shared__ float part[kAttnThreads];
-    const uint32_t h = blockIdx.x, hd = a.head_dim, kvh = h / (a.num_heads / a.num_kv_heads);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = kAttnThreads / 32;
+    const uint32_t h = blockIdx.x, hd = a.head_dim, per = a.num_heads / a.num_kv_heads, kvh = h / per;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = kAttnThreads / 32;
     uint32_t slot, valid;
     attn_slot_valid(a, slot, valid);
-    for (uint32_t i = threadIdx.x; i < hd; i += blockDim.x) qs[i] = a.qbuf[size_t(h) * hd + i];
+    for (uint32_t i = tid; i < hd; i += blockDim.x) {
+        qs[i] = a.q[size_t(h) * hd + i];
+        ks[i] = a.k[size_t(kvh) * hd + i];
+        vs[i] = a.v[size_t(kvh) * hd + i];
+    }
     __syncthreads();
-    for (uint32_t i = warp; i < valid; i += nw) {               // one warp per position
-        const uint32_t ki = (slot + a.attn_ctx - i) % a.attn_ctx;
-        const float* kr = a.k_cache + size_t(ki) * a.kv_dim + size_t(kvh) * hd;
+    head_norm_rope(qs, a.q_norm_w, a.rope_cos, a.rope_sin, hd, red32);
+    head_norm_rope(ks, a.k_norm_w, a.rope_cos, a.rope_sin, hd, red32);
+    for (uint32_t i = tid; i < hd; i += blockDim.x) {
+        a.qbuf[size_t(h) * hd + i] = qs[i];
+        if (h % per == 0) {
+            a.k_cache[size_t(slot) * a.kv_dim + size_t(kvh) * hd + i] = ks[i];
+            a.v_cache[size_t(slot) * a.kv_dim + size_t(kvh) * hd + i] = vs[i];
+        }
+    }
+    // scores
+    const uint32_t sub = lane & 3, q4 = hd / 16;                  // float4s per lane and position
+    const float4* qv = reinterpret_cast<const float4*>(qs) + sub * q4;
+    for (uint32_t base = warp * 8; base < valid; base += nw * 8) {
+        const uint32_t i = base + (lane >> 2);
         float s = 0.f;
-        for (uint32_t j = lane; j < hd; j += 32) s = fmaf(qs[j], kr[j], s);
+        if (i < valid) {
+            const float4* kr = i == 0 ? reinterpret_cast<const float4*>(ks) + sub * q4
+                                      : reinterpret_cast<const float4*>(
+                                            a.k_cache + size_t((slot + a.attn_ctx - i) % a.attn_ctx) * a.kv_dim +
+                                            size_t(kvh) * hd) + sub * q4;
+            float4 kk[16];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (lane == 0) sc[i] = s * a.scale;
+            for (int j = 0; j < 16; ++j)
+                if (j < int(q4)) kk[j] = kr[j];
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                if (j < int(q4)) {
+                    const float4 qq = qv[j];
+                    s = fmaf(qq.x, kk[j].x, s);
+                    s = fmaf(qq.y, kk[j].y, s);
+                    s = fmaf(qq.z, kk[j].z, s);
+                    s = fmaf(qq.w, kk[j].w, s);
+                }
+        }
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        s += __shfl_xor_sync(0xffffffffu, s, 2);
+        if (sub == 0 && i < valid) sc[i] = s * a.scale;
     }
     __syncthreads();
     float m = -INFINITY;
-    for (uint32_t i = threadIdx.x; i < valid; i += blockDim.x) m = fmaxf(m, sc[i]);
+    for (uint32_t i = tid; i < valid; i += blockDim.x) m = fmaxf(m, sc[i]);
     m = block_max(m, red32);
     float sum = 0.f;
-    for (uint32_t i = threadIdx.x; i < valid; i += blockDim.x) {
+    for (uint32_t i = tid; i < valid; i += blockDim.x) {
         const float e = expf(sc[i] - m);
         sc[i] = e;
         sum += e;
@@ -207,20 +294,28 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(AttnArgs a) {
     sum = block_sum(sum, red32);
     const float inv = sum > 0.f ? 1.0f / sum : 0.f;
     __syncthreads();
-    // thread t handles dim t % hd over positions t / hd, t / hd + g, ...
-    const uint32_t g = kAttnThreads / hd, dim = threadIdx.x % hd, grp = threadIdx.x / hd;
+    // thread t: dim t % hd over positions t / hd + g k; 4 loads in flight
+    const uint32_t g = kAttnThreads / hd, dim = tid % hd, grp = tid / hd;
     float acc = 0.f;
-    if (grp < g)
-        for (uint32_t i = grp; i < valid; i += g) {
-            const uint32_t vi = (slot + a.attn_ctx - i) % a.attn_ctx;
-            acc = fmaf(sc[i] * inv, a.v_cache[size_t(vi) * a.kv_dim + size_t(kvh) * hd + dim], acc);
+    if (grp < g) {
+        if (grp == 0) acc = sc[0] * vs[dim];
+        const float* vb = a.v_cache + size_t(kvh) * hd + dim;
+        uint32_t i = grp == 0 ? g : grp;
+        for (; i + 3 * g < valid; i += 4 * g) {
+            float vv[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) vv[q] = vb[size_t((slot + a.attn_ctx - (i + q * g)) % a.attn_ctx) * a.kv_dim];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) acc = fmaf(sc[i + q * g], vv[q], acc);
         }
-    part[threadIdx.x] = acc;
+        for (; i < valid; i += g) acc = fmaf(sc[i], vb[size_t((slot + a.attn_ctx - i) % a.attn_ctx) * a.kv_dim], acc);
+    }
+    part[tid] = acc;
     __syncthreads();
-    if (threadIdx.x < hd) {
+    if (uint32_t(tid) < hd) {
         float o = 0.f;
-        for (uint32_t q = 0; q < g; ++q) o += part[q * hd + threadIdx.x];
-        a.attn_out[size_t(h) * hd + threadIdx.x] = o;
+        for (uint32_t q = 0; q < g; ++q) o += part[q * hd + tid];
+        a.attn_out[size_t(h) * hd + tid] = o * inv;
     }
 }
 

@@ -699,10 +699,11 @@ int gemv_set(SmoeCudaCtx* c, const smoe::GemvSet& g) {
         total += g.rows[m];
     }
     if (!g.x || g.cols == 0 || g.cols % 8 || g.cols > 16384) { set_err("bad matvec cols %s%ld", "", (long)g.cols); return SMOE_ERR_ARG; }
-    const size_t smem = size_t(g.cols) * 4;
-    int rc = prep_kernel(c, smoe::k_gemv_set, smem);
-    if (rc) return rc;
-    smoe::k_gemv_set<<<(total + smoe::kGemvRowsPerCta - 1) / smoe::kGemvRowsPerCta, 256, smem, c->stream>>>(g);
+    if (!aligned16(g.x)) { set_err("matvec input must be 16-byte aligned %s%ld", "", 0); return SMOE_ERR_ARG; }
+    // one warp per row pair, at most 8 CTAs of 8 warps per SM (grid-stride beyond)
+    const uint32_t pairs = (total + 1) / 2, warps = smoe::kGemvThreads / 32;
+    const uint32_t want = (pairs + warps - 1) / warps, cap = uint32_t(c->num_sms) * 8;
+    smoe::k_gemv_set<<<want < cap ? want : cap, smoe::kGemvThreads, 0, c->stream>>>(g, total);
     c->dispatches += 1;
     return cudaGetLastError() == cudaSuccess ? SMOE_OK : SMOE_ERR_CUDA;
 }
@@ -788,9 +789,8 @@ int smoe_cuda_attention_layer_async(SmoeCudaCtx* c, const SmoeCudaAttnLayerArgs*
     t.slot = a->slot; t.valid = a->valid; t.attn_ctx = a->attn_ctx;
     t.pos = pos;
     t.scale = a->attn_scale;
-    smoe::k_qk_rope_append<<<a->num_heads + 2 * a->num_kv_heads, a->head_dim, 0, c->stream>>>(t);
     smoe::k_attn_decode<<<a->num_heads, smoe::kAttnThreads, 0, c->stream>>>(t);
-    c->dispatches += 2;
+    c->dispatches += 1;
     // 4. O projection
     smoe::GemvSet o{};
     o.w[0] = a->w_o; o.y[0] = a->o_out; o.rows[0] = a->d_model;
