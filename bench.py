@@ -367,8 +367,79 @@ def run_ours(args, rank, world, local):
                 "value": round(LAYER_BYTES * n / el / 1e9, 4), "unit": "GB/s", "cores": used,
                 "kind": kind, "sample": f"{n} layer steps in {el:.1f} s (reference router + "
                                         "restated Q4 FFN, OpenMP)"}
+        if world == 1 and not args.no_extra:
+            line["sampler"] = sampler_leg(ctx, stream)
+            line["decode_30b"] = decode_leg(ctx)
         print(json.dumps(line), flush=True)
     ctx.close()
+
+
+def sampler_leg(ctx, stream, reps=50):
+    """Config 0: one sampler row (T 0.7, top-k 20, top-p 0.8, repetition
+    penalty 1.1 over 64 history ids) on fp32[151,936] logits ~ N(0, 2^2)
+    resident on the device; graph replays, device time per row."""
+    import numpy as np
+    import torch
+    import smoe_cuda as S
+    V = 151_936
+    rng = np.random.default_rng(5)
+    logits = torch.from_numpy((rng.standard_normal(V) * 2).astype(np.float32)).cuda()
+    hist = torch.from_numpy(rng.integers(0, V, 64).astype(np.int32)).cuda()
+    row = np.zeros(6, np.float32)
+    row[0:2] = (0.7, 0.8)
+    row.view(np.uint32)[2] = 20
+    row[3:5] = (1.1, 0.37)
+    row.view(np.uint32)[5] = 64
+    drow = torch.from_numpy(row.view(np.int32)).cuda()
+    tok = torch.zeros(1, dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        ctx.sample(logits, V, 1, drow, hist, 64, tok)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            ctx.sample(logits, V, 1, drow, hist, 64, tok)
+        for _ in range(3):
+            g.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) / reps * 1e3
+    return {"workload": "config0: sampler, batch 1, vocab 151,936 (T 0.7, top-k 20, top-p 0.8, rep 1.1)",
+            "us_per_row": round(us, 2), "logit_bytes_per_row": V * 4,
+            "achieved_gbs": round(V * 4 / (us * 1e-6) / 1e9, 1)}
+
+
+def decode_leg(ctx, prompt=45, gen=256):
+    """Config 2 shape: Qwen3-30B-A3B decode (48 layers, random weights with
+    the benchmark distributions), batch 1, one CUDA graph per token
+    (s-moe_b200/decode.py); tokens per second over the generated tokens."""
+    import numpy as np
+    import torch
+    import smoe_cuda as S
+    import decode as DEC
+    sh = DEC.Shape()
+    model = DEC.Model(ctx, sh)
+    rng = np.random.default_rng(11)
+    dec = DEC.Decoder(model, uniforms=rng.integers(0, 1 << 24, 4096).astype(np.float64) / (1 << 24))
+    dec.capture(torch.cuda.Stream())
+    pr = rng.integers(0, sh.vocab, prompt).tolist()
+    dec.run(pr, 8)
+    dec.reset()
+    _, t = dec.run(pr, gen)
+    attn = (2 * sh.q_dim + 2 * sh.kv_dim) * sh.d_model * 2
+    per_tok = (sh.layers * (sh.top_k * S.expert_bytes(sh.fmt, sh.d_model, sh.d_ff) + attn
+                            + sh.n_experts * sh.d_model * 2) + sh.vocab * sh.d_model * 2)
+    out = {"workload": f"config2 shape: Qwen3-30B-A3B decode, 48 layers, batch 1, prompt {prompt}, "
+                       f"{gen} generated (random weights)", "tok_per_s": round(gen / t, 2),
+           "ms_per_token": round(1e3 * t / gen, 4), "weight_bytes_per_token": per_tok,
+           "achieved_gbs": round(per_tok * gen / t / 1e9, 1)}
+    del dec, model
+    torch.cuda.empty_cache()
+    return out
 
 
 def main():
@@ -378,6 +449,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="skip the sampler and decode legs")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
     rank, world, local = dist_init(args.gpus)
