@@ -16,6 +16,7 @@
 #include "router.cuh"
 #include "sampler.cuh"
 #include "decode.cuh"
+#include "ffn_grouped.cuh"
 
 namespace {
 
@@ -67,6 +68,14 @@ struct SmoeCudaCtx {
     int fused_grid[2][4] = {};       // fused kernel grid per (format, groups per warp)
     size_t fused_smem_seen[2][4] = {};
     unsigned long long* trace = nullptr;   // phase timestamps of the fused kernel (profiling aid)
+    // expert-grouped batch path: per-expert slot lists, operand tables, per-slot outputs
+    uint32_t* g_list = nullptr;      // [max_experts][max_batch * 16]
+    uint32_t* g_count = nullptr;     // [max_experts]
+    uint2* g_xtab = nullptr;         // [max_batch][max_d_model / 16][8]
+    float2* g_xgs = nullptr;         // [max_batch][max_d_model / 64]
+    uint2* g_htab = nullptr;         // [max_batch * 16][max_d_ff / 16][8]
+    float2* g_hgs = nullptr;         // [max_batch * 16][max_d_ff / 64]
+    float* g_ys = nullptr;           // [max_batch * 16][max_d_model]
     // expert parallel: this rank's exchange window (IPC-exported) and rank 0's, mapped
     uint8_t* ep_win = nullptr;
     size_t ep_win_bytes = 0;
@@ -150,6 +159,54 @@ int check_ffn_dims(SmoeCudaCtx* c, uint32_t d, uint32_t dff) {
 }
 
 // Launch gate_up then down/combine for a prepared FfnArgs.
+// Token batches (> 4 tokens) on the vault layout: the expert-grouped path,
+// each expert's weights read once per layer whatever its token count.
+int launch_grouped(SmoeCudaCtx* c, smoe::FfnArgs& a, int fmt, uint32_t E) {
+    const uint32_t nslots = a.ntok * a.k, lcap = c->cfg.max_batch * 16u;
+    if (nslots == 0) return SMOE_OK;
+    if (nslots > lcap || E > c->cfg.max_experts || !a.ids) {
+        set_err("bad grouped FFN arguments %s%ld", "", (long)nslots);
+        return SMOE_ERR_ARG;
+    }
+    const uint32_t d = a.d_model, dff = a.d_ff;
+    int rc;
+    smoe::k_group_slots<<<E, 32, 0, c->stream>>>(a.ids, nslots, c->g_list, c->g_count, lcap);
+    if ((rc = prep_kernel(c, smoe::k_build_tabs, size_t(d / 4) * 8))) return rc;
+    if ((rc = prep_kernel(c, smoe::k_build_tabs, size_t(dff / 4) * 8))) return rc;
+    smoe::k_build_tabs<<<a.ntok, 256, size_t(d / 4) * 8, c->stream>>>(a.x, a.x_dtype == 1, d, c->g_xtab, c->g_xgs);
+    smoe::GroupedArgs g{};
+    g.base = a.base;
+    g.stride = a.stride;
+    for (int i = 0; i < 9; ++i) g.off[i] = a.off[i];
+    g.list = c->g_list;
+    g.count = c->g_count;
+    g.lcap = lcap;
+    g.d_model = d;
+    g.d_ff = dff;
+    g.err = c->err;
+    smoe::GroupedArgs g1 = g, g2 = g;
+    g1.tab = c->g_xtab; g1.gs = c->g_xgs; g1.tab_div = a.k; g1.out = c->hidden;
+    g2.tab = c->g_htab; g2.gs = c->g_hgs; g2.tab_div = 1; g2.out = c->g_ys;
+    const size_t s1 = smoe::grouped_smem_bytes(d, 2), s2 = smoe::grouped_smem_bytes(dff, 1);
+    auto run = [&](auto k1, auto k2) -> int {
+        int r;
+        if ((r = prep_kernel(c, k1, s1))) return r;
+        if ((r = prep_kernel(c, k2, s2))) return r;
+        k1<<<dim3(dff / 16, E), 256, s1, c->stream>>>(g1);
+        smoe::k_build_tabs<<<nslots, 256, size_t(dff / 4) * 8, c->stream>>>(c->hidden, 0, dff, c->g_htab, c->g_hgs);
+        k2<<<dim3(d / 16, E), 256, s2, c->stream>>>(g2);
+        return SMOE_OK;
+    };
+    rc = fmt == SMOE_FMT_AFFINE_Q4 ? run(smoe::k_ffn_grouped<smoe::kFmtAffine, 2>, smoe::k_ffn_grouped<smoe::kFmtAffine, 1>)
+                                   : run(smoe::k_ffn_grouped<smoe::kFmtSmoe, 2>, smoe::k_ffn_grouped<smoe::kFmtSmoe, 1>);
+    if (rc) return rc;
+    smoe::k_combine_slots<<<dim3((d + 255) / 256, a.ntok), 256, 0, c->stream>>>(c->g_ys, a.wts, a.k, d, a.y,
+                                                                               a.y_dtype);
+    CK(cudaGetLastError());
+    c->dispatches += 6;
+    return SMOE_OK;
+}
+
 int launch_ffn(SmoeCudaCtx* c, smoe::FfnArgs& a, int fmt) {
     const uint32_t nslots = a.ntok * a.k;
     if (nslots == 0) return SMOE_OK;
@@ -336,6 +393,13 @@ SmoeCudaCtx* smoe_cuda_init_ex(const SmoeCudaInitArgs* args) {
     if ((e = cudaMalloc(&c->err, 4)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->fstate, sizeof(smoe::FusedState))) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->acc, size_t(smoe::kFusedMaxTok) * a.max_d_model * 4)) != cudaSuccess) return fail(e);
+    if ((e = cudaMalloc(&c->g_list, size_t(a.max_experts) * slots * 4)) != cudaSuccess) return fail(e);
+    if ((e = cudaMalloc(&c->g_count, size_t(a.max_experts) * 4)) != cudaSuccess) return fail(e);
+    if ((e = cudaMalloc(&c->g_xtab, size_t(a.max_batch) * a.max_d_model * 4)) != cudaSuccess) return fail(e);
+    if ((e = cudaMalloc(&c->g_xgs, size_t(a.max_batch) * (a.max_d_model / 64) * 8)) != cudaSuccess) return fail(e);
+    if ((e = cudaMalloc(&c->g_htab, slots * a.max_d_ff * 4)) != cudaSuccess) return fail(e);
+    if ((e = cudaMalloc(&c->g_hgs, slots * (a.max_d_ff / 64) * 8)) != cudaSuccess) return fail(e);
+    if ((e = cudaMalloc(&c->g_ys, slots * a.max_d_model * 4)) != cudaSuccess) return fail(e);
     cudaMemsetAsync(c->acc, 0, size_t(smoe::kFusedMaxTok) * a.max_d_model * 4, c->stream);
     cudaMemsetAsync(c->fstate, 0, sizeof(smoe::FusedState), c->stream);
     c->gemv_cap = a.max_vocab > a.max_d_model ? a.max_vocab : a.max_d_model;
@@ -365,7 +429,7 @@ void smoe_cuda_destroy(SmoeCudaCtx* c) {
     if (c->ep_win) cudaFree(c->ep_win);
     for (auto& ev : c->events)
         if (ev) cudaEventDestroy(ev);
-    void* bufs[] = {c->fstate, c->acc, c->hidden, c->slot_out, c->in_stage, c->batch_out, c->logits, c->ids,
+    void* bufs[] = {c->g_list, c->g_count, c->g_xtab, c->g_xgs, c->g_htab, c->g_hgs, c->g_ys, c->fstate, c->acc, c->hidden, c->slot_out, c->in_stage, c->batch_out, c->logits, c->ids,
                     c->wts, c->ticket, c->err, c->gemv_out, c->gemv_in};
     for (void* b : bufs)
         if (b) cudaFree(b);
@@ -655,6 +719,8 @@ int smoe_cuda_moe_ffn(SmoeCudaCtx* c, const SmoeMoeLayer* L, const void* x, int 
             set_err("tiled layout needs batch <= 4 and a shape whose tiles fit shared memory %s%ld", "", (long)batch);
         return rc;
     }
+    if (batch > uint32_t(smoe::kFusedMaxTok))          // token batches: expert-grouped path
+        return launch_grouped(c, a, fmt, L->n_experts);
     return launch_ffn(c, a, fmt);
 }
 

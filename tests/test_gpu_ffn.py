@@ -189,3 +189,29 @@ def test_tiled_moe_ffn_given_routing(ctx):
         for j in range(k):
             ref = ref + w[t, j] * O.expert_ffn(O.FMT_AFFINE_Q4, L.arena[ids[t, j]], d, dff, X[t])
         assert rel_err(got[t], ref) < TIGHT
+
+
+@pytest.mark.parametrize("fmt,x_dtype", [(O.FMT_AFFINE_Q4, S.DTYPE_BF16), (O.FMT_SMOE_Q4, S.DTYPE_F32)])
+def test_moe_layer_token_batch_grouped(ctx, fmt, x_dtype):
+    """Token batches (> 4 tokens) on the vault layout run the expert-grouped
+    path: router + grouped FFN + rank-order combine vs the oracle per token,
+    and the same result on a second call (deterministic order)."""
+    B, d, dff, E, k = 48, 2048, 768, 32, 8
+    L = Layer(fmt, E, d, dff, seed=80 + fmt)
+    Xb = O.normal_bf16(90 + fmt, 5, B * d)
+    Xf = O.bf16_to_f32(Xb).reshape(B, d)
+    xin = dev(Xb) if x_dtype == S.DTYPE_BF16 else dev(np.ascontiguousarray(Xf))
+    outs = []
+    for call in range(2):
+        y = torch.zeros(B, d, dtype=torch.float32, device="cuda")
+        ids = torch.zeros(B, k, dtype=torch.int32, device="cuda")
+        w = torch.zeros(B, k, dtype=torch.float32, device="cuda")
+        ctx.moe_layer(L.desc, xin, x_dtype, B, k, True, y, S.DTYPE_F32, ids, w)
+        ctx.synchronize()
+        outs.append(y.cpu().numpy())
+    assert np.array_equal(outs[0], outs[1])
+    gid = ids.cpu().numpy().view(np.uint32)
+    for t in range(B):
+        ref, rids, rw = O.moe_layer(fmt, Xf[t], L.router_w, L.arena, L.stride, E, d, dff, k)
+        assert (gid[t] == rids).all()
+        assert rel_err(outs[0][t], ref) < TIGHT
