@@ -2,18 +2,19 @@
 // batched-decode shape: hundreds of tokens, each expert routed ~16 of them).
 //
 // The per-slot path (ffn_q4.cuh) streams an expert's weights once per
-// (token, expert) slot. Here the work is grouped by expert: a CTA owns 16
-// rows of one expert's matrices, loads that weight tile once and applies it
-// to every token routed to the expert, four tokens per MMA (B columns 2t,
+// (token, expert) slot. Here the work is grouped by expert: a CTA owns 32
+// (gate/up) or 64 (down) rows of one expert's matrices, loads that weight
+// tile once and applies it to every token routed to the expert, four tokens
+// per MMA (B columns 2t,
 // 2t+1 = hi and lo halves of token t). The arithmetic is that of
 // ffn_q4.cuh (exact fp16 operands q / 16q, activations split hi + lo with a
 // per-vector power-of-two scale, per-group scale/bias epilogue), so results
 // match the per-slot path to fp32 rounding. Launch sequence per layer:
 //   k_group_slots   ids -> per-expert slot lists in slot order
 //   k_build_tabs    x rows -> B-operand tables (once per token)
-//   k_gate_up_grp   h[slot] = silu(g) * u for the expert's slots
+//   k_ffn_grouped<2> h[slot] = silu(g) * u for the expert's slots
 //   k_build_tabs    h rows -> tables (once per slot)
-//   k_down_grp      y_slot = W_down . h[slot]
+//   k_ffn_grouped<1> y_slot = W_down . h[slot]
 //   k_combine_slots y[t] = sum_j w[t,j] * y_slot[t*k+j] in rank order
 //                   (product then sum, as axpy_f32 in decode.cpp:485-499)
 #pragma once
@@ -36,19 +37,24 @@ struct GroupedArgs {
     uint32_t* err;
 };
 
-// One 64-group of a 16-row tile against 4 vectors: B entries of column g
-// (lane / 4) come from vector g / 2, hi (g even) or lo (g odd) half. Returns
-// the group sums of rows lane/4 and lane/4 + 8 for vector lane % 4.
-SMOE_DEVINL void group_mma4(const uint8_t* rowp, int rs, int grp, const uint2* tabg, int lane, float& r0,
+// B registers of group grp (4 k-steps) for this lane: column g (lane / 4)
+// comes from vector g / 2, hi (g even) or lo (g odd) half.
+SMOE_DEVINL void load_b4(const uint2* tabg, int grp, int lane, uint2* bs) {
+    const int gr = lane >> 2, c = lane & 3;
+#pragma unroll
+    for (int s = 0; s < 4; ++s) bs[s] = tabg ? __ldg(tabg + (grp * 4 + s) * 8 + (gr & 1) * 4 + c) : make_uint2(0u, 0u);
+}
+
+// One 64-group of a 16-row tile against 4 vectors (B registers bs from
+// load_b4): returns the group sums of rows lane/4 and lane/4 + 8 for vector
+// lane % 4.
+SMOE_DEVINL void group_mma4(const uint8_t* rowp, int rs, int grp, const uint2* bs, int lane, float& r0,
                             float& r8) {
     const int gr = lane >> 2, c = lane & 3;
     const uint2 w = *reinterpret_cast<const uint2*>(rowp + gr * rs + grp * 32 + c * 8);
     const uint2 v = *reinterpret_cast<const uint2*>(rowp + (gr + 8) * rs + grp * 32 + c * 8);
     float d[4] = {0.f, 0.f, 0.f, 0.f};
     const uint32_t M0 = 0x000F000Fu, M1 = 0x00F000F0u, OR = 0x64006400u;
-    uint2 bs[4];
-#pragma unroll
-    for (int s = 0; s < 4; ++s) bs[s] = tabg ? __ldg(tabg + (grp * 4 + s) * 8 + (gr & 1) * 4 + c) : make_uint2(0u, 0u);
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
         const uint32_t wg = i ? w.y : w.x, wh = i ? v.y : v.x;
@@ -101,26 +107,28 @@ __global__ void __launch_bounds__(256) k_build_tabs(const void* src, int bf16, u
     }
 }
 
-// Shared layout of a grouped CTA: tile [mats][16][rs] nibbles, scales/biases
-// [mats][2][16 * G], partial sums [8 warps][mats][4 vectors][16 rows].
-inline size_t grouped_smem_bytes(int K, int mats) {
+// Shared layout of a grouped CTA: tile [mats][rb][rs] nibbles (rows padded
+// by 32 B: conflict-free fragment loads), scales/biases [mats][2][rb * G].
+inline size_t grouped_smem_bytes(int K, int mats, int rb) {
     const int rs = K / 2 + 32, G = K / 64;
-    return size_t(mats * 16 * rs) + size_t(mats) * 2 * 16 * G * 2 + 8 * mats * 4 * 16 * 4 + 16;
+    return size_t(mats * rb * rs) + size_t(mats) * 2 * rb * G * 2 + 16;
 }
 
 // MATS = 2: gate + up rows (K = d_model) -> h; MATS = 1: down rows (K = d_ff)
-// -> y_slot. grid (rows / 16, E), 256 threads.
-template <int FMT, int MATS>
+// -> y_slot. grid (rows / RB, E), 256 threads. A warp task is (16-row tile,
+// chunk of 4 of the expert's vectors) over all K groups, so results are
+// complete inside the warp: no CTA barrier and no cross-warp reduction in
+// the token loop.
+template <int FMT, int MATS, int RB>
 __global__ void __launch_bounds__(256) k_ffn_grouped(GroupedArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t e = blockIdx.y, T = a.count[e];
     if (T == 0) return;
     const int K = MATS == 2 ? a.d_model : a.d_ff, R = MATS == 2 ? a.d_ff : a.d_model;
-    const int tile = blockIdx.x, rs = K / 2 + 32, G = K / 64, nsb = 16 * G;
-    uint8_t* wt = smem;                                                 // [MATS][16][rs]
-    uint16_t* sb = reinterpret_cast<uint16_t*>(wt + MATS * 16 * rs);    // [MATS][2][nsb]
-    float* red = reinterpret_cast<float*>(sb + MATS * 2 * nsb);         // [8][MATS][4][16]
-    uint64_t* bar = reinterpret_cast<uint64_t*>(red + 8 * MATS * 4 * 16);
+    const int blk = blockIdx.x, rs = K / 2 + 32, G = K / 64, nsb = RB * G;
+    uint8_t* wt = smem;                                                 // [MATS][RB][rs]
+    uint16_t* sb = reinterpret_cast<uint16_t*>(wt + MATS * RB * rs);    // [MATS][2][nsb]
+    uint64_t* bar = reinterpret_cast<uint64_t*>(sb + MATS * 2 * nsb);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gr = lane >> 2, c = lane & 3;
     const uint8_t* eb = a.base + uint64_t(e) * a.stride;
     if (tid == 0) {
@@ -130,18 +138,18 @@ __global__ void __launch_bounds__(256) k_ffn_grouped(GroupedArgs a) {
     __syncthreads();
     if (warp == 0) {
         const uint32_t sbytes = nsb * 2;
-        const uint32_t total = MATS * 16 * (K / 2) + MATS * (FMT == kFmtAffine ? 2 : 1) * sbytes;
+        const uint32_t total = MATS * RB * (K / 2) + MATS * (FMT == kFmtAffine ? 2 : 1) * sbytes;
         if (lane == 0) mbar_arrive_expect_tx(bar, total);
         __syncwarp();
         const int m0 = MATS == 2 ? 0 : 2;
-        if (lane < MATS * 16) {
-            const int m = lane >> 4, r = lane & 15;
-            bulk_g2s(wt + (m * 16 + r) * rs, eb + a.off[3 * (m0 + m)] + size_t(tile * 16 + r) * (K / 2), K / 2, bar);
+        for (int i = lane; i < MATS * RB; i += 32) {
+            const int m = i / RB, r = i % RB;
+            bulk_g2s(wt + (m * RB + r) * rs, eb + a.off[3 * (m0 + m)] + size_t(blk * RB + r) * (K / 2), K / 2, bar);
         }
         if (lane < MATS)
-            bulk_g2s(sb + (lane * 2) * nsb, eb + a.off[3 * (m0 + lane) + 1] + size_t(tile) * sbytes, sbytes, bar);
+            bulk_g2s(sb + (lane * 2) * nsb, eb + a.off[3 * (m0 + lane) + 1] + size_t(blk) * sbytes, sbytes, bar);
         if (FMT == kFmtAffine && lane >= 2 && lane < 2 + MATS)
-            bulk_g2s(sb + ((lane - 2) * 2 + 1) * nsb, eb + a.off[3 * (m0 + lane - 2) + 2] + size_t(tile) * sbytes,
+            bulk_g2s(sb + ((lane - 2) * 2 + 1) * nsb, eb + a.off[3 * (m0 + lane - 2) + 2] + size_t(blk) * sbytes,
                      sbytes, bar);
     }
     if (!mbar_wait_bounded(bar, 0)) {
@@ -149,46 +157,52 @@ __global__ void __launch_bounds__(256) k_ffn_grouped(GroupedArgs a) {
         return;
     }
     const uint32_t* lst = a.list + size_t(e) * a.lcap;
-    for (uint32_t c0 = 0; c0 < T; c0 += 4) {
-        // vector of column pair g/2 of this lane's B, and of this lane's results (c)
+    const int nchunk = int((T + 3) / 4), ntask = (RB / 16) * nchunk;
+    for (int task = warp; task < ntask; task += 8) {
+        const int tile = task % (RB / 16), c0 = (task / (RB / 16)) * 4;
         const uint32_t tb = c0 + (gr >> 1), tc = c0 + c;
         const uint2* tabg = tb < T ? a.tab + size_t(lst[tb] / a.tab_div) * (K / 16) * 8 : nullptr;
         const float2* gsv = tc < T ? a.gs + size_t(lst[tc] / a.tab_div) * G : nullptr;
         float acc[MATS][2];
 #pragma unroll
         for (int m = 0; m < MATS; ++m) acc[m][0] = acc[m][1] = 0.f;
-        for (int grp = warp; grp < G; grp += 8) {
-            const float2 gsum = gsv ? __ldg(gsv + grp) : make_float2(0.f, 0.f);
+        // four groups at a time: their 16 B loads and 4 group sums are in
+        // flight together (the tables come from L2), then their MMAs
+        for (int g0 = 0; g0 < G; g0 += 4) {
+            uint2 bs[4][4];
+            float2 gsum[4];
 #pragma unroll
-            for (int m = 0; m < MATS; ++m) {
-                float r0, r8;
-                group_mma4(wt + m * 16 * rs, rs, grp, tabg, lane, r0, r8);
-                const uint16_t* sc = sb + (m * 2) * nsb;
-                const uint16_t* bi = sb + (m * 2 + 1) * nsb;
-                acc[m][0] += group_epilogue<FMT>(r0, gsum, sc, bi, gr * G + grp);
-                acc[m][1] += group_epilogue<FMT>(r8, gsum, sc, bi, (gr + 8) * G + grp);
+            for (int q = 0; q < 4; ++q) {
+                const int grp = min(g0 + q, G - 1);
+                load_b4(tabg, grp, lane, bs[q]);
+                gsum[q] = gsv ? __ldg(gsv + grp) : make_float2(0.f, 0.f);
             }
-        }
 #pragma unroll
-        for (int m = 0; m < MATS; ++m) {
-            red[((warp * MATS + m) * 4 + c) * 16 + gr] = acc[m][0];
-            red[((warp * MATS + m) * 4 + c) * 16 + gr + 8] = acc[m][1];
-        }
-        __syncthreads();
-        if (tid < 64) {
-            const uint32_t t = tid >> 4, r = tid & 15;
-            if (c0 + t < T) {
-                float s0 = 0.f, s1 = 0.f;
-                for (int w = 0; w < 8; ++w) {
-                    s0 += red[((w * MATS + 0) * 4 + t) * 16 + r];
-                    if (MATS == 2) s1 += red[((w * MATS + 1) * 4 + t) * 16 + r];
+            for (int q = 0; q < 4; ++q) {
+                const int grp = g0 + q;
+                if (grp < G) {
+#pragma unroll
+                    for (int m = 0; m < MATS; ++m) {
+                        float r0, r8;
+                        group_mma4(wt + (m * RB + tile * 16) * rs, rs, grp, bs[q], lane, r0, r8);
+                        const uint16_t* sc = sb + (m * 2) * nsb;
+                        const uint16_t* bi = sb + (m * 2 + 1) * nsb;
+                        acc[m][0] += group_epilogue<FMT>(r0, gsum[q], sc, bi, (tile * 16 + gr) * G + grp);
+                        acc[m][1] += group_epilogue<FMT>(r8, gsum[q], sc, bi, (tile * 16 + gr + 8) * G + grp);
+                    }
                 }
-                const float v = MATS == 2 ? s0 * (1.0f / (1.0f + expf(-s0))) * s1   // kernels.metal:61-63
-                                          : s0;
-                a.out[size_t(lst[c0 + t]) * R + tile * 16 + r] = v;
             }
         }
-        __syncthreads();
+        if (tc < T) {
+            float* o = a.out + size_t(lst[tc]) * R + blk * RB + tile * 16 + gr;
+            if (MATS == 2) {
+                o[0] = acc[0][0] * (1.0f / (1.0f + expf(-acc[0][0]))) * acc[1][0];   // kernels.metal:61-63
+                o[8] = acc[0][1] * (1.0f / (1.0f + expf(-acc[0][1]))) * acc[MATS - 1][1];
+            } else {
+                o[0] = acc[0][0];
+                o[8] = acc[0][1];
+            }
+        }
     }
 }
 

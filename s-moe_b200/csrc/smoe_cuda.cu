@@ -187,18 +187,22 @@ int launch_grouped(SmoeCudaCtx* c, smoe::FfnArgs& a, int fmt, uint32_t E) {
     smoe::GroupedArgs g1 = g, g2 = g;
     g1.tab = c->g_xtab; g1.gs = c->g_xgs; g1.tab_div = a.k; g1.out = c->hidden;
     g2.tab = c->g_htab; g2.gs = c->g_hgs; g2.tab_div = 1; g2.out = c->g_ys;
-    const size_t s1 = smoe::grouped_smem_bytes(d, 2), s2 = smoe::grouped_smem_bytes(dff, 1);
+    // gate/up: 32 rows x 2 matrices per CTA; down: 64 rows per CTA
+    constexpr int kRbGu = 32, kRbDn = 64;
+    if (dff % kRbGu || d % kRbDn) { set_err("grouped FFN needs d_ff % 32 == 0 and d_model % 64 == 0 %s%ld", "", 0); return SMOE_ERR_ARG; }
+    const size_t s1 = smoe::grouped_smem_bytes(d, 2, kRbGu), s2 = smoe::grouped_smem_bytes(dff, 1, kRbDn);
     auto run = [&](auto k1, auto k2) -> int {
         int r;
         if ((r = prep_kernel(c, k1, s1))) return r;
         if ((r = prep_kernel(c, k2, s2))) return r;
-        k1<<<dim3(dff / 16, E), 256, s1, c->stream>>>(g1);
+        k1<<<dim3(dff / kRbGu, E), 256, s1, c->stream>>>(g1);
         smoe::k_build_tabs<<<nslots, 256, size_t(dff / 4) * 8, c->stream>>>(c->hidden, 0, dff, c->g_htab, c->g_hgs);
-        k2<<<dim3(d / 16, E), 256, s2, c->stream>>>(g2);
+        k2<<<dim3(d / kRbDn, E), 256, s2, c->stream>>>(g2);
         return SMOE_OK;
     };
-    rc = fmt == SMOE_FMT_AFFINE_Q4 ? run(smoe::k_ffn_grouped<smoe::kFmtAffine, 2>, smoe::k_ffn_grouped<smoe::kFmtAffine, 1>)
-                                   : run(smoe::k_ffn_grouped<smoe::kFmtSmoe, 2>, smoe::k_ffn_grouped<smoe::kFmtSmoe, 1>);
+    rc = fmt == SMOE_FMT_AFFINE_Q4
+             ? run(smoe::k_ffn_grouped<smoe::kFmtAffine, 2, kRbGu>, smoe::k_ffn_grouped<smoe::kFmtAffine, 1, kRbDn>)
+             : run(smoe::k_ffn_grouped<smoe::kFmtSmoe, 2, kRbGu>, smoe::k_ffn_grouped<smoe::kFmtSmoe, 1, kRbDn>);
     if (rc) return rc;
     smoe::k_combine_slots<<<dim3((d + 255) / 256, a.ntok), 256, 0, c->stream>>>(c->g_ys, a.wts, a.k, d, a.y,
                                                                                a.y_dtype);
