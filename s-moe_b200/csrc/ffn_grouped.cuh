@@ -75,18 +75,28 @@ SMOE_DEVINL void group_mma4(const uint8_t* rowp, int rs, int grp, const uint2* b
 }
 
 // Per-expert slot lists: one CTA (one warp) per expert, ballot compaction
-// over the slots in order (deterministic).
+// over the slots in order (deterministic); ids are read 16 per lane ahead of
+// the ballots so the scan is not a chain of dependent loads.
 __global__ void k_group_slots(const uint32_t* ids, uint32_t nslots, uint32_t* list, uint32_t* count,
                               uint32_t lcap) {
     const uint32_t e = blockIdx.x, lane = threadIdx.x;
     uint32_t n = 0;
-    for (uint32_t s0 = 0; s0 < nslots; s0 += 32) {
-        const uint32_t s = s0 + lane;
-        const bool mine = s < nslots && ids[s] == e;
-        const uint32_t m = __ballot_sync(0xffffffffu, mine);
-        const uint32_t pos = n + __popc(m & ((1u << lane) - 1u));
-        if (mine && pos < lcap) list[size_t(e) * lcap + pos] = s;
-        n += __popc(m);
+    for (uint32_t b0 = 0; b0 < nslots; b0 += 32 * 16) {
+        uint32_t v[16];
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+            const uint32_t s = b0 + q * 32 + lane;
+            v[q] = s < nslots ? __ldg(ids + s) : 0xffffffffu;
+        }
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+            const uint32_t s = b0 + q * 32 + lane;
+            const bool mine = v[q] == e;
+            const uint32_t m = __ballot_sync(0xffffffffu, mine);
+            const uint32_t pos = n + __popc(m & ((1u << lane) - 1u));
+            if (mine && pos < lcap) list[size_t(e) * lcap + pos] = s;
+            n += __popc(m);
+        }
     }
     if (lane == 0) count[e] = n < lcap ? n : lcap;
 }

@@ -161,6 +161,24 @@ __global__ void __launch_bounds__(256) k_router(RouterArgs a) {
     if (lane == 0) a.ticket[tok] = 0;                 // ready for the next call
 }
 
+// Token batches: one CTA per token computes all its logit rows (x staged
+// once, 16 warps over the rows), then warp 0 selects. Same arithmetic per
+// row and the same selection as k_router. grid (batch), 512 threads.
+__global__ void __launch_bounds__(512) k_router_tok(RouterArgs a) {
+    extern __shared__ __align__(16) float xs[];
+    const int tok = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    stage_vec<float>(a.x, a.x_dtype, size_t(tok) * a.d, a.d, xs);
+    __syncthreads();
+    float* lg = a.logits + size_t(tok) * a.E;
+    for (int e = warp; e < int(a.E); e += 16) {
+        const float v = warp_row_dot_bf16(a.w + size_t(e) * a.d, xs, a.d, lane);
+        if (lane == 0) lg[e] = v;
+    }
+    __threadfence_block();
+    __syncthreads();
+    if (warp == 0) warp_topk(lg, a.E, a.k, a.norm, a.ids + size_t(tok) * a.k, a.wts + size_t(tok) * a.k, lane);
+}
+
 // Plain bf16 GEMV y = W . x (metal_bridge.h:157), one warp per row.
 __global__ void __launch_bounds__(256) k_gemv_bf16(const uint16_t* w, const float* x, float* y,
                                                    uint32_t rows, uint32_t cols) {

@@ -667,10 +667,16 @@ int smoe_cuda_router_topk(SmoeCudaCtx* c, const uint16_t* w, const void* x, int 
     smoe::RouterArgs a{w, x, x_dtype, E, d, k, norm, logits ? logits : c->logits, ids, wts,
                        c->ticket, c->err};
     const size_t smem = size_t(d) * 4;
-    int rc = prep_kernel(c, smoe::k_router, smem);
-    if (rc) return rc;
-    dim3 g((E + smoe::kRouterRowsPerCta - 1) / smoe::kRouterRowsPerCta, batch);
-    smoe::k_router<<<g, 256, smem, c->stream>>>(a);
+    if (batch >= 16) {                     // one CTA per token (x staged once per token)
+        int rc = prep_kernel(c, smoe::k_router_tok, smem);
+        if (rc) return rc;
+        smoe::k_router_tok<<<batch, 512, smem, c->stream>>>(a);
+    } else {                               // rows spread over CTAs (latency at small batch)
+        int rc = prep_kernel(c, smoe::k_router, smem);
+        if (rc) return rc;
+        dim3 g((E + smoe::kRouterRowsPerCta - 1) / smoe::kRouterRowsPerCta, batch);
+        smoe::k_router<<<g, 256, smem, c->stream>>>(a);
+    }
     CK(cudaGetLastError());
     c->dispatches += 1;
     return SMOE_OK;
