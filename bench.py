@@ -370,6 +370,7 @@ def run_ours(args, rank, world, local):
         if world == 1 and not args.no_extra:
             line["sampler"] = sampler_leg(ctx, stream)
             line["decode_30b"] = decode_leg(ctx)
+            line["batch256"] = batch_leg(ctx, stream)
         print(json.dumps(line), flush=True)
     ctx.close()
 
@@ -382,6 +383,7 @@ def sampler_leg(ctx, stream, reps=50):
     import torch
     import smoe_cuda as S
     V = 151_936
+    ctx.set_stream(stream.cuda_stream)
     rng = np.random.default_rng(5)
     logits = torch.from_numpy((rng.standard_normal(V) * 2).astype(np.float32)).cuda()
     hist = torch.from_numpy(rng.integers(0, V, 64).astype(np.int32)).cuda()
@@ -413,6 +415,61 @@ def sampler_leg(ctx, stream, reps=50):
             "achieved_gbs": round(V * 4 / (us * 1e-6) / 1e9, 1)}
 
 
+def batch_leg(ctx, stream, B=256, reps=10):
+    """Config 4 shape: one 30B MoE layer for 256 tokens (router + expert-
+    grouped FFN + combine, vault layout, AFFINE-Q4, bf16 x ~ N(0, 1)), and
+    256 sampler rows (T in {0.6, 0.7, 1.0}, top-k in {20, 40}, top-p in
+    {0.8, 0.95}, rep 1.1, 128-token histories) - device time per call."""
+    import numpy as np
+    import torch
+    import oracle as O
+    import smoe_cuda as S
+    arena, stride, off = O.make_experts(O.FMT_AFFINE_Q4, E, D, DFF, 4242)
+    rw = O.normal_bf16(4242, 6, E * D, 0.0, 0.02)
+    da, dr = torch.from_numpy(arena).cuda(), torch.from_numpy(rw.view(np.int16)).cuda()
+    L = S.make_layer(da, stride, off, E, D, DFF, S.FMT_AFFINE_Q4, dr)
+    x = torch.from_numpy(np.stack([O.normal_bf16(77 + i, 5, D) for i in range(B)]).view(np.int16)).cuda()
+    y = torch.zeros(B, D, dtype=torch.bfloat16, device="cuda")
+    ids = torch.zeros(B, K, dtype=torch.int32, device="cuda")
+    w = torch.zeros(B, K, dtype=torch.float32, device="cuda")
+    V = 151_936
+    rng = np.random.default_rng(9)
+    logits = torch.from_numpy((rng.standard_normal(B * V) * 2).astype(np.float32)).cuda()
+    hist = torch.from_numpy(rng.integers(0, V, B * 128).astype(np.int32)).cuda()
+    rows = np.zeros((B, 6), np.float32)
+    rows[:, 0] = np.array([0.6, 0.7, 1.0])[np.arange(B) % 3]
+    rows[:, 1] = np.array([0.8, 0.95])[np.arange(B) % 2]
+    rows.view(np.uint32)[:, 2] = np.array([20, 40])[(np.arange(B) // 2) % 2]
+    rows[:, 3] = 1.1
+    rows[:, 4] = (rng.integers(0, 1 << 24, B) / (1 << 24)).astype(np.float32)
+    rows.view(np.uint32)[:, 5] = 128
+    drows = torch.from_numpy(rows.view(np.int32)).cuda()
+    toks = torch.zeros(B, dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    ctx.set_stream(stream.cuda_stream)        # the events below are recorded on this stream
+
+    def timed(fn):
+        with torch.cuda.stream(stream):
+            fn()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(reps):
+                fn()
+            e1.record(stream)
+            torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps * 1e3
+    layer_us = timed(lambda: ctx.moe_layer(L, x, S.DTYPE_BF16, B, K, True, y, S.DTYPE_BF16, ids, w))
+    touched = int((np.bincount(ids.cpu().numpy().reshape(-1), minlength=E) > 0).sum())
+    samp_us = timed(lambda: ctx.sample(logits, V, B, drows, hist, 128, toks))
+    layer_bytes = 524_288 + touched * 2_654_208 + 2 * B * D * 2
+    return {"workload": "config4 shape: one 30B MoE layer for 256 tokens + 256 sampler rows",
+            "layer_us": round(layer_us, 1), "tokens_per_s_per_layer": round(B / (layer_us * 1e-6)),
+            "experts_touched": touched, "layer_bytes": layer_bytes,
+            "achieved_gbs": round(layer_bytes / (layer_us * 1e-6) / 1e9, 1),
+            "sampler_us_256_rows": round(samp_us, 1)}
+
+
 def decode_leg(ctx, prompt=45, gen=256):
     """Config 2 shape: Qwen3-30B-A3B decode (48 layers, random weights with
     the benchmark distributions), batch 1, one CUDA graph per token
@@ -430,6 +487,7 @@ def decode_leg(ctx, prompt=45, gen=256):
     dec.run(pr, 8)
     dec.reset()
     _, t = dec.run(pr, gen)
+    ctx.synchronize()
     attn = (2 * sh.q_dim + 2 * sh.kv_dim) * sh.d_model * 2
     per_tok = (sh.layers * (sh.top_k * S.expert_bytes(sh.fmt, sh.d_model, sh.d_ff) + attn
                             + sh.n_experts * sh.d_model * 2) + sh.vocab * sh.d_model * 2)
