@@ -17,6 +17,13 @@
 
 namespace smoe {
 
+// Programmatic dependent launch: every trunk kernel lets the next kernel in
+// the stream launch at once (its CTAs then wait in pdl_wait, which returns
+// only when this whole grid has completed and its writes are visible), and
+// waits for its own predecessor before reading anything that one wrote.
+SMOE_DEVINL void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+SMOE_DEVINL void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 constexpr int kAttnThreads = 256;
 constexpr int kAttnMaxCtx = 8192;      // scores of one head held in shared memory
 
@@ -48,6 +55,8 @@ SMOE_DEVINL float block_max(float v, float* red32) {
 
 // out[t*d + i] = embedding row token[t] (decode.cpp:103-107). grid (ceil(d/256), ntok).
 __global__ void k_embed(const uint16_t* table, const uint32_t* token, uint32_t d, float* out) {
+    pdl_trigger();
+    pdl_wait();
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x, t = blockIdx.y;
     if (i < d) out[size_t(t) * d + i] = bf16_bits_to_f32(table[size_t(token[t]) * d + i]);
 }
@@ -57,6 +66,8 @@ __global__ void k_embed(const uint16_t* table, const uint32_t* token, uint32_t d
 __global__ void k_add_rms_norm(float* hidden, const float* delta, const uint16_t* w, float* normed,
                                uint32_t n) {
     __shared__ float red32[32];
+    pdl_trigger();
+    pdl_wait();
     float* h = hidden + size_t(blockIdx.x) * n;
     const float* dl = delta ? delta + size_t(blockIdx.x) * n : nullptr;
     float* o = normed + size_t(blockIdx.x) * n;
@@ -115,54 +126,68 @@ SMOE_DEVINL float dot8_bf16(uint4 v, const float4* xp) {
     return s;
 }
 
+// RPW rows per warp (1 for small matrices, so the grid covers the SMs; 2
+// for large ones). The first chunk of weight loads is issued before waiting
+// for the kernel that produced x (weights do not depend on it).
+template <int RPW>
 __global__ void __launch_bounds__(kGemvThreads) k_gemv_set(GemvSet a, uint32_t total) {
     const int lane = threadIdx.x & 31;
+    pdl_trigger();
     const uint32_t nwarp = gridDim.x * (kGemvThreads / 32);
     const uint32_t n = a.cols / 8;                                   // 16-byte chunks per row
     const float4* x4 = reinterpret_cast<const float4*>(a.x);
-    for (uint32_t r0 = (blockIdx.x * (kGemvThreads / 32) + (threadIdx.x >> 5)) * 2; r0 < total; r0 += nwarp * 2) {
-        const uint16_t *w0, *w1;
-        float *y0, *y1;
-        gemv_locate(a, r0, w0, y0);
-        gemv_locate(a, r0 + 1 < total ? r0 + 1 : r0, w1, y1);
-        if (r0 + 1 >= total) y1 = nullptr;
-        const uint4* p0 = reinterpret_cast<const uint4*>(w0);
-        const uint4* p1 = reinterpret_cast<const uint4*>(w1);
-        float s0 = 0.f, s1 = 0.f;
+    bool waited = false;
+    for (uint32_t r0 = (blockIdx.x * (kGemvThreads / 32) + (threadIdx.x >> 5)) * RPW; r0 < total;
+         r0 += nwarp * RPW) {
+        const uint4* p[RPW];
+        float* y[RPW];
+#pragma unroll
+        for (int q = 0; q < RPW; ++q) {
+            const uint16_t* w;
+            gemv_locate(a, r0 + q < total ? r0 + q : r0, w, y[q]);
+            if (r0 + q >= total) y[q] = nullptr;
+            p[q] = reinterpret_cast<const uint4*>(w);
+        }
+        float sacc[RPW];
+#pragma unroll
+        for (int q = 0; q < RPW; ++q) sacc[q] = 0.f;
         for (uint32_t c0 = lane; c0 < n; c0 += 32 * 8) {
-            uint4 v0[8], v1[8];
+            uint4 v[RPW][8];
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                const uint32_t c = c0 + q * 32;
-                if (c < n) {
-                    v0[q] = __ldcs(p0 + c);                          // streamed once: do not keep in L2
-                    v1[q] = __ldcs(p1 + c);
-                }
+            for (int j = 0; j < 8; ++j) {
+                const uint32_t c = c0 + j * 32;
+#pragma unroll
+                for (int q = 0; q < RPW; ++q)
+                    if (c < n) v[q][j] = __ldcs(p[q] + c);           // streamed once: do not keep in L2
+            }
+            if (!waited) {
+                pdl_wait();
+                waited = true;
             }
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                const uint32_t c = c0 + q * 32;
-                if (c < n) {
-                    s0 += dot8_bf16(v0[q], x4 + 2 * c);
-                    s1 += dot8_bf16(v1[q], x4 + 2 * c);
-                }
+            for (int j = 0; j < 8; ++j) {
+                const uint32_t c = c0 + j * 32;
+#pragma unroll
+                for (int q = 0; q < RPW; ++q)
+                    if (c < n) sacc[q] += dot8_bf16(v[q][j], x4 + 2 * c);
             }
         }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            s0 += __shfl_xor_sync(0xffffffffu, s0, o);
-            s1 += __shfl_xor_sync(0xffffffffu, s1, o);
-        }
-        if (lane == 0) {
-            *y0 = s0;
-            if (y1) *y1 = s1;
+        for (int q = 0; q < RPW; ++q) {
+            float sv = sacc[q];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) sv += __shfl_xor_sync(0xffffffffu, sv, o);
+            if (lane == 0 && y[q]) *y[q] = sv;
         }
     }
+    if (!waited) pdl_wait();
 }
 
 // cos/sin of this step's RoPE angles: angle = float(pos) * inv_freq[i]
 // (decode.cpp:113-118), pos read from the device.
 __global__ void k_rope_table(const uint32_t* pos, const float* inv_freq, float* cs, float* sn, uint32_t half) {
+    pdl_trigger();
+    pdl_wait();
     const uint32_t i = threadIdx.x + blockIdx.x * blockDim.x;
     if (i < half) {
         const float a = float(*pos) * inv_freq[i];
@@ -235,6 +260,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(AttnArgs a) {
     __shared__ float part[kAttnThreads];
     const uint32_t h = blockIdx.x, hd = a.head_dim, per = a.num_heads / a.num_kv_heads, kvh = h / per;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = kAttnThreads / 32;
+    pdl_trigger();
+    pdl_wait();
     uint32_t slot, valid;
     attn_slot_valid(a, slot, valid);
     for (uint32_t i = tid; i < hd; i += blockDim.x) {
@@ -330,6 +357,8 @@ struct SamplerRowDevMut {
 };
 __global__ void k_decode_advance(SamplerRowDevMut* row, uint32_t* history, uint32_t hcap,
                                  const uint32_t* token, uint32_t* pos, const float* u_seq, uint32_t u_len) {
+    pdl_trigger();
+    pdl_wait();
     if (threadIdx.x != 0 || blockIdx.x != 0) return;
     const uint32_t n = row->history_len;
     if (n < hcap) {

@@ -768,6 +768,24 @@ int smoe_cuda_moe_layer(SmoeCudaCtx* c, const SmoeMoeLayer* L, const void* x, in
 
 // ------------------------------------------------------- dense trunk (decode)
 namespace {
+// Launch a trunk kernel with programmatic stream serialization: it may start
+// while its predecessor drains, and waits for it in pdl_wait().
+extern "C++" template <typename... KArgs, typename... Args>
+int pdl_launch(SmoeCudaCtx* c, void (*kern)(KArgs...), dim3 grid, dim3 block, Args... args) {
+    cudaLaunchConfig_t lc{};
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.gridDim = grid;
+    lc.blockDim = block;
+    lc.dynamicSmemBytes = 0;
+    lc.stream = c->stream;
+    lc.attrs = at;
+    lc.numAttrs = 1;
+    c->dispatches += 1;
+    return cudaLaunchKernelEx(&lc, kern, KArgs(args)...) == cudaSuccess ? SMOE_OK : SMOE_ERR_CUDA;
+}
+
 int gemv_set(SmoeCudaCtx* c, const smoe::GemvSet& g) {
     uint32_t total = 0;
     for (uint32_t m = 0; m < g.nmat; ++m) {
@@ -776,12 +794,14 @@ int gemv_set(SmoeCudaCtx* c, const smoe::GemvSet& g) {
     }
     if (!g.x || g.cols == 0 || g.cols % 8 || g.cols > 16384) { set_err("bad matvec cols %s%ld", "", (long)g.cols); return SMOE_ERR_ARG; }
     if (!aligned16(g.x)) { set_err("matvec input must be 16-byte aligned %s%ld", "", 0); return SMOE_ERR_ARG; }
-    // one warp per row pair, at most 8 CTAs of 8 warps per SM (grid-stride beyond)
-    const uint32_t pairs = (total + 1) / 2, warps = smoe::kGemvThreads / 32;
-    const uint32_t want = (pairs + warps - 1) / warps, cap = uint32_t(c->num_sms) * 8;
-    smoe::k_gemv_set<<<want < cap ? want : cap, smoe::kGemvThreads, 0, c->stream>>>(g, total);
-    c->dispatches += 1;
-    return cudaGetLastError() == cudaSuccess ? SMOE_OK : SMOE_ERR_CUDA;
+    // one warp per row (two for large matrices), at most 8 CTAs of 8 warps
+    // per SM (grid-stride beyond)
+    const uint32_t warps = smoe::kGemvThreads / 32, cap = uint32_t(c->num_sms) * 8;
+    const bool pair = total > cap * warps;
+    const uint32_t units = pair ? (total + 1) / 2 : total;
+    const uint32_t want = (units + warps - 1) / warps;
+    return pdl_launch(c, pair ? smoe::k_gemv_set<2> : smoe::k_gemv_set<1>, dim3(want < cap ? want : cap),
+                      dim3(smoe::kGemvThreads), g, total);
 }
 }  // namespace
 
@@ -801,35 +821,29 @@ int smoe_cuda_matvec_bf16(SmoeCudaCtx* c, const uint16_t* w, const float* x, flo
 int smoe_cuda_rms_norm(SmoeCudaCtx* c, float* hidden, const float* delta, const uint16_t* w, float* normed,
                        uint32_t n, uint32_t rows) {
     if (!c || !hidden || !w || !normed || n == 0 || rows == 0) { set_err("bad rms_norm arguments %s%ld", "", (long)n); return SMOE_ERR_ARG; }
-    smoe::k_add_rms_norm<<<rows, 1024, 0, c->stream>>>(hidden, delta, w, normed, n);
-    c->dispatches += 1;
-    return cudaGetLastError() == cudaSuccess ? SMOE_OK : SMOE_ERR_CUDA;
+    return pdl_launch(c, smoe::k_add_rms_norm, dim3(rows), dim3(1024), hidden, delta, w, normed, n);
 }
 
 int smoe_cuda_embed_bf16(SmoeCudaCtx* c, const uint16_t* table, const uint32_t* tokens, uint32_t n_tokens,
                          uint32_t d_model, float* out) {
     if (!c || !table || !tokens || !out || n_tokens == 0 || d_model == 0) { set_err("bad embed arguments %s%ld", "", 0); return SMOE_ERR_ARG; }
-    smoe::k_embed<<<dim3((d_model + 255) / 256, n_tokens), 256, 0, c->stream>>>(table, tokens, d_model, out);
-    c->dispatches += 1;
-    return cudaGetLastError() == cudaSuccess ? SMOE_OK : SMOE_ERR_CUDA;
+    return pdl_launch(c, smoe::k_embed, dim3((d_model + 255) / 256, n_tokens), dim3(256), table, tokens, d_model,
+                      out);
 }
 
 int smoe_cuda_rope_table(SmoeCudaCtx* c, const uint32_t* pos, const float* inv_freq, float* cos_out,
                          float* sin_out, uint32_t half) {
     if (!c || !pos || !inv_freq || !cos_out || !sin_out || half == 0) { set_err("bad rope arguments %s%ld", "", 0); return SMOE_ERR_ARG; }
-    smoe::k_rope_table<<<(half + 127) / 128, 128, 0, c->stream>>>(pos, inv_freq, cos_out, sin_out, half);
-    c->dispatches += 1;
-    return cudaGetLastError() == cudaSuccess ? SMOE_OK : SMOE_ERR_CUDA;
+    return pdl_launch(c, smoe::k_rope_table, dim3((half + 127) / 128), dim3(128), pos, inv_freq, cos_out, sin_out,
+                      half);
 }
 
 int smoe_cuda_decode_advance(SmoeCudaCtx* c, SmoeSamplerRow* row, uint32_t* history, uint32_t hcap,
                              const uint32_t* token, uint32_t* pos, const float* u_seq, uint32_t u_len) {
     if (!c || !row || !token || !pos || (hcap && !history)) { set_err("bad decode_advance arguments %s%ld", "", 0); return SMOE_ERR_ARG; }
     static_assert(sizeof(SmoeSamplerRow) == sizeof(smoe::SamplerRowDevMut), "row layout");
-    smoe::k_decode_advance<<<1, 32, 0, c->stream>>>(reinterpret_cast<smoe::SamplerRowDevMut*>(row), history,
-                                                     hcap, token, pos, u_seq, u_len);
-    c->dispatches += 1;
-    return cudaGetLastError() == cudaSuccess ? SMOE_OK : SMOE_ERR_CUDA;
+    return pdl_launch(c, smoe::k_decode_advance, dim3(1), dim3(32),
+                      reinterpret_cast<smoe::SamplerRowDevMut*>(row), history, hcap, token, pos, u_seq, u_len);
 }
 
 int smoe_cuda_attention_layer_async(SmoeCudaCtx* c, const SmoeCudaAttnLayerArgs* a, const uint32_t* pos) {
@@ -865,8 +879,8 @@ int smoe_cuda_attention_layer_async(SmoeCudaCtx* c, const SmoeCudaAttnLayerArgs*
     t.slot = a->slot; t.valid = a->valid; t.attn_ctx = a->attn_ctx;
     t.pos = pos;
     t.scale = a->attn_scale;
-    smoe::k_attn_decode<<<a->num_heads, smoe::kAttnThreads, 0, c->stream>>>(t);
-    c->dispatches += 1;
+    rc = pdl_launch(c, smoe::k_attn_decode, dim3(a->num_heads), dim3(smoe::kAttnThreads), t);
+    if (rc) return rc;
     // 4. O projection
     smoe::GemvSet o{};
     o.w[0] = a->w_o; o.y[0] = a->o_out; o.rows[0] = a->d_model;
