@@ -500,6 +500,20 @@ def decode_leg(ctx, prompt=45, gen=256):
     return out
 
 
+def run_leg(name):
+    import torch
+    import smoe_cuda as S
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    torch.cuda.set_device(0)
+    ctx = S.Context(0)
+    stream = torch.cuda.Stream()
+    ctx.set_stream(stream.cuda_stream)
+    out = {"sampler": lambda: sampler_leg(ctx, stream), "decode_30b": lambda: decode_leg(ctx),
+           "batch256": lambda: batch_leg(ctx, stream)}[name]()
+    print(json.dumps({name: out}), flush=True)
+    ctx.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -509,7 +523,12 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the sampler and decode legs")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--only", choices=["sampler", "decode_30b", "batch256"],
+                    help="run one side leg alone on GPU 0 and print its JSON (profiling)")
     args = ap.parse_args()
+    if args.only:
+        run_leg(args.only)
+        return
     rank, world, local = dist_init(args.gpus)
     if args.impl == "reference":
         run_reference(args, rank, world)
