@@ -18,6 +18,7 @@
 //   k_combine_slots y[t] = sum_j w[t,j] * y_slot[t*k+j] in rank order
 //                   (product then sum, as axpy_f32 in decode.cpp:485-499)
 #pragma once
+#include <type_traits>
 #include "ffn_q4.cuh"
 
 namespace smoe {
@@ -32,54 +33,20 @@ struct GroupedArgs {
     const uint2* tab;             // B tables of the input vectors [nvec][K/16][8]
     const float2* gs;             // their group sums [nvec][K/64]
     uint32_t tab_div;             // input vector of a slot = slot / tab_div (k for x, 1 for h)
+    const uint32_t* lo_flag;      // 0: every table's lo halves are zero (16-token MMAs); null: 8
     float* out;                   // gate/up: h [nslots][d_ff]; down: y_slot [nslots][d_model]
     uint32_t d_model, d_ff;
     uint32_t* err;
 };
 
-// B registers of group grp (4 k-steps) for this lane: column g (lane / 4)
-// comes from vector g / 2, hi (g even) or lo (g odd) half.
-SMOE_DEVINL void load_b4(const uint2* tabg, int grp, int lane, uint2* bs) {
-    const int gr = lane >> 2, c = lane & 3;
-#pragma unroll
-    for (int s = 0; s < 4; ++s) bs[s] = tabg ? __ldg(tabg + (grp * 4 + s) * 8 + (gr & 1) * 4 + c) : make_uint2(0u, 0u);
-}
-
-// One 64-group of a 16-row tile against 4 vectors (B registers bs from
-// load_b4): returns the group sums of rows lane/4 and lane/4 + 8 for vector
-// lane % 4.
-SMOE_DEVINL void group_mma4(const uint8_t* rowp, int rs, int grp, const uint2* bs, int lane, float& r0,
-                            float& r8) {
-    const int gr = lane >> 2, c = lane & 3;
-    const uint2 w = *reinterpret_cast<const uint2*>(rowp + gr * rs + grp * 32 + c * 8);
-    const uint2 v = *reinterpret_cast<const uint2*>(rowp + (gr + 8) * rs + grp * 32 + c * 8);
-    float d[4] = {0.f, 0.f, 0.f, 0.f};
-    const uint32_t M0 = 0x000F000Fu, M1 = 0x00F000F0u, OR = 0x64006400u;
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-        const uint32_t wg = i ? w.y : w.x, wh = i ? v.y : v.x;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const uint32_t g8 = h ? (wg >> 8) : wg, h8 = h ? (wh >> 8) : wh;
-            uint32_t a[4];
-            a[0] = hsub_1024(lop3_and_or(g8, M0, OR));
-            a[1] = hsub_1024(lop3_and_or(h8, M0, OR));
-            a[2] = hsub_1024(lop3_and_or(g8, M1, OR));
-            a[3] = hsub_1024(lop3_and_or(h8, M1, OR));
-            const uint32_t bb[2] = {bs[i * 2 + h].x, bs[i * 2 + h].y};
-            mma_f16_16816(d, a, bb);
-        }
-    }
-    r0 = d[0] + d[1];
-    r8 = d[2] + d[3];
-}
-
 // Per-expert slot lists: one CTA (one warp) per expert, ballot compaction
 // over the slots in order (deterministic); ids are read 16 per lane ahead of
 // the ballots so the scan is not a chain of dependent loads.
+// Also clears the lo flag that the following k_build_tabs of x sets.
 __global__ void k_group_slots(const uint32_t* ids, uint32_t nslots, uint32_t* list, uint32_t* count,
-                              uint32_t lcap) {
+                              uint32_t lcap, uint32_t* lo_flag) {
     const uint32_t e = blockIdx.x, lane = threadIdx.x;
+    if (e == 0 && lane == 0 && lo_flag) *lo_flag = 0u;
     uint32_t n = 0;
     for (uint32_t b0 = 0; b0 < nslots; b0 += 32 * 16) {
         uint32_t v[16];
@@ -103,42 +70,74 @@ __global__ void k_group_slots(const uint32_t* ids, uint32_t nslots, uint32_t* li
 
 // B tables of n vectors (one CTA each): f32 or bf16 rows of K, row stride K.
 __global__ void __launch_bounds__(256) k_build_tabs(const void* src, int bf16, uint32_t K, uint2* tab,
-                                                    float2* gs) {
+                                                    float2* gs, uint32_t* lo_flag) {
     extern __shared__ __align__(16) float2 part[];            // [K/4]
     const size_t v = blockIdx.x;
     uint2* t = tab + v * (K / 16) * 8;
     float2* g = gs + v * (K / 64);
     if (bf16) {
         const uint16_t* xv = static_cast<const uint16_t*>(src) + v * K;
-        build_btab([&](int i) { return bf16_bits_to_f32(xv[i]); }, int(K), t, g, part);
+        build_btab<true>([&](int i) { return bf16_bits_to_f32(xv[i]); }, int(K), t, g, part, lo_flag);
     } else {
         const float* xv = static_cast<const float*>(src) + v * K;
-        build_btab([&](int i) { return xv[i]; }, int(K), t, g, part);
+        build_btab<true>([&](int i) { return xv[i]; }, int(K), t, g, part, lo_flag);
     }
 }
 
-// Shared layout of a grouped CTA: tile [mats][rb][rs] nibbles (rows padded
-// by 32 B: conflict-free fragment loads), scales/biases [mats][2][rb * G].
-inline size_t grouped_smem_bytes(int K, int mats, int rb) {
+// Shared layout of a grouped CTA: weight tile [MATS][RB][rs] nibbles (rows
+// padded by 32 B: conflict-free fragment loads), the scales/biases in the
+// lanes' order [MATS][2][G][WN][c][NTW][2], one region holding first the
+// scales/biases as copied [MATS][2][RB][G] and afterwards the split-K
+// partial sums [8 warps][accumulators][32 lanes] of one token chunk, and
+// the first kSlotCache entries of the expert's slot list.
+constexpr int kSlotCache = 256;
+__host__ __device__ inline size_t grouped_union_bytes(int K, int mats, int rb, int wn) {
+    const size_t sbb = size_t(mats) * 2 * rb * (K / 64) * 2;
+    const size_t redb = size_t(8) * mats * (rb / 8 / wn) * 4 * 32 * 4;      // 16-token chunks
+    return sbb > redb ? sbb : redb;
+}
+inline size_t grouped_smem_bytes(int K, int mats, int rb, int wn) {
     const int rs = K / 2 + 32, G = K / 64;
-    return size_t(mats * rb * rs) + size_t(mats) * 2 * rb * G * 2 + 16;
+    return size_t(mats * rb * rs) + size_t(mats) * 2 * rb * G * 2 + grouped_union_bytes(K, mats, rb, wn) +
+           kSlotCache * 4 + 16;
 }
 
 // MATS = 2: gate + up rows (K = d_model) -> h; MATS = 1: down rows (K = d_ff)
-// -> y_slot. grid (rows / RB, E), 256 threads. A warp task is (16-row tile,
-// chunk of 4 of the expert's vectors) over all K groups, so results are
-// complete inside the warp: no CTA barrier and no cross-warp reduction in
-// the token loop.
-template <int FMT, int MATS, int RB>
-__global__ void __launch_bounds__(256) k_ffn_grouped(GroupedArgs a) {
+// -> y_slot. grid (rows / RB, E), 256 threads = WK k-slices x WN row slices.
+// Token-major MMAs: M rows = tokens, N columns = 8 weight rows, so one
+// dequantised weight fragment (2 registers; one 8-byte shared load covers
+// 4 k-steps) serves every token of the MMA. Two row modes:
+//   16 tokens (rows g and g+8 = two tokens) when every input vector of the
+//     batch is exact in fp16 after its power-of-two scale (lo halves all
+//     zero, flagged by k_build_tabs: any bf16 input with a dynamic range
+//     below 2^27);
+//   8 tokens (rows g = hi halves, g+8 = lo halves of the same tokens;
+//     d0 + d2, d1 + d3 add them) otherwise - the fp32 hidden vectors.
+// Lane (g, c) holds weight rows 2c, 2c+1 of each of its NTW n-tiles. Each
+// warp runs its 64-groups for all NTW n-tiles of every matrix, so an x
+// fragment is loaded once per CTA and feeds MATS * NTW MMAs; a warp's
+// (chunk, group) items form one software pipeline whose loads run ahead
+// across chunk boundaries; the WK partial sums are added in shared memory in
+// k-slice order (fixed order: deterministic), with SiLU(gate) * up or the
+// down output written there. Group epilogue as group_epilogue, the
+// per-vector scale gs.x applied once at the end.
+// KC: K when known at compile time (0: read from the arguments), which makes
+// every shared-memory offset of the inner loop an immediate.
+template <int FMT, int MATS, int RB, int WN, int KC>
+__global__ void __launch_bounds__(256, 2) k_ffn_grouped(GroupedArgs a) {
+    constexpr int WK = 8 / WN, NTW = RB / 8 / WN;
+    static_assert(NTW % 4 == 0, "scale rows are read 8 at a time");
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t e = blockIdx.y, T = a.count[e];
     if (T == 0) return;
-    const int K = MATS == 2 ? a.d_model : a.d_ff, R = MATS == 2 ? a.d_ff : a.d_model;
+    const int K = KC ? KC : (MATS == 2 ? int(a.d_model) : int(a.d_ff)), R = MATS == 2 ? a.d_ff : a.d_model;
     const int blk = blockIdx.x, rs = K / 2 + 32, G = K / 64, nsb = RB * G;
     uint8_t* wt = smem;                                                 // [MATS][RB][rs]
-    uint16_t* sb = reinterpret_cast<uint16_t*>(wt + MATS * RB * rs);    // [MATS][2][nsb]
-    uint64_t* bar = reinterpret_cast<uint64_t*>(sb + MATS * 2 * nsb);
+    uint16_t* st = reinterpret_cast<uint16_t*>(wt + MATS * RB * rs);    // [MATS][2][G][WN][4][NTW][2]
+    uint16_t* sb = st + MATS * 2 * nsb;                                 // [MATS][2][RB][G], then:
+    float* red = reinterpret_cast<float*>(sb);                          // [8][acc][32]
+    uint32_t* sl = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(sb) + grouped_union_bytes(K, MATS, RB, WN));
+    uint64_t* bar = reinterpret_cast<uint64_t*>(sl + kSlotCache);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gr = lane >> 2, c = lane & 3;
     const uint8_t* eb = a.base + uint64_t(e) * a.stride;
     if (tid == 0) {
@@ -162,58 +161,170 @@ __global__ void __launch_bounds__(256) k_ffn_grouped(GroupedArgs a) {
             bulk_g2s(sb + ((lane - 2) * 2 + 1) * nsb, eb + a.off[3 * (m0 + lane - 2) + 2] + size_t(blk) * sbytes,
                      sbytes, bar);
     }
+    const uint32_t* lst = a.list + size_t(e) * a.lcap;
+    for (uint32_t i = tid; i < T && i < uint32_t(kSlotCache); i += 256) sl[i] = lst[i];
+    const bool hi_only = a.lo_flag && *a.lo_flag == 0u;
     if (!mbar_wait_bounded(bar, 0)) {
         if (tid == 0) atomicExch(a.err, SMOE_DEVERR_MBAR_TIMEOUT);
         return;
     }
-    const uint32_t* lst = a.list + size_t(e) * a.lcap;
-    const int nchunk = int((T + 3) / 4), ntask = (RB / 16) * nchunk;
-    for (int task = warp; task < ntask; task += 8) {
-        const int tile = task % (RB / 16), c0 = (task / (RB / 16)) * 4;
-        const uint32_t tb = c0 + (gr >> 1), tc = c0 + c;
-        const uint2* tabg = tb < T ? a.tab + size_t(lst[tb] / a.tab_div) * (K / 16) * 8 : nullptr;
-        const float2* gsv = tc < T ? a.gs + size_t(lst[tc] / a.tab_div) * G : nullptr;
-        float acc[MATS][2];
+    // scales/biases into the lanes' order: lane c of row slice wn reads its
+    // 2 * NTW values of a group with NTW / 4 16-byte loads
+    for (int i = tid; i < MATS * 2 * nsb; i += 256) {
+        const int q = i & 1, nt = (i >> 1) % NTW, c4 = (i / (2 * NTW)) & 3, wn = (i / (8 * NTW)) % WN;
+        const int grp = (i / RB) % G, mk = i / (RB * G);
+        st[i] = sb[mk * nsb + (wn * NTW * 8 + nt * 8 + 2 * c4 + q) * G + grp];
+    }
+    __syncthreads();                      // sb is dead from here: red may overwrite it
+    auto slot_of = [&](uint32_t i) { return i < uint32_t(kSlotCache) ? sl[i] : lst[i]; };
+    const int wk = warp / WN, wn = warp % WN;
+    const int gpw = (G + WK - 1) / WK, g0 = wk * gpw, g1 = min(G, g0 + gpw), ng = max(g1 - g0, 0);
+    const uint32_t M0 = 0x000F000Fu, M1 = 0x00F000F0u, OR = 0x64006400u;
+
+    auto body = [&](auto tpc_tag) {
+        constexpr int TPC = decltype(tpc_tag)::value;       // tokens per chunk: 8 or 16
+        constexpr int TT = TPC / 8;                          // tokens per lane
+        constexpr int NAC = MATS * NTW * TT * 2;             // accumulators per lane
+        const int nchunk = int((T + TPC - 1) / TPC), nit = nchunk * ng;
+        // loads of item j = (chunk j / ng, group g0 + j % ng): A registers
+        // x[s][0..3] of the 4 k-steps and the group sums of the lane's tokens
+        auto issue = [&](int j, uint32_t (&x)[4][4], float (&y)[TT]) {
+            if (j >= nit) return;
+            const int chj = j / ng, grp = g0 + j % ng;
 #pragma unroll
-        for (int m = 0; m < MATS; ++m) acc[m][0] = acc[m][1] = 0.f;
-        // four groups at a time: their 16 B loads and 4 group sums are in
-        // flight together (the tables come from L2), then their MMAs
-        for (int g0 = 0; g0 < G; g0 += 4) {
-            uint2 bs[4][4];
-            float2 gsum[4];
+            for (int tt = 0; tt < TT; ++tt) {
+                const uint32_t tk = chj * TPC + tt * 8 + gr;
+                const uint32_t vec = slot_of(tk < T ? tk : 0) / a.tab_div;
+                const size_t ent = (size_t(vec) * (K / 16) + grp * 4) * 4 + c;   // 16-byte entries
+                if (TT == 1) {
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const int grp = min(g0 + q, G - 1);
-                load_b4(tabg, grp, lane, bs[q]);
-                gsum[q] = gsv ? __ldg(gsv + grp) : make_float2(0.f, 0.f);
-            }
+                    for (int s = 0; s < 4; ++s) {
+                        const uint4 q = __ldg(reinterpret_cast<const uint4*>(a.tab) + ent + s * 4);
+                        x[s][0] = q.x; x[s][1] = q.z; x[s][2] = q.y; x[s][3] = q.w;   // hi.x lo.x hi.y lo.y
+                    }
+                } else {
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const int grp = g0 + q;
-                if (grp < G) {
-#pragma unroll
-                    for (int m = 0; m < MATS; ++m) {
-                        float r0, r8;
-                        group_mma4(wt + (m * RB + tile * 16) * rs, rs, grp, bs[q], lane, r0, r8);
-                        const uint16_t* sc = sb + (m * 2) * nsb;
-                        const uint16_t* bi = sb + (m * 2 + 1) * nsb;
-                        acc[m][0] += group_epilogue<FMT>(r0, gsum[q], sc, bi, (tile * 16 + gr) * G + grp);
-                        acc[m][1] += group_epilogue<FMT>(r8, gsum[q], sc, bi, (tile * 16 + gr + 8) * G + grp);
+                    for (int s = 0; s < 4; ++s) {
+                        const uint2 h = __ldg(reinterpret_cast<const uint2*>(a.tab) + (ent + s * 4) * 2);
+                        x[s][tt] = h.x;
+                        x[s][2 + tt] = h.y;
                     }
                 }
+                y[tt] = __ldg(&a.gs[size_t(vec) * G + grp].y);
             }
-        }
-        if (tc < T) {
-            float* o = a.out + size_t(lst[tc]) * R + blk * RB + tile * 16 + gr;
-            if (MATS == 2) {
-                o[0] = acc[0][0] * (1.0f / (1.0f + expf(-acc[0][0]))) * acc[1][0];   // kernels.metal:61-63
-                o[8] = acc[0][1] * (1.0f / (1.0f + expf(-acc[0][1]))) * acc[MATS - 1][1];
-            } else {
-                o[0] = acc[0][0];
-                o[8] = acc[0][1];
+        };
+        constexpr int NB = TT == 1 ? 3 : 2;                  // load buffers (pipeline depth NB - 1)
+        uint32_t xb[NB][4][4];
+        float yb[NB][TT];
+#pragma unroll
+        for (int p = 0; p < NB - 1; ++p) issue(p, xb[p], yb[p]);
+        int it = 0;
+        for (int ch = 0; ch < nchunk; ++ch) {
+            float acc[NAC];
+#pragma unroll
+            for (int i = 0; i < NAC; ++i) acc[i] = 0.f;
+            for (int grp = g0; grp < g1; ++grp, ++it) {
+                issue(it + NB - 1, xb[NB - 1], yb[NB - 1]);
+                const uint8_t* wl = wt + (wn * NTW * 8 + gr) * rs + grp * 32 + c * 8;   // this lane's rows
+#pragma unroll
+                for (int m = 0; m < MATS; ++m) {
+                    uint32_t scw[NTW], biw[NTW];
+                    const uint16_t* sp = st + ((((m * 2) * G + grp) * WN + wn) * 4 + c) * NTW * 2;
+#pragma unroll
+                    for (int v = 0; v < NTW / 4; ++v) {
+                        const uint4 s4 = *reinterpret_cast<const uint4*>(sp + v * 8);
+                        scw[v * 4 + 0] = s4.x; scw[v * 4 + 1] = s4.y; scw[v * 4 + 2] = s4.z; scw[v * 4 + 3] = s4.w;
+                        if (FMT == kFmtAffine) {
+                            const uint4 b4 = *reinterpret_cast<const uint4*>(sp + G * WN * 4 * NTW * 2 + v * 8);
+                            biw[v * 4 + 0] = b4.x; biw[v * 4 + 1] = b4.y; biw[v * 4 + 2] = b4.z; biw[v * 4 + 3] = b4.w;
+                        }
+                    }
+#pragma unroll
+                    for (int nt = 0; nt < NTW; ++nt) {
+                        const uint2 w = *reinterpret_cast<const uint2*>(wl + (m * RB + nt * 8) * rs);
+                        float d[4];
+#pragma unroll
+                        for (int s = 0; s < 4; ++s) {
+                            const uint32_t wi = (s >> 1) ? w.y : w.x;
+                            const uint32_t g8 = (s & 1) ? (wi >> 8) : wi;
+                            const uint32_t b[2] = {hsub_1024(lop3_and_or(g8, M0, OR)),
+                                                   hsub_1024(lop3_and_or(g8, M1, OR))};
+                            if (s == 0) mma_f16_16816_z(d, xb[0][s], b);
+                            else mma_f16_16816(d, xb[0][s], b);
+                        }
+#pragma unroll
+                        for (int q = 0; q < 2; ++q) {
+                            float* ac = acc + (m * NTW + nt) * TT * 2;
+                            if (FMT == kFmtAffine) {
+                                const float sv = __uint_as_float(q ? (scw[nt] & 0xffff0000u) : (scw[nt] << 16));
+                                const float bv = __uint_as_float(q ? (biw[nt] & 0xffff0000u) : (biw[nt] << 16));
+                                if (TT == 1) {
+                                    ac[q] = fmaf(sv, d[q] + d[2 + q], fmaf(bv, yb[0][0], ac[q]));
+                                } else {
+#pragma unroll
+                                    for (int tt = 0; tt < TT; ++tt)
+                                        ac[tt * 2 + q] = fmaf(sv, d[tt * 2 + q], fmaf(bv, yb[0][tt], ac[tt * 2 + q]));
+                                }
+                            } else {
+                                const float sv = f16_bits_to_f32(uint16_t(q ? (scw[nt] >> 16) : (scw[nt] & 0xffffu)));
+                                if (TT == 1) {
+                                    ac[q] = fmaf(sv, fmaf(d[q] + d[2 + q], 1.0f / 7.5f, -yb[0][0]), ac[q]);
+                                } else {
+#pragma unroll
+                                    for (int tt = 0; tt < TT; ++tt)
+                                        ac[tt * 2 + q] = fmaf(sv, fmaf(d[tt * 2 + q], 1.0f / 7.5f, -yb[0][tt]),
+                                                              ac[tt * 2 + q]);
+                                }
+                            }
+                        }
+                    }
+                }
+#pragma unroll
+                for (int p = 0; p < NB - 1; ++p) {
+#pragma unroll
+                    for (int s = 0; s < 4; ++s)
+#pragma unroll
+                        for (int r = 0; r < 4; ++r) xb[p][s][r] = xb[p + 1][s][r];
+#pragma unroll
+                    for (int tt = 0; tt < TT; ++tt) yb[p][tt] = yb[p + 1][tt];
+                }
             }
+            float* rw = red + warp * NAC * 32 + lane;
+#pragma unroll
+            for (int i = 0; i < NAC; ++i) rw[i * 32] = acc[i];
+            __syncthreads();
+            for (int o = tid; o < TPC * RB; o += 256) {
+                const int t = o / RB, r = o % RB;
+                const uint32_t tk2 = ch * TPC + t;
+                if (tk2 < T) {
+                    const int wn2 = r / (NTW * 8), nt = (r / 8) % NTW, q = r & 1;
+                    const int ln = (t & 7) * 4 + ((r & 7) >> 1), tt = t >> 3;
+                    float v[MATS];
+#pragma unroll
+                    for (int m = 0; m < MATS; ++m) {
+                        float sum = 0.f;
+#pragma unroll
+                        for (int k2 = 0; k2 < WK; ++k2)
+                            sum += red[((k2 * WN + wn2) * NAC + ((m * NTW + nt) * TT + tt) * 2 + q) * 32 + ln];
+                        v[m] = sum;
+                    }
+                    const uint32_t slot = slot_of(tk2);
+                    const float inv = __ldg(&a.gs[size_t(slot / a.tab_div) * G].x);
+                    float outv;
+                    if (MATS == 2) {
+                        const float g = v[0] * inv, u = v[MATS - 1] * inv;
+                        outv = g * (1.0f / (1.0f + expf(-g))) * u;                  // kernels.metal:61-63
+                    } else {
+                        outv = v[0] * inv;
+                    }
+                    a.out[size_t(slot) * R + blk * RB + r] = outv;
+                }
+            }
+            __syncthreads();
         }
-    }
+    };
+    if (MATS == 2 && hi_only) body(std::integral_constant<int, 16>{});     // down inputs are fp32
+    else body(std::integral_constant<int, 8>{});
 }
 
 // y[t] = sum_j w[t*k+j] * ys[t*k+j] in rank order j (axpy_f32: product, then

@@ -96,8 +96,13 @@ SMOE_DEVINL float pow2_scale_for(float amax) {
     return ldexpf(1.0f, 14 - e);
 }
 
-template <typename Load>
-SMOE_DEVINL void build_btab(Load ld, int K, uint2* btab, float2* gsum, float2* part) {
+// QUAD: the grouped path's layout - per (group, k-step, c) one 16-byte
+// entry {hi.x, hi.y, lo.x, lo.y}: the hi pair alone is the A-fragment pair of
+// one token in a 16-token MMA. lo_flag (QUAD only) gets a nonzero word if
+// any lo half of this vector is nonzero.
+template <bool QUAD = false, typename Load>
+SMOE_DEVINL void build_btab(Load ld, int K, uint2* btab, float2* gsum, float2* part,
+                            uint32_t* lo_flag = nullptr) {
     // max |v| over the vector (block reduction through `part`)
     float amax = 0.0f;
     for (int i = threadIdx.x; i < K; i += blockDim.x) amax = fmaxf(amax, fabsf(ld(i)));
@@ -121,8 +126,14 @@ SMOE_DEVINL void build_btab(Load ld, int K, uint2* btab, float2* gsum, float2* p
         __half lo1 = __float2half_rn(o1 - __half2float(ho1));
         __half lo5 = __float2half_rn(o5 - __half2float(ho5));
         const int row = (grp * 4 + s) * 8;
-        btab[row + c] = make_uint2(pack_half2(he0, he4), pack_half2(ho1, ho5));
-        btab[row + 4 + c] = make_uint2(pack_half2(le0, le4), pack_half2(lo1, lo5));
+        if (QUAD) {
+            const uint32_t l0 = pack_half2(le0, le4), l1 = pack_half2(lo1, lo5);
+            reinterpret_cast<uint4*>(btab)[row / 2 + c] = make_uint4(pack_half2(he0, he4), pack_half2(ho1, ho5), l0, l1);
+            if (lo_flag && ((l0 | l1) & 0x7fff7fffu)) atomicOr(lo_flag, 1u);
+        } else {
+            btab[row + c] = make_uint2(pack_half2(he0, he4), pack_half2(ho1, ho5));
+            btab[row + 4 + c] = make_uint2(pack_half2(le0, le4), pack_half2(lo1, lo5));
+        }
         float x0 = __half2float(he0) + __half2float(le0);
         float x4 = __half2float(he4) + __half2float(le4);
         float x1 = 16.0f * (__half2float(ho1) + __half2float(lo1));

@@ -23,7 +23,15 @@ def gpu_available() -> bool:
 
 @pytest.fixture(scope="session")
 def ctx():
+    """One context for the session, bound to a torch stream that is also
+    torch's current stream while the tests run: tensors the tests allocate,
+    fill and read back are then ordered with the context's kernels."""
+    import torch
     import smoe_cuda
     c = smoe_cuda.Context(0)
-    yield c
+    s = torch.cuda.Stream()
+    c.set_stream(s.cuda_stream)
+    with torch.cuda.stream(s):
+        yield c
+    c.synchronize()
     c.close()

@@ -191,12 +191,16 @@ def test_tiled_moe_ffn_given_routing(ctx):
         assert rel_err(got[t], ref) < TIGHT
 
 
-@pytest.mark.parametrize("fmt,x_dtype", [(O.FMT_AFFINE_Q4, S.DTYPE_BF16), (O.FMT_SMOE_Q4, S.DTYPE_F32)])
-def test_moe_layer_token_batch_grouped(ctx, fmt, x_dtype):
+@pytest.mark.parametrize("fmt,x_dtype,d,dff", [(O.FMT_AFFINE_Q4, S.DTYPE_BF16, 2048, 768),
+                                                (O.FMT_SMOE_Q4, S.DTYPE_F32, 2048, 768),
+                                                (O.FMT_AFFINE_Q4, S.DTYPE_BF16, 1024, 512),
+                                                (O.FMT_SMOE_Q4, S.DTYPE_BF16, 1536, 256)])
+def test_moe_layer_token_batch_grouped(ctx, fmt, x_dtype, d, dff):
     """Token batches (> 4 tokens) on the vault layout run the expert-grouped
     path: router + grouped FFN + rank-order combine vs the oracle per token,
-    and the same result on a second call (deterministic order)."""
-    B, d, dff, E, k = 48, 2048, 768, 32, 8
+    and the same result on a second call (deterministic order). The 30B
+    shape runs the compile-time-K kernels, the others the generic ones."""
+    B, E, k = 48, 32, 8
     L = Layer(fmt, E, d, dff, seed=80 + fmt)
     Xb = O.normal_bf16(90 + fmt, 5, B * d)
     Xf = O.bf16_to_f32(Xb).reshape(B, d)
