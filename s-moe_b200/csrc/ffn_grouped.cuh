@@ -185,46 +185,60 @@ __global__ void __launch_bounds__(256, 2) k_ffn_grouped(GroupedArgs a) {
         constexpr int TPC = decltype(tpc_tag)::value;       // tokens per chunk: 8 or 16
         constexpr int TT = TPC / 8;                          // tokens per lane
         constexpr int NAC = MATS * NTW * TT * 2;             // accumulators per lane
-        const int nchunk = int((T + TPC - 1) / TPC), nit = nchunk * ng;
-        // loads of item j = (chunk j / ng, group g0 + j % ng): A registers
-        // x[s][0..3] of the 4 k-steps and the group sums of the lane's tokens
-        auto issue = [&](int j, uint32_t (&x)[4][4], float (&y)[TT]) {
-            if (j >= nit) return;
-            const int chj = j / ng, grp = g0 + j % ng;
+        const int nchunk = int((T + TPC - 1) / TPC);
+        // load cursor (chunk ich, group igrp), running NB - 1 items ahead of
+        // the MMAs: A registers x[s][0..3] of the 4 k-steps and the group
+        // sums of the lane's tokens; per-chunk table pointers ip / gp
+        int ich = ng > 0 ? 0 : nchunk, igrp = g0;
+        const uint4* ip[TT];
+        const float* gp[TT];
+        auto set_chunk = [&]() {
 #pragma unroll
             for (int tt = 0; tt < TT; ++tt) {
-                const uint32_t tk = chj * TPC + tt * 8 + gr;
+                const uint32_t tk = ich * TPC + tt * 8 + gr;
                 const uint32_t vec = slot_of(tk < T ? tk : 0) / a.tab_div;
-                const size_t ent = (size_t(vec) * (K / 16) + grp * 4) * 4 + c;   // 16-byte entries
+                ip[tt] = reinterpret_cast<const uint4*>(a.tab) + size_t(vec) * (K / 16) * 4 + c;
+                gp[tt] = &a.gs[size_t(vec) * G].y;
+            }
+        };
+        if (ich < nchunk) set_chunk();
+        auto issue = [&](uint32_t (&x)[4][4], float (&y)[TT]) {
+            if (ich >= nchunk) return;
+#pragma unroll
+            for (int tt = 0; tt < TT; ++tt) {
+                const uint4* q4 = ip[tt] + igrp * 16;
                 if (TT == 1) {
 #pragma unroll
                     for (int s = 0; s < 4; ++s) {
-                        const uint4 q = __ldg(reinterpret_cast<const uint4*>(a.tab) + ent + s * 4);
+                        const uint4 q = __ldg(q4 + s * 4);
                         x[s][0] = q.x; x[s][1] = q.z; x[s][2] = q.y; x[s][3] = q.w;   // hi.x lo.x hi.y lo.y
                     }
                 } else {
 #pragma unroll
                     for (int s = 0; s < 4; ++s) {
-                        const uint2 h = __ldg(reinterpret_cast<const uint2*>(a.tab) + (ent + s * 4) * 2);
+                        const uint2 h = __ldg(reinterpret_cast<const uint2*>(q4 + s * 4));
                         x[s][tt] = h.x;
                         x[s][2 + tt] = h.y;
                     }
                 }
-                y[tt] = __ldg(&a.gs[size_t(vec) * G + grp].y);
+                y[tt] = __ldg(gp[tt] + igrp * 2);
+            }
+            if (++igrp == g1) {
+                igrp = g0;
+                if (++ich < nchunk) set_chunk();
             }
         };
         constexpr int NB = TT == 1 ? 3 : 2;                  // load buffers (pipeline depth NB - 1)
         uint32_t xb[NB][4][4];
         float yb[NB][TT];
 #pragma unroll
-        for (int p = 0; p < NB - 1; ++p) issue(p, xb[p], yb[p]);
-        int it = 0;
+        for (int p = 0; p < NB - 1; ++p) issue(xb[p], yb[p]);
         for (int ch = 0; ch < nchunk; ++ch) {
             float acc[NAC];
 #pragma unroll
             for (int i = 0; i < NAC; ++i) acc[i] = 0.f;
-            for (int grp = g0; grp < g1; ++grp, ++it) {
-                issue(it + NB - 1, xb[NB - 1], yb[NB - 1]);
+            for (int grp = g0; grp < g1; ++grp) {
+                issue(xb[NB - 1], yb[NB - 1]);
                 const uint8_t* wl = wt + (wn * NTW * 8 + gr) * rs + grp * 32 + c * 8;   // this lane's rows
 #pragma unroll
                 for (int m = 0; m < MATS; ++m) {
