@@ -2,24 +2,24 @@
 // batched-decode shape: hundreds of tokens, each expert routed ~16 of them).
 //
 // The per-slot path (ffn_q4.cuh) streams an expert's weights once per
-// (token, expert) slot. Here the work is grouped by expert: a CTA owns 32
-// (gate/up) or 64 (down) rows of one expert's matrices, loads that weight
-// tile once and applies it to every token routed to the expert, four tokens
-// per MMA (B columns 2t,
-// 2t+1 = hi and lo halves of token t). The arithmetic is that of
-// ffn_q4.cuh (exact fp16 operands q / 16q, activations split hi + lo with a
+// (token, expert) slot. Here the work is grouped by expert: a CTA owns a
+// block of rows of one expert's matrices, loads that weight tile once and
+// applies it to every token routed to the expert. The arithmetic is that of
+// ffn_q4.cuh (exact fp16 operands q / 16 q, activations split hi + lo with a
 // per-vector power-of-two scale, per-group scale/bias epilogue), so results
 // match the per-slot path to fp32 rounding. Launch sequence per layer:
-//   k_group_slots   ids -> per-expert slot lists in slot order
-//   k_build_tabs    x rows -> B-operand tables (once per token)
-//   k_ffn_grouped<2> h[slot] = silu(g) * u for the expert's slots
-//   k_build_tabs    h rows -> tables (once per slot)
-//   k_ffn_grouped<1> y_slot = W_down . h[slot]
-//   k_combine_slots y[t] = sum_j w[t,j] * y_slot[t*k+j] in rank order
-//                   (product then sum, as axpy_f32 in decode.cpp:485-499)
+//   k_group_slots        ids -> per-expert slot lists in slot order
+//   k_build_tabs<Mma>    x rows -> B-operand tables (once per token)
+//   k_ffn_grouped<.., 2> gate/up with mma.sync, token-major:
+//                        h[slot] = silu(g) * u for the expert's slots
+//   k_build_tabs<Tc>     h rows -> tables (once per slot)
+//   k_ffn_down_tc        down with tcgen05: y_slot = W_down . h[slot]
+//   k_combine_slots      y[t] = sum_j w[t,j] * y_slot[t*k+j] in rank order
+//                        (product then sum, as axpy_f32 in decode.cpp:485-499)
 #pragma once
 #include <type_traits>
 #include "ffn_q4.cuh"
+#include "tc05.cuh"
 
 namespace smoe {
 
@@ -69,6 +69,9 @@ __global__ void k_group_slots(const uint32_t* ids, uint32_t nslots, uint32_t* li
 }
 
 // B tables of n vectors (one CTA each): f32 or bf16 rows of K, row stride K.
+// LAYOUT: kTabMma for the x tables the gate/up kernel reads, kTabTc for
+// the hidden-vector tables of the tensor-core down kernel.
+template <int LAYOUT>
 __global__ void __launch_bounds__(256) k_build_tabs(const void* src, int bf16, uint32_t K, uint2* tab,
                                                     float2* gs, uint32_t* lo_flag) {
     extern __shared__ __align__(16) float2 part[];            // [K/4]
@@ -77,10 +80,10 @@ __global__ void __launch_bounds__(256) k_build_tabs(const void* src, int bf16, u
     float2* g = gs + v * (K / 64);
     if (bf16) {
         const uint16_t* xv = static_cast<const uint16_t*>(src) + v * K;
-        build_btab<true>([&](int i) { return bf16_bits_to_f32(xv[i]); }, int(K), t, g, part, lo_flag);
+        build_btab<LAYOUT>([&](int i) { return bf16_bits_to_f32(xv[i]); }, int(K), t, g, part, lo_flag);
     } else {
         const float* xv = static_cast<const float*>(src) + v * K;
-        build_btab<true>([&](int i) { return xv[i]; }, int(K), t, g, part, lo_flag);
+        build_btab<LAYOUT>([&](int i) { return xv[i]; }, int(K), t, g, part, lo_flag);
     }
 }
 
@@ -339,6 +342,258 @@ __global__ void __launch_bounds__(256, 2) k_ffn_grouped(GroupedArgs a) {
     };
     if (MATS == 2 && hi_only) body(std::integral_constant<int, 16>{});     // down inputs are fp32
     else body(std::integral_constant<int, 8>{});
+}
+
+// ------------------------------------------------------------------------
+// tcgen05 down projection of the grouped path. CTA = (128 rows of W_down,
+// expert), 256 threads: thread (r, h) = (tid & 127, tid >> 7) serves weight
+// row r, which is tensor-memory lane r (warps w and w + 4 share lanes
+// 32 (w % 4)..). The expert's slots are taken 32 at a time (a pass); per
+// pass the K = d_ff dimension runs in slabs of one 64-column group:
+//   each thread cp.asyncs 16 bytes of its row's codes 4 slabs ahead and
+//     dequantises them into A (fp16 q or 16 q, exact) in the no-swizzle
+//     K-major core-matrix layout; the B rows (slot t: rows 2t and 2t+1 =
+//     hi and lo half of its scaled hidden vector, from the table k_build_tabs
+//     wrote in the same column order) come from registers loaded two slabs
+//     ahead;
+//   one thread issues the 4 k-steps of D[slab] = A B^T (M 128, N = 2 x
+//     slots rounded up to 16) into one of two tensor-memory column buffers
+//     and commits them to that buffer's mbarrier;
+//   meanwhile every thread reads the previous slab's D for its row and its
+//     8-slot blocks (h = block parity) and adds the group epilogue
+//     (group_epilogue's arithmetic) to its accumulators: the MMAs of one slab
+//     overlap the epilogue of the last and the dequantisation of the next.
+// The hidden vectors are fp32, so two B rows per slot keep the products
+// exact (the gate/up kernel above takes its bf16 x as one fp16 row).
+constexpr int kTcPass = 32;        // slots per pass
+constexpr int kTcNib = 5;          // code stages (prefetch depth 4)
+struct TcSmem {
+    static constexpr int A = 16384, B = 8192, NIB = 4096;
+    __host__ __device__ static size_t scales(int G) { return size_t(2) * G * 128 * 2; }
+    __host__ __device__ static size_t bytes(int G) {
+        return 2 * A + 2 * B + kTcNib * NIB + scales(G) + (3 + 1 + 1 + 1) * kTcPass * 4 + 64;
+    }
+};
+
+SMOE_DEVINL void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(smem_u32(dst)), "l"(src) : "memory");
+}
+SMOE_DEVINL void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+SMOE_DEVINL void cp_async_wait() { asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory"); }
+
+template <int FMT>
+__global__ void __launch_bounds__(256, 2) k_ffn_down_tc(GroupedArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const uint32_t e = blockIdx.y, T = a.count[e];
+    if (T == 0) return;
+    const int K = int(a.d_ff), R = int(a.d_model), G = K / 64;
+    const int tid = threadIdx.x, warp = tid >> 5, row = tid & 127, hh = tid >> 7;
+    uint8_t* sA = smem;                                                  // [2][128 rows x 64 cols fp16]
+    uint8_t* sB = sA + 2 * TcSmem::A;                                    // [2][64 rows x 64 cols fp16]
+    uint8_t* sN = sB + 2 * TcSmem::B;                                    // [kTcNib][2][128][16 B]
+    uint16_t* sS = reinterpret_cast<uint16_t*>(sN + kTcNib * TcSmem::NIB);   // [2][G][128]
+    float* gsm = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(sS) + TcSmem::scales(G));   // [3][32]
+    float* sinv = gsm + 3 * kTcPass;                                     // [32]
+    uint32_t* sslot = reinterpret_cast<uint32_t*>(sinv + kTcPass);      // [32]
+    uint32_t* svec = sslot + kTcPass;                                    // [32]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(svec + kTcPass);       // [2]
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2);
+    uint32_t* sfail = tslot + 1;
+
+    // this thread's weight row (matrix 2 = down)
+    const int mrow = blockIdx.x * 128 + row;
+    const uint8_t* eb = a.base + uint64_t(e) * a.stride;
+    const uint8_t* nsrc = eb + a.off[6] + size_t(mrow) * (K / 2) + hh * 16;
+
+    if (tid == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        *sfail = 0u;
+        fence_mbar_init();
+    }
+    if (warp == 0) tmem_alloc(tslot, 128);
+    // code prefetch: one commit group per slab; slabs run over the groups
+    // of every pass in order
+    const int npass = int((T + kTcPass - 1) / kTcPass);
+    uint8_t* nst = sN + hh * 2048 + row * 16;                            // this thread's 16 B of a stage
+    int is_stage = 0, is_g = 0, is_left = npass * G, rd_stage = 0;
+    auto nib_issue = [&]() {
+        if (is_left > 0) cp_async16(nst + is_stage * TcSmem::NIB, nsrc + is_g * 32);
+        cp_async_commit();
+        is_stage = is_stage + 1 == kTcNib ? 0 : is_stage + 1;
+        is_g = is_g + 1 == G ? 0 : is_g + 1;
+        --is_left;
+    };
+#pragma unroll
+    for (int i = 0; i < kTcNib - 1; ++i) nib_issue();
+    {
+        const uint16_t* sc = reinterpret_cast<const uint16_t*>(eb + a.off[7 + hh]) + size_t(mrow) * G;
+        if (hh == 0 || FMT == kFmtAffine)
+            for (int g = 0; g < G; ++g) sS[(hh * G + g) * 128 + row] = __ldg(sc + g);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t taddr = *tslot;
+    const uint32_t lane_base = taddr + (uint32_t((warp & 3) * 32) << 16);
+    const uint32_t* lst = a.list + size_t(e) * a.lcap;
+    // descriptors of k-step 0 of buffer 0 (the start address field is in
+    // the low bits: k-step ks adds 256 bytes >> 4)
+    const uint64_t adesc0 = tc_desc(smem_u32(sA), 128, 1024), bdesc0 = tc_desc(smem_u32(sB), 128, 1024);
+
+    // slab pipeline state (identical in every thread): buffer of the slab
+    // being prepared (cb, its group-sum buffer c3) and of the previous one
+    // (pb, p3), and each MMA buffer's next mbarrier parity
+    int cb = 0, c3 = 0, pb = 0, p3 = 0;
+    uint32_t par0 = 0, par1 = 0;
+    // B rows: 64 rows (slot n / 2, half n & 1) x 8 chunks; thread -> row
+    // tid & 63, chunks (tid >> 6) and (tid >> 6) + 4
+    const int bn = tid & 63, bkc0 = tid >> 6, bt = bn >> 1, bpart = bn & 1;
+    uint8_t* bdst0 = sB + (bn >> 3) * 1024 + (bn & 7) * 16 + bkc0 * 128;
+    uint8_t* arow0 = sA + (row >> 3) * 1024 + hh * 512 + (row & 7) * 16;
+    for (int pass = 0; pass < npass; ++pass) {
+        const int p0 = pass * kTcPass, TP = min(int(T) - p0, kTcPass);
+        const int N = (2 * TP + 15) & ~15;
+        const uint32_t idesc = tc_idesc_f16(128, N);
+        if (tid < TP) {
+            const uint32_t slot = lst[p0 + tid], vec = slot / a.tab_div;
+            sslot[tid] = slot;
+            svec[tid] = vec;
+            sinv[tid] = __ldg(&a.gs[size_t(vec) * G].x);
+        }
+        __syncthreads();
+        const bool bvalid = bt < TP;
+        const uint4* btab = reinterpret_cast<const uint4*>(a.tab) + (bvalid ? size_t(svec[bt]) * G * 16 : 0) +
+                            bkc0 * 2 + bpart;
+        const float* gsrc = tid < TP ? &a.gs[size_t(svec[tid]) * G].y : nullptr;
+        uint4 bq0[2], bq1[2];                   // B chunks of groups g and g + 1
+        float gq0 = 0.f, gq1 = 0.f;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            bq0[j] = bvalid ? __ldg(btab + 8 * j) : make_uint4(0u, 0u, 0u, 0u);
+            bq1[j] = (bvalid && G > 1) ? __ldg(btab + 16 + 8 * j) : make_uint4(0u, 0u, 0u, 0u);
+        }
+        if (gsrc) {
+            gq0 = __ldg(gsrc);
+            if (G > 1) gq1 = __ldg(gsrc + 2);
+        }
+        float acc[2][8];                        // slots 8 (2 i + hh) + k
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+#pragma unroll
+            for (int k = 0; k < 8; ++k) acc[i][k] = 0.f;
+
+        for (int g = 0; g <= G; ++g) {
+            if (g < G) {
+                // 1. this thread's 32 codes of the slab (and the next prefetch)
+                cp_async_wait<kTcNib - 2>();
+                const uint4 w = *reinterpret_cast<const uint4*>(nst + rd_stage * TcSmem::NIB);
+                rd_stage = rd_stage + 1 == kTcNib ? 0 : rd_stage + 1;
+                nib_issue();
+                // 2. dequantise: word i (8 codes) -> core-matrix row chunk 4 hh + i
+                {
+                    const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+                    const uint32_t M0 = 0x000F000Fu, M1 = 0x00F000F0u, OR = 0x64006400u;
+                    uint8_t* arow = arow0 + cb * TcSmem::A;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const uint32_t x = wv[i], x8 = x >> 8;
+                        uint4 o;
+                        o.x = hsub_1024(lop3_and_or(x, M0, OR));
+                        o.y = hsub_1024(lop3_and_or(x, M1, OR));
+                        o.z = hsub_1024(lop3_and_or(x8, M0, OR));
+                        o.w = hsub_1024(lop3_and_or(x8, M1, OR));
+                        *reinterpret_cast<uint4*>(arow + i * 128) = o;
+                    }
+                }
+                // 3. B rows of group g (rows of absent slots are zero), group sums
+                {
+                    uint8_t* bdst = bdst0 + cb * TcSmem::B;
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) *reinterpret_cast<uint4*>(bdst + j * 512) = bq0[j];
+                    if (tid < TP) gsm[c3 * kTcPass + tid] = gq0;
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) bq0[j] = bq1[j];
+                    gq0 = gq1;
+                    btab += 16;                             // now group g + 1
+                    if (g + 2 < G) {
+#pragma unroll
+                        for (int j = 0; j < 2; ++j) bq1[j] = bvalid ? __ldg(btab + 16 + 8 * j) : make_uint4(0u, 0u, 0u, 0u);
+                        if (gsrc) gq1 = __ldg(gsrc + 2 * (g + 2));
+                    }
+                }
+                fence_proxy_async();
+                tc_fence_before();
+                __syncthreads();
+                // 4. one thread issues the slab's MMAs
+                if (tid == 0) {
+                    tc_fence_after();
+                    const uint64_t ad = adesc0 + uint64_t(cb * (TcSmem::A >> 4)), bd = bdesc0 + uint64_t(cb * (TcSmem::B >> 4));
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks) tc_mma_f16(taddr + cb * 64, ad + ks * 16, bd + ks * 16, idesc, ks > 0);
+                    tc_commit(&bars[cb]);
+                }
+            }
+            // 5. epilogue of the previous slab (buffers pb, p3, group g - 1):
+            //    this row's dots for the thread's slot blocks 2 i + hh
+            if (g > 0) {
+                const int gv = g - 1;
+                const uint32_t par = pb ? par1 : par0;
+                if (!mbar_try_wait(&bars[pb], par)) {
+                    if (!*reinterpret_cast<volatile uint32_t*>(sfail) && !mbar_wait_slow(&bars[pb], par)) {
+                        *reinterpret_cast<volatile uint32_t*>(sfail) = 1u;
+                        atomicExch(a.err, SMOE_DEVERR_MBAR_TIMEOUT);
+                    }
+                }
+                if (pb) par1 ^= 1u; else par0 ^= 1u;
+                tc_fence_after();
+                const float* gs3 = gsm + p3 * kTcPass;
+                const float sv = FMT == kFmtAffine ? bf16_bits_to_f32(sS[gv * 128 + row])
+                                                   : f16_bits_to_f32(sS[gv * 128 + row]);
+                const float bv = bf16_bits_to_f32(sS[(G + gv) * 128 + row]);
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    const int t0 = (2 * i + hh) * 8;
+                    if (t0 < TP) {
+                        float d[16];
+                        tmem_ld16(lane_base + pb * 64 + t0 * 2, d);
+                        const float4 ga = *reinterpret_cast<const float4*>(gs3 + t0);
+                        const float4 gb = *reinterpret_cast<const float4*>(gs3 + t0 + 4);
+                        const float gsv[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) {
+                            const float dsum = d[2 * k] + d[2 * k + 1];
+                            if (FMT == kFmtAffine) acc[i][k] = fmaf(sv, dsum, fmaf(bv, gsv[k], acc[i][k]));
+                            else acc[i][k] = fmaf(sv, fmaf(dsum, 1.0f / 7.5f, -gsv[k]), acc[i][k]);
+                        }
+                    }
+                }
+                tc_fence_before();
+            }
+            if (g < G) {
+                pb = cb;
+                p3 = c3;
+                cb ^= 1;
+                c3 = c3 == 2 ? 0 : c3 + 1;
+            }
+        }
+        // output: this thread's slots 8 (2 i + hh) + k
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const int t = (2 * i + hh) * 8 + k;
+                if (t < TP) a.out[size_t(sslot[t]) * R + mrow] = acc[i][k] * sinv[t];
+            }
+        __syncthreads();                       // sslot / svec / sinv reused by the next pass
+    }
+    cp_async_wait<0>();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 0) tmem_dealloc(taddr, 128);
 }
 
 // y[t] = sum_j w[t*k+j] * ys[t*k+j] in rank order j (axpy_f32: product, then

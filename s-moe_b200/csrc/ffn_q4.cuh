@@ -96,11 +96,19 @@ SMOE_DEVINL float pow2_scale_for(float amax) {
     return ldexpf(1.0f, 14 - e);
 }
 
-// QUAD: the grouped path's layout - per (group, k-step, c) one 16-byte
-// entry {hi.x, hi.y, lo.x, lo.y}: the hi pair alone is the A-fragment pair of
-// one token in a 16-token MMA. lo_flag (QUAD only) gets a nonzero word if
+// Table layouts. kTabSlot: the per-slot kernels' [g][k-step][hi 4 c, lo 4 c]
+// uint2 entries. kTabMma: the grouped mma.sync kernel's - per (group,
+// k-step, c) one 16-byte entry {hi.x, hi.y, lo.x, lo.y}; the hi pair alone
+// is the A-fragment pair of one token in a 16-token MMA. kTabTc: the
+// tensor-core kernel's - per (group g, 8-column chunk kc) a hi and a lo
+// 16-byte row of fp16, [g][kc][hi, lo][8], each in the order in which one
+// 32-bit word of 4-bit codes dequantises (columns 0, 4, 1/16, 5/16, 2, 6,
+// 3/16, 7/16 of the chunk, the odd ones pre-divided by 16 as their codes
+// come out as 16 q): B-operand rows of a tcgen05 MMA against codes
+// dequantised that way. lo_flag (grouped layouts) gets a nonzero word if
 // any lo half of this vector is nonzero.
-template <bool QUAD = false, typename Load>
+constexpr int kTabSlot = 0, kTabMma = 1, kTabTc = 2;
+template <int LAYOUT = kTabSlot, typename Load>
 SMOE_DEVINL void build_btab(Load ld, int K, uint2* btab, float2* gsum, float2* part,
                             uint32_t* lo_flag = nullptr) {
     // max |v| over the vector (block reduction through `part`)
@@ -126,9 +134,17 @@ SMOE_DEVINL void build_btab(Load ld, int K, uint2* btab, float2* gsum, float2* p
         __half lo1 = __float2half_rn(o1 - __half2float(ho1));
         __half lo5 = __float2half_rn(o5 - __half2float(ho5));
         const int row = (grp * 4 + s) * 8;
-        if (QUAD) {
+        if (LAYOUT == kTabMma) {
             const uint32_t l0 = pack_half2(le0, le4), l1 = pack_half2(lo1, lo5);
             reinterpret_cast<uint4*>(btab)[row / 2 + c] = make_uint4(pack_half2(he0, he4), pack_half2(ho1, ho5), l0, l1);
+            if (lo_flag && ((l0 | l1) & 0x7fff7fffu)) atomicOr(lo_flag, 1u);
+        } else if (LAYOUT == kTabTc) {
+            // tuple (s, c) holds columns base + {0, 4, 1, 5}: 8 bytes of chunk
+            // kc = 2c + s/2, at byte 8 (s & 1)
+            const uint32_t l0 = pack_half2(le0, le4), l1 = pack_half2(lo1, lo5);
+            uint2* ch = btab + (size_t(grp * 8 + 2 * c + (s >> 1)) * 2) * 2 + (s & 1);
+            ch[0] = make_uint2(pack_half2(he0, he4), pack_half2(ho1, ho5));
+            ch[2] = make_uint2(l0, l1);
             if (lo_flag && ((l0 | l1) & 0x7fff7fffu)) atomicOr(lo_flag, 1u);
         } else {
             btab[row + c] = make_uint2(pack_half2(he0, he4), pack_half2(ho1, ho5));

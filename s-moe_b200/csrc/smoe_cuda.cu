@@ -169,13 +169,17 @@ int launch_grouped(SmoeCudaCtx* c, smoe::FfnArgs& a, int fmt, uint32_t E) {
         return SMOE_ERR_ARG;
     }
     const uint32_t d = a.d_model, dff = a.d_ff;
+    // gate/up: 32 rows x 2 matrices per CTA; down: 128 rows per CTA
+    constexpr int kRbGu = 32, kWnGu = 1;
+    if (dff % kRbGu || d % 128) { set_err("grouped FFN needs d_ff % 32 == 0 and d_model % 128 == 0 %s%ld", "", 0); return SMOE_ERR_ARG; }
     int rc;
     uint32_t* lo_flag = c->g_count + c->cfg.max_experts;
+    using namespace smoe;
     smoe::k_group_slots<<<E, 32, 0, c->stream>>>(a.ids, nslots, c->g_list, c->g_count, lcap, lo_flag);
-    if ((rc = prep_kernel(c, smoe::k_build_tabs, size_t(d / 4) * 8))) return rc;
-    if ((rc = prep_kernel(c, smoe::k_build_tabs, size_t(dff / 4) * 8))) return rc;
-    smoe::k_build_tabs<<<a.ntok, 256, size_t(d / 4) * 8, c->stream>>>(a.x, a.x_dtype == 1, d, c->g_xtab, c->g_xgs,
-                                                                 lo_flag);
+    if ((rc = prep_kernel(c, k_build_tabs<kTabMma>, size_t(d / 4) * 8))) return rc;
+    if ((rc = prep_kernel(c, k_build_tabs<kTabTc>, size_t(dff / 4) * 8))) return rc;
+    k_build_tabs<kTabMma><<<a.ntok, 256, size_t(d / 4) * 8, c->stream>>>(a.x, a.x_dtype == 1, d, c->g_xtab, c->g_xgs,
+                                                                        lo_flag);
     smoe::GroupedArgs g{};
     g.base = a.base;
     g.stride = a.stride;
@@ -189,32 +193,24 @@ int launch_grouped(SmoeCudaCtx* c, smoe::FfnArgs& a, int fmt, uint32_t E) {
     smoe::GroupedArgs g1 = g, g2 = g;
     g1.tab = c->g_xtab; g1.gs = c->g_xgs; g1.tab_div = a.k; g1.out = c->hidden; g1.lo_flag = lo_flag;
     g2.tab = c->g_htab; g2.gs = c->g_hgs; g2.tab_div = 1; g2.out = c->g_ys; g2.lo_flag = nullptr;
-    // gate/up: 32 rows x 2 matrices per CTA; down: 64 rows per CTA
-    constexpr int kRbGu = 32, kRbDn = 128;
-    if (dff % kRbGu || d % kRbDn) { set_err("grouped FFN needs d_ff % 32 == 0 and d_model % 128 == 0 %s%ld", "", 0); return SMOE_ERR_ARG; }
-    constexpr int kWnGu = 1, kWnDn = 2;
-    const size_t s1 = smoe::grouped_smem_bytes(d, 2, kRbGu, kWnGu), s2 = smoe::grouped_smem_bytes(dff, 1, kRbDn, kWnDn);
+    const size_t s1 = grouped_smem_bytes(d, 2, kRbGu, kWnGu), s2 = TcSmem::bytes(dff / 64);
     auto run = [&](auto k1, auto k2) -> int {
         int r;
-        if ((r = prep_kernel(c, k1, s1))) return r;
-        if ((r = prep_kernel(c, k2, s2))) return r;
+        if ((r = prep_kernel(c, k1, s1)) || (r = prep_kernel(c, k2, s2))) return r;
         k1<<<dim3(dff / kRbGu, E), 256, s1, c->stream>>>(g1);
-        smoe::k_build_tabs<<<nslots, 256, size_t(dff / 4) * 8, c->stream>>>(c->hidden, 0, dff, c->g_htab, c->g_hgs, nullptr);
-        k2<<<dim3(d / kRbDn, E), 256, s2, c->stream>>>(g2);
+        k_build_tabs<kTabTc><<<nslots, 256, size_t(dff / 4) * 8, c->stream>>>(c->hidden, 0, dff, c->g_htab, c->g_hgs,
+                                                                              nullptr);
+        k2<<<dim3(d / 128, E), 256, s2, c->stream>>>(g2);
         return SMOE_OK;
     };
-    // the 30B shape (d_model 2048, d_ff 768) runs with compile-time K
-    const bool k30b = d == 2048 && dff == 768;
+    // the 30B shape (d_model 2048) runs the gate/up kernel with compile-time K
+    const bool k30b = d == 2048;
     if (fmt == SMOE_FMT_AFFINE_Q4)
-        rc = k30b ? run(smoe::k_ffn_grouped<smoe::kFmtAffine, 2, kRbGu, kWnGu, 2048>,
-                        smoe::k_ffn_grouped<smoe::kFmtAffine, 1, kRbDn, kWnDn, 768>)
-                  : run(smoe::k_ffn_grouped<smoe::kFmtAffine, 2, kRbGu, kWnGu, 0>,
-                        smoe::k_ffn_grouped<smoe::kFmtAffine, 1, kRbDn, kWnDn, 0>);
+        rc = k30b ? run(k_ffn_grouped<kFmtAffine, 2, kRbGu, kWnGu, 2048>, k_ffn_down_tc<kFmtAffine>)
+                  : run(k_ffn_grouped<kFmtAffine, 2, kRbGu, kWnGu, 0>, k_ffn_down_tc<kFmtAffine>);
     else
-        rc = k30b ? run(smoe::k_ffn_grouped<smoe::kFmtSmoe, 2, kRbGu, kWnGu, 2048>,
-                        smoe::k_ffn_grouped<smoe::kFmtSmoe, 1, kRbDn, kWnDn, 768>)
-                  : run(smoe::k_ffn_grouped<smoe::kFmtSmoe, 2, kRbGu, kWnGu, 0>,
-                        smoe::k_ffn_grouped<smoe::kFmtSmoe, 1, kRbDn, kWnDn, 0>);
+        rc = k30b ? run(k_ffn_grouped<kFmtSmoe, 2, kRbGu, kWnGu, 2048>, k_ffn_down_tc<kFmtSmoe>)
+                  : run(k_ffn_grouped<kFmtSmoe, 2, kRbGu, kWnGu, 0>, k_ffn_down_tc<kFmtSmoe>);
     if (rc) return rc;
     smoe::k_combine_slots<<<dim3((d + 255) / 256, a.ntok), 256, 0, c->stream>>>(c->g_ys, a.wts, a.k, d, a.y,
                                                                                a.y_dtype);
