@@ -427,10 +427,21 @@ __global__ void __launch_bounds__(256, 2) k_ffn_down_tc(GroupedArgs a) {
     };
 #pragma unroll
     for (int i = 0; i < kTcNib - 1; ++i) nib_issue();
-    {
-        const uint16_t* sc = reinterpret_cast<const uint16_t*>(eb + a.off[7 + hh]) + size_t(mrow) * G;
-        if (hh == 0 || FMT == kFmtAffine)
-            for (int g = 0; g < G; ++g) sS[(hh * G + g) * 128 + row] = __ldg(sc + g);
+    // this row's scales (hh = 0) or biases (hh = 1): all loads first (G <= 64
+    // in 8-byte pieces), then the transposed shared-memory stores
+    if (hh == 0 || FMT == kFmtAffine) {
+        const uint2* sc = reinterpret_cast<const uint2*>(eb + a.off[7 + hh] + size_t(mrow) * G * 2);
+        uint2 v[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = j * 4 < G ? __ldg(sc + j) : make_uint2(0u, 0u);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            if (j * 4 < G) {
+                uint16_t* d = sS + (hh * G + j * 4) * 128 + row;
+                d[0] = uint16_t(v[j].x); d[128] = uint16_t(v[j].x >> 16);
+                d[256] = uint16_t(v[j].y); d[384] = uint16_t(v[j].y >> 16);
+            }
+        }
     }
     tc_fence_before();
     __syncthreads();

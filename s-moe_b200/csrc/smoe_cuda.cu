@@ -171,7 +171,7 @@ int launch_grouped(SmoeCudaCtx* c, smoe::FfnArgs& a, int fmt, uint32_t E) {
     const uint32_t d = a.d_model, dff = a.d_ff;
     // gate/up: 32 rows x 2 matrices per CTA; down: 128 rows per CTA
     constexpr int kRbGu = 32, kWnGu = 1;
-    if (dff % kRbGu || d % 128) { set_err("grouped FFN needs d_ff % 32 == 0 and d_model % 128 == 0 %s%ld", "", 0); return SMOE_ERR_ARG; }
+    if (dff % 256 || d % 128 || dff > 4096) { set_err("grouped FFN needs d_ff % 256 == 0, d_ff <= 4096 and d_model % 128 == 0 %s%ld", "", 0); return SMOE_ERR_ARG; }
     int rc;
     uint32_t* lo_flag = c->g_count + c->cfg.max_experts;
     using namespace smoe;
@@ -737,7 +737,8 @@ int smoe_cuda_moe_ffn(SmoeCudaCtx* c, const SmoeMoeLayer* L, const void* x, int 
             set_err("tiled layout needs batch <= 4 and a shape whose tiles fit shared memory %s%ld", "", (long)batch);
         return rc;
     }
-    if (batch > uint32_t(smoe::kFusedMaxTok))          // token batches: expert-grouped path
+    // token batches: expert-grouped path (shapes whose tiles it covers)
+    if (batch > uint32_t(smoe::kFusedMaxTok) && L->d_model % 128 == 0 && L->d_ff % 256 == 0 && L->d_ff <= 4096)
         return launch_grouped(c, a, fmt, L->n_experts);
     return launch_ffn(c, a, fmt);
 }
