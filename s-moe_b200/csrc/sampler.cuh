@@ -270,15 +270,38 @@ k_sample(SamplerArgs a) {
             tot[tid] = t;
         }
         __syncthreads();
-        if (tid == 0) {
-            uint32_t cum = 0;
-            int b = 255;
-            for (; b > 0; --b) {
-                if (cum + tot[b] >= krem) break;
-                cum += tot[b];
+        if (tid < 32) {
+            // the highest bin b >= 1 whose count from bin 255 down reaches krem,
+            // else bin 0; cum = count above b. Lane l scans bins 255 - 8l ..
+            // 248 - 8l; the lane holding the answer walks its 8 bins.
+            const int lane = tid;
+            uint32_t v[8], sl = 0;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                v[q] = tot[255 - 8 * lane - q];
+                sl += v[q];
             }
-            sel_krem = krem - cum;
-            sel_prefix = prefix | (uint32_t(b) << shift);
+            uint32_t incl = sl;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            const unsigned m = __ballot_sync(0xffffffffu, incl >= krem);
+            const int owner = m ? __ffs(m) - 1 : 31;
+            if (lane == owner) {
+                uint32_t cum = incl - sl;
+                int b = 0;
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const int bin = 255 - 8 * lane - q;
+                    if (bin == 0) break;
+                    if (cum + v[q] >= krem) { b = bin; break; }
+                    cum += v[q];
+                }
+                sel_krem = krem - cum;
+                sel_prefix = prefix | (uint32_t(b) << shift);
+            }
         }
         __syncthreads();
         krem = sel_krem;
