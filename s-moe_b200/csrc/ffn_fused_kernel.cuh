@@ -572,7 +572,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
             A.st->done = 0;
             if (epm) A.st->epoch = epoch;
         }
-        __threadfence();
+        // (no fence: the next launch reads these counters only after this
+        // grid has completed - stream order or griddepcontrol.wait)
     }
     trace_mark(A.trace, 7);
     SMOE_PROF(if (A.trace && tid == 0) A.trace[gridDim.x * 32 + blockIdx.x * 8 + 5] = clock64();)
