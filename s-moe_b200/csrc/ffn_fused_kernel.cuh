@@ -519,14 +519,16 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
     // ------------------------------------- last CTA: write y, clear scratch
     __syncthreads();
     if (tid == 0) {
-        __threadfence();
         trace_mark(A.trace, 14);
-        last_cta = (atomicAdd(&A.st->done, 1u) == gridDim.x - 1) ? 1u : 0u;
+        // acq_rel: releases this CTA's reductions (ordered before it by the
+        // barrier) and, in the last CTA, acquires every other CTA's
+        uint32_t old;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(&A.st->done) : "memory");
+        last_cta = (old == gridDim.x - 1) ? 1u : 0u;
         trace_mark(A.trace, 15);
     }
     __syncthreads();
     if (last_cta) {
-        __threadfence();
         const int n4 = g.ntok * d / 4;                               // d % 64 == 0: whole float4s
         float4* acc4 = reinterpret_cast<float4*>(A.acc);
         if (epm && ep.rank > 0) {
