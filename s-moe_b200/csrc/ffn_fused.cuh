@@ -175,10 +175,14 @@ SMOE_DEVINL bool spin_sys_until_geq(const uint32_t* p, uint32_t target) {
     return false;
 }
 
+// Bounded wait on a word other CTAs of this grid advance with release
+// atomics; the acquire load orders the caller's later reads after theirs.
 SMOE_DEVINL bool spin_until_geq(const uint32_t* p, uint32_t target) {
     for (uint32_t i = 0; i < SMOE_SPIN_LIMIT; ++i) {
-        if (ld_volatile_u32(p) >= target) return true;
-        if (i > 32) __nanosleep(i > 256 ? 256 : 64);
+        uint32_t v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+        if (v >= target) return true;
+        if (i > 32) __nanosleep(64);
     }
     return false;
 }

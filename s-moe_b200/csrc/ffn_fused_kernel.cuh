@@ -188,8 +188,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_moe_fused(FusedArgs A) {
                 float sum = 0.f;
                 for (int w = 0; w < kFusedConsumers; ++w) sum += red[w];
                 A.logits[r] = sum;
-                __threadfence();
-                atomicAdd(&A.st->rdone, 1u);
+                asm volatile("red.release.gpu.global.add.u32 [%0], 1;" :: "l"(&A.st->rdone) : "memory");
             }
             __syncthreads();
         }
