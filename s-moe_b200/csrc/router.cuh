@@ -56,6 +56,44 @@ SMOE_DEVINL float warp_row_dot_bf16(const uint16_t* row, const float* xs, int d,
     return acc;
 }
 
+// Two rows at once: both rows' loads are in flight together; each row's
+// accumulator sees exactly warp_row_dot_bf16's operation sequence.
+SMOE_DEVINL void warp_row_dot_bf16_x2(const uint16_t* row0, const uint16_t* row1, const float* xs, int d,
+                                      int lane, float& o0, float& o1) {
+    float acc[2] = {0.f, 0.f};
+    const uint4* rp[2] = {reinterpret_cast<const uint4*>(row0), reinterpret_cast<const uint4*>(row1)};
+    const int n = d / 8;
+    for (int c0 = lane; c0 < n; c0 += 32 * 8) {
+        uint4 v[2][8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+#pragma unroll
+            for (int m = 0; m < 2; ++m)
+                if (c0 + q * 32 < n) v[m][q] = __ldg(rp[m] + c0 + q * 32);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            if (c0 + q * 32 >= n) break;
+            const float* xv = xs + (c0 + q * 32) * 8;
+#pragma unroll
+            for (int m = 0; m < 2; ++m) {
+                const uint32_t u[4] = {v[m][q].x, v[m][q].y, v[m][q].z, v[m][q].w};
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    acc[m] = fmaf(__uint_as_float(u[r] << 16), xv[2 * r], acc[m]);
+                    acc[m] = fmaf(__uint_as_float(u[r] & 0xffff0000u), xv[2 * r + 1], acc[m]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], o);
+        acc[1] += __shfl_xor_sync(0xffffffffu, acc[1], o);
+    }
+    o0 = acc[0];
+    o1 = acc[1];
+}
+
 template <typename T>
 SMOE_DEVINL void stage_vec(const void* src, int x_dtype, size_t off, int d, float* xs) {
     if (x_dtype == 0) {
@@ -170,7 +208,16 @@ __global__ void __launch_bounds__(512) k_router_tok(RouterArgs a) {
     stage_vec<float>(a.x, a.x_dtype, size_t(tok) * a.d, a.d, xs);
     __syncthreads();
     float* lg = a.logits + size_t(tok) * a.E;
-    for (int e = warp; e < int(a.E); e += 16) {
+    int e = warp;
+    for (; e + 16 < int(a.E); e += 32) {             // rows e and e + 16 together
+        float v0, v1;
+        warp_row_dot_bf16_x2(a.w + size_t(e) * a.d, a.w + size_t(e + 16) * a.d, xs, a.d, lane, v0, v1);
+        if (lane == 0) {
+            lg[e] = v0;
+            lg[e + 16] = v1;
+        }
+    }
+    if (e < int(a.E)) {
         const float v = warp_row_dot_bf16(a.w + size_t(e) * a.d, xs, a.d, lane);
         if (lane == 0) lg[e] = v;
     }
