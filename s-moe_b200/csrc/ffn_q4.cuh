@@ -111,9 +111,31 @@ constexpr int kTabSlot = 0, kTabMma = 1, kTabTc = 2;
 template <int LAYOUT = kTabSlot, typename Load>
 SMOE_DEVINL void build_btab(Load ld, int K, uint2* btab, float2* gsum, float2* part,
                             uint32_t* lo_flag = nullptr) {
-    // max |v| over the vector (block reduction through `part`)
+    // Tuple t (4 columns: base + {0, 4, 1, 5}) of a 64-group; the tuples
+    // cover every column once. Up to kCache tuples per thread are read once
+    // and kept in registers for both passes (max, then the split).
+    const int ntup = K / 4;
+    auto tbase = [](int t) {
+        const int grp = t >> 4, r = t & 15, s = r >> 2, c = r & 3;
+        return grp * 64 + c * 16 + (s >> 1) * 8 + (s & 1) * 2;
+    };
+    constexpr int kCache = 4;
+    const bool cached = ntup <= kCache * int(blockDim.x);
+    float cv[kCache][4];
     float amax = 0.0f;
-    for (int i = threadIdx.x; i < K; i += blockDim.x) amax = fmaxf(amax, fabsf(ld(i)));
+    if (cached) {
+#pragma unroll
+        for (int j = 0; j < kCache; ++j) {
+            const int t = threadIdx.x + j * blockDim.x;
+            if (t < ntup) {
+                const int base = tbase(t);
+                cv[j][0] = ld(base); cv[j][1] = ld(base + 4); cv[j][2] = ld(base + 1); cv[j][3] = ld(base + 5);
+                amax = fmaxf(amax, fmaxf(fmaxf(fabsf(cv[j][0]), fabsf(cv[j][1])), fmaxf(fabsf(cv[j][2]), fabsf(cv[j][3]))));
+            }
+        }
+    } else {
+        for (int i = threadIdx.x; i < K; i += blockDim.x) amax = fmaxf(amax, fabsf(ld(i)));
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5].x = amax;
@@ -121,12 +143,10 @@ SMOE_DEVINL void build_btab(Load ld, int K, uint2* btab, float2* gsum, float2* p
     for (int w = 0; w < (int)(blockDim.x >> 5); ++w) amax = fmaxf(amax, part[w].x);
     __syncthreads();
     const float sc = pow2_scale_for(amax), inv = 1.0f / sc;
-    const int ntup = K / 4;
-    for (int t = threadIdx.x; t < ntup; t += blockDim.x) {
+    auto emit = [&](int t, float v0, float v4, float v1, float v5) {
         const int grp = t >> 4, r = t & 15, s = r >> 2, c = r & 3;
-        const int base = grp * 64 + c * 16 + (s >> 1) * 8 + (s & 1) * 2;
-        float e0 = ld(base) * sc, e4 = ld(base + 4) * sc;
-        float o1 = ld(base + 1) * (sc * 0.0625f), o5 = ld(base + 5) * (sc * 0.0625f);
+        float e0 = v0 * sc, e4 = v4 * sc;
+        float o1 = v1 * (sc * 0.0625f), o5 = v5 * (sc * 0.0625f);
         __half he0 = __float2half_rn(e0), he4 = __float2half_rn(e4);
         __half le0 = __float2half_rn(e0 - __half2float(he0));
         __half le4 = __float2half_rn(e4 - __half2float(he4));
@@ -155,6 +175,18 @@ SMOE_DEVINL void build_btab(Load ld, int K, uint2* btab, float2* gsum, float2* p
         float x1 = 16.0f * (__half2float(ho1) + __half2float(lo1));
         float x5 = 16.0f * (__half2float(ho5) + __half2float(lo5));
         part[t] = make_float2(0.0f, (x0 + x4) + (x1 + x5));
+    };
+    if (cached) {
+#pragma unroll
+        for (int j = 0; j < kCache; ++j) {
+            const int t = threadIdx.x + j * blockDim.x;
+            if (t < ntup) emit(t, cv[j][0], cv[j][1], cv[j][2], cv[j][3]);
+        }
+    } else {
+        for (int t = threadIdx.x; t < ntup; t += blockDim.x) {
+            const int base = tbase(t);
+            emit(t, ld(base), ld(base + 4), ld(base + 1), ld(base + 5));
+        }
     }
     __syncthreads();
     for (int grp = threadIdx.x; grp < K / 64; grp += blockDim.x) {
