@@ -40,20 +40,27 @@ struct GroupedArgs {
 };
 
 // Per-expert slot lists: one CTA (one warp) per expert, ballot compaction
-// over the slots in order (deterministic); ids are read 16 per lane ahead of
-// the ballots so the scan is not a chain of dependent loads.
+// over the slots in order (deterministic); ids are read 16 per lane, one
+// 512-slot round ahead of the ballots, so the scan is not a chain of loads.
 // Also clears the lo flag that the following k_build_tabs of x sets.
 __global__ void k_group_slots(const uint32_t* ids, uint32_t nslots, uint32_t* list, uint32_t* count,
                               uint32_t lcap, uint32_t* lo_flag) {
     const uint32_t e = blockIdx.x, lane = threadIdx.x;
     if (e == 0 && lane == 0 && lo_flag) *lo_flag = 0u;
     uint32_t n = 0;
+    uint32_t nx[16];                                   // ids of the next round, loaded ahead
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+        const uint32_t s = q * 32 + lane;
+        nx[q] = s < nslots ? __ldg(ids + s) : 0xffffffffu;
+    }
     for (uint32_t b0 = 0; b0 < nslots; b0 += 32 * 16) {
         uint32_t v[16];
 #pragma unroll
         for (int q = 0; q < 16; ++q) {
-            const uint32_t s = b0 + q * 32 + lane;
-            v[q] = s < nslots ? __ldg(ids + s) : 0xffffffffu;
+            v[q] = nx[q];
+            const uint32_t s = b0 + 512 + q * 32 + lane;
+            nx[q] = s < nslots ? __ldg(ids + s) : 0xffffffffu;
         }
 #pragma unroll
         for (int q = 0; q < 16; ++q) {
