@@ -68,6 +68,10 @@ typedef struct {
     uint32_t max_batch;     /* tokens per call, 0 -> 256                    */
     uint32_t max_vocab;     /* sampler rows, 0 -> 262144                    */
     uint32_t timeout_ms;    /* host waits, 0 -> 10000                       */
+    uint32_t device_wait_us;/* limit of every wait inside the MoE-layer
+                               kernel (other CTAs, other GPUs, bulk copies),
+                               0 -> 1000000; a wait that runs out raises
+                               SMOE_ERR_DEVICE at the next synchronize     */
 } SmoeCudaInitArgs;
 
 /* Mirror of smoe_metal_init (metal_bridge.h:47): defaults, current device.
@@ -140,6 +144,19 @@ void smoe_cuda_wait_ffn_batch(SmoeCudaCtx* ctx, void* handle, float* out_mat,
 void smoe_cuda_scout_matvec_bf16(SmoeCudaCtx* ctx, const uint16_t* weight,
                                  const float* input_vec, float* output_vec,
                                  uint32_t rows, uint32_t cols);
+
+/* metal_bridge.h:199-206: `count` GEMVs outputs[i] = weights[i] . inputs[i]
+ * (rows[i] x cols[i] bf16, fp32 vectors, host or device), in order - a
+ * dispatch may read an earlier one's output. Synchronous. */
+void smoe_cuda_scout_matvec_batch_bf16(SmoeCudaCtx* ctx, const uint16_t** weights,
+                                       const float** inputs, float** outputs,
+                                       const uint32_t* rows, const uint32_t* cols, uint32_t count);
+
+/* metal_bridge.h:212-219: the same for dispatches with distinct outputs that
+ * no dispatch reads (no ordering needed between them). Synchronous. */
+void smoe_cuda_scout_matvec_group_bf16(SmoeCudaCtx* ctx, const uint16_t** weights,
+                                       const float** inputs, float** outputs,
+                                       const uint32_t* rows, const uint32_t* cols, uint32_t count);
 
 /* metal_bridge.h:221. Pins a host buffer (cudaHostRegister); device
  * pointers are accepted and ignored. */
@@ -247,6 +264,7 @@ int smoe_cuda_moe_layer_ep(SmoeCudaCtx* ctx, const SmoeMoeLayer* shard, uint32_t
  * scratch is one fixed array compiled into the library, which every GPU that
  * loads the library holds until the process exits. Limits: batch * k * d_ff
  * <= 65536 (256 KiB of hidden vectors); larger calls return SMOE_ERR_ARG.
+ * Vault layout only (layers with SMOE_LAYOUT_TILED set return SMOE_ERR_ARG).
  * The first call on each device looks up the array's device address, so make
  * that call before any stream capture. All calls share the array: calls that
  * overlap on the GPU (different streams, or different host threads) race.
@@ -255,6 +273,13 @@ int smoe_cuda_moe_ffn_noalloc(const SmoeMoeLayer* layer, const void* x, int x_dt
                               const uint32_t* ids, const float* weights, uint32_t k,
                               uint32_t batch, void* y, int y_dtype, void* stream);
 const char* smoe_cuda_noalloc_last_error(void);
+/* Companion status call of smoe_cuda_moe_ffn_noalloc, allocating nothing
+ * either: waits (bounded by timeout_ms, polling) until `stream` is idle, then
+ * reads and clears the library's device error word. SMOE_ERR_DEVICE when a
+ * call since the previous check raised it (an expert id >= layer->n_experts,
+ * whose slot then used expert 0's weights, or a bounded device wait that ran
+ * out), SMOE_ERR_TIMEOUT when the stream stayed busy. */
+int smoe_cuda_noalloc_check(void* stream, uint32_t timeout_ms);
 
 /* ------------------------------------------------------------- sampler */
 /* One row of sampler state (sampler.hpp:11-17 SamplerConfig + the draw). */

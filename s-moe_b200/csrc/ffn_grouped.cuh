@@ -44,7 +44,7 @@ struct GroupedArgs {
 // 512-slot round ahead of the ballots, so the scan is not a chain of loads.
 // Also clears the lo flag that the following k_build_tabs of x sets.
 __global__ void k_group_slots(const uint32_t* ids, uint32_t nslots, uint32_t* list, uint32_t* count,
-                              uint32_t lcap, uint32_t* lo_flag) {
+                              uint32_t lcap, uint32_t* lo_flag, uint32_t* err) {
     const uint32_t e = blockIdx.x, lane = threadIdx.x;
     if (e == 0 && lane == 0 && lo_flag) *lo_flag = 0u;
     uint32_t n = 0;
@@ -66,6 +66,8 @@ __global__ void k_group_slots(const uint32_t* ids, uint32_t nslots, uint32_t* li
         for (int q = 0; q < 16; ++q) {
             const uint32_t s = b0 + q * 32 + lane;
             const bool mine = v[q] == e;
+            if (e == 0 && s < nslots && v[q] >= gridDim.x)   // an id past the layer's experts: no list takes it
+                atomicCAS(err, 0u, uint32_t(SMOE_DEVERR_BAD_EXPERT));
             const uint32_t m = __ballot_sync(0xffffffffu, mine);
             const uint32_t pos = n + __popc(m & ((1u << lane) - 1u));
             if (mine && pos < lcap) list[size_t(e) * lcap + pos] = s;

@@ -49,6 +49,7 @@ struct FfnArgs {
     int             y_dtype;
     int             per_slot;              // 1 -> write each slot's y (mirror API)
     uint32_t        d_model, d_ff, k, ntok;
+    uint32_t        n_experts;             // table mode: ids >= n_experts are rejected
     uint32_t*       err;
 };
 
@@ -61,7 +62,12 @@ struct SlotW {
 SMOE_DEVINL SlotW slot_weights(const FfnArgs& a, uint32_t slot) {
     SlotW w;
     if (a.ids) {
-        const uint8_t* b = a.base + uint64_t(a.ids[slot]) * a.stride;
+        uint32_t e = a.ids[slot];
+        if (e >= a.n_experts) {           // never index past the arena: flag it, read expert 0
+            atomicCAS(a.err, 0u, uint32_t(SMOE_DEVERR_BAD_EXPERT));
+            e = 0;
+        }
+        const uint8_t* b = a.base + uint64_t(e) * a.stride;
 #pragma unroll
         for (int m = 0; m < 3; ++m) {
             w.nib[m] = b + a.off[3 * m];

@@ -1,0 +1,777 @@
+// moe_layer.cuh - the persistent MoE-layer kernel for decode batches of up
+// to kLMaxTok tokens (sm_100a), on the tiled expert layout (tiled.cuh).
+//
+// One launch, one CTA per SM:
+//   routing (optional; decode.cpp:280-303): router logit rows spread over
+//     the grid; every CTA then runs the softmax / top-k / renorm of
+//     router.cuh on all logits (identical results in every CTA);
+//   phase A - gate/up (kernels.metal:240-337): the A units (slot, 16 hidden
+//     rows) are split evenly over the CTAs; each yields
+//     h = silu(Wg.x) * (Wu.x) * w_slot for its 16 rows, stored to a global
+//     scratch record already in the bf16 hi/lo B-fragment order of the down
+//     MMA (64 B) plus the unit's sum of h (4 B);
+//   one grid-wide arrive/wait (every CTA is resident: one CTA per SM);
+//   phase B - down + combine (kernels.metal:340-365, decode.cpp:485-499):
+//     the B units (token, 16 output rows) are split evenly over the CTAs;
+//     each computes its 16 rows of y = sum_slots W_down . h over all of the
+//     token's slots and writes them - every output row has exactly one
+//     owner, so there are no atomics and the sums are in a fixed order
+//     (bitwise reproducible).
+// Every byte a CTA needs is streamed by one producer lane with 1-D bulk
+// copies (no multicast) into two rings of shared-memory stages - gate/up
+// chunks first, then the down tiles - so the down weights are already on
+// chip when the grid-wide wait ends. Sixteen consumer warps run the gate/up
+// dots as integer MMAs on the raw codes (arithmetic below) and the down
+// tiles as bf16 MMAs; warp 16 turns each unit's 16 warp partials into h.
+//
+// Gate/up arithmetic: integer tensor-core MMA m16n8k32 (u8 x s8 -> s32).
+// A 32-bit word of the fragments holds 8 codes; masking it with 0x0F0F0F0F
+// gives the even columns' codes q as u8, with 0xF0F0F0F0 the odd columns'
+// 16q - no shifts. The activation of each 64-group becomes fixed point
+// X = round(x * 2^(20-E)) (E = exponent of the group's largest |x|, so
+// |X| < 2^21) split into signed 8-bit digits X = p0 + 2^8 p1 + 2^16 p2. Two B
+// sets carry them: set 0 has (p0, p1) of token t in columns (2t, 2t+1), set
+// 1 has p2 in column 2t. Four MMAs per 16 x 64 group give the exact int32
+// sums, and per (row, group) sum w.x = scale * sum q x + bias * sum x
+// (AFFINE-Q4) or scale * (sum q x / 7.5 - sum x) (SMOE-Q4, the identity of
+// kernels.metal:136-143), sum x taken over the same fixed-point values. The
+// only roundings are the fixed-point step of x and the fp32 epilogue.
+// Down arithmetic: the codes are ORed into the mantissa of bf16 128.0 (the
+// exact operand 128+q) against h split into bf16 hi + lo columns, fp32
+// accumulate; per 16-column k-step scale * (D - 128 sum h) + bias * sum h.
+//
+// Expert parallel (world > 1, one process per GPU, experts [r*E/G,
+// (r+1)*E/G) on rank r): every rank routes (the same ids), runs the A units
+// of the slots whose expert it holds, and the B units of every token over its
+// local slots; ranks > 0 store their partial rows into rank 0's window with
+// peer stores and count them per B unit with system-scope atomics; rank 0's
+// owner of that B unit waits for the count (bounded), adds the partials in
+// rank order and writes y. x is published by rank 0 (release flag) and read
+// by the others with peer loads. No TMA or bulk copy touches peer memory.
+//
+// Every wait is bounded by a %globaltimer deadline (LayerArgs.wait_ns after
+// the kernel starts); a wait that runs out sets the error word and the
+// kernel carries on to its end, so the host sees SMOE_ERR_DEVICE and the
+// context stays usable.
+#pragma once
+#include "ffn_q4.cuh"
+#include "router.cuh"
+#include "tiled.cuh"
+
+namespace smoe {
+
+constexpr int kLCons = 16;                    // consumer warps
+constexpr int kLCThreads = kLCons * 32;
+constexpr int kLHWarp = kLCons;               // h warp (also runs the top-k)
+constexpr int kLProdWarp = kLCons + 1;        // producer warp (lane 0 issues the copies)
+constexpr int kLThreads = kLCThreads + 64;
+constexpr int kLMaxTok = 4;
+constexpr int kLMaxK = 16;
+constexpr int kLMaxNA = 4;                    // gate/up ring stages (at most)
+constexpr int kLMaxNB = 16;                   // down ring stages (at most)
+constexpr int kHRec = 80;                     // bytes per h record: 8 x uint2 fragment + sum + pad
+constexpr int kEpMaxWorld = 8;
+
+struct LayerState {          // device scratch, zero at context creation and after every launch
+    uint32_t rdone;                 // router logit rows finished
+    uint32_t arrive;                // CTAs past phase A
+    uint32_t done;                  // CTAs finished
+    uint32_t epoch;                 // expert-parallel launches completed (advanced by the last CTA)
+    uint32_t pad[4];
+};
+
+SMOE_DEVINL void cons_sync() {
+    asm volatile("bar.sync 1, %0;" :: "n"(kLCThreads) : "memory");
+}
+
+// Geometry of one launch, shared by host (shared-memory sizing) and device.
+struct LayerGeom {
+    int d, dff, k, ntok;
+    TiledGeom tg;
+    int G, tilesU, outTiles, NA, NB;
+    int o_xtab, o_xg, o_red, o_red2, o_bar, o_ids, o_w, o_loc, o_ringA, o_ringB, total;
+
+    __host__ __device__ bool init(int fmt, int d_, int dff_, int k_, int ntok_, int max_smem) {
+        d = d_; dff = dff_; k = k_; ntok = ntok_;
+        if (!tg.init(fmt, d, dff) || tg.Gc > 32 || ntok < 1 || ntok > kLMaxTok || k < 1 || k > kLMaxK) return false;
+        G = d / 64; tilesU = dff / 16; outTiles = d / 16;
+        int off = 0;
+        auto take = [&](int bytes) { int o = off; off += (bytes + 127) & ~127; return o; };
+        const int xt = G * 1024, hr = k * tilesU * kHRec;    // x table, then (phase B) one token's h records
+        o_xtab = take(xt > hr ? xt : hr);
+        o_xg = take(G * 4 * 8);
+        const int rs = 2 * kLCons * 32 * 4, ps = 4 * kLMaxTok * kRouterMaxE;
+        o_red = take(rs);                                    // double-buffered unit partials / router partials
+        o_red2 = take(kLCons * 16 * 4);
+        o_bar = take((2 * kLMaxNA + 2 * kLMaxNB + 5) * 8);
+        o_ids = take(kLMaxTok * kLMaxK * 4);
+        o_w = take(kLMaxTok * kLMaxK * 4);
+        o_loc = take(4 * (kLMaxTok * kLMaxK + kLMaxTok + 2));  // local slots, token starts, count
+        (void)ps;
+        off = (off + 1023) & ~1023;
+        const int fixed = off;
+        const int avail = max_smem - fixed;
+        const int ca = int((tg.chunk + 127) & ~127u), cb = int((tg.btile + 127) & ~127u);
+        NA = 3;
+        if (avail < 3 * ca + 2 * cb) NA = 2;
+        if (NA > kLMaxNA) NA = kLMaxNA;
+        NB = (avail - NA * ca) / cb;
+        if (NB > kLMaxNB) NB = kLMaxNB;
+        if (NB < 2) return false;
+        o_ringA = fixed;
+        o_ringB = fixed + NA * ca;
+        total = o_ringB + NB * cb;
+        return total <= max_smem;
+    }
+    __host__ __device__ int stageA() const { return int((tg.chunk + 127) & ~127u); }
+    __host__ __device__ int stageB() const { return int((tg.btile + 127) & ~127u); }
+};
+
+struct LayerEp {
+    int world, rank;
+    uint32_t base, nlocal;     // global id of this rank's first expert, experts held
+    uint8_t* x0;               // rank 0's copy of x (peer memory on ranks > 0)
+    uint32_t* flag0;           // rank 0's x epoch
+    float* part0;              // [world][kLMaxTok * d] partial rows, in rank 0's window
+    uint32_t* cnt0;            // [kLMaxTok * d/16] partial B units arrived, in rank 0's window
+    uint32_t part_stride;      // floats per rank in part0
+};
+
+struct LayerArgs {
+    const uint8_t* base;       // tiled experts held here: expert (id - ep.base) at base + i * stride
+    uint64_t stride;
+    const void* x;             // [ntok x d]
+    int x_dtype;
+    void* y;                   // [ntok x d] (rank 0)
+    int y_dtype;
+    const uint32_t* ids_in;    // routing given: [ntok x k] (null when rw)
+    const float* wts_in;
+    uint32_t* ids_out;         // routing computed: written by CTA 0 (may be null)
+    float* wts_out;
+    uint32_t n_experts;        // router rows = id bound
+    const uint16_t* rw;        // router W [E x d] bf16, null: routing given
+    int norm;
+    float* logits;             // scratch [ntok x E]
+    uint8_t* hbuf;             // scratch h records [ntok*k][d_ff/16][kHRec]
+    LayerState* st;
+    uint32_t* err;
+    uint64_t wait_ns;          // limit of every wait
+    unsigned long long* trace; // optional [grid x 32] phase timestamps (ns)
+    LayerGeom g;
+    LayerEp ep;
+};
+
+SMOE_DEVINL void ltrace(unsigned long long* tr, int i, bool who = threadIdx.x == 0) {
+    if (tr && who && i < 32) tr[blockIdx.x * 32 + i] = gtimer();
+}
+
+SMOE_DEVINL uint32_t ld_acq_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+SMOE_DEVINL uint32_t ld_acq_gpu(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+SMOE_DEVINL void st_rel_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
+}
+SMOE_DEVINL void red_rel_gpu(uint32_t* p, uint32_t v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
+}
+// Bounded waits for a counter that other CTAs (gpu scope) or other GPUs
+// (sys scope) advance with release operations; false when the deadline passes.
+template <bool kSys>
+SMOE_DEVINL bool spin_geq(const uint32_t* p, uint32_t target, uint64_t deadline) {
+    for (uint32_t i = 0; i < SMOE_SPIN_LIMIT; ++i) {
+        if ((kSys ? ld_acq_sys(p) : ld_acq_gpu(p)) >= target) return true;
+        if ((i & 7) == 7 && gtimer() > deadline) return false;
+        if (i > 16) __nanosleep(i > 256 ? 256 : 32);
+    }
+    return false;
+}
+
+SMOE_DEVINL void raise_err(uint32_t* err, uint32_t code) { atomicCAS(err, 0u, code); }
+
+// Phase R: one logit row (token t, expert e) by all consumer warps; returns
+// this warp's partial sum (reduced across warps by the caller).
+SMOE_DEVINL float router_row_part(const LayerArgs& A, const void* xsrc, uint32_t t, uint32_t e, int ctid) {
+    const int d = A.g.d;
+    float acc = 0.f;
+    const uint4* wp = reinterpret_cast<const uint4*>(A.rw + size_t(e) * d);
+    for (int c = ctid; c < d / 8; c += kLCThreads) {
+        const uint4 v = __ldg(wp + c);
+        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+        float xv[8];
+        if (A.x_dtype == 0) {
+            const float4* xp = reinterpret_cast<const float4*>(static_cast<const float*>(xsrc) + size_t(t) * d + c * 8);
+            const float4 a0 = xp[0], a1 = xp[1];
+            xv[0] = a0.x; xv[1] = a0.y; xv[2] = a0.z; xv[3] = a0.w;
+            xv[4] = a1.x; xv[5] = a1.y; xv[6] = a1.z; xv[7] = a1.w;
+        } else {
+            const uint4 b = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(xsrc) + size_t(t) * d + c * 8);
+            const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                xv[2 * q] = __uint_as_float(bw[q] << 16);
+                xv[2 * q + 1] = __uint_as_float(bw[q] & 0xffff0000u);
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            acc = fmaf(__uint_as_float(u[q] << 16), xv[2 * q], acc);
+            acc = fmaf(__uint_as_float(u[q] & 0xffff0000u), xv[2 * q + 1], acc);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    return acc;
+}
+
+// x table of the gate/up MMAs, read straight from global x (ntok x K):
+// xtab[(grp*2 + set)*32 + lane] = the four B registers {b(even, k 0-15),
+// b(even, k 16-31), b(odd, k 0-15), b(odd, k 16-31)} of lane 4g + c, and
+// xg[grp*4 + t] = (2^(E-24) (/7.5 for SMOE-Q4), sum of the fixed-point x).
+// Columns of absent tokens stay 0. All consumer threads.
+template <int FMT>
+SMOE_DEVINL void build_xtab(const void* xsrc, int x_dtype, int ntok, int K, uint4* xtab, float2* xg, int ctid) {
+    const int G = K / 64;
+    for (int i = ctid; i < G * 64; i += kLCThreads) xtab[i] = make_uint4(0u, 0u, 0u, 0u);
+    const int warp = ctid >> 5, lane = ctid & 31;
+    constexpr int U = 4;
+    float v[U][2];
+    // first round of loads before the barrier that orders the zeroing
+    auto load = [&](int p0) {
+#pragma unroll
+        for (int q = 0; q < U; ++q) {
+            const int p = p0 + q * kLCons;
+            v[q][0] = v[q][1] = 0.f;
+            if (p < ntok * G) {
+                const int t = p / G, grp = p - t * G;
+                const size_t base = size_t(t) * K + grp * 64;
+                if (x_dtype == 0) {
+                    const float* s = static_cast<const float*>(xsrc) + base;
+                    v[q][0] = s[lane];
+                    v[q][1] = s[lane + 32];
+                } else {
+                    const uint16_t* s = static_cast<const uint16_t*>(xsrc) + base;
+                    v[q][0] = bf16_bits_to_f32(s[lane]);
+                    v[q][1] = bf16_bits_to_f32(s[lane + 32]);
+                }
+            }
+        }
+    };
+    load(warp);
+    cons_sync();
+    uint8_t* tb = reinterpret_cast<uint8_t*>(xtab);
+    for (int p0 = warp; p0 < ntok * G; p0 += U * kLCons) {
+        if (p0 != warp) load(p0);
+#pragma unroll
+        for (int q = 0; q < U; ++q) {
+            const int p = p0 + q * kLCons;
+            if (p >= ntok * G) break;
+            const int t = p / G, grp = p - t * G;
+            const float v0 = v[q][0], v1 = v[q][1];
+            float m = fmaxf(fabsf(v0), fabsf(v1));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            const int E = m > 0.f ? int((__float_as_uint(m) >> 23) & 0xff) - 127 : 0;
+            const int X0 = __float2int_rn(ldexpf(v0, 20 - E)), X1 = __float2int_rn(ldexpf(v1, 20 - E));
+            int xs_i = X0 + X1;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) xs_i += __shfl_xor_sync(0xffffffffu, xs_i, o);
+            if (lane == 0) {
+                const float xs = ldexpf(1.0f, E - 24);
+                xg[grp * 4 + t] = make_float2(FMT == kFmtAffine ? xs : xs * (1.0f / 7.5f), ldexpf(float(xs_i), E - 20));
+            }
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int j = lane + 32 * h;                        // column within the group
+                const int X = h ? X1 : X0;
+                const int p0d = ((X + 128) & 255) - 128, r = (X - p0d) >> 8;
+                const int p1 = ((r + 128) & 255) - 128, p2 = (r - p1) >> 8;
+                const int odd = j & 1, kk = j >> 1;                 // MMA (even/odd columns), k slot
+                const int c = (kk >> 2) & 3, reg = odd * 2 + (kk >> 4), byte = kk & 3;
+                uint8_t* e = tb + (size_t(grp) * 64 + (2 * t) * 4 + c) * 16 + reg * 4 + byte;
+                e[0] = uint8_t(p0d);                                // set 0, column 2t   (lane 8t + c)
+                e[4 * 16] = uint8_t(p1);                            // set 0, column 2t+1 (lane 8t + 4 + c)
+                e[32 * 16] = uint8_t(p2);                           // set 1, column 2t
+            }
+        }
+    }
+}
+
+// GW: 64-groups of a gate/up chunk per consumer warp, ceil(Gc / 16)
+template <int FMT, int GW>
+__global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
+    extern __shared__ __align__(1024) uint8_t sm[];
+    const LayerGeom& g = A.g;
+    const TiledGeom& tg = g.tg;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const bool consumer = warp < kLCons;
+    uint4* xtab = reinterpret_cast<uint4*>(sm + g.o_xtab);
+    float2* xg = reinterpret_cast<float2*>(sm + g.o_xg);
+    float* red = reinterpret_cast<float*>(sm + g.o_red);          // [2][16 warps][32]
+    float* red2 = reinterpret_cast<float*>(sm + g.o_red2);        // [16 warps][16]
+    uint64_t* fullA = reinterpret_cast<uint64_t*>(sm + g.o_bar);
+    uint64_t* emptyA = fullA + kLMaxNA;
+    uint64_t* fullB = emptyA + kLMaxNA;
+    uint64_t* emptyB = fullB + kLMaxNB;
+    uint64_t* redF = emptyB + kLMaxNB;                            // [2] unit partials written (16 arrivals)
+    uint64_t* redE = redF + 2;                                    // [2] unit partials consumed (1 arrival)
+    uint64_t* routed = redE + 2;                                  // s_ids / s_w / s_loc ready (1 arrival)
+    uint32_t* s_ids = reinterpret_cast<uint32_t*>(sm + g.o_ids);
+    float* s_w = reinterpret_cast<float*>(sm + g.o_w);
+    uint32_t* s_loc = reinterpret_cast<uint32_t*>(sm + g.o_loc);  // local slots in slot order
+    uint32_t* s_tok = s_loc + kLMaxTok * kLMaxK;                  // [ntok + 1] first local slot index per token
+    uint32_t* s_nloc = s_tok + kLMaxTok + 1;
+    uint8_t* ringA = sm + g.o_ringA;
+    uint8_t* ringB = sm + g.o_ringB;
+    const int NA = g.NA, NB = g.NB, k = g.k, d = g.d;
+    const uint32_t nslots = uint32_t(g.ntok * k);
+    const int cta = blockIdx.x, ncta = gridDim.x;
+    __shared__ uint32_t last_cta;
+
+    ltrace(A.trace, 0);
+    // inputs (x, routing) may come from the previous kernel in the stream
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const uint64_t deadline = gtimer() + A.wait_ns;
+    const LayerEp& ep = A.ep;
+    const bool epm = ep.world > 1;
+    const uint32_t epoch = epm ? A.st->epoch + 1u : 0u;           // written by the previous launch only
+    // x: the caller's, or on ranks > 0 rank 0's published copy (peer memory)
+    const void* xsrc = A.x;
+    if (epm) {
+        const size_t xbytes = size_t(g.ntok) * d * (A.x_dtype == 0 ? 4 : 2);
+        if (ep.rank == 0 && cta == 0) {
+            for (size_t i = tid; i < xbytes / 16; i += blockDim.x)
+                reinterpret_cast<uint4*>(ep.x0)[i] = reinterpret_cast<const uint4*>(A.x)[i];
+        } else if (ep.rank > 0) {
+            if (tid == 0 && !spin_geq<true>(ep.flag0, epoch, deadline)) raise_err(A.err, SMOE_DEVERR_SPIN_TIMEOUT);
+            xsrc = ep.x0;
+        }
+    }
+    if (tid == 0) {
+        for (int i = 0; i < kLMaxNA; ++i) {
+            mbar_init(fullA + i, 1);
+            mbar_init(emptyA + i, kLCons);
+        }
+        for (int i = 0; i < kLMaxNB; ++i) {
+            mbar_init(fullB + i, 1);
+            mbar_init(emptyB + i, kLCons);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(redF + b, kLCons);
+            mbar_init(redE + b, 1);
+        }
+        mbar_init(routed, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();              // (ranks > 0: rank 0's x is published; rank 0 CTA 0: x0 is written)
+    if (epm && ep.rank == 0 && cta == 0 && tid == 0) {
+        __threadfence_system();
+        st_rel_sys(ep.flag0, epoch);
+    }
+
+    // The CTA's share of the A units [a0, a1) and the B units [b0, b1), known
+    // once the routing (and so the local slot list) is.
+    auto a_range = [&](int& a0, int& a1) {
+        const int nA = int(*s_nloc) * g.tilesU;
+        a0 = int(int64_t(cta) * nA / ncta);
+        a1 = int(int64_t(cta + 1) * nA / ncta);
+    };
+    const int nB = g.ntok * g.outTiles;
+    const int b0 = int(int64_t(cta) * nB / ncta), b1 = int(int64_t(cta + 1) * nB / ncta);
+    // expert blob of a slot (its id is local: the slot is in s_loc)
+    auto expert_of = [&](uint32_t slot) { return A.base + uint64_t(s_ids[slot] - ep.base) * A.stride; };
+    // local slot list and per-token starts (one warp, after s_ids is final)
+    auto finish_routing = [&]() {
+        uint32_t cnt = 0;
+        for (uint32_t s0 = 0; s0 < nslots; s0 += 32) {
+            const uint32_t sl = s0 + lane;
+            bool loc = false;
+            if (sl < nslots) {
+                const uint32_t id = s_ids[sl];
+                loc = id < A.n_experts && id - ep.base < ep.nlocal;
+            }
+            const uint32_t m = __ballot_sync(0xffffffffu, loc);
+            if (loc) s_loc[cnt + __popc(m & ((1u << lane) - 1u))] = sl;
+            cnt += __popc(m);
+        }
+        __syncwarp();
+        if (lane <= g.ntok) {                      // first local index whose slot belongs to token >= lane
+            uint32_t f = 0;
+            while (f < cnt && s_loc[f] < uint32_t(lane * k)) ++f;
+            s_tok[lane] = f;
+        }
+        if (lane == 0) *s_nloc = cnt;
+        __syncwarp();
+    };
+    // producer lane: issue every copy of the CTA, gate/up chunks first
+    auto produce = [&]() {
+        int a0, a1;
+        a_range(a0, a1);
+        const int nAi = (a1 - a0) * int(tg.nchunk);
+        int nBi = 0;
+        for (int b = b0; b < b1; ++b) {
+            const int t = b / g.outTiles;
+            nBi += int(s_tok[t + 1] - s_tok[t]);
+        }
+        int iA = 0, iB = 0, bb = b0, jj = 0;
+        auto issueA = [&]() {
+            const int st = iA % NA, r = iA / NA;
+            if (r > 0 && !mbar_wait_dl(emptyA + st, (r - 1) & 1, deadline)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+            const int a = a0 + iA / int(tg.nchunk), c = iA % int(tg.nchunk);
+            const uint32_t slot = s_loc[a / g.tilesU];
+            mbar_arrive_expect_tx(fullA + st, tg.chunk);
+            bulk_g2s(ringA + size_t(st) * g.stageA(), expert_of(slot) + tg.chunk_off(a % g.tilesU, c), tg.chunk,
+                     fullA + st);
+            ++iA;
+        };
+        auto issueB = [&]() {
+            int t = bb / g.outTiles;
+            while (jj >= int(s_tok[t + 1])) {         // next B unit (skip tokens without local slots)
+                ++bb;
+                t = bb / g.outTiles;
+                jj = int(s_tok[t]);
+            }
+            const int st = iB % NB, r = iB / NB;
+            if (r > 0 && !mbar_wait_dl(emptyB + st, (r - 1) & 1, deadline)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+            const uint32_t slot = s_loc[jj];
+            mbar_arrive_expect_tx(fullB + st, tg.btile);
+            bulk_g2s(ringB + size_t(st) * g.stageB(), expert_of(slot) + tg.btile_off(bb % g.outTiles), tg.btile,
+                     fullB + st);
+            ++jj;
+            ++iB;
+        };
+        if (b0 < b1) jj = int(s_tok[b0 / g.outTiles]);
+        while (iA < nAi && iA < NA) issueA();
+        while (iB < nBi && iB < NB) issueB();
+        while (iA < nAi) issueA();
+        while (iB < nBi) issueB();
+    };
+
+    // ------------------------------------------------------------- routing
+    if (A.rw) {
+        // logit rows r = cta + i * grid, all consumer warps per row
+        const uint32_t rows = A.n_experts * g.ntok;
+        for (uint32_t r = cta; r < rows; r += ncta) {
+            if (consumer) {
+                const float v = router_row_part(A, xsrc, r / A.n_experts, r % A.n_experts, tid);
+                if (lane == 0) red[warp] = v;
+                cons_sync();
+                if (tid == 0) {
+                    float s = 0.f;
+                    for (int w = 0; w < kLCons; ++w) s += red[w];
+                    A.logits[r] = s;
+                    red_rel_gpu(&A.st->rdone, 1u);
+                }
+                cons_sync();
+            }
+        }
+        ltrace(A.trace, 1);
+        if (warp == kLHWarp) {
+            if (lane == 0 && !spin_geq<false>(&A.st->rdone, rows, deadline)) raise_err(A.err, SMOE_DEVERR_SPIN_TIMEOUT);
+            __syncwarp();
+            for (int t = 0; t < g.ntok; ++t) {
+                warp_topk(A.logits + size_t(t) * A.n_experts, A.n_experts, k, A.norm, s_ids + t * k, s_w + t * k, lane);
+                __syncwarp();
+                if (cta == 0 && lane < k) {
+                    if (A.ids_out) A.ids_out[t * k + lane] = s_ids[t * k + lane];
+                    if (A.wts_out) A.wts_out[t * k + lane] = s_w[t * k + lane];
+                }
+            }
+            __syncwarp();
+            finish_routing();
+            if (lane == 0) mbar_arrive(routed);
+            ltrace(A.trace, 2, lane == 0);
+        }
+    } else if (warp == kLProdWarp) {
+        // routing given: read it, start the weight stream at once
+        for (uint32_t i = lane; i < nslots; i += 32) {
+            uint32_t id = A.ids_in[i];
+            if (id >= A.n_experts) {
+                raise_err(A.err, SMOE_DEVERR_BAD_EXPERT);      // skipped: never local
+                id = 0xffffffffu;
+            }
+            s_ids[i] = id;
+            s_w[i] = A.wts_in[i];
+        }
+        __syncwarp();
+        finish_routing();
+        if (lane == 0) {
+            mbar_arrive(routed);
+            produce();
+        }
+        __syncwarp();
+        ltrace(A.trace, 2);
+    }
+    if (A.rw && warp == kLProdWarp) {
+        if (lane == 0) {
+            if (!mbar_wait_dl(routed, 0, deadline)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+            produce();
+        }
+        __syncwarp();
+    }
+
+    if (consumer) {
+        // ------------------------------------------------ x table, phase A
+        build_xtab<FMT>(xsrc, A.x_dtype, g.ntok, d, xtab, xg, tid);
+        cons_sync();
+        ltrace(A.trace, 3);
+        if (!mbar_wait_dl(routed, 0, deadline)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+        int a0, a1;
+        a_range(a0, a1);
+        const int gr = lane >> 2, cq = lane & 3;
+        int iA = 0;
+        for (int a = a0; a < a1; ++a) {
+            const int n = a - a0, b = n & 1;
+            const uint32_t slot = s_loc[a / g.tilesU];
+            const int tok = int(slot) / k;
+            float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+            for (int c = 0; c < int(tg.nchunk); ++c, ++iA) {
+                const int st = iA % NA;
+                if (!mbar_wait_dl(fullA + st, (iA / NA) & 1, deadline)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+                if (n == 0 && c == 0) ltrace(A.trace, 4);
+                const uint8_t* sp = ringA + size_t(st) * g.stageA();
+                const uint8_t* sbp = sp + 2 * tg.fragC;          // [gate sb][up sb]
+                uint4 w[GW][2];
+#pragma unroll
+                for (int j = 0; j < GW; ++j) {
+                    const int gl = min(warp + j * kLCons, int(tg.Gc) - 1);
+#pragma unroll
+                    for (int m = 0; m < 2; ++m)
+                        w[j][m] = *reinterpret_cast<const uint4*>(sp + m * tg.fragC + (gl * 32 + lane) * 16);
+                }
+#pragma unroll
+                for (int j = 0; j < GW; ++j) {
+                    const int gl = warp + j * kLCons;
+                    if (gl < int(tg.Gc)) {
+                        const int grp = c * int(tg.Gc) + gl;
+                        const float2 xv = xg[grp * 4 + cq];
+                        const uint4 bA = xtab[(grp * 2) * 32 + lane], bB = xtab[(grp * 2 + 1) * 32 + lane];
+                        const uint32_t be[2] = {bA.x, bA.y}, bo[2] = {bA.z, bA.w};
+                        const uint32_t be2[2] = {bB.x, bB.y}, bo2[2] = {bB.z, bB.w};
+#pragma unroll
+                        for (int m = 0; m < 2; ++m) {
+                            const uint32_t ae[4] = {w[j][m].x & 0x0F0F0F0Fu, w[j][m].y & 0x0F0F0F0Fu,
+                                                    w[j][m].z & 0x0F0F0F0Fu, w[j][m].w & 0x0F0F0F0Fu};
+                            const uint32_t ao[4] = {w[j][m].x & 0xF0F0F0F0u, w[j][m].y & 0xF0F0F0F0u,
+                                                    w[j][m].z & 0xF0F0F0F0u, w[j][m].w & 0xF0F0F0F0u};
+                            int de[4] = {0, 0, 0, 0}, dO[4] = {0, 0, 0, 0}, de2[4] = {0, 0, 0, 0}, dO2[4] = {0, 0, 0, 0};
+                            mma_u8s8_16832(de, ae, be);
+                            mma_u8s8_16832(dO, ao, bo);
+                            mma_u8s8_16832(de2, ae, be2);
+                            mma_u8s8_16832(dO2, ao, bo2);
+                            const float v0 = fmaf(float(16 * de2[0] + dO2[0]), 65536.0f,
+                                                  float((16 * de[0] + dO[0]) + 256 * (16 * de[1] + dO[1])));
+                            const float v8 = fmaf(float(16 * de2[2] + dO2[2]), 65536.0f,
+                                                  float((16 * de[2] + dO[2]) + 256 * (16 * de[3] + dO[3])));
+                            if (FMT == kFmtAffine) {
+                                const uint32_t* sbw = reinterpret_cast<const uint32_t*>(sbp + m * tg.sbC) + gl * 16 + gr;
+                                const uint32_t s0 = sbw[0], s8 = sbw[8];
+                                acc[m][0] += fmaf(bf16_bits_to_f32(uint16_t(s0)), v0 * xv.x,
+                                                  bf16_bits_to_f32(uint16_t(s0 >> 16)) * xv.y);
+                                acc[m][1] += fmaf(bf16_bits_to_f32(uint16_t(s8)), v8 * xv.x,
+                                                  bf16_bits_to_f32(uint16_t(s8 >> 16)) * xv.y);
+                            } else {
+                                const uint16_t* sbh = reinterpret_cast<const uint16_t*>(sbp + m * tg.sbC) + gl * 16 + gr;
+                                acc[m][0] += f16_bits_to_f32(sbh[0]) * fmaf(v0, xv.x, -xv.y);
+                                acc[m][1] += f16_bits_to_f32(sbh[8]) * fmaf(v8, xv.x, -xv.y);
+                            }
+                        }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(emptyA + st);          // chunk fully consumed
+            }
+            // the unit's warp partials -> buffer b (free once the h warp read use n-2)
+            if (n >= 2 && !mbar_wait_dl(redE + b, ((n >> 1) - 1) & 1, deadline))
+                raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+            float* rb = red + (b * kLCons + warp) * 32;
+            if (cq == tok) {
+                rb[gr] = acc[0][0];
+                rb[gr + 8] = acc[0][1];
+                rb[16 + gr] = acc[1][0];
+                rb[16 + gr + 8] = acc[1][1];
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(redF + b);
+        }
+        ltrace(A.trace, 5);
+
+        // ------------------------------------------------ phase B
+        if (b0 < b1) {
+            if (tid == 0 && !spin_geq<false>(&A.st->arrive, uint32_t(ncta), deadline))
+                raise_err(A.err, SMOE_DEVERR_SPIN_TIMEOUT);
+            cons_sync();
+            ltrace(A.trace, 6);
+            const uint32_t M = 0x000F000Fu, OR = 0x43004300u;
+            const uint32_t* codes_dummy = nullptr;
+            (void)codes_dummy;
+            uint8_t* hsm = reinterpret_cast<uint8_t*>(xtab);          // the x table is no longer needed
+            int cur = -1, iB = 0;
+            for (int bu = b0; bu < b1; ++bu) {
+                const int t = bu / g.outTiles, o = bu % g.outTiles;
+                const int ls = int(s_tok[t]), le = int(s_tok[t + 1]);
+                if (t != cur) {
+                    // this token's h records (local slots ls..le) into shared memory
+                    const uint4* src = reinterpret_cast<const uint4*>(A.hbuf + size_t(ls) * g.tilesU * kHRec);
+                    const int n16 = (le - ls) * g.tilesU * kHRec / 16;
+                    constexpr int U = 8;
+                    for (int base = 0; base < n16; base += U * kLCThreads) {
+                        uint4 v[U];
+#pragma unroll
+                        for (int q = 0; q < U; ++q) {
+                            const int i = base + q * kLCThreads + tid;
+                            if (i < n16) v[q] = __ldcg(src + i);
+                        }
+#pragma unroll
+                        for (int q = 0; q < U; ++q) {
+                            const int i = base + q * kLCThreads + tid;
+                            if (i < n16) reinterpret_cast<uint4*>(hsm)[i] = v[q];
+                        }
+                    }
+                    cons_sync();
+                    cur = t;
+                }
+                float y0 = 0.f, y8 = 0.f;
+                for (int jj = ls; jj < le; ++jj, ++iB) {
+                    const int st = iB % NB;
+                    if (!mbar_wait_dl(fullB + st, (iB / NB) & 1, deadline)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+                    const uint8_t* sp = ringB + size_t(st) * g.stageB();
+                    const uint32_t* cw = reinterpret_cast<const uint32_t*>(sp);
+                    const uint8_t* sbp = sp + tg.bcodes;
+                    const uint8_t* hr = hsm + size_t(jj - ls) * g.tilesU * kHRec;
+                    for (int us = warp; us < g.tilesU; us += kLCons) {
+                        const uint32_t wv = cw[us * 32 + lane];
+                        uint32_t a[4];
+                        a[0] = lop3_and_or(wv, M, OR);
+                        a[1] = lop3_and_or(wv >> 4, M, OR);
+                        a[2] = lop3_and_or(wv >> 8, M, OR);
+                        a[3] = lop3_and_or(wv >> 12, M, OR);
+                        const uint8_t* rec = hr + us * kHRec;
+                        const uint2 bv = lane < 8 ? *reinterpret_cast<const uint2*>(rec + 8 * lane) : make_uint2(0u, 0u);
+                        const uint32_t bb[2] = {bv.x, bv.y};
+                        float dd[4] = {0.f, 0.f, 0.f, 0.f};
+                        mma_bf16_16816(dd, a, bb);
+                        if (cq == 0) {
+                            const float hs = *reinterpret_cast<const float*>(rec + 64);
+                            const int grp = us >> 2;
+                            const float q0 = fmaf(-128.0f, hs, dd[0] + dd[1]);
+                            const float q8 = fmaf(-128.0f, hs, dd[2] + dd[3]);
+                            if (FMT == kFmtAffine) {
+                                const uint32_t* sbw = reinterpret_cast<const uint32_t*>(sbp) + grp * 16 + gr;
+                                const uint32_t s0 = sbw[0], s8 = sbw[8];
+                                y0 += fmaf(bf16_bits_to_f32(uint16_t(s0)), q0, bf16_bits_to_f32(uint16_t(s0 >> 16)) * hs);
+                                y8 += fmaf(bf16_bits_to_f32(uint16_t(s8)), q8, bf16_bits_to_f32(uint16_t(s8 >> 16)) * hs);
+                            } else {
+                                const uint16_t* sbh = reinterpret_cast<const uint16_t*>(sbp) + grp * 16 + gr;
+                                y0 += f16_bits_to_f32(sbh[0]) * fmaf(q0, 1.0f / 7.5f, -hs);
+                                y8 += f16_bits_to_f32(sbh[8]) * fmaf(q8, 1.0f / 7.5f, -hs);
+                            }
+                        }
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(emptyB + st);
+                }
+                if (cq == 0) {
+                    red2[warp * 16 + gr] = y0;
+                    red2[warp * 16 + gr + 8] = y8;
+                }
+                cons_sync();
+                if (tid < 16) {                                   // warp 0, lanes 0-15: row 16o + tid
+                    float s = 0.f;
+#pragma unroll
+                    for (int w = 0; w < kLCons; ++w) s += red2[w * 16 + tid];
+                    const size_t yi = size_t(t) * d + o * 16 + tid;
+                    bool write = true;
+                    if (epm && ep.rank > 0) {
+                        __stcg(ep.part0 + size_t(ep.rank) * ep.part_stride + yi, s);
+                        __threadfence_system();
+                        __syncwarp(0xffffu);
+                        if (tid == 0) atomicAdd_system(ep.cnt0 + bu, 1u);
+                        write = false;
+                    } else if (epm) {
+                        if (tid == 0 && !spin_geq<true>(ep.cnt0 + bu, uint32_t(ep.world - 1), deadline))
+                            raise_err(A.err, SMOE_DEVERR_SPIN_TIMEOUT);
+                        __syncwarp(0xffffu);
+                        for (int r = 1; r < ep.world; ++r) s += __ldcv(ep.part0 + size_t(r) * ep.part_stride + yi);
+                        __syncwarp(0xffffu);
+                        if (tid == 0) ep.cnt0[bu] = 0u;           // ready for the next launch
+                    }
+                    if (write) {
+                        if (A.y_dtype == 0) static_cast<float*>(A.y)[yi] = s;
+                        else static_cast<__nv_bfloat16*>(A.y)[yi] = __float2bfloat16_rn(s);
+                    }
+                }
+                cons_sync();
+            }
+            ltrace(A.trace, 7);
+        }
+    } else if (warp == kLHWarp) {
+        // ------------------------------------------------ h warp
+        if (!mbar_wait_dl(routed, 0, deadline)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+        int a0, a1;
+        a_range(a0, a1);
+        for (int a = a0; a < a1; ++a) {
+            const int n = a - a0, b = n & 1;
+            const uint32_t li = uint32_t(a / g.tilesU), u = uint32_t(a % g.tilesU);
+            const uint32_t slot = s_loc[li];
+            if (!mbar_wait_dl(redF + b, (n >> 1) & 1, deadline)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+            const float* rb = red + b * kLCons * 32;
+            float v = 0.f;                                        // lane = (matrix, row)
+#pragma unroll
+            for (int w = 0; w < kLCons; ++w) v += rb[w * 32 + lane];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(redE + b);
+            const float up = __shfl_down_sync(0xffffffffu, v, 16);
+            const float hv = lane < 16 ? v * (1.0f / (1.0f + expf(-v))) * up * s_w[slot] : 0.f;  // kernels.metal:61-63
+            const float hi = __bfloat162float(__float2bfloat16_rn(hv));
+            float part = hi + __bfloat162float(__float2bfloat16_rn(hv - hi));   // what the MMA sees
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+            // B fragment of the down MMA, lanes 0-7 (0-3 hi column, 4-7 lo column):
+            // rows 2c, 2c+1 and 2c+8, 2c+9 of the unit
+            const int c = lane & 3;
+            float e[4] = {__shfl_sync(0xffffffffu, hv, 2 * c), __shfl_sync(0xffffffffu, hv, 2 * c + 1),
+                          __shfl_sync(0xffffffffu, hv, 2 * c + 8), __shfl_sync(0xffffffffu, hv, 2 * c + 9)};
+            if (lane >= 4) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) e[q] -= __bfloat162float(__float2bfloat16_rn(e[q]));
+            }
+            uint8_t* rec = A.hbuf + (size_t(li) * g.tilesU + u) * kHRec;
+            if (lane < 8)
+                *reinterpret_cast<uint2*>(rec + 8 * lane) = make_uint2(pack_bf16x2(e[0], e[1]), pack_bf16x2(e[2], e[3]));
+            if (lane == 8) *reinterpret_cast<float*>(rec + 64) = part;
+        }
+        // phase A of this CTA is done: publish (release) for phase B of all CTAs
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) red_rel_gpu(&A.st->arrive, 1u);
+        ltrace(A.trace, 8, lane == 0);
+    }
+
+    // the next kernel in the stream may start its launch now
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // ------------------------------------------------- last CTA: reset state
+    __syncthreads();
+    if (tid == 0) {
+        uint32_t old;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(&A.st->done) : "memory");
+        last_cta = (old == uint32_t(ncta) - 1) ? 1u : 0u;
+        if (last_cta) {
+            A.st->rdone = 0;
+            A.st->arrive = 0;
+            A.st->done = 0;
+            if (epm) A.st->epoch = epoch;
+        }
+        // (no fence: the next launch reads these only after this grid has
+        // completed - stream order or griddepcontrol.wait)
+    }
+    ltrace(A.trace, 9);
+}
+
+}  // namespace smoe

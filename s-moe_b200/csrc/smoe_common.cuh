@@ -10,12 +10,22 @@
 enum : uint32_t {
     SMOE_DEVERR_NONE = 0,
     SMOE_DEVERR_MBAR_TIMEOUT = 1,   // a bulk copy never completed
-    SMOE_DEVERR_SPIN_TIMEOUT = 2,   // a cross-CTA wait ran out
+    SMOE_DEVERR_SPIN_TIMEOUT = 2,   // a cross-CTA or cross-GPU wait ran out
+    SMOE_DEVERR_BAD_EXPERT = 3,     // an expert id >= the layer's expert count (slot skipped)
 };
 
-// Bounded spins: ~2^24 polls with back-off is far beyond any legitimate wait
-// (a few microseconds) and far below a watchdog.
-#define SMOE_SPIN_LIMIT (1u << 24)
+// Waits without a caller-given limit (the bulk-copy completions of the
+// two-kernel and grouped paths) give up after this many nanoseconds of
+// %globaltimer time: far beyond any legitimate wait (microseconds), far below
+// a watchdog. An iteration cap backs the clock up.
+#define SMOE_WAIT_NS_DEFAULT 1000000000ull
+#define SMOE_SPIN_LIMIT (1u << 26)
+
+SMOE_DEVINL uint64_t gtimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
 
 SMOE_DEVINL uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -111,15 +121,23 @@ SMOE_DEVINL bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // the phase never completes.
 // The loop is kept out of line: the many wait sites then add one try_wait
 // and a call each to the hot code instead of a copy of the loop.
-static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity) {
+// Bounded by a %globaltimer deadline (absolute, ns).
+static __device__ __noinline__ bool mbar_wait_until(uint64_t* bar, uint32_t parity, uint64_t deadline) {
     for (uint32_t i = 0; i < SMOE_SPIN_LIMIT; ++i) {
         if (mbar_try_wait(bar, parity)) return true;   // try_wait itself suspends a while
+        if ((i & 15) == 15 && gtimer() > deadline) return false;
         if (i > 4096) __nanosleep(64);
     }
     return false;
 }
+static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity) {
+    return mbar_wait_until(bar, parity, gtimer() + SMOE_WAIT_NS_DEFAULT);
+}
 SMOE_DEVINL bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
     return mbar_try_wait(bar, parity) || mbar_wait_slow(bar, parity);
+}
+SMOE_DEVINL bool mbar_wait_dl(uint64_t* bar, uint32_t parity, uint64_t deadline) {
+    return mbar_try_wait(bar, parity) || mbar_wait_until(bar, parity, deadline);
 }
 
 // 1-D bulk copy global -> shared, completion counted on `bar` (bytes).

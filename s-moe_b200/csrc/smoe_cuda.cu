@@ -12,7 +12,7 @@
 
 #include "../../include/smoe_cuda.h"
 #include "ffn_q4.cuh"
-#include "ffn_fused_kernel.cuh"
+#include "moe_layer.cuh"
 #include "router.cuh"
 #include "sampler.cuh"
 #include "decode.cuh"
@@ -63,11 +63,10 @@ struct SmoeCudaCtx {
     std::atomic<uint64_t> dispatches{0};
     size_t smem_optin = 0;
     int num_sms = 0;
-    smoe::FusedState* fstate = nullptr;
-    float* acc = nullptr;            // fused kernel's output accumulator [kFusedMaxTok][max_d_model]
-    int fused_grid[2][4] = {};       // fused kernel grid per (format, groups per warp)
-    size_t fused_smem_seen[2][4] = {};
-    unsigned long long* trace = nullptr;   // phase timestamps of the fused kernel (profiling aid)
+    smoe::LayerState* lstate = nullptr;   // layer kernel's grid counters (zero between launches)
+    uint8_t* hbuf = nullptr;              // layer kernel's h records [kLMaxTok*kLMaxK][max_d_ff/16][kHRec]
+    uint64_t wait_ns = 0;                 // limit of every device-side wait of the layer kernel
+    unsigned long long* trace = nullptr;   // phase timestamps of the layer kernel (profiling aid)
     // expert-grouped batch path: per-expert slot lists, operand tables, per-slot outputs
     uint32_t* g_list = nullptr;      // [max_experts][max_batch * 16]
     uint32_t* g_count = nullptr;     // [max_experts], then the grouped path's lo flag
@@ -175,7 +174,7 @@ int launch_grouped(SmoeCudaCtx* c, smoe::FfnArgs& a, int fmt, uint32_t E) {
     int rc;
     uint32_t* lo_flag = c->g_count + c->cfg.max_experts;
     using namespace smoe;
-    smoe::k_group_slots<<<E, 32, 0, c->stream>>>(a.ids, nslots, c->g_list, c->g_count, lcap, lo_flag);
+    smoe::k_group_slots<<<E, 32, 0, c->stream>>>(a.ids, nslots, c->g_list, c->g_count, lcap, lo_flag, c->err);
     if ((rc = prep_kernel(c, k_build_tabs<kTabMma>, size_t(d / 4) * 8))) return rc;
     if ((rc = prep_kernel(c, k_build_tabs<kTabTc>, size_t(dff / 4) * 8))) return rc;
     k_build_tabs<kTabMma><<<a.ntok, 256, size_t(d / 4) * 8, c->stream>>>(a.x, a.x_dtype == 1, d, c->g_xtab, c->g_xgs,
@@ -247,78 +246,80 @@ int launch_ffn(SmoeCudaCtx* c, smoe::FfnArgs& a, int fmt) {
     return SMOE_OK;
 }
 
-// The persistent fused layer kernel: one CTA per SM, cooperative launch so
-// that all CTAs are co-resident (phase B waits on phase-A results of other
-// CTAs). Returns SMOE_ERR_UNSUPPORTED when the shape does not fit, so the
-// caller can use the two-kernel path.
-int launch_fused(SmoeCudaCtx* c, smoe::FfnArgs& f, int fmt, const uint16_t* rw, uint32_t E,
-                 int norm, const smoe::FusedEp* ep = nullptr) {
-    if (f.ntok > (uint32_t)smoe::kFusedMaxTok || f.k > (uint32_t)smoe::kFusedMaxK || f.d_model > 4096 ||
-        (rw && E > (uint32_t)smoe::kRouterMaxE) || (rw && f.d_model % 8))
+// The persistent MoE-layer kernel (moe_layer.cuh): one CTA per SM, all
+// resident at once (one CTA fills an SM's shared memory; the grid is the SM
+// count), so its grid-wide wait is safe; every wait is bounded anyway.
+// Returns SMOE_ERR_UNSUPPORTED when the shape does not fit, so the caller can
+// use another path.
+struct LayerCall {
+    const SmoeMoeLayer* L;       // tiled layer (the experts held here)
+    uint32_t n_experts;          // router rows / id bound
+    uint32_t expert_base;        // id of the first expert held here
+    const void* x; int x_dtype;
+    void* y; int y_dtype;
+    const uint32_t* ids_in; const float* wts_in;
+    uint32_t* ids_out; float* wts_out;
+    const uint16_t* rw; int norm;
+    uint32_t k, batch;
+    const smoe::LayerEp* ep;
+};
+
+int launch_layer(SmoeCudaCtx* c, const LayerCall& q) {
+    const int fmt = int(q.L->fmt & ~uint32_t(SMOE_LAYOUT_TILED));
+    if (q.batch > (uint32_t)smoe::kLMaxTok || q.k > (uint32_t)smoe::kLMaxK || q.L->d_ff > c->cfg.max_d_ff ||
+        (q.rw && (q.n_experts > (uint32_t)smoe::kRouterMaxE || q.L->d_model % 8)))
         return SMOE_ERR_UNSUPPORTED;
-    if (!aligned16(f.x) || !aligned16(f.y)) {            // whole-vector loads and stores
-        set_err("fused layer kernel needs 16-byte aligned x and y %s%ld", "", 0);
+    if (!aligned16(q.x) || (q.y && !aligned16(q.y))) {            // whole-vector loads
+        set_err("layer kernel needs 16-byte aligned x and y %s%ld", "", 0);
         return SMOE_ERR_ARG;
     }
-    smoe::FusedArgs A{};
-    A.g.init(fmt, (int)f.d_model, (int)f.d_ff, (int)f.k, (int)f.ntok, (int)c->smem_optin - 2048);
-    if (A.g.nstages < 2) return SMOE_ERR_UNSUPPORTED;
-    f.hidden = c->hidden;
-    f.err = c->err;
-    A.f = f;
-    A.st = c->fstate;
-    A.rw = rw;
-    A.E = E;
-    A.norm = norm;
+    smoe::LayerArgs A{};
+    if (!A.g.init(fmt, (int)q.L->d_model, (int)q.L->d_ff, (int)q.k, (int)q.batch, (int)c->smem_optin - 1024))
+        return SMOE_ERR_UNSUPPORTED;
+    A.base = q.L->base;
+    A.stride = q.L->expert_stride;
+    A.x = q.x; A.x_dtype = q.x_dtype;
+    A.y = q.y; A.y_dtype = q.y_dtype;
+    A.ids_in = q.ids_in; A.wts_in = q.wts_in;
+    A.ids_out = q.ids_out; A.wts_out = q.wts_out;
+    A.n_experts = q.n_experts;
+    A.rw = q.rw;
+    A.norm = q.norm;
     A.logits = c->logits;
-    A.acc = c->acc;                       // [ntok x d] fp32, zeroed at init and by each launch's last CTA
+    A.hbuf = c->hbuf;
+    A.st = c->lstate;
+    A.err = c->err;
+    A.wait_ns = c->wait_ns;
     A.trace = c->trace;
-    if (ep) A.ep = *ep;
+    if (q.ep) {
+        A.ep = *q.ep;
+    } else {
+        A.ep.world = 1;
+        A.ep.base = 0;
+        A.ep.nlocal = q.n_experts;
+    }
     const size_t smem = (size_t)A.g.total;
-    // gate/up groups per consumer warp (GW = 1, 2, 4, 8)
-    const int gw_need = (A.g.G + smoe::kFusedConsumers - 1) / smoe::kFusedConsumers;
-    const int gwi = gw_need <= 1 ? 0 : gw_need <= 2 ? 1 : gw_need <= 4 ? 2 : 3;
-    if (gw_need > 8) return SMOE_ERR_UNSUPPORTED;
-    using smoe::k_moe_fused;
+    const int gw = (int(A.g.tg.Gc) + smoe::kLCons - 1) / smoe::kLCons;   // 1 or 2 (Gc <= 32)
+    using smoe::k_moe_layer;
     using smoe::kFmtAffine;
     using smoe::kFmtSmoe;
-    static void* const kerns[2][4] = {
-        {(void*)k_moe_fused<kFmtSmoe, 1>, (void*)k_moe_fused<kFmtSmoe, 2>, (void*)k_moe_fused<kFmtSmoe, 4>,
-         (void*)k_moe_fused<kFmtSmoe, 8>},
-        {(void*)k_moe_fused<kFmtAffine, 1>, (void*)k_moe_fused<kFmtAffine, 2>, (void*)k_moe_fused<kFmtAffine, 4>,
-         (void*)k_moe_fused<kFmtAffine, 8>}};
-    const int fi = fmt == SMOE_FMT_AFFINE_Q4 ? 1 : 0;
-    void* kern = kerns[fi][gwi];
+    static void* const kerns[2][2] = {{(void*)k_moe_layer<kFmtSmoe, 1>, (void*)k_moe_layer<kFmtSmoe, 2>},
+                                      {(void*)k_moe_layer<kFmtAffine, 1>, (void*)k_moe_layer<kFmtAffine, 2>}};
+    void* kern = kerns[fmt == SMOE_FMT_AFFINE_Q4 ? 1 : 0][gw - 1];
     int rc = prep_kernel(c, kern, smem);
     if (rc) return rc;
     cudaLaunchConfig_t lc{};
-    lc.blockDim = dim3(smoe::kFusedThreads);
+    lc.blockDim = dim3(smoe::kLThreads);
     lc.dynamicSmemBytes = smem;
     lc.stream = c->stream;
-    // With a router phase CTAs wait on each other's logits: cooperative
-    // launch (co-residency guaranteed). With the routing given nothing waits,
-    // so a plain launch, marked for programmatic dependent launch so that its
-    // setup overlaps the previous kernel's tail.
+    lc.gridDim = dim3(c->num_sms);
+    // programmatic dependent launch: the kernel's set-up overlaps the
+    // previous kernel's tail; it waits for it in griddepcontrol.wait
     cudaLaunchAttribute at[1];
-    if (rw) {
-        at[0].id = cudaLaunchAttributeCooperative;
-        at[0].val.cooperative = 1;
-    } else {
-        at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        at[0].val.programmaticStreamSerializationAllowed = 1;
-    }
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
     lc.attrs = at;
     lc.numAttrs = 1;
-    // one CTA per SM (the shared-memory ring fills an SM); cached per kernel and size
-    int& best = c->fused_grid[fi][gwi];
-    if (best == 0 || c->fused_smem_seen[fi][gwi] != smem) {
-        int per_sm = 0;
-        CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, smoe::kFusedThreads, smem));
-        if (per_sm < 1) { set_err("fused kernel does not fit an SM with %s%ld bytes", "", (long)smem); return SMOE_ERR_CUDA; }
-        best = c->num_sms;
-        c->fused_smem_seen[fi][gwi] = smem;
-    }
-    lc.gridDim = dim3(best);
     void* args[] = {&A};
     CK(cudaLaunchKernelExC(&lc, kern, args));
     c->dispatches += 1;
@@ -372,6 +373,7 @@ SmoeCudaCtx* smoe_cuda_init_ex(const SmoeCudaInitArgs* args) {
     if (!a.max_batch) a.max_batch = 256;
     if (!a.max_vocab) a.max_vocab = 262144;
     if (!a.timeout_ms) a.timeout_ms = 10000;
+    if (!a.device_wait_us) a.device_wait_us = 1000000;
     if (a.max_experts > (uint32_t)smoe::kRouterMaxE) {
         set_err("max_experts above %s%ld", "", (long)smoe::kRouterMaxE);
         return nullptr;
@@ -380,6 +382,7 @@ SmoeCudaCtx* smoe_cuda_init_ex(const SmoeCudaInitArgs* args) {
     if (!c) return nullptr;
     c->device = a.device;
     c->cfg = a;
+    c->wait_ns = uint64_t(a.device_wait_us) * 1000u;
     auto fail = [&](cudaError_t e) {
         set_err("init failed: %s (%ld)", cudaGetErrorString(e), 0);
         smoe_cuda_destroy(c);
@@ -403,8 +406,8 @@ SmoeCudaCtx* smoe_cuda_init_ex(const SmoeCudaInitArgs* args) {
     if ((e = cudaMalloc(&c->wts, size_t(a.max_batch) * 16 * 4)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->ticket, size_t(a.max_batch) * 4)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->err, 4)) != cudaSuccess) return fail(e);
-    if ((e = cudaMalloc(&c->fstate, sizeof(smoe::FusedState))) != cudaSuccess) return fail(e);
-    if ((e = cudaMalloc(&c->acc, size_t(smoe::kFusedMaxTok) * a.max_d_model * 4)) != cudaSuccess) return fail(e);
+    if ((e = cudaMalloc(&c->lstate, sizeof(smoe::LayerState))) != cudaSuccess) return fail(e);
+    if ((e = cudaMalloc(&c->hbuf, size_t(smoe::kLMaxTok) * smoe::kLMaxK * (a.max_d_ff / 16) * smoe::kHRec)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->g_list, size_t(a.max_experts) * slots * 4)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->g_count, size_t(a.max_experts + 1) * 4)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->g_xtab, size_t(a.max_batch) * a.max_d_model * 4)) != cudaSuccess) return fail(e);
@@ -412,8 +415,7 @@ SmoeCudaCtx* smoe_cuda_init_ex(const SmoeCudaInitArgs* args) {
     if ((e = cudaMalloc(&c->g_htab, slots * a.max_d_ff * 4)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->g_hgs, slots * (a.max_d_ff / 64) * 8)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->g_ys, slots * a.max_d_model * 4)) != cudaSuccess) return fail(e);
-    cudaMemsetAsync(c->acc, 0, size_t(smoe::kFusedMaxTok) * a.max_d_model * 4, c->stream);
-    cudaMemsetAsync(c->fstate, 0, sizeof(smoe::FusedState), c->stream);
+    cudaMemsetAsync(c->lstate, 0, sizeof(smoe::LayerState), c->stream);
     c->gemv_cap = a.max_vocab > a.max_d_model ? a.max_vocab : a.max_d_model;
     if ((e = cudaMalloc(&c->gemv_out, c->gemv_cap * 4)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->gemv_in, size_t(a.max_d_model) * 4)) != cudaSuccess) return fail(e);
@@ -441,7 +443,7 @@ void smoe_cuda_destroy(SmoeCudaCtx* c) {
     if (c->ep_win) cudaFree(c->ep_win);
     for (auto& ev : c->events)
         if (ev) cudaEventDestroy(ev);
-    void* bufs[] = {c->g_list, c->g_count, c->g_xtab, c->g_xgs, c->g_htab, c->g_hgs, c->g_ys, c->fstate, c->acc, c->hidden, c->slot_out, c->in_stage, c->batch_out, c->logits, c->ids,
+    void* bufs[] = {c->g_list, c->g_count, c->g_xtab, c->g_xgs, c->g_htab, c->g_hgs, c->g_ys, c->lstate, c->hbuf, c->hidden, c->slot_out, c->in_stage, c->batch_out, c->logits, c->ids,
                     c->wts, c->ticket, c->err, c->gemv_out, c->gemv_in};
     for (void* b : bufs)
         if (b) cudaFree(b);
@@ -634,31 +636,69 @@ void smoe_cuda_wait_ffn_batch(SmoeCudaCtx* c, void* h, float* out, uint32_t batc
         set_err("output copy failed %s%ld", "", 0);
 }
 
-void smoe_cuda_scout_matvec_bf16(SmoeCudaCtx* c, const uint16_t* w, const float* in, float* out,
-                                 uint32_t rows, uint32_t cols) {
-    if (!c || !w || !in || !out || cols % 8 || cols > c->cfg.max_d_model || !aligned16(w)) {
+}  // extern "C"
+
+namespace {
+// One bf16 GEMV of the mirrored entries, asynchronous: host or device input
+// and output (host ones are staged through the context's buffers, in stream
+// order, so consecutive calls may reuse them).
+int matvec_one(SmoeCudaCtx* c, const uint16_t* w, const float* in, float* out, uint32_t rows, uint32_t cols) {
+    if (!c || !w || !in || !out || cols == 0 || cols % 8 || cols > c->cfg.max_d_model || !aligned16(w)) {
         set_err("bad matvec arguments %s%ld", "", (long)cols);
-        return;
+        return SMOE_ERR_ARG;
     }
     const bool out_dev = is_device_ptr(out);
     if (!out_dev && rows > c->gemv_cap) {
         set_err("matvec rows exceed staging %s%ld", "", (long)rows);
-        return;
+        return SMOE_ERR_ARG;
     }
     const float* x = in;
     if (!is_device_ptr(in)) {
-        if (cudaMemcpyAsync(c->gemv_in, in, size_t(cols) * 4, cudaMemcpyHostToDevice, c->stream)) return;
+        CK(cudaMemcpyAsync(c->gemv_in, in, size_t(cols) * 4, cudaMemcpyHostToDevice, c->stream));
         x = c->gemv_in;
     }
     float* y = out_dev ? out : c->gemv_out;
     const uint32_t blocks = (rows + 7) / 8 < 148u * 8u ? (rows + 7) / 8 : 148u * 8u;
     const size_t smem = size_t(cols) * 4;
-    if (prep_kernel(c, smoe::k_gemv_bf16, smem)) return;
+    int rc = prep_kernel(c, smoe::k_gemv_bf16, smem);
+    if (rc) return rc;
     smoe::k_gemv_bf16<<<blocks, 256, smem, c->stream>>>(w, x, y, rows, cols);
+    CK(cudaGetLastError());
     c->dispatches += 1;
-    if (!out_dev)
-        cudaMemcpyAsync(out, y, size_t(rows) * 4, cudaMemcpyDeviceToHost, c->stream);
-    smoe_cuda_synchronize(c);   // synchronous, as metal_bridge.h:157
+    if (!out_dev) CK(cudaMemcpyAsync(out, y, size_t(rows) * 4, cudaMemcpyDeviceToHost, c->stream));
+    return SMOE_OK;
+}
+}  // namespace
+
+extern "C" {
+
+void smoe_cuda_scout_matvec_bf16(SmoeCudaCtx* c, const uint16_t* w, const float* in, float* out,
+                                 uint32_t rows, uint32_t cols) {
+    if (matvec_one(c, w, in, out, rows, cols) == SMOE_OK)
+        smoe_cuda_synchronize(c);   // synchronous, as metal_bridge.h:157
+}
+
+// metal_bridge.h:199-206: dispatch i may read what an earlier one wrote; the
+// context's single stream orders them.
+void smoe_cuda_scout_matvec_batch_bf16(SmoeCudaCtx* c, const uint16_t** weights, const float** inputs,
+                                       float** outputs, const uint32_t* rows, const uint32_t* cols,
+                                       uint32_t count) {
+    if (!c || (count && (!weights || !inputs || !outputs || !rows || !cols))) {
+        set_err("bad matvec batch arguments %s%ld", "", (long)count);
+        return;
+    }
+    for (uint32_t i = 0; i < count; ++i)
+        if (matvec_one(c, weights[i], inputs[i], outputs[i], rows[i], cols[i]) != SMOE_OK) return;
+    smoe_cuda_synchronize(c);
+}
+
+// metal_bridge.h:212-219: the caller guarantees distinct outputs that no
+// dispatch reads, so no ordering between them is needed; on one stream they
+// run back to back (each kernel fills the GPU on its own at these sizes).
+void smoe_cuda_scout_matvec_group_bf16(SmoeCudaCtx* c, const uint16_t** weights, const float** inputs,
+                                       float** outputs, const uint32_t* rows, const uint32_t* cols,
+                                       uint32_t count) {
+    smoe_cuda_scout_matvec_batch_bf16(c, weights, inputs, outputs, rows, cols, count);
 }
 
 // ------------------------------------------------------- native entries
@@ -730,15 +770,20 @@ int smoe_cuda_moe_ffn(SmoeCudaCtx* c, const SmoeMoeLayer* L, const void* x, int 
     a.per_slot = 0;
     a.k = k;
     a.ntok = batch;
+    a.n_experts = L->n_experts;
     const int fmt = int(L->fmt & ~uint32_t(SMOE_LAYOUT_TILED));
     if (L->fmt & SMOE_LAYOUT_TILED) {
-        rc = launch_fused(c, a, fmt, nullptr, 0, 0);
+        LayerCall q{};
+        q.L = L; q.n_experts = L->n_experts;
+        q.x = x; q.x_dtype = x_dtype; q.y = y; q.y_dtype = y_dtype;
+        q.ids_in = ids; q.wts_in = wts; q.k = k; q.batch = batch;
+        rc = launch_layer(c, q);
         if (rc == SMOE_ERR_UNSUPPORTED)
             set_err("tiled layout needs batch <= 4 and a shape whose tiles fit shared memory %s%ld", "", (long)batch);
         return rc;
     }
     // token batches: expert-grouped path (shapes whose tiles it covers)
-    if (batch > uint32_t(smoe::kFusedMaxTok) && L->d_model % 128 == 0 && L->d_ff % 256 == 0 && L->d_ff <= 4096)
+    if (batch > uint32_t(smoe::kLMaxTok) && L->d_model % 128 == 0 && L->d_ff % 256 == 0 && L->d_ff <= 4096)
         return launch_grouped(c, a, fmt, L->n_experts);
     return launch_ffn(c, a, fmt);
 }
@@ -756,15 +801,12 @@ int smoe_cuda_moe_layer(SmoeCudaCtx* c, const SmoeMoeLayer* L, const void* x, in
         smoe::FfnArgs a{};
         int rc = layer_args(c, L, a);
         if (rc) return rc;
-        a.ids = ids;
-        a.wts = wts;
-        a.x = x;
-        a.x_dtype = x_dtype;
-        a.y = y;
-        a.y_dtype = y_dtype;
-        a.k = k;
-        a.ntok = batch;
-        rc = launch_fused(c, a, int(L->fmt & ~uint32_t(SMOE_LAYOUT_TILED)), L->router_w, L->n_experts, norm);
+        LayerCall q{};
+        q.L = L; q.n_experts = L->n_experts;
+        q.x = x; q.x_dtype = x_dtype; q.y = y; q.y_dtype = y_dtype;
+        q.ids_out = ids; q.wts_out = wts;
+        q.rw = L->router_w; q.norm = norm; q.k = k; q.batch = batch;
+        rc = launch_layer(c, q);
         if (rc == SMOE_ERR_UNSUPPORTED)
             set_err("tiled layout needs batch <= 4 and a shape whose tiles fit shared memory %s%ld", "", (long)batch);
         return rc;
@@ -907,15 +949,21 @@ int smoe_cuda_attention_layer(SmoeCudaCtx* c, const SmoeCudaAttnLayerArgs* a) {
 
 // ----------------------------------------------------------- expert parallel
 namespace {
-constexpr size_t kEpFlagOff = 0, kEpDoneOff = 128, kEpXOff = 256;
-size_t ep_x_bytes(const SmoeCudaCtx* c) { return size_t(smoe::kFusedMaxTok) * c->cfg.max_d_model * 4; }
-size_t ep_part_stride(const SmoeCudaCtx* c) { return size_t(smoe::kFusedMaxTok) * c->cfg.max_d_model; }
+// Exchange window of a rank (rank 0's is the one used): x epoch flag, x copy,
+// [kEpMaxWorld][kLMaxTok * max_d_model] partial rows, [kLMaxTok *
+// max_d_model/16] partial-unit counts.
+constexpr size_t kEpFlagOff = 0, kEpXOff = 256;
+size_t ep_x_bytes(const SmoeCudaCtx* c) { return size_t(smoe::kLMaxTok) * c->cfg.max_d_model * 4; }
+size_t ep_part_stride(const SmoeCudaCtx* c) { return size_t(smoe::kLMaxTok) * c->cfg.max_d_model; }
+size_t ep_cnt_off(const SmoeCudaCtx* c) {
+    return kEpXOff + ep_x_bytes(c) + size_t(smoe::kEpMaxWorld) * ep_part_stride(c) * 4;
+}
 }  // namespace
 
 int smoe_cuda_ep_export(SmoeCudaCtx* c, SmoeEpHandle* out) {
     if (!c || !out) { set_err("null argument %s%ld", "", 0); return SMOE_ERR_ARG; }
     if (!c->ep_win) {
-        c->ep_win_bytes = kEpXOff + ep_x_bytes(c) + size_t(smoe::kEpMaxWorld) * ep_part_stride(c) * 4;
+        c->ep_win_bytes = ep_cnt_off(c) + size_t(smoe::kLMaxTok) * (c->cfg.max_d_model / 16) * 4;
         CK(cudaMalloc(&c->ep_win, c->ep_win_bytes));
         CK(cudaMemset(c->ep_win, 0, c->ep_win_bytes));
     }
@@ -934,8 +982,10 @@ int smoe_cuda_ep_attach(SmoeCudaCtx* c, int rank, int world, const SmoeEpHandle*
     }
     if (c->ep_peer0 && c->ep_peer0 != c->ep_win) cudaIpcCloseMemHandle(c->ep_peer0);
     c->ep_peer0 = nullptr;
-    if (rank == 0) {
-        c->ep_peer0 = c->ep_win;
+    cudaIpcMemHandle_t mine;
+    CK(cudaIpcGetMemHandle(&mine, c->ep_win));
+    if (rank == 0 || memcmp(&mine, handles[0].bytes, sizeof(mine)) == 0) {
+        c->ep_peer0 = c->ep_win;          // rank 0, or a window this process owns
     } else {
         cudaIpcMemHandle_t h;
         memcpy(&h, handles[0].bytes, sizeof(h));
@@ -948,7 +998,7 @@ int smoe_cuda_ep_attach(SmoeCudaCtx* c, int rank, int world, const SmoeEpHandle*
     // a fresh exchange: window and this rank's epoch count start at 0 (every
     // rank attaches before any rank launches an expert-parallel layer)
     CK(cudaMemsetAsync(c->ep_win, 0, c->ep_win_bytes, c->stream));
-    CK(cudaMemsetAsync(&c->fstate->epoch, 0, sizeof(uint32_t), c->stream));
+    CK(cudaMemsetAsync(&c->lstate->epoch, 0, sizeof(uint32_t), c->stream));
     CK(cudaStreamSynchronize(c->stream));
     return SMOE_OK;
 }
@@ -961,33 +1011,42 @@ int smoe_cuda_moe_layer_ep(SmoeCudaCtx* c, const SmoeMoeLayer* shard, uint32_t n
     if (!(shard->fmt & SMOE_LAYOUT_TILED) || !shard->router_w || !aligned16(shard->router_w) ||
         n_experts_total < k || k == 0 || k > SMOE_MAX_ACTIVE || n_experts_total > c->cfg.max_experts ||
         expert_base + shard->n_experts > n_experts_total || (x_dtype != 0 && x_dtype != 1) ||
-        (y_dtype != 0 && y_dtype != 1) || (r0 && (!x || !y))) {
+        (y_dtype != 0 && y_dtype != 1) || batch == 0 || (r0 && (!x || !y))) {
         set_err("bad expert-parallel layer arguments %s%ld", "", (long)k);
         return SMOE_ERR_ARG;
     }
     smoe::FfnArgs a{};
     int rc = layer_args(c, shard, a);
     if (rc) return rc;
-    a.ids = ids_out ? ids_out : c->ids;
-    a.wts = w_out ? w_out : c->wts;
-    a.x = r0 ? x : c->ep_peer0 + kEpXOff;            // ranks > 0 read rank 0's published copy
-    a.x_dtype = x_dtype;
-    a.y = r0 ? y : c->acc;                           // (not written on ranks > 0)
-    a.y_dtype = y_dtype;
-    a.k = k;
-    a.ntok = batch;
-    smoe::FusedEp ep{};
+    smoe::LayerEp ep{};
     ep.world = c->ep_world;
     ep.rank = c->ep_rank;
     ep.base = expert_base;
     ep.nlocal = shard->n_experts;
     ep.x0 = c->ep_peer0 + kEpXOff;
     ep.flag0 = reinterpret_cast<uint32_t*>(c->ep_peer0 + kEpFlagOff);
-    ep.done0 = reinterpret_cast<uint32_t*>(c->ep_peer0 + kEpDoneOff);
     ep.part0 = reinterpret_cast<float*>(c->ep_peer0 + kEpXOff + ep_x_bytes(c));
+    ep.cnt0 = reinterpret_cast<uint32_t*>(c->ep_peer0 + ep_cnt_off(c));
     ep.part_stride = uint32_t(ep_part_stride(c));
-    const int fmt = int(shard->fmt & ~uint32_t(SMOE_LAYOUT_TILED));
-    rc = launch_fused(c, a, fmt, shard->router_w, n_experts_total, norm, c->ep_world > 1 ? &ep : nullptr);
+    LayerCall q{};
+    q.L = shard;
+    q.n_experts = n_experts_total;
+    q.expert_base = expert_base;
+    q.x = r0 ? x : c->ep_peer0 + kEpXOff;            // ranks > 0 read rank 0's published copy
+    q.x_dtype = x_dtype;
+    q.y = r0 ? y : nullptr;                          // (only rank 0 writes y)
+    q.y_dtype = y_dtype;
+    q.ids_out = ids_out;
+    q.wts_out = w_out;
+    q.rw = shard->router_w;
+    q.norm = norm;
+    q.k = k;
+    q.batch = batch;
+    q.ep = &ep;
+    if (c->ep_world == 1) {                          // a world of one: plain single-GPU layer
+        ep.world = 1;
+    }
+    rc = launch_layer(c, q);
     if (rc == SMOE_ERR_UNSUPPORTED)
         set_err("tiled layout needs batch <= 4 and a shape whose tiles fit shared memory %s%ld", "", (long)batch);
     return rc;
@@ -1023,7 +1082,7 @@ uint64_t smoe_cuda_tiled_expert_bytes(uint32_t fmt, uint32_t d, uint32_t dff) {
     fmt &= ~uint32_t(SMOE_LAYOUT_TILED);
     if ((fmt != SMOE_FMT_SMOE_Q4 && fmt != SMOE_FMT_AFFINE_Q4) || !d || !dff || d % 64 || dff % 64) return 0;
     smoe::TiledGeom t;
-    t.init((int)fmt, d, dff);
+    if (!t.init((int)fmt, d, dff)) return 0;
     return t.expert;
 }
 
@@ -1046,8 +1105,8 @@ int smoe_cuda_prepack_layer(SmoeCudaCtx* c, const SmoeMoeLayer* src, void* dst, 
     p.dst = static_cast<uint8_t*>(dst);
     p.dst_stride = dst_stride;
     p.fmt = (int)src->fmt;
-    p.tg.init((int)src->fmt, src->d_model, src->d_ff);
-    dim3 grid(src->d_ff / 16 + src->d_ff / 64, src->n_experts);
+    if (!p.tg.init((int)src->fmt, src->d_model, src->d_ff)) { set_err("shape has no tiled layout %s%ld", "", 0); return SMOE_ERR_ARG; }
+    dim3 grid(src->d_ff / 16 + src->d_model / 16, src->n_experts);
     smoe::k_prepack<<<grid, 256, 0, c->stream>>>(p);
     CK(cudaGetLastError());
     c->dispatches += 1;

@@ -12,7 +12,9 @@
 // until the process exits.
 #include <cuda_runtime.h>
 
+#include <chrono>
 #include <cstdio>
+#include <thread>
 
 #include "../../include/smoe_cuda.h"
 #include "ffn_q4.cuh"
@@ -73,6 +75,8 @@ int smoe_cuda_moe_ffn_noalloc(const SmoeMoeLayer* L, const void* x, int x_dtype,
                               uint32_t batch, void* y, int y_dtype, void* stream) {
     if (!L || !L->base || !x || !ids || !weights || !y)
         return fail(SMOE_ERR_ARG, "null argument", 0);
+    if (L->fmt & SMOE_LAYOUT_TILED)
+        return fail(SMOE_ERR_ARG, "the tiled layout is not supported here; pass the vault layout", (long)L->fmt);
     if (L->fmt != SMOE_FMT_SMOE_Q4 && L->fmt != SMOE_FMT_AFFINE_Q4)
         return fail(SMOE_ERR_ARG, "unknown weight format", (long)L->fmt);
     if (L->d_model == 0 || L->d_ff == 0 || L->d_model % 64 || L->d_ff % 64)
@@ -109,6 +113,7 @@ int smoe_cuda_moe_ffn_noalloc(const SmoeMoeLayer* L, const void* x, int x_dtype,
     a.d_ff = L->d_ff;
     a.k = k;
     a.ntok = batch;
+    a.n_experts = L->n_experts;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (cudaMemsetAsync(a.err, 0, sizeof(uint32_t), s) != cudaSuccess)   // the one word that must start at 0
         return fail(SMOE_ERR_CUDA, "clearing the error word failed", 0);
@@ -127,6 +132,38 @@ int smoe_cuda_moe_ffn_noalloc(const SmoeMoeLayer* L, const void* x, int x_dtype,
     }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(SMOE_ERR_CUDA, cudaGetErrorString(e), 0);
+    return SMOE_OK;
+}
+
+// The device error word of the calls above (bounded waits that ran out, an
+// expert id past the layer): wait (bounded, polling) until `stream` is idle,
+// read the word, clear it. Allocates nothing either.
+int smoe_cuda_noalloc_check(void* stream, uint32_t timeout_ms) {
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    float* scratch = nullptr;
+    int rc = scratch_for_current_device(&scratch);
+    if (rc) return rc;
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        const cudaError_t q = cudaStreamQuery(s);
+        if (q == cudaSuccess) break;
+        if (q != cudaErrorNotReady) return fail(SMOE_ERR_CUDA, cudaGetErrorString(q), 0);
+        const long ms = (long)std::chrono::duration_cast<std::chrono::milliseconds>(
+                            std::chrono::steady_clock::now() - t0).count();
+        if (ms > (long)timeout_ms) return fail(SMOE_ERR_TIMEOUT, "stream still busy after (ms)", ms);
+        std::this_thread::yield();
+    }
+    uint32_t word = 0;          // the stream is idle: the copy returns at once
+    cudaError_t e = cudaMemcpyFromSymbolAsync(&word, g_noalloc_scratch, sizeof(word),
+                                              kNoAllocHiddenFloats * sizeof(float), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return fail(SMOE_ERR_CUDA, cudaGetErrorString(e), 0);
+    if (word != 0) {
+        e = cudaMemsetAsync(scratch + kNoAllocHiddenFloats, 0, sizeof(uint32_t), s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) return fail(SMOE_ERR_CUDA, cudaGetErrorString(e), 0);
+        return fail(SMOE_ERR_DEVICE, "a kernel raised device error code", (long)word);
+    }
     return SMOE_OK;
 }
 

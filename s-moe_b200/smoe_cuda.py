@@ -15,6 +15,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("SMOE_CUDA_LIB") or os.path.join(HERE, "libsmoe_cuda.so")   # override: another build of the library
 
 SMOE_OK = 0
+SMOE_ERR_ARG, SMOE_ERR_CUDA, SMOE_ERR_TIMEOUT, SMOE_ERR_DEVICE = 1, 2, 3, 5
 STATUS = {0: "OK", 1: "ERR_ARG", 2: "ERR_CUDA", 3: "ERR_TIMEOUT", 4: "ERR_NCCL",
           5: "ERR_DEVICE", 6: "ERR_UNSUPPORTED"}
 FMT_SMOE_Q4 = 0
@@ -34,6 +35,7 @@ EXPORTS = [
     "smoe_cuda_register_buffer", "smoe_cuda_kernel_dispatches", "smoe_cuda_router_topk",
     "smoe_cuda_moe_ffn", "smoe_cuda_moe_layer", "smoe_cuda_sample",
     "smoe_cuda_canonical_from_u32", "smoe_cuda_moe_ffn_noalloc", "smoe_cuda_noalloc_last_error",
+    "smoe_cuda_noalloc_check", "smoe_cuda_scout_matvec_batch_bf16", "smoe_cuda_scout_matvec_group_bf16",
     "smoe_cuda_tiled_expert_bytes", "smoe_cuda_prepack_layer",
     "smoe_cuda_ep_export", "smoe_cuda_ep_attach", "smoe_cuda_moe_layer_ep",
     "smoe_cuda_attention_layer", "smoe_cuda_attention_layer_async", "smoe_cuda_matvec_bf16",
@@ -71,7 +73,8 @@ class SmoeCudaError(RuntimeError):
 class InitArgs(C.Structure):
     _fields_ = [("device", C.c_int), ("max_d_model", C.c_uint32), ("max_d_ff", C.c_uint32),
                 ("max_experts", C.c_uint32), ("max_batch", C.c_uint32),
-                ("max_vocab", C.c_uint32), ("timeout_ms", C.c_uint32)]
+                ("max_vocab", C.c_uint32), ("timeout_ms", C.c_uint32),
+                ("device_wait_us", C.c_uint32)]
 
 
 class ExpertBlob(C.Structure):
@@ -122,6 +125,8 @@ def lib():
         L.smoe_cuda_fused_ffn_batch.restype = vp
         L.smoe_cuda_wait_ffn_batch.argtypes = [vp, vp, vp, u32, u32]
         L.smoe_cuda_scout_matvec_bf16.argtypes = [vp, vp, vp, vp, u32, u32]
+        L.smoe_cuda_scout_matvec_batch_bf16.argtypes = [vp, vp, vp, vp, vp, vp, u32]
+        L.smoe_cuda_scout_matvec_group_bf16.argtypes = [vp, vp, vp, vp, vp, vp, u32]
         L.smoe_cuda_register_buffer.argtypes = [vp, vp, C.c_size_t]
         L.smoe_cuda_kernel_dispatches.argtypes = [vp]
         L.smoe_cuda_kernel_dispatches.restype = u64
@@ -144,6 +149,7 @@ def lib():
         L.smoe_cuda_moe_ffn_noalloc.argtypes = [C.POINTER(MoeLayer), vp, i32, vp, vp, u32, u32, vp,
                                                 i32, vp]
         L.smoe_cuda_noalloc_last_error.restype = C.c_char_p
+        L.smoe_cuda_noalloc_check.argtypes = [vp, u32]
         L.smoe_cuda_tiled_expert_bytes.argtypes = [u32, u32, u32]
         L.smoe_cuda_tiled_expert_bytes.restype = u64
         L.smoe_cuda_prepack_layer.argtypes = [vp, C.POINTER(MoeLayer), vp, u64, C.POINTER(MoeLayer)]
@@ -182,8 +188,9 @@ class Context:
     """One smoe_cuda context (scratch, stream, event ring) on one device."""
 
     def __init__(self, device: int = 0, max_d_model=0, max_d_ff=0, max_experts=0,
-                 max_batch=0, max_vocab=0, timeout_ms=0):
-        a = InitArgs(device, max_d_model, max_d_ff, max_experts, max_batch, max_vocab, timeout_ms)
+                 max_batch=0, max_vocab=0, timeout_ms=0, device_wait_us=0):
+        a = InitArgs(device, max_d_model, max_d_ff, max_experts, max_batch, max_vocab, timeout_ms,
+                     device_wait_us)
         self.L = lib()
         self.h = self.L.smoe_cuda_init_ex(C.byref(a))
         if not self.h:
