@@ -67,6 +67,11 @@ def lib():
         L.or_set_threads.restype = i32
         L.or_f32_to_bf16.argtypes = [f32]
         L.or_f32_to_bf16.restype = C.c_uint16
+        L.or_expf_ref.argtypes = [f32]
+        L.or_expf_ref.restype = f32
+        L.or_expf_batch.argtypes = [_f32, _f32, C.c_long]
+        L.or_expf_mismatches.argtypes = [u32, u32]
+        L.or_expf_mismatches.restype = C.c_long
         _lib = L
     return _lib
 
@@ -242,3 +247,17 @@ def canonical_from_word(word: int) -> float:
 
 def set_threads(n: int) -> int:
     return int(lib().or_set_threads(n))
+
+
+def expf_ref(x: np.ndarray) -> np.ndarray:
+    """The reference sampler's expf (glibc's FMA build), restated."""
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty_like(x)
+    lib().or_expf_batch(x, y, x.size)
+    return y
+
+
+def expf_mismatches(lo_bits: int, hi_bits: int) -> int:
+    """Float bit patterns in [lo_bits, hi_bits] where the restated expf and
+    this host's libm expf differ."""
+    return int(lib().or_expf_mismatches(lo_bits, hi_bits))

@@ -18,6 +18,8 @@
  *   - expert blob layout          scripts/shatter_moe.py:627-674
  *   - weighted combine            decode.cpp:481-509 (axpy in rank order)
  *   - token sampler               sampler.hpp:33-157
+ *   - the sampler's expf          glibc e_expf.c (FMA build), called by
+ *                                 sampler.hpp:116 through std::exp(float)
  *
  * The sampler restatement is pinned against the reference's own compiled
  * sampler.hpp (oracle/_ref/libsmoe_ref.so) in tests/test_oracle.py; the Q4
@@ -434,4 +436,69 @@ float or_canonical_from_word(uint32_t w) {
     float r = (float)w / 4294967296.0f;
     if (r >= 1.0f) r = nextafterf(1.0f, 0.0f);
     return r;
+}
+
+/* glibc's expf as the reference's sampler.hpp:116 runs it on x86-64 hosts
+ * with FMA: the table-driven method of ARM optimized-routines (Szabolcs
+ * Nagy; glibc e_expf.c since 2.28). N = 32; z = x*N/ln2 = k + r (k by adding
+ * and subtracting 1.5*2^52); 2^(k/N) = T[k mod N] with k/N added to the
+ * exponent field; 2^(r/N) ~ 1 + C2 r + C1 r^2 + C0 r^3 with the published
+ * exp2 coefficients scaled by 1/N^i; the FMA build fuses the multiply-adds
+ * (written out here as fma() - the file is compiled with
+ * -ffp-contract=off). T[i] = bits(2^(i/N), correctly rounded) - (i << 47).
+ * or_expf_mismatches() compares it with the libm expf of this host over a
+ * range of float bit patterns (tests/test_oracle.py: every float in
+ * [-104, 88]). The CUDA sampler (expf_ref) performs the same operations. */
+static const uint64_t kExp2Tab[32] = {
+    0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull,
+    0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull,
+    0x3fef06fe0a31b715ull, 0x3feef1a7373aa9cbull, 0x3feedea64c123422ull, 0x3feece086061892dull,
+    0x3feebfdad5362a27ull, 0x3feeb42b569d4f82ull, 0x3feeab07dd485429ull, 0x3feea47eb03a5585ull,
+    0x3feea09e667f3bcdull, 0x3fee9f75e8ec5f74ull, 0x3feea11473eb0187ull, 0x3feea589994cce13ull,
+    0x3feeace5422aa0dbull, 0x3feeb737b0cdc5e5ull, 0x3feec49182a3f090ull, 0x3feed503b23e255dull,
+    0x3feee89f995ad3adull, 0x3feeff76f2fb5e47ull, 0x3fef199bdd85529cull, 0x3fef3720dcef9069ull,
+    0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull};
+
+float or_expf_ref(float x) {
+    if (x < -0x1.9fe368p6f) return 0.0f;
+    if (x > 0x1.62e42ep6f) return INFINITY;
+    const double N = 32.0;
+    const double C0 = 0x1.c6af84b912394p-5 / N / N / N, C1 = 0x1.ebfce50fac4f3p-3 / N / N,
+                 C2 = 0x1.62e42ff0c52d6p-1 / N;
+    const double InvLn2N = 0x1.71547652b82fep+0 * N, Shift = 0x1.8p+52;
+    const double xd = (double)x;
+    const double kd0 = fma(InvLn2N, xd, Shift);
+    uint64_t ki;
+    memcpy(&ki, &kd0, 8);
+    const double kd = kd0 - Shift;
+    const double r = fma(InvLn2N, xd, -kd);
+    const uint64_t t = kExp2Tab[ki & 31u] + (ki << 47);
+    double sc;
+    memcpy(&sc, &t, 8);
+    const double zc = fma(C0, r, C1);
+    const double r2 = r * r;
+    double y = fma(C2, r, 1.0);
+    y = fma(zc, r2, y);
+    y = y * sc;
+    return (float)y;
+}
+
+void or_expf_batch(const float* x, float* y, long n) {
+#pragma omp parallel for schedule(static)
+    for (long i = 0; i < n; ++i) y[i] = or_expf_ref(x[i]);
+}
+
+/* Float bit patterns lo..hi (inclusive, same sign) on which or_expf_ref and
+ * this host's libm expf differ. */
+long or_expf_mismatches(uint32_t lo, uint32_t hi) {
+    long bad = 0;
+#pragma omp parallel for schedule(static) reduction(+ : bad)
+    for (long u = (long)lo; u <= (long)hi; ++u) {
+        const uint32_t w = (uint32_t)u;
+        float x;
+        memcpy(&x, &w, 4);
+        const float a = or_expf_ref(x), b = expf(x);
+        if (memcmp(&a, &b, 4) != 0) ++bad;
+    }
+    return bad;
 }

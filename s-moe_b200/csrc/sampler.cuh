@@ -6,19 +6,19 @@
 //   1. repetition penalty over the last 256 history ids, each distinct
 //      non-exempt id once, in place (sampler.hpp:42-70), written back;
 //   2. greedy argmax when T < 1e-4, lowest index on ties (sampler.hpp:73-83);
-//   3. max, then e = exp((s - max)/T) for every entry, correctly rounded
-//      (double-precision evaluation), and the reference's sequential fp32
-//      sum of all e reproduced exactly (seqsum.cuh) (sampler.hpp:86-129);
+//   3. max, then e = exp((s - max)/T) for every entry, bit-identical to the
+//      reference's glibc expf (expf_ref below), and the reference's
+//      sequential fp32 sum of all e reproduced exactly (seqsum.cuh)
+//      (sampler.hpp:86-129);
 //   4. top-K candidates by e via a 4 x 8-bit radix select (K = max(top_k,1)
 //      <= 1024), ties at the threshold taken lowest index first;
 //   5. CTA 0 sorts the K candidates (e desc, index asc) and walks the top-p /
 //      top-k cutoff and the draw with the reference's float operations
 //      (sampler.hpp:132-156).
-// Bit-exactness: token ids equal the reference's whenever each e equals
-// glibc's expf result; glibc's expf is within 0.502 ulp (measured here:
-// it differs from the correctly rounded value on 6.3e-4 of random inputs),
-// and ties between equal e values are ordered by index here and unspecified
-// in the reference's heap + sort.
+// Bit-exactness: every e equals the reference's, the sum is its sequential
+// fp32 sum, the cutoff and draw are its float operations; ties between equal
+// e values are ordered by index here and unspecified in the reference's heap
+// + sort.
 #pragma once
 #include <cooperative_groups.h>
 #include "smoe_common.cuh"
@@ -56,20 +56,50 @@ constexpr int kSampCluster = 8;
 constexpr int kSampThreads = 1024;
 constexpr int kSampCand = 1024;
 
-// exp(x) for x <= 0 in double: Cody-Waite reduction x = k ln2 + r with ln 2
-// split into a 32-significant-bit head and its remainder, |r| <= ln2/2, then
-// the Taylor series of e^r to degree 13 (truncation < 5e-18), scaled by 2^k.
-SMOE_DEVINL double exp_neg_d(double x) {
-    if (x < -745.0) return 0.0;
-    const double k = rint(x * 1.4426950408889634);
-    const double r = fma(-k, 1.9082149292705877e-10, fma(-k, 0.6931471803691238, x));
-    double p = 1.0 / 6227020800.0;                       // 1/13!
-    const double inv_fact[13] = {1.0 / 479001600.0, 1.0 / 39916800.0, 1.0 / 3628800.0,
-                                 1.0 / 362880.0, 1.0 / 40320.0, 1.0 / 5040.0, 1.0 / 720.0,
-                                 1.0 / 120.0, 1.0 / 24.0, 1.0 / 6.0, 0.5, 1.0, 1.0};
-#pragma unroll
-    for (int i = 0; i < 13; ++i) p = fma(p, r, inv_fact[i]);
-    return scalbn(p, int(k));
+// e = exp(x) for the sampler exactly as the reference computes it.
+// sampler.hpp:116 calls std::exp on a float, i.e. glibc's expf, whose x86-64
+// build on CPUs with FMA (every host of a B200) is the table-driven method of
+// Szabolcs Nagy (ARM optimized-routines, glibc >= 2.28, e_expf.c): with N = 32,
+//   z = x N/ln2 = k + r, |r| <= 1/2 (k by adding and subtracting 1.5*2^52),
+//   2^(k/N) = T[k mod N] with k/N added to its exponent field,
+//   2^(r/N) ~ 1 + C2 r + C1 r^2 + C0 r^3 (C = the published degree-3 exp2
+//   coefficients scaled by 1/N, 1/N^2, 1/N^3),
+// all in double with the FMA build's fused multiply-adds, rounded to float
+// once. T[i] holds the bits of 2^(i/N) (correctly rounded; computed from the
+// definition) minus i << 47. Every step is an IEEE-exact double operation, so
+// the result equals the CPU's bit for bit: the restatement in
+// oracle/smoe_oracle.c (or_expf_ref) reproduces glibc 2.39's expf on every
+// float in [-104, 88] (tests/test_oracle.py), and the GPU sampler tests
+// compare with the compiled reference.
+__device__ __align__(256) const uint64_t kExp2Tab[32] = {
+    0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull,
+    0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull,
+    0x3fef06fe0a31b715ull, 0x3feef1a7373aa9cbull, 0x3feedea64c123422ull, 0x3feece086061892dull,
+    0x3feebfdad5362a27ull, 0x3feeb42b569d4f82ull, 0x3feeab07dd485429ull, 0x3feea47eb03a5585ull,
+    0x3feea09e667f3bcdull, 0x3fee9f75e8ec5f74ull, 0x3feea11473eb0187ull, 0x3feea589994cce13ull,
+    0x3feeace5422aa0dbull, 0x3feeb737b0cdc5e5ull, 0x3feec49182a3f090ull, 0x3feed503b23e255dull,
+    0x3feee89f995ad3adull, 0x3feeff76f2fb5e47ull, 0x3fef199bdd85529cull, 0x3fef3720dcef9069ull,
+    0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull};
+
+SMOE_DEVINL float expf_ref(float x) {
+    if (x < -0x1.9fe368p6f) return 0.0f;                 // below: the reference underflows to +0
+    constexpr double N = 32.0;
+    constexpr double C0 = 0x1.c6af84b912394p-5 / N / N / N, C1 = 0x1.ebfce50fac4f3p-3 / N / N,
+                     C2 = 0x1.62e42ff0c52d6p-1 / N;
+    constexpr double InvLn2N = 0x1.71547652b82fep+0 * N, Shift = 0x1.8p+52;
+    const double xd = (double)x;
+    const double kd0 = __fma_rn(InvLn2N, xd, Shift);
+    const uint64_t ki = (uint64_t)__double_as_longlong(kd0);
+    const double kd = __dsub_rn(kd0, Shift);
+    const double r = __fma_rn(InvLn2N, xd, -kd);
+    const uint64_t t = __ldg(&kExp2Tab[ki & 31u]) + (ki << 47);
+    const double sc = __longlong_as_double((long long)t);
+    const double zc = __fma_rn(C0, r, C1);
+    const double r2 = __dmul_rn(r, r);
+    double y = __fma_rn(C2, r, 1.0);
+    y = __fma_rn(zc, r2, y);
+    y = __dmul_rn(y, sc);
+    return __double2float_rn(y);
 }
 
 SMOE_DEVINL uint32_t score_key(float s) {
@@ -224,7 +254,7 @@ k_sample(SamplerArgs a) {
     }
     cl.sync();     // every CTA has read rank 0's s[0] before any e overwrites it
     const float T = P.temperature;
-    // e_v = exp((s_v - max) / T), correctly rounded, in place of s; then the
+    // e_v = exp((s_v - max) / T) as the reference's expf computes it, in place of s; then the
     // reference's sequential fp32 sum of all e_v, reproduced exactly
     const uint32_t C = (L + kSampThreads - 1) / kSampThreads;
     {
@@ -232,7 +262,7 @@ k_sample(SamplerArgs a) {
         float v[kSeqMaxC];                       // independent evaluations, unrolled for ILP
 #pragma unroll
         for (int q = 0; q < kSeqMaxC; ++q)
-            if (q < (int)cnt) v[q] = (float)exp_neg_d((double)__fdiv_rn(__fsub_rn(s[c0 + q], mx), T));
+            if (q < (int)cnt) v[q] = expf_ref(__fdiv_rn(__fsub_rn(s[c0 + q], mx), T));
 #pragma unroll
         for (int q = 0; q < kSeqMaxC; ++q)
             if (q < (int)cnt) s[c0 + q] = v[q];

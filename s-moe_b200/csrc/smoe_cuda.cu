@@ -471,6 +471,26 @@ int smoe_cuda_synchronize(SmoeCudaCtx* c) {
 
 uint64_t smoe_cuda_kernel_dispatches(const SmoeCudaCtx* c) { return c ? c->dispatches.load() : 0; }
 
+}  // extern "C"
+
+namespace smoe {
+__global__ void k_expf_ref(const float* x, float* y, uint32_t n) {
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+        y[i] = expf_ref(x[i]);
+}
+}  // namespace smoe
+
+extern "C" {
+
+// Test aid, not part of the public header: the sampler's e = expf(x)
+// (expf_ref of sampler.cuh) over n device floats, on `stream`.
+int smoe_cuda_debug_expf(const float* x, float* y, uint32_t n, void* stream) {
+    if (!x || !y) return SMOE_ERR_ARG;
+    const uint32_t blocks = n / 256 + 1 < 148u * 16u ? n / 256 + 1 : 148u * 16u;
+    smoe::k_expf_ref<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, y, n);
+    return cudaGetLastError() == cudaSuccess ? SMOE_OK : SMOE_ERR_CUDA;
+}
+
 // Profiling aid, not part of the public header: record per-CTA phase
 // timestamps of the fused layer kernel into `buf` ([num_SMs x 8] u64, device;
 // NULL turns it off).

@@ -153,6 +153,7 @@ def lib():
         L.smoe_cuda_tiled_expert_bytes.argtypes = [u32, u32, u32]
         L.smoe_cuda_tiled_expert_bytes.restype = u64
         L.smoe_cuda_prepack_layer.argtypes = [vp, C.POINTER(MoeLayer), vp, u64, C.POINTER(MoeLayer)]
+        L.smoe_cuda_debug_expf.argtypes = [vp, vp, u32, vp]
         L.smoe_cuda_canonical_from_u32.argtypes = [u32]
         L.smoe_cuda_canonical_from_u32.restype = f32
         _lib = L

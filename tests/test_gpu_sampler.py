@@ -108,3 +108,42 @@ def test_sampler_edge_cases(ctx):
         tok, _ = gpu_sample(ctx, l[None, :], [p], np.zeros((1, 1), np.uint32))
         T, tp, k, r, u, hl = p
         assert tok[0] == O.sample_token(l.copy(), T, tp, k, r, np.zeros(0, np.uint32), u), p
+
+
+def test_sampler_expf_equals_reference_expf(ctx):
+    """The kernel's e = expf(x) against the restated glibc expf (itself equal
+    to the host libm on every float, test_oracle.py) on 4M floats spread over
+    the sampler's domain [-104, 0] plus the boundaries."""
+    bits = np.linspace(0x80000000, 0xC2D00000, 1 << 22).astype(np.uint64).astype(np.uint32)
+    extra = np.array([0x80000000, 0x00000000, 0xC2CFF1B4, 0xC2CFF1B5, 0xC2CFF1B3, 0xFF800000,
+                      0xC2AEAC50, 0xC2AEAC4F, 0xBF800000, 0xB3800000], np.uint32)
+    x = np.concatenate([bits, extra]).view(np.float32)
+    y = torch.empty(x.size, dtype=torch.float32, device="cuda")
+    dx = dev(x)
+    stream = torch.cuda.current_stream().cuda_stream
+    assert S.lib().smoe_cuda_debug_expf(dx.data_ptr(), y.data_ptr(), x.size, stream) == 0
+    torch.cuda.synchronize()
+    got = y.cpu().numpy()
+    ref = O.expf_ref(x)
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), \
+        np.nonzero(got.view(np.uint32) != ref.view(np.uint32))[0][:10]
+
+
+@pytest.mark.skipif(not O.ref_available(), reason="reference sampler not compiled")
+def test_sampler_config0_10000_seeds_vs_compiled_reference(ctx):
+    """Config 0, 10,000 seeds: the token of the kernel against the reference's
+    own compiled sample_token (sampler.hpp, std::mt19937 fed the same 32-bit
+    draw). Every token must be identical (exact-match rate 1.0)."""
+    B, total, mism = 250, 10_000, []
+    for c0 in range(0, total, B):
+        seeds = range(20_000 + c0, 20_000 + c0 + B)
+        logits = np.stack([O.normal_f32(s, 1, V, 0.0, 2.0) for s in seeds])
+        hist = np.stack([O.random_ids(s, 2, 64, V) for s in seeds])
+        words = [int(O.random_ids(s, 3, 1, 1 << 24)[0]) << 8 for s in seeds]
+        params = [(0.7, 0.8, 20, 1.1, O.canonical_from_word(w), 64) for w in words]
+        tok, _ = gpu_sample(ctx, logits, params, hist)
+        for i, s in enumerate(seeds):
+            ref = O.ref_sample_token(logits[i].copy(), 0.7, 0.8, 20, 1.1, hist[i], words[i])
+            if int(tok[i]) != int(ref):
+                mism.append(s)
+    assert not mism, f"exact-match rate {(total - len(mism)) / total:.5f}; seeds {mism[:10]}"

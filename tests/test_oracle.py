@@ -105,3 +105,14 @@ def test_moe_layer_combine_order():
         ye = O.expert_ffn(O.FMT_AFFINE_Q4, arena[ids[j]], d, dff, x)
         ref = ref + np.float32(w[j]) * ye
     np.testing.assert_allclose(out, ref, rtol=0, atol=0)
+
+
+def test_expf_restatement_equals_host_libm_everywhere():
+    """The sampler's e = expf(x) (sampler.hpp:116): the restated glibc
+    algorithm equals this host's libm expf on every float in [-104, 88]
+    (2.2e9 inputs; below -103.97 both give +0). The CUDA sampler performs the
+    same IEEE operations, so its e values are the reference's."""
+    neg_lo, neg_hi = 0x80000000, 0xC2D00000          # -0 .. -104
+    pos_lo, pos_hi = 0x00000000, 0x42B00000          # +0 .. 88
+    assert O.expf_mismatches(neg_lo, neg_hi) == 0
+    assert O.expf_mismatches(pos_lo, pos_hi) == 0
