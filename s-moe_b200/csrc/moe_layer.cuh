@@ -49,9 +49,11 @@
 // rank order and writes y. x is published by rank 0 (release flag) and read
 // by the others with peer loads. No TMA or bulk copy touches peer memory.
 //
-// Every wait is bounded by a %globaltimer deadline (LayerArgs.wait_ns after
-// the kernel starts); a wait that runs out sets the error word and the
-// kernel carries on to its end, so the host sees SMOE_ERR_DEVICE and the
+// Every wait is bounded by %globaltimer: LayerArgs.wait_ns from its own
+// start, and the whole kernel by 8 x wait_ns. A wait that runs out sets the
+// error word and the kernel carries on to its end with whatever shared state
+// it has - every index read back from that state is clamped to its valid
+// range before it forms an address - so the host sees SMOE_ERR_DEVICE and the
 // context stays usable.
 #pragma once
 #include "ffn_q4.cuh"
@@ -184,7 +186,8 @@ SMOE_DEVINL void red_rel_gpu(uint32_t* p, uint32_t v) {
 // Bounded waits for a counter that other CTAs (gpu scope) or other GPUs
 // (sys scope) advance with release operations; false when the deadline passes.
 template <bool kSys>
-SMOE_DEVINL bool spin_geq(const uint32_t* p, uint32_t target, uint64_t deadline) {
+SMOE_DEVINL bool spin_geq(const uint32_t* p, uint32_t target, const WaitBudget& wb) {
+    const uint64_t deadline = wb.deadline();
     for (uint32_t i = 0; i < SMOE_SPIN_LIMIT; ++i) {
         if ((kSys ? ld_acq_sys(p) : ld_acq_gpu(p)) >= target) return true;
         if ((i & 7) == 7 && gtimer() > deadline) return false;
@@ -337,7 +340,9 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
     ltrace(A.trace, 0);
     // inputs (x, routing) may come from the previous kernel in the stream
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    const uint64_t deadline = gtimer() + A.wait_ns;
+    ltrace(A.trace, 10);
+    // every wait: A.wait_ns from its start, the whole kernel at most 8 x that
+    const WaitBudget wb{A.wait_ns, gtimer() + 8 * A.wait_ns};
     const LayerEp& ep = A.ep;
     const bool epm = ep.world > 1;
     const uint32_t epoch = epm ? A.st->epoch + 1u : 0u;           // written by the previous launch only
@@ -349,7 +354,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
             for (size_t i = tid; i < xbytes / 16; i += blockDim.x)
                 reinterpret_cast<uint4*>(ep.x0)[i] = reinterpret_cast<const uint4*>(A.x)[i];
         } else if (ep.rank > 0) {
-            if (tid == 0 && !spin_geq<true>(ep.flag0, epoch, deadline)) raise_err(A.err, SMOE_DEVERR_SPIN_TIMEOUT);
+            if (tid == 0 && !spin_geq<true>(ep.flag0, epoch, wb)) raise_err(A.err, SMOE_DEVERR_SPIN_TIMEOUT);
             xsrc = ep.x0;
         }
     }
@@ -368,6 +373,10 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         }
         mbar_init(routed, 1);
         fence_mbar_init();
+        // empty routing until it is known (a wait that runs out then finds
+        // nothing to do rather than stale shared memory)
+        *s_nloc = 0;
+        for (int t = 0; t <= kLMaxTok; ++t) s_tok[t] = 0;
     }
     __syncthreads();              // (ranks > 0: rank 0's x is published; rank 0 CTA 0: x0 is written)
     if (epm && ep.rank == 0 && cta == 0 && tid == 0) {
@@ -377,15 +386,25 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
 
     // The CTA's share of the A units [a0, a1) and the B units [b0, b1), known
     // once the routing (and so the local slot list) is.
+    // Everything read back from the routing state is clamped to its valid
+    // range before it forms an address: after a wait that ran out, the state
+    // may be half written.
+    auto nloc = [&]() { return min(*s_nloc, nslots); };
+    auto slot_at = [&](uint32_t li) { return min(s_loc[li], nslots - 1u); };
+    auto tok_at = [&](int t) { return min(s_tok[t], nloc()); };
     auto a_range = [&](int& a0, int& a1) {
-        const int nA = int(*s_nloc) * g.tilesU;
+        const int nA = int(nloc()) * g.tilesU;
         a0 = int(int64_t(cta) * nA / ncta);
         a1 = int(int64_t(cta + 1) * nA / ncta);
     };
     const int nB = g.ntok * g.outTiles;
     const int b0 = int(int64_t(cta) * nB / ncta), b1 = int(int64_t(cta + 1) * nB / ncta);
     // expert blob of a slot (its id is local: the slot is in s_loc)
-    auto expert_of = [&](uint32_t slot) { return A.base + uint64_t(s_ids[slot] - ep.base) * A.stride; };
+    auto expert_of = [&](uint32_t slot) {
+        uint32_t e = s_ids[slot] - ep.base;
+        if (e >= ep.nlocal) e = 0;
+        return A.base + uint64_t(e) * A.stride;
+    };
     // local slot list and per-token starts (one warp, after s_ids is final)
     auto finish_routing = [&]() {
         uint32_t cnt = 0;
@@ -417,40 +436,44 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         int nBi = 0;
         for (int b = b0; b < b1; ++b) {
             const int t = b / g.outTiles;
-            nBi += int(s_tok[t + 1] - s_tok[t]);
+            nBi += max(int(tok_at(t + 1)) - int(tok_at(t)), 0);
         }
         int iA = 0, iB = 0, bb = b0, jj = 0;
         auto issueA = [&]() {
             const int st = iA % NA, r = iA / NA;
-            if (r > 0 && !mbar_wait_dl(emptyA + st, (r - 1) & 1, deadline)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+            if (r > 0 && !mbar_wait_b(emptyA + st, (r - 1) & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
             const int a = a0 + iA / int(tg.nchunk), c = iA % int(tg.nchunk);
-            const uint32_t slot = s_loc[a / g.tilesU];
+            const uint32_t slot = slot_at(uint32_t(a / g.tilesU));
             mbar_arrive_expect_tx(fullA + st, tg.chunk);
             bulk_g2s(ringA + size_t(st) * g.stageA(), expert_of(slot) + tg.chunk_off(a % g.tilesU, c), tg.chunk,
                      fullA + st);
             ++iA;
         };
-        auto issueB = [&]() {
+        auto issueB = [&]() -> bool {
             int t = bb / g.outTiles;
-            while (jj >= int(s_tok[t + 1])) {         // next B unit (skip tokens without local slots)
+            while (jj >= int(tok_at(t + 1)) && bb < b1) {   // next B unit (skip tokens without local slots)
                 ++bb;
                 t = bb / g.outTiles;
-                jj = int(s_tok[t]);
+                jj = int(tok_at(t));
             }
+            if (bb >= b1) return false;
             const int st = iB % NB, r = iB / NB;
-            if (r > 0 && !mbar_wait_dl(emptyB + st, (r - 1) & 1, deadline)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
-            const uint32_t slot = s_loc[jj];
+            if (r > 0 && !mbar_wait_b(emptyB + st, (r - 1) & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+            const uint32_t slot = slot_at(uint32_t(jj));
             mbar_arrive_expect_tx(fullB + st, tg.btile);
             bulk_g2s(ringB + size_t(st) * g.stageB(), expert_of(slot) + tg.btile_off(bb % g.outTiles), tg.btile,
                      fullB + st);
             ++jj;
             ++iB;
+            return true;
         };
-        if (b0 < b1) jj = int(s_tok[b0 / g.outTiles]);
+        if (b0 < b1) jj = int(tok_at(b0 / g.outTiles));
+        ltrace(A.trace, 11, true);
         while (iA < nAi && iA < NA) issueA();
-        while (iB < nBi && iB < NB) issueB();
+        while (iB < nBi && iB < NB && issueB()) {}
         while (iA < nAi) issueA();
-        while (iB < nBi) issueB();
+        while (iB < nBi && issueB()) {}
+        ltrace(A.trace, 12, true);
     };
 
     // ------------------------------------------------------------- routing
@@ -473,7 +496,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         }
         ltrace(A.trace, 1);
         if (warp == kLHWarp) {
-            if (lane == 0 && !spin_geq<false>(&A.st->rdone, rows, deadline)) raise_err(A.err, SMOE_DEVERR_SPIN_TIMEOUT);
+            if (lane == 0 && !spin_geq<false>(&A.st->rdone, rows, wb)) raise_err(A.err, SMOE_DEVERR_SPIN_TIMEOUT);
             __syncwarp();
             for (int t = 0; t < g.ntok; ++t) {
                 warp_topk(A.logits + size_t(t) * A.n_experts, A.n_experts, k, A.norm, s_ids + t * k, s_w + t * k, lane);
@@ -510,7 +533,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
     }
     if (A.rw && warp == kLProdWarp) {
         if (lane == 0) {
-            if (!mbar_wait_dl(routed, 0, deadline)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+            if (!mbar_wait_b(routed, 0, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
             produce();
         }
         __syncwarp();
@@ -521,19 +544,19 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         build_xtab<FMT>(xsrc, A.x_dtype, g.ntok, d, xtab, xg, tid);
         cons_sync();
         ltrace(A.trace, 3);
-        if (!mbar_wait_dl(routed, 0, deadline)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+        if (!mbar_wait_b(routed, 0, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
         int a0, a1;
         a_range(a0, a1);
         const int gr = lane >> 2, cq = lane & 3;
         int iA = 0;
         for (int a = a0; a < a1; ++a) {
             const int n = a - a0, b = n & 1;
-            const uint32_t slot = s_loc[a / g.tilesU];
+            const uint32_t slot = slot_at(uint32_t(a / g.tilesU));
             const int tok = int(slot) / k;
             float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
             for (int c = 0; c < int(tg.nchunk); ++c, ++iA) {
                 const int st = iA % NA;
-                if (!mbar_wait_dl(fullA + st, (iA / NA) & 1, deadline)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+                if (!mbar_wait_b(fullA + st, (iA / NA) & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
                 if (n == 0 && c == 0) ltrace(A.trace, 4);
                 const uint8_t* sp = ringA + size_t(st) * g.stageA();
                 const uint8_t* sbp = sp + 2 * tg.fragC;          // [gate sb][up sb]
@@ -588,7 +611,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
                 if (lane == 0) mbar_arrive(emptyA + st);          // chunk fully consumed
             }
             // the unit's warp partials -> buffer b (free once the h warp read use n-2)
-            if (n >= 2 && !mbar_wait_dl(redE + b, ((n >> 1) - 1) & 1, deadline))
+            if (n >= 2 && !mbar_wait_b(redE + b, ((n >> 1) - 1) & 1, wb))
                 raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
             float* rb = red + (b * kLCons + warp) * 32;
             if (cq == tok) {
@@ -604,18 +627,16 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
 
         // ------------------------------------------------ phase B
         if (b0 < b1) {
-            if (tid == 0 && !spin_geq<false>(&A.st->arrive, uint32_t(ncta), deadline))
+            if (tid == 0 && !spin_geq<false>(&A.st->arrive, uint32_t(ncta), wb))
                 raise_err(A.err, SMOE_DEVERR_SPIN_TIMEOUT);
             cons_sync();
             ltrace(A.trace, 6);
             const uint32_t M = 0x000F000Fu, OR = 0x43004300u;
-            const uint32_t* codes_dummy = nullptr;
-            (void)codes_dummy;
             uint8_t* hsm = reinterpret_cast<uint8_t*>(xtab);          // the x table is no longer needed
             int cur = -1, iB = 0;
             for (int bu = b0; bu < b1; ++bu) {
                 const int t = bu / g.outTiles, o = bu % g.outTiles;
-                const int ls = int(s_tok[t]), le = int(s_tok[t + 1]);
+                const int ls = int(tok_at(t)), le = max(ls, min(int(tok_at(t + 1)), ls + k));
                 if (t != cur) {
                     // this token's h records (local slots ls..le) into shared memory
                     const uint4* src = reinterpret_cast<const uint4*>(A.hbuf + size_t(ls) * g.tilesU * kHRec);
@@ -637,29 +658,45 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
                     cons_sync();
                     cur = t;
                 }
+                // The token's parts (local slots) stream through the ring in
+                // waves of at most NB: every warp waits for all parts of a
+                // wave, takes its share of the wave's (part, 64-group)
+                // items, then releases all of the wave's stages. (A warp
+                // releases a stage only after that stage's new data arrived,
+                // so its arrival always counts toward the right round.)
                 float y0 = 0.f, y8 = 0.f;
-                for (int jj = ls; jj < le; ++jj, ++iB) {
-                    const int st = iB % NB;
-                    if (!mbar_wait_dl(fullB + st, (iB / NB) & 1, deadline)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
-                    const uint8_t* sp = ringB + size_t(st) * g.stageB();
-                    const uint32_t* cw = reinterpret_cast<const uint32_t*>(sp);
-                    const uint8_t* sbp = sp + tg.bcodes;
-                    const uint8_t* hr = hsm + size_t(jj - ls) * g.tilesU * kHRec;
-                    for (int us = warp; us < g.tilesU; us += kLCons) {
-                        const uint32_t wv = cw[us * 32 + lane];
-                        uint32_t a[4];
-                        a[0] = lop3_and_or(wv, M, OR);
-                        a[1] = lop3_and_or(wv >> 4, M, OR);
-                        a[2] = lop3_and_or(wv >> 8, M, OR);
-                        a[3] = lop3_and_or(wv >> 12, M, OR);
-                        const uint8_t* rec = hr + us * kHRec;
-                        const uint2 bv = lane < 8 ? *reinterpret_cast<const uint2*>(rec + 8 * lane) : make_uint2(0u, 0u);
-                        const uint32_t bb[2] = {bv.x, bv.y};
+                for (int w0 = ls; w0 < le; w0 += NB) {
+                    const int W = min(NB, le - w0);
+                    for (int q = 0; q < W; ++q) {
+                        const int ib = iB + q;
+                        if (!mbar_wait_b(fullB + ib % NB, (ib / NB) & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+                    }
+                    if (w0 == ls && bu == b0) ltrace(A.trace, 13);
+                    const int nit = W * int(tg.Gd);
+                    const int i0 = warp * nit / kLCons, i1 = (warp + 1) * nit / kLCons;
+                    for (int it = i0; it < i1; ++it) {
+                        const int q = it / int(tg.Gd), grp = it - q * int(tg.Gd);
+                        const uint8_t* sp = ringB + size_t((iB + q) % NB) * g.stageB();
+                        const uint32_t* cw = reinterpret_cast<const uint32_t*>(sp) + grp * 4 * 32 + lane;
+                        const uint8_t* hr = hsm + (size_t(w0 + q - ls) * g.tilesU + grp * 4) * kHRec;
                         float dd[4] = {0.f, 0.f, 0.f, 0.f};
-                        mma_bf16_16816(dd, a, bb);
+                        float hs = 0.f;
+#pragma unroll
+                        for (int s4 = 0; s4 < 4; ++s4) {             // the group's four 16-column k-steps
+                            const uint32_t wv = cw[s4 * 32];
+                            uint32_t a[4];
+                            a[0] = lop3_and_or(wv, M, OR);
+                            a[1] = lop3_and_or(wv >> 4, M, OR);
+                            a[2] = lop3_and_or(wv >> 8, M, OR);
+                            a[3] = lop3_and_or(wv >> 12, M, OR);
+                            const uint8_t* rec = hr + s4 * kHRec;
+                            const uint2 bv = lane < 8 ? *reinterpret_cast<const uint2*>(rec + 8 * lane) : make_uint2(0u, 0u);
+                            const uint32_t bb[2] = {bv.x, bv.y};
+                            hs += *reinterpret_cast<const float*>(rec + 64);
+                            mma_bf16_16816(dd, a, bb);
+                        }
                         if (cq == 0) {
-                            const float hs = *reinterpret_cast<const float*>(rec + 64);
-                            const int grp = us >> 2;
+                            const uint8_t* sbp = sp + tg.bcodes;
                             const float q0 = fmaf(-128.0f, hs, dd[0] + dd[1]);
                             const float q8 = fmaf(-128.0f, hs, dd[2] + dd[3]);
                             if (FMT == kFmtAffine) {
@@ -675,7 +712,9 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
                         }
                     }
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(emptyB + st);
+                    if (lane == 0)
+                        for (int q = 0; q < W; ++q) mbar_arrive(emptyB + (iB + q) % NB);
+                    iB += W;
                 }
                 if (cq == 0) {
                     red2[warp * 16 + gr] = y0;
@@ -695,7 +734,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
                         if (tid == 0) atomicAdd_system(ep.cnt0 + bu, 1u);
                         write = false;
                     } else if (epm) {
-                        if (tid == 0 && !spin_geq<true>(ep.cnt0 + bu, uint32_t(ep.world - 1), deadline))
+                        if (tid == 0 && !spin_geq<true>(ep.cnt0 + bu, uint32_t(ep.world - 1), wb))
                             raise_err(A.err, SMOE_DEVERR_SPIN_TIMEOUT);
                         __syncwarp(0xffffu);
                         for (int r = 1; r < ep.world; ++r) s += __ldcv(ep.part0 + size_t(r) * ep.part_stride + yi);
@@ -713,14 +752,14 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         }
     } else if (warp == kLHWarp) {
         // ------------------------------------------------ h warp
-        if (!mbar_wait_dl(routed, 0, deadline)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+        if (!mbar_wait_b(routed, 0, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
         int a0, a1;
         a_range(a0, a1);
         for (int a = a0; a < a1; ++a) {
             const int n = a - a0, b = n & 1;
             const uint32_t li = uint32_t(a / g.tilesU), u = uint32_t(a % g.tilesU);
-            const uint32_t slot = s_loc[li];
-            if (!mbar_wait_dl(redF + b, (n >> 1) & 1, deadline)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+            const uint32_t slot = slot_at(li);
+            if (!mbar_wait_b(redF + b, (n >> 1) & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
             const float* rb = red + b * kLCons * 32;
             float v = 0.f;                                        // lane = (matrix, row)
 #pragma unroll
@@ -747,8 +786,9 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
                 *reinterpret_cast<uint2*>(rec + 8 * lane) = make_uint2(pack_bf16x2(e[0], e[1]), pack_bf16x2(e[2], e[3]));
             if (lane == 8) *reinterpret_cast<float*>(rec + 64) = part;
         }
-        // phase A of this CTA is done: publish (release) for phase B of all CTAs
-        __threadfence();
+        // phase A of this CTA is done: publish for phase B of all CTAs (the
+        // warp barrier orders every lane's record stores before lane 0's
+        // gpu-scope release)
         __syncwarp();
         if (lane == 0) red_rel_gpu(&A.st->arrive, 1u);
         ltrace(A.trace, 8, lane == 0);

@@ -136,8 +136,18 @@ static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parit
 SMOE_DEVINL bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
     return mbar_try_wait(bar, parity) || mbar_wait_slow(bar, parity);
 }
-SMOE_DEVINL bool mbar_wait_dl(uint64_t* bar, uint32_t parity, uint64_t deadline) {
-    return mbar_try_wait(bar, parity) || mbar_wait_until(bar, parity, deadline);
+// Budget of one wait: `ns` from when the wait starts, but never past `cap`
+// (an absolute limit for the whole kernel). A wait that ran out thus does
+// not use up the budget of the waits after it, and the kernel still ends.
+struct WaitBudget {
+    uint64_t ns, cap;
+    SMOE_DEVINL uint64_t deadline() const {
+        const uint64_t t = gtimer() + ns;
+        return t < cap ? t : cap;
+    }
+};
+SMOE_DEVINL bool mbar_wait_b(uint64_t* bar, uint32_t parity, const WaitBudget& w) {
+    return mbar_try_wait(bar, parity) || mbar_wait_until(bar, parity, w.deadline());
 }
 
 // 1-D bulk copy global -> shared, completion counted on `bar` (bytes).

@@ -79,10 +79,10 @@ def test_noalloc_matches_context_entry_two_calls(fmt):
 
 def test_noalloc_at_the_scratch_limit():
     """batch * k * d_ff == 65536 exactly (the largest call the array serves)."""
-    d, dff, E, k, B = 256, 4096, 16, 16, 1
+    d, dff, E, k, B = 256, 1024, 16, 16, 4
     L = Layer(O.FMT_AFFINE_Q4, E, d, dff, seed=93)
     X = O.normal_f32(93, 9, B * d).reshape(B, d)
-    ids = np.random.default_rng(93).permutation(E)[:k].astype(np.uint32).reshape(B, k)
+    ids = np.stack([np.random.default_rng(93 + t).permutation(E)[:k] for t in range(B)]).astype(np.uint32)
     w = np.random.default_rng(94).random((B, k)).astype(np.float32)
     y = torch.full((B, d), float("nan"), dtype=torch.float32, device="cuda")
     rc, msg = noalloc(L.desc, dev(X), S.DTYPE_F32, dev(ids), dev(w), k, B, y, S.DTYPE_F32)
@@ -91,7 +91,9 @@ def test_noalloc_at_the_scratch_limit():
     assert rc == S.SMOE_OK, msg
     torch.cuda.synchronize()
     got = y.cpu().numpy()
-    assert rel_err(got[0], oracle_y(L, O.FMT_AFFINE_Q4, X, ids, w, d, dff)[0]) < TIGHT
+    ref = oracle_y(L, O.FMT_AFFINE_Q4, X, ids, w, d, dff)
+    for t in range(B):
+        assert rel_err(got[t], ref[t]) < TIGHT
 
 
 def test_noalloc_reports_device_error_then_recovers():
