@@ -186,8 +186,9 @@ SMOE_DEVINL void red_rel_gpu(uint32_t* p, uint32_t v) {
 // Bounded waits for a counter that other CTAs (gpu scope) or other GPUs
 // (sys scope) advance with release operations; false when the deadline passes.
 template <bool kSys>
-SMOE_DEVINL bool spin_geq(const uint32_t* p, uint32_t target, const WaitBudget& wb) {
+static __device__ __noinline__ bool spin_geq(const uint32_t* p, uint32_t target, const WaitBudget wb) {
     const uint64_t deadline = wb.deadline();
+#pragma unroll 1
     for (uint32_t i = 0; i < SMOE_SPIN_LIMIT; ++i) {
         if ((kSys ? ld_acq_sys(p) : ld_acq_gpu(p)) >= target) return true;
         if ((i & 7) == 7 && gtimer() > deadline) return false;
@@ -233,6 +234,14 @@ SMOE_DEVINL float router_row_part(const LayerArgs& A, const void* xsrc, uint32_t
     return acc;
 }
 
+// v * 2^e for e in [-200, 200] by two exact power-of-two multiplies (the
+// same value ldexpf gives, without its general-case code).
+SMOE_DEVINL float pow2i(int e) { return __int_as_float((127 + e) << 23); }   // e in [-126, 127]
+SMOE_DEVINL float scale2(float v, int e) {
+    const int a = e / 2;
+    return (v * pow2i(a)) * pow2i(e - a);
+}
+
 // x table of the gate/up MMAs, read straight from global x (ntok x K):
 // xtab[(grp*2 + set)*32 + lane] = the four B registers {b(even, k 0-15),
 // b(even, k 16-31), b(odd, k 0-15), b(odd, k 16-31)} of lane 4g + c, and
@@ -243,7 +252,7 @@ SMOE_DEVINL void build_xtab(const void* xsrc, int x_dtype, int ntok, int K, uint
     const int G = K / 64;
     for (int i = ctid; i < G * 64; i += kLCThreads) xtab[i] = make_uint4(0u, 0u, 0u, 0u);
     const int warp = ctid >> 5, lane = ctid & 31;
-    constexpr int U = 4;
+    constexpr int U = 2;
     float v[U][2];
     // first round of loads before the barrier that orders the zeroing
     auto load = [&](int p0) {
@@ -281,13 +290,13 @@ SMOE_DEVINL void build_xtab(const void* xsrc, int x_dtype, int ntok, int K, uint
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
             const int E = m > 0.f ? int((__float_as_uint(m) >> 23) & 0xff) - 127 : 0;
-            const int X0 = __float2int_rn(ldexpf(v0, 20 - E)), X1 = __float2int_rn(ldexpf(v1, 20 - E));
+            const int X0 = __float2int_rn(scale2(v0, 20 - E)), X1 = __float2int_rn(scale2(v1, 20 - E));
             int xs_i = X0 + X1;
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) xs_i += __shfl_xor_sync(0xffffffffu, xs_i, o);
             if (lane == 0) {
-                const float xs = ldexpf(1.0f, E - 24);
-                xg[grp * 4 + t] = make_float2(FMT == kFmtAffine ? xs : xs * (1.0f / 7.5f), ldexpf(float(xs_i), E - 20));
+                const float xs = scale2(1.0f, E - 24);
+                xg[grp * 4 + t] = make_float2(FMT == kFmtAffine ? xs : xs * (1.0f / 7.5f), scale2(float(xs_i), E - 20));
             }
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
@@ -358,6 +367,20 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
             xsrc = ep.x0;
         }
     }
+    // routing given: the producer warp's loads of it are issued before the
+    // set-up barrier, so their latency overlaps it
+    uint32_t pre_id[2] = {0u, 0u};
+    float pre_w[2] = {0.f, 0.f};
+    if (!A.rw && warp == kLProdWarp) {
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            const uint32_t i = lane + 32u * q;
+            if (i < nslots) {
+                pre_id[q] = __ldcg(A.ids_in + i);
+                pre_w[q] = __ldcg(A.wts_in + i);
+            }
+        }
+    }
     if (tid == 0) {
         for (int i = 0; i < kLMaxNA; ++i) {
             mbar_init(fullA + i, 1);
@@ -379,6 +402,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         for (int t = 0; t <= kLMaxTok; ++t) s_tok[t] = 0;
     }
     __syncthreads();              // (ranks > 0: rank 0's x is published; rank 0 CTA 0: x0 is written)
+    ltrace(A.trace, 31);
     if (epm && ep.rank == 0 && cta == 0 && tid == 0) {
         __threadfence_system();
         st_rel_sys(ep.flag0, epoch);
@@ -394,11 +418,12 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
     auto tok_at = [&](int t) { return min(s_tok[t], nloc()); };
     auto a_range = [&](int& a0, int& a1) {
         const int nA = int(nloc()) * g.tilesU;
-        a0 = int(int64_t(cta) * nA / ncta);
-        a1 = int(int64_t(cta + 1) * nA / ncta);
+        a0 = int(uint32_t(cta) * uint32_t(nA) / uint32_t(ncta));      // nA * grid < 2^32
+        a1 = int(uint32_t(cta + 1) * uint32_t(nA) / uint32_t(ncta));
     };
     const int nB = g.ntok * g.outTiles;
-    const int b0 = int(int64_t(cta) * nB / ncta), b1 = int(int64_t(cta + 1) * nB / ncta);
+    const int b0 = int(uint32_t(cta) * uint32_t(nB) / uint32_t(ncta)),
+              b1 = int(uint32_t(cta + 1) * uint32_t(nB) / uint32_t(ncta));
     // expert blob of a slot (its id is local: the slot is in s_loc)
     auto expert_of = [&](uint32_t slot) {
         uint32_t e = s_ids[slot] - ep.base;
@@ -407,6 +432,18 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
     };
     // local slot list and per-token starts (one warp, after s_ids is final)
     auto finish_routing = [&]() {
+        if (!epm) {
+            // single GPU: every slot is local unless its id is bad
+            bool ok = true;
+            for (uint32_t sl = lane; sl < nslots; sl += 32) ok = ok && s_ids[sl] < A.n_experts;
+            if (__all_sync(0xffffffffu, ok)) {
+                for (uint32_t sl = lane; sl < nslots; sl += 32) s_loc[sl] = sl;
+                if (lane <= g.ntok) s_tok[lane] = uint32_t(lane * k);
+                if (lane == 0) *s_nloc = nslots;
+                __syncwarp();
+                return;
+            }
+        }
         uint32_t cnt = 0;
         for (uint32_t s0 = 0; s0 < nslots; s0 += 32) {
             const uint32_t sl = s0 + lane;
@@ -434,45 +471,73 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         a_range(a0, a1);
         const int nAi = (a1 - a0) * int(tg.nchunk);
         int nBi = 0;
-        for (int b = b0; b < b1; ++b) {
-            const int t = b / g.outTiles;
-            nBi += max(int(tok_at(t + 1)) - int(tok_at(t)), 0);
-        }
-        int iA = 0, iB = 0, bb = b0, jj = 0;
-        auto issueA = [&]() {
-            const int st = iA % NA, r = iA / NA;
-            if (r > 0 && !mbar_wait_b(emptyA + st, (r - 1) & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
-            const int a = a0 + iA / int(tg.nchunk), c = iA % int(tg.nchunk);
-            const uint32_t slot = slot_at(uint32_t(a / g.tilesU));
-            mbar_arrive_expect_tx(fullA + st, tg.chunk);
-            bulk_g2s(ringA + size_t(st) * g.stageA(), expert_of(slot) + tg.chunk_off(a % g.tilesU, c), tg.chunk,
-                     fullA + st);
-            ++iA;
-        };
-        auto issueB = [&]() -> bool {
-            int t = bb / g.outTiles;
-            while (jj >= int(tok_at(t + 1)) && bb < b1) {   // next B unit (skip tokens without local slots)
-                ++bb;
-                t = bb / g.outTiles;
-                jj = int(tok_at(t));
+        {
+            int t = b0 / g.outTiles, o = b0 - t * g.outTiles;
+            for (int b = b0; b < b1; ++b) {
+                nBi += max(int(tok_at(t + 1)) - int(tok_at(t)), 0);
+                if (++o == g.outTiles) { o = 0; ++t; }
             }
-            if (bb >= b1) return false;
-            const int st = iB % NB, r = iB / NB;
-            if (r > 0 && !mbar_wait_b(emptyB + st, (r - 1) & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
-            const uint32_t slot = slot_at(uint32_t(jj));
-            mbar_arrive_expect_tx(fullB + st, tg.btile);
-            bulk_g2s(ringB + size_t(st) * g.stageB(), expert_of(slot) + tg.btile_off(bb % g.outTiles), tg.btile,
-                     fullB + st);
-            ++jj;
-            ++iB;
-            return true;
-        };
-        if (b0 < b1) jj = int(tok_at(b0 / g.outTiles));
+        }
+        // One issue site (code size: this runs cold once per launch), and no
+        // integer division in the loop (each costs ~100 cycles of latency on
+        // this lane's critical path): every index advances by counters.
+        // Order: the first NA gate/up chunks, the first NB down parts, then
+        // the rest of each as stages free up.
+        int iA = 0, iB = 0;
+        int ali = a0 / g.tilesU, au = a0 - ali * g.tilesU, ac = 0;          // next A item: (local slot, unit, chunk)
+        int stA = 0, rA = 0, stB = 0, rB = 0;
+        int bt = b0 / g.outTiles, bo = b0 - bt * g.outTiles, bb = b0;     // next B part: (token, tile), slot jj
+        int jj = b0 < b1 ? int(tok_at(bt)) : 0;
         ltrace(A.trace, 11, true);
-        while (iA < nAi && iA < NA) issueA();
-        while (iB < nBi && iB < NB && issueB()) {}
-        while (iA < nAi) issueA();
-        while (iB < nBi && issueB()) {}
+        const int limA0 = min(NA, nAi), limB0 = min(NB, nBi);
+#pragma unroll 1
+        for (int step = 0; step < 4; ++step) {
+#ifdef SMOE_EXP_BFIRST
+            const bool isA = (step & 1) == 1;
+#else
+            const bool isA = (step & 1) == 0;
+#endif
+            const int lim = isA ? (step < 2 ? limA0 : nAi) : (step < 2 ? limB0 : nBi);
+            if (step == 1) ltrace(A.trace, 17, true);
+#pragma unroll 1
+            while ((isA ? iA : iB) < lim) {
+                const int st = isA ? stA : stB, r = isA ? rA : rB;
+                uint64_t* full = (isA ? fullA : fullB) + st;
+                if (r > 0 && !mbar_wait_b((isA ? emptyA : emptyB) + st, (r - 1) & 1, wb))
+                    raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+                uint64_t off;
+                uint32_t slot, bytes;
+                uint8_t* dst;
+                if (isA) {
+                    slot = slot_at(uint32_t(ali));
+                    off = tg.chunk_off(au, ac);
+                    bytes = tg.chunk;
+                    dst = ringA + size_t(st) * g.stageA();
+                    if (++ac == int(tg.nchunk)) {
+                        ac = 0;
+                        if (++au == g.tilesU) { au = 0; ++ali; }
+                    }
+                    ++iA;
+                    if (++stA == NA) { stA = 0; ++rA; }
+                } else {
+                    while (jj >= int(tok_at(bt + 1)) && bb < b1) {   // next B unit (skip tokens without local slots)
+                        ++bb;
+                        if (++bo == g.outTiles) { bo = 0; ++bt; }
+                        jj = int(tok_at(bt));
+                    }
+                    if (bb >= b1) break;
+                    slot = slot_at(uint32_t(jj));
+                    off = tg.btile_off(bo);
+                    bytes = tg.btile;
+                    dst = ringB + size_t(st) * g.stageB();
+                    ++jj;
+                    ++iB;
+                    if (++stB == NB) { stB = 0; ++rB; }
+                }
+                mbar_arrive_expect_tx(full, bytes);
+                bulk_g2s(dst, expert_of(slot) + off, bytes, full);
+            }
+        }
         ltrace(A.trace, 12, true);
     };
 
@@ -480,6 +545,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
     if (A.rw) {
         // logit rows r = cta + i * grid, all consumer warps per row
         const uint32_t rows = A.n_experts * g.ntok;
+        #pragma unroll 1
         for (uint32_t r = cta; r < rows; r += ncta) {
             if (consumer) {
                 const float v = router_row_part(A, xsrc, r / A.n_experts, r % A.n_experts, tid);
@@ -499,7 +565,9 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
             if (lane == 0 && !spin_geq<false>(&A.st->rdone, rows, wb)) raise_err(A.err, SMOE_DEVERR_SPIN_TIMEOUT);
             __syncwarp();
             for (int t = 0; t < g.ntok; ++t) {
-                warp_topk(A.logits + size_t(t) * A.n_experts, A.n_experts, k, A.norm, s_ids + t * k, s_w + t * k, lane);
+                // (the host routes layers of more than 128 experts with k_router)
+                warp_topk_n<4>(A.logits + size_t(t) * A.n_experts, int(A.n_experts), min(uint32_t(k), A.n_experts),
+                               A.norm, s_ids + t * k, s_w + t * k, lane);
                 __syncwarp();
                 if (cta == 0 && lane < k) {
                     if (A.ids_out) A.ids_out[t * k + lane] = s_ids[t * k + lane];
@@ -512,26 +580,29 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
             ltrace(A.trace, 2, lane == 0);
         }
     } else if (warp == kLProdWarp) {
-        // routing given: read it, start the weight stream at once
-        for (uint32_t i = lane; i < nslots; i += 32) {
-            uint32_t id = A.ids_in[i];
-            if (id >= A.n_experts) {
-                raise_err(A.err, SMOE_DEVERR_BAD_EXPERT);      // skipped: never local
-                id = 0xffffffffu;
+        // routing given (loaded above): into shared memory, then start the
+        // weight stream at once
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            const uint32_t i = lane + 32u * q;
+            if (i < nslots) {
+                uint32_t id = pre_id[q];
+                if (id >= A.n_experts) {
+                    raise_err(A.err, SMOE_DEVERR_BAD_EXPERT);      // skipped: never local
+                    id = 0xffffffffu;
+                }
+                s_ids[i] = id;
+                s_w[i] = pre_w[q];
             }
-            s_ids[i] = id;
-            s_w[i] = A.wts_in[i];
         }
         __syncwarp();
+        ltrace(A.trace, 28, lane == 0);
         finish_routing();
-        if (lane == 0) {
-            mbar_arrive(routed);
-            produce();
-        }
-        __syncwarp();
+        ltrace(A.trace, 29, lane == 0);
+        if (lane == 0) mbar_arrive(routed);
         ltrace(A.trace, 2);
     }
-    if (A.rw && warp == kLProdWarp) {
+    if (warp == kLProdWarp) {       // one call site of the producer loop for both modes
         if (lane == 0) {
             if (!mbar_wait_b(routed, 0, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
             produce();
@@ -541,6 +612,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
 
     if (consumer) {
         // ------------------------------------------------ x table, phase A
+        ltrace(A.trace, 30);
         build_xtab<FMT>(xsrc, A.x_dtype, g.ntok, d, xtab, xg, tid);
         cons_sync();
         ltrace(A.trace, 3);
@@ -548,16 +620,22 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         int a0, a1;
         a_range(a0, a1);
         const int gr = lane >> 2, cq = lane & 3;
-        int iA = 0;
+        int iA = 0, stA = 0, rA = 0;
+        int ali = a0 / g.tilesU, au = a0 - ali * g.tilesU;
+        uint32_t slot = slot_at(uint32_t(ali));
+        int tok = int(slot) / k;
+        #pragma unroll 1
         for (int a = a0; a < a1; ++a) {
             const int n = a - a0, b = n & 1;
-            const uint32_t slot = slot_at(uint32_t(a / g.tilesU));
-            const int tok = int(slot) / k;
             float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+            #pragma unroll 1
             for (int c = 0; c < int(tg.nchunk); ++c, ++iA) {
-                const int st = iA % NA;
-                if (!mbar_wait_b(fullA + st, (iA / NA) & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+                const int st = stA;
+                if (!mbar_wait_b(fullA + st, rA & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+                if (++stA == NA) { stA = 0; ++rA; }
                 if (n == 0 && c == 0) ltrace(A.trace, 4);
+                if (iA < 3) ltrace(A.trace, 25 + iA);
+                if (a + 1 == a1 && c + 1 == int(tg.nchunk)) ltrace(A.trace, 14);
                 const uint8_t* sp = ringA + size_t(st) * g.stageA();
                 const uint8_t* sbp = sp + 2 * tg.fragC;          // [gate sb][up sb]
                 uint4 w[GW][2];
@@ -622,26 +700,44 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(redF + b);
+            if (++au == g.tilesU) {
+                au = 0;
+                slot = slot_at(uint32_t(++ali));
+                tok = int(slot) / k;
+            }
         }
         ltrace(A.trace, 5);
 
         // ------------------------------------------------ phase B
         if (b0 < b1) {
+            // the first wave's down parts stream in during phase A: wait for
+            // them before the grid-wide wait, which is the longer one
+            int pre_w = 0;
+            {
+                const int t0 = b0 / g.outTiles, l0 = int(tok_at(t0));
+                pre_w = min(NB, max(l0, min(int(tok_at(t0 + 1)), l0 + k)) - l0);
+                #pragma unroll 1
+                for (int q = 0; q < pre_w; ++q)
+                    if (!mbar_wait_b(fullB + q, 0, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+            }
             if (tid == 0 && !spin_geq<false>(&A.st->arrive, uint32_t(ncta), wb))
                 raise_err(A.err, SMOE_DEVERR_SPIN_TIMEOUT);
             cons_sync();
             ltrace(A.trace, 6);
             const uint32_t M = 0x000F000Fu, OR = 0x43004300u;
             uint8_t* hsm = reinterpret_cast<uint8_t*>(xtab);          // the x table is no longer needed
-            int cur = -1, iB = 0;
+            int cur = -1, stB = 0, rB = 0;
+            int t = b0 / g.outTiles, o = b0 - t * g.outTiles - 1;
+            #pragma unroll 1
             for (int bu = b0; bu < b1; ++bu) {
-                const int t = bu / g.outTiles, o = bu % g.outTiles;
+                if (++o == g.outTiles) { o = 0; ++t; }
                 const int ls = int(tok_at(t)), le = max(ls, min(int(tok_at(t + 1)), ls + k));
                 if (t != cur) {
                     // this token's h records (local slots ls..le) into shared memory
                     const uint4* src = reinterpret_cast<const uint4*>(A.hbuf + size_t(ls) * g.tilesU * kHRec);
                     const int n16 = (le - ls) * g.tilesU * kHRec / 16;
-                    constexpr int U = 8;
+                    constexpr int U = 4;
+#pragma unroll 1
                     for (int base = 0; base < n16; base += U * kLCThreads) {
                         uint4 v[U];
 #pragma unroll
@@ -656,6 +752,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
                         }
                     }
                     cons_sync();
+                    if (cur < 0) ltrace(A.trace, 16);
                     cur = t;
                 }
                 // The token's parts (local slots) stream through the ring in
@@ -665,62 +762,108 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
                 // releases a stage only after that stage's new data arrived,
                 // so its arrival always counts toward the right round.)
                 float y0 = 0.f, y8 = 0.f;
+                #pragma unroll 1
                 for (int w0 = ls; w0 < le; w0 += NB) {
                     const int W = min(NB, le - w0);
-                    for (int q = 0; q < W; ++q) {
-                        const int ib = iB + q;
-                        if (!mbar_wait_b(fullB + ib % NB, (ib / NB) & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+                    if (pre_w > 0) {
+                        pre_w = 0;                    // the first wave: waited for above
+                    } else {
+                        int sb = stB, rb = rB;
+                        #pragma unroll 1
+                        for (int q = 0; q < W; ++q) {
+                            if (!mbar_wait_b(fullB + sb, rb & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+                            if (bu == b0 && w0 == ls && q < 7) ltrace(A.trace, 18 + q);
+                            if (++sb == NB) { sb = 0; ++rb; }
+                        }
                     }
                     if (w0 == ls && bu == b0) ltrace(A.trace, 13);
+                    // this warp's items [i0, i1) of the wave's W x Gd (part, group) items
                     const int nit = W * int(tg.Gd);
-                    const int i0 = warp * nit / kLCons, i1 = (warp + 1) * nit / kLCons;
-                    for (int it = i0; it < i1; ++it) {
-                        const int q = it / int(tg.Gd), grp = it - q * int(tg.Gd);
-                        const uint8_t* sp = ringB + size_t((iB + q) % NB) * g.stageB();
-                        const uint32_t* cw = reinterpret_cast<const uint32_t*>(sp) + grp * 4 * 32 + lane;
-                        const uint8_t* hr = hsm + (size_t(w0 + q - ls) * g.tilesU + grp * 4) * kHRec;
-                        float dd[4] = {0.f, 0.f, 0.f, 0.f};
-                        float hs = 0.f;
+                    const int i0 = (warp * nit) >> 4, i1 = ((warp + 1) * nit) >> 4;   // kLCons == 16
+                    int iq = i0 / int(tg.Gd), ig = i0 - iq * int(tg.Gd);
+                    #pragma unroll 1
+                    for (int it = i0; it < i1; it += 2) {
+                        // two items at once: all their shared-memory operands are
+                        // loaded before the first MMA (latency-bound otherwise)
+                        int qq[2], gg[2];
+                        qq[0] = iq; gg[0] = ig;
+                        if (++ig == int(tg.Gd)) { ig = 0; ++iq; }
+                        qq[1] = iq; gg[1] = ig;
+                        const bool two = it + 1 < i1;
+                        if (two && ++ig == int(tg.Gd)) { ig = 0; ++iq; }
+                        if (!two) { qq[1] = qq[0]; gg[1] = gg[0]; }
+                        uint32_t wv[2][4];
+                        uint2 bv[2][4];
+                        float hs[2] = {0.f, 0.f};
+                        const uint8_t* sp[2];
 #pragma unroll
-                        for (int s4 = 0; s4 < 4; ++s4) {             // the group's four 16-column k-steps
-                            const uint32_t wv = cw[s4 * 32];
-                            uint32_t a[4];
-                            a[0] = lop3_and_or(wv, M, OR);
-                            a[1] = lop3_and_or(wv >> 4, M, OR);
-                            a[2] = lop3_and_or(wv >> 8, M, OR);
-                            a[3] = lop3_and_or(wv >> 12, M, OR);
-                            const uint8_t* rec = hr + s4 * kHRec;
-                            const uint2 bv = lane < 8 ? *reinterpret_cast<const uint2*>(rec + 8 * lane) : make_uint2(0u, 0u);
-                            const uint32_t bb[2] = {bv.x, bv.y};
-                            hs += *reinterpret_cast<const float*>(rec + 64);
-                            mma_bf16_16816(dd, a, bb);
+                        for (int m = 0; m < 2; ++m) {
+                            int sidx = stB + qq[m];
+                            if (sidx >= NB) sidx -= NB;
+                            sp[m] = ringB + size_t(sidx) * g.stageB();
+                            const uint32_t* cw = reinterpret_cast<const uint32_t*>(sp[m]) + gg[m] * 4 * 32 + lane;
+                            const uint8_t* hr = hsm + (size_t(w0 + qq[m] - ls) * g.tilesU + gg[m] * 4) * kHRec;
+#pragma unroll
+                            for (int s4 = 0; s4 < 4; ++s4) {
+                                wv[m][s4] = cw[s4 * 32];
+                                bv[m][s4] = lane < 8 ? *reinterpret_cast<const uint2*>(hr + s4 * kHRec + 8 * lane)
+                                                     : make_uint2(0u, 0u);
+                                hs[m] += *reinterpret_cast<const float*>(hr + s4 * kHRec + 64);
+                            }
+                        }
+                        float dd[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+                        for (int s4 = 0; s4 < 4; ++s4) {             // the groups' four 16-column k-steps
+#pragma unroll
+                            for (int m = 0; m < 2; ++m) {
+                                uint32_t a[4];
+                                a[0] = lop3_and_or(wv[m][s4], M, OR);
+                                a[1] = lop3_and_or(wv[m][s4] >> 4, M, OR);
+                                a[2] = lop3_and_or(wv[m][s4] >> 8, M, OR);
+                                a[3] = lop3_and_or(wv[m][s4] >> 12, M, OR);
+                                const uint32_t bb[2] = {bv[m][s4].x, bv[m][s4].y};
+                                mma_bf16_16816(dd[m], a, bb);
+                            }
                         }
                         if (cq == 0) {
-                            const uint8_t* sbp = sp + tg.bcodes;
-                            const float q0 = fmaf(-128.0f, hs, dd[0] + dd[1]);
-                            const float q8 = fmaf(-128.0f, hs, dd[2] + dd[3]);
-                            if (FMT == kFmtAffine) {
-                                const uint32_t* sbw = reinterpret_cast<const uint32_t*>(sbp) + grp * 16 + gr;
-                                const uint32_t s0 = sbw[0], s8 = sbw[8];
-                                y0 += fmaf(bf16_bits_to_f32(uint16_t(s0)), q0, bf16_bits_to_f32(uint16_t(s0 >> 16)) * hs);
-                                y8 += fmaf(bf16_bits_to_f32(uint16_t(s8)), q8, bf16_bits_to_f32(uint16_t(s8 >> 16)) * hs);
-                            } else {
-                                const uint16_t* sbh = reinterpret_cast<const uint16_t*>(sbp) + grp * 16 + gr;
-                                y0 += f16_bits_to_f32(sbh[0]) * fmaf(q0, 1.0f / 7.5f, -hs);
-                                y8 += f16_bits_to_f32(sbh[8]) * fmaf(q8, 1.0f / 7.5f, -hs);
+#pragma unroll
+                            for (int m = 0; m < 2; ++m) {
+                                if (m == 1 && !two) break;
+                                const uint8_t* sbp = sp[m] + tg.bcodes;
+                                const float h = hs[m];
+                                const float q0 = fmaf(-128.0f, h, dd[m][0] + dd[m][1]);
+                                const float q8 = fmaf(-128.0f, h, dd[m][2] + dd[m][3]);
+                                if (FMT == kFmtAffine) {
+                                    const uint32_t* sbw = reinterpret_cast<const uint32_t*>(sbp) + gg[m] * 16 + gr;
+                                    const uint32_t s0 = sbw[0], s8 = sbw[8];
+                                    y0 += fmaf(bf16_bits_to_f32(uint16_t(s0)), q0, bf16_bits_to_f32(uint16_t(s0 >> 16)) * h);
+                                    y8 += fmaf(bf16_bits_to_f32(uint16_t(s8)), q8, bf16_bits_to_f32(uint16_t(s8 >> 16)) * h);
+                                } else {
+                                    const uint16_t* sbh = reinterpret_cast<const uint16_t*>(sbp) + gg[m] * 16 + gr;
+                                    y0 += f16_bits_to_f32(sbh[0]) * fmaf(q0, 1.0f / 7.5f, -h);
+                                    y8 += f16_bits_to_f32(sbh[8]) * fmaf(q8, 1.0f / 7.5f, -h);
+                                }
                             }
                         }
                     }
                     __syncwarp();
-                    if (lane == 0)
-                        for (int q = 0; q < W; ++q) mbar_arrive(emptyB + (iB + q) % NB);
-                    iB += W;
+                    if (lane == 0) {
+                        int sb = stB;
+                        #pragma unroll 1
+                        for (int q = 0; q < W; ++q) {
+                            mbar_arrive(emptyB + sb);
+                            if (++sb == NB) sb = 0;
+                        }
+                    }
+                    stB += W;                                         // W <= NB
+                    if (stB >= NB) { stB -= NB; ++rB; }
                 }
                 if (cq == 0) {
                     red2[warp * 16 + gr] = y0;
                     red2[warp * 16 + gr + 8] = y8;
                 }
                 cons_sync();
+                if (bu == b0) ltrace(A.trace, 15);
                 if (tid < 16) {                                   // warp 0, lanes 0-15: row 16o + tid
                     float s = 0.f;
 #pragma unroll
@@ -755,9 +898,12 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         if (!mbar_wait_b(routed, 0, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
         int a0, a1;
         a_range(a0, a1);
-        for (int a = a0; a < a1; ++a) {
+        int hli = a0 / g.tilesU, hu = a0 - hli * g.tilesU;
+        #pragma unroll 1
+        for (int a = a0; a < a1; ++a, ++hu) {
+            if (hu == g.tilesU) { hu = 0; ++hli; }
             const int n = a - a0, b = n & 1;
-            const uint32_t li = uint32_t(a / g.tilesU), u = uint32_t(a % g.tilesU);
+            const uint32_t li = uint32_t(hli), u = uint32_t(hu);
             const uint32_t slot = slot_at(li);
             if (!mbar_wait_b(redF + b, (n >> 1) & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
             const float* rb = red + b * kLCons * 32;

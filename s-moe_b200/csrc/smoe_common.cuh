@@ -123,6 +123,7 @@ SMOE_DEVINL bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // and a call each to the hot code instead of a copy of the loop.
 // Bounded by a %globaltimer deadline (absolute, ns).
 static __device__ __noinline__ bool mbar_wait_until(uint64_t* bar, uint32_t parity, uint64_t deadline) {
+#pragma unroll 1
     for (uint32_t i = 0; i < SMOE_SPIN_LIMIT; ++i) {
         if (mbar_try_wait(bar, parity)) return true;   // try_wait itself suspends a while
         if ((i & 15) == 15 && gtimer() > deadline) return false;

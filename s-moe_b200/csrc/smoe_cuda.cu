@@ -267,7 +267,7 @@ struct LayerCall {
 int launch_layer(SmoeCudaCtx* c, const LayerCall& q) {
     const int fmt = int(q.L->fmt & ~uint32_t(SMOE_LAYOUT_TILED));
     if (q.batch > (uint32_t)smoe::kLMaxTok || q.k > (uint32_t)smoe::kLMaxK || q.L->d_ff > c->cfg.max_d_ff ||
-        (q.rw && (q.n_experts > (uint32_t)smoe::kRouterMaxE || q.L->d_model % 8)))
+        (q.rw && (q.n_experts > 128u || q.L->d_model % 8)))
         return SMOE_ERR_UNSUPPORTED;
     if (!aligned16(q.x) || (q.y && !aligned16(q.y))) {            // whole-vector loads
         set_err("layer kernel needs 16-byte aligned x and y %s%ld", "", 0);
@@ -814,9 +814,11 @@ int smoe_cuda_moe_layer(SmoeCudaCtx* c, const SmoeMoeLayer* L, const void* x, in
     if (!c || !L) { set_err("null argument %s%ld", "", 0); return SMOE_ERR_ARG; }
     uint32_t* ids = ids_out ? ids_out : c->ids;
     float* wts = w_out ? w_out : c->wts;
+    // the layer kernel routes in-kernel up to 128 experts (larger routers:
+    // k_router first, then the layer kernel with the routing given)
     if ((L->fmt & SMOE_LAYOUT_TILED) && L->router_w && x && y &&
         aligned16(L->router_w) && L->n_experts >= k && k > 0 && k <= SMOE_MAX_ACTIVE &&
-        L->n_experts <= c->cfg.max_experts && (x_dtype == 0 || x_dtype == 1) &&
+        L->n_experts <= 128u && L->n_experts <= c->cfg.max_experts && (x_dtype == 0 || x_dtype == 1) &&
         (y_dtype == 0 || y_dtype == 1)) {
         smoe::FfnArgs a{};
         int rc = layer_args(c, L, a);
