@@ -7,9 +7,8 @@
 //     router.cuh on all logits (identical results in every CTA);
 //   phase A - gate/up (kernels.metal:240-337): the A units (slot, 16 hidden
 //     rows) are split evenly over the CTAs; each yields
-//     h = silu(Wg.x) * (Wu.x) * w_slot for its 16 rows, stored to a global
-//     scratch record already in the bf16 hi/lo B-fragment order of the down
-//     MMA (64 B) plus the unit's sum of h (4 B);
+//     h = silu(Wg.x) * (Wu.x) * w_slot for its 16 rows, stored as fp32 to a
+//     global scratch record (64 B);
 //   one grid-wide arrive/wait (every CTA is resident: one CTA per SM);
 //   phase B - down + combine (kernels.metal:340-365, decode.cpp:485-499):
 //     the B units (token, 16 output rows) are split evenly over the CTAs;
@@ -36,9 +35,12 @@
 // (AFFINE-Q4) or scale * (sum q x / 7.5 - sum x) (SMOE-Q4, the identity of
 // kernels.metal:136-143), sum x taken over the same fixed-point values. The
 // only roundings are the fixed-point step of x and the fp32 epilogue.
-// Down arithmetic: the codes are ORed into the mantissa of bf16 128.0 (the
-// exact operand 128+q) against h split into bf16 hi + lo columns, fp32
-// accumulate; per 16-column k-step scale * (D - 128 sum h) + bias * sum h.
+// Down arithmetic: the same fixed-point digits, for h: the h warp quantises
+// each 16-row unit (exponent of the unit's max|h|) into three signed byte
+// planes, and the down product runs as integer MMAs m16n8k16 (u8 x s8), one
+// per unit, with the planes in columns 0-2 of B; per unit the exact int32
+// sums are scaled by the unit's 2^(E-20), and per 64-group the fp32 epilogue
+// applies the down matrix's scale (and bias).
 //
 // Expert parallel (world > 1, one process per GPU, experts [r*E/G,
 // (r+1)*E/G) on rank r): every rank routes (the same ids), runs the A units
@@ -71,7 +73,11 @@ constexpr int kLMaxTok = 4;
 constexpr int kLMaxK = 16;
 constexpr int kLMaxNA = 4;                    // gate/up ring stages (at most)
 constexpr int kLMaxNB = 16;                   // down ring stages (at most)
-constexpr int kHRec = 80;                     // bytes per h record: 8 x uint2 fragment + sum + pad
+// h record of one A unit (16 hidden rows), in digit form for the down MMA:
+// [plane 0: 16 B][plane 1][plane 2][xs f32][sum f32][pad 8], X = round(h
+// 2^(20-E)) = p0 + 2^8 p1 + 2^16 p2 with E the exponent of the unit's max|h|,
+// xs = 2^(E-20) (/7.5 for SMOE-Q4), sum = sum X 2^(E-20) (= sum h as seen).
+constexpr int kHRec = 64;
 constexpr int kEpMaxWorld = 8;
 
 struct LayerState {          // device scratch, zero at context creation and after every launch
@@ -164,7 +170,10 @@ struct LayerArgs {
 };
 
 SMOE_DEVINL void ltrace(unsigned long long* tr, int i, bool who = threadIdx.x == 0) {
-    if (tr && who && i < 32) tr[blockIdx.x * 32 + i] = gtimer();
+    if (tr && who && i < 32) {
+        tr[blockIdx.x * 32 + i] = gtimer();
+        tr[(gridDim.x + blockIdx.x) * 32 + i] = clock64();          // same mark in SM cycles
+    }
 }
 
 SMOE_DEVINL uint32_t ld_acq_sys(const uint32_t* p) {
@@ -381,26 +390,25 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
             }
         }
     }
-    if (tid == 0) {
-        for (int i = 0; i < kLMaxNA; ++i) {
-            mbar_init(fullA + i, 1);
-            mbar_init(emptyA + i, kLCons);
-        }
-        for (int i = 0; i < kLMaxNB; ++i) {
-            mbar_init(fullB + i, 1);
-            mbar_init(emptyB + i, kLCons);
-        }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(redF + b, kLCons);
-            mbar_init(redE + b, 1);
-        }
+    // barrier set-up, one barrier per thread of warp 0 and 1
+    if (tid < kLMaxNA) {
+        mbar_init(fullA + tid, 1);
+        mbar_init(emptyA + tid, kLCons);
+    } else if (tid >= 32 && tid < 32 + kLMaxNB) {
+        mbar_init(fullB + (tid - 32), 1);
+        mbar_init(emptyB + (tid - 32), kLCons);
+    } else if (tid >= 8 && tid < 10) {
+        mbar_init(redF + (tid - 8), kLCons);
+        mbar_init(redE + (tid - 8), 1);
+    } else if (tid == 10) {
         mbar_init(routed, 1);
-        fence_mbar_init();
+    } else if (tid == 11) {
         // empty routing until it is known (a wait that runs out then finds
         // nothing to do rather than stale shared memory)
         *s_nloc = 0;
         for (int t = 0; t <= kLMaxTok; ++t) s_tok[t] = 0;
     }
+    if (tid < 64) fence_mbar_init();
     __syncthreads();              // (ranks > 0: rank 0's x is published; rank 0 CTA 0: x0 is written)
     ltrace(A.trace, 31);
     if (epm && ep.rank == 0 && cta == 0 && tid == 0) {
@@ -724,7 +732,6 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
                 raise_err(A.err, SMOE_DEVERR_SPIN_TIMEOUT);
             cons_sync();
             ltrace(A.trace, 6);
-            const uint32_t M = 0x000F000Fu, OR = 0x43004300u;
             uint8_t* hsm = reinterpret_cast<uint8_t*>(xtab);          // the x table is no longer needed
             int cur = -1, stB = 0, rB = 0;
             int t = b0 / g.outTiles, o = b0 - t * g.outTiles - 1;
@@ -734,8 +741,9 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
                 const int ls = int(tok_at(t)), le = max(ls, min(int(tok_at(t + 1)), ls + k));
                 if (t != cur) {
                     // this token's h records (local slots ls..le) into shared memory
+                    if (cur >= 0) cons_sync();                        // the previous token's are done with
                     const uint4* src = reinterpret_cast<const uint4*>(A.hbuf + size_t(ls) * g.tilesU * kHRec);
-                    const int n16 = (le - ls) * g.tilesU * kHRec / 16;
+                    const int n16 = (le - ls) * g.tilesU * (kHRec / 16);
                     constexpr int U = 4;
 #pragma unroll 1
                     for (int base = 0; base < n16; base += U * kLCThreads) {
@@ -772,80 +780,74 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
                         #pragma unroll 1
                         for (int q = 0; q < W; ++q) {
                             if (!mbar_wait_b(fullB + sb, rb & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
-                            if (bu == b0 && w0 == ls && q < 7) ltrace(A.trace, 18 + q);
                             if (++sb == NB) { sb = 0; ++rb; }
                         }
                     }
                     if (w0 == ls && bu == b0) ltrace(A.trace, 13);
+                    const bool tr_items = w0 == ls && bu == b0;
                     // this warp's items [i0, i1) of the wave's W x Gd (part, group) items
                     const int nit = W * int(tg.Gd);
                     const int i0 = (warp * nit) >> 4, i1 = ((warp + 1) * nit) >> 4;   // kLCons == 16
                     int iq = i0 / int(tg.Gd), ig = i0 - iq * int(tg.Gd);
-                    #pragma unroll 1
-                    for (int it = i0; it < i1; it += 2) {
-                        // two items at once: all their shared-memory operands are
-                        // loaded before the first MMA (latency-bound otherwise)
-                        int qq[2], gg[2];
-                        qq[0] = iq; gg[0] = ig;
-                        if (++ig == int(tg.Gd)) { ig = 0; ++iq; }
-                        qq[1] = iq; gg[1] = ig;
-                        const bool two = it + 1 < i1;
-                        if (two && ++ig == int(tg.Gd)) { ig = 0; ++iq; }
-                        if (!two) { qq[1] = qq[0]; gg[1] = gg[0]; }
-                        uint32_t wv[2][4];
-                        uint2 bv[2][4];
-                        float hs[2] = {0.f, 0.f};
-                        const uint8_t* sp[2];
+                    int sidx = stB + iq;
+                    if (sidx >= NB) sidx -= NB;
+                    #pragma unroll 2
+                    for (int it = i0; it < i1; ++it) {
+                        // one (part, 64-group): four int8 MMAs m16n8k16, one per
+                        // 16-column unit, B = the unit's digit planes in columns 0-2
+                        const uint8_t* sp = ringB + size_t(sidx) * g.stageB();
+                        const uint4 wq = *reinterpret_cast<const uint4*>(sp + (ig * 32 + lane) * 16);
+                        const uint8_t* rec0 = hsm + (size_t(w0 + iq - ls) * g.tilesU + ig * 4) * kHRec;
+                        uint32_t bq[4];
+                        float2 xsv[4];
 #pragma unroll
-                        for (int m = 0; m < 2; ++m) {
-                            int sidx = stB + qq[m];
-                            if (sidx >= NB) sidx -= NB;
-                            sp[m] = ringB + size_t(sidx) * g.stageB();
-                            const uint32_t* cw = reinterpret_cast<const uint32_t*>(sp[m]) + gg[m] * 4 * 32 + lane;
-                            const uint8_t* hr = hsm + (size_t(w0 + qq[m] - ls) * g.tilesU + gg[m] * 4) * kHRec;
-#pragma unroll
-                            for (int s4 = 0; s4 < 4; ++s4) {
-                                wv[m][s4] = cw[s4 * 32];
-                                bv[m][s4] = lane < 8 ? *reinterpret_cast<const uint2*>(hr + s4 * kHRec + 8 * lane)
-                                                     : make_uint2(0u, 0u);
-                                hs[m] += *reinterpret_cast<const float*>(hr + s4 * kHRec + 64);
-                            }
+                        for (int u = 0; u < 4; ++u) {
+                            bq[u] = gr < 3 ? *reinterpret_cast<const uint32_t*>(rec0 + u * kHRec + gr * 16 + cq * 4) : 0u;
+                            xsv[u] = *reinterpret_cast<const float2*>(rec0 + u * kHRec + 48);
                         }
-                        float dd[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+                        int dq[4][4];
 #pragma unroll
-                        for (int s4 = 0; s4 < 4; ++s4) {             // the groups' four 16-column k-steps
+                        for (int u = 0; u < 4; ++u) {
+                            const uint32_t mk = (u & 1) ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
+                            const uint32_t a[2] = {(u < 2 ? wq.x : wq.z) & mk, (u < 2 ? wq.y : wq.w) & mk};
+                            dq[u][0] = dq[u][1] = dq[u][2] = dq[u][3] = 0;
+                            mma_u8s8_16816(dq[u], a, bq[u]);
+                        }
+                        // columns 0, 1 (planes p0, p1) are in lane c = 0, column 2 (p2) in c = 1
+                        int p2g[4], p2h[4];
 #pragma unroll
-                            for (int m = 0; m < 2; ++m) {
-                                uint32_t a[4];
-                                a[0] = lop3_and_or(wv[m][s4], M, OR);
-                                a[1] = lop3_and_or(wv[m][s4] >> 4, M, OR);
-                                a[2] = lop3_and_or(wv[m][s4] >> 8, M, OR);
-                                a[3] = lop3_and_or(wv[m][s4] >> 12, M, OR);
-                                const uint32_t bb[2] = {bv[m][s4].x, bv[m][s4].y};
-                                mma_bf16_16816(dd[m], a, bb);
-                            }
+                        for (int u = 0; u < 4; ++u) {
+                            p2g[u] = __shfl_down_sync(0xffffffffu, dq[u][0], 1);
+                            p2h[u] = __shfl_down_sync(0xffffffffu, dq[u][2], 1);
                         }
                         if (cq == 0) {
+                            float s0 = 0.f, s8 = 0.f, sh = 0.f;
 #pragma unroll
-                            for (int m = 0; m < 2; ++m) {
-                                if (m == 1 && !two) break;
-                                const uint8_t* sbp = sp[m] + tg.bcodes;
-                                const float h = hs[m];
-                                const float q0 = fmaf(-128.0f, h, dd[m][0] + dd[m][1]);
-                                const float q8 = fmaf(-128.0f, h, dd[m][2] + dd[m][3]);
-                                if (FMT == kFmtAffine) {
-                                    const uint32_t* sbw = reinterpret_cast<const uint32_t*>(sbp) + gg[m] * 16 + gr;
-                                    const uint32_t s0 = sbw[0], s8 = sbw[8];
-                                    y0 += fmaf(bf16_bits_to_f32(uint16_t(s0)), q0, bf16_bits_to_f32(uint16_t(s0 >> 16)) * h);
-                                    y8 += fmaf(bf16_bits_to_f32(uint16_t(s8)), q8, bf16_bits_to_f32(uint16_t(s8 >> 16)) * h);
-                                } else {
-                                    const uint16_t* sbh = reinterpret_cast<const uint16_t*>(sbp) + gg[m] * 16 + gr;
-                                    y0 += f16_bits_to_f32(sbh[0]) * fmaf(q0, 1.0f / 7.5f, -h);
-                                    y8 += f16_bits_to_f32(sbh[8]) * fmaf(q8, 1.0f / 7.5f, -h);
-                                }
+                            for (int u = 0; u < 4; ++u) {
+                                const float xs = (u & 1) ? xsv[u].x * 0.0625f : xsv[u].x;    // odd units: 16q
+                                s0 = fmaf(fmaf(float(p2g[u]), 65536.0f, float(dq[u][0] + 256 * dq[u][1])), xs, s0);
+                                s8 = fmaf(fmaf(float(p2h[u]), 65536.0f, float(dq[u][2] + 256 * dq[u][3])), xs, s8);
+                                sh += xsv[u].y;
+                            }
+                            const uint8_t* sbp = sp + tg.bcodes;
+                            if (FMT == kFmtAffine) {
+                                const uint32_t* sbw = reinterpret_cast<const uint32_t*>(sbp) + ig * 16 + gr;
+                                const uint32_t w0s = sbw[0], w8s = sbw[8];
+                                y0 += fmaf(bf16_bits_to_f32(uint16_t(w0s)), s0, bf16_bits_to_f32(uint16_t(w0s >> 16)) * sh);
+                                y8 += fmaf(bf16_bits_to_f32(uint16_t(w8s)), s8, bf16_bits_to_f32(uint16_t(w8s >> 16)) * sh);
+                            } else {
+                                const uint16_t* sbh = reinterpret_cast<const uint16_t*>(sbp) + ig * 16 + gr;
+                                y0 += f16_bits_to_f32(sbh[0]) * (s0 - sh);
+                                y8 += f16_bits_to_f32(sbh[8]) * (s8 - sh);
                             }
                         }
+                        if (++ig == int(tg.Gd)) {
+                            ig = 0;
+                            ++iq;
+                            if (++sidx == NB) sidx = 0;
+                        }
                     }
+                    if (tr_items) ltrace(A.trace, 21, lane == 0 && warp == 0);
                     __syncwarp();
                     if (lane == 0) {
                         int sb = stB;
@@ -914,23 +916,28 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
             if (lane == 0) mbar_arrive(redE + b);
             const float up = __shfl_down_sync(0xffffffffu, v, 16);
             const float hv = lane < 16 ? v * (1.0f / (1.0f + expf(-v))) * up * s_w[slot] : 0.f;  // kernels.metal:61-63
-            const float hi = __bfloat162float(__float2bfloat16_rn(hv));
-            float part = hi + __bfloat162float(__float2bfloat16_rn(hv - hi));   // what the MMA sees
+            // digit record of the unit (lanes 0-15 hold its h; 16-31 zero)
+            float m = fabsf(hv);
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-            // B fragment of the down MMA, lanes 0-7 (0-3 hi column, 4-7 lo column):
-            // rows 2c, 2c+1 and 2c+8, 2c+9 of the unit
-            const int c = lane & 3;
-            float e[4] = {__shfl_sync(0xffffffffu, hv, 2 * c), __shfl_sync(0xffffffffu, hv, 2 * c + 1),
-                          __shfl_sync(0xffffffffu, hv, 2 * c + 8), __shfl_sync(0xffffffffu, hv, 2 * c + 9)};
-            if (lane >= 4) {
+            for (int sh = 8; sh > 0; sh >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, sh));
+            const int E = m > 0.f ? int((__float_as_uint(m) >> 23) & 0xff) - 127 : 0;
+            const int X = __float2int_rn(scale2(hv, 20 - E));
+            int sx = X;
 #pragma unroll
-                for (int q = 0; q < 4; ++q) e[q] -= __bfloat162float(__float2bfloat16_rn(e[q]));
-            }
+            for (int sh = 8; sh > 0; sh >>= 1) sx += __shfl_xor_sync(0xffffffffu, sx, sh);
             uint8_t* rec = A.hbuf + (size_t(li) * g.tilesU + u) * kHRec;
-            if (lane < 8)
-                *reinterpret_cast<uint2*>(rec + 8 * lane) = make_uint2(pack_bf16x2(e[0], e[1]), pack_bf16x2(e[2], e[3]));
-            if (lane == 8) *reinterpret_cast<float*>(rec + 64) = part;
+            if (lane < 16) {
+                const int d0 = ((X + 128) & 255) - 128, r = (X - d0) >> 8;
+                const int d1 = ((r + 128) & 255) - 128, d2 = (r - d1) >> 8;
+                rec[lane] = uint8_t(d0);
+                rec[16 + lane] = uint8_t(d1);
+                rec[32 + lane] = uint8_t(d2);
+            }
+            if (lane == 0) {
+                const float xs = scale2(1.0f, E - 20);
+                *reinterpret_cast<float2*>(rec + 48) =
+                    make_float2(FMT == kFmtAffine ? xs : xs * (1.0f / 7.5f), scale2(float(sx), E - 20));
+            }
         }
         // phase A of this CTA is done: publish for phase B of all CTAs (the
         // warp barrier orders every lane's record stores before lane 0's

@@ -12,7 +12,7 @@
 //     chunk c (64-groups c*Gc .. c*Gc+Gc-1 of the input dimension) =
 //       [gate frag][up frag][gate sb][up sb]
 //   B tile o (output rows 16o..16o+15 of down, all d_ff columns) =
-//       [codes: d_ff/16 k-steps x 32 lanes x 32 bits][sb: d_ff/64 groups x 16 rows]
+//       [codes: d_ff/64 groups x 512 B, the frag order below][sb: d_ff/64 groups x 16 rows]
 //
 // nchunk = ceil(G / 32) (G = d_model/64 groups), Gc = G / nchunk: chunks of
 // at most 32 groups (36 KB) so that a few of them fit in shared memory.
@@ -28,12 +28,13 @@
 // sb: per-group scales transposed to [group][16 rows]; AFFINE-Q4 packs
 //   (scale, bias) into one 32-bit word (scale in the low half), SMOE-Q4 holds
 //   the 16-bit scale alone.
-// B codes: k-step s covers hidden columns 16s..16s+15; word L (row g = L/4,
-//   pair c = L%4) holds the codes of rows g and g+8 at columns 2c, 2c+1,
-//   2c+8, 2c+9 of the step in the bit order the kernel unpacks with one mask
-//   per operand register of the bf16 m16n8k16 MMA (bits 0-3/16-19 row g cols
-//   2c/2c+1, 4-7/20-23 row g+8, 8-11/24-27 row g cols 2c+8/2c+9, 12-15/28-31
-//   row g+8). A step is 128 contiguous bytes: conflict-free 32-bit loads.
+// B codes: per 64-group 512 B in the A-fragment order of the integer MMA
+//   m16n8k16 (u8), one MMA per 16-column unit u of the group: lane L = 4g + c
+//   holds 16 B = words {row g, units 0-1}, {row g+8, units 0-1}, {row g,
+//   units 2-3}, {row g+8, units 2-3}; byte b of a word holds the code of
+//   column 16u + 4c + b of the even unit in its low nibble and of the odd unit
+//   in its high nibble, so one mask per register gives q (even unit) or 16q
+//   (odd unit).
 // Byte count equals the vault layout's.
 #pragma once
 #include "smoe_common.cuh"
@@ -117,19 +118,22 @@ __global__ void k_prepack(PrepackArgs a) {
     } else {
         const uint32_t o = blk - t.dff / 16;                // B tile: output rows 16o..16o+15
         uint8_t* p = dexp + t.btile_off(o);
-        uint32_t* codes = reinterpret_cast<uint32_t*>(p);
+        uint4* codes = reinterpret_cast<uint4*>(p);
         const uint8_t* dn = NIB(2);
-        for (uint32_t i = threadIdx.x; i < (t.dff / 16) * 32; i += blockDim.x) {
-            const uint32_t st = i >> 5, L = i & 31, g = L >> 2, c = L & 3;
-            const uint8_t* rg = dn + size_t(o * 16 + g) * (t.dff / 2);
-            const uint8_t* rh = dn + size_t(o * 16 + g + 8) * (t.dff / 2);
-            const uint32_t k0 = st * 16 + 2 * c, k8 = k0 + 8;
-            uint32_t w = 0;
-            w |= nib_at(rg, k0) << 0;       w |= nib_at(rg, k0 + 1) << 16;
-            w |= nib_at(rh, k0) << 4;       w |= nib_at(rh, k0 + 1) << 20;
-            w |= nib_at(rg, k8) << 8;       w |= nib_at(rg, k8 + 1) << 24;
-            w |= nib_at(rh, k8) << 12;      w |= nib_at(rh, k8 + 1) << 28;
-            codes[i] = w;
+        for (uint32_t i = threadIdx.x; i < t.Gd * 32; i += blockDim.x) {
+            const uint32_t gi = i >> 5, L = i & 31, g = L >> 2, c = L & 3;
+            uint32_t w[4];
+            for (int q = 0; q < 4; ++q) {                         // (row g / g+8) x (units 0-1 / 2-3)
+                const uint8_t* row = dn + size_t(o * 16 + g + 8 * (q & 1)) * (t.dff / 2);
+                const uint32_t u0 = 2 * (q >> 1);
+                uint32_t v = 0;
+                for (uint32_t b = 0; b < 4; ++b) {
+                    const uint32_t col = gi * 64 + 4 * c + b;
+                    v |= (nib_at(row, col + 16 * u0) | (nib_at(row, col + 16 * (u0 + 1)) << 4)) << (8 * b);
+                }
+                w[q] = v;
+            }
+            codes[i] = make_uint4(w[0], w[1], w[2], w[3]);
         }
         uint8_t* sb = p + t.bcodes;
         for (uint32_t i = threadIdx.x; i < t.Gd * 16; i += blockDim.x) {
