@@ -317,9 +317,11 @@ def run_ours(args, rank, world, local):
     def e2e_step(i):
         L = descs[i % N_LAYERS]
         if not ep:
-            stage_x.view(torch.int16).copy_(hx[(2000 + i) % 64], non_blocking=True)
-            ctx.moe_layer(L, stage_x, S.DTYPE_BF16, 1, K, True, d_y, S.DTYPE_BF16)
-            hy[i % N_LAYERS].copy_(d_y, non_blocking=True)
+            # the step's x read from pinned host memory and its y written back
+            # into pinned host memory by the library itself (staging kernel in,
+            # direct row stores out; the bytes below cross the host link)
+            ctx.moe_layer(L, hx[(2000 + i) % 64].data_ptr(), S.DTYPE_BF16, 1, K, True,
+                          hy[i % N_LAYERS].data_ptr(), S.DTYPE_BF16)
         elif rank == 0:
             stage_x.view(torch.int16).copy_(hx[(2000 + i) % 64], non_blocking=True)
             ctx.moe_layer_ep(L, E, base, stage_x, S.DTYPE_BF16, 1, K, True, d_y, S.DTYPE_BF16)

@@ -219,7 +219,11 @@ int smoe_cuda_moe_ffn(SmoeCudaCtx* ctx, const SmoeMoeLayer* layer, const void* x
                       uint32_t k, uint32_t batch, void* y, int y_dtype);
 
 /* Router + expert FFN + combine, all on the device. ids_out / w_out
- * (optional, device, [batch x k]) receive the routing. */
+ * (optional, device, [batch x k]) receive the routing. On the tiled layout
+ * (and for smoe_cuda_moe_ffn on it) x and y may also be pinned host memory
+ * (cudaHostAlloc / cudaHostRegister): x is staged by a small copy kernel and
+ * y's rows are stored straight into the host buffer, with no memcpy call;
+ * pageable host memory is rejected with SMOE_ERR_ARG. */
 int smoe_cuda_moe_layer(SmoeCudaCtx* ctx, const SmoeMoeLayer* layer, const void* x,
                         int x_dtype, uint32_t batch, uint32_t k, int norm_topk,
                         void* y, int y_dtype, uint32_t* ids_out, float* w_out);

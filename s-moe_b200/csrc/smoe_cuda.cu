@@ -84,6 +84,19 @@ struct SmoeCudaCtx {
 
 namespace {
 
+// 0: device (or managed) memory, 1: pinned host memory the GPU can address,
+// 2: pageable host memory or unknown.
+int mem_kind(const void* p) {
+    cudaPointerAttributes at{};
+    if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        cudaGetLastError();
+        return 2;
+    }
+    if (at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged) return 0;
+    if (at.type == cudaMemoryTypeHost && at.devicePointer == p) return 1;
+    return 2;
+}
+
 bool is_device_ptr(const void* p) {
     cudaPointerAttributes at{};
     if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
@@ -264,6 +277,15 @@ struct LayerCall {
     const smoe::LayerEp* ep;
 };
 
+}  // namespace
+namespace smoe {
+// One small copy of the caller's x from pinned host memory into device scratch.
+__global__ void k_stage_in(const uint4* __restrict__ src, uint4* __restrict__ dst, uint32_t n16) {
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += gridDim.x * blockDim.x) dst[i] = src[i];
+}
+}  // namespace smoe
+namespace {
+
 int launch_layer(SmoeCudaCtx* c, const LayerCall& q) {
     const int fmt = int(q.L->fmt & ~uint32_t(SMOE_LAYOUT_TILED));
     if (q.batch > (uint32_t)smoe::kLMaxTok || q.k > (uint32_t)smoe::kLMaxK || q.L->d_ff > c->cfg.max_d_ff ||
@@ -276,9 +298,26 @@ int launch_layer(SmoeCudaCtx* c, const LayerCall& q) {
     smoe::LayerArgs A{};
     if (!A.g.init(fmt, (int)q.L->d_model, (int)q.L->d_ff, (int)q.k, (int)q.batch, (int)c->smem_optin - 1024))
         return SMOE_ERR_UNSUPPORTED;
+    // x and y may be pinned host buffers (as the reference's engine passes
+    // them): x is then staged into device scratch by one small copy kernel,
+    // and the layer kernel stores y's rows straight into the host buffer -
+    // no memcpy in between (a memcpy per call costs several microseconds).
+    const void* xin = q.x;
+    const int xk = mem_kind(q.x), yk = q.y ? mem_kind(q.y) : 0;
+    if (xk == 2 || yk == 2) {
+        set_err("layer x / y must be device memory or pinned host memory %s%ld", "", 0);
+        return SMOE_ERR_ARG;
+    }
+    if (xk == 1) {
+        const uint32_t n16 = uint32_t(size_t(q.batch) * q.L->d_model * (q.x_dtype == 0 ? 4 : 2) / 16);
+        smoe::k_stage_in<<<(n16 + 255) / 256 < 16 ? (n16 + 255) / 256 : 16, 256, 0, c->stream>>>(
+            static_cast<const uint4*>(q.x), reinterpret_cast<uint4*>(c->in_stage), n16);
+        c->dispatches += 1;
+        xin = c->in_stage;
+    }
     A.base = q.L->base;
     A.stride = q.L->expert_stride;
-    A.x = q.x; A.x_dtype = q.x_dtype;
+    A.x = xin; A.x_dtype = q.x_dtype;
     A.y = q.y; A.y_dtype = q.y_dtype;
     A.ids_in = q.ids_in; A.wts_in = q.wts_in;
     A.ids_out = q.ids_out; A.wts_out = q.wts_out;

@@ -153,3 +153,27 @@ def test_host_wait_runs_out():
     s.synchronize()
     ctx.synchronize()
     ctx.close()
+
+
+def test_layer_with_pinned_host_x_and_y(ctx):
+    """x and y in pinned host memory (the reference engine's buffers): the
+    library stages x with a copy kernel and stores y's rows into host memory;
+    the result equals the device-buffer call bit for bit. Pageable host
+    memory is refused."""
+    d, dff, E, k = 2048, 768, 32, 8
+    L = Layer(O.FMT_AFFINE_Q4, E, d, dff, seed=211)
+    desc, buf = tiled(ctx, L)
+    xb = O.normal_bf16(211, 5, d)
+    y_dev = torch.zeros(d, dtype=torch.bfloat16, device="cuda")
+    ctx.moe_layer(desc, dev(xb), S.DTYPE_BF16, 1, k, True, y_dev, S.DTYPE_BF16)
+    hx = torch.from_numpy(xb.view(np.int16)).pin_memory()
+    hy = torch.zeros(d, dtype=torch.bfloat16).pin_memory()
+    ctx.moe_layer(desc, hx.data_ptr(), S.DTYPE_BF16, 1, k, True, hy.data_ptr(), S.DTYPE_BF16)
+    ctx.synchronize()
+    assert torch.equal(hy.view(torch.int16), y_dev.cpu().view(torch.int16))
+    ref, _, _ = O.moe_layer(O.FMT_AFFINE_Q4, O.bf16_to_f32(xb), L.router_w, L.arena, L.stride, E, d, dff, k)
+    got = hy.view(torch.int16).numpy().view(np.uint16).astype(np.uint32).__lshift__(16).view(np.float32)
+    assert rel_err(got, ref) < 1e-2
+    pageable = np.zeros(d, np.uint16)
+    with pytest.raises(S.SmoeCudaError):
+        ctx.moe_layer(desc, pageable.ctypes.data, S.DTYPE_BF16, 1, k, True, hy.data_ptr(), S.DTYPE_BF16)
