@@ -1,21 +1,25 @@
-"""Benchmark: one Qwen3-30B-A3B-shaped MoE layer decode step.
-
-A step = router GEMV + softmax/top-8/renorm + fused 4-bit (AFFINE-Q4) SwiGLU
-FFN of the 8 routed experts + weighted combine, batch 1, x bf16[2048] ->
-y bf16[2048], all through the C ABI (libsmoe_cuda.so).
+"""Benchmark: one MoE layer decode step through the C ABI (libsmoe_cuda.so).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-`value`: algorithmic HBM bytes of the layer step (router 524,288 + x 4,096 +
-8 experts x 2,654,208 + y 4,096 = 21,762,144 B) / device time, inputs
-resident. L2 is defeated by cycling through 8 distinct resident layers
-(8 x 340 MB) with a fresh x per step: each step's experts were last touched
-7 steps (>= 150 MB of other traffic) earlier. `e2e`: the same step with x
-copied from pinned host memory and y read back to the host inside the timed
-region. N > 1 (torchrun, one rank per GPU): the same layer step expert-
-parallel - rank r holds experts [r*128/N, (r+1)*128/N) of every layer, x and
-y live on rank 0, and the exchange runs inside the layer kernel over NVLink
-(smoe_cuda_moe_layer_ep); strong scaling, timed as the max over ranks.
+N = 1: BASELINE config 1 - one Qwen3-30B-A3B-shaped layer: router GEMV +
+softmax/top-8/renorm + fused 4-bit (AFFINE-Q4) SwiGLU FFN of the 8 routed
+experts + weighted combine, batch 1, x bf16[2048] -> y bf16[2048].
+N > 1 (torchrun, one rank per GPU): BASELINE config 3's layer - the
+Qwen3-235B-A22B shape (d 4096, d_ff 1536) - expert parallel: rank r holds
+experts [r*128/N, (r+1)*128/N) of every layer, x and y live on rank 0, and the
+exchange runs inside the layer kernel over NVLink (smoe_cuda_moe_layer_ep);
+strong scaling, timed as the max over ranks; rank 0 also times the same layer
+on its own GPU alone (`single_gpu_same_layer`), and the N = 1 line carries
+config 3's 1-GPU point (`config3_layer_1gpu`).
+
+`value`: algorithmic HBM bytes of the layer step (router + x + 8 experts + y;
+config 1: 524,288 + 4,096 + 8 x 2,654,208 + 4,096 = 21,762,144 B) / device
+time, inputs resident. Exactly K steps are timed, as one CUDA-graph replay of
+K layer calls; step i runs resident layer i % L (L = 8 for config 1, 4 for
+config 3, each far beyond L2 in total) on x row i % 64, so every step's
+experts and x are fresh. `e2e`: the same K steps with each step's x read from
+pinned host memory and its y written into pinned host memory by the library.
 """
 from __future__ import annotations
 
@@ -29,14 +33,12 @@ import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "s-moe_b200"))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
 
 D, DFF, E, K = 2048, 768, 128, 8
 N_LAYERS = 8
 LAYER_BYTES = 524_288 + 4_096 + 8 * 2_654_208 + 4_096      # 21,762,144
 FFN_BYTES = 8 * 2_654_208                                    # 21,233,664
-# dram__bytes_read.sum + dram__bytes_write.sum of one k_moe_fused launch on
-# this workload, measured once with ncu (--set full, one launch)
-NCU_TRAFFIC = 21_848_320
 METRIC = "expert-FFN HBM GB/s, Qwen3-30B-A3B MoE layer decode step, batch 1"
 
 
@@ -117,22 +119,43 @@ def barrier(world):
         dist.barrier()
 
 
+SHAPES = {
+    # config 1: one Qwen3-30B-A3B MoE layer
+    "30b": dict(d=2048, dff=768, E=128, k=8, layers=8,
+                workload="config1: Qwen3-30B-A3B MoE layer (d 2048, 128 experts, top-8, d_ff 768, "
+                         "AFFINE-Q4 g64), batch 1, bf16 in/out"),
+    # config 3: one Qwen3-235B-A22B MoE layer, expert parallel over the GPUs
+    "235b": dict(d=4096, dff=1536, E=128, k=8, layers=4,
+                 workload="config3: Qwen3-235B-A22B MoE layer (d 4096, 128 experts, top-8, d_ff 1536, "
+                          "AFFINE-Q4 g64), batch 1, bf16 in/out"),
+}
+
+
+def shape_bytes(sh):
+    """(layer step bytes, expert-FFN bytes) of one batch-1 layer step."""
+    import smoe_cuda as S
+    ffn = sh["k"] * S.expert_bytes(S.FMT_AFFINE_Q4, sh["d"], sh["dff"])
+    return sh["E"] * sh["d"] * 2 + 2 * sh["d"] * 2 + ffn, ffn
+
+
 # ------------------------------------------------------------------ data
-def make_inputs(seed=1234):
+def make_inputs(sh=None, n_layers=None, seed=1234):
+    """CPU copies of the benchmark layers (all experts) and 64 x rows."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import numpy as np
     import oracle as O
+    sh = sh or SHAPES["30b"]
     layers = []
-    for l in range(N_LAYERS):
-        arena, stride, off = O.make_experts(O.FMT_AFFINE_Q4, E, D, DFF, seed=seed + l)
-        rw = O.normal_bf16(seed + l, 6, E * D, 0.0, 0.02)
+    for l in range(n_layers or sh["layers"]):
+        arena, stride, off = O.make_experts(O.FMT_AFFINE_Q4, sh["E"], sh["d"], sh["dff"], seed=seed + l)
+        rw = O.normal_bf16(seed + l, 6, sh["E"] * sh["d"], 0.0, 0.02)
         layers.append((arena, stride, off, rw))
-    xs = np.stack([O.normal_bf16(seed + 7919 + i, 5, D) for i in range(64)])
+    xs = np.stack([O.normal_bf16(seed + 7919 + i, 5, sh["d"]) for i in range(64)])
     return layers, xs
 
 
 # ------------------------------------------------------------ CPU legs
-def cpu_layer_time(layers, xs, budget_s, threads):
+def cpu_layer_time(layers, xs, budget_s, threads, sh=None):
     """Reference router (compiled sampler/top-k/matvec of the reference) +
     the oracle's restated Q4 FFN (there is no reference CPU FFN) + combine."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
@@ -140,6 +163,8 @@ def cpu_layer_time(layers, xs, budget_s, threads):
     import oracle as O
     used = O.set_threads(threads)
     R = O.ref()
+    sh = sh or SHAPES["30b"]
+    E, D, DFF, K = sh["E"], sh["d"], sh["dff"], sh["k"]
     n, t0 = 0, time.perf_counter()
     while True:
         arena, stride, off, rw = layers[n % len(layers)]
@@ -166,25 +191,29 @@ def run_reference(args, rank, world):
     """The reference's own CPU path, timed on this host: its compiled router
     (matvec_bf16 + top_k + renorm, sampler.hpp/scout.cpp/common.hpp built
     unmodified into oracle/_ref) plus the restated Q4 FFN (the reference has
-    no CPU FFN), all host threads. One step = one MoE layer step."""
+    no CPU FFN), all host threads. One step = one MoE layer step of the
+    workload our arm runs at this N (config 1 at N = 1, config 3 at N > 1)."""
     if rank != 0:
         return
-    layers, xs = make_inputs()
+    sh = SHAPES["235b" if world > 1 else "30b"]
+    layer_bytes, _ = shape_bytes(sh)
+    layers, xs = make_inputs(sh, n_layers=2 if world > 1 else None)
     threads = os.cpu_count() or 1
     for i in range(args.warmup):
-        cpu_layer_time(layers, xs, 0.0, threads)
+        cpu_layer_time(layers, xs, 0.0, threads, sh)
     n_total, el_total, used, kind = 0, 0.0, threads, "port"
     for i in range(args.steps):
-        n, el, used, kind = cpu_layer_time(layers, xs, 0.0, threads)   # exactly one layer step
+        n, el, used, kind = cpu_layer_time(layers, xs, 0.0, threads, sh)   # exactly one layer step
         n_total += n
         el_total += el
-    gbs = LAYER_BYTES * n_total / el_total / 1e9
-    line = {"impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s",
+    gbs = layer_bytes * n_total / el_total / 1e9
+    metric = METRIC if world == 1 else METRIC.replace("Qwen3-30B-A3B", "Qwen3-235B-A22B")
+    line = {"impl": "reference", "metric": metric, "value": round(gbs, 3), "unit": "GB/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(1e3 * el_total / n_total, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "config1: Qwen3-30B-A3B MoE layer (d 2048, 128 experts, top-8, "
-                                   "AFFINE-Q4 g64), batch 1", "layers_cycled": N_LAYERS},
+            "scaling": "weak" if world == 1 else "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": sh["workload"], "layers_cycled": len(layers)},
             "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": used, "kind": kind,
                              "sample": f"{n_total} layer steps in {el_total:.2f} s: reference "
                                        "router (compiled from the reference) + restated Q4 FFN, "
@@ -195,32 +224,76 @@ def run_reference(args, rank, world):
 
 
 # -------------------------------------------------------------- GPU arm
-def run_ours(args, rank, world, local):
+def load_layers(ctx, sh, base, per, seed=1234):
+    """sh["layers"] resident layers (experts [base, base+per) of each) in the
+    tiled device layout, with the full router; returns (descs, keep)."""
     import numpy as np
     import torch
+    import oracle as O
     import smoe_cuda as S
-
-    torch.cuda.set_device(local)
-    layers, xs = make_inputs()
-    ctx = S.Context(local)
-    stream = torch.cuda.Stream()
-    ctx.set_stream(stream.cuda_stream)
-    ep = world > 1
-    base, per = S.ep_partition(E, world, rank) if ep else (0, E)
     descs, keep = [], []
-    for arena, stride, off, rw in layers:
-        da = torch.from_numpy(np.ascontiguousarray(arena[base:base + per])).cuda()
+    for l in range(sh["layers"]):
+        arena, stride, off = O.make_experts(O.FMT_AFFINE_Q4, per, sh["d"], sh["dff"], seed + l, first=base)
+        rw = O.normal_bf16(seed + l, 6, sh["E"] * sh["d"], 0.0, 0.02)
+        da = torch.from_numpy(arena).cuda()
         dr = torch.from_numpy(rw.view(np.int16)).cuda()
-        keep += [da, dr]
-        vault = S.make_layer(da, stride, off, per, D, DFF, S.FMT_AFFINE_Q4, dr)
+        vault = S.make_layer(da, stride, off, per, sh["d"], sh["dff"], S.FMT_AFFINE_Q4, dr)
         # one-time load-time re-layout into the tiled device format (the
         # vault-layout copy is dropped afterwards)
-        tstride = S.tiled_stride(S.FMT_AFFINE_Q4, D, DFF)
+        tstride = S.tiled_stride(S.FMT_AFFINE_Q4, sh["d"], sh["dff"])
         tb = torch.empty(per * tstride, dtype=torch.uint8, device="cuda")
         torch.cuda.synchronize()             # the arena was copied on torch's stream
         descs.append(ctx.prepack_layer(vault, tb, tstride))
         ctx.synchronize()
-        keep[-2] = tb
+        keep += [tb, dr]
+        del da
+    return descs, keep
+
+
+def graph_of(stream, calls):
+    import torch
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for c in calls:
+            c()
+    return g
+
+
+def timed_replay(graph, stream, world):
+    """Device time (ms) of one replay, barrier + synchronize on both sides."""
+    import torch
+    barrier(world)
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        t0.record(stream)
+        graph.replay()
+        t1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    return t0.elapsed_time(t1)
+
+
+def run_ours(args, rank, world, local):
+    """N = 1: config 1 (the 30B layer). N > 1: config 3 (the 235B layer),
+    expert parallel - rank r holds experts [r*128/N, (r+1)*128/N) of every
+    layer, x and y live on rank 0, the exchange runs inside the layer kernel
+    over NVLink; rank 0 also times the same layer on its own GPU alone."""
+    import numpy as np
+    import torch
+    import oracle as O
+    import smoe_cuda as S
+
+    torch.cuda.set_device(local)
+    ep = world > 1
+    sh = SHAPES["235b" if ep else "30b"]
+    d, E, K, NL = sh["d"], sh["E"], sh["k"], sh["layers"]
+    layer_bytes, ffn_bytes = shape_bytes(sh)
+    ctx = S.Context(local)
+    stream = torch.cuda.Stream()
+    ctx.set_stream(stream.cuda_stream)
+    base, per = S.ep_partition(E, world, rank) if ep else (0, E)
+    descs, keep = load_layers(ctx, sh, base, per)
     if ep:
         import torch.distributed as dist
         grp = dist.new_group(backend="gloo")
@@ -228,175 +301,183 @@ def run_ours(args, rank, world, local):
         dist.all_gather_object(handles, ctx.ep_export(), group=grp)
         ctx.ep_attach(rank, world, handles)
         barrier(world)
-    d_x = torch.from_numpy(xs.view(np.int16)).cuda()          # [64, D] bf16
-    d_y = torch.zeros(D, dtype=torch.bfloat16, device="cuda")
-    ids = torch.zeros(N_LAYERS, K, dtype=torch.int32, device="cuda")
-    wts = torch.zeros(N_LAYERS, K, dtype=torch.float32, device="cuda")
+    xs = np.stack([O.normal_bf16(1234 + 7919 + i, 5, d) for i in range(64)])
+    d_x = torch.from_numpy(xs.view(np.int16)).cuda()          # [64, d] bf16: a fresh x each step
+    d_y = torch.zeros(d, dtype=torch.bfloat16, device="cuda")
+    ids = torch.zeros(NL, K, dtype=torch.int32, device="cuda")
+    wts = torch.zeros(NL, K, dtype=torch.float32, device="cuda")
     torch.cuda.synchronize()
 
-    def layer(l):      # router + top-k + expert FFN + combine: one fused launch
+    def layer(i, xptr=None, yptr=None):   # router + top-k + expert FFN + combine: one launch
+        l = i % NL
+        x = d_x[i % 64].data_ptr() if xptr is None else xptr
+        y = d_y if yptr is None else yptr
         if ep:
-            ctx.moe_layer_ep(descs[l], E, base, d_x[l].data_ptr() if rank == 0 else None,
-                             S.DTYPE_BF16, 1, K, True, d_y if rank == 0 else None, S.DTYPE_BF16,
-                             ids[l], wts[l])
+            ctx.moe_layer_ep(descs[l], E, base, x if rank == 0 else None, S.DTYPE_BF16, 1, K, True,
+                             y if rank == 0 else None, S.DTYPE_BF16, ids[l], wts[l])
         else:
-            ctx.moe_layer(descs[l], d_x[l].data_ptr(), S.DTYPE_BF16, 1, K, True, d_y, S.DTYPE_BF16,
-                          ids[l], wts[l])
+            ctx.moe_layer(descs[l], x, S.DTYPE_BF16, 1, K, True, y, S.DTYPE_BF16, ids[l], wts[l])
 
-    def ffn(l):        # the same with the routing already on the device
-        ctx.moe_ffn(descs[l], d_x[l].data_ptr(), S.DTYPE_BF16, ids[l], wts[l], K, 1, d_y,
-                    S.DTYPE_BF16)
+    def ffn(i):                           # the same with the routing already on the device
+        l = i % NL
+        ctx.moe_ffn(descs[l], d_x[i % 64].data_ptr(), S.DTYPE_BF16, ids[l], wts[l], K, 1, d_y, S.DTYPE_BF16)
 
-    # eager warm-up (also sets kernel attributes before capture)
-    for i in range(max(args.warmup, 3)):
-        for l in range(N_LAYERS):
-            layer(l)
-            if not ep:
-                ffn(l)
+    W, steps = max(args.warmup, 3), args.steps
+    # eager warm-up (also sets kernel attributes and fills the routing)
+    for i in range(max(W, NL)):
+        layer(i)
     ctx.synchronize()
-    # One graph = one MoE layer step on each of the 8 resident layers.
-    g_step, g_ffn = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g_step, stream=stream):
-        for l in range(N_LAYERS):
-            layer(l)
-    with torch.cuda.graph(g_ffn, stream=stream):
-        for l in range(N_LAYERS):
-            if ep:
-                layer(l)           # routing-given mode is single-GPU: time the layer again
-            else:
-                ffn(l)
-    reps = max(1, args.steps // N_LAYERS)
-    steps = reps * N_LAYERS
+    # exactly `steps` layer steps per graph; step i: layer i % NL, x row i % 64
+    g_warm = graph_of(stream, [lambda i=i: layer(i) for i in range(W)])
+    g_step = graph_of(stream, [lambda i=i: layer(i) for i in range(steps)])
+    g_ffn = None if ep else graph_of(stream, [lambda i=i: ffn(i) for i in range(steps)])
     with torch.cuda.stream(stream):
-        for _ in range(max(args.warmup, 3)):
-            g_step.replay()
-            g_ffn.replay()
+        g_warm.replay()
     torch.cuda.synchronize()
-    barrier(world)
-
-    def timed(graph):
-        barrier(world)
-        torch.cuda.synchronize()
-        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(stream):      # replay() launches on the current stream
-            t0.record(stream)
-            for _ in range(reps):
-                graph.replay()
-            t1.record(stream)
-        torch.cuda.synchronize()
-        barrier(world)
-        return t0.elapsed_time(t1)
-
-    # ---- device-resident timing (CUDA graph replays)
     clocks = Clocks(local)
     clocks.start()
     time.sleep(0.3)
-    d0 = ctx.dispatches()
-    ms = timed(g_step)
-    ffn_ms_total = timed(g_ffn)
-    ck = clocks.stop()
-    launches = steps * 1           # one fused MoE-layer kernel per step (graph replays)
-    ctx.synchronize()
-    ms = max_over_ranks(ms, world)
-    per_step = ms / steps
-    ffn_ms = ffn_ms_total / steps
-    # replicas would be weak scaling; expert parallel splits one layer step
-    value = LAYER_BYTES * steps / (ms * 1e-3) / 1e9
-    args.steps = steps
-    del d0
-
-    # ---- end to end through the C ABI with host buffers: every step copies
-    # its x from pinned host memory, runs the layer call and copies y back.
-    # Single GPU: the calls of the 8 steps are captured once as a CUDA graph
-    # (as a serving loop would drive them) and replayed, so the host's Python
-    # launch overhead is not what is timed; expert parallel: issued eagerly.
-    hx = torch.from_numpy(xs.view(np.int16)).pin_memory()
-    hy = torch.zeros(N_LAYERS, D, dtype=torch.bfloat16).pin_memory()
-    stage_x = torch.zeros(D, dtype=torch.bfloat16, device="cuda")
-
-    def e2e_step(i):
-        L = descs[i % N_LAYERS]
-        if not ep:
-            # the step's x read from pinned host memory and its y written back
-            # into pinned host memory by the library itself (staging kernel in,
-            # direct row stores out; the bytes below cross the host link)
-            ctx.moe_layer(L, hx[(2000 + i) % 64].data_ptr(), S.DTYPE_BF16, 1, K, True,
-                          hy[i % N_LAYERS].data_ptr(), S.DTYPE_BF16)
-        elif rank == 0:
-            stage_x.view(torch.int16).copy_(hx[(2000 + i) % 64], non_blocking=True)
-            ctx.moe_layer_ep(L, E, base, stage_x, S.DTYPE_BF16, 1, K, True, d_y, S.DTYPE_BF16)
-            hy[i % N_LAYERS].copy_(d_y, non_blocking=True)
-        else:
-            ctx.moe_layer_ep(L, E, base, None, S.DTYPE_BF16, 1, K, True, None, S.DTYPE_BF16)
-
+    ms = max_over_ranks(timed_replay(g_step, stream, world), world)
+    ffn_ms = None
     if not ep:
-        g_e2e = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g_e2e, stream=stream):
-            for i in range(N_LAYERS):
-                e2e_step(i)
         with torch.cuda.stream(stream):
-            for _ in range(3):
-                g_e2e.replay()
-        torch.cuda.synchronize()
-        e2e_ms = timed(g_e2e)
-        e2e_steps = reps * N_LAYERS
-    else:
-        barrier(world)
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
+            g_ffn.replay()                     # its own warm-up
+        ffn_ms = timed_replay(g_ffn, stream, world)
+    ck = clocks.stop()
+    per_step = ms / steps
+    value = layer_bytes * steps / (ms * 1e-3) / 1e9
+
+    # ---- end to end through the C ABI with host buffers: every step reads its
+    # x from pinned host memory and writes y into pinned host memory (the
+    # library stages x with a copy kernel and stores y's rows to the host).
+    hx = torch.from_numpy(xs.view(np.int16)).pin_memory()
+    hy = torch.zeros(NL, d, dtype=torch.bfloat16).pin_memory()
+    g_e2e = graph_of(stream, [lambda i=i: layer(i, hx[(2000 + i) % 64].data_ptr(), hy[i % NL].data_ptr())
+                              for i in range(steps)])
+    with torch.cuda.stream(stream):
+        g_e2e.replay()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(timed_replay(g_e2e, stream, world), world)
+    e2e = layer_bytes * steps / (e2e_ms * 1e-3) / 1e9
+
+    single = None
+    if ep and rank == 0:
+        # the same layer on this GPU alone (all 128 experts), for the scaling curve
+        ctx1 = S.Context(local)
+        ctx1.set_stream(stream.cuda_stream)
+        d1, k1 = load_layers(ctx1, sh, 0, E)
+        ids1 = torch.zeros(NL, K, dtype=torch.int32, device="cuda")
+        w1 = torch.zeros(NL, K, dtype=torch.float32, device="cuda")
+        calls = [lambda i=i: ctx1.moe_layer(d1[i % NL], d_x[i % 64].data_ptr(), S.DTYPE_BF16, 1, K, True, d_y,
+                                            S.DTYPE_BF16, ids1[i % NL], w1[i % NL]) for i in range(steps)]
+        for c in calls[:NL]:
+            c()
+        ctx1.synchronize()
+        g1 = graph_of(stream, calls)
         with torch.cuda.stream(stream):
-            for i in range(args.steps):
-                e2e_step(i)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        ctx.synchronize()
-        e2e_ms = e0.elapsed_time(e1)
-        e2e_steps = args.steps
-    e2e_ms = max_over_ranks(e2e_ms, world)
-    e2e = LAYER_BYTES * e2e_steps / (e2e_ms * 1e-3) / 1e9
+            g1.replay()
+        ms1 = timed_replay(g1, stream, 1)
+        single = {"value": round(layer_bytes * steps / (ms1 * 1e-3) / 1e9, 2), "unit": "GB/s",
+                  "layer_us": round(ms1 / steps * 1e3, 3)}
+        del g1, d1, k1
+        ctx1.close()
 
     if rank == 0:
         peak, peak_kind = peaks()
-        # per GPU: the fused kernel's share of the expert bytes / its time
-        ach = FFN_BYTES / world / (ffn_ms * 1e-3) / 1e9
+        traffic = profile_traffic()
+        if ep:
+            ach = ffn_bytes / world / (per_step * 1e-3) / 1e9
+            kern = (f"k_moe_layer expert parallel x{world} (layer incl. routing and NVLink exchange), "
+                    f"{ffn_bytes // world:,} B of experts per GPU per launch, {per_step * 1e3:.2f} us avg")
+        else:
+            ach = ffn_bytes / (ffn_ms / steps * 1e-3) / 1e9
+            kern = (f"k_moe_layer (expert FFN + combine, routing given), {ffn_bytes:,} B per launch, "
+                    f"{ffn_ms / steps * 1e3:.2f} us avg")
         line = {
-            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step, 5),
+            "metric": METRIC if not ep else METRIC.replace("Qwen3-30B-A3B", "Qwen3-235B-A22B"),
+            "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": steps, "warmup": args.warmup, "ms_per_step": round(per_step, 5),
             "higher_is_better": True, "scaling": "strong" if ep else "weak", "vs_baseline": None,
             "dtype": "bf16",
-            "data": "synthetic (seeded; BASELINE config-1 distributions)",
-            "config": {"workload": "config1: Qwen3-30B-A3B MoE layer (d 2048, 128 experts, "
-                                   "top-8, d_ff 768, AFFINE-Q4 g64), batch 1, bf16 in/out",
-                       "layers_cycled": N_LAYERS, "l2": "inputs larger than L2 (8 resident "
-                       "layers x 340 MB cycled, fresh x per step)",
+            "data": "synthetic (seeded; BASELINE config distributions)",
+            "config": {"workload": sh["workload"], "layers_cycled": NL,
+                       "l2": (f"inputs larger than L2 ({NL} resident layers cycled, a fresh x per step from "
+                              "64 rows)"),
                        "parallelism": (f"expert parallel x{world} ({per} experts per GPU, exchange "
                                        "in-kernel over NVLink)") if ep else "single GPU"},
             "layer_us": round(per_step * 1e3, 3),
             "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(ach / peak, 4), "traffic": None if ep else NCU_TRAFFIC,
-                         "kernel": (f"k_moe_fused expert parallel (layer incl. routing and NVLink "
-                                    f"exchange), {FFN_BYTES // world:,} B of experts per GPU per launch, "
-                                    f"{ffn_ms * 1e3:.2f} us avg") if ep else
-                                   ("k_moe_fused (expert FFN + combine, routing given), 21,233,664 B "
-                                    f"per launch, {ffn_ms * 1e3:.2f} us avg"), "peak_kind": peak_kind},
-            "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": D * 2,
-                    "d2h_bytes_per_step": D * 2},
-            "gpu_launches": int(launches),
+                         "frac": round(ach / peak, 4), "traffic": None if ep else traffic,
+                         "kernel": kern, "peak_kind": peak_kind},
+            "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": d * 2,
+                    "d2h_bytes_per_step": d * 2},
+            "gpu_launches": int(steps),
             "clocks": ck,
         }
+        if single:
+            line["single_gpu_same_layer"] = single
         if world == 1 and not args.no_cpu:
-            n, el, used, kind = cpu_layer_time(layers, xs, args.cpu_seconds, os.cpu_count() or 1)
-            line["cpu_baseline"] = {
-                "value": round(LAYER_BYTES * n / el / 1e9, 4), "unit": "GB/s", "cores": used,
-                "kind": kind, "sample": f"{n} layer steps in {el:.1f} s (reference router + "
-                                        "restated Q4 FFN, OpenMP)"}
+            layers_cpu, xs_cpu = make_inputs(n_layers=4)
+            cpu = {}
+            for label, threads in (("all", os.cpu_count() or 1), ("one", 1)):
+                n, el, used, kind = cpu_layer_time(layers_cpu, xs_cpu, args.cpu_seconds / 2, threads)
+                cpu[label] = {"value": round(LAYER_BYTES * n / el / 1e9, 4), "unit": "GB/s", "cores": used,
+                              "kind": kind, "sample": f"{n} layer steps in {el:.1f} s (reference router + "
+                                                      "restated Q4 FFN, OpenMP)"}
+            line["cpu_baseline"] = cpu["all"]
+            line["cpu_baseline_1core"] = cpu["one"]
         if world == 1 and not args.no_extra:
+            line["config3_layer_1gpu"] = config3_leg(ctx, stream, args)
             line["sampler"] = sampler_leg(ctx, stream)
             line["decode_30b"] = decode_leg(ctx)
             line["batch256"] = batch_leg(ctx, stream)
         print(json.dumps(line), flush=True)
     ctx.close()
+
+
+def config3_leg(ctx, stream, args):
+    """Config 3's layer (Qwen3-235B-A22B shape) on this GPU alone, batch 1:
+    the 1-GPU point of the expert-parallel scaling curve."""
+    import numpy as np
+    import torch
+    import oracle as O
+    import smoe_cuda as S
+    sh = SHAPES["235b"]
+    layer_bytes, _ = shape_bytes(sh)
+    descs, keep = load_layers(ctx, sh, 0, sh["E"])
+    xs = np.stack([O.normal_bf16(99 + i, 5, sh["d"]) for i in range(64)])
+    d_x = torch.from_numpy(xs.view(np.int16)).cuda()
+    d_y = torch.zeros(sh["d"], dtype=torch.bfloat16, device="cuda")
+    steps = 100
+    calls = [lambda i=i: ctx.moe_layer(descs[i % sh["layers"]], d_x[i % 64].data_ptr(), S.DTYPE_BF16, 1, sh["k"],
+                                       True, d_y, S.DTYPE_BF16) for i in range(steps)]
+    for c in calls[:sh["layers"]]:
+        c()
+    ctx.synchronize()
+    g = graph_of(stream, calls)
+    with torch.cuda.stream(stream):
+        g.replay()
+    ms = timed_replay(g, stream, 1)
+    out = {"workload": sh["workload"], "layer_us": round(ms / steps * 1e3, 3),
+           "value": round(layer_bytes * steps / (ms * 1e-3) / 1e9, 2), "unit": "GB/s"}
+    del g, descs, keep
+    torch.cuda.empty_cache()
+    return out
+
+
+def profile_traffic():
+    """dram bytes (read + write) per launch of the layer kernel from the
+    committed ncu summary (profiles/k_moe_layer_config1.md, line
+    'traffic_bytes_per_launch: N'), or None."""
+    p = os.path.join(ROOT, "profiles", "k_moe_layer_config1.md")
+    try:
+        with open(p) as f:
+            for line in f:
+                if line.strip().startswith("traffic_bytes_per_launch:"):
+                    return int(line.split(":")[1].strip().replace(",", ""))
+    except OSError:
+        pass
+    return None
 
 
 def sampler_leg(ctx, stream, reps=50):

@@ -163,17 +163,20 @@ def blob_layout(fmt, d, dff):
     return [int(o) for o in off], int(tot.value)
 
 
-def make_experts(fmt, n_experts, d, dff, seed, blob_align=256):
+def make_experts(fmt, n_experts, d, dff, seed, blob_align=256, first=0):
     """Layer arena of n_experts blobs with the benchmark's distributions.
 
     Nibbles uniform in [0, 15]; AFFINE: scale bf16 ~ U(0.001, 0.01), bias bf16
-    ~ N(0, 0.01^2); SMOE: fp16 scale ~ U(0.001, 0.01). Returns (arena uint8
-    [n_experts, stride], stride, offsets)."""
+    ~ N(0, 0.01^2); SMOE: fp16 scale ~ U(0.001, 0.01). Expert e has its own
+    generator streams, so experts [first, first + n_experts) of a layer are
+    the same whichever range is made. Returns (arena uint8 [n_experts,
+    stride], stride, offsets)."""
     off, tot = blob_layout(fmt, d, dff)
     stride = (tot + blob_align - 1) // blob_align * blob_align
     arena = np.zeros((n_experts, stride), np.uint8)
-    for e in range(n_experts):
-        b = arena[e]
+    for i in range(n_experts):
+        e = first + i
+        b = arena[i]
         for m in range(3):
             rows, cols = (dff, d) if m < 2 else (d, dff)
             nb = rows * cols // 2

@@ -6,7 +6,9 @@ through a gloo group on 127.0.0.1, and runs smoe_cuda_moe_layer_ep. Rank 0
 checks y against the CPU oracle for the whole layer; every rank checks the
 routing. Exit code 0 = pass; the failure is printed otherwise.
 
-    python tests/ep_worker.py RANK WORLD PORT FMT
+    python tests/ep_worker.py RANK WORLD PORT FMT [SHAPE]
+
+SHAPE: 30b (d 2048, d_ff 768; default) or 235b (d 4096, d_ff 1536).
 """
 import os
 import sys
@@ -33,9 +35,10 @@ def rel_err(got, ref) -> float:
 
 def main():
     rank, world, port, fmt = (int(a) for a in sys.argv[1:5])
+    shape = sys.argv[5] if len(sys.argv) > 5 else "30b"
     torch.cuda.set_device(rank)
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
-    d, dff, E, k = 2048, 768, 128, 8
+    d, dff, E, k = (2048, 768, 128, 8) if shape == "30b" else (4096, 1536, 128, 8)
     arena, stride, off = O.make_experts(fmt, E, d, dff, 41)
     router = O.normal_bf16(41, 6, E * d, 0.0, 0.02)
     base, per = S.ep_partition(E, world, rank)
@@ -56,7 +59,7 @@ def main():
     dist.barrier()                           # every rank attached before any launch
 
     failures = []
-    for call in range(3):
+    for call in range(3 if shape == "30b" else 2):
         for B in (1, 3):
             xb = O.normal_bf16(200 + call, 5 + B, B * d)
             x = torch.from_numpy(xb.view(np.int16)).cuda() if rank == 0 else None

@@ -1,5 +1,6 @@
 """GPU parity of the expert-parallel layer (smoe_cuda_moe_layer_ep): one
-process per GPU over 2 GPUs (and 4 when present), exchange inside the layer
+process per GPU over 2, 4 and 8 GPUs (as many as present), both layer shapes
+(Qwen3-30B-A3B and Qwen3-235B-A22B), exchange inside the layer
 kernel over NVLink, results against the CPU oracle of the whole layer.
 Skipped on a box with a single GPU (ranks that wait on each other never run
 as processes sharing one GPU)."""
@@ -25,13 +26,14 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("world,fmt", [(2, 1), (2, 0), (4, 1)])
-def test_moe_layer_expert_parallel(world, fmt):
+@pytest.mark.parametrize("world,fmt,shape", [(2, 1, "30b"), (2, 0, "30b"), (4, 1, "30b"), (8, 1, "30b"),
+                                             (2, 1, "235b"), (4, 1, "235b"), (8, 1, "235b")])
+def test_moe_layer_expert_parallel(world, fmt, shape):
     if _gpus() < world:
         pytest.skip(f"needs {world} GPUs")
     port = _free_port()
     procs = [subprocess.Popen([sys.executable, os.path.join(HERE, "ep_worker.py"), str(r), str(world),
-                               str(port), str(fmt)], stdout=subprocess.PIPE, stderr=subprocess.STDOUT,
+                               str(port), str(fmt), shape], stdout=subprocess.PIPE, stderr=subprocess.STDOUT,
                               text=True, env={**os.environ, "NCCL_NVLS_ENABLE": "0"})
              for r in range(world)]
     outs = []
