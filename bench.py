@@ -297,8 +297,7 @@ def run_ours(args, rank, world, local):
     if ep:
         import torch.distributed as dist
         grp = dist.new_group(backend="gloo")
-        handles = [None] * world
-        dist.all_gather_object(handles, ctx.ep_export(), group=grp)
+        handles = S.ep_exchange_handles(ctx.ep_export(), world, group=grp)
         ctx.ep_attach(rank, world, handles)
         barrier(world)
     xs = np.stack([O.normal_bf16(1234 + 7919 + i, 5, d) for i in range(64)])

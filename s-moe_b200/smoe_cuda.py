@@ -70,6 +70,29 @@ class SmoeCudaError(RuntimeError):
     pass
 
 
+def ep_exchange_handles(mine: bytes, world: int, group=None, timeout_s: float = 60.0):
+    """All-gather every rank's 64-byte exchange-window handle in rank order
+    (what ep_attach expects) over a torch.distributed group (gloo is enough).
+    A rank that never joins makes the others raise SmoeCudaError after
+    timeout_s instead of waiting forever."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    if len(mine) != 64:
+        raise ValueError("an exchange handle is 64 bytes")
+    if world == 1:
+        return [mine]
+    t = torch.frombuffer(bytearray(mine), dtype=torch.uint8)
+    out = [torch.empty(64, dtype=torch.uint8) for _ in range(world)]
+    try:
+        work = dist.all_gather(out, t, group=group, async_op=True)
+        if not work.wait(timeout=datetime.timedelta(seconds=timeout_s)):
+            raise SmoeCudaError("expert-parallel handle exchange timed out")
+    except RuntimeError as e:             # gloo reports the missing peer as an error
+        raise SmoeCudaError(f"expert-parallel handle exchange failed: {e}") from e
+    return [bytes(o.numpy().tobytes()) for o in out]
+
+
 class InitArgs(C.Structure):
     _fields_ = [("device", C.c_int), ("max_d_model", C.c_uint32), ("max_d_ff", C.c_uint32),
                 ("max_experts", C.c_uint32), ("max_batch", C.c_uint32),

@@ -52,9 +52,7 @@ def main():
     shard = ctx.prepack_layer(vault, tbuf, tstride)
     ctx.synchronize()
 
-    mine = ctx.ep_export()
-    handles = [None] * world
-    dist.all_gather_object(handles, mine)
+    handles = S.ep_exchange_handles(ctx.ep_export(), world)
     ctx.ep_attach(rank, world, handles)
     dist.barrier()                           # every rank attached before any launch
 
