@@ -88,6 +88,15 @@ struct LayerState {          // device scratch, zero at context creation and aft
     uint32_t pad[4];
 };
 
+// Division by a launch constant d without the integer divide (whose ~100
+// cycles of latency sit on the producer's and the phases' critical paths):
+// m = ceil(2^32 / d), q = hi32(x * m) = floor(x / d) for x * d < 2^32 (every
+// use here: x < 2^22, d < 2^10).
+__host__ __device__ inline uint32_t magic_of(uint32_t d) {
+    return d <= 1 ? 0u : uint32_t((0x100000000ull + d - 1) / d);
+}
+SMOE_DEVINL uint32_t divu(uint32_t x, uint32_t d, uint32_t m) { return d <= 1 ? x : __umulhi(x, m); }
+
 SMOE_DEVINL void cons_sync() {
     asm volatile("bar.sync 1, %0;" :: "n"(kLCThreads) : "memory");
 }
@@ -97,12 +106,18 @@ struct LayerGeom {
     int d, dff, k, ntok;
     TiledGeom tg;
     int G, tilesU, outTiles, NA, NB;
+    uint32_t mg_tilesU, mg_outTiles, mg_Gd, mg_G, mg_k;   // division magics (divu below)
     int o_xtab, o_xg, o_red, o_red2, o_bar, o_ids, o_w, o_loc, o_ringA, o_ringB, total;
 
     __host__ __device__ bool init(int fmt, int d_, int dff_, int k_, int ntok_, int max_smem) {
         d = d_; dff = dff_; k = k_; ntok = ntok_;
         if (!tg.init(fmt, d, dff) || tg.Gc > 32 || ntok < 1 || ntok > kLMaxTok || k < 1 || k > kLMaxK) return false;
         G = d / 64; tilesU = dff / 16; outTiles = d / 16;
+        mg_tilesU = magic_of(uint32_t(tilesU));
+        mg_outTiles = magic_of(uint32_t(outTiles));
+        mg_Gd = magic_of(tg.Gd);
+        mg_G = magic_of(uint32_t(G));
+        mg_k = magic_of(uint32_t(k));
         int off = 0;
         auto take = [&](int bytes) { int o = off; off += (bytes + 127) & ~127; return o; };
         const int xt = G * 1024, hr = k * tilesU * kHRec;    // x table, then (phase B) one token's h records
@@ -164,6 +179,7 @@ struct LayerArgs {
     LayerState* st;
     uint32_t* err;
     uint64_t wait_ns;          // limit of every wait
+    uint32_t mg_grid;          // magic_of(grid size)
     unsigned long long* trace; // optional [grid x 32] phase timestamps (ns)
     LayerGeom g;
     LayerEp ep;
@@ -257,7 +273,8 @@ SMOE_DEVINL float scale2(float v, int e) {
 // xg[grp*4 + t] = (2^(E-24) (/7.5 for SMOE-Q4), sum of the fixed-point x).
 // Columns of absent tokens stay 0. All consumer threads.
 template <int FMT>
-SMOE_DEVINL void build_xtab(const void* xsrc, int x_dtype, int ntok, int K, uint4* xtab, float2* xg, int ctid) {
+SMOE_DEVINL void build_xtab(const void* xsrc, int x_dtype, int ntok, int K, uint4* xtab, float2* xg, int ctid,
+                            uint32_t mgG) {
     const int G = K / 64;
     for (int i = ctid; i < G * 64; i += kLCThreads) xtab[i] = make_uint4(0u, 0u, 0u, 0u);
     const int warp = ctid >> 5, lane = ctid & 31;
@@ -270,7 +287,7 @@ SMOE_DEVINL void build_xtab(const void* xsrc, int x_dtype, int ntok, int K, uint
             const int p = p0 + q * kLCons;
             v[q][0] = v[q][1] = 0.f;
             if (p < ntok * G) {
-                const int t = p / G, grp = p - t * G;
+                const int t = int(divu(uint32_t(p), uint32_t(G), mgG)), grp = p - t * G;
                 const size_t base = size_t(t) * K + grp * 64;
                 if (x_dtype == 0) {
                     const float* s = static_cast<const float*>(xsrc) + base;
@@ -293,7 +310,7 @@ SMOE_DEVINL void build_xtab(const void* xsrc, int x_dtype, int ntok, int K, uint
         for (int q = 0; q < U; ++q) {
             const int p = p0 + q * kLCons;
             if (p >= ntok * G) break;
-            const int t = p / G, grp = p - t * G;
+            const int t = int(divu(uint32_t(p), uint32_t(G), mgG)), grp = p - t * G;
             const float v0 = v[q][0], v1 = v[q][1];
             float m = fmaxf(fabsf(v0), fabsf(v1));
 #pragma unroll
@@ -426,12 +443,12 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
     auto tok_at = [&](int t) { return min(s_tok[t], nloc()); };
     auto a_range = [&](int& a0, int& a1) {
         const int nA = int(nloc()) * g.tilesU;
-        a0 = int(uint32_t(cta) * uint32_t(nA) / uint32_t(ncta));      // nA * grid < 2^32
-        a1 = int(uint32_t(cta + 1) * uint32_t(nA) / uint32_t(ncta));
+        a0 = int(divu(uint32_t(cta) * uint32_t(nA), uint32_t(ncta), A.mg_grid));
+        a1 = int(divu(uint32_t(cta + 1) * uint32_t(nA), uint32_t(ncta), A.mg_grid));
     };
     const int nB = g.ntok * g.outTiles;
-    const int b0 = int(uint32_t(cta) * uint32_t(nB) / uint32_t(ncta)),
-              b1 = int(uint32_t(cta + 1) * uint32_t(nB) / uint32_t(ncta));
+    const int b0 = int(divu(uint32_t(cta) * uint32_t(nB), uint32_t(ncta), A.mg_grid)),
+              b1 = int(divu(uint32_t(cta + 1) * uint32_t(nB), uint32_t(ncta), A.mg_grid));
     // expert blob of a slot (its id is local: the slot is in s_loc)
     auto expert_of = [&](uint32_t slot) {
         uint32_t e = s_ids[slot] - ep.base;
@@ -480,7 +497,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         const int nAi = (a1 - a0) * int(tg.nchunk);
         int nBi = 0;
         {
-            int t = b0 / g.outTiles, o = b0 - t * g.outTiles;
+            int t = int(divu(uint32_t(b0), uint32_t(g.outTiles), g.mg_outTiles)), o = b0 - t * g.outTiles;
             for (int b = b0; b < b1; ++b) {
                 nBi += max(int(tok_at(t + 1)) - int(tok_at(t)), 0);
                 if (++o == g.outTiles) { o = 0; ++t; }
@@ -492,9 +509,9 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         // Order: the first NA gate/up chunks, the first NB down parts, then
         // the rest of each as stages free up.
         int iA = 0, iB = 0;
-        int ali = a0 / g.tilesU, au = a0 - ali * g.tilesU, ac = 0;          // next A item: (local slot, unit, chunk)
+        int ali = int(divu(uint32_t(a0), uint32_t(g.tilesU), g.mg_tilesU)), au = a0 - ali * g.tilesU, ac = 0;          // next A item: (local slot, unit, chunk)
         int stA = 0, rA = 0, stB = 0, rB = 0;
-        int bt = b0 / g.outTiles, bo = b0 - bt * g.outTiles, bb = b0;     // next B part: (token, tile), slot jj
+        int bt = int(divu(uint32_t(b0), uint32_t(g.outTiles), g.mg_outTiles)), bo = b0 - bt * g.outTiles, bb = b0;     // next B part: (token, tile), slot jj
         int jj = b0 < b1 ? int(tok_at(bt)) : 0;
         ltrace(A.trace, 11, true);
         const int limA0 = min(NA, nAi), limB0 = min(NB, nBi);
@@ -621,7 +638,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
     if (consumer) {
         // ------------------------------------------------ x table, phase A
         ltrace(A.trace, 30);
-        build_xtab<FMT>(xsrc, A.x_dtype, g.ntok, d, xtab, xg, tid);
+        build_xtab<FMT>(xsrc, A.x_dtype, g.ntok, d, xtab, xg, tid, g.mg_G);
         cons_sync();
         ltrace(A.trace, 3);
         if (!mbar_wait_b(routed, 0, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
@@ -629,9 +646,9 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         a_range(a0, a1);
         const int gr = lane >> 2, cq = lane & 3;
         int iA = 0, stA = 0, rA = 0;
-        int ali = a0 / g.tilesU, au = a0 - ali * g.tilesU;
+        int ali = int(divu(uint32_t(a0), uint32_t(g.tilesU), g.mg_tilesU)), au = a0 - ali * g.tilesU;
         uint32_t slot = slot_at(uint32_t(ali));
-        int tok = int(slot) / k;
+        int tok = int(divu(slot, uint32_t(k), g.mg_k));
         #pragma unroll 1
         for (int a = a0; a < a1; ++a) {
             const int n = a - a0, b = n & 1;
@@ -711,7 +728,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
             if (++au == g.tilesU) {
                 au = 0;
                 slot = slot_at(uint32_t(++ali));
-                tok = int(slot) / k;
+                tok = int(divu(slot, uint32_t(k), g.mg_k));
             }
         }
         ltrace(A.trace, 5);
@@ -722,7 +739,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
             // them before the grid-wide wait, which is the longer one
             int pre_w = 0;
             {
-                const int t0 = b0 / g.outTiles, l0 = int(tok_at(t0));
+                const int t0 = int(divu(uint32_t(b0), uint32_t(g.outTiles), g.mg_outTiles)), l0 = int(tok_at(t0));
                 pre_w = min(NB, max(l0, min(int(tok_at(t0 + 1)), l0 + k)) - l0);
                 #pragma unroll 1
                 for (int q = 0; q < pre_w; ++q)
@@ -734,7 +751,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
             ltrace(A.trace, 6);
             uint8_t* hsm = reinterpret_cast<uint8_t*>(xtab);          // the x table is no longer needed
             int cur = -1, stB = 0, rB = 0;
-            int t = b0 / g.outTiles, o = b0 - t * g.outTiles - 1;
+            int t = int(divu(uint32_t(b0), uint32_t(g.outTiles), g.mg_outTiles)), o = b0 - t * g.outTiles - 1;
             #pragma unroll 1
             for (int bu = b0; bu < b1; ++bu) {
                 if (++o == g.outTiles) { o = 0; ++t; }
@@ -788,7 +805,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
                     // this warp's items [i0, i1) of the wave's W x Gd (part, group) items
                     const int nit = W * int(tg.Gd);
                     const int i0 = (warp * nit) >> 4, i1 = ((warp + 1) * nit) >> 4;   // kLCons == 16
-                    int iq = i0 / int(tg.Gd), ig = i0 - iq * int(tg.Gd);
+                    int iq = int(divu(uint32_t(i0), tg.Gd, g.mg_Gd)), ig = i0 - iq * int(tg.Gd);
                     int sidx = stB + iq;
                     if (sidx >= NB) sidx -= NB;
                     #pragma unroll 2
@@ -813,22 +830,20 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
                             dq[u][0] = dq[u][1] = dq[u][2] = dq[u][3] = 0;
                             mma_u8s8_16816(dq[u], a, bq[u]);
                         }
-                        // columns 0, 1 (planes p0, p1) are in lane c = 0, column 2 (p2) in c = 1
-                        int p2g[4], p2h[4];
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            p2g[u] = __shfl_down_sync(0xffffffffu, dq[u][0], 1);
-                            p2h[u] = __shfl_down_sync(0xffffffffu, dq[u][2], 1);
-                        }
-                        if (cq == 0) {
+                        // columns 0, 1 (planes p0, p1) are in lane c = 0, column 2 (p2)
+                        // in c = 1: each of the two lanes scales its own columns and
+                        // keeps its own partial (added together once per B unit)
+                        if (cq < 2) {
                             float s0 = 0.f, s8 = 0.f, sh = 0.f;
+                            const float pw = cq == 0 ? 1.0f : 65536.0f;
 #pragma unroll
                             for (int u = 0; u < 4; ++u) {
-                                const float xs = (u & 1) ? xsv[u].x * 0.0625f : xsv[u].x;    // odd units: 16q
-                                s0 = fmaf(fmaf(float(p2g[u]), 65536.0f, float(dq[u][0] + 256 * dq[u][1])), xs, s0);
-                                s8 = fmaf(fmaf(float(p2h[u]), 65536.0f, float(dq[u][2] + 256 * dq[u][3])), xs, s8);
+                                const float xs = ((u & 1) ? xsv[u].x * 0.0625f : xsv[u].x) * pw;   // odd units: 16q
+                                s0 = fmaf(float(dq[u][0] + (cq == 0 ? 256 * dq[u][1] : 0)), xs, s0);
+                                s8 = fmaf(float(dq[u][2] + (cq == 0 ? 256 * dq[u][3] : 0)), xs, s8);
                                 sh += xsv[u].y;
                             }
+                            if (cq != 0) sh = 0.f;                         // the sum term once
                             const uint8_t* sbp = sp + tg.bcodes;
                             if (FMT == kFmtAffine) {
                                 const uint32_t* sbw = reinterpret_cast<const uint32_t*>(sbp) + ig * 16 + gr;
@@ -860,6 +875,8 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
                     stB += W;                                         // W <= NB
                     if (stB >= NB) { stB -= NB; ++rB; }
                 }
+                y0 += __shfl_down_sync(0xffffffffu, y0, 1);         // + the p2 columns' partial
+                y8 += __shfl_down_sync(0xffffffffu, y8, 1);
                 if (cq == 0) {
                     red2[warp * 16 + gr] = y0;
                     red2[warp * 16 + gr + 8] = y8;
@@ -900,7 +917,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         if (!mbar_wait_b(routed, 0, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
         int a0, a1;
         a_range(a0, a1);
-        int hli = a0 / g.tilesU, hu = a0 - hli * g.tilesU;
+        int hli = int(divu(uint32_t(a0), uint32_t(g.tilesU), g.mg_tilesU)), hu = a0 - hli * g.tilesU;
         #pragma unroll 1
         for (int a = a0; a < a1; ++a, ++hu) {
             if (hu == g.tilesU) { hu = 0; ++hli; }

@@ -329,6 +329,7 @@ int launch_layer(SmoeCudaCtx* c, const LayerCall& q) {
     A.st = c->lstate;
     A.err = c->err;
     A.wait_ns = c->wait_ns;
+    A.mg_grid = smoe::magic_of(uint32_t(c->num_sms));
     A.trace = c->trace;
     if (q.ep) {
         A.ep = *q.ep;
