@@ -129,7 +129,9 @@ SMOE_DEVINL float dot8_bf16(uint4 v, const float4* xp) {
 // RPW rows per warp (1 for small matrices, so the grid covers the SMs; 2
 // for large ones). The first chunk of weight loads is issued before waiting
 // for the kernel that produced x (weights do not depend on it).
-template <int RPW>
+// CH: 16-byte chunks per lane per row in flight at once (8: rows of up to
+// 2048 bf16 in one round trip; 16 for rows up to 4096).
+template <int RPW, int CH = 8>
 __global__ void __launch_bounds__(kGemvThreads) k_gemv_set(GemvSet a, uint32_t total) {
     const int lane = threadIdx.x & 31;
     pdl_trigger();
@@ -151,10 +153,10 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_set(GemvSet a, uint32_t t
         float sacc[RPW];
 #pragma unroll
         for (int q = 0; q < RPW; ++q) sacc[q] = 0.f;
-        for (uint32_t c0 = lane; c0 < n; c0 += 32 * 8) {
-            uint4 v[RPW][8];
+        for (uint32_t c0 = lane; c0 < n; c0 += 32 * CH) {
+            uint4 v[RPW][CH];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
+            for (int j = 0; j < CH; ++j) {
                 const uint32_t c = c0 + j * 32;
 #pragma unroll
                 for (int q = 0; q < RPW; ++q)
@@ -165,7 +167,7 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_set(GemvSet a, uint32_t t
                 waited = true;
             }
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
+            for (int j = 0; j < CH; ++j) {
                 const uint32_t c = c0 + j * 32;
 #pragma unroll
                 for (int q = 0; q < RPW; ++q)
