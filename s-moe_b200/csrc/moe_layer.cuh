@@ -491,6 +491,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         __syncwarp();
     };
     // producer lane: issue every copy of the CTA, gate/up chunks first
+    int preA = 0;                              // A items the head start issued
     auto produce = [&]() {
         int a0, a1;
         a_range(a0, a1);
@@ -511,6 +512,13 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         int iA = 0, iB = 0;
         int ali = int(divu(uint32_t(a0), uint32_t(g.tilesU), g.mg_tilesU)), au = a0 - ali * g.tilesU, ac = 0;          // next A item: (local slot, unit, chunk)
         int stA = 0, rA = 0, stB = 0, rB = 0;
+        for (; iA < preA; ++iA) {              // issued already by the head start below
+            if (++ac == int(tg.nchunk)) {
+                ac = 0;
+                if (++au == g.tilesU) { au = 0; ++ali; }
+            }
+            if (++stA == NA) { stA = 0; ++rA; }
+        }
         int bt = int(divu(uint32_t(b0), uint32_t(g.outTiles), g.mg_outTiles)), bo = b0 - bt * g.outTiles, bb = b0;     // next B part: (token, tile), slot jj
         int jj = b0 < b1 ? int(tok_at(bt)) : 0;
         ltrace(A.trace, 11, true);
@@ -622,6 +630,31 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         }
         __syncwarp();
         ltrace(A.trace, 28, lane == 0);
+        // head start (single GPU, all ids valid): every slot is local, so the
+        // CTA's A range is known without the routing state - issue its first
+        // gate/up chunks now, before the routing state is built
+        if (!epm) {
+            bool ok = true;
+            for (uint32_t sl = lane; sl < nslots; sl += 32) ok = ok && s_ids[sl] < A.n_experts;
+            if (__all_sync(0xffffffffu, ok) && lane == 0) {
+                const uint32_t nA = nslots * uint32_t(g.tilesU);
+                const int a0 = int(divu(uint32_t(cta) * nA, uint32_t(ncta), A.mg_grid));
+                const int a1 = int(divu(uint32_t(cta + 1) * nA, uint32_t(ncta), A.mg_grid));
+                const int n = min(NA, (a1 - a0) * int(tg.nchunk));
+                int li = int(divu(uint32_t(a0), uint32_t(g.tilesU), g.mg_tilesU)), u = a0 - li * g.tilesU, c = 0;
+                for (int i = 0; i < n; ++i) {
+                    mbar_arrive_expect_tx(fullA + i, tg.chunk);
+                    bulk_g2s(ringA + size_t(i) * g.stageA(), A.base + uint64_t(s_ids[li]) * A.stride + tg.chunk_off(u, c),
+                             tg.chunk, fullA + i);
+                    if (++c == int(tg.nchunk)) {
+                        c = 0;
+                        if (++u == g.tilesU) { u = 0; ++li; }
+                    }
+                }
+                preA = n;
+            }
+            __syncwarp();
+        }
         finish_routing();
         ltrace(A.trace, 29, lane == 0);
         if (lane == 0) mbar_arrive(routed);
