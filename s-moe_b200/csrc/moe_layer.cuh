@@ -35,12 +35,15 @@
 // (AFFINE-Q4) or scale * (sum q x / 7.5 - sum x) (SMOE-Q4, the identity of
 // kernels.metal:136-143), sum x taken over the same fixed-point values. The
 // only roundings are the fixed-point step of x and the fp32 epilogue.
-// Down arithmetic: the same fixed-point digits, for h: the h warp quantises
-// each 16-row unit (exponent of the unit's max|h|) into three signed byte
-// planes, and the down product runs as integer MMAs m16n8k16 (u8 x s8), one
-// per unit, with the planes in columns 0-2 of B; per unit the exact int32
-// sums are scaled by the unit's 2^(E-20), and per 64-group the fp32 epilogue
-// applies the down matrix's scale (and bias).
+// Down arithmetic: the same fixed-point digits, for h: the h warp stores
+// each 16-row unit's h as fp32; when phase B loads a token's h, each 64-group
+// (four units) is quantised with the exponent of its max|h| into three
+// unsigned byte planes (offset 2^21). The down product runs as integer MMAs
+// m16n8k16 (u8 x u8), one per unit with the planes in columns 0-2 of B and
+// ones in column 3 (to take the offset back out), the four units of a group
+// chained into one exact int32 accumulator (odd units' codes shifted down to
+// q); per group the sums are scaled by 2^(E-20) and the fp32 epilogue applies
+// the down matrix's scale (and bias).
 //
 // Expert parallel (world > 1, one process per GPU, experts [r*E/G,
 // (r+1)*E/G) on rank r): every rank routes (the same ids), runs the A units
@@ -66,26 +69,24 @@ namespace smoe {
 
 constexpr int kLCons = 16;                    // consumer warps
 constexpr int kLCThreads = kLCons * 32;
-constexpr int kLHWarp = kLCons;               // h warp (also runs the top-k)
-constexpr int kLProdWarp = kLCons + 1;        // producer warp (lane 0 issues the copies)
+constexpr int kLHWarp = kLCons;               // h warp
+constexpr int kLProdWarp = kLCons + 1;        // producer warp (top-k; lane 0 issues the copies)
 constexpr int kLThreads = kLCThreads + 64;
 constexpr int kLMaxTok = 4;
 constexpr int kLMaxK = 16;
 constexpr int kLMaxNA = 4;                    // gate/up ring stages (at most)
 constexpr int kLMaxNB = 16;                   // down ring stages (at most)
-// h record of one A unit (16 hidden rows), in digit form for the down MMA:
-// [plane 0: 16 B][plane 1][plane 2][xs f32][sum f32][pad 8], X = round(h
-// 2^(20-E)) = p0 + 2^8 p1 + 2^16 p2 with E the exponent of the unit's max|h|,
-// xs = 2^(E-20) (/7.5 for SMOE-Q4), sum = sum X 2^(E-20) (= sum h as seen).
-constexpr int kHRec = 64;
+constexpr int kHRec = 64;                      // one unit's h: 16 fp32
+constexpr int kHGrp = 4 * kHRec;               // one 64-group's digit record in shared memory
 constexpr int kEpMaxWorld = 8;
 
-struct LayerState {          // device scratch, zero at context creation and after every launch
-    uint32_t rdone;                 // router logit rows finished
+struct LayerState {          // device scratch, zero at context creation; the counters zero after every launch
+    uint32_t rdone;                 // router logit rows stored (a hint: the logits carry their own tag)
     uint32_t arrive;                // CTAs past phase A
     uint32_t done;                  // CTAs finished
     uint32_t epoch;                 // expert-parallel launches completed (advanced by the last CTA)
-    uint32_t pad[4];
+    uint32_t seq;                   // launches completed (advanced by the last CTA): tags this launch's logits
+    uint32_t pad[3];
 };
 
 // Division by a launch constant d without the integer divide (whose ~100
@@ -174,8 +175,8 @@ struct LayerArgs {
     uint32_t n_experts;        // router rows = id bound
     const uint16_t* rw;        // router W [E x d] bf16, null: routing given
     int norm;
-    float* logits;             // scratch [ntok x E]
-    uint8_t* hbuf;             // scratch h records [ntok*k][d_ff/16][kHRec]
+    unsigned long long* logits;  // scratch [ntok x E]: (launch tag << 32) | fp32 bits of the logit
+    uint8_t* hbuf;             // scratch h, fp32 [ntok*k][d_ff/16][16]
     LayerState* st;
     uint32_t* err;
     uint64_t wait_ns;          // limit of every wait
@@ -224,6 +225,41 @@ static __device__ __noinline__ bool spin_geq(const uint32_t* p, uint32_t target,
 
 SMOE_DEVINL void raise_err(uint32_t* err, uint32_t code) { atomicCAS(err, 0u, code); }
 
+SMOE_DEVINL void st_relaxed_gpu_u64(unsigned long long* p, uint64_t v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" :: "l"(p), "l"(v) : "memory");
+}
+SMOE_DEVINL uint64_t ld_relaxed_gpu_u64(const unsigned long long* p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Bounded wait (one warp) for a token's E <= 128 tagged logits of this
+// launch: lane l gets logits l + 32j in p[j] (-inf past E). Polls the values
+// themselves - the first poll that sees every tag returns them.
+static __device__ __noinline__ bool wait_logits(const unsigned long long* lg, int E, uint32_t tag, float (&p)[4],
+                                                int lane, const WaitBudget wb) {
+    const uint64_t deadline = wb.deadline();
+#pragma unroll 1
+    for (uint32_t i = 0; i < SMOE_SPIN_LIMIT; ++i) {
+        bool ok = true;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int e = lane + 32 * j;
+            p[j] = -INFINITY;
+            if (e < E) {
+                const uint64_t v = ld_relaxed_gpu_u64(lg + e);
+                p[j] = __uint_as_float(uint32_t(v));
+                ok = ok && uint32_t(v >> 32) == tag;
+            }
+        }
+        if (__all_sync(0xffffffffu, ok)) return true;
+        if ((i & 7) == 7 && gtimer() > deadline) return false;
+        if (i > 64) __nanosleep(32);
+    }
+    return false;
+}
+
 // Phase R: one logit row (token t, expert e) by all consumer warps; returns
 // this warp's partial sum (reduced across warps by the caller).
 SMOE_DEVINL float router_row_part(const LayerArgs& A, const void* xsrc, uint32_t t, uint32_t e, int ctid) {
@@ -265,6 +301,45 @@ SMOE_DEVINL float pow2i(int e) { return __int_as_float((127 + e) << 23); }   // 
 SMOE_DEVINL float scale2(float v, int e) {
     const int a = e / 2;
     return (v * pow2i(a)) * pow2i(e - a);
+}
+
+// Digit record of one (slot, 64-group) of h for the down MMAs, built by a
+// half-warp (j = 0..15 its thread, v = h rows 4(j&3)..+3 of unit j>>2): one
+// exponent E for the group's 64 values, X = round(h * 2^(20-E)) (|X| <= 2^21)
+// offset to Xu = X + 2^21 in [0, 2^22] and split into three unsigned byte
+// planes. Plane p holds at p*64 + c*16 + u*4 + b the digit of unit u, row
+// 4c + b (lane 4g + c's B register of unit u = one 32-bit word, its four
+// units one 16-byte load); at 192 the fp32 pair (2^(E-20) (/7.5 for
+// SMOE-Q4), sum of the fixed-point h). The offset comes back out through a
+// column of ones in the MMA (sum q * X = sum q * Xu - 2^21 sum q). Every
+// lane of the warp calls it; `valid` is the same for the 16 threads of a group.
+template <int FMT>
+SMOE_DEVINL void h_digits(float4 v, uint8_t* rec, int j, bool valid) {
+    float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    // below 2^-100 every X rounds to 0 anyway; the clamp keeps 2^(20-E) a normal float
+    const int E = max(int((__float_as_uint(m) >> 23) & 0xff) - 127, -100);
+    const float f = pow2i(20 - E);
+    const int X[4] = {__float2int_rn(v.x * f), __float2int_rn(v.y * f), __float2int_rn(v.z * f),
+                      __float2int_rn(v.w * f)};
+    int sx = X[0] + X[1] + X[2] + X[3];
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) sx += __shfl_xor_sync(0xffffffffu, sx, o);
+    const uint32_t u0 = uint32_t(X[0] + (1 << 21)), u1 = uint32_t(X[1] + (1 << 21)),
+                   u2 = uint32_t(X[2] + (1 << 21)), u3 = uint32_t(X[3] + (1 << 21));
+    if (valid) {
+        uint32_t* w = reinterpret_cast<uint32_t*>(rec + (j & 3) * 16 + (j >> 2) * 4);
+#pragma unroll
+        for (int p = 0; p < 3; ++p)                      // byte p of each value: plane p
+            w[16 * p] = __byte_perm(__byte_perm(u0, u1, 0x0040u + 0x0011u * p),
+                                    __byte_perm(u2, u3, 0x0040u + 0x0011u * p), 0x5410u);
+        if (j == 0) {
+            const float xs = pow2i(E - 20);
+            *reinterpret_cast<float2*>(rec + 192) =
+                make_float2(FMT == kFmtAffine ? xs : xs * (1.0f / 7.5f), float(sx) * xs);
+        }
+    }
 }
 
 // x table of the gate/up MMAs, read straight from global x (ntok x K):
@@ -381,6 +456,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
     const LayerEp& ep = A.ep;
     const bool epm = ep.world > 1;
     const uint32_t epoch = epm ? A.st->epoch + 1u : 0u;           // written by the previous launch only
+    const uint32_t seq = A.st->seq + 1u;                          // this launch's tag (never 0 in use)
     // x: the caller's, or on ranks > 0 rank 0's published copy (peer memory)
     const void* xsrc = A.x;
     if (epm) {
@@ -490,8 +566,34 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         if (lane == 0) *s_nloc = cnt;
         __syncwarp();
     };
-    // producer lane: issue every copy of the CTA, gate/up chunks first
+    // head start (producer warp, single GPU, all ids valid, s_ids final):
+    // every slot is local, so the CTA's A range is known without the routing
+    // state - issue its first gate/up chunks before that state is built
     int preA = 0;                              // A items the head start issued
+    auto head_start = [&]() {
+        if (epm) return;
+        bool ok = true;
+        for (uint32_t sl = lane; sl < nslots; sl += 32) ok = ok && s_ids[sl] < A.n_experts;
+        if (__all_sync(0xffffffffu, ok) && lane == 0) {
+            const uint32_t nA = nslots * uint32_t(g.tilesU);
+            const int a0 = int(divu(uint32_t(cta) * nA, uint32_t(ncta), A.mg_grid));
+            const int a1 = int(divu(uint32_t(cta + 1) * nA, uint32_t(ncta), A.mg_grid));
+            const int n = min(NA, (a1 - a0) * int(tg.nchunk));
+            int li = int(divu(uint32_t(a0), uint32_t(g.tilesU), g.mg_tilesU)), u = a0 - li * g.tilesU, c = 0;
+            for (int i = 0; i < n; ++i) {
+                mbar_arrive_expect_tx(fullA + i, tg.chunk);
+                bulk_g2s(ringA + size_t(i) * g.stageA(), A.base + uint64_t(s_ids[li]) * A.stride + tg.chunk_off(u, c),
+                         tg.chunk, fullA + i);
+                if (++c == int(tg.nchunk)) {
+                    c = 0;
+                    if (++u == g.tilesU) { u = 0; ++li; }
+                }
+            }
+            preA = n;
+        }
+        __syncwarp();
+    };
+    // producer lane: issue every copy of the CTA, gate/up chunks first
     auto produce = [&]() {
         int a0, a1;
         a_range(a0, a1);
@@ -587,20 +689,31 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
                 if (tid == 0) {
                     float s = 0.f;
                     for (int w = 0; w < kLCons; ++w) s += red[w];
-                    A.logits[r] = s;
-                    red_rel_gpu(&A.st->rdone, 1u);
+                    // value and tag in one 64-bit store: a reader that sees
+                    // this launch's tag sees the value (no fence)
+                    st_relaxed_gpu_u64(A.logits + r, (uint64_t(seq) << 32) | __float_as_uint(s));
+                    asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" :: "l"(&A.st->rdone) : "memory");
                 }
                 cons_sync();
             }
         }
         ltrace(A.trace, 1);
-        if (warp == kLHWarp) {
+        if (warp == kLProdWarp) {
+            // the producer warp selects (it then starts the weight stream
+            // without a hand-over); one lane waits for the row count (cheap to poll), then the
+            // warp reads the tagged logits (and re-reads any that are not
+            // this launch's yet: the count is not ordered with the stores)
             if (lane == 0 && !spin_geq<false>(&A.st->rdone, rows, wb)) raise_err(A.err, SMOE_DEVERR_SPIN_TIMEOUT);
             __syncwarp();
+            ltrace(A.trace, 18, lane == 0);
             for (int t = 0; t < g.ntok; ++t) {
                 // (the host routes layers of more than 128 experts with k_router)
-                warp_topk_n<4>(A.logits + size_t(t) * A.n_experts, int(A.n_experts), min(uint32_t(k), A.n_experts),
-                               A.norm, s_ids + t * k, s_w + t * k, lane);
+                float p[4];
+                if (!wait_logits(A.logits + size_t(t) * A.n_experts, int(A.n_experts), seq, p, lane, wb))
+                    raise_err(A.err, SMOE_DEVERR_SPIN_TIMEOUT);
+                if (t == 0) ltrace(A.trace, 19, lane == 0);
+                warp_topk_regs<4>(p, int(A.n_experts), min(uint32_t(k), A.n_experts), A.norm, s_ids + t * k,
+                                  s_w + t * k, lane);
                 __syncwarp();
                 if (cta == 0 && lane < k) {
                     if (A.ids_out) A.ids_out[t * k + lane] = s_ids[t * k + lane];
@@ -608,6 +721,8 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
                 }
             }
             __syncwarp();
+            ltrace(A.trace, 20, lane == 0);
+            head_start();
             finish_routing();
             if (lane == 0) mbar_arrive(routed);
             ltrace(A.trace, 2, lane == 0);
@@ -630,31 +745,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         }
         __syncwarp();
         ltrace(A.trace, 28, lane == 0);
-        // head start (single GPU, all ids valid): every slot is local, so the
-        // CTA's A range is known without the routing state - issue its first
-        // gate/up chunks now, before the routing state is built
-        if (!epm) {
-            bool ok = true;
-            for (uint32_t sl = lane; sl < nslots; sl += 32) ok = ok && s_ids[sl] < A.n_experts;
-            if (__all_sync(0xffffffffu, ok) && lane == 0) {
-                const uint32_t nA = nslots * uint32_t(g.tilesU);
-                const int a0 = int(divu(uint32_t(cta) * nA, uint32_t(ncta), A.mg_grid));
-                const int a1 = int(divu(uint32_t(cta + 1) * nA, uint32_t(ncta), A.mg_grid));
-                const int n = min(NA, (a1 - a0) * int(tg.nchunk));
-                int li = int(divu(uint32_t(a0), uint32_t(g.tilesU), g.mg_tilesU)), u = a0 - li * g.tilesU, c = 0;
-                for (int i = 0; i < n; ++i) {
-                    mbar_arrive_expect_tx(fullA + i, tg.chunk);
-                    bulk_g2s(ringA + size_t(i) * g.stageA(), A.base + uint64_t(s_ids[li]) * A.stride + tg.chunk_off(u, c),
-                             tg.chunk, fullA + i);
-                    if (++c == int(tg.nchunk)) {
-                        c = 0;
-                        if (++u == g.tilesU) { u = 0; ++li; }
-                    }
-                }
-                preA = n;
-            }
-            __syncwarp();
-        }
+        head_start();
         finish_routing();
         ltrace(A.trace, 29, lane == 0);
         if (lane == 0) mbar_arrive(routed);
@@ -784,29 +875,33 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
             ltrace(A.trace, 6);
             uint8_t* hsm = reinterpret_cast<uint8_t*>(xtab);          // the x table is no longer needed
             int cur = -1, stB = 0, rB = 0;
+            const uint32_t bones = gr == 3 ? 0x01010101u : 0u;        // B column 3 of the down MMAs
+            const int cmul = cq == 0 ? 256 : -32;
             int t = int(divu(uint32_t(b0), uint32_t(g.outTiles), g.mg_outTiles)), o = b0 - t * g.outTiles - 1;
             #pragma unroll 1
             for (int bu = b0; bu < b1; ++bu) {
                 if (++o == g.outTiles) { o = 0; ++t; }
                 const int ls = int(tok_at(t)), le = max(ls, min(int(tok_at(t + 1)), ls + k));
                 if (t != cur) {
-                    // this token's h records (local slots ls..le) into shared memory
+                    // this token's h (local slots ls..le) into shared memory as
+                    // digit records, one per (slot, 64-group): 16 threads (a
+                    // half-warp) per group, 4 values each
                     if (cur >= 0) cons_sync();                        // the previous token's are done with
-                    const uint4* src = reinterpret_cast<const uint4*>(A.hbuf + size_t(ls) * g.tilesU * kHRec);
-                    const int n16 = (le - ls) * g.tilesU * (kHRec / 16);
+                    const float4* src = reinterpret_cast<const float4*>(A.hbuf + size_t(ls) * g.tilesU * kHRec);
+                    const int n16 = (le - ls) * g.tilesU * (kHRec / 16);   // a multiple of 16
                     constexpr int U = 4;
 #pragma unroll 1
                     for (int base = 0; base < n16; base += U * kLCThreads) {
-                        uint4 v[U];
+                        float4 v[U];
 #pragma unroll
                         for (int q = 0; q < U; ++q) {
                             const int i = base + q * kLCThreads + tid;
-                            if (i < n16) v[q] = __ldcg(src + i);
+                            v[q] = i < n16 ? __ldcg(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
                         }
 #pragma unroll
                         for (int q = 0; q < U; ++q) {
                             const int i = base + q * kLCThreads + tid;
-                            if (i < n16) reinterpret_cast<uint4*>(hsm)[i] = v[q];
+                            h_digits<FMT>(v[q], hsm + size_t(i >> 4) * kHGrp, i & 15, i < n16);
                         }
                     }
                     cons_sync();
@@ -847,36 +942,33 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
                         // 16-column unit, B = the unit's digit planes in columns 0-2
                         const uint8_t* sp = ringB + size_t(sidx) * g.stageB();
                         const uint4 wq = *reinterpret_cast<const uint4*>(sp + (ig * 32 + lane) * 16);
-                        const uint8_t* rec0 = hsm + (size_t(w0 + iq - ls) * g.tilesU + ig * 4) * kHRec;
-                        uint32_t bq[4];
-                        float2 xsv[4];
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            bq[u] = gr < 3 ? *reinterpret_cast<const uint32_t*>(rec0 + u * kHRec + gr * 16 + cq * 4) : 0u;
-                            xsv[u] = *reinterpret_cast<const float2*>(rec0 + u * kHRec + 48);
-                        }
-                        int dq[4][4];
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            const uint32_t mk = (u & 1) ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
-                            const uint32_t a[2] = {(u < 2 ? wq.x : wq.z) & mk, (u < 2 ? wq.y : wq.w) & mk};
-                            dq[u][0] = dq[u][1] = dq[u][2] = dq[u][3] = 0;
-                            mma_u8s8_16816(dq[u], a, bq[u]);
+                        const uint8_t* rec = hsm + (size_t(w0 + iq - ls) * tg.Gd + ig) * kHGrp;
+                        const uint4 bq = gr < 3 ? *reinterpret_cast<const uint4*>(rec + gr * 64 + cq * 16)
+                                                : make_uint4(bones, bones, bones, bones);   // column 3: ones
+                        const float2 xsv = *reinterpret_cast<const float2*>(rec + 192);
+                        // one exponent for the group: the four unit MMAs chain
+                        // into one exact int32 accumulator
+                        constexpr uint32_t lo = 0x0F0F0F0Fu;
+                        int dq[4] = {0, 0, 0, 0};
+                        {
+                            const uint32_t a0[2] = {wq.x & lo, wq.y & lo};
+                            mma_u8u8_16816(dq, a0, bq.x);
+                            const uint32_t a1[2] = {(wq.x >> 4) & lo, (wq.y >> 4) & lo};
+                            mma_u8u8_16816(dq, a1, bq.y);
+                            const uint32_t a2[2] = {wq.z & lo, wq.w & lo};
+                            mma_u8u8_16816(dq, a2, bq.z);
+                            const uint32_t a3[2] = {(wq.z >> 4) & lo, (wq.w >> 4) & lo};
+                            mma_u8u8_16816(dq, a3, bq.w);
                         }
                         // columns 0, 1 (planes p0, p1) are in lane c = 0, column 2 (p2)
                         // in c = 1: each of the two lanes scales its own columns and
                         // keeps its own partial (added together once per B unit)
                         if (cq < 2) {
-                            float s0 = 0.f, s8 = 0.f, sh = 0.f;
-                            const float pw = cq == 0 ? 1.0f : 65536.0f;
-#pragma unroll
-                            for (int u = 0; u < 4; ++u) {
-                                const float xs = ((u & 1) ? xsv[u].x * 0.0625f : xsv[u].x) * pw;   // odd units: 16q
-                                s0 = fmaf(float(dq[u][0] + (cq == 0 ? 256 * dq[u][1] : 0)), xs, s0);
-                                s8 = fmaf(float(dq[u][2] + (cq == 0 ? 256 * dq[u][3] : 0)), xs, s8);
-                                sh += xsv[u].y;
-                            }
-                            if (cq != 0) sh = 0.f;                         // the sum term once
+                            // lane 0: p0 + 256 p1; lane 1: 65536 (p2 - 32 * ones) - exact
+                            const float xs = cq == 0 ? xsv.x : xsv.x * 65536.0f;
+                            const float s0 = float(dq[0] + cmul * dq[1]) * xs;
+                            const float s8 = float(dq[2] + cmul * dq[3]) * xs;
+                            const float sh = cq == 0 ? xsv.y : 0.f;          // the sum term once
                             const uint8_t* sbp = sp + tg.bcodes;
                             if (FMT == kFmtAffine) {
                                 const uint32_t* sbw = reinterpret_cast<const uint32_t*>(sbp) + ig * 16 + gr;
@@ -965,29 +1057,9 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
             __syncwarp();
             if (lane == 0) mbar_arrive(redE + b);
             const float up = __shfl_down_sync(0xffffffffu, v, 16);
-            const float hv = lane < 16 ? v * (1.0f / (1.0f + expf(-v))) * up * s_w[slot] : 0.f;  // kernels.metal:61-63
-            // digit record of the unit (lanes 0-15 hold its h; 16-31 zero)
-            float m = fabsf(hv);
-#pragma unroll
-            for (int sh = 8; sh > 0; sh >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, sh));
-            const int E = m > 0.f ? int((__float_as_uint(m) >> 23) & 0xff) - 127 : 0;
-            const int X = __float2int_rn(scale2(hv, 20 - E));
-            int sx = X;
-#pragma unroll
-            for (int sh = 8; sh > 0; sh >>= 1) sx += __shfl_xor_sync(0xffffffffu, sx, sh);
-            uint8_t* rec = A.hbuf + (size_t(li) * g.tilesU + u) * kHRec;
-            if (lane < 16) {
-                const int d0 = ((X + 128) & 255) - 128, r = (X - d0) >> 8;
-                const int d1 = ((r + 128) & 255) - 128, d2 = (r - d1) >> 8;
-                rec[lane] = uint8_t(d0);
-                rec[16 + lane] = uint8_t(d1);
-                rec[32 + lane] = uint8_t(d2);
-            }
-            if (lane == 0) {
-                const float xs = scale2(1.0f, E - 20);
-                *reinterpret_cast<float2*>(rec + 48) =
-                    make_float2(FMT == kFmtAffine ? xs : xs * (1.0f / 7.5f), scale2(float(sx), E - 20));
-            }
+            if (lane < 16)                                        // kernels.metal:61-63
+                reinterpret_cast<float*>(A.hbuf + (size_t(li) * g.tilesU + u) * kHRec)[lane] =
+                    v * (1.0f / (1.0f + expf(-v))) * up * s_w[slot];
         }
         // phase A of this CTA is done: publish for phase B of all CTAs (the
         // warp barrier orders every lane's record stores before lane 0's
@@ -1006,9 +1078,10 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(&A.st->done) : "memory");
         last_cta = (old == uint32_t(ncta) - 1) ? 1u : 0u;
         if (last_cta) {
-            A.st->rdone = 0;
             A.st->arrive = 0;
             A.st->done = 0;
+            A.st->rdone = 0;
+            A.st->seq = seq;
             if (epm) A.st->epoch = epoch;
         }
         // (no fence: the next launch reads these only after this grid has

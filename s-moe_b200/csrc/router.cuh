@@ -111,20 +111,16 @@ SMOE_DEVINL void stage_vec(const void* src, int x_dtype, size_t off, int d, floa
 // denominator is a warp tree sum; expert ids do not depend on it.
 // ids/wts: k outputs (global or shared).
 template <int NV>
-SMOE_DEVINL void warp_topk_n(const float* lg, int E, uint32_t k, int norm, uint32_t* ids, float* wts,
-                             int lane) {
-    // Lane l holds entries l + 32j. Selection keys: bits(p) + 1 for a live
-    // probability (p >= 0, so the order of the keys is the order of p), 0 for
-    // removed or absent entries. Each round is two warp reductions: the
-    // largest key, then the lowest index among the lanes holding it.
-    float p[NV];
+SMOE_DEVINL void warp_topk_regs(float (&p)[NV], int E, uint32_t k, int norm, uint32_t* ids, float* wts,
+                                int lane) {
+    // Lane l holds logits l + 32j in p[j] (-inf past E). Selection keys:
+    // bits(p) + 1 for a live probability (p >= 0, so the order of the keys is
+    // the order of p), 0 for removed or absent entries. Each round is two warp
+    // reductions: the largest key, then the lowest index among the lanes
+    // holding it.
     float mx = -INFINITY;
 #pragma unroll
-    for (int j = 0; j < NV; ++j) {
-        const int i = lane + 32 * j;
-        p[j] = i < E ? __ldcg(lg + i) : -INFINITY;
-        mx = fmaxf(mx, p[j]);
-    }
+    for (int j = 0; j < NV; ++j) mx = fmaxf(mx, p[j]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     float se = 0.f;
@@ -163,6 +159,18 @@ SMOE_DEVINL void warp_topk_n(const float* lg, int E, uint32_t k, int norm, uint3
         ids[lane] = idsel;
         wts[lane] = wsel * winv;
     }
+}
+
+template <int NV>
+SMOE_DEVINL void warp_topk_n(const float* lg, int E, uint32_t k, int norm, uint32_t* ids, float* wts,
+                             int lane) {
+    float p[NV];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+        const int i = lane + 32 * j;
+        p[j] = i < E ? __ldcg(lg + i) : -INFINITY;
+    }
+    warp_topk_regs<NV>(p, E, k, norm, ids, wts, lane);
 }
 
 SMOE_DEVINL void warp_topk(const float* lg, uint32_t E_, uint32_t k_, int norm, uint32_t* ids, float* wts,

@@ -78,6 +78,14 @@ SMOE_DEVINL void mma_u8s8_16816(int d[4], const uint32_t a[2], uint32_t b) {
         : "r"(a[0]), "r"(a[1]), "r"(b));
 }
 
+// D += A(16x16, u8, row) * B(16x8, u8, col), s32 accumulate.
+SMOE_DEVINL void mma_u8u8_16816(int d[4], const uint32_t a[2], uint32_t b) {
+    asm("mma.sync.aligned.m16n8k16.row.col.s32.u8.u8.s32 "
+        "{%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(b));
+}
+
 SMOE_DEVINL uint32_t pack_bf16x2(float lo, float hi) {
     const __nv_bfloat16 a = __float2bfloat16_rn(lo), b = __float2bfloat16_rn(hi);
     return uint32_t(__bfloat16_as_ushort(a)) | (uint32_t(__bfloat16_as_ushort(b)) << 16);

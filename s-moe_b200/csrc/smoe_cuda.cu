@@ -50,6 +50,7 @@ struct SmoeCudaCtx {
     float* in_stage = nullptr;      // [64][max_d_model]           mirror inputs
     float* batch_out = nullptr;     // [64][max_d_model]           token-batch outputs
     float* logits = nullptr;        // [max_batch][max_experts]
+    unsigned long long* lpair = nullptr;  // layer kernel's tagged logits [kLMaxTok][128] (zero: no tag)
     uint32_t* ids = nullptr;        // [max_batch][16]
     float* wts = nullptr;           // [max_batch][16]
     uint32_t* ticket = nullptr;     // [max_batch]
@@ -65,7 +66,7 @@ struct SmoeCudaCtx {
     int num_sms = 0;
     int gemv_res[2] = {0, 0};        // resident CTAs per SM of k_gemv_set<1>, <2>
     smoe::LayerState* lstate = nullptr;   // layer kernel's grid counters (zero between launches)
-    uint8_t* hbuf = nullptr;              // layer kernel's h records [kLMaxTok*kLMaxK][max_d_ff/16][kHRec]
+    uint8_t* hbuf = nullptr;              // layer kernel's h, fp32 [kLMaxTok*kLMaxK][max_d_ff/16][16]
     uint64_t wait_ns = 0;                 // limit of every device-side wait of the layer kernel
     unsigned long long* trace = nullptr;   // phase timestamps of the layer kernel (profiling aid)
     // expert-grouped batch path: per-expert slot lists, operand tables, per-slot outputs
@@ -325,7 +326,7 @@ int launch_layer(SmoeCudaCtx* c, const LayerCall& q) {
     A.n_experts = q.n_experts;
     A.rw = q.rw;
     A.norm = q.norm;
-    A.logits = c->logits;
+    A.logits = c->lpair;
     A.hbuf = c->hbuf;
     A.st = c->lstate;
     A.err = c->err;
@@ -447,6 +448,7 @@ SmoeCudaCtx* smoe_cuda_init_ex(const SmoeCudaInitArgs* args) {
     if ((e = cudaMalloc(&c->batch_out, size_t(SMOE_MAX_FFN_BATCH) * a.max_d_model * 4)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->in_stage, size_t(SMOE_MAX_FFN_BATCH) * a.max_d_model * 4)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->logits, size_t(a.max_batch) * a.max_experts * 4)) != cudaSuccess) return fail(e);
+    if ((e = cudaMalloc(&c->lpair, size_t(smoe::kLMaxTok) * 128 * 8)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->ids, size_t(a.max_batch) * 16 * 4)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->wts, size_t(a.max_batch) * 16 * 4)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->ticket, size_t(a.max_batch) * 4)) != cudaSuccess) return fail(e);
@@ -461,6 +463,7 @@ SmoeCudaCtx* smoe_cuda_init_ex(const SmoeCudaInitArgs* args) {
     if ((e = cudaMalloc(&c->g_hgs, slots * (a.max_d_ff / 64) * 8)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->g_ys, slots * a.max_d_model * 4)) != cudaSuccess) return fail(e);
     cudaMemsetAsync(c->lstate, 0, sizeof(smoe::LayerState), c->stream);
+    cudaMemsetAsync(c->lpair, 0, size_t(smoe::kLMaxTok) * 128 * 8, c->stream);
     c->gemv_cap = a.max_vocab > a.max_d_model ? a.max_vocab : a.max_d_model;
     if ((e = cudaMalloc(&c->gemv_out, c->gemv_cap * 4)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->gemv_in, size_t(a.max_d_model) * 4)) != cudaSuccess) return fail(e);
@@ -488,7 +491,7 @@ void smoe_cuda_destroy(SmoeCudaCtx* c) {
     if (c->ep_win) cudaFree(c->ep_win);
     for (auto& ev : c->events)
         if (ev) cudaEventDestroy(ev);
-    void* bufs[] = {c->g_list, c->g_count, c->g_xtab, c->g_xgs, c->g_htab, c->g_hgs, c->g_ys, c->lstate, c->hbuf, c->hidden, c->slot_out, c->in_stage, c->batch_out, c->logits, c->ids,
+    void* bufs[] = {c->g_list, c->g_count, c->g_xtab, c->g_xgs, c->g_htab, c->g_hgs, c->g_ys, c->lstate, c->lpair, c->hbuf, c->hidden, c->slot_out, c->in_stage, c->batch_out, c->logits, c->ids,
                     c->wts, c->ticket, c->err, c->gemv_out, c->gemv_in};
     for (void* b : bufs)
         if (b) cudaFree(b);
