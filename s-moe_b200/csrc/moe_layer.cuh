@@ -3,25 +3,27 @@
 //
 // One launch, one CTA per SM:
 //   routing (optional; decode.cpp:280-303): router logit rows spread over
-//     the grid; every CTA then runs the softmax / top-k / renorm of
-//     router.cuh on all logits (identical results in every CTA);
-//   phase A - gate/up (kernels.metal:240-337): the A units (slot, 16 hidden
-//     rows) are split evenly over the CTAs; each yields
-//     h = silu(Wg.x) * (Wu.x) * w_slot for its 16 rows, stored as fp32 to a
-//     global scratch record (64 B);
-//   one grid-wide arrive/wait (every CTA is resident: one CTA per SM);
-//   phase B - down + combine (kernels.metal:340-365, decode.cpp:485-499):
-//     the B units (token, 16 output rows) are split evenly over the CTAs;
-//     each computes its 16 rows of y = sum_slots W_down . h over all of the
-//     token's slots and writes them - every output row has exactly one
-//     owner, so there are no atomics and the sums are in a fixed order
-//     (bitwise reproducible).
+//     the grid, each stored with this launch's tag; every CTA's producer
+//     warp then runs the softmax / top-k / renorm of router.cuh on all
+//     logits (identical results in every CTA);
+//   phase A - gate/up and down (kernels.metal:240-365): the units (slot, 16
+//     hidden rows) are split evenly over the CTAs. Per unit the consumer
+//     warps run gate/up, the h warp turns the partials into
+//     h = silu(Wg.x) * (Wu.x) * w_slot for the unit's 16 rows, and the
+//     consumers multiply those 16 h by the unit's 16 columns of W_down (all
+//     d_model rows) into the CTA's partial output rows (split-K over d_ff);
+//     each CTA stores its partial rows per token, tagged;
+//   phase R - combine (decode.cpp:485-499): the row blocks (token, 16 output
+//     rows) are split evenly over the CTAs; each sums the partial rows of
+//     the CTAs that hold the token's units, in CTA order, as soon as their
+//     tags show up, and writes y. Every output row has one owner and a fixed
+//     summation order (bitwise reproducible); no grid-wide barrier, no
+//     atomics on the data.
 // Every byte a CTA needs is streamed by one producer lane with 1-D bulk
-// copies (no multicast) into two rings of shared-memory stages - gate/up
-// chunks first, then the down tiles - so the down weights are already on
-// chip when the grid-wide wait ends. Sixteen consumer warps run the gate/up
-// dots as integer MMAs on the raw codes (arithmetic below) and the down
-// tiles as bf16 MMAs; warp 16 turns each unit's 16 warp partials into h.
+// copies (no multicast) into three rings of shared-memory stages: per unit
+// its gate/up chunks, its down scales when it starts a new scale group, its
+// down columns. Sixteen consumer warps run the dots as integer MMAs on the
+// raw codes (arithmetic below).
 //
 // Gate/up arithmetic: integer tensor-core MMA m16n8k32 (u8 x s8 -> s32).
 // A 32-bit word of the fragments holds 8 codes; masking it with 0x0F0F0F0F
@@ -35,24 +37,24 @@
 // (AFFINE-Q4) or scale * (sum q x / 7.5 - sum x) (SMOE-Q4, the identity of
 // kernels.metal:136-143), sum x taken over the same fixed-point values. The
 // only roundings are the fixed-point step of x and the fp32 epilogue.
-// Down arithmetic: the same fixed-point digits, for h: the h warp stores
-// each 16-row unit's h as fp32; when phase B loads a token's h, each 64-group
-// (four units) is quantised with the exponent of its max|h| into three
-// unsigned byte planes (offset 2^21). The down product runs as integer MMAs
-// m16n8k16 (u8 x u8), one per unit with the planes in columns 0-2 of B and
-// ones in column 3 (to take the offset back out), the four units of a group
-// chained into one exact int32 accumulator (odd units' codes shifted down to
-// q); per group the sums are scaled by 2^(E-20) and the fp32 epilogue applies
-// the down matrix's scale (and bias).
+// Down arithmetic: the same fixed-point digits, for h: the h warp
+// quantises each unit's 16 h with the exponent of their max|h| into three
+// signed byte planes. One MMA m16n8k32 (u8 x s8) covers two 16-row tiles of
+// the unit's down columns: k 0-15 multiply the even tile's codes with the
+// planes in columns 0-2 of B, k 16-31 the odd tile's with the planes in
+// columns 4-6, so all four lanes of a quad hold results; the exact int32
+// sums are scaled by 2^(E-20) and the fp32 epilogue applies the down
+// matrix's scale (and bias) per row.
 //
 // Expert parallel (world > 1, one process per GPU, experts [r*E/G,
-// (r+1)*E/G) on rank r): every rank routes (the same ids), runs the A units
-// of the slots whose expert it holds, and the B units of every token over its
-// local slots; ranks > 0 store their partial rows into rank 0's window with
-// peer stores and count them per B unit with system-scope atomics; rank 0's
-// owner of that B unit waits for the count (bounded), adds the partials in
-// rank order and writes y. x is published by rank 0 (release flag) and read
-// by the others with peer loads. No TMA or bulk copy touches peer memory.
+// (r+1)*E/G) on rank r): every rank routes (the same ids) and runs phase A
+// on the units of the slots whose expert it holds and phase R over its own
+// CTAs; ranks > 0 store their combined rows into rank 0's window with peer
+// stores and count them per row block with system-scope atomics; rank 0's
+// owner of that row block waits for the count (bounded), adds the ranks'
+// rows in rank order and writes y. x is published by rank 0 (release flag)
+// and read by the others with peer loads. No TMA or bulk copy touches peer
+// memory.
 //
 // Every wait is bounded by %globaltimer: LayerArgs.wait_ns from its own
 // start, and the whole kernel by 8 x wait_ns. A wait that runs out sets the
@@ -74,15 +76,17 @@ constexpr int kLProdWarp = kLCons + 1;        // producer warp (top-k; lane 0 is
 constexpr int kLThreads = kLCThreads + 64;
 constexpr int kLMaxTok = 4;
 constexpr int kLMaxK = 16;
+constexpr int kLMaxD = 4096;                  // d_model limit (partial rows, accumulators)
 constexpr int kLMaxNA = 4;                    // gate/up ring stages (at most)
-constexpr int kLMaxNB = 16;                   // down ring stages (at most)
-constexpr int kHRec = 64;                      // one unit's h: 16 fp32
-constexpr int kHGrp = 4 * kHRec;               // one 64-group's digit record in shared memory
+constexpr int kLMaxND = 3;                    // down-unit ring stages (at most)
+constexpr int kLMaxNS = 2;                    // down-scale ring stages (at most)
+constexpr int kHRec = 64;                     // one unit's h digit record (shared memory)
 constexpr int kEpMaxWorld = 8;
+constexpr int kLRedMax = 8;                   // phase R: partial rows per thread (grid <= 256)
 
 struct LayerState {          // device scratch, zero at context creation; the counters zero after every launch
     uint32_t rdone;                 // router logit rows stored (a hint: the logits carry their own tag)
-    uint32_t arrive;                // CTAs past phase A
+    uint32_t unused;
     uint32_t done;                  // CTAs finished
     uint32_t epoch;                 // expert-parallel launches completed (advanced by the last CTA)
     uint32_t seq;                   // launches completed (advanced by the last CTA): tags this launch's logits
@@ -106,49 +110,56 @@ SMOE_DEVINL void cons_sync() {
 struct LayerGeom {
     int d, dff, k, ntok;
     TiledGeom tg;
-    int G, tilesU, outTiles, NA, NB;
-    uint32_t mg_tilesU, mg_outTiles, mg_Gd, mg_G, mg_k;   // division magics (divu below)
-    int o_xtab, o_xg, o_red, o_red2, o_bar, o_ids, o_w, o_loc, o_ringA, o_ringB, total;
+    int G, tilesU, outTiles, NA, ND, NS;
+    int dparts, bpp;           // a down unit streams in dparts parts of bpp 64-row blocks (512 B each)
+    uint32_t mg_tilesU, mg_outTiles, mg_G, mg_k;   // division magics (divu below)
+    int o_xtab, o_xg, o_red, o_red2, o_hrec, o_bar, o_ids, o_w, o_loc, o_ringA, o_ringD, o_ringS, total;
 
     __host__ __device__ bool init(int fmt, int d_, int dff_, int k_, int ntok_, int max_smem) {
         d = d_; dff = dff_; k = k_; ntok = ntok_;
-        if (!tg.init(fmt, d, dff) || tg.Gc > 32 || ntok < 1 || ntok > kLMaxTok || k < 1 || k > kLMaxK) return false;
+        if (!tg.init(fmt, d, dff) || tg.Gc > 32 || ntok < 1 || ntok > kLMaxTok || k < 1 || k > kLMaxK ||
+            d > kLMaxD)
+            return false;
         G = d / 64; tilesU = dff / 16; outTiles = d / 16;
+        dparts = d > 2048 ? 2 : 1;
+        bpp = (d / 64 + dparts - 1) / dparts;
         mg_tilesU = magic_of(uint32_t(tilesU));
         mg_outTiles = magic_of(uint32_t(outTiles));
-        mg_Gd = magic_of(tg.Gd);
         mg_G = magic_of(uint32_t(G));
         mg_k = magic_of(uint32_t(k));
         int off = 0;
         auto take = [&](int bytes) { int o = off; off += (bytes + 127) & ~127; return o; };
-        const int xt = G * 1024, hr = k * tilesU * kHRec;    // x table, then (phase B) one token's h records
-        o_xtab = take(xt > hr ? xt : hr);
+        o_xtab = take(G * 1024);                             // x table
         o_xg = take(G * 4 * 8);
-        const int rs = 2 * kLCons * 32 * 4, ps = 4 * kLMaxTok * kRouterMaxE;
-        o_red = take(rs);                                    // double-buffered unit partials / router partials
-        o_red2 = take(kLCons * 16 * 4);
-        o_bar = take((2 * kLMaxNA + 2 * kLMaxNB + 5) * 8);
+        o_red = take(2 * kLCons * 32 * 4);                   // double-buffered unit partials / router partials
+        o_red2 = take(32 * 16 * 4);                          // phase R: [32 CTA lanes][16 rows]
+        o_hrec = take(2 * kHRec);                            // double-buffered h digit records
+        o_bar = take((2 * kLMaxNA + 2 * kLMaxND + 2 * kLMaxNS + 9) * 8);
         o_ids = take(kLMaxTok * kLMaxK * 4);
         o_w = take(kLMaxTok * kLMaxK * 4);
         o_loc = take(4 * (kLMaxTok * kLMaxK + kLMaxTok + 2));  // local slots, token starts, count
-        (void)ps;
         off = (off + 1023) & ~1023;
         const int fixed = off;
         const int avail = max_smem - fixed;
-        const int ca = int((tg.chunk + 127) & ~127u), cb = int((tg.btile + 127) & ~127u);
-        NA = 3;
-        if (avail < 3 * ca + 2 * cb) NA = 2;
-        if (NA > kLMaxNA) NA = kLMaxNA;
-        NB = (avail - NA * ca) / cb;
-        if (NB > kLMaxNB) NB = kLMaxNB;
-        if (NB < 2) return false;
+        const int ca = stageA(), cd = stageD(), cs = stageS();
+        // gate/up chunks 3 (else 2) deep, down units 3 (else 2) deep, down
+        // scales 2 (else 1: a CTA's units then wait once per new scale group)
+        NA = avail >= 3 * ca + 2 * cd + 2 * cs ? 3 : 2;
+        ND = avail >= NA * ca + 3 * cd + 2 * cs ? 3 : 2;
+        NS = avail >= NA * ca + ND * cd + 2 * cs ? 2 : 1;
         o_ringA = fixed;
-        o_ringB = fixed + NA * ca;
-        total = o_ringB + NB * cb;
+        o_ringD = o_ringA + NA * ca;
+        o_ringS = o_ringD + ND * cd;
+        total = o_ringS + NS * cs;
         return total <= max_smem;
     }
     __host__ __device__ int stageA() const { return int((tg.chunk + 127) & ~127u); }
-    __host__ __device__ int stageB() const { return int((tg.btile + 127) & ~127u); }
+    __host__ __device__ int stageD() const { return bpp * 512; }
+    __host__ __device__ uint32_t dpart_bytes(int p) const {
+        const int nb = d / 64 - p * bpp;
+        return uint32_t((nb < bpp ? nb : bpp) * 512);
+    }
+    __host__ __device__ int stageS() const { return int((tg.sgrp + 127) & ~127u); }
 };
 
 struct LayerEp {
@@ -157,7 +168,7 @@ struct LayerEp {
     uint8_t* x0;               // rank 0's copy of x (peer memory on ranks > 0)
     uint32_t* flag0;           // rank 0's x epoch
     float* part0;              // [world][kLMaxTok * d] partial rows, in rank 0's window
-    uint32_t* cnt0;            // [kLMaxTok * d/16] partial B units arrived, in rank 0's window
+    uint32_t* cnt0;            // [kLMaxTok * d/16] partial row blocks arrived, in rank 0's window
     uint32_t part_stride;      // floats per rank in part0
 };
 
@@ -176,7 +187,7 @@ struct LayerArgs {
     const uint16_t* rw;        // router W [E x d] bf16, null: routing given
     int norm;
     unsigned long long* logits;  // scratch [ntok x E]: (launch tag << 32) | fp32 bits of the logit
-    uint8_t* hbuf;             // scratch h, fp32 [ntok*k][d_ff/16][16]
+    unsigned long long* part;  // scratch partial rows [grid][kLMaxTok][kLMaxD]: (launch tag << 32) | fp32 bits
     LayerState* st;
     uint32_t* err;
     uint64_t wait_ns;          // limit of every wait
@@ -224,6 +235,12 @@ static __device__ __noinline__ bool spin_geq(const uint32_t* p, uint32_t target,
 }
 
 SMOE_DEVINL void raise_err(uint32_t* err, uint32_t code) { atomicCAS(err, 0u, code); }
+
+SMOE_DEVINL uint32_t ld_relaxed_gpu_u32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
 
 SMOE_DEVINL void st_relaxed_gpu_u64(unsigned long long* p, uint64_t v) {
     asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" :: "l"(p), "l"(v) : "memory");
@@ -303,45 +320,6 @@ SMOE_DEVINL float scale2(float v, int e) {
     return (v * pow2i(a)) * pow2i(e - a);
 }
 
-// Digit record of one (slot, 64-group) of h for the down MMAs, built by a
-// half-warp (j = 0..15 its thread, v = h rows 4(j&3)..+3 of unit j>>2): one
-// exponent E for the group's 64 values, X = round(h * 2^(20-E)) (|X| <= 2^21)
-// offset to Xu = X + 2^21 in [0, 2^22] and split into three unsigned byte
-// planes. Plane p holds at p*64 + c*16 + u*4 + b the digit of unit u, row
-// 4c + b (lane 4g + c's B register of unit u = one 32-bit word, its four
-// units one 16-byte load); at 192 the fp32 pair (2^(E-20) (/7.5 for
-// SMOE-Q4), sum of the fixed-point h). The offset comes back out through a
-// column of ones in the MMA (sum q * X = sum q * Xu - 2^21 sum q). Every
-// lane of the warp calls it; `valid` is the same for the 16 threads of a group.
-template <int FMT>
-SMOE_DEVINL void h_digits(float4 v, uint8_t* rec, int j, bool valid) {
-    float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    // below 2^-100 every X rounds to 0 anyway; the clamp keeps 2^(20-E) a normal float
-    const int E = max(int((__float_as_uint(m) >> 23) & 0xff) - 127, -100);
-    const float f = pow2i(20 - E);
-    const int X[4] = {__float2int_rn(v.x * f), __float2int_rn(v.y * f), __float2int_rn(v.z * f),
-                      __float2int_rn(v.w * f)};
-    int sx = X[0] + X[1] + X[2] + X[3];
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) sx += __shfl_xor_sync(0xffffffffu, sx, o);
-    const uint32_t u0 = uint32_t(X[0] + (1 << 21)), u1 = uint32_t(X[1] + (1 << 21)),
-                   u2 = uint32_t(X[2] + (1 << 21)), u3 = uint32_t(X[3] + (1 << 21));
-    if (valid) {
-        uint32_t* w = reinterpret_cast<uint32_t*>(rec + (j & 3) * 16 + (j >> 2) * 4);
-#pragma unroll
-        for (int p = 0; p < 3; ++p)                      // byte p of each value: plane p
-            w[16 * p] = __byte_perm(__byte_perm(u0, u1, 0x0040u + 0x0011u * p),
-                                    __byte_perm(u2, u3, 0x0040u + 0x0011u * p), 0x5410u);
-        if (j == 0) {
-            const float xs = pow2i(E - 20);
-            *reinterpret_cast<float2*>(rec + 192) =
-                make_float2(FMT == kFmtAffine ? xs : xs * (1.0f / 7.5f), float(sx) * xs);
-        }
-    }
-}
-
 // x table of the gate/up MMAs, read straight from global x (ntok x K):
 // xtab[(grp*2 + set)*32 + lane] = the four B registers {b(even, k 0-15),
 // b(even, k 16-31), b(odd, k 0-15), b(odd, k 16-31)} of lane 4g + c, and
@@ -416,8 +394,9 @@ SMOE_DEVINL void build_xtab(const void* xsrc, int x_dtype, int ntok, int K, uint
     }
 }
 
-// GW: 64-groups of a gate/up chunk per consumer warp, ceil(Gc / 16)
-template <int FMT, int GW>
+// GW: 64-groups of a gate/up chunk per consumer warp, ceil(Gc / 16);
+// DB: 64-row blocks of the output per consumer warp, ceil(d / 1024)
+template <int FMT, int GW, int DB>
 __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
     extern __shared__ __align__(1024) uint8_t sm[];
     const LayerGeom& g = A.g;
@@ -430,22 +409,27 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
     float* red2 = reinterpret_cast<float*>(sm + g.o_red2);        // [16 warps][16]
     uint64_t* fullA = reinterpret_cast<uint64_t*>(sm + g.o_bar);
     uint64_t* emptyA = fullA + kLMaxNA;
-    uint64_t* fullB = emptyA + kLMaxNA;
-    uint64_t* emptyB = fullB + kLMaxNB;
-    uint64_t* redF = emptyB + kLMaxNB;                            // [2] unit partials written (16 arrivals)
+    uint64_t* fullD = emptyA + kLMaxNA;
+    uint64_t* emptyD = fullD + kLMaxND;
+    uint64_t* fullS = emptyD + kLMaxND;
+    uint64_t* emptyS = fullS + kLMaxNS;
+    uint64_t* redF = emptyS + kLMaxNS;                            // [2] unit partials written (16 arrivals)
     uint64_t* redE = redF + 2;                                    // [2] unit partials consumed (1 arrival)
     uint64_t* routed = redE + 2;                                  // s_ids / s_w / s_loc ready (1 arrival)
+    uint64_t* hF = routed + 1;                                    // [2] h digit record written (1 arrival)
+    uint64_t* hE = hF + 2;                                        // [2] h digit record consumed (16 arrivals)
+    uint8_t* hrec = sm + g.o_hrec;                                // [2][kHRec]
     uint32_t* s_ids = reinterpret_cast<uint32_t*>(sm + g.o_ids);
     float* s_w = reinterpret_cast<float*>(sm + g.o_w);
     uint32_t* s_loc = reinterpret_cast<uint32_t*>(sm + g.o_loc);  // local slots in slot order
     uint32_t* s_tok = s_loc + kLMaxTok * kLMaxK;                  // [ntok + 1] first local slot index per token
     uint32_t* s_nloc = s_tok + kLMaxTok + 1;
     uint8_t* ringA = sm + g.o_ringA;
-    uint8_t* ringB = sm + g.o_ringB;
-    const int NA = g.NA, NB = g.NB, k = g.k, d = g.d;
+    uint8_t* ringD = sm + g.o_ringD;
+    uint8_t* ringS = sm + g.o_ringS;
+    const int NA = g.NA, NS = g.NS, k = g.k, d = g.d;
     const uint32_t nslots = uint32_t(g.ntok * k);
     const int cta = blockIdx.x, ncta = gridDim.x;
-    __shared__ uint32_t last_cta;
 
     ltrace(A.trace, 0);
     // inputs (x, routing) may come from the previous kernel in the stream
@@ -455,8 +439,10 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
     const WaitBudget wb{A.wait_ns, gtimer() + 8 * A.wait_ns};
     const LayerEp& ep = A.ep;
     const bool epm = ep.world > 1;
-    const uint32_t epoch = epm ? A.st->epoch + 1u : 0u;           // written by the previous launch only
-    const uint32_t seq = A.st->seq + 1u;                          // this launch's tag (never 0 in use)
+    // (read before the set-up barrier: the last CTA past its producer loop
+    // advances them)
+    const uint32_t epoch = epm ? ld_relaxed_gpu_u32(&A.st->epoch) + 1u : 0u;
+    const uint32_t seq = ld_relaxed_gpu_u32(&A.st->seq) + 1u;     // this launch's tag (never 0 in use)
     // x: the caller's, or on ranks > 0 rank 0's published copy (peer memory)
     const void* xsrc = A.x;
     if (epm) {
@@ -487,12 +473,18 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
     if (tid < kLMaxNA) {
         mbar_init(fullA + tid, 1);
         mbar_init(emptyA + tid, kLCons);
-    } else if (tid >= 32 && tid < 32 + kLMaxNB) {
-        mbar_init(fullB + (tid - 32), 1);
-        mbar_init(emptyB + (tid - 32), kLCons);
+    } else if (tid >= 32 && tid < 32 + kLMaxND) {
+        mbar_init(fullD + (tid - 32), 1);
+        mbar_init(emptyD + (tid - 32), kLCons);
+    } else if (tid >= 40 && tid < 40 + kLMaxNS) {
+        mbar_init(fullS + (tid - 40), 1);
+        mbar_init(emptyS + (tid - 40), kLCons);
     } else if (tid >= 8 && tid < 10) {
         mbar_init(redF + (tid - 8), kLCons);
         mbar_init(redE + (tid - 8), 1);
+    } else if (tid >= 12 && tid < 14) {
+        mbar_init(hF + (tid - 12), 1);
+        mbar_init(hE + (tid - 12), kLCons);
     } else if (tid == 10) {
         mbar_init(routed, 1);
     } else if (tid == 11) {
@@ -522,6 +514,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         a0 = int(divu(uint32_t(cta) * uint32_t(nA), uint32_t(ncta), A.mg_grid));
         a1 = int(divu(uint32_t(cta + 1) * uint32_t(nA), uint32_t(ncta), A.mg_grid));
     };
+    // phase R: row blocks (token, 16 output rows) of y
     const int nB = g.ntok * g.outTiles;
     const int b0 = int(divu(uint32_t(cta) * uint32_t(nB), uint32_t(ncta), A.mg_grid)),
               b1 = int(divu(uint32_t(cta + 1) * uint32_t(nB), uint32_t(ncta), A.mg_grid));
@@ -594,84 +587,46 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         __syncwarp();
     };
     // producer lane: issue every copy of the CTA, gate/up chunks first
+    // Order per unit: its gate/up chunks, its down scales when the unit starts
+    // a new (slot, scale group), its down unit. One issue site per ring, no
+    // integer division in the loop (each costs ~100 cycles on this lane's
+    // critical path): every index advances by counters.
     auto produce = [&]() {
         int a0, a1;
         a_range(a0, a1);
-        const int nAi = (a1 - a0) * int(tg.nchunk);
-        int nBi = 0;
-        {
-            int t = int(divu(uint32_t(b0), uint32_t(g.outTiles), g.mg_outTiles)), o = b0 - t * g.outTiles;
-            for (int b = b0; b < b1; ++b) {
-                nBi += max(int(tok_at(t + 1)) - int(tok_at(t)), 0);
-                if (++o == g.outTiles) { o = 0; ++t; }
-            }
-        }
-        // One issue site (code size: this runs cold once per launch), and no
-        // integer division in the loop (each costs ~100 cycles of latency on
-        // this lane's critical path): every index advances by counters.
-        // Order: the first NA gate/up chunks, the first NB down parts, then
-        // the rest of each as stages free up.
-        int iA = 0, iB = 0;
-        int ali = int(divu(uint32_t(a0), uint32_t(g.tilesU), g.mg_tilesU)), au = a0 - ali * g.tilesU, ac = 0;          // next A item: (local slot, unit, chunk)
-        int stA = 0, rA = 0, stB = 0, rB = 0;
-        for (; iA < preA; ++iA) {              // issued already by the head start below
-            if (++ac == int(tg.nchunk)) {
-                ac = 0;
-                if (++au == g.tilesU) { au = 0; ++ali; }
-            }
-            if (++stA == NA) { stA = 0; ++rA; }
-        }
-        int bt = int(divu(uint32_t(b0), uint32_t(g.outTiles), g.mg_outTiles)), bo = b0 - bt * g.outTiles, bb = b0;     // next B part: (token, tile), slot jj
-        int jj = b0 < b1 ? int(tok_at(bt)) : 0;
+        int li = int(divu(uint32_t(a0), uint32_t(g.tilesU), g.mg_tilesU)), u = a0 - li * g.tilesU;
+        int iA = 0, stA = 0, rA = 0, stD = 0, rD = 0, stS = 0, rS = 0, sg_li = -1, sg_j = -1;
         ltrace(A.trace, 11, true);
-        const int limA0 = min(NA, nAi), limB0 = min(NB, nBi);
 #pragma unroll 1
-        for (int step = 0; step < 4; ++step) {
-#ifdef SMOE_EXP_BFIRST
-            const bool isA = (step & 1) == 1;
-#else
-            const bool isA = (step & 1) == 0;
-#endif
-            const int lim = isA ? (step < 2 ? limA0 : nAi) : (step < 2 ? limB0 : nBi);
-            if (step == 1) ltrace(A.trace, 17, true);
+        for (int a = a0; a < a1; ++a) {
+            const uint8_t* ex = expert_of(slot_at(uint32_t(li)));
 #pragma unroll 1
-            while ((isA ? iA : iB) < lim) {
-                const int st = isA ? stA : stB, r = isA ? rA : rB;
-                uint64_t* full = (isA ? fullA : fullB) + st;
-                if (r > 0 && !mbar_wait_b((isA ? emptyA : emptyB) + st, (r - 1) & 1, wb))
-                    raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
-                uint64_t off;
-                uint32_t slot, bytes;
-                uint8_t* dst;
-                if (isA) {
-                    slot = slot_at(uint32_t(ali));
-                    off = tg.chunk_off(au, ac);
-                    bytes = tg.chunk;
-                    dst = ringA + size_t(st) * g.stageA();
-                    if (++ac == int(tg.nchunk)) {
-                        ac = 0;
-                        if (++au == g.tilesU) { au = 0; ++ali; }
-                    }
-                    ++iA;
-                    if (++stA == NA) { stA = 0; ++rA; }
-                } else {
-                    while (jj >= int(tok_at(bt + 1)) && bb < b1) {   // next B unit (skip tokens without local slots)
-                        ++bb;
-                        if (++bo == g.outTiles) { bo = 0; ++bt; }
-                        jj = int(tok_at(bt));
-                    }
-                    if (bb >= b1) break;
-                    slot = slot_at(uint32_t(jj));
-                    off = tg.btile_off(bo);
-                    bytes = tg.btile;
-                    dst = ringB + size_t(st) * g.stageB();
-                    ++jj;
-                    ++iB;
-                    if (++stB == NB) { stB = 0; ++rB; }
+            for (int c = 0; c < int(tg.nchunk); ++c, ++iA) {
+                if (iA >= preA) {                       // (the head start issued the first preA)
+                    if (rA > 0 && !mbar_wait_b(emptyA + stA, (rA - 1) & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+                    mbar_arrive_expect_tx(fullA + stA, tg.chunk);
+                    bulk_g2s(ringA + size_t(stA) * g.stageA(), ex + tg.chunk_off(u, c), tg.chunk, fullA + stA);
                 }
-                mbar_arrive_expect_tx(full, bytes);
-                bulk_g2s(dst, expert_of(slot) + off, bytes, full);
+                if (++stA == NA) { stA = 0; ++rA; }
             }
+            if (li != sg_li || (u >> 2) != sg_j) {
+                sg_li = li;
+                sg_j = u >> 2;
+                if (rS > 0 && !mbar_wait_b(emptyS + stS, (rS - 1) & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+                mbar_arrive_expect_tx(fullS + stS, tg.sgrp);
+                bulk_g2s(ringS + size_t(stS) * g.stageS(), ex + tg.sgrp_off(uint32_t(sg_j)), tg.sgrp, fullS + stS);
+                if (++stS == NS) { stS = 0; ++rS; }
+            }
+#pragma unroll 1
+            for (int p = 0; p < g.dparts; ++p) {
+                if (rD > 0 && !mbar_wait_b(emptyD + stD, (rD - 1) & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+                const uint32_t bytes = g.dpart_bytes(p);
+                mbar_arrive_expect_tx(fullD + stD, bytes);
+                bulk_g2s(ringD + size_t(stD) * g.stageD(), ex + tg.dunit_off(uint32_t(u)) + size_t(p) * g.stageD(), bytes,
+                         fullD + stD);
+                if (++stD == g.ND) { stD = 0; ++rD; }
+            }
+            if (++u == g.tilesU) { u = 0; ++li; }
         }
         ltrace(A.trace, 12, true);
     };
@@ -755,6 +710,19 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         if (lane == 0) {
             if (!mbar_wait_b(routed, 0, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
             produce();
+            // This CTA is done with the launch state (its threads read seq and
+            // epoch before the set-up barrier; its row-count wait has passed):
+            // the last CTA to get here resets it for the next launch. (No
+            // fence: the next launch reads it only after this grid has
+            // completed - stream order or griddepcontrol.wait.)
+            uint32_t old;
+            asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(&A.st->done) : "memory");
+            if (old == uint32_t(ncta) - 1) {
+                A.st->done = 0;
+                A.st->rdone = 0;
+                A.st->seq = seq;
+                if (epm) A.st->epoch = epoch;
+            }
         }
         __syncwarp();
     }
@@ -773,245 +741,272 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         int ali = int(divu(uint32_t(a0), uint32_t(g.tilesU), g.mg_tilesU)), au = a0 - ali * g.tilesU;
         uint32_t slot = slot_at(uint32_t(ali));
         int tok = int(divu(slot, uint32_t(k), g.mg_k));
-        #pragma unroll 1
-        for (int a = a0; a < a1; ++a) {
-            const int n = a - a0, b = n & 1;
-            float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
-            #pragma unroll 1
-            for (int c = 0; c < int(tg.nchunk); ++c, ++iA) {
-                const int st = stA;
-                if (!mbar_wait_b(fullA + st, rA & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
-                if (++stA == NA) { stA = 0; ++rA; }
-                if (n == 0 && c == 0) ltrace(A.trace, 4);
-                if (iA < 3) ltrace(A.trace, 25 + iA);
-                if (a + 1 == a1 && c + 1 == int(tg.nchunk)) ltrace(A.trace, 14);
-                const uint8_t* sp = ringA + size_t(st) * g.stageA();
-                const uint8_t* sbp = sp + 2 * tg.fragC;          // [gate sb][up sb]
-                uint4 w[GW][2];
+        // Down side: unit n - 1 runs after the gate/up of unit n (the h warp
+        // turns unit n - 1's partials into its digit record meanwhile). Warp
+        // w owns row blocks b = w + 16 i (64 rows each); lanes c = 0 (digit
+        // planes 0-1) and c = 1 (plane 2) keep partial sums of rows g, g + 8
+        // of each of a block's four tiles, per token, flushed to the CTA's
+        // partial rows when the token changes and at the end.
+        const int nblk = d >> 6;
+        constexpr int DBP = DB == 4 ? 2 : DB;                      // blocks per warp per down part
+        float dacc[DB][2][2];
+        int dli = ali, du = au, stD = 0, rD = 0, stS = 0, rS = 0, sg_li = -1, sg_j = -1, acc_t = -1;
+        auto flush = [&](int t) {
+            unsigned long long* pr = A.part + (size_t(cta) * kLMaxTok + t) * kLMaxD;
 #pragma unroll
-                for (int j = 0; j < GW; ++j) {
-                    const int gl = min(warp + j * kLCons, int(tg.Gc) - 1);
+            for (int i = 0; i < DB; ++i) {
+                const int lb = warp + kLCons * (i % DBP), bk = (i / DBP) * g.bpp + lb;
 #pragma unroll
-                    for (int m = 0; m < 2; ++m)
-                        w[j][m] = *reinterpret_cast<const uint4*>(sp + m * tg.fragC + (gl * 32 + lane) * 16);
+                for (int pq = 0; pq < 2; ++pq)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        // lanes c, c ^ 1: planes 0-1 and plane 2 of tile 2pq + c / 2
+                        const float v = dacc[i][pq][h] + __shfl_xor_sync(0xffffffffu, dacc[i][pq][h], 1);
+                        if ((cq & 1) == 0 && lb < g.bpp && bk < nblk)
+                            st_relaxed_gpu_u64(pr + 64 * bk + 16 * (2 * pq + (cq >> 1)) + gr + 8 * h,
+                                               (uint64_t(seq) << 32) | __float_as_uint(v));
+                        dacc[i][pq][h] = 0.f;
+                    }
+            }
+        };
+        auto down = [&](int n, bool last) {
+            const int t = int(divu(slot_at(uint32_t(dli)), uint32_t(k), g.mg_k));
+            if (t != acc_t) {
+                if (acc_t >= 0) flush(acc_t);
+                else {
+#pragma unroll
+                    for (int i = 0; i < DB; ++i)
+#pragma unroll
+                        for (int pq = 0; pq < 2; ++pq) dacc[i][pq][0] = dacc[i][pq][1] = 0.f;
                 }
+                acc_t = t;
+            }
+            if (dli != sg_li || (du >> 2) != sg_j) {             // a new (slot, scale group)
+                if (sg_li >= 0) {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(emptyS + stS);
+                    if (++stS == NS) { stS = 0; ++rS; }
+                }
+                sg_li = dli;
+                sg_j = du >> 2;
+                if (!mbar_wait_b(fullS + stS, rS & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+            }
+            const int hb = n & 1;
+            if (!mbar_wait_b(hF + hb, (n >> 1) & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+            if (last) ltrace(A.trace, 17);
+            const uint8_t* rec = hrec + hb * kHRec;
+            // One MMA m16n8k32 covers two row tiles: k 0-15 = the even tile's
+            // codes x digit planes in columns 0-2, k 16-31 = the odd tile's x the
+            // same planes in columns 4-6. Lane c then holds (c even) planes 0-1
+            // or (c odd) plane 2 of tile c / 2 of the pair.
+            const uint32_t pl = *reinterpret_cast<const uint32_t*>(rec + (gr & 3) * 16 + cq * 4);
+            const uint32_t bq[2] = {gr < 3 ? pl : 0u, gr >= 4 && gr < 7 ? pl : 0u};
+            const float2 xsv = *reinterpret_cast<const float2*>(rec + 48);
+            const float xsl = (cq & 1) ? xsv.x * 65536.0f : xsv.x;
+            const float shl = (cq & 1) ? 0.f : xsv.y;              // the sum term once
+            const uint8_t* sp = ringS + size_t(stS) * g.stageS();
+            constexpr uint32_t lo = 0x0F0F0F0Fu;
 #pragma unroll
-                for (int j = 0; j < GW; ++j) {
-                    const int gl = warp + j * kLCons;
-                    if (gl < int(tg.Gc)) {
-                        const int grp = c * int(tg.Gc) + gl;
-                        const float2 xv = xg[grp * 4 + cq];
-                        const uint4 bA = xtab[(grp * 2) * 32 + lane], bB = xtab[(grp * 2 + 1) * 32 + lane];
-                        const uint32_t be[2] = {bA.x, bA.y}, bo[2] = {bA.z, bA.w};
-                        const uint32_t be2[2] = {bB.x, bB.y}, bo2[2] = {bB.z, bB.w};
+            for (int i = 0; i < DB; ++i) {
+                const int p = i / DBP, lb = warp + kLCons * (i % DBP), bk = p * g.bpp + lb;
+                if (i % DBP == 0) {                                   // the part's blocks are in its stage
+                    if (i > 0) {
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(emptyD + stD);
+                        if (++stD == g.ND) { stD = 0; ++rD; }
+                    }
+                    if (!mbar_wait_b(fullD + stD, rD & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+                    if (last && i == 0) ltrace(A.trace, 18);
+                }
+                const uint8_t* dp = ringD + size_t(stD) * g.stageD();
+                if (lb < g.bpp && bk < nblk) {
+                    const uint4 wq = *reinterpret_cast<const uint4*>(dp + (lb * 32 + lane) * 16);
 #pragma unroll
-                        for (int m = 0; m < 2; ++m) {
-                            const uint32_t ae[4] = {w[j][m].x & 0x0F0F0F0Fu, w[j][m].y & 0x0F0F0F0Fu,
-                                                    w[j][m].z & 0x0F0F0F0Fu, w[j][m].w & 0x0F0F0F0Fu};
-                            const uint32_t ao[4] = {w[j][m].x & 0xF0F0F0F0u, w[j][m].y & 0xF0F0F0F0u,
-                                                    w[j][m].z & 0xF0F0F0F0u, w[j][m].w & 0xF0F0F0F0u};
-                            int de[4] = {0, 0, 0, 0}, dO[4] = {0, 0, 0, 0}, de2[4] = {0, 0, 0, 0}, dO2[4] = {0, 0, 0, 0};
-                            mma_u8s8_16832(de, ae, be);
-                            mma_u8s8_16832(dO, ao, bo);
-                            mma_u8s8_16832(de2, ae, be2);
-                            mma_u8s8_16832(dO2, ao, bo2);
-                            const float v0 = fmaf(float(16 * de2[0] + dO2[0]), 65536.0f,
-                                                  float((16 * de[0] + dO[0]) + 256 * (16 * de[1] + dO[1])));
-                            const float v8 = fmaf(float(16 * de2[2] + dO2[2]), 65536.0f,
-                                                  float((16 * de[2] + dO[2]) + 256 * (16 * de[3] + dO[3])));
-                            if (FMT == kFmtAffine) {
-                                const uint32_t* sbw = reinterpret_cast<const uint32_t*>(sbp + m * tg.sbC) + gl * 16 + gr;
-                                const uint32_t s0 = sbw[0], s8 = sbw[8];
-                                acc[m][0] += fmaf(bf16_bits_to_f32(uint16_t(s0)), v0 * xv.x,
-                                                  bf16_bits_to_f32(uint16_t(s0 >> 16)) * xv.y);
-                                acc[m][1] += fmaf(bf16_bits_to_f32(uint16_t(s8)), v8 * xv.x,
-                                                  bf16_bits_to_f32(uint16_t(s8 >> 16)) * xv.y);
-                            } else {
-                                const uint16_t* sbh = reinterpret_cast<const uint16_t*>(sbp + m * tg.sbC) + gl * 16 + gr;
-                                acc[m][0] += f16_bits_to_f32(sbh[0]) * fmaf(v0, xv.x, -xv.y);
-                                acc[m][1] += f16_bits_to_f32(sbh[8]) * fmaf(v8, xv.x, -xv.y);
-                            }
+                    for (int pq = 0; pq < 2; ++pq) {                  // tiles 2pq (low nibbles), 2pq + 1 (high)
+                        const uint32_t w0 = pq == 0 ? wq.x : wq.z, w1 = pq == 0 ? wq.y : wq.w;
+                        const uint32_t af[4] = {w0 & lo, w1 & lo, (w0 >> 4) & lo, (w1 >> 4) & lo};
+                        int dq[4] = {0, 0, 0, 0};
+                        mma_u8s8_16832(dq, af, bq);
+                        // (for c odd, column 2c + 1 is a zero column: dq[1] = dq[3] = 0)
+                        const int r0 = 64 * bk + 16 * (2 * pq + (cq >> 1)) + gr;
+                        const float v0 = float(dq[0] + 256 * dq[1]) * xsl, v8 = float(dq[2] + 256 * dq[3]) * xsl;
+                        if (FMT == kFmtAffine) {
+                            const uint32_t s0 = reinterpret_cast<const uint32_t*>(sp)[r0];
+                            const uint32_t s8 = reinterpret_cast<const uint32_t*>(sp)[r0 + 8];
+                            dacc[i][pq][0] += fmaf(bf16_bits_to_f32(uint16_t(s0)), v0, bf16_bits_to_f32(uint16_t(s0 >> 16)) * shl);
+                            dacc[i][pq][1] += fmaf(bf16_bits_to_f32(uint16_t(s8)), v8, bf16_bits_to_f32(uint16_t(s8 >> 16)) * shl);
+                        } else {
+                            const uint16_t* sh = reinterpret_cast<const uint16_t*>(sp);
+                            dacc[i][pq][0] += f16_bits_to_f32(sh[r0]) * (v0 - shl);
+                            dacc[i][pq][1] += f16_bits_to_f32(sh[r0 + 8]) * (v8 - shl);
                         }
                     }
                 }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(emptyA + st);          // chunk fully consumed
-            }
-            // the unit's warp partials -> buffer b (free once the h warp read use n-2)
-            if (n >= 2 && !mbar_wait_b(redE + b, ((n >> 1) - 1) & 1, wb))
-                raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
-            float* rb = red + (b * kLCons + warp) * 32;
-            if (cq == tok) {
-                rb[gr] = acc[0][0];
-                rb[gr + 8] = acc[0][1];
-                rb[16 + gr] = acc[1][0];
-                rb[16 + gr + 8] = acc[1][1];
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(redF + b);
-            if (++au == g.tilesU) {
-                au = 0;
-                slot = slot_at(uint32_t(++ali));
-                tok = int(divu(slot, uint32_t(k), g.mg_k));
+            if (lane == 0) {
+                mbar_arrive(hE + hb);
+                mbar_arrive(emptyD + stD);
             }
+            if (++stD == g.ND) { stD = 0; ++rD; }
+            if (++du == g.tilesU) { du = 0; ++dli; }
+        };
+        #pragma unroll 1
+        for (int a = a0; a <= a1; ++a) {
+            const int n = a - a0, b = n & 1;
+            if (a < a1) {
+                float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+                #pragma unroll 1
+                for (int c = 0; c < int(tg.nchunk); ++c, ++iA) {
+                    const int st = stA;
+                    if (!mbar_wait_b(fullA + st, rA & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+                    if (++stA == NA) { stA = 0; ++rA; }
+                    if (n == 0 && c == 0) ltrace(A.trace, 4);
+                    if (iA < 3) ltrace(A.trace, 25 + iA);
+                    if (a + 1 == a1 && c + 1 == int(tg.nchunk)) ltrace(A.trace, 14);
+                    const uint8_t* sp = ringA + size_t(st) * g.stageA();
+                    const uint8_t* sbp = sp + 2 * tg.fragC;          // [gate sb][up sb]
+                    uint4 w[GW][2];
+    #pragma unroll
+                    for (int j = 0; j < GW; ++j) {
+                        const int gl = min(warp + j * kLCons, int(tg.Gc) - 1);
+    #pragma unroll
+                        for (int m = 0; m < 2; ++m)
+                            w[j][m] = *reinterpret_cast<const uint4*>(sp + m * tg.fragC + (gl * 32 + lane) * 16);
+                    }
+    #pragma unroll
+                    for (int j = 0; j < GW; ++j) {
+                        const int gl = warp + j * kLCons;
+                        if (gl < int(tg.Gc)) {
+                            const int grp = c * int(tg.Gc) + gl;
+                            const float2 xv = xg[grp * 4 + cq];
+                            const uint4 bA = xtab[(grp * 2) * 32 + lane], bB = xtab[(grp * 2 + 1) * 32 + lane];
+                            const uint32_t be[2] = {bA.x, bA.y}, bo[2] = {bA.z, bA.w};
+                            const uint32_t be2[2] = {bB.x, bB.y}, bo2[2] = {bB.z, bB.w};
+    #pragma unroll
+                            for (int m = 0; m < 2; ++m) {
+                                const uint32_t ae[4] = {w[j][m].x & 0x0F0F0F0Fu, w[j][m].y & 0x0F0F0F0Fu,
+                                                        w[j][m].z & 0x0F0F0F0Fu, w[j][m].w & 0x0F0F0F0Fu};
+                                const uint32_t ao[4] = {w[j][m].x & 0xF0F0F0F0u, w[j][m].y & 0xF0F0F0F0u,
+                                                        w[j][m].z & 0xF0F0F0F0u, w[j][m].w & 0xF0F0F0F0u};
+                                int de[4] = {0, 0, 0, 0}, dO[4] = {0, 0, 0, 0}, de2[4] = {0, 0, 0, 0}, dO2[4] = {0, 0, 0, 0};
+                                mma_u8s8_16832(de, ae, be);
+                                mma_u8s8_16832(dO, ao, bo);
+                                mma_u8s8_16832(de2, ae, be2);
+                                mma_u8s8_16832(dO2, ao, bo2);
+                                const float v0 = fmaf(float(16 * de2[0] + dO2[0]), 65536.0f,
+                                                      float((16 * de[0] + dO[0]) + 256 * (16 * de[1] + dO[1])));
+                                const float v8 = fmaf(float(16 * de2[2] + dO2[2]), 65536.0f,
+                                                      float((16 * de[2] + dO[2]) + 256 * (16 * de[3] + dO[3])));
+                                if (FMT == kFmtAffine) {
+                                    const uint32_t* sbw = reinterpret_cast<const uint32_t*>(sbp + m * tg.sbC) + gl * 16 + gr;
+                                    const uint32_t s0 = sbw[0], s8 = sbw[8];
+                                    acc[m][0] += fmaf(bf16_bits_to_f32(uint16_t(s0)), v0 * xv.x,
+                                                      bf16_bits_to_f32(uint16_t(s0 >> 16)) * xv.y);
+                                    acc[m][1] += fmaf(bf16_bits_to_f32(uint16_t(s8)), v8 * xv.x,
+                                                      bf16_bits_to_f32(uint16_t(s8 >> 16)) * xv.y);
+                                } else {
+                                    const uint16_t* sbh = reinterpret_cast<const uint16_t*>(sbp + m * tg.sbC) + gl * 16 + gr;
+                                    acc[m][0] += f16_bits_to_f32(sbh[0]) * fmaf(v0, xv.x, -xv.y);
+                                    acc[m][1] += f16_bits_to_f32(sbh[8]) * fmaf(v8, xv.x, -xv.y);
+                                }
+                            }
+                        }
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(emptyA + st);          // chunk fully consumed
+                }
+                // the unit's warp partials -> buffer b (free once the h warp read use n-2)
+                if (n >= 2 && !mbar_wait_b(redE + b, ((n >> 1) - 1) & 1, wb))
+                    raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+                float* rb = red + (b * kLCons + warp) * 32;
+                if (cq == tok) {
+                    rb[gr] = acc[0][0];
+                    rb[gr + 8] = acc[0][1];
+                    rb[16 + gr] = acc[1][0];
+                    rb[16 + gr + 8] = acc[1][1];
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(redF + b);
+                if (++au == g.tilesU) {
+                    au = 0;
+                    slot = slot_at(uint32_t(++ali));
+                    tok = int(divu(slot, uint32_t(k), g.mg_k));
+                }
+            }
+            if (a == a1) ltrace(A.trace, 20);
+            if (n > 0) down(n - 1, a == a1);
+            if (a == a1) ltrace(A.trace, 19);
+            if (n == 1) ltrace(A.trace, 13);
         }
+        if (acc_t >= 0) flush(acc_t);
         ltrace(A.trace, 5);
 
-        // ------------------------------------------------ phase B
+        ltrace(A.trace, 16);
+
+        // ------------------------------------------------ phase R
+        // Row block (token t, rows 16o..16o+15): the sum of the partial rows
+        // of the CTAs whose unit ranges hold t's units, in CTA order - thread
+        // (j, r) adds CTAs c_lo + j, + 32, ... of row r, then one thread per
+        // row adds the 32 in j order (fixed order: bitwise repeatable). The
+        // partial rows carry this launch's tag: no grid-wide barrier, each
+        // thread polls its own values until every tag is there.
         if (b0 < b1) {
-            // the first wave's down parts stream in during phase A: wait for
-            // them before the grid-wide wait, which is the longer one
-            int pre_w = 0;
-            {
-                const int t0 = int(divu(uint32_t(b0), uint32_t(g.outTiles), g.mg_outTiles)), l0 = int(tok_at(t0));
-                pre_w = min(NB, max(l0, min(int(tok_at(t0 + 1)), l0 + k)) - l0);
-                #pragma unroll 1
-                for (int q = 0; q < pre_w; ++q)
-                    if (!mbar_wait_b(fullB + q, 0, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
-            }
-            if (tid == 0 && !spin_geq<false>(&A.st->arrive, uint32_t(ncta), wb))
-                raise_err(A.err, SMOE_DEVERR_SPIN_TIMEOUT);
-            cons_sync();
-            ltrace(A.trace, 6);
-            uint8_t* hsm = reinterpret_cast<uint8_t*>(xtab);          // the x table is no longer needed
-            int cur = -1, stB = 0, rB = 0;
-            const uint32_t bones = gr == 3 ? 0x01010101u : 0u;        // B column 3 of the down MMAs
-            const int cmul = cq == 0 ? 256 : -32;
+            const int r = tid & 15, j = tid >> 4;
+            const uint32_t nA = nloc() * uint32_t(g.tilesU);
             int t = int(divu(uint32_t(b0), uint32_t(g.outTiles), g.mg_outTiles)), o = b0 - t * g.outTiles - 1;
             #pragma unroll 1
             for (int bu = b0; bu < b1; ++bu) {
                 if (++o == g.outTiles) { o = 0; ++t; }
-                const int ls = int(tok_at(t)), le = max(ls, min(int(tok_at(t + 1)), ls + k));
-                if (t != cur) {
-                    // this token's h (local slots ls..le) into shared memory as
-                    // digit records, one per (slot, 64-group): 16 threads (a
-                    // half-warp) per group, 4 values each
-                    if (cur >= 0) cons_sync();                        // the previous token's are done with
-                    const float4* src = reinterpret_cast<const float4*>(A.hbuf + size_t(ls) * g.tilesU * kHRec);
-                    const int n16 = (le - ls) * g.tilesU * (kHRec / 16);   // a multiple of 16
-                    constexpr int U = 4;
-#pragma unroll 1
-                    for (int base = 0; base < n16; base += U * kLCThreads) {
-                        float4 v[U];
-#pragma unroll
-                        for (int q = 0; q < U; ++q) {
-                            const int i = base + q * kLCThreads + tid;
-                            v[q] = i < n16 ? __ldcg(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-                        }
-#pragma unroll
-                        for (int q = 0; q < U; ++q) {
-                            const int i = base + q * kLCThreads + tid;
-                            h_digits<FMT>(v[q], hsm + size_t(i >> 4) * kHGrp, i & 15, i < n16);
-                        }
-                    }
-                    cons_sync();
-                    if (cur < 0) ltrace(A.trace, 16);
-                    cur = t;
+                const uint32_t ulo = tok_at(t) * uint32_t(g.tilesU), uhi = tok_at(t + 1) * uint32_t(g.tilesU);
+                // CTA c holds units [c nA / grid, (c+1) nA / grid): unit u is in
+                // CTA ((u + 1) grid - 1) / nA
+                int c_lo = 0, c_hi = -1;
+                if (uhi > ulo) {
+                    c_lo = int(((ulo + 1) * uint32_t(ncta) - 1) / nA);
+                    c_hi = min(int((uhi * uint32_t(ncta) - 1) / nA), ncta - 1);
                 }
-                // The token's parts (local slots) stream through the ring in
-                // waves of at most NB: every warp waits for all parts of a
-                // wave, takes its share of the wave's (part, 64-group)
-                // items, then releases all of the wave's stages. (A warp
-                // releases a stage only after that stage's new data arrived,
-                // so its arrival always counts toward the right round.)
-                float y0 = 0.f, y8 = 0.f;
+                float pv[kLRedMax];
+                uint32_t need = 0;                                 // bit m: value m still to arrive
+                const unsigned long long* col = A.part + size_t(t) * kLMaxD + o * 16 + r;
+#pragma unroll
+                for (int m = 0; m < kLRedMax; ++m) {
+                    const int c = c_lo + j + 32 * m;
+                    pv[m] = 0.f;
+                    if (c <= c_hi && divu(uint32_t(c + 1) * nA, uint32_t(ncta), A.mg_grid) >
+                                         divu(uint32_t(c) * nA, uint32_t(ncta), A.mg_grid))
+                        need |= 1u << m;
+                }
+                const uint64_t deadline = wb.deadline();
                 #pragma unroll 1
-                for (int w0 = ls; w0 < le; w0 += NB) {
-                    const int W = min(NB, le - w0);
-                    if (pre_w > 0) {
-                        pre_w = 0;                    // the first wave: waited for above
-                    } else {
-                        int sb = stB, rb = rB;
-                        #pragma unroll 1
-                        for (int q = 0; q < W; ++q) {
-                            if (!mbar_wait_b(fullB + sb, rb & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
-                            if (++sb == NB) { sb = 0; ++rb; }
+                for (uint32_t it = 0; need; ++it) {
+                    uint64_t v[kLRedMax];
+#pragma unroll
+                    for (int m = 0; m < kLRedMax; ++m)
+                        if (need & (1u << m)) v[m] = ld_relaxed_gpu_u64(col + size_t(c_lo + j + 32 * m) * kLMaxTok * kLMaxD);
+#pragma unroll
+                    for (int m = 0; m < kLRedMax; ++m)
+                        if ((need & (1u << m)) && uint32_t(v[m] >> 32) == seq) {
+                            pv[m] = __uint_as_float(uint32_t(v[m]));
+                            need &= ~(1u << m);
                         }
+                    if (need && (it & 3) == 3 && gtimer() > deadline) {
+                        raise_err(A.err, SMOE_DEVERR_SPIN_TIMEOUT);
+                        break;
                     }
-                    if (w0 == ls && bu == b0) ltrace(A.trace, 13);
-                    const bool tr_items = w0 == ls && bu == b0;
-                    // this warp's items [i0, i1) of the wave's W x Gd (part, group) items
-                    const int nit = W * int(tg.Gd);
-                    const int i0 = (warp * nit) >> 4, i1 = ((warp + 1) * nit) >> 4;   // kLCons == 16
-                    int iq = int(divu(uint32_t(i0), tg.Gd, g.mg_Gd)), ig = i0 - iq * int(tg.Gd);
-                    int sidx = stB + iq;
-                    if (sidx >= NB) sidx -= NB;
-                    #pragma unroll 2
-                    for (int it = i0; it < i1; ++it) {
-                        // one (part, 64-group): four int8 MMAs m16n8k16, one per
-                        // 16-column unit, B = the unit's digit planes in columns 0-2
-                        const uint8_t* sp = ringB + size_t(sidx) * g.stageB();
-                        const uint4 wq = *reinterpret_cast<const uint4*>(sp + (ig * 32 + lane) * 16);
-                        const uint8_t* rec = hsm + (size_t(w0 + iq - ls) * tg.Gd + ig) * kHGrp;
-                        const uint4 bq = gr < 3 ? *reinterpret_cast<const uint4*>(rec + gr * 64 + cq * 16)
-                                                : make_uint4(bones, bones, bones, bones);   // column 3: ones
-                        const float2 xsv = *reinterpret_cast<const float2*>(rec + 192);
-                        // one exponent for the group: the four unit MMAs chain
-                        // into one exact int32 accumulator
-                        constexpr uint32_t lo = 0x0F0F0F0Fu;
-                        int dq[4] = {0, 0, 0, 0};
-                        {
-                            const uint32_t a0[2] = {wq.x & lo, wq.y & lo};
-                            mma_u8u8_16816(dq, a0, bq.x);
-                            const uint32_t a1[2] = {(wq.x >> 4) & lo, (wq.y >> 4) & lo};
-                            mma_u8u8_16816(dq, a1, bq.y);
-                            const uint32_t a2[2] = {wq.z & lo, wq.w & lo};
-                            mma_u8u8_16816(dq, a2, bq.z);
-                            const uint32_t a3[2] = {(wq.z >> 4) & lo, (wq.w >> 4) & lo};
-                            mma_u8u8_16816(dq, a3, bq.w);
-                        }
-                        // columns 0, 1 (planes p0, p1) are in lane c = 0, column 2 (p2)
-                        // in c = 1: each of the two lanes scales its own columns and
-                        // keeps its own partial (added together once per B unit)
-                        if (cq < 2) {
-                            // lane 0: p0 + 256 p1; lane 1: 65536 (p2 - 32 * ones) - exact
-                            const float xs = cq == 0 ? xsv.x : xsv.x * 65536.0f;
-                            const float s0 = float(dq[0] + cmul * dq[1]) * xs;
-                            const float s8 = float(dq[2] + cmul * dq[3]) * xs;
-                            const float sh = cq == 0 ? xsv.y : 0.f;          // the sum term once
-                            const uint8_t* sbp = sp + tg.bcodes;
-                            if (FMT == kFmtAffine) {
-                                const uint32_t* sbw = reinterpret_cast<const uint32_t*>(sbp) + ig * 16 + gr;
-                                const uint32_t w0s = sbw[0], w8s = sbw[8];
-                                y0 += fmaf(bf16_bits_to_f32(uint16_t(w0s)), s0, bf16_bits_to_f32(uint16_t(w0s >> 16)) * sh);
-                                y8 += fmaf(bf16_bits_to_f32(uint16_t(w8s)), s8, bf16_bits_to_f32(uint16_t(w8s >> 16)) * sh);
-                            } else {
-                                const uint16_t* sbh = reinterpret_cast<const uint16_t*>(sbp) + ig * 16 + gr;
-                                y0 += f16_bits_to_f32(sbh[0]) * (s0 - sh);
-                                y8 += f16_bits_to_f32(sbh[8]) * (s8 - sh);
-                            }
-                        }
-                        if (++ig == int(tg.Gd)) {
-                            ig = 0;
-                            ++iq;
-                            if (++sidx == NB) sidx = 0;
-                        }
-                    }
-                    if (tr_items) ltrace(A.trace, 21, lane == 0 && warp == 0);
-                    __syncwarp();
-                    if (lane == 0) {
-                        int sb = stB;
-                        #pragma unroll 1
-                        for (int q = 0; q < W; ++q) {
-                            mbar_arrive(emptyB + sb);
-                            if (++sb == NB) sb = 0;
-                        }
-                    }
-                    stB += W;                                         // W <= NB
-                    if (stB >= NB) { stB -= NB; ++rB; }
+                    if (need && it >= 8) __nanosleep(32);
                 }
-                y0 += __shfl_down_sync(0xffffffffu, y0, 1);         // + the p2 columns' partial
-                y8 += __shfl_down_sync(0xffffffffu, y8, 1);
-                if (cq == 0) {
-                    red2[warp * 16 + gr] = y0;
-                    red2[warp * 16 + gr + 8] = y8;
-                }
+                if (bu == b0) ltrace(A.trace, 6);
+                float s = 0.f;
+#pragma unroll
+                for (int m = 0; m < kLRedMax; ++m) s += pv[m];
+                red2[j * 16 + r] = s;
                 cons_sync();
                 if (bu == b0) ltrace(A.trace, 15);
                 if (tid < 16) {                                   // warp 0, lanes 0-15: row 16o + tid
-                    float s = 0.f;
+                    s = 0.f;
 #pragma unroll
-                    for (int w = 0; w < kLCons; ++w) s += red2[w * 16 + tid];
+                    for (int jj = 0; jj < 32; ++jj) s += red2[jj * 16 + tid];
                     const size_t yi = size_t(t) * d + o * 16 + tid;
                     bool write = true;
                     if (epm && ep.rank > 0) {
@@ -1024,7 +1019,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
                         if (tid == 0 && !spin_geq<true>(ep.cnt0 + bu, uint32_t(ep.world - 1), wb))
                             raise_err(A.err, SMOE_DEVERR_SPIN_TIMEOUT);
                         __syncwarp(0xffffu);
-                        for (int r = 1; r < ep.world; ++r) s += __ldcv(ep.part0 + size_t(r) * ep.part_stride + yi);
+                        for (int rk = 1; rk < ep.world; ++rk) s += __ldcv(ep.part0 + size_t(rk) * ep.part_stride + yi);
                         __syncwarp(0xffffu);
                         if (tid == 0) ep.cnt0[bu] = 0u;           // ready for the next launch
                     }
@@ -1039,6 +1034,11 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         }
     } else if (warp == kLHWarp) {
         // ------------------------------------------------ h warp
+        // per unit: h = silu(gate) * up * w_slot (kernels.metal:61-63) of its
+        // 16 rows, then the unit's digit record for the down MMAs: E = the
+        // exponent of max|h|, X = round(h 2^(20-E)) = p0 + 2^8 p1 + 2^16 p2
+        // (signed bytes) at 0 / 16 / 32, and at 48 the fp32 pair (2^(E-20)
+        // (/7.5 for SMOE-Q4), sum X 2^(E-20))
         if (!mbar_wait_b(routed, 0, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
         int a0, a1;
         a_range(a0, a1);
@@ -1047,8 +1047,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         for (int a = a0; a < a1; ++a, ++hu) {
             if (hu == g.tilesU) { hu = 0; ++hli; }
             const int n = a - a0, b = n & 1;
-            const uint32_t li = uint32_t(hli), u = uint32_t(hu);
-            const uint32_t slot = slot_at(li);
+            const uint32_t slot = slot_at(uint32_t(hli));
             if (!mbar_wait_b(redF + b, (n >> 1) & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
             const float* rb = red + b * kLCons * 32;
             float v = 0.f;                                        // lane = (matrix, row)
@@ -1057,36 +1056,38 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
             __syncwarp();
             if (lane == 0) mbar_arrive(redE + b);
             const float up = __shfl_down_sync(0xffffffffu, v, 16);
-            if (lane < 16)                                        // kernels.metal:61-63
-                reinterpret_cast<float*>(A.hbuf + (size_t(li) * g.tilesU + u) * kHRec)[lane] =
-                    v * (1.0f / (1.0f + expf(-v))) * up * s_w[slot];
+            const float hv = lane < 16 ? v * (1.0f / (1.0f + expf(-v))) * up * s_w[slot] : 0.f;
+            float m = fabsf(hv);
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            const int E = max(int((__float_as_uint(m) >> 23) & 0xff) - 127, -100);
+            const float f = pow2i(20 - E);
+            const int X = __float2int_rn(hv * f);
+            int sx = X;
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) sx += __shfl_xor_sync(0xffffffffu, sx, o);
+            if (n >= 2 && !mbar_wait_b(hE + b, ((n >> 1) - 1) & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+            uint8_t* rec = hrec + b * kHRec;
+            if (lane < 16) {
+                const int d0 = ((X + 128) & 255) - 128, rr = (X - d0) >> 8;
+                const int d1 = ((rr + 128) & 255) - 128, d2 = (rr - d1) >> 8;
+                rec[lane] = uint8_t(d0);
+                rec[16 + lane] = uint8_t(d1);
+                rec[32 + lane] = uint8_t(d2);
+            }
+            if (lane == 0) {
+                const float xs = pow2i(E - 20);
+                *reinterpret_cast<float2*>(rec + 48) =
+                    make_float2(FMT == kFmtAffine ? xs : xs * (1.0f / 7.5f), float(sx) * xs);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(hF + b);
         }
-        // phase A of this CTA is done: publish for phase B of all CTAs (the
-        // warp barrier orders every lane's record stores before lane 0's
-        // gpu-scope release)
-        __syncwarp();
-        if (lane == 0) red_rel_gpu(&A.st->arrive, 1u);
         ltrace(A.trace, 8, lane == 0);
     }
 
     // the next kernel in the stream may start its launch now
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    // ------------------------------------------------- last CTA: reset state
-    __syncthreads();
-    if (tid == 0) {
-        uint32_t old;
-        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(&A.st->done) : "memory");
-        last_cta = (old == uint32_t(ncta) - 1) ? 1u : 0u;
-        if (last_cta) {
-            A.st->arrive = 0;
-            A.st->done = 0;
-            A.st->rdone = 0;
-            A.st->seq = seq;
-            if (epm) A.st->epoch = epoch;
-        }
-        // (no fence: the next launch reads these only after this grid has
-        // completed - stream order or griddepcontrol.wait)
-    }
     ltrace(A.trace, 9);
 }
 

@@ -66,7 +66,7 @@ struct SmoeCudaCtx {
     int num_sms = 0;
     int gemv_res[2] = {0, 0};        // resident CTAs per SM of k_gemv_set<1>, <2>
     smoe::LayerState* lstate = nullptr;   // layer kernel's grid counters (zero between launches)
-    uint8_t* hbuf = nullptr;              // layer kernel's h, fp32 [kLMaxTok*kLMaxK][max_d_ff/16][16]
+    unsigned long long* lpart = nullptr;  // layer kernel's tagged partial rows [num_sms][kLMaxTok][kLMaxD] (zero: no tag)
     uint64_t wait_ns = 0;                 // limit of every device-side wait of the layer kernel
     unsigned long long* trace = nullptr;   // phase timestamps of the layer kernel (profiling aid)
     // expert-grouped batch path: per-expert slot lists, operand tables, per-slot outputs
@@ -291,6 +291,7 @@ namespace {
 int launch_layer(SmoeCudaCtx* c, const LayerCall& q) {
     const int fmt = int(q.L->fmt & ~uint32_t(SMOE_LAYOUT_TILED));
     if (q.batch > (uint32_t)smoe::kLMaxTok || q.k > (uint32_t)smoe::kLMaxK || q.L->d_ff > c->cfg.max_d_ff ||
+        c->num_sms > 32 * smoe::kLRedMax ||
         (q.rw && (q.n_experts > 128u || q.L->d_model % 8)))
         return SMOE_ERR_UNSUPPORTED;
     if (!aligned16(q.x) || (q.y && !aligned16(q.y))) {            // whole-vector loads
@@ -327,7 +328,7 @@ int launch_layer(SmoeCudaCtx* c, const LayerCall& q) {
     A.rw = q.rw;
     A.norm = q.norm;
     A.logits = c->lpair;
-    A.hbuf = c->hbuf;
+    A.part = c->lpart;
     A.st = c->lstate;
     A.err = c->err;
     A.wait_ns = c->wait_ns;
@@ -342,12 +343,15 @@ int launch_layer(SmoeCudaCtx* c, const LayerCall& q) {
     }
     const size_t smem = (size_t)A.g.total;
     const int gw = (int(A.g.tg.Gc) + smoe::kLCons - 1) / smoe::kLCons;   // 1 or 2 (Gc <= 32)
+    const int dbi = A.g.d <= 1024 ? 0 : A.g.d <= 2048 ? 1 : 2;           // 64-row blocks per warp: 1, 2, 4
     using smoe::k_moe_layer;
     using smoe::kFmtAffine;
     using smoe::kFmtSmoe;
-    static void* const kerns[2][2] = {{(void*)k_moe_layer<kFmtSmoe, 1>, (void*)k_moe_layer<kFmtSmoe, 2>},
-                                      {(void*)k_moe_layer<kFmtAffine, 1>, (void*)k_moe_layer<kFmtAffine, 2>}};
-    void* kern = kerns[fmt == SMOE_FMT_AFFINE_Q4 ? 1 : 0][gw - 1];
+#define SMOE_LAYER_K(F, G) {(void*)k_moe_layer<F, G, 1>, (void*)k_moe_layer<F, G, 2>, (void*)k_moe_layer<F, G, 4>}
+    static void* const kerns[2][2][3] = {{SMOE_LAYER_K(kFmtSmoe, 1), SMOE_LAYER_K(kFmtSmoe, 2)},
+                                         {SMOE_LAYER_K(kFmtAffine, 1), SMOE_LAYER_K(kFmtAffine, 2)}};
+#undef SMOE_LAYER_K
+    void* kern = kerns[fmt == SMOE_FMT_AFFINE_Q4 ? 1 : 0][gw - 1][dbi];
     int rc = prep_kernel(c, kern, smem);
     if (rc) return rc;
     cudaLaunchConfig_t lc{};
@@ -454,7 +458,7 @@ SmoeCudaCtx* smoe_cuda_init_ex(const SmoeCudaInitArgs* args) {
     if ((e = cudaMalloc(&c->ticket, size_t(a.max_batch) * 4)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->err, 4)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->lstate, sizeof(smoe::LayerState))) != cudaSuccess) return fail(e);
-    if ((e = cudaMalloc(&c->hbuf, size_t(smoe::kLMaxTok) * smoe::kLMaxK * (a.max_d_ff / 16) * smoe::kHRec)) != cudaSuccess) return fail(e);
+    if ((e = cudaMalloc(&c->lpart, size_t(c->num_sms) * smoe::kLMaxTok * smoe::kLMaxD * 8)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->g_list, size_t(a.max_experts) * slots * 4)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->g_count, size_t(a.max_experts + 1) * 4)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->g_xtab, size_t(a.max_batch) * a.max_d_model * 4)) != cudaSuccess) return fail(e);
@@ -464,6 +468,7 @@ SmoeCudaCtx* smoe_cuda_init_ex(const SmoeCudaInitArgs* args) {
     if ((e = cudaMalloc(&c->g_ys, slots * a.max_d_model * 4)) != cudaSuccess) return fail(e);
     cudaMemsetAsync(c->lstate, 0, sizeof(smoe::LayerState), c->stream);
     cudaMemsetAsync(c->lpair, 0, size_t(smoe::kLMaxTok) * 128 * 8, c->stream);
+    cudaMemsetAsync(c->lpart, 0, size_t(c->num_sms) * smoe::kLMaxTok * smoe::kLMaxD * 8, c->stream);
     c->gemv_cap = a.max_vocab > a.max_d_model ? a.max_vocab : a.max_d_model;
     if ((e = cudaMalloc(&c->gemv_out, c->gemv_cap * 4)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->gemv_in, size_t(a.max_d_model) * 4)) != cudaSuccess) return fail(e);
@@ -491,7 +496,7 @@ void smoe_cuda_destroy(SmoeCudaCtx* c) {
     if (c->ep_win) cudaFree(c->ep_win);
     for (auto& ev : c->events)
         if (ev) cudaEventDestroy(ev);
-    void* bufs[] = {c->g_list, c->g_count, c->g_xtab, c->g_xgs, c->g_htab, c->g_hgs, c->g_ys, c->lstate, c->lpair, c->hbuf, c->hidden, c->slot_out, c->in_stage, c->batch_out, c->logits, c->ids,
+    void* bufs[] = {c->g_list, c->g_count, c->g_xtab, c->g_xgs, c->g_htab, c->g_hgs, c->g_ys, c->lstate, c->lpair, c->lpart, c->hidden, c->slot_out, c->in_stage, c->batch_out, c->logits, c->ids,
                     c->wts, c->ticket, c->err, c->gemv_out, c->gemv_in};
     for (void* b : bufs)
         if (b) cudaFree(b);
@@ -1181,7 +1186,7 @@ int smoe_cuda_prepack_layer(SmoeCudaCtx* c, const SmoeMoeLayer* src, void* dst, 
     p.dst_stride = dst_stride;
     p.fmt = (int)src->fmt;
     if (!p.tg.init((int)src->fmt, src->d_model, src->d_ff)) { set_err("shape has no tiled layout %s%ld", "", 0); return SMOE_ERR_ARG; }
-    dim3 grid(src->d_ff / 16 + src->d_model / 16, src->n_experts);
+    dim3 grid(2 * (src->d_ff / 16) + src->d_ff / 64, src->n_experts);
     smoe::k_prepack<<<grid, 256, 0, c->stream>>>(p);
     CK(cudaGetLastError());
     c->dispatches += 1;

@@ -7,12 +7,13 @@
 // 5.5 TB/s over 148 SMs). The tiled layout makes each piece of work of the
 // layer kernel (moe_layer.cuh) one contiguous block of a few tens of KB:
 //
-//   expert = [A unit 0 .. d_ff/16-1][B tile 0 .. d_model/16-1]
+//   expert = [A unit 0 .. d_ff/16-1][D unit 0 .. d_ff/16-1][S group 0 .. d_ff/64-1]
 //   A unit u (hidden rows 16u..16u+15 of gate and up) = nchunk chunks,
 //     chunk c (64-groups c*Gc .. c*Gc+Gc-1 of the input dimension) =
 //       [gate frag][up frag][gate sb][up sb]
-//   B tile o (output rows 16o..16o+15 of down, all d_ff columns) =
-//       [codes: d_ff/64 groups x 512 B, the frag order below][sb: d_ff/64 groups x 16 rows]
+//   D unit u (columns 16u..16u+15 of down - the ones hidden unit u feeds -
+//     all d_model rows) = d_model/64 blocks of 512 B, the frag order below
+//   S group j (down's scales of d_ff group j, all d_model rows, row order)
 //
 // nchunk = ceil(G / 32) (G = d_model/64 groups), Gc = G / nchunk: chunks of
 // at most 32 groups (36 KB) so that a few of them fit in shared memory.
@@ -28,13 +29,13 @@
 // sb: per-group scales transposed to [group][16 rows]; AFFINE-Q4 packs
 //   (scale, bias) into one 32-bit word (scale in the low half), SMOE-Q4 holds
 //   the 16-bit scale alone.
-// B codes: per 64-group 512 B in the A-fragment order of the integer MMA
-//   m16n8k16 (u8), one MMA per 16-column unit u of the group: lane L = 4g + c
-//   holds 16 B = words {row g, units 0-1}, {row g+8, units 0-1}, {row g,
-//   units 2-3}, {row g+8, units 2-3}; byte b of a word holds the code of
-//   column 16u + 4c + b of the even unit in its low nibble and of the odd unit
-//   in its high nibble, so one mask per register gives q (even unit) or 16q
-//   (odd unit).
+// D block b (rows 64b..64b+63 of down, the unit's 16 columns): four row
+//   tiles of 16 rows in the A-fragment order of the integer MMA m16n8k16
+//   (u8), two tiles per byte: lane L = 4g + c holds 16 B = words {tiles 0-1,
+//   row g}, {tiles 0-1, row g+8}, {tiles 2-3, row g}, {tiles 2-3, row g+8}
+//   (row r of tile q = row 64b + 16q + r); byte j of a word holds column
+//   16u + 4c + j of the even tile in its low nibble and of the odd tile in
+//   its high nibble.
 // Byte count equals the vault layout's.
 #pragma once
 #include "smoe_common.cuh"
@@ -46,7 +47,7 @@ struct TiledGeom {
     uint32_t nchunk, Gc;            // chunks per A unit, groups per chunk
     uint32_t fragC, sbC, chunk;     // one gate/up frag of a chunk, one sb block, whole chunk
     uint32_t aunit;                 // A unit bytes (nchunk chunks)
-    uint32_t bcodes, btile;         // B tile codes, whole B tile
+    uint32_t dunit, sgrp;           // one D unit, one S group
     uint64_t expert;
     __host__ __device__ bool init(int fmt, uint32_t d_, uint32_t dff_) {
         d = d_; dff = dff_; G = d / 64; Gd = dff / 64;
@@ -56,13 +57,16 @@ struct TiledGeom {
         fragC = Gc * 512; sbC = 16 * Gc * e;
         chunk = 2 * fragC + 2 * sbC;
         aunit = nchunk * chunk;
-        bcodes = (dff / 16) * 128;
-        btile = bcodes + Gd * 16 * e;
-        expert = uint64_t(dff / 16) * aunit + uint64_t(d / 16) * btile;
+        dunit = d * 8;
+        sgrp = d * e;
+        expert = uint64_t(dff / 16) * (aunit + dunit) + uint64_t(Gd) * sgrp;
         return d % 64 == 0 && dff % 64 == 0 && d > 0 && dff > 0 && G % nchunk == 0;
     }
     __host__ __device__ uint64_t chunk_off(uint32_t u, uint32_t c) const { return uint64_t(u) * aunit + uint64_t(c) * chunk; }
-    __host__ __device__ uint64_t btile_off(uint32_t o) const { return uint64_t(dff / 16) * aunit + uint64_t(o) * btile; }
+    __host__ __device__ uint64_t dunit_off(uint32_t u) const { return uint64_t(dff / 16) * aunit + uint64_t(u) * dunit; }
+    __host__ __device__ uint64_t sgrp_off(uint32_t j) const {
+        return uint64_t(dff / 16) * (aunit + dunit) + uint64_t(j) * sgrp;
+    }
 };
 
 struct PrepackArgs {
@@ -79,7 +83,7 @@ SMOE_DEVINL uint32_t nib_at(const uint8_t* rowp, uint32_t col) {
     return (rowp[col >> 1] >> ((col & 1) * 4)) & 0xfu;
 }
 
-// grid (d_ff/16 + d_model/16, n_experts), 256 threads
+// grid (2 * d_ff/16 + d_ff/64, n_experts), 256 threads
 __global__ void k_prepack(PrepackArgs a) {
     const TiledGeom& t = a.tg;
     const uint32_t e = blockIdx.y, blk = blockIdx.x;
@@ -115,31 +119,30 @@ __global__ void k_prepack(PrepackArgs a) {
                 }
             }
         }
-    } else {
-        const uint32_t o = blk - t.dff / 16;                // B tile: output rows 16o..16o+15
-        uint8_t* p = dexp + t.btile_off(o);
-        uint4* codes = reinterpret_cast<uint4*>(p);
+    } else if (blk < 2 * (t.dff / 16)) {
+        const uint32_t u = blk - t.dff / 16;                // D unit: down columns 16u..16u+15
+        uint4* codes = reinterpret_cast<uint4*>(dexp + t.dunit_off(u));
         const uint8_t* dn = NIB(2);
-        for (uint32_t i = threadIdx.x; i < t.Gd * 32; i += blockDim.x) {
-            const uint32_t gi = i >> 5, L = i & 31, g = L >> 2, c = L & 3;
+        for (uint32_t i = threadIdx.x; i < (t.d / 64) * 32; i += blockDim.x) {
+            const uint32_t b = i >> 5, L = i & 31, g = L >> 2, c = L & 3;
             uint32_t w[4];
-            for (int q = 0; q < 4; ++q) {                         // (row g / g+8) x (units 0-1 / 2-3)
-                const uint8_t* row = dn + size_t(o * 16 + g + 8 * (q & 1)) * (t.dff / 2);
-                const uint32_t u0 = 2 * (q >> 1);
+            for (int q = 0; q < 4; ++q) {                   // (tiles 0-1 / 2-3) x (row g / g+8)
+                const uint32_t tp = q >> 1, r = g + 8 * (q & 1);
+                const uint8_t* lo = dn + size_t(64 * b + 16 * (2 * tp) + r) * (t.dff / 2);
+                const uint8_t* hi = dn + size_t(64 * b + 16 * (2 * tp + 1) + r) * (t.dff / 2);
                 uint32_t v = 0;
-                for (uint32_t b = 0; b < 4; ++b) {
-                    const uint32_t col = gi * 64 + 4 * c + b;
-                    v |= (nib_at(row, col + 16 * u0) | (nib_at(row, col + 16 * (u0 + 1)) << 4)) << (8 * b);
+                for (uint32_t j = 0; j < 4; ++j) {
+                    const uint32_t col = 16 * u + 4 * c + j;
+                    v |= (nib_at(lo, col) | (nib_at(hi, col) << 4)) << (8 * j);
                 }
                 w[q] = v;
             }
             codes[i] = make_uint4(w[0], w[1], w[2], w[3]);
         }
-        uint8_t* sb = p + t.bcodes;
-        for (uint32_t i = threadIdx.x; i < t.Gd * 16; i += blockDim.x) {
-            const uint32_t grp = i >> 4, r = i & 15;
-            put_sb(sb, i, 2, size_t(o * 16 + r) * t.Gd + grp);
-        }
+    } else {
+        const uint32_t j = blk - 2 * (t.dff / 16);          // S group j: down's scales, row order
+        uint8_t* sb = dexp + t.sgrp_off(j);
+        for (uint32_t r = threadIdx.x; r < t.d; r += blockDim.x) put_sb(sb, r, 2, size_t(r) * t.Gd + j);
     }
 }
 

@@ -39,7 +39,7 @@ names = {0: 'start', 1: 'router rows done', 2: 'routed (prod/h)', 3: 'x table bu
          5: 'phase A consumers done', 6: 'grid wait passed', 7: 'phase B done', 8: 'h warp arrived', 9: 'end',
          10: 'griddep wait returned', 11: 'producer starts', 12: 'producer issued all', 13: 'first B wave in smem',
          14: 'last A chunk in smem', 15: 'first B unit reduced', 16: 'h records loaded',
-         17: 'producer starts B issue', 18: 'routing: row count seen', 19: 'routing: logits read', 20: 'routing: top-k done', 21: 'B items done (w0)', **{25 + i: f'A chunk {i} in smem' for i in range(3)}, 28: 'prod: ids loaded', 29: 'prod: routing state built', 30: 'cons: xtab starts', 31: 'after first syncthreads'}
+         17: 'last D: h ready', 18: 'routing: row count seen / last D: data', 19: 'routing: logits read / last D: done', 20: 'routing: top-k done / A done, last D starts', 21: 'B items done (w0)', **{25 + i: f'A chunk {i} in smem' for i in range(3)}, 28: 'prod: ids loaded', 29: 'prod: routing state built', 30: 'cons: xtab starts', 31: 'after first syncthreads'}
 modes = sys.argv[2].split(',') if len(sys.argv) > 2 else ['given', 'routing']
 for mode in modes:
     def call(l):
