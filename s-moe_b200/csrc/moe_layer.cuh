@@ -571,7 +571,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
             const uint32_t nA = nslots * uint32_t(g.tilesU);
             const int a0 = int(divu(uint32_t(cta) * nA, uint32_t(ncta), A.mg_grid));
             const int a1 = int(divu(uint32_t(cta + 1) * nA, uint32_t(ncta), A.mg_grid));
-            const int n = min(NA, (a1 - a0) * int(tg.nchunk));
+            const int n = min(NA, min(a1 - a0, 2) * int(tg.nchunk));   // units 0 and 1 come first
             int li = int(divu(uint32_t(a0), uint32_t(g.tilesU), g.mg_tilesU)), u = a0 - li * g.tilesU, c = 0;
             for (int i = 0; i < n; ++i) {
                 mbar_arrive_expect_tx(fullA + i, tg.chunk);
@@ -587,31 +587,41 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         __syncwarp();
     };
     // producer lane: issue every copy of the CTA, gate/up chunks first
-    // Order per unit: its gate/up chunks, its down scales when the unit starts
-    // a new (slot, scale group), its down unit. One issue site per ring, no
-    // integer division in the loop (each costs ~100 cycles on this lane's
+    // Order: the gate/up chunks of units 0 and 1, then per unit n the down
+    // scales of n (when n starts a new (slot, scale group)) and its down
+    // columns, each after the gate/up chunks of unit n + 1 - the order in
+    // which the consumers use them (gate/up of n + 1, then down of n), so
+    // every copy lands in the order it is needed. One issue site per ring,
+    // no integer division in the loop (each costs ~100 cycles on this lane's
     // critical path): every index advances by counters.
     auto produce = [&]() {
         int a0, a1;
         a_range(a0, a1);
-        int li = int(divu(uint32_t(a0), uint32_t(g.tilesU), g.mg_tilesU)), u = a0 - li * g.tilesU;
+        const int nun = a1 - a0;
+        int ali = int(divu(uint32_t(a0), uint32_t(g.tilesU), g.mg_tilesU)), au = a0 - ali * g.tilesU;
+        int dli = ali, du = au;
         int iA = 0, stA = 0, rA = 0, stD = 0, rD = 0, stS = 0, rS = 0, sg_li = -1, sg_j = -1;
         ltrace(A.trace, 11, true);
 #pragma unroll 1
-        for (int a = a0; a < a1; ++a) {
-            const uint8_t* ex = expert_of(slot_at(uint32_t(li)));
+        for (int s = -1; s < nun; ++s) {
+            if (s + 1 < nun) {                          // gate/up chunks of unit s + 1
+                const uint8_t* ex = expert_of(slot_at(uint32_t(ali)));
 #pragma unroll 1
-            for (int c = 0; c < int(tg.nchunk); ++c, ++iA) {
-                if (iA >= preA) {                       // (the head start issued the first preA)
-                    if (rA > 0 && !mbar_wait_b(emptyA + stA, (rA - 1) & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
-                    mbar_arrive_expect_tx(fullA + stA, tg.chunk);
-                    bulk_g2s(ringA + size_t(stA) * g.stageA(), ex + tg.chunk_off(u, c), tg.chunk, fullA + stA);
+                for (int c = 0; c < int(tg.nchunk); ++c, ++iA) {
+                    if (iA >= preA) {                   // (the head start issued the first preA)
+                        if (rA > 0 && !mbar_wait_b(emptyA + stA, (rA - 1) & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+                        mbar_arrive_expect_tx(fullA + stA, tg.chunk);
+                        bulk_g2s(ringA + size_t(stA) * g.stageA(), ex + tg.chunk_off(au, c), tg.chunk, fullA + stA);
+                    }
+                    if (++stA == NA) { stA = 0; ++rA; }
                 }
-                if (++stA == NA) { stA = 0; ++rA; }
+                if (++au == g.tilesU) { au = 0; ++ali; }
             }
-            if (li != sg_li || (u >> 2) != sg_j) {
-                sg_li = li;
-                sg_j = u >> 2;
+            if (s < 0) continue;
+            const uint8_t* ex = expert_of(slot_at(uint32_t(dli)));   // down of unit s
+            if (dli != sg_li || (du >> 2) != sg_j) {
+                sg_li = dli;
+                sg_j = du >> 2;
                 if (rS > 0 && !mbar_wait_b(emptyS + stS, (rS - 1) & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
                 mbar_arrive_expect_tx(fullS + stS, tg.sgrp);
                 bulk_g2s(ringS + size_t(stS) * g.stageS(), ex + tg.sgrp_off(uint32_t(sg_j)), tg.sgrp, fullS + stS);
@@ -622,11 +632,11 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
                 if (rD > 0 && !mbar_wait_b(emptyD + stD, (rD - 1) & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
                 const uint32_t bytes = g.dpart_bytes(p);
                 mbar_arrive_expect_tx(fullD + stD, bytes);
-                bulk_g2s(ringD + size_t(stD) * g.stageD(), ex + tg.dunit_off(uint32_t(u)) + size_t(p) * g.stageD(), bytes,
+                bulk_g2s(ringD + size_t(stD) * g.stageD(), ex + tg.dunit_off(uint32_t(du)) + size_t(p) * g.stageD(), bytes,
                          fullD + stD);
                 if (++stD == g.ND) { stD = 0; ++rD; }
             }
-            if (++u == g.tilesU) { u = 0; ++li; }
+            if (++du == g.tilesU) { du = 0; ++dli; }
         }
         ltrace(A.trace, 12, true);
     };
