@@ -1,6 +1,11 @@
 """Build libsmoe_cuda.so (sm_100a) in-tree with nvcc.
 
-    python s-moe_b200/build.py
+    python s-moe_b200/build.py [--force] [--trace]
+
+--trace builds libsmoe_cuda_trace.so instead: the same library with the
+layer kernel's phase timestamps compiled in (smoe_cuda_debug_trace; read by
+trace_layer.py). The product library has none of that code - the kernel's
+instruction footprint is on its critical path.
 """
 from __future__ import annotations
 
@@ -11,6 +16,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 LIB = os.path.join(HERE, "libsmoe_cuda.so")
+LIB_TRACE = os.path.join(HERE, "libsmoe_cuda_trace.so")
 SOURCES = [os.path.join(HERE, "csrc", "smoe_cuda.cu"), os.path.join(HERE, "csrc", "smoe_noalloc.cu")]
 DEPS = SOURCES + [os.path.join(HERE, "csrc", f) for f in os.listdir(os.path.join(HERE, "csrc"))] + [
     os.path.join(ROOT, "include", "smoe_cuda.h")]
@@ -30,24 +36,25 @@ def nvcc() -> str:
     return "nvcc"
 
 
-def up_to_date() -> bool:
-    if not os.path.exists(LIB):
+def up_to_date(lib: str = LIB) -> bool:
+    if not os.path.exists(lib):
         return False
-    t = os.path.getmtime(LIB)
+    t = os.path.getmtime(lib)
     return all(os.path.getmtime(p) <= t for p in DEPS if os.path.exists(p))
 
 
-def build(force: bool = False, verbose: bool = False) -> str:
-    if not force and up_to_date():
-        return LIB
-    cmd = [nvcc(), *NVCC_FLAGS, *SOURCES, "-o", LIB]
+def build(force: bool = False, verbose: bool = False, trace: bool = False) -> str:
+    lib = LIB_TRACE if trace else LIB
+    if not force and up_to_date(lib):
+        return lib
+    cmd = [nvcc(), *NVCC_FLAGS, *(["-DSMOE_TRACE"] if trace else []), *SOURCES, "-o", lib]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if verbose or r.returncode != 0:
         sys.stderr.write(r.stdout + r.stderr)
     if r.returncode != 0:
-        raise RuntimeError("nvcc failed building libsmoe_cuda.so")
-    return LIB
+        raise RuntimeError("nvcc failed building " + os.path.basename(lib))
+    return lib
 
 
 if __name__ == "__main__":
-    print(build(force="--force" in sys.argv, verbose=True))
+    print(build(force="--force" in sys.argv, verbose=True, trace="--trace" in sys.argv))

@@ -82,7 +82,7 @@ constexpr int kLMaxND = 3;                    // down-unit ring stages (at most)
 constexpr int kLMaxNS = 2;                    // down-scale ring stages (at most)
 constexpr int kHRec = 64;                     // one unit's h digit record (shared memory)
 constexpr int kEpMaxWorld = 8;
-constexpr int kLRedMax = 8;                   // phase R: partial rows per thread (grid <= 256)
+constexpr int kLRedMax = 5;                   // phase R: partial rows per lane (grid <= 160)
 
 struct LayerState {          // device scratch, zero at context creation; the counters zero after every launch
     uint32_t rdone;                 // router logit rows stored (a hint: the logits carry their own tag)
@@ -197,11 +197,17 @@ struct LayerArgs {
     LayerEp ep;
 };
 
+// Phase timestamps, in the trace build only (SMOE_TRACE): the code of the
+// marks alone adds about 1 us to the kernel (instruction fetch).
 SMOE_DEVINL void ltrace(unsigned long long* tr, int i, bool who = threadIdx.x == 0) {
+#ifdef SMOE_TRACE
     if (tr && who && i < 32) {
         tr[blockIdx.x * 32 + i] = gtimer();
         tr[(gridDim.x + blockIdx.x) * 32 + i] = clock64();          // same mark in SM cycles
     }
+#else
+    (void)tr; (void)i; (void)who;
+#endif
 }
 
 SMOE_DEVINL uint32_t ld_acq_sys(const uint32_t* p) {
@@ -249,6 +255,29 @@ SMOE_DEVINL uint64_t ld_relaxed_gpu_u64(const unsigned long long* p) {
     uint64_t v;
     asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
+}
+
+// Expert parallel, phase R: one row block across the ranks, by threads
+// 0-15 (row 16o + tid, its sum s on this rank). Ranks > 0 store their rows
+// into rank 0's window and count the block once; rank 0 waits for the count
+// and adds the ranks' rows in rank order. Returns whether this thread
+// writes y. Out of line: the single-GPU kernel never runs it.
+static __device__ __noinline__ bool ep_combine16(int rank, int world, float* part0, uint32_t part_stride,
+                                                 uint32_t* cnt0, float& s, size_t yi, int bu, int tid,
+                                                 uint32_t* err, const WaitBudget wb) {
+    if (rank > 0) {
+        __stcg(part0 + size_t(rank) * part_stride + yi, s);
+        __threadfence_system();
+        __syncwarp(0xffffu);
+        if (tid == 0) atomicAdd_system(cnt0 + bu, 1u);
+        return false;
+    }
+    if (tid == 0 && !spin_geq<true>(cnt0 + bu, uint32_t(world - 1), wb)) raise_err(err, SMOE_DEVERR_SPIN_TIMEOUT);
+    __syncwarp(0xffffu);
+    for (int rk = 1; rk < world; ++rk) s += __ldcv(part0 + size_t(rk) * part_stride + yi);
+    __syncwarp(0xffffu);
+    if (tid == 0) cnt0[bu] = 0u;                          // ready for the next launch
+    return true;
 }
 
 // Bounded wait (one warp) for a token's E <= 128 tagged logits of this
@@ -331,7 +360,7 @@ SMOE_DEVINL void build_xtab(const void* xsrc, int x_dtype, int ntok, int K, uint
     const int G = K / 64;
     for (int i = ctid; i < G * 64; i += kLCThreads) xtab[i] = make_uint4(0u, 0u, 0u, 0u);
     const int warp = ctid >> 5, lane = ctid & 31;
-    constexpr int U = 2;
+    constexpr int U = 1;
     float v[U][2];
     // first round of loads before the barrier that orders the zeroing
     auto load = [&](int p0) {
@@ -443,6 +472,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
     // advances them)
     const uint32_t epoch = epm ? ld_relaxed_gpu_u32(&A.st->epoch) + 1u : 0u;
     const uint32_t seq = ld_relaxed_gpu_u32(&A.st->seq) + 1u;     // this launch's tag (never 0 in use)
+    ltrace(A.trace, 21);
     // x: the caller's, or on ranks > 0 rank 0's published copy (peer memory)
     const void* xsrc = A.x;
     if (epm) {
@@ -493,7 +523,9 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         *s_nloc = 0;
         for (int t = 0; t <= kLMaxTok; ++t) s_tok[t] = 0;
     }
+    ltrace(A.trace, 22);
     if (tid < 64) fence_mbar_init();
+    ltrace(A.trace, 23);
     __syncthreads();              // (ranks > 0: rank 0's x is published; rank 0 CTA 0: x0 is written)
     ltrace(A.trace, 31);
     if (epm && ep.rank == 0 && cta == 0 && tid == 0) {
@@ -760,7 +792,12 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         const int nblk = d >> 6;
         constexpr int DBP = DB == 4 ? 2 : DB;                      // blocks per warp per down part
         float dacc[DB][2][2];
-        int dli = ali, du = au, stD = 0, rD = 0, stS = 0, rS = 0, sg_li = -1, sg_j = -1, acc_t = -1;
+        int dli = ali, du = au, stD = 0, rD = 0, stS = 0, rS = 0, sg_li = -1, sg_j = -1;
+#pragma unroll
+        for (int i = 0; i < DB; ++i)
+#pragma unroll
+            for (int pq = 0; pq < 2; ++pq) dacc[i][pq][0] = dacc[i][pq][1] = 0.f;
+        auto tok_of = [&](int li) { return int(divu(slot_at(uint32_t(li)), uint32_t(k), g.mg_k)); };
         auto flush = [&](int t) {
             unsigned long long* pr = A.part + (size_t(cta) * kLMaxTok + t) * kLMaxD;
 #pragma unroll
@@ -780,17 +817,6 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
             }
         };
         auto down = [&](int n, bool last) {
-            const int t = int(divu(slot_at(uint32_t(dli)), uint32_t(k), g.mg_k));
-            if (t != acc_t) {
-                if (acc_t >= 0) flush(acc_t);
-                else {
-#pragma unroll
-                    for (int i = 0; i < DB; ++i)
-#pragma unroll
-                        for (int pq = 0; pq < 2; ++pq) dacc[i][pq][0] = dacc[i][pq][1] = 0.f;
-                }
-                acc_t = t;
-            }
             if (dli != sg_li || (du >> 2) != sg_j) {             // a new (slot, scale group)
                 if (sg_li >= 0) {
                     __syncwarp();
@@ -945,11 +971,14 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
                 }
             }
             if (a == a1) ltrace(A.trace, 20);
-            if (n > 0) down(n - 1, a == a1);
+            if (n > 0) {
+                const int t = tok_of(dli);
+                down(n - 1, a == a1);                              // (advances dli, du)
+                if (a == a1 || tok_of(dli) != t) flush(t);        // the token's last unit here
+            }
             if (a == a1) ltrace(A.trace, 19);
             if (n == 1) ltrace(A.trace, 13);
         }
-        if (acc_t >= 0) flush(acc_t);
         ltrace(A.trace, 5);
 
         ltrace(A.trace, 16);
@@ -1018,21 +1047,8 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
 #pragma unroll
                     for (int jj = 0; jj < 32; ++jj) s += red2[jj * 16 + tid];
                     const size_t yi = size_t(t) * d + o * 16 + tid;
-                    bool write = true;
-                    if (epm && ep.rank > 0) {
-                        __stcg(ep.part0 + size_t(ep.rank) * ep.part_stride + yi, s);
-                        __threadfence_system();
-                        __syncwarp(0xffffu);
-                        if (tid == 0) atomicAdd_system(ep.cnt0 + bu, 1u);
-                        write = false;
-                    } else if (epm) {
-                        if (tid == 0 && !spin_geq<true>(ep.cnt0 + bu, uint32_t(ep.world - 1), wb))
-                            raise_err(A.err, SMOE_DEVERR_SPIN_TIMEOUT);
-                        __syncwarp(0xffffu);
-                        for (int rk = 1; rk < ep.world; ++rk) s += __ldcv(ep.part0 + size_t(rk) * ep.part_stride + yi);
-                        __syncwarp(0xffffu);
-                        if (tid == 0) ep.cnt0[bu] = 0u;           // ready for the next launch
-                    }
+                    const bool write = !epm || ep_combine16(ep.rank, ep.world, ep.part0, ep.part_stride, ep.cnt0, s,
+                                                            yi, bu, tid, A.err, wb);
                     if (write) {
                         if (A.y_dtype == 0) static_cast<float*>(A.y)[yi] = s;
                         else static_cast<__nv_bfloat16*>(A.y)[yi] = __float2bfloat16_rn(s);

@@ -2,15 +2,20 @@
 
     python s-moe_b200/trace_layer.py [LAYERS] [given,routing]
 
-Loads LAYERS (default 8) resident config-1 layers, runs warm back-to-back
-launches and records, for one launch, per-CTA %globaltimer and SM-cycle marks
-of the kernel's phases (smoe_cuda_debug_trace, a profiling aid outside the
-public header); prints min / median / max over CTAs relative to the moment
-griddepcontrol.wait returned, and the eager time per launch.
+Runs on the trace build of the library (libsmoe_cuda_trace.so, built by
+`build.py --trace`; the marks cost about 1 us of the kernel's time, so the
+product library has none). Loads LAYERS (default 8) resident config-1
+layers, runs warm back-to-back launches and records, for one launch, per-CTA
+%globaltimer and SM-cycle marks of the kernel's phases
+(smoe_cuda_debug_trace, a profiling aid outside the public header); prints
+min / median / max over CTAs relative to the moment griddepcontrol.wait
+returned, and the eager time per launch (of the trace build).
 """
 import os, sys, ctypes as C
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path[:0] = [HERE, os.path.join(os.path.dirname(HERE), 'oracle')]
+import build as B
+os.environ['SMOE_CUDA_LIB'] = B.LIB_TRACE if os.path.exists(B.LIB_TRACE) else B.build(trace=True)
 import numpy as np, torch
 import smoe_cuda as S, oracle as O
 E, D, DFF, K = 128, 2048, 768, 8
@@ -39,7 +44,7 @@ names = {0: 'start', 1: 'router rows done', 2: 'routed (prod/h)', 3: 'x table bu
          5: 'phase A consumers done', 6: 'grid wait passed', 7: 'phase B done', 8: 'h warp arrived', 9: 'end',
          10: 'griddep wait returned', 11: 'producer starts', 12: 'producer issued all', 13: 'first B wave in smem',
          14: 'last A chunk in smem', 15: 'first B unit reduced', 16: 'h records loaded',
-         17: 'last D: h ready', 18: 'routing: row count seen / last D: data', 19: 'routing: logits read / last D: done', 20: 'routing: top-k done / A done, last D starts', 21: 'B items done (w0)', **{25 + i: f'A chunk {i} in smem' for i in range(3)}, 28: 'prod: ids loaded', 29: 'prod: routing state built', 30: 'cons: xtab starts', 31: 'after first syncthreads'}
+         17: 'last D: h ready', 18: 'routing: row count seen / last D: data', 19: 'routing: logits read / last D: done', 20: 'routing: top-k done / A done, last D starts', 21: 'setup: seq loaded', 22: 'setup: barriers init', 23: 'setup: fence', **{25 + i: f'A chunk {i} in smem' for i in range(3)}, 28: 'prod: ids loaded', 29: 'prod: routing state built', 30: 'cons: xtab starts', 31: 'after first syncthreads'}
 modes = sys.argv[2].split(',') if len(sys.argv) > 2 else ['given', 'routing']
 for mode in modes:
     def call(l):
