@@ -312,6 +312,7 @@ SMOE_DEVINL float router_row_part(const LayerArgs& A, const void* xsrc, uint32_t
     const int d = A.g.d;
     float acc = 0.f;
     const uint4* wp = reinterpret_cast<const uint4*>(A.rw + size_t(e) * d);
+    #pragma unroll 1
     for (int c = ctid; c < d / 8; c += kLCThreads) {
         const uint4 v = __ldg(wp + c);
         const uint32_t u[4] = {v.x, v.y, v.z, v.w};
@@ -358,6 +359,7 @@ template <int FMT>
 SMOE_DEVINL void build_xtab(const void* xsrc, int x_dtype, int ntok, int K, uint4* xtab, float2* xg, int ctid,
                             uint32_t mgG) {
     const int G = K / 64;
+    #pragma unroll 1
     for (int i = ctid; i < G * 64; i += kLCThreads) xtab[i] = make_uint4(0u, 0u, 0u, 0u);
     const int warp = ctid >> 5, lane = ctid & 31;
     constexpr int U = 1;
@@ -386,6 +388,7 @@ SMOE_DEVINL void build_xtab(const void* xsrc, int x_dtype, int ntok, int K, uint
     load(warp);
     cons_sync();
     uint8_t* tb = reinterpret_cast<uint8_t*>(xtab);
+    #pragma unroll 1
     for (int p0 = warp; p0 < ntok * G; p0 += U * kLCons) {
         if (p0 != warp) load(p0);
 #pragma unroll
@@ -478,6 +481,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
     if (epm) {
         const size_t xbytes = size_t(g.ntok) * d * (A.x_dtype == 0 ? 4 : 2);
         if (ep.rank == 0 && cta == 0) {
+            #pragma unroll 1
             for (size_t i = tid; i < xbytes / 16; i += blockDim.x)
                 reinterpret_cast<uint4*>(ep.x0)[i] = reinterpret_cast<const uint4*>(A.x)[i];
         } else if (ep.rank > 0) {
@@ -561,8 +565,10 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         if (!epm) {
             // single GPU: every slot is local unless its id is bad
             bool ok = true;
+            #pragma unroll 1
             for (uint32_t sl = lane; sl < nslots; sl += 32) ok = ok && s_ids[sl] < A.n_experts;
             if (__all_sync(0xffffffffu, ok)) {
+                #pragma unroll 1
                 for (uint32_t sl = lane; sl < nslots; sl += 32) s_loc[sl] = sl;
                 if (lane <= g.ntok) s_tok[lane] = uint32_t(lane * k);
                 if (lane == 0) *s_nloc = nslots;
@@ -571,6 +577,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
             }
         }
         uint32_t cnt = 0;
+        #pragma unroll 1
         for (uint32_t s0 = 0; s0 < nslots; s0 += 32) {
             const uint32_t sl = s0 + lane;
             bool loc = false;
@@ -598,6 +605,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
     auto head_start = [&]() {
         if (epm) return;
         bool ok = true;
+        #pragma unroll 1
         for (uint32_t sl = lane; sl < nslots; sl += 32) ok = ok && s_ids[sl] < A.n_experts;
         if (__all_sync(0xffffffffu, ok) && lane == 0) {
             const uint32_t nA = nslots * uint32_t(g.tilesU);
@@ -605,6 +613,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
             const int a1 = int(divu(uint32_t(cta + 1) * nA, uint32_t(ncta), A.mg_grid));
             const int n = min(NA, min(a1 - a0, 2) * int(tg.nchunk));   // units 0 and 1 come first
             int li = int(divu(uint32_t(a0), uint32_t(g.tilesU), g.mg_tilesU)), u = a0 - li * g.tilesU, c = 0;
+            #pragma unroll 1
             for (int i = 0; i < n; ++i) {
                 mbar_arrive_expect_tx(fullA + i, tg.chunk);
                 bulk_g2s(ringA + size_t(i) * g.stageA(), A.base + uint64_t(s_ids[li]) * A.stride + tg.chunk_off(u, c),
@@ -641,7 +650,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
 #pragma unroll 1
                 for (int c = 0; c < int(tg.nchunk); ++c, ++iA) {
                     if (iA >= preA) {                   // (the head start issued the first preA)
-                        if (rA > 0 && !mbar_wait_b(emptyA + stA, (rA - 1) & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+                        if (rA > 0) mbar_wait_e(emptyA + stA, (rA - 1) & 1, wb, A.err);
                         mbar_arrive_expect_tx(fullA + stA, tg.chunk);
                         bulk_g2s(ringA + size_t(stA) * g.stageA(), ex + tg.chunk_off(au, c), tg.chunk, fullA + stA);
                     }
@@ -654,14 +663,14 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
             if (dli != sg_li || (du >> 2) != sg_j) {
                 sg_li = dli;
                 sg_j = du >> 2;
-                if (rS > 0 && !mbar_wait_b(emptyS + stS, (rS - 1) & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+                if (rS > 0) mbar_wait_e(emptyS + stS, (rS - 1) & 1, wb, A.err);
                 mbar_arrive_expect_tx(fullS + stS, tg.sgrp);
                 bulk_g2s(ringS + size_t(stS) * g.stageS(), ex + tg.sgrp_off(uint32_t(sg_j)), tg.sgrp, fullS + stS);
                 if (++stS == NS) { stS = 0; ++rS; }
             }
 #pragma unroll 1
             for (int p = 0; p < g.dparts; ++p) {
-                if (rD > 0 && !mbar_wait_b(emptyD + stD, (rD - 1) & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+                if (rD > 0) mbar_wait_e(emptyD + stD, (rD - 1) & 1, wb, A.err);
                 const uint32_t bytes = g.dpart_bytes(p);
                 mbar_arrive_expect_tx(fullD + stD, bytes);
                 bulk_g2s(ringD + size_t(stD) * g.stageD(), ex + tg.dunit_off(uint32_t(du)) + size_t(p) * g.stageD(), bytes,
@@ -703,6 +712,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
             if (lane == 0 && !spin_geq<false>(&A.st->rdone, rows, wb)) raise_err(A.err, SMOE_DEVERR_SPIN_TIMEOUT);
             __syncwarp();
             ltrace(A.trace, 18, lane == 0);
+            #pragma unroll 1
             for (int t = 0; t < g.ntok; ++t) {
                 // (the host routes layers of more than 128 experts with k_router)
                 float p[4];
@@ -750,7 +760,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
     }
     if (warp == kLProdWarp) {       // one call site of the producer loop for both modes
         if (lane == 0) {
-            if (!mbar_wait_b(routed, 0, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+            mbar_wait_e(routed, 0, wb, A.err);
             produce();
             // This CTA is done with the launch state (its threads read seq and
             // epoch before the set-up barrier; its row-count wait has passed):
@@ -775,7 +785,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         build_xtab<FMT>(xsrc, A.x_dtype, g.ntok, d, xtab, xg, tid, g.mg_G);
         cons_sync();
         ltrace(A.trace, 3);
-        if (!mbar_wait_b(routed, 0, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+        mbar_wait_e(routed, 0, wb, A.err);
         int a0, a1;
         a_range(a0, a1);
         const int gr = lane >> 2, cq = lane & 3;
@@ -825,10 +835,10 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
                 }
                 sg_li = dli;
                 sg_j = du >> 2;
-                if (!mbar_wait_b(fullS + stS, rS & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+                mbar_wait_e(fullS + stS, rS & 1, wb, A.err);
             }
             const int hb = n & 1;
-            if (!mbar_wait_b(hF + hb, (n >> 1) & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+            mbar_wait_e(hF + hb, (n >> 1) & 1, wb, A.err);
             if (last) ltrace(A.trace, 17);
             const uint8_t* rec = hrec + hb * kHRec;
             // One MMA m16n8k32 covers two row tiles: k 0-15 = the even tile's
@@ -851,7 +861,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
                         if (lane == 0) mbar_arrive(emptyD + stD);
                         if (++stD == g.ND) { stD = 0; ++rD; }
                     }
-                    if (!mbar_wait_b(fullD + stD, rD & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+                    mbar_wait_e(fullD + stD, rD & 1, wb, A.err);
                     if (last && i == 0) ltrace(A.trace, 18);
                 }
                 const uint8_t* dp = ringD + size_t(stD) * g.stageD();
@@ -895,7 +905,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
                 #pragma unroll 1
                 for (int c = 0; c < int(tg.nchunk); ++c, ++iA) {
                     const int st = stA;
-                    if (!mbar_wait_b(fullA + st, rA & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+                    mbar_wait_e(fullA + st, rA & 1, wb, A.err);
                     if (++stA == NA) { stA = 0; ++rA; }
                     if (n == 0 && c == 0) ltrace(A.trace, 4);
                     if (iA < 3) ltrace(A.trace, 25 + iA);
@@ -953,8 +963,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
                     if (lane == 0) mbar_arrive(emptyA + st);          // chunk fully consumed
                 }
                 // the unit's warp partials -> buffer b (free once the h warp read use n-2)
-                if (n >= 2 && !mbar_wait_b(redE + b, ((n >> 1) - 1) & 1, wb))
-                    raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+                if (n >= 2) mbar_wait_e(redE + b, ((n >> 1) - 1) & 1, wb, A.err);
                 float* rb = red + (b * kLCons + warp) * 32;
                 if (cq == tok) {
                     rb[gr] = acc[0][0];
@@ -1065,7 +1074,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         // exponent of max|h|, X = round(h 2^(20-E)) = p0 + 2^8 p1 + 2^16 p2
         // (signed bytes) at 0 / 16 / 32, and at 48 the fp32 pair (2^(E-20)
         // (/7.5 for SMOE-Q4), sum X 2^(E-20))
-        if (!mbar_wait_b(routed, 0, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+        mbar_wait_e(routed, 0, wb, A.err);
         int a0, a1;
         a_range(a0, a1);
         int hli = int(divu(uint32_t(a0), uint32_t(g.tilesU), g.mg_tilesU)), hu = a0 - hli * g.tilesU;
@@ -1074,7 +1083,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
             if (hu == g.tilesU) { hu = 0; ++hli; }
             const int n = a - a0, b = n & 1;
             const uint32_t slot = slot_at(uint32_t(hli));
-            if (!mbar_wait_b(redF + b, (n >> 1) & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+            mbar_wait_e(redF + b, (n >> 1) & 1, wb, A.err);
             const float* rb = red + b * kLCons * 32;
             float v = 0.f;                                        // lane = (matrix, row)
 #pragma unroll
@@ -1092,7 +1101,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
             int sx = X;
 #pragma unroll
             for (int o = 8; o > 0; o >>= 1) sx += __shfl_xor_sync(0xffffffffu, sx, o);
-            if (n >= 2 && !mbar_wait_b(hE + b, ((n >> 1) - 1) & 1, wb)) raise_err(A.err, SMOE_DEVERR_MBAR_TIMEOUT);
+            if (n >= 2) mbar_wait_e(hE + b, ((n >> 1) - 1) & 1, wb, A.err);
             uint8_t* rec = hrec + b * kHRec;
             if (lane < 16) {
                 const int d0 = ((X + 128) & 255) - 128, rr = (X - d0) >> 8;

@@ -139,6 +139,7 @@ SMOE_DEVINL void warp_topk_regs(float (&p)[NV], int E, uint32_t k, int norm, uin
     for (int j = 0; j < NV; ++j) key[j] = lane + 32 * j < E ? __float_as_uint(p[j] * inv) + 1u : 0u;
     float wsel = 0.f;
     uint32_t idsel = 0;
+#pragma unroll 1
     for (uint32_t s = 0; s < k; ++s) {
         uint32_t lb = 0u;
         int lj = 0;
@@ -153,6 +154,7 @@ SMOE_DEVINL void warp_topk_regs(float (&p)[NV], int E, uint32_t k, int norm, uin
             if (win == uint32_t(lane + 32 * j)) key[j] = 0u;
     }
     float ws = 0.f;                                   // rank-order sum (decode.cpp:296-303)
+#pragma unroll 1
     for (uint32_t s = 0; s < k; ++s) ws += __shfl_sync(0xffffffffu, wsel, s);
     const float winv = (norm && ws > 0.f) ? 1.0f / ws : 1.0f;
     if (lane < (int)k) {

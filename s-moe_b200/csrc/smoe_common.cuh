@@ -166,6 +166,16 @@ struct WaitBudget {
 SMOE_DEVINL bool mbar_wait_b(uint64_t* bar, uint32_t parity, const WaitBudget& w) {
     return mbar_try_wait(bar, parity) || mbar_wait_until(bar, parity, w.deadline());
 }
+// The same, setting the device error word when the wait runs out; the slow
+// path is out of line, so a call site is a try_wait and a branch.
+static __device__ __noinline__ void mbar_wait_flag_slow(uint64_t* bar, uint32_t parity, uint64_t ns, uint64_t cap,
+                                                        uint32_t* err) {
+    const WaitBudget w{ns, cap};
+    if (!mbar_wait_until(bar, parity, w.deadline())) atomicCAS(err, 0u, SMOE_DEVERR_MBAR_TIMEOUT);
+}
+SMOE_DEVINL void mbar_wait_e(uint64_t* bar, uint32_t parity, const WaitBudget& w, uint32_t* err) {
+    if (!mbar_try_wait(bar, parity)) mbar_wait_flag_slow(bar, parity, w.ns, w.cap, err);
+}
 
 // 1-D bulk copy global -> shared, completion counted on `bar` (bytes).
 // dst, src 16-byte aligned; bytes a multiple of 16. No multicast.
