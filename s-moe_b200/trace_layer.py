@@ -1,6 +1,6 @@
 """Phase timeline of the MoE-layer kernel (k_moe_layer) on BASELINE config 1.
 
-    python s-moe_b200/trace_layer.py [LAYERS] [given,routing]
+    python s-moe_b200/trace_layer.py [LAYERS] [given,routing] [product]
 
 Runs on the trace build of the library (libsmoe_cuda_trace.so, built by
 `build.py --trace`; the marks cost about 1 us of the kernel's time, so the
@@ -9,13 +9,17 @@ layers, runs warm back-to-back launches and records, for one launch, per-CTA
 %globaltimer and SM-cycle marks of the kernel's phases
 (smoe_cuda_debug_trace, a profiling aid outside the public header); prints
 min / median / max over CTAs relative to the moment griddepcontrol.wait
-returned, and the eager time per launch (of the trace build).
+returned, and the eager time per launch (of the trace build). With
+`product` it runs the same launches on the product library and prints the
+time per launch only (the command the committed ncu captures profile).
 """
 import os, sys, ctypes as C
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path[:0] = [HERE, os.path.join(os.path.dirname(HERE), 'oracle')]
 import build as B
-os.environ['SMOE_CUDA_LIB'] = B.LIB_TRACE if os.path.exists(B.LIB_TRACE) else B.build(trace=True)
+PRODUCT = 'product' in sys.argv[3:]          # the product library: the same launches, no marks (for ncu)
+if not PRODUCT:
+    os.environ['SMOE_CUDA_LIB'] = B.LIB_TRACE if os.path.exists(B.LIB_TRACE) else B.build(trace=True)
 import numpy as np, torch
 import smoe_cuda as S, oracle as O
 E, D, DFF, K = 128, 2048, 768, 8
@@ -66,6 +70,7 @@ for mode in modes:
         e1.record(st)
         torch.cuda.synchronize()
     print(f'== {mode}: {e0.elapsed_time(e1) / 200 * 1e3:.2f} us per launch (eager)')
+    if PRODUCT: continue
     t = trace.cpu().numpy()[:148 * 32].reshape(148, 32).astype(np.int64)
     cy = trace.cpu().numpy()[148 * 32:148 * 64].reshape(148, 32).astype(np.int64)
     tw = t[:, 10][t[:, 10] > 0].min()
