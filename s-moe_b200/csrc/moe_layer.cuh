@@ -464,46 +464,9 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
     const int cta = blockIdx.x, ncta = gridDim.x;
 
     ltrace(A.trace, 0);
-    // inputs (x, routing) may come from the previous kernel in the stream
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    ltrace(A.trace, 10);
-    // every wait: A.wait_ns from its start, the whole kernel at most 8 x that
-    const WaitBudget wb{A.wait_ns, gtimer() + 8 * A.wait_ns};
-    const LayerEp& ep = A.ep;
-    const bool epm = ep.world > 1;
-    // (read before the set-up barrier: the last CTA past its producer loop
-    // advances them)
-    const uint32_t epoch = epm ? ld_relaxed_gpu_u32(&A.st->epoch) + 1u : 0u;
-    const uint32_t seq = ld_relaxed_gpu_u32(&A.st->seq) + 1u;     // this launch's tag (never 0 in use)
-    ltrace(A.trace, 21);
-    // x: the caller's, or on ranks > 0 rank 0's published copy (peer memory)
-    const void* xsrc = A.x;
-    if (epm) {
-        const size_t xbytes = size_t(g.ntok) * d * (A.x_dtype == 0 ? 4 : 2);
-        if (ep.rank == 0 && cta == 0) {
-            #pragma unroll 1
-            for (size_t i = tid; i < xbytes / 16; i += blockDim.x)
-                reinterpret_cast<uint4*>(ep.x0)[i] = reinterpret_cast<const uint4*>(A.x)[i];
-        } else if (ep.rank > 0) {
-            if (tid == 0 && !spin_geq<true>(ep.flag0, epoch, wb)) raise_err(A.err, SMOE_DEVERR_SPIN_TIMEOUT);
-            xsrc = ep.x0;
-        }
-    }
-    // routing given: the producer warp's loads of it are issued before the
-    // set-up barrier, so their latency overlaps it
-    uint32_t pre_id[2] = {0u, 0u};
-    float pre_w[2] = {0.f, 0.f};
-    if (!A.rw && warp == kLProdWarp) {
-#pragma unroll
-        for (int q = 0; q < 2; ++q) {
-            const uint32_t i = lane + 32u * q;
-            if (i < nslots) {
-                pre_id[q] = __ldcg(A.ids_in + i);
-                pre_w[q] = __ldcg(A.wts_in + i);
-            }
-        }
-    }
-    // barrier set-up, one barrier per thread of warp 0 and 1
+    // Set-up that reads nothing the previous kernel in the stream writes:
+    // with programmatic dependent launch it runs while that kernel drains.
+    // Barriers, one per thread of warps 0 and 1.
     if (tid < kLMaxNA) {
         mbar_init(fullA + tid, 1);
         mbar_init(emptyA + tid, kLCons);
@@ -525,13 +488,58 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         // empty routing until it is known (a wait that runs out then finds
         // nothing to do rather than stale shared memory)
         *s_nloc = 0;
+#pragma unroll 1
         for (int t = 0; t <= kLMaxTok; ++t) s_tok[t] = 0;
     }
-    ltrace(A.trace, 22);
     if (tid < 64) fence_mbar_init();
-    ltrace(A.trace, 23);
-    __syncthreads();              // (ranks > 0: rank 0's x is published; rank 0 CTA 0: x0 is written)
+    // the router row this CTA computes first, into L2
+    if (A.rw && uint32_t(cta) < A.n_experts * uint32_t(g.ntok) && tid < d / 64)
+        asm volatile("prefetch.global.L2 [%0];" :: "l"(A.rw + size_t(uint32_t(cta) % A.n_experts) * d + tid * 64));
+    __syncthreads();
     ltrace(A.trace, 31);
+    // the next kernel in the stream may start launching its CTAs as this
+    // one's exit (its griddepcontrol.wait still waits for all of this grid)
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // inputs (x, routing, the launch state) may come from the previous kernel
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    ltrace(A.trace, 10);
+    // every wait: A.wait_ns from its start, the whole kernel at most 8 x that
+    const WaitBudget wb{A.wait_ns, gtimer() + 8 * A.wait_ns};
+    const LayerEp& ep = A.ep;
+    const bool epm = ep.world > 1;
+    // (read before the barrier below, and so before this CTA's producer
+    // counts it done with the launch state: the last CTA to do so advances
+    // them)
+    const uint32_t epoch = epm ? ld_relaxed_gpu_u32(&A.st->epoch) + 1u : 0u;
+    const uint32_t seq = ld_relaxed_gpu_u32(&A.st->seq) + 1u;     // this launch's tag (never 0 in use)
+    ltrace(A.trace, 21);
+    // x: the caller's, or on ranks > 0 rank 0's published copy (peer memory)
+    const void* xsrc = A.x;
+    if (epm) {
+        const size_t xbytes = size_t(g.ntok) * d * (A.x_dtype == 0 ? 4 : 2);
+        if (ep.rank == 0 && cta == 0) {
+            #pragma unroll 1
+            for (size_t i = tid; i < xbytes / 16; i += blockDim.x)
+                reinterpret_cast<uint4*>(ep.x0)[i] = reinterpret_cast<const uint4*>(A.x)[i];
+        } else if (ep.rank > 0) {
+            if (tid == 0 && !spin_geq<true>(ep.flag0, epoch, wb)) raise_err(A.err, SMOE_DEVERR_SPIN_TIMEOUT);
+            xsrc = ep.x0;
+        }
+    }
+    __syncthreads();              // (ranks > 0: rank 0's x is published; rank 0 CTA 0: x0 is written)
+    // routing given: the producer warp's loads of it
+    uint32_t pre_id[2] = {0u, 0u};
+    float pre_w[2] = {0.f, 0.f};
+    if (!A.rw && warp == kLProdWarp) {
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            const uint32_t i = lane + 32u * q;
+            if (i < nslots) {
+                pre_id[q] = __ldcg(A.ids_in + i);
+                pre_w[q] = __ldcg(A.wts_in + i);
+            }
+        }
+    }
     if (epm && ep.rank == 0 && cta == 0 && tid == 0) {
         __threadfence_system();
         st_rel_sys(ep.flag0, epoch);
@@ -1121,8 +1129,6 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         ltrace(A.trace, 8, lane == 0);
     }
 
-    // the next kernel in the stream may start its launch now
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     ltrace(A.trace, 9);
 }
 
