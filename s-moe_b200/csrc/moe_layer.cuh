@@ -242,12 +242,6 @@ static __device__ __noinline__ bool spin_geq(const uint32_t* p, uint32_t target,
 
 SMOE_DEVINL void raise_err(uint32_t* err, uint32_t code) { atomicCAS(err, 0u, code); }
 
-SMOE_DEVINL uint32_t ld_relaxed_gpu_u32(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
 SMOE_DEVINL void st_relaxed_gpu_u64(unsigned long long* p, uint64_t v) {
     asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" :: "l"(p), "l"(v) : "memory");
 }
@@ -492,6 +486,7 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         for (int t = 0; t <= kLMaxTok; ++t) s_tok[t] = 0;
     }
     if (tid < 64) fence_mbar_init();
+    const uint64_t t_start = gtimer();      // (the first clock read is slow: taken while the previous kernel drains)
     // the router row this CTA computes first, into L2
     if (A.rw && uint32_t(cta) < A.n_experts * uint32_t(g.ntok) && tid < d / 64)
         asm volatile("prefetch.global.L2 [%0];" :: "l"(A.rw + size_t(uint32_t(cta) % A.n_experts) * d + tid * 64));
@@ -504,14 +499,14 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
     ltrace(A.trace, 10);
     // every wait: A.wait_ns from its start, the whole kernel at most 8 x that
-    const WaitBudget wb{A.wait_ns, gtimer() + 8 * A.wait_ns};
+    const WaitBudget wb{A.wait_ns, t_start + 8 * A.wait_ns};
     const LayerEp& ep = A.ep;
     const bool epm = ep.world > 1;
     // (read before the barrier below, and so before this CTA's producer
     // counts it done with the launch state: the last CTA to do so advances
     // them)
-    const uint32_t epoch = epm ? ld_relaxed_gpu_u32(&A.st->epoch) + 1u : 0u;
-    const uint32_t seq = ld_relaxed_gpu_u32(&A.st->seq) + 1u;     // this launch's tag (never 0 in use)
+    const uint32_t epoch = epm ? __ldcg(&A.st->epoch) + 1u : 0u;
+    const uint32_t seq = __ldcg(&A.st->seq) + 1u;                 // this launch's tag (never 0 in use)
     ltrace(A.trace, 21);
     // x: the caller's, or on ranks > 0 rank 0's published copy (peer memory)
     const void* xsrc = A.x;
