@@ -165,11 +165,11 @@ struct LayerGeom {
 struct LayerEp {
     int world, rank;
     uint32_t base, nlocal;     // global id of this rank's first expert, experts held
-    uint8_t* x0;               // rank 0's copy of x (peer memory on ranks > 0)
-    uint32_t* flag0;           // rank 0's x epoch
-    float* part0;              // [world][kLMaxTok * d] partial rows, in rank 0's window
-    uint32_t* cnt0;            // [kLMaxTok * d/16] partial row blocks arrived, in rank 0's window
-    uint32_t part_stride;      // floats per rank in part0
+    uint8_t* xw[kEpMaxWorld];  // rank 0: the x area of rank r's window (peer memory), r >= 1
+    uint32_t* flagw[kEpMaxWorld];  // rank 0: rank r's x epoch flag (peer memory), r >= 1
+    uint32_t* flag;            // ranks > 0: this rank's own x epoch flag (rank 0 advances it)
+    unsigned long long* part0; // [world][kLMaxTok * d] tagged rows (epoch << 32 | fp32), in rank 0's window
+    uint32_t part_stride;      // entries per rank in part0
 };
 
 struct LayerArgs {
@@ -252,26 +252,47 @@ SMOE_DEVINL uint64_t ld_relaxed_gpu_u64(const unsigned long long* p) {
 }
 
 // Expert parallel, phase R: one row block across the ranks, by threads
-// 0-15 (row 16o + tid, its sum s on this rank). Ranks > 0 store their rows
-// into rank 0's window and count the block once; rank 0 waits for the count
-// and adds the ranks' rows in rank order. Returns whether this thread
-// writes y. Out of line: the single-GPU kernel never runs it.
-static __device__ __noinline__ bool ep_combine16(int rank, int world, float* part0, uint32_t part_stride,
-                                                 uint32_t* cnt0, float& s, size_t yi, int bu, int tid,
-                                                 uint32_t* err, const WaitBudget wb) {
+// 0-15 (row yi, its sum s on this rank). Ranks > 0 store their row into rank
+// 0's window tagged with the epoch (one 64-bit peer store: no fence, no
+// counter); rank 0 polls its window until every rank's row carries this
+// epoch and adds them in rank order. Returns whether this thread writes y.
+// Out of line: the single-GPU kernel never runs it.
+static __device__ __noinline__ bool ep_combine16(int rank, int world, unsigned long long* part0, uint32_t part_stride,
+                                                 uint32_t epoch, float& s, size_t yi, uint32_t* err,
+                                                 const WaitBudget wb) {
     if (rank > 0) {
-        __stcg(part0 + size_t(rank) * part_stride + yi, s);
-        __threadfence_system();
-        __syncwarp(0xffffu);
-        if (tid == 0) atomicAdd_system(cnt0 + bu, 1u);
+        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" :: "l"(part0 + size_t(rank) * part_stride + yi),
+                     "l"((uint64_t(epoch) << 32) | __float_as_uint(s)) : "memory");
         return false;
     }
-    if (tid == 0 && !spin_geq<true>(cnt0 + bu, uint32_t(world - 1), wb)) raise_err(err, SMOE_DEVERR_SPIN_TIMEOUT);
-    __syncwarp(0xffffu);
-    for (int rk = 1; rk < world; ++rk) s += __ldcv(part0 + size_t(rk) * part_stride + yi);
-    __syncwarp(0xffffu);
-    if (tid == 0) cnt0[bu] = 0u;                          // ready for the next launch
+    const uint64_t deadline = wb.deadline();
+#pragma unroll 1
+    for (int rk = 1; rk < world; ++rk) {
+        uint64_t v;
+#pragma unroll 1
+        for (uint32_t it = 0;; ++it) {
+            asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(part0 + size_t(rk) * part_stride + yi)
+                         : "memory");
+            if (uint32_t(v >> 32) == epoch) break;
+            if ((it & 7) == 7 && gtimer() > deadline) {
+                raise_err(err, SMOE_DEVERR_SPIN_TIMEOUT);
+                v = 0;
+                break;
+            }
+            if (it >= 8) __nanosleep(64);
+        }
+        s += __uint_as_float(uint32_t(v));
+    }
     return true;
+}
+
+// Expert parallel: rank 0 pushes x into another rank's window (peer stores
+// by one warp).
+static __device__ __noinline__ void ep_push_x(uint8_t* xw, const void* x, uint32_t xbytes, int lane) {
+    const uint4* src = static_cast<const uint4*>(x);
+    uint4* dst = reinterpret_cast<uint4*>(xw);
+#pragma unroll 1
+    for (uint32_t i = lane; i < xbytes / 16; i += 32) dst[i] = src[i];
 }
 
 // Bounded wait (one warp) for a token's E <= 128 tagged logits of this
@@ -508,20 +529,26 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
     const uint32_t epoch = epm ? __ldcg(&A.st->epoch) + 1u : 0u;
     const uint32_t seq = __ldcg(&A.st->seq) + 1u;                 // this launch's tag (never 0 in use)
     ltrace(A.trace, 21);
-    // x: the caller's, or on ranks > 0 rank 0's published copy (peer memory)
+    // x: the caller's on rank 0; on ranks > 0 the copy rank 0 pushed into this
+    // rank's own window (A.x points there), once its flag shows this epoch
     const void* xsrc = A.x;
-    if (epm) {
-        const size_t xbytes = size_t(g.ntok) * d * (A.x_dtype == 0 ? 4 : 2);
-        if (ep.rank == 0 && cta == 0) {
-            #pragma unroll 1
-            for (size_t i = tid; i < xbytes / 16; i += blockDim.x)
-                reinterpret_cast<uint4*>(ep.x0)[i] = reinterpret_cast<const uint4*>(A.x)[i];
-        } else if (ep.rank > 0) {
-            if (tid == 0 && !spin_geq<true>(ep.flag0, epoch, wb)) raise_err(A.err, SMOE_DEVERR_SPIN_TIMEOUT);
-            xsrc = ep.x0;
-        }
+    if (epm && ep.rank > 0 && tid == 0 && !spin_geq<true>(ep.flag, epoch, wb))
+        raise_err(A.err, SMOE_DEVERR_SPIN_TIMEOUT);
+    __syncthreads();              // (ranks > 0: x is here)
+    ltrace(A.trace, 24);
+    if (epm && ep.rank == 0 && cta == ncta - 1 && warp == kLHWarp) {   // (a CTA without a router row)
+        // push x into every other rank's window, then advance each one's
+        // epoch flag with a system-scope release (after the warp barrier it
+        // orders every lane's stores); they read x and poll the flag locally
+        const uint32_t xbytes = uint32_t(size_t(g.ntok) * d * (A.x_dtype == 0 ? 4 : 2));
+#pragma unroll
+        for (int r = 1; r < kEpMaxWorld; ++r)
+            if (r < ep.world) ep_push_x(ep.xw[r], A.x, xbytes, lane);
+        __syncwarp();
+#pragma unroll
+        for (int r = 1; r < kEpMaxWorld; ++r)
+            if (r < ep.world && lane == 0) st_rel_sys(ep.flagw[r], epoch);
     }
-    __syncthreads();              // (ranks > 0: rank 0's x is published; rank 0 CTA 0: x0 is written)
     // routing given: the producer warp's loads of it
     uint32_t pre_id[2] = {0u, 0u};
     float pre_w[2] = {0.f, 0.f};
@@ -534,10 +561,6 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
                 pre_w[q] = __ldcg(A.wts_in + i);
             }
         }
-    }
-    if (epm && ep.rank == 0 && cta == 0 && tid == 0) {
-        __threadfence_system();
-        st_rel_sys(ep.flag0, epoch);
     }
 
     // The CTA's share of the A units [a0, a1) and the B units [b0, b1), known
@@ -1059,8 +1082,9 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
 #pragma unroll
                     for (int jj = 0; jj < 32; ++jj) s += red2[jj * 16 + tid];
                     const size_t yi = size_t(t) * d + o * 16 + tid;
-                    const bool write = !epm || ep_combine16(ep.rank, ep.world, ep.part0, ep.part_stride, ep.cnt0, s,
-                                                            yi, bu, tid, A.err, wb);
+                    const bool write = !epm || ep_combine16(ep.rank, ep.world, ep.part0, ep.part_stride, epoch, s,
+                                                            yi, A.err, wb);
+                    if (bu == b0) ltrace(A.trace, 22);
                     if (write) {
                         if (A.y_dtype == 0) static_cast<float*>(A.y)[yi] = s;
                         else static_cast<__nv_bfloat16*>(A.y)[yi] = __float2bfloat16_rn(s);

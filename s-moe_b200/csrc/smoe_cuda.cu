@@ -80,7 +80,7 @@ struct SmoeCudaCtx {
     // expert parallel: this rank's exchange window (IPC-exported) and rank 0's, mapped
     uint8_t* ep_win = nullptr;
     size_t ep_win_bytes = 0;
-    uint8_t* ep_peer0 = nullptr;
+    uint8_t* ep_peer[smoe::kEpMaxWorld] = {};   // windows of the ranks this one writes to (own: ep_win)
     int ep_world = 0, ep_rank = 0;
 };
 
@@ -492,7 +492,8 @@ void smoe_cuda_destroy(SmoeCudaCtx* c) {
     if (!c) return;
     cudaSetDevice(c->device);
     if (c->own_stream) cudaStreamSynchronize(c->own_stream);
-    if (c->ep_peer0 && c->ep_peer0 != c->ep_win) cudaIpcCloseMemHandle(c->ep_peer0);
+    for (int r = 0; r < smoe::kEpMaxWorld; ++r)
+        if (c->ep_peer[r] && c->ep_peer[r] != c->ep_win) cudaIpcCloseMemHandle(c->ep_peer[r]);
     if (c->ep_win) cudaFree(c->ep_win);
     for (auto& ev : c->events)
         if (ev) cudaEventDestroy(ev);
@@ -1035,15 +1036,16 @@ namespace {
 constexpr size_t kEpFlagOff = 0, kEpXOff = 256;
 size_t ep_x_bytes(const SmoeCudaCtx* c) { return size_t(smoe::kLMaxTok) * c->cfg.max_d_model * 4; }
 size_t ep_part_stride(const SmoeCudaCtx* c) { return size_t(smoe::kLMaxTok) * c->cfg.max_d_model; }
-size_t ep_cnt_off(const SmoeCudaCtx* c) {
-    return kEpXOff + ep_x_bytes(c) + size_t(smoe::kEpMaxWorld) * ep_part_stride(c) * 4;
+size_t ep_part_off(const SmoeCudaCtx* c) { return kEpXOff + ep_x_bytes(c); }
+size_t ep_win_size(const SmoeCudaCtx* c) {
+    return ep_part_off(c) + size_t(smoe::kEpMaxWorld) * ep_part_stride(c) * 8;   // tagged rows, 8 B each
 }
 }  // namespace
 
 int smoe_cuda_ep_export(SmoeCudaCtx* c, SmoeEpHandle* out) {
     if (!c || !out) { set_err("null argument %s%ld", "", 0); return SMOE_ERR_ARG; }
     if (!c->ep_win) {
-        c->ep_win_bytes = ep_cnt_off(c) + size_t(smoe::kLMaxTok) * (c->cfg.max_d_model / 16) * 4;
+        c->ep_win_bytes = ep_win_size(c);
         CK(cudaMalloc(&c->ep_win, c->ep_win_bytes));
         CK(cudaMemset(c->ep_win, 0, c->ep_win_bytes));
     }
@@ -1060,18 +1062,25 @@ int smoe_cuda_ep_attach(SmoeCudaCtx* c, int rank, int world, const SmoeEpHandle*
         set_err("bad expert-parallel attach (rank %s%ld)", "", (long)rank);
         return SMOE_ERR_ARG;
     }
-    if (c->ep_peer0 && c->ep_peer0 != c->ep_win) cudaIpcCloseMemHandle(c->ep_peer0);
-    c->ep_peer0 = nullptr;
+    for (int r = 0; r < smoe::kEpMaxWorld; ++r) {
+        if (c->ep_peer[r] && c->ep_peer[r] != c->ep_win) cudaIpcCloseMemHandle(c->ep_peer[r]);
+        c->ep_peer[r] = nullptr;
+    }
     cudaIpcMemHandle_t mine;
     CK(cudaIpcGetMemHandle(&mine, c->ep_win));
-    if (rank == 0 || memcmp(&mine, handles[0].bytes, sizeof(mine)) == 0) {
-        c->ep_peer0 = c->ep_win;          // rank 0, or a window this process owns
-    } else {
-        cudaIpcMemHandle_t h;
-        memcpy(&h, handles[0].bytes, sizeof(h));
-        void* p = nullptr;
-        CK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
-        c->ep_peer0 = static_cast<uint8_t*>(p);
+    // rank 0 writes x into every rank's window; the others write their rows
+    // into rank 0's
+    for (int r = 0; r < world; ++r) {
+        if (r != 0 && rank != 0) continue;
+        if (r == rank || memcmp(&mine, handles[r].bytes, sizeof(mine)) == 0) {
+            c->ep_peer[r] = c->ep_win;    // this rank, or a window this process owns
+        } else {
+            cudaIpcMemHandle_t h;
+            memcpy(&h, handles[r].bytes, sizeof(h));
+            void* p = nullptr;
+            CK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+            c->ep_peer[r] = static_cast<uint8_t*>(p);
+        }
     }
     c->ep_rank = rank;
     c->ep_world = world;
@@ -1086,7 +1095,7 @@ int smoe_cuda_ep_attach(SmoeCudaCtx* c, int rank, int world, const SmoeEpHandle*
 int smoe_cuda_moe_layer_ep(SmoeCudaCtx* c, const SmoeMoeLayer* shard, uint32_t n_experts_total,
                            uint32_t expert_base, const void* x, int x_dtype, uint32_t batch, uint32_t k,
                            int norm, void* y, int y_dtype, uint32_t* ids_out, float* w_out) {
-    if (!c || !shard || !c->ep_peer0) { set_err("expert parallel not attached %s%ld", "", 0); return SMOE_ERR_ARG; }
+    if (!c || !shard || !c->ep_peer[0]) { set_err("expert parallel not attached %s%ld", "", 0); return SMOE_ERR_ARG; }
     const bool r0 = c->ep_rank == 0;
     if (!(shard->fmt & SMOE_LAYOUT_TILED) || !shard->router_w || !aligned16(shard->router_w) ||
         n_experts_total < k || k == 0 || k > SMOE_MAX_ACTIVE || n_experts_total > c->cfg.max_experts ||
@@ -1103,16 +1112,19 @@ int smoe_cuda_moe_layer_ep(SmoeCudaCtx* c, const SmoeMoeLayer* shard, uint32_t n
     ep.rank = c->ep_rank;
     ep.base = expert_base;
     ep.nlocal = shard->n_experts;
-    ep.x0 = c->ep_peer0 + kEpXOff;
-    ep.flag0 = reinterpret_cast<uint32_t*>(c->ep_peer0 + kEpFlagOff);
-    ep.part0 = reinterpret_cast<float*>(c->ep_peer0 + kEpXOff + ep_x_bytes(c));
-    ep.cnt0 = reinterpret_cast<uint32_t*>(c->ep_peer0 + ep_cnt_off(c));
+    for (int r = 1; r < c->ep_world; ++r)
+        if (r0) {
+            ep.xw[r] = c->ep_peer[r] + kEpXOff;
+            ep.flagw[r] = reinterpret_cast<uint32_t*>(c->ep_peer[r] + kEpFlagOff);
+        }
+    ep.flag = reinterpret_cast<uint32_t*>(c->ep_win + kEpFlagOff);
+    ep.part0 = reinterpret_cast<unsigned long long*>(c->ep_peer[0] + ep_part_off(c));
     ep.part_stride = uint32_t(ep_part_stride(c));
     LayerCall q{};
     q.L = shard;
     q.n_experts = n_experts_total;
     q.expert_base = expert_base;
-    q.x = r0 ? x : c->ep_peer0 + kEpXOff;            // ranks > 0 read rank 0's published copy
+    q.x = r0 ? x : c->ep_win + kEpXOff;              // ranks > 0 read the copy rank 0 pushed here
     q.x_dtype = x_dtype;
     q.y = r0 ? y : nullptr;                          // (only rank 0 writes y)
     q.y_dtype = y_dtype;
