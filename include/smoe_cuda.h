@@ -237,9 +237,10 @@ int smoe_cuda_moe_layer(SmoeCudaCtx* ctx, const SmoeMoeLayer* layer, const void*
  * gathers the handles in rank order by any means (e.g. an all-gather of
  * the 64-byte blobs), and every rank calls smoe_cuda_ep_attach with all of
  * them. The exchange then runs inside the layer kernel over NVLink: rank 0
- * publishes x, the other ranks read it with peer loads, every rank routes
- * (identical ids), runs the experts it holds and stores its fp32 partial
- * output into rank 0's window; rank 0 sums the partials in rank order.
+ * pushes x into every rank's window (peer stores, then a release flag),
+ * every rank routes (identical ids), runs the experts it holds and stores
+ * its fp32 output rows, tagged with the call's epoch, into rank 0's window;
+ * rank 0 adds the ranks' rows in rank order.
  * All ranks must make the same sequence of smoe_cuda_moe_layer_ep calls.
  * Waits on other GPUs are bounded (a rank that never arrives raises
  * SMOE_ERR_DEVICE at the next synchronize instead of hanging). */
