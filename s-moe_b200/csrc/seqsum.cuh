@@ -181,6 +181,9 @@ SMOE_DEVINL void seq_sum_cluster(cooperative_groups::cluster_group& cl, const fl
                 const uint32_t nr = min(V - min(V, uint32_t(r) * L), L);
                 const uint32_t a0 = min(nr, uint32_t(th) * C), a1 = min(nr, a0 + C);
                 const int cnt = int(a1 - a0);
+                float my_e[kSeqMaxC];                      // this lane's elements, loaded once per replay
+#pragma unroll
+                for (int q = 0; q < kSeqMaxC; ++q) my_e[q] = (q < cnt) ? er[a0 + q] : 0.0f;
                 int ls = 0;
                 while (ls < 32) {
                     const int ex = f32_expo(s);
@@ -190,12 +193,7 @@ SMOE_DEVINL void seq_sum_cluster(cooperative_groups::cluster_group& cl, const fl
                         if (ex == 0 || ex == 255) ev = (cnt > 0);
                         else if (ex == ce) { li = ti0; ev = (tf & 1) || ti0 >= (1ll << 30); }
                         else if (ex == ce + 1) { li = ti1; ev = (tf & 2) || ti1 >= (1ll << 30); }
-                        else
-                            for (int q = 0; q < cnt; ++q) {
-                                bool ti;
-                                li += inc_for(er[a0 + q], ex, &ti);
-                                ev |= ti;
-                            }
+                        else ev = (cnt > 0);   // another binade: replay element by element
                     }
                     long long incl = li;
 #pragma unroll
@@ -216,12 +214,9 @@ SMOE_DEVINL void seq_sum_cluster(cooperative_groups::cluster_group& cl, const fl
                     if (evl > ls && ex != 0 && ex != 255) s = f32_from(ex, su + before);
                     float sv = s;
                     if (lane == evl) {
-                        float ev_[kSeqMaxC];              // all loads in flight, then the adds
-#pragma unroll
-                        for (int q = 0; q < kSeqMaxC; ++q) ev_[q] = (q < cnt) ? er[a0 + q] : 0.0f;
 #pragma unroll
                         for (int q = 0; q < kSeqMaxC; ++q)
-                            if (q < cnt) sv = __fadd_rn(sv, ev_[q]);
+                            if (q < cnt) sv = __fadd_rn(sv, my_e[q]);
                     }
                     s = __shfl_sync(0xffffffffu, sv, evl);
                     ls = evl + 1;
