@@ -536,18 +536,20 @@ __global__ void __launch_bounds__(kLThreads, 1) k_moe_layer(LayerArgs A) {
         raise_err(A.err, SMOE_DEVERR_SPIN_TIMEOUT);
     __syncthreads();              // (ranks > 0: x is here)
     ltrace(A.trace, 24);
-    if (epm && ep.rank == 0 && cta == ncta - 1 && warp == kLHWarp) {   // (a CTA without a router row)
-        // push x into every other rank's window, then advance each one's
-        // epoch flag with a system-scope release (after the warp barrier it
-        // orders every lane's stores); they read x and poll the flag locally
+    if (epm && ep.rank == 0 && cta >= ncta - (ep.world - 1) && warp == kLHWarp) {
+        // rank r's copy of x is pushed by the h warp of CTA grid - r (idle
+        // until the routing is known), then that rank's epoch flag is advanced with
+        // a system-scope release (after the warp barrier it orders every
+        // lane's stores); the rank reads x and polls the flag locally
+        const int r = ncta - cta;
         const uint32_t xbytes = uint32_t(size_t(g.ntok) * d * (A.x_dtype == 0 ? 4 : 2));
 #pragma unroll
-        for (int r = 1; r < kEpMaxWorld; ++r)
-            if (r < ep.world) ep_push_x(ep.xw[r], A.x, xbytes, lane);
-        __syncwarp();
-#pragma unroll
-        for (int r = 1; r < kEpMaxWorld; ++r)
-            if (r < ep.world && lane == 0) st_rel_sys(ep.flagw[r], epoch);
+        for (int q = 1; q < kEpMaxWorld; ++q)
+            if (q == r) {
+                ep_push_x(ep.xw[q], A.x, xbytes, lane);
+                __syncwarp();
+                if (lane == 0) st_rel_sys(ep.flagw[q], epoch);
+            }
     }
     // routing given: the producer warp's loads of it
     uint32_t pre_id[2] = {0u, 0u};
