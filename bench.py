@@ -332,7 +332,9 @@ def run_ours(args, rank, world, local):
     g_ffn = None if ep else graph_of(stream, [lambda i=i: ffn(i) for i in range(steps)])
     with torch.cuda.stream(stream):
         g_warm.replay()
+        g_step.replay()        # untimed: a graph's first launch also uploads it to the device
     torch.cuda.synchronize()
+    barrier(world)
     clocks = Clocks(local)
     clocks.start()
     time.sleep(0.3)
@@ -402,6 +404,8 @@ def run_ours(args, rank, world, local):
             "config": {"workload": sh["workload"], "layers_cycled": NL,
                        "l2": (f"inputs larger than L2 ({NL} resident layers cycled, a fresh x per step from "
                               "64 rows)"),
+                       "warm_up": (f"{max(args.warmup, 3)} eager steps, then one untimed replay of the "
+                                   "timed graph (its first launch uploads it)"),
                        "parallelism": (f"expert parallel x{world} ({per} experts per GPU, exchange "
                                        "in-kernel over NVLink)") if ep else "single GPU"},
             "layer_us": round(per_step * 1e3, 3),
