@@ -281,9 +281,18 @@ struct LayerCall {
 
 }  // namespace
 namespace smoe {
-// One small copy of the caller's x from pinned host memory into device scratch.
+// One small copy of the caller's x from pinned host memory into device
+// scratch, one 16-byte piece per thread. Launched as a programmatic
+// dependent: the read over the host link is issued before waiting for the
+// previous kernel (which may still read the scratch), and the layer kernel
+// that follows may start its set-up at once.
 __global__ void k_stage_in(const uint4* __restrict__ src, uint4* __restrict__ dst, uint32_t n16) {
-    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += gridDim.x * blockDim.x) dst[i] = src[i];
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (i < n16) v = src[i];
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (i < n16) dst[i] = v;
 }
 }  // namespace smoe
 namespace {
@@ -313,8 +322,18 @@ int launch_layer(SmoeCudaCtx* c, const LayerCall& q) {
     }
     if (xk == 1) {
         const uint32_t n16 = uint32_t(size_t(q.batch) * q.L->d_model * (q.x_dtype == 0 ? 4 : 2) / 16);
-        smoe::k_stage_in<<<(n16 + 255) / 256 < 16 ? (n16 + 255) / 256 : 16, 256, 0, c->stream>>>(
-            static_cast<const uint4*>(q.x), reinterpret_cast<uint4*>(c->in_stage), n16);
+        cudaLaunchConfig_t sc{};
+        cudaLaunchAttribute sa[1];
+        sa[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        sa[0].val.programmaticStreamSerializationAllowed = 1;
+        sc.gridDim = dim3((n16 + 255) / 256);               // n16 <= 4 x 4096 x 4 / 16: at most 16 CTAs
+        sc.blockDim = dim3(256);
+        sc.stream = c->stream;
+        sc.attrs = sa;
+        sc.numAttrs = 1;
+        const uint4* xs = static_cast<const uint4*>(q.x);
+        uint4* xd = reinterpret_cast<uint4*>(c->in_stage);
+        CK(cudaLaunchKernelEx(&sc, smoe::k_stage_in, xs, xd, n16));
         c->dispatches += 1;
         xin = c->in_stage;
     }
