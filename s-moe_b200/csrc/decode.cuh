@@ -26,6 +26,8 @@ SMOE_DEVINL void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory");
 
 constexpr int kAttnThreads = 256;
 constexpr int kAttnMaxCtx = 8192;      // scores of one head held in shared memory
+constexpr int kAttnSplits = 8;         // position splits per head (flash-decoding)
+constexpr int kAttnMaxHeads = 128;
 
 // Block-wide sum (blockDim.x a multiple of 32, <= 1024); result in every thread.
 SMOE_DEVINL float block_sum(float v, float* red32) {
@@ -209,6 +211,8 @@ struct AttnArgs {
     uint32_t slot, valid, attn_ctx;
     const uint32_t* pos;                 // when set: slot = pos % ctx, valid = min(pos + 1, ctx)
     float scale;
+    float* part;                         // split partials [num_heads][gridDim.y][head_dim + 2]
+    uint32_t* cnt;                       // [num_heads] splits done (zero between launches)
 };
 
 SMOE_DEVINL void attn_slot_valid(const AttnArgs& a, uint32_t& slot, uint32_t& valid) {
@@ -246,13 +250,18 @@ SMOE_DEVINL void head_norm_rope(float* x, const uint16_t* w, const float* cs, co
     __syncthreads();
 }
 
-// One CTA per query head (decode.cpp:159-226): QK norm + RoPE of its Q head
-// (-> qbuf) and of its KV head's K, the V head as is; the first Q head of
-// each KV group appends K and V to the ring slot. Scores against the
-// `valid` newest positions (i = 0: this step, taken from shared memory, the
-// others from the ring, written by earlier steps), softmax, weighted sum of
-// V. Scores: a warp takes 8 positions per round, 4 lanes per position with
-// all their loads issued before the reduction. head_dim % 16 == 0, <= 256.
+// Grid (query head h, split s) (decode.cpp:159-226, split-K over the
+// positions as in flash-decoding): QK norm + RoPE of head h's Q (-> qbuf,
+// split 0) and of its KV head's K; split 0 of the first Q head of each KV
+// group appends K and V to the ring slot. Split s takes positions
+// [s P, (s+1) P) of the `valid` newest (i = 0: this step, from shared
+// memory; the others from the ring, written by earlier steps), P =
+// ceil(valid / splits): scores, its own max m, l = sum exp(score - m) and
+// o = sum exp(score - m) v, stored as a partial; the head's last split to
+// finish adds the partials in split order (weights exp(m_s - M)) and writes
+// attn_out. Scores: a warp takes 8 positions per round, 4 lanes per position
+// with all their loads issued before the reduction. head_dim % 16 == 0,
+// <= 256.
 __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(AttnArgs a) {
     __shared__ float red32[32];
     __shared__ __align__(16) float qs[256];
@@ -260,7 +269,9 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(AttnArgs a) {
     __shared__ __align__(16) float vs[256];
     __shared__ float sc[kAttnMaxCtx];
     __shared__ float part[kAttnThreads];
+    __shared__ uint32_t last;
     const uint32_t h = blockIdx.x, hd = a.head_dim, per = a.num_heads / a.num_kv_heads, kvh = h / per;
+    const uint32_t split = blockIdx.y, nsplit = gridDim.y;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = kAttnThreads / 32;
     pdl_trigger();
     pdl_wait();
@@ -274,20 +285,23 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(AttnArgs a) {
     __syncthreads();
     head_norm_rope(qs, a.q_norm_w, a.rope_cos, a.rope_sin, hd, red32);
     head_norm_rope(ks, a.k_norm_w, a.rope_cos, a.rope_sin, hd, red32);
-    for (uint32_t i = tid; i < hd; i += blockDim.x) {
-        a.qbuf[size_t(h) * hd + i] = qs[i];
-        if (h % per == 0) {
-            a.k_cache[size_t(slot) * a.kv_dim + size_t(kvh) * hd + i] = ks[i];
-            a.v_cache[size_t(slot) * a.kv_dim + size_t(kvh) * hd + i] = vs[i];
+    if (split == 0)
+        for (uint32_t i = tid; i < hd; i += blockDim.x) {
+            a.qbuf[size_t(h) * hd + i] = qs[i];
+            if (h % per == 0) {
+                a.k_cache[size_t(slot) * a.kv_dim + size_t(kvh) * hd + i] = ks[i];
+                a.v_cache[size_t(slot) * a.kv_dim + size_t(kvh) * hd + i] = vs[i];
+            }
         }
-    }
-    // scores
+    const uint32_t P = (valid + nsplit - 1) / nsplit;
+    const uint32_t i0 = min(valid, split * P), i1 = min(valid, i0 + P);
+    // scores of positions [i0, i1), at sc[i - i0]
     const uint32_t sub = lane & 3, q4 = hd / 16;                  // float4s per lane and position
     const float4* qv = reinterpret_cast<const float4*>(qs) + sub * q4;
-    for (uint32_t base = warp * 8; base < valid; base += nw * 8) {
+    for (uint32_t base = i0 + warp * 8; base < i1; base += nw * 8) {
         const uint32_t i = base + (lane >> 2);
         float s = 0.f;
-        if (i < valid) {
+        if (i < i1) {
             const float4* kr = i == 0 ? reinterpret_cast<const float4*>(ks) + sub * q4
                                       : reinterpret_cast<const float4*>(
                                             a.k_cache + size_t((slot + a.attn_ctx - i) % a.attn_ctx) * a.kv_dim +
@@ -308,44 +322,74 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(AttnArgs a) {
         }
         s += __shfl_xor_sync(0xffffffffu, s, 1);
         s += __shfl_xor_sync(0xffffffffu, s, 2);
-        if (sub == 0 && i < valid) sc[i] = s * a.scale;
+        if (sub == 0 && i < i1) sc[i - i0] = s * a.scale;
     }
     __syncthreads();
     float m = -INFINITY;
-    for (uint32_t i = tid; i < valid; i += blockDim.x) m = fmaxf(m, sc[i]);
+    for (uint32_t i = i0 + tid; i < i1; i += blockDim.x) m = fmaxf(m, sc[i - i0]);
     m = block_max(m, red32);
     float sum = 0.f;
-    for (uint32_t i = tid; i < valid; i += blockDim.x) {
-        const float e = expf(sc[i] - m);
-        sc[i] = e;
+    for (uint32_t i = i0 + tid; i < i1; i += blockDim.x) {
+        const float e = expf(sc[i - i0] - m);
+        sc[i - i0] = e;
         sum += e;
     }
     sum = block_sum(sum, red32);
-    const float inv = sum > 0.f ? 1.0f / sum : 0.f;
     __syncthreads();
-    // thread t: dim t % hd over positions t / hd + g k; 4 loads in flight
+    // thread t: dim t % hd over positions i0 + t / hd + g k; 4 loads in flight
     const uint32_t g = kAttnThreads / hd, dim = tid % hd, grp = tid / hd;
     float acc = 0.f;
     if (grp < g) {
-        if (grp == 0) acc = sc[0] * vs[dim];
         const float* vb = a.v_cache + size_t(kvh) * hd + dim;
-        uint32_t i = grp == 0 ? g : grp;
-        for (; i + 3 * g < valid; i += 4 * g) {
+        uint32_t i = i0 + grp;
+        if (i == 0 && i < i1) {
+            acc = sc[0] * vs[dim];
+            i += g;
+        }
+        for (; i + 3 * g < i1; i += 4 * g) {
             float vv[4];
 #pragma unroll
             for (int q = 0; q < 4; ++q) vv[q] = vb[size_t((slot + a.attn_ctx - (i + q * g)) % a.attn_ctx) * a.kv_dim];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) acc = fmaf(sc[i + q * g], vv[q], acc);
+            for (int q = 0; q < 4; ++q) acc = fmaf(sc[i - i0 + q * g], vv[q], acc);
         }
-        for (; i < valid; i += g) acc = fmaf(sc[i], vb[size_t((slot + a.attn_ctx - i) % a.attn_ctx) * a.kv_dim], acc);
+        for (; i < i1; i += g)
+            acc = fmaf(sc[i - i0], vb[size_t((slot + a.attn_ctx - i) % a.attn_ctx) * a.kv_dim], acc);
     }
     part[tid] = acc;
     __syncthreads();
-    if (uint32_t(tid) < hd) {
-        float o = 0.f;
+    float o = 0.f;
+    if (uint32_t(tid) < hd)
         for (uint32_t q = 0; q < g; ++q) o += part[q * hd + tid];
-        a.attn_out[size_t(h) * hd + tid] = o * inv;
+    if (nsplit == 1) {
+        if (uint32_t(tid) < hd) a.attn_out[size_t(h) * hd + tid] = o * (sum > 0.f ? 1.0f / sum : 0.f);
+        return;
     }
+    // this split's partial; the head's last split combines them
+    float* pp = a.part + (size_t(h) * nsplit + split) * (hd + 2);
+    if (uint32_t(tid) < hd) pp[2 + tid] = o;
+    if (tid == 0) {
+        pp[0] = m;
+        pp[1] = sum;
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) last = atomicAdd(a.cnt + h, 1u) == nsplit - 1 ? 1u : 0u;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    float M = -INFINITY;
+    for (uint32_t q = 0; q < nsplit; ++q) M = fmaxf(M, __ldcg(a.part + (size_t(h) * nsplit + q) * (hd + 2)));
+    float L = 0.f, out = 0.f;
+    for (uint32_t q = 0; q < nsplit; ++q) {
+        const float* pq = a.part + (size_t(h) * nsplit + q) * (hd + 2);
+        const float mq = __ldcg(pq);
+        const float wq = mq == -INFINITY ? 0.f : expf(mq - M);
+        L = fmaf(__ldcg(pq + 1), wq, L);
+        if (uint32_t(tid) < hd) out = fmaf(__ldcg(pq + 2 + tid), wq, out);
+    }
+    if (uint32_t(tid) < hd) a.attn_out[size_t(h) * hd + tid] = out * (L > 0.f ? 1.0f / L : 0.f);
+    if (tid == 0) a.cnt[h] = 0u;                  // ready for the next launch
 }
 
 // End of a decode step on the device: append this step's token to the

@@ -50,7 +50,9 @@ struct SmoeCudaCtx {
     float* in_stage = nullptr;      // [64][max_d_model]           mirror inputs
     float* batch_out = nullptr;     // [64][max_d_model]           token-batch outputs
     float* logits = nullptr;        // [max_batch][max_experts]
-    unsigned long long* lpair = nullptr;  // layer kernel's tagged logits [kLMaxTok][128] (zero: no tag)
+    unsigned long long* lpair = nullptr;
+    float* attn_part = nullptr;           // decode attention split partials [heads][splits][258]
+    uint32_t* attn_cnt = nullptr;         // [heads] splits done (zero between launches)  // layer kernel's tagged logits [kLMaxTok][128] (zero: no tag)
     uint32_t* ids = nullptr;        // [max_batch][16]
     float* wts = nullptr;           // [max_batch][16]
     uint32_t* ticket = nullptr;     // [max_batch]
@@ -472,6 +474,9 @@ SmoeCudaCtx* smoe_cuda_init_ex(const SmoeCudaInitArgs* args) {
     if ((e = cudaMalloc(&c->in_stage, size_t(SMOE_MAX_FFN_BATCH) * a.max_d_model * 4)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->logits, size_t(a.max_batch) * a.max_experts * 4)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->lpair, size_t(smoe::kLMaxTok) * 128 * 8)) != cudaSuccess) return fail(e);
+    if ((e = cudaMalloc(&c->attn_part, size_t(smoe::kAttnMaxHeads) * smoe::kAttnSplits * 258 * 4)) != cudaSuccess)
+        return fail(e);
+    if ((e = cudaMalloc(&c->attn_cnt, size_t(smoe::kAttnMaxHeads) * 4)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->ids, size_t(a.max_batch) * 16 * 4)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->wts, size_t(a.max_batch) * 16 * 4)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->ticket, size_t(a.max_batch) * 4)) != cudaSuccess) return fail(e);
@@ -487,6 +492,7 @@ SmoeCudaCtx* smoe_cuda_init_ex(const SmoeCudaInitArgs* args) {
     if ((e = cudaMalloc(&c->g_ys, slots * a.max_d_model * 4)) != cudaSuccess) return fail(e);
     cudaMemsetAsync(c->lstate, 0, sizeof(smoe::LayerState), c->stream);
     cudaMemsetAsync(c->lpair, 0, size_t(smoe::kLMaxTok) * 128 * 8, c->stream);
+    cudaMemsetAsync(c->attn_cnt, 0, size_t(smoe::kAttnMaxHeads) * 4, c->stream);
     cudaMemsetAsync(c->lpart, 0, size_t(c->num_sms) * smoe::kLMaxTok * smoe::kLMaxD * 8, c->stream);
     c->gemv_cap = a.max_vocab > a.max_d_model ? a.max_vocab : a.max_d_model;
     if ((e = cudaMalloc(&c->gemv_out, c->gemv_cap * 4)) != cudaSuccess) return fail(e);
@@ -516,7 +522,7 @@ void smoe_cuda_destroy(SmoeCudaCtx* c) {
     if (c->ep_win) cudaFree(c->ep_win);
     for (auto& ev : c->events)
         if (ev) cudaEventDestroy(ev);
-    void* bufs[] = {c->g_list, c->g_count, c->g_xtab, c->g_xgs, c->g_htab, c->g_hgs, c->g_ys, c->lstate, c->lpair, c->lpart, c->hidden, c->slot_out, c->in_stage, c->batch_out, c->logits, c->ids,
+    void* bufs[] = {c->g_list, c->g_count, c->g_xtab, c->g_xgs, c->g_htab, c->g_hgs, c->g_ys, c->lstate, c->lpair, c->lpart, c->attn_part, c->attn_cnt, c->hidden, c->slot_out, c->in_stage, c->batch_out, c->logits, c->ids,
                     c->wts, c->ticket, c->err, c->gemv_out, c->gemv_in};
     for (void* b : bufs)
         if (b) cudaFree(b);
@@ -1003,6 +1009,7 @@ int smoe_cuda_attention_layer_async(SmoeCudaCtx* c, const SmoeCudaAttnLayerArgs*
         !a->o_out || a->head_dim == 0 || a->head_dim > 256 || a->head_dim % 32 || a->num_kv_heads == 0 ||
         a->num_heads % a->num_kv_heads || a->q_dim != a->num_heads * a->head_dim ||
         a->kv_dim != a->num_kv_heads * a->head_dim || a->attn_ctx == 0 || a->attn_ctx > smoe::kAttnMaxCtx ||
+        a->num_heads > (uint32_t)smoe::kAttnMaxHeads ||
         (!pos && (a->valid == 0 || a->valid > a->attn_ctx || a->slot >= a->attn_ctx))) {
         set_err("bad attention-layer arguments %s%ld", "", 0);
         return SMOE_ERR_ARG;
@@ -1030,7 +1037,11 @@ int smoe_cuda_attention_layer_async(SmoeCudaCtx* c, const SmoeCudaAttnLayerArgs*
     t.slot = a->slot; t.valid = a->valid; t.attn_ctx = a->attn_ctx;
     t.pos = pos;
     t.scale = a->attn_scale;
-    rc = pdl_launch(c, smoe::k_attn_decode, dim3(a->num_heads), dim3(smoe::kAttnThreads), t);
+    t.part = c->attn_part;
+    t.cnt = c->attn_cnt;
+    // positions split over up to kAttnSplits CTAs per head (>= 32 positions of the ring each)
+    const uint32_t splits = std::min<uint32_t>(smoe::kAttnSplits, (a->attn_ctx + 31) / 32);
+    rc = pdl_launch(c, smoe::k_attn_decode, dim3(a->num_heads, splits), dim3(smoe::kAttnThreads), t);
     if (rc) return rc;
     // 4. O projection
     smoe::GemvSet o{};

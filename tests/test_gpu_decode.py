@@ -53,10 +53,14 @@ def test_rms_norm_and_matvec(ctx):
     assert rel(y.cpu().numpy(), bf16(W).reshape(300, d) @ dh.cpu().numpy().astype(np.float64)) < 1e-5
 
 
-@pytest.mark.parametrize("pos", [0, 5, 63, 100])
-def test_attention_layer_mirror(ctx, pos):
-    """smoe_cuda_attention_layer (synchronous mirror) on a pre-filled ring."""
+@pytest.mark.parametrize("ctx_len,pos", [(64, 0), (64, 5), (64, 63), (64, 100), (512, 300), (512, 700)])
+def test_attention_layer_mirror(ctx, ctx_len, pos):
+    """smoe_cuda_attention_layer (synchronous mirror) on a pre-filled ring.
+    The positions are split over up to 8 CTAs per head (ctx / 32, at most
+    8): 2 splits at ctx 64, 8 at ctx 512, with and without the ring
+    wrapping."""
     sh = small_shape()
+    sh.attn_ctx = ctx_len
     W = make_weights(sh, 5)
     ref = RefDecoder(W, sh)
     rng = np.random.default_rng(pos)
