@@ -434,6 +434,15 @@ def run_ours(args, rank, world, local):
             line["sampler"] = sampler_leg(ctx, stream)
             line["decode_30b"] = decode_leg(ctx)
             line["batch256"] = batch_leg(ctx, stream)
+            for key, fn in (("decode_b256", lambda: batched_decode_leg(ctx, "30b", 256, 45, 128)),
+                            ("decode_235b", lambda: decode_235b_leg(ctx)),
+                            ("decode_235b_b32", lambda: batched_decode_leg(ctx, "235b", 32, 45, 32))):
+                try:                    # a side leg that fails leaves the headline line intact
+                    line[key] = fn()
+                except Exception as ex:  # noqa: BLE001
+                    line[key] = {"error": f"{type(ex).__name__}: {ex}"[:300]}
+                    import torch
+                    torch.cuda.empty_cache()
         print(json.dumps(line), flush=True)
     ctx.close()
 
@@ -608,6 +617,50 @@ def decode_leg(ctx, prompt=45, gen=256):
     return out
 
 
+def batched_decode_leg(ctx, shape, batch, prompt, gen):
+    """Config 4 (30B shape, 256 sequences) or config 3 at batch 32 (235B
+    shape, one GPU): every sequence its own random prompt, KV ring (256
+    positions), sampler row (config-4 parameters) and history; one CUDA
+    graph per step (s-moe_b200/decode.py BatchDecoder); tokens per second
+    summed over the sequences, over the generated steps."""
+    import decode as DEC
+    sh = DEC.Shape.qwen3_235b() if shape == "235b" else DEC.Shape()
+    sh.attn_ctx = 256
+    out = DEC.run_batched(ctx, sh, batch, prompt, gen)
+    name = "Qwen3-235B-A22B" if shape == "235b" else "Qwen3-30B-A3B"
+    out["workload"] = (f"{name}-shaped decode, {sh.layers} layers, batch {batch}, prompt {prompt}, {gen} "
+                       "generated per sequence (random weights, vault-layout experts, expert-grouped MoE path)")
+    return out
+
+
+def decode_235b_leg(ctx, prompt=45, gen=64):
+    """Config 3 at batch 1 on one GPU: the Qwen3-235B-A22B shape (94 layers,
+    ~128 GB of tiled Q4 experts resident), one CUDA graph per token."""
+    import numpy as np
+    import torch
+    import decode as DEC
+    sh = DEC.Shape.qwen3_235b()
+    t0 = time.time()
+    model = DEC.Model(ctx, sh)
+    load = time.time() - t0
+    rng = np.random.default_rng(11)
+    dec = DEC.Decoder(model, uniforms=rng.integers(0, 1 << 24, 4096).astype(np.float64) / (1 << 24))
+    dec.capture(torch.cuda.Stream())
+    pr = rng.integers(0, sh.vocab, prompt).tolist()
+    dec.run(pr, 4)
+    dec.reset()
+    _, t = dec.run(pr, gen)
+    ctx.synchronize()
+    ptb = DEC.per_token_bytes(sh)
+    out = {"workload": f"config3 shape: Qwen3-235B-A22B decode, 94 layers, batch 1, 1 GPU, prompt {prompt}, "
+                       f"{gen} generated (random weights)", "tok_per_s": round(gen / t, 2),
+           "ms_per_token": round(1e3 * t / gen, 4), "weight_bytes_per_token": ptb,
+           "achieved_gbs": round(ptb * gen / t / 1e9, 1), "load_s": round(load, 1)}
+    del dec, model
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_leg(name):
     import torch
     import smoe_cuda as S
@@ -617,7 +670,10 @@ def run_leg(name):
     stream = torch.cuda.Stream()
     ctx.set_stream(stream.cuda_stream)
     out = {"sampler": lambda: sampler_leg(ctx, stream), "decode_30b": lambda: decode_leg(ctx),
-           "batch256": lambda: batch_leg(ctx, stream)}[name]()
+           "batch256": lambda: batch_leg(ctx, stream),
+           "decode_b256": lambda: batched_decode_leg(ctx, "30b", 256, 45, 128),
+           "decode_235b": lambda: decode_235b_leg(ctx),
+           "decode_235b_b32": lambda: batched_decode_leg(ctx, "235b", 32, 45, 32)}[name]()
     print(json.dumps({name: out}), flush=True)
     ctx.close()
 
@@ -631,7 +687,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the sampler and decode legs")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--only", choices=["sampler", "decode_30b", "batch256"],
+    ap.add_argument("--only", choices=["sampler", "decode_30b", "batch256", "decode_b256", "decode_235b",
+                                         "decode_235b_b32"],
                     help="run one side leg alone on GPU 0 and print its JSON (profiling)")
     args = ap.parse_args()
     if args.only:

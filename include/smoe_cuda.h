@@ -370,6 +370,35 @@ int smoe_cuda_decode_advance(SmoeCudaCtx* ctx, SmoeSamplerRow* row, uint32_t* hi
                              uint32_t hcap, const uint32_t* token, uint32_t* pos,
                              const float* u_seq, uint32_t u_len);
 
+/* ---- Batched decode: `batch` sequences at one shared position, each with
+ * its own KV ring (256 sequences; the reference decodes
+ * one sequence at a time and batches tokens only per expert in prefill,
+ * prefill.cpp:321-417, kernels.metal:662-769). */
+
+/* Y[b][r] = sum_j W[r, j] X[b][j] for b < batch: matvec_bf16
+ * (common.hpp:293-306) over a batch of fp32 rows. batch == 1 is
+ * smoe_cuda_matvec_bf16. Larger batches run on the tensor cores (cuBLAS bf16
+ * GEMM, fp32 accumulation) over X split into two bf16 planes (hi = bf16(x),
+ * lo = bf16(x - hi)), which keeps the activations to ~2^-17 relative.
+ * batch <= max_batch, cols <= max_d_model, cols % 8 == 0. Asynchronous. */
+int smoe_cuda_gemm_bf16(SmoeCudaCtx* ctx, const uint16_t* w, const float* x, float* y,
+                        uint32_t rows, uint32_t cols, uint32_t batch);
+
+/* The attention layer (decode.cpp:150-231) for `batch` sequences at the
+ * device position *pos: normed_in [batch x d_model], qbuf/attn_out [batch x
+ * q_dim], kbuf/vbuf [batch x kv_dim], o_out [batch x d_model]; sequence b's
+ * rings at k_cache / v_cache + b * kv_seq_stride floats. slot/valid are
+ * ignored (pos decides them). Asynchronous. */
+int smoe_cuda_attention_batch_async(SmoeCudaCtx* ctx, const SmoeCudaAttnLayerArgs* args,
+                                    uint32_t batch, uint64_t kv_seq_stride, const uint32_t* pos);
+
+/* End of a batched decode step: tokens[b] joins rows[b]'s history (history
+ * [batch x hcap]), ++*pos, and rows[b].u = u_seq[(*pos * batch + b) % u_len]
+ * when u_seq is given. batch <= 1024. */
+int smoe_cuda_decode_advance_batch(SmoeCudaCtx* ctx, SmoeSamplerRow* rows, uint32_t* history,
+                                   uint32_t hcap, const uint32_t* tokens, uint32_t batch,
+                                   uint32_t* pos, const float* u_seq, uint32_t u_len);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -26,6 +26,7 @@ NVCC_FLAGS = [
     "-lineinfo", "-O3", "-std=c++17",
     "-Xcompiler", "-fPIC", "-shared",
     "-Xptxas", "-v",
+    "-lcublas",
 ]
 
 

@@ -213,6 +213,9 @@ struct AttnArgs {
     float scale;
     float* part;                         // split partials [num_heads][gridDim.y][head_dim + 2]
     uint32_t* cnt;                       // [num_heads] splits done (zero between launches)
+    size_t kv_seq_stride;                // batched decode (gridDim.z sequences): floats between the
+                                         // rings of consecutive sequences; q/k/v/qbuf/attn_out are
+                                         // [sequences][q_dim or kv_dim] (one split per head then)
 };
 
 SMOE_DEVINL void attn_slot_valid(const AttnArgs& a, uint32_t& slot, uint32_t& valid) {
@@ -263,6 +266,7 @@ SMOE_DEVINL void head_norm_rope(float* x, const uint16_t* w, const float* cs, co
 // with all their loads issued before the reduction. head_dim % 16 == 0,
 // <= 256.
 __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(AttnArgs a) {
+    // (a is this CTA's own copy: the batched offsets below rebase it)
     __shared__ float red32[32];
     __shared__ __align__(16) float qs[256];
     __shared__ __align__(16) float ks[256];
@@ -277,6 +281,16 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(AttnArgs a) {
     pdl_wait();
     uint32_t slot, valid;
     attn_slot_valid(a, slot, valid);
+    if (blockIdx.z) {                    // sequence z of a batch: its rows and its own ring
+        const size_t z = blockIdx.z;
+        a.q += z * a.q_dim;
+        a.k += z * a.kv_dim;
+        a.v += z * a.kv_dim;
+        a.qbuf += z * a.q_dim;
+        a.attn_out += z * a.q_dim;
+        a.k_cache += z * a.kv_seq_stride;
+        a.v_cache += z * a.kv_seq_stride;
+    }
     for (uint32_t i = tid; i < hd; i += blockDim.x) {
         qs[i] = a.q[size_t(h) * hd + i];
         ks[i] = a.k[size_t(kvh) * hd + i];
@@ -414,6 +428,45 @@ __global__ void k_decode_advance(SamplerRowDevMut* row, uint32_t* history, uint3
     const uint32_t p = *pos + 1;
     *pos = p;
     if (u_seq && u_len) row->u = u_seq[p % u_len];
+}
+
+// Batched decode (one position shared by `batch` sequences): sequence b's
+// token joins its sampler row's history, its next uniform is u_seq[(p *
+// batch + b) % u_len] for the new position p, and the position advances once.
+// One CTA, batch <= 1024 threads.
+__global__ void k_decode_advance_batch(SamplerRowDevMut* rows, uint32_t* history, uint32_t hcap,
+                                       const uint32_t* tokens, uint32_t batch, uint32_t* pos,
+                                       const float* u_seq, uint32_t u_len) {
+    pdl_trigger();
+    pdl_wait();
+    const uint32_t b = threadIdx.x;
+    const uint32_t p = *pos + 1;
+    __syncthreads();                     // every thread has read the position
+    if (b < batch) {
+        SamplerRowDevMut* r = rows + b;
+        const uint32_t n = r->history_len;
+        if (n < hcap) {
+            history[size_t(b) * hcap + n] = tokens[b];
+            r->history_len = n + 1;
+        }
+        if (u_seq && u_len) r->u = u_seq[(size_t(p) * batch + b) % u_len];
+    }
+    if (b == 0) *pos = p;
+}
+
+// fp32 rows -> two bf16 planes, hi = bf16(x) and lo = bf16(x - hi), so that a
+// bf16 tensor-core GEMM over both planes (fp32 accumulation) reproduces an
+// fp32-activation matvec to ~2^-17 relative per element. out: [2][n].
+__global__ void k_split_bf16(const float* x, uint16_t* out, size_t n) {
+    pdl_trigger();
+    pdl_wait();
+    for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) {
+        const float v = x[i];
+        const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+        const __nv_bfloat16 lo = __float2bfloat16_rn(v - __bfloat162float(hi));
+        out[i] = __bfloat16_as_ushort(hi);
+        out[n + i] = __bfloat16_as_ushort(lo);
+    }
 }
 
 }  // namespace smoe

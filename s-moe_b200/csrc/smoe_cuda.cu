@@ -1,6 +1,7 @@
 // smoe_cuda.cu - the C ABI of include/smoe_cuda.h: context, scratch,
 // launches and bounded waits. Kernels live in the *.cuh files.
 #include <cuda_runtime.h>
+#include <cublas_v2.h>
 
 #include <atomic>
 #include <chrono>
@@ -36,6 +37,7 @@ void set_err(const char* fmt, const char* a = "", long b = 0) {
     } while (0)
 
 constexpr int kEventRing = 64;
+constexpr size_t kBlasWorkspace = size_t(32) << 20;
 
 }  // namespace
 
@@ -59,6 +61,10 @@ struct SmoeCudaCtx {
     uint32_t* err = nullptr;        // device error word
     float* gemv_out = nullptr;      // staging for the mirrored matvec
     float* gemv_in = nullptr;
+    // batched trunk GEMMs (cuBLAS bf16, fp32 accumulation)
+    cublasHandle_t blas = nullptr;
+    void* blas_ws = nullptr;        // cuBLAS workspace (fixed, so graph capture allocates nothing)
+    uint16_t* xsplit = nullptr;     // [2][max_batch * max_d_model] bf16 hi / lo planes
     size_t gemv_cap = 0;
     // waits
     cudaEvent_t events[kEventRing] = {};
@@ -497,6 +503,14 @@ SmoeCudaCtx* smoe_cuda_init_ex(const SmoeCudaInitArgs* args) {
     c->gemv_cap = a.max_vocab > a.max_d_model ? a.max_vocab : a.max_d_model;
     if ((e = cudaMalloc(&c->gemv_out, c->gemv_cap * 4)) != cudaSuccess) return fail(e);
     if ((e = cudaMalloc(&c->gemv_in, size_t(a.max_d_model) * 4)) != cudaSuccess) return fail(e);
+    if ((e = cudaMalloc(&c->blas_ws, kBlasWorkspace)) != cudaSuccess) return fail(e);
+    if ((e = cudaMalloc(&c->xsplit, size_t(2) * a.max_batch * a.max_d_model * 2)) != cudaSuccess) return fail(e);
+    if (cublasCreate(&c->blas) != CUBLAS_STATUS_SUCCESS ||
+        cublasSetWorkspace(c->blas, c->blas_ws, kBlasWorkspace) != CUBLAS_STATUS_SUCCESS) {
+        set_err("init failed: cuBLAS handle %s%ld", "", 0);
+        smoe_cuda_destroy(c);
+        return nullptr;
+    }
     cudaMemsetAsync(c->ticket, 0, size_t(a.max_batch) * 4, c->stream);
     cudaMemsetAsync(c->hidden, 0, slots * a.max_d_ff * 4, c->stream);
     cudaMemsetAsync(c->err, 0, 4, c->stream);
@@ -517,13 +531,14 @@ void smoe_cuda_destroy(SmoeCudaCtx* c) {
     if (!c) return;
     cudaSetDevice(c->device);
     if (c->own_stream) cudaStreamSynchronize(c->own_stream);
+    if (c->blas) cublasDestroy(c->blas);
     for (int r = 0; r < smoe::kEpMaxWorld; ++r)
         if (c->ep_peer[r] && c->ep_peer[r] != c->ep_win) cudaIpcCloseMemHandle(c->ep_peer[r]);
     if (c->ep_win) cudaFree(c->ep_win);
     for (auto& ev : c->events)
         if (ev) cudaEventDestroy(ev);
     void* bufs[] = {c->g_list, c->g_count, c->g_xtab, c->g_xgs, c->g_htab, c->g_hgs, c->g_ys, c->lstate, c->lpair, c->lpart, c->attn_part, c->attn_cnt, c->hidden, c->slot_out, c->in_stage, c->batch_out, c->logits, c->ids,
-                    c->wts, c->ticket, c->err, c->gemv_out, c->gemv_in};
+                    c->wts, c->ticket, c->err, c->gemv_out, c->gemv_in, c->blas_ws, c->xsplit};
     for (void* b : bufs)
         if (b) cudaFree(b);
     if (c->own_stream) cudaStreamDestroy(c->own_stream);
@@ -1050,6 +1065,91 @@ int smoe_cuda_attention_layer_async(SmoeCudaCtx* c, const SmoeCudaAttnLayerArgs*
     o.cols = a->q_dim;
     o.x = a->attn_out;
     return gemv_set(c, o);
+}
+
+int smoe_cuda_gemm_bf16(SmoeCudaCtx* c, const uint16_t* w, const float* x, float* y, uint32_t rows,
+                        uint32_t cols, uint32_t batch) {
+    if (!c) { set_err("null context %s%ld", "", 0); return SMOE_ERR_ARG; }
+    if (batch == 1) return smoe_cuda_matvec_bf16(c, w, x, y, rows, cols);
+    if (!w || !x || !y || rows == 0 || cols == 0 || cols % 8 || batch == 0 || batch > c->cfg.max_batch ||
+        cols > c->cfg.max_d_model || !aligned16(w)) {
+        set_err("bad batched matvec arguments %s%ld", "", (long)batch);
+        return SMOE_ERR_ARG;
+    }
+    const size_t n = size_t(batch) * cols;
+    int rc = pdl_launch(c, smoe::k_split_bf16, dim3(unsigned((n + 1023) / 1024 < 1184 ? (n + 1023) / 1024 : 1184)),
+                        dim3(1024), x, c->xsplit, n);
+    if (rc) return rc;
+    // cuBLAS is column-major: row-major W [rows x cols] is A = W^T (cols x
+    // rows, ld cols), X [batch x cols] is B = X^T (cols x batch, ld cols) and
+    // Y [batch x rows] is C = Y^T (rows x batch, ld rows); C = A^T B.
+    if (cublasSetStream(c->blas, c->stream) != CUBLAS_STATUS_SUCCESS) {
+        set_err("cuBLAS stream %s%ld", "", 0);
+        return SMOE_ERR_CUDA;
+    }
+    const float one = 1.0f, zero = 0.0f;
+    for (int plane = 0; plane < 2; ++plane) {
+        const cublasStatus_t st = cublasGemmEx(
+            c->blas, CUBLAS_OP_T, CUBLAS_OP_N, int(rows), int(batch), int(cols), &one, w, CUDA_R_16BF, int(cols),
+            c->xsplit + plane * n, CUDA_R_16BF, int(cols), plane ? &one : &zero, y, CUDA_R_32F, int(rows),
+            CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+        if (st != CUBLAS_STATUS_SUCCESS) {
+            set_err("cuBLAS GEMM failed %s(status %ld)", "", (long)st);
+            return SMOE_ERR_CUDA;
+        }
+        c->dispatches += 1;
+    }
+    return SMOE_OK;
+}
+
+int smoe_cuda_attention_batch_async(SmoeCudaCtx* c, const SmoeCudaAttnLayerArgs* a, uint32_t batch,
+                                    uint64_t kv_seq_stride, const uint32_t* pos) {
+    if (!c || !a || !pos || batch == 0 || batch > 65535 || !a->w_q || !a->w_k || !a->w_v || !a->w_o ||
+        !a->rope_cos || !a->rope_sin || !a->normed_in || !a->qbuf || !a->kbuf || !a->vbuf || !a->k_cache ||
+        !a->v_cache || !a->attn_out || !a->o_out || a->head_dim == 0 || a->head_dim > 256 || a->head_dim % 32 ||
+        a->num_kv_heads == 0 || a->num_heads % a->num_kv_heads || a->q_dim != a->num_heads * a->head_dim ||
+        a->kv_dim != a->num_kv_heads * a->head_dim || a->attn_ctx == 0 || a->attn_ctx > smoe::kAttnMaxCtx ||
+        a->num_heads > (uint32_t)smoe::kAttnMaxHeads ||
+        (batch > 1 && kv_seq_stride < uint64_t(a->attn_ctx) * a->kv_dim)) {
+        set_err("bad batched attention arguments %s%ld", "", (long)batch);
+        return SMOE_ERR_ARG;
+    }
+    int rc;
+    if ((rc = smoe_cuda_gemm_bf16(c, a->w_q, a->normed_in, a->qbuf, a->q_dim, a->d_model, batch))) return rc;
+    if ((rc = smoe_cuda_gemm_bf16(c, a->w_k, a->normed_in, a->kbuf, a->kv_dim, a->d_model, batch))) return rc;
+    if ((rc = smoe_cuda_gemm_bf16(c, a->w_v, a->normed_in, a->vbuf, a->kv_dim, a->d_model, batch))) return rc;
+    smoe::AttnArgs t{};
+    t.q = a->qbuf; t.k = a->kbuf; t.v = a->vbuf;
+    t.q_norm_w = a->q_norm_w; t.k_norm_w = a->k_norm_w;
+    t.rope_cos = a->rope_cos; t.rope_sin = a->rope_sin;
+    t.qbuf = a->qbuf; t.kbuf = a->kbuf; t.vbuf = a->vbuf;
+    t.k_cache = a->k_cache; t.v_cache = a->v_cache;
+    t.attn_out = a->attn_out;
+    t.q_dim = a->q_dim; t.kv_dim = a->kv_dim; t.head_dim = a->head_dim;
+    t.num_heads = a->num_heads; t.num_kv_heads = a->num_kv_heads;
+    t.attn_ctx = a->attn_ctx;
+    t.pos = pos;
+    t.scale = a->attn_scale;
+    t.part = c->attn_part;
+    t.cnt = c->attn_cnt;
+    t.kv_seq_stride = size_t(kv_seq_stride);
+    // batch x heads CTAs cover the GPU: one split per head (no partials)
+    const uint32_t splits = batch > 1 ? 1u : std::min<uint32_t>(smoe::kAttnSplits, (a->attn_ctx + 31) / 32);
+    rc = pdl_launch(c, smoe::k_attn_decode, dim3(a->num_heads, splits, batch), dim3(smoe::kAttnThreads), t);
+    if (rc) return rc;
+    return smoe_cuda_gemm_bf16(c, a->w_o, a->attn_out, a->o_out, a->d_model, a->q_dim, batch);
+}
+
+int smoe_cuda_decode_advance_batch(SmoeCudaCtx* c, SmoeSamplerRow* rows, uint32_t* history, uint32_t hcap,
+                                   const uint32_t* tokens, uint32_t batch, uint32_t* pos, const float* u_seq,
+                                   uint32_t u_len) {
+    if (!c || !rows || !tokens || !pos || (hcap && !history) || batch == 0 || batch > 1024) {
+        set_err("bad decode_advance_batch arguments %s%ld", "", (long)batch);
+        return SMOE_ERR_ARG;
+    }
+    return pdl_launch(c, smoe::k_decode_advance_batch, dim3(1), dim3((batch + 31) / 32 * 32),
+                      reinterpret_cast<smoe::SamplerRowDevMut*>(rows), history, hcap, tokens, batch, pos, u_seq,
+                      u_len);
 }
 
 int smoe_cuda_attention_layer(SmoeCudaCtx* c, const SmoeCudaAttnLayerArgs* a) {

@@ -11,7 +11,16 @@ no host work; prompt tokens are written into the token slot before their
 step. (During the prompt the sampled token is discarded but still appended
 to the device history, which the repetition penalty reads.)
 
-    python s-moe_b200/decode.py --layers 48 --gen 256     # 30B-shaped decode timing
+BatchDecoder steps `batch` sequences at one shared position (BASELINE
+config 4: 256 sequences of the 30B shape; config 3 at batch 32): each has its
+own KV ring, sampler row and history; the trunk matmuls run as batched GEMMs
+and the MoE layer takes all the batch's tokens at once (the expert-grouped
+path, vault layout).
+
+    python s-moe_b200/decode.py --layers 48 --gen 256                 # 30B-shaped decode, batch 1
+    python s-moe_b200/decode.py --batch 256 --gen 128 --ctx 256       # config 4: 256 sequences
+    python s-moe_b200/decode.py --shape 235b --gen 128                # config 3, batch 1, one GPU
+    python s-moe_b200/decode.py --shape 235b --batch 32 --gen 128 --ctx 256
 """
 from __future__ import annotations
 
@@ -47,6 +56,14 @@ class Shape:
     attn_ctx: int = 4096
     fmt: int = S.FMT_AFFINE_Q4
 
+    @classmethod
+    def qwen3_235b(cls, **kw):
+        """Qwen3-235B-A22B shape."""
+        base = dict(layers=94, d_model=4096, num_heads=64, num_kv_heads=4, head_dim=128, n_experts=128,
+                    top_k=8, d_ff=1536)
+        base.update(kw)
+        return cls(**base)
+
     @property
     def q_dim(self):
         return self.num_heads * self.head_dim
@@ -75,7 +92,7 @@ class Model:
     in the vault layout. Without `weights`, random weights with the
     benchmark's distributions are generated on the device (seeded)."""
 
-    def __init__(self, ctx: "S.Context", shape: Shape, weights=None, seed: int = 7):
+    def __init__(self, ctx: "S.Context", shape: Shape, weights=None, seed: int = 7, layout: str = "tiled"):
         self.ctx, self.shape = ctx, shape
         sh = shape
         dev = "cuda"
@@ -112,6 +129,10 @@ class Model:
             else:
                 varena, stride, off = self._random_experts(g)
             vault = S.make_layer(varena, stride, off, sh.n_experts, sh.d_model, sh.d_ff, sh.fmt, L["router"])
+            if layout == "vault":            # batched decode: the expert-grouped path reads the vault layout
+                L["vault"], L["vault_buf"] = vault, varena
+                self.layers.append(L)
+                continue
             tb = torch.empty(sh.n_experts * tstride, dtype=torch.uint8, device=dev)
             # the arena was written on torch's stream, the prepack runs on the
             # context's: finish the former first, the latter before the arena
@@ -251,14 +272,184 @@ class Decoder:
         return toks.cpu().numpy().tolist(), e0.elapsed_time(e1) / 1e3
 
 
+class BatchDecoder:
+    """`batch` sequences decoded together at one shared position. Per
+    sequence: its own KV ring (attn_ctx positions), sampler row
+    (temperature, top_p, top_k, rep_penalty, u, history_len) and history.
+    Step graph: embed B tokens, L x (B-row input norm, batched attention
+    layer, B-row post norm, MoE layer over the B tokens), final norm, LM head
+    as a batched GEMM, B-row sampler, batched bookkeeping. The model must be
+    built with layout="vault"."""
+
+    def __init__(self, model: Model, batch: int, rows: np.ndarray | None = None,
+                 uniforms: np.ndarray | None = None, hcap: int = 512):
+        self.m, self.ctx, self.B = model, model.ctx, batch
+        sh = model.shape
+        B = batch
+        f32 = dict(dtype=torch.float32, device="cuda")
+        self.hidden = torch.zeros(B, sh.d_model, **f32)
+        self.normed = torch.zeros(B, sh.d_model, **f32)
+        self.attn_o = torch.zeros(B, sh.d_model, **f32)
+        self.ffn_out = torch.zeros(B, sh.d_model, **f32)
+        self.qbuf = torch.zeros(B, sh.q_dim, **f32)
+        self.kbuf = torch.zeros(B, sh.kv_dim, **f32)
+        self.vbuf = torch.zeros(B, sh.kv_dim, **f32)
+        self.attn_out = torch.zeros(B, sh.q_dim, **f32)
+        self.kv = torch.zeros(sh.layers, 2, B, sh.attn_ctx, sh.kv_dim, **f32)
+        self.rope_cos = torch.zeros(sh.head_dim // 2, **f32)
+        self.rope_sin = torch.zeros(sh.head_dim // 2, **f32)
+        self.inv_freq = torch.from_numpy(rope_inv_freq(sh)).cuda()
+        self.logits = torch.zeros(B, sh.vocab, **f32)
+        self.tokens = torch.zeros(B, dtype=torch.int32, device="cuda")
+        self.pos = torch.zeros(1, dtype=torch.int32, device="cuda")
+        self.hcap = hcap
+        self.history = torch.zeros(B, hcap, dtype=torch.int32, device="cuda")
+        if rows is None:
+            rows = batch_rows(B)
+        self.rows0 = np.ascontiguousarray(rows, np.float32).copy()
+        self.rows = torch.from_numpy(self.rows0.view(np.int32)).cuda()
+        self.u_seq = torch.from_numpy((uniforms if uniforms is not None else np.full(1, 0.5)).astype(np.float32)).cuda()
+        torch.cuda.synchronize()
+        self.args = []
+        for l, L in enumerate(model.layers):
+            a = S.AttnLayerArgs()
+            for name in ("w_q", "w_k", "w_v", "w_o"):
+                setattr(a, name, L[name].data_ptr())
+            a.q_norm_w, a.k_norm_w = L["q_norm"].data_ptr(), L["k_norm"].data_ptr()
+            a.rope_cos, a.rope_sin = self.rope_cos.data_ptr(), self.rope_sin.data_ptr()
+            a.normed_in = self.normed.data_ptr()
+            a.qbuf, a.kbuf, a.vbuf = self.qbuf.data_ptr(), self.kbuf.data_ptr(), self.vbuf.data_ptr()
+            a.k_cache, a.v_cache = self.kv[l, 0].data_ptr(), self.kv[l, 1].data_ptr()
+            a.attn_out, a.o_out = self.attn_out.data_ptr(), self.attn_o.data_ptr()
+            a.d_model, a.q_dim, a.kv_dim = sh.d_model, sh.q_dim, sh.kv_dim
+            a.head_dim, a.num_heads, a.num_kv_heads = sh.head_dim, sh.num_heads, sh.num_kv_heads
+            a.slot, a.valid, a.attn_ctx = 0, 1, sh.attn_ctx
+            a.attn_scale = 1.0 / math.sqrt(sh.head_dim)
+            self.args.append(a)
+        self.kv_seq_stride = sh.attn_ctx * sh.kv_dim
+        self.graph = None
+
+    def _step(self):
+        c, sh, B = self.ctx, self.m.shape, self.B
+        c.embed_bf16(self.m.embed, self.tokens, B, sh.d_model, self.hidden)
+        c.rope_table(self.pos, self.inv_freq, self.rope_cos, self.rope_sin, sh.head_dim // 2)
+        for l, L in enumerate(self.m.layers):
+            c.rms_norm(self.hidden, self.ffn_out if l > 0 else None, L["in_norm"], self.normed, sh.d_model, rows=B)
+            c.attention_batch(self.args[l], B, self.kv_seq_stride, self.pos)
+            c.rms_norm(self.hidden, self.attn_o, L["post_norm"], self.normed, sh.d_model, rows=B)
+            c.moe_layer(L["vault"], self.normed, S.DTYPE_F32, B, sh.top_k, sh.norm_topk, self.ffn_out, S.DTYPE_F32)
+        c.rms_norm(self.hidden, self.ffn_out, self.m.model_norm, self.normed, sh.d_model, rows=B)
+        c.gemm_bf16(self.m.lm_head, self.normed, self.logits, sh.vocab, sh.d_model, B)
+        c.sample(self.logits, sh.vocab, B, self.rows, self.history, self.hcap, self.tokens)
+        c.decode_advance_batch(self.rows, self.history, self.hcap, self.tokens, B, self.pos, self.u_seq,
+                               self.u_seq.numel())
+
+    def capture(self, stream: torch.cuda.Stream):
+        self.stream = stream
+        self.ctx.set_stream(stream.cuda_stream)
+        with torch.cuda.stream(stream):
+            self._step()
+        torch.cuda.synchronize()
+        self.reset()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=stream):
+            self._step()
+        torch.cuda.synchronize()
+
+    def reset(self):
+        torch.cuda.synchronize()
+        self.kv.zero_()
+        self.pos.zero_()
+        self.history.zero_()
+        self.rows.copy_(torch.from_numpy(self.rows0.view(np.int32)))
+        torch.cuda.synchronize()
+
+    def run(self, prompts: np.ndarray, n_gen: int):
+        """prompts [B, P] token ids (one prompt per sequence, fed in step), then
+        n_gen sampled steps; returns (generated ids [n_gen, B], seconds)."""
+        assert self.graph is not None
+        pr = torch.from_numpy(np.ascontiguousarray(prompts.T, np.int32)).cuda()
+        with torch.cuda.stream(self.stream):
+            for p in range(pr.shape[0]):
+                self.tokens.copy_(pr[p])
+                self.graph.replay()
+            toks = torch.zeros(n_gen, self.B, dtype=torch.int32, device="cuda")
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(self.stream)
+            for i in range(n_gen):
+                self.graph.replay()
+                toks[i].copy_(self.tokens)
+            e1.record(self.stream)
+            torch.cuda.synchronize()
+        return toks.cpu().numpy(), e0.elapsed_time(e1) / 1e3
+
+
+def batch_rows(B: int, seed: int = 5) -> np.ndarray:
+    """BASELINE config 4 sampler rows: temperature in {0.6, 0.7, 1.0}, top-k
+    in {20, 40}, top-p in {0.8, 0.95}, repetition penalty 1.1, a seeded
+    uniform each; history starts empty. [B, 6] float32 (top_k and
+    history_len as uint32 bits)."""
+    rng = np.random.default_rng(seed)
+    rows = np.zeros((B, 6), np.float32)
+    rows[:, 0] = np.array([0.6, 0.7, 1.0], np.float32)[np.arange(B) % 3]
+    rows[:, 1] = np.array([0.8, 0.95], np.float32)[np.arange(B) % 2]
+    rows.view(np.uint32)[:, 2] = np.array([20, 40])[(np.arange(B) // 2) % 2]
+    rows[:, 3] = 1.1
+    rows[:, 4] = (rng.integers(0, 1 << 24, B) / (1 << 24)).astype(np.float32)
+    rows.view(np.uint32)[:, 5] = 0
+    return rows
+
+
+def per_token_bytes(sh: Shape) -> int:
+    """Weights one batch-1 token reads: top-k experts, attention, router, LM head."""
+    attn = (2 * sh.q_dim + 2 * sh.kv_dim) * sh.d_model * 2
+    return (sh.layers * (sh.top_k * S.expert_bytes(sh.fmt, sh.d_model, sh.d_ff) + attn
+                         + sh.n_experts * sh.d_model * 2) + sh.vocab * sh.d_model * 2)
+
+
+def run_batched(ctx, sh: Shape, batch: int, prompt: int, gen: int, seed: int = 11) -> dict:
+    t0 = time.time()
+    model = Model(ctx, sh, layout="vault")
+    t_load = time.time() - t0
+    rng = np.random.default_rng(seed)
+    dec = BatchDecoder(model, batch, uniforms=rng.integers(0, 1 << 24, 1 << 16).astype(np.float64) / (1 << 24),
+                       hcap=max(512, prompt + gen + 16))
+    dec.capture(torch.cuda.Stream())
+    prompts = rng.integers(0, sh.vocab, (batch, prompt))
+    dec.run(prompts, 4)                                  # warm-up
+    dec.reset()
+    toks, t = dec.run(prompts, gen)
+    ctx.synchronize()
+    out = {"batch": batch, "tok_per_s": round(batch * gen / t, 1), "ms_per_step": round(1e3 * t / gen, 3),
+           "load_s": round(t_load, 1), "first_tokens_seq0": toks[:8, 0].tolist()}
+    del dec, model
+    torch.cuda.empty_cache()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--layers", type=int, default=48)
+    ap.add_argument("--shape", choices=["30b", "235b"], default="30b")
+    ap.add_argument("--layers", type=int, default=0, help="0: the shape's own layer count")
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--ctx", type=int, default=4096, help="KV ring positions per sequence")
     ap.add_argument("--prompt", type=int, default=45)
     ap.add_argument("--gen", type=int, default=256)
     args = ap.parse_args()
-    sh = Shape(layers=args.layers)
+    sh = Shape.qwen3_235b() if args.shape == "235b" else Shape()
+    if args.layers:
+        sh.layers = args.layers
+    sh.attn_ctx = args.ctx
+    name = "Qwen3-235B-A22B" if args.shape == "235b" else "Qwen3-30B-A3B"
     ctx = S.Context(0)
+    if args.batch > 1:
+        out = run_batched(ctx, sh, args.batch, args.prompt, args.gen)
+        out["workload"] = (f"{name}-shaped decode, {sh.layers} layers, batch {args.batch}, prompt {args.prompt}, "
+                           f"{args.gen} generated per sequence (random weights)")
+        print(json.dumps(out))
+        ctx.close()
+        return
     t0 = time.time()
     model = Model(ctx, sh)
     t_load = time.time() - t0
@@ -270,14 +461,12 @@ def main():
     dec.reset()
     toks, t = dec.run(prompt, args.gen)
     ctx.synchronize()
-    attn = (2 * sh.q_dim + 2 * sh.kv_dim) * sh.d_model * 2           # q, k, v, o bf16
-    per_token_bytes = (sh.layers * (sh.top_k * S.expert_bytes(sh.fmt, sh.d_model, sh.d_ff) + attn
-                                    + sh.n_experts * sh.d_model * 2) + sh.vocab * sh.d_model * 2)
-    print(json.dumps({"workload": f"Qwen3-30B-A3B-shaped decode, {sh.layers} layers, batch 1, prompt "
+    ptb = per_token_bytes(sh)
+    print(json.dumps({"workload": f"{name}-shaped decode, {sh.layers} layers, batch 1, prompt "
                                   f"{args.prompt}, {args.gen} generated (random weights)",
                       "tok_per_s": round(args.gen / t, 2), "ms_per_token": round(1e3 * t / args.gen, 4),
-                      "load_s": round(t_load, 1), "weights_gb_per_token": round(per_token_bytes / 1e9, 3),
-                      "achieved_gbs": round(per_token_bytes * args.gen / t / 1e9, 1),
+                      "load_s": round(t_load, 1), "weights_gb_per_token": round(ptb / 1e9, 3),
+                      "achieved_gbs": round(ptb * args.gen / t / 1e9, 1),
                       "first_tokens": toks[:8]}))
     ctx.close()
 

@@ -40,6 +40,7 @@ EXPORTS = [
     "smoe_cuda_ep_export", "smoe_cuda_ep_attach", "smoe_cuda_moe_layer_ep",
     "smoe_cuda_attention_layer", "smoe_cuda_attention_layer_async", "smoe_cuda_matvec_bf16",
     "smoe_cuda_rms_norm", "smoe_cuda_embed_bf16", "smoe_cuda_rope_table", "smoe_cuda_decode_advance",
+    "smoe_cuda_gemm_bf16", "smoe_cuda_attention_batch_async", "smoe_cuda_decode_advance_batch",
 ]
 
 
@@ -166,6 +167,9 @@ def lib():
         L.smoe_cuda_embed_bf16.argtypes = [vp, vp, vp, u32, u32, vp]
         L.smoe_cuda_rope_table.argtypes = [vp, vp, vp, vp, vp, u32]
         L.smoe_cuda_decode_advance.argtypes = [vp, vp, vp, u32, vp, vp, vp, u32]
+        L.smoe_cuda_gemm_bf16.argtypes = [vp, vp, vp, vp, u32, u32, u32]
+        L.smoe_cuda_attention_batch_async.argtypes = [vp, C.POINTER(AttnLayerArgs), u32, u64, vp]
+        L.smoe_cuda_decode_advance_batch.argtypes = [vp, vp, vp, u32, vp, u32, vp, vp, u32]
         L.smoe_cuda_ep_attach.argtypes = [vp, i32, i32, C.POINTER(EpHandle)]
         L.smoe_cuda_moe_layer_ep.argtypes = [vp, C.POINTER(MoeLayer), u32, u32, vp, i32, u32, u32, i32,
                                              vp, i32, vp, vp]
@@ -345,6 +349,18 @@ class Context:
     def decode_advance(self, row, history, hcap, token, pos, u_seq=None, u_len=0):
         check(self.L.smoe_cuda_decode_advance(self.h, ptr(row), ptr(history), hcap, ptr(token), ptr(pos),
                                               ptr(u_seq), u_len), "decode_advance")
+
+    # ---- batched decode (sequences at one shared position)
+    def gemm_bf16(self, w, x, y, rows, cols, batch):
+        check(self.L.smoe_cuda_gemm_bf16(self.h, ptr(w), ptr(x), ptr(y), rows, cols, batch), "gemm_bf16")
+
+    def attention_batch(self, args: AttnLayerArgs, batch, kv_seq_stride, pos):
+        check(self.L.smoe_cuda_attention_batch_async(self.h, C.byref(args), batch, kv_seq_stride, ptr(pos)),
+              "attention_batch")
+
+    def decode_advance_batch(self, rows, history, hcap, tokens, batch, pos, u_seq=None, u_len=0):
+        check(self.L.smoe_cuda_decode_advance_batch(self.h, ptr(rows), ptr(history), hcap, ptr(tokens), batch,
+                                                    ptr(pos), ptr(u_seq), u_len), "decode_advance_batch")
 
     def sample(self, logits, vocab, batch, rows, history, history_stride, tokens):
         check(self.L.smoe_cuda_sample(self.h, ptr(logits), vocab, batch, ptr(rows), ptr(history),
