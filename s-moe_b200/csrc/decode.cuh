@@ -406,6 +406,193 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(AttnArgs a) {
     if (tid == 0) a.cnt[h] = 0u;                  // ready for the next launch
 }
 
+// Batched decode attention, one CTA per (KV head, sequence): the ring of a
+// KV head is read once for all G = num_heads / num_kv_heads query heads of
+// its group (the per-query-head kernel above reads it G times). Same math
+// as k_attn_decode (decode.cpp:159-226), one split per head:
+//  1. warp w takes heads w, w + 8, ... (and the KV head's K last): QK
+//     RMSNorm + half-split RoPE with a lane holding dims lane + 32 j (a RoPE
+//     pair d, d + hd/2 stays in one lane: hd % 64 == 0); normed + roped Q
+//     to qbuf, K and V to the ring slot;
+//  2. scores: 4 lanes per position (hd / 4 dims each, all loads issued
+//     before the dots), G dot products per K row, reduced over the 4 lanes;
+//  3. softmax per head (warp per head): max, exp, sum;
+//  4. out[g][d] = sum_i p[g][i] V[i][d] / sum_g: a warp takes every 8th
+//     position, a lane 4 dims of the row (one float4), G float4
+//     accumulators, 4 rows in flight; the warps' partials added through
+//     shared memory.
+// head_dim == 128. Dynamic shared memory (floats): q [G hd], k [hd], v [hd],
+// scores [G ctx], warp partials [8][G hd].
+constexpr int kAttnGqaMaxG = 16;
+__global__ void __launch_bounds__(kAttnThreads) k_attn_batch_gqa(AttnArgs a) {
+    extern __shared__ __align__(16) float gqa_sm[];
+    const uint32_t hd = a.head_dim, G = a.num_heads / a.num_kv_heads, kvh = blockIdx.x;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = kAttnThreads / 32;
+    float* qs = gqa_sm;
+    float* ks = qs + G * hd;
+    float* vs = ks + hd;
+    float* sc = vs + hd;
+    float* gp = sc + size_t(G) * a.attn_ctx;
+    pdl_trigger();
+    pdl_wait();
+    uint32_t slot, valid;
+    attn_slot_valid(a, slot, valid);
+    const size_t z = blockIdx.y;
+    const float* q = a.q + z * a.q_dim + size_t(kvh) * G * hd;
+    float* k_cache = a.k_cache + z * a.kv_seq_stride;
+    float* v_cache = a.v_cache + z * a.kv_seq_stride;
+    // 1. norm + RoPE: rows 0..G-1 are the query heads, row G the K head
+    const uint32_t per_lane = hd / 32, half = hd / 2;
+    for (uint32_t r = warp; r <= G; r += nw) {
+        const float* src = r < G ? q + size_t(r) * hd : a.k + z * a.kv_dim + size_t(kvh) * hd;
+        const uint16_t* nw_ = r < G ? a.q_norm_w : a.k_norm_w;
+        float v[8];
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (uint32_t(j) < per_lane) {
+                v[j] = src[lane + 32 * j];
+                ss = fmaf(v[j], v[j], ss);
+            }
+        if (nw_) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            const float inv = 1.0f / sqrtf(ss / float(hd) + 1e-6f);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (uint32_t(j) < per_lane) v[j] = (v[j] * inv) * bf16_bits_to_f32(nw_[lane + 32 * j]);
+        }
+        const uint32_t jh = per_lane / 2;                   // dims lane + 32 j, j < jh, are the first half
+        float o[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (uint32_t(j) < per_lane) {
+                const uint32_t t = lane + 32 * j;
+                const uint32_t d = t < half ? t : t - half;
+                o[j] = uint32_t(j) < jh ? v[j] * a.rope_cos[d] - v[j + jh] * a.rope_sin[d]
+                                        : v[j - jh] * a.rope_sin[d] + v[j] * a.rope_cos[d];
+            }
+        float* dst = r < G ? qs + size_t(r) * hd : ks;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (uint32_t(j) < per_lane) dst[lane + 32 * j] = o[j];
+        if (r < G) {
+            float* qb = a.qbuf + z * a.q_dim + (size_t(kvh) * G + r) * hd;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (uint32_t(j) < per_lane) qb[lane + 32 * j] = o[j];
+        }
+    }
+    for (uint32_t i = tid; i < hd; i += blockDim.x) vs[i] = a.v[z * a.kv_dim + size_t(kvh) * hd + i];
+    __syncthreads();
+    for (uint32_t i = tid; i < hd; i += blockDim.x) {
+        k_cache[size_t(slot) * a.kv_dim + size_t(kvh) * hd + i] = ks[i];
+        v_cache[size_t(slot) * a.kv_dim + size_t(kvh) * hd + i] = vs[i];
+    }
+    // 2. scores: position i (0 = this step) at sc[g * ctx + i]
+    const uint32_t sub = lane & 3, q4 = hd / 16;                  // float4s per lane and position
+    for (uint32_t base = warp * 8; base < valid; base += nw * 8) {
+        const uint32_t i = base + (lane >> 2);
+        float4 kk[16];
+        if (i < valid) {
+            const float4* kr = i == 0 ? reinterpret_cast<const float4*>(ks) + sub * q4
+                                      : reinterpret_cast<const float4*>(
+                                            k_cache + size_t((slot + a.attn_ctx - i) % a.attn_ctx) * a.kv_dim +
+                                            size_t(kvh) * hd) + sub * q4;
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                if (j < int(q4)) kk[j] = kr[j];
+        }
+        for (uint32_t g = 0; g < G; ++g) {
+            const float4* qv = reinterpret_cast<const float4*>(qs + size_t(g) * hd) + sub * q4;
+            float s = 0.f;
+            if (i < valid) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    if (j < int(q4)) {
+                        const float4 qq = qv[j];
+                        s = fmaf(qq.x, kk[j].x, s);
+                        s = fmaf(qq.y, kk[j].y, s);
+                        s = fmaf(qq.z, kk[j].z, s);
+                        s = fmaf(qq.w, kk[j].w, s);
+                    }
+            }
+            s += __shfl_xor_sync(0xffffffffu, s, 1);
+            s += __shfl_xor_sync(0xffffffffu, s, 2);
+            if (sub == 0 && i < valid) sc[size_t(g) * a.attn_ctx + i] = s * a.scale;
+        }
+    }
+    __syncthreads();
+    // 3. softmax per head (a warp per head), the sums to shared memory
+    __shared__ float sums[kAttnGqaMaxG];
+    for (uint32_t g = warp; g < G; g += nw) {
+        float* sg = sc + size_t(g) * a.attn_ctx;
+        float m = -INFINITY;
+        for (uint32_t i = lane; i < valid; i += 32) m = fmaxf(m, sg[i]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        float sum = 0.f;
+        for (uint32_t i = lane; i < valid; i += 32) {
+            const float e = expf(sg[i] - m);
+            sg[i] = e;
+            sum += e;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (lane == 0) sums[g] = sum;
+    }
+    __syncthreads();
+    // 4. weighted V sum: warp w takes positions w, w + 8, ..., a lane the
+    //    float4 of dims 4 lane.. of each V row (hd == 128), 4 rows in flight;
+    //    the 8 warps' partials are added through shared memory
+    float4 acc[kAttnGqaMaxG];
+#pragma unroll
+    for (int g = 0; g < kAttnGqaMaxG; ++g) acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4* vb = reinterpret_cast<const float4*>(v_cache + size_t(kvh) * hd) + lane;
+    const float4 vnew = reinterpret_cast<const float4*>(vs)[lane];
+    for (uint32_t i = warp; i < valid; i += 4 * nw) {
+        float4 vv[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const uint32_t p = i + u * nw;
+            vv[u] = p == 0 ? vnew
+                  : p < valid ? vb[size_t((slot + a.attn_ctx - p) % a.attn_ctx) * (a.kv_dim / 4)]
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const uint32_t p = i + u * nw;
+            if (p < valid)
+#pragma unroll
+                for (int g = 0; g < kAttnGqaMaxG; ++g)
+                    if (uint32_t(g) < G) {
+                        const float w = sc[size_t(g) * a.attn_ctx + p];
+                        acc[g].x = fmaf(w, vv[u].x, acc[g].x);
+                        acc[g].y = fmaf(w, vv[u].y, acc[g].y);
+                        acc[g].z = fmaf(w, vv[u].z, acc[g].z);
+                        acc[g].w = fmaf(w, vv[u].w, acc[g].w);
+                    }
+        }
+    }
+    float4* gp4 = reinterpret_cast<float4*>(gp);                 // [8 warps][G][32 float4]
+#pragma unroll
+    for (int g = 0; g < kAttnGqaMaxG; ++g)
+        if (uint32_t(g) < G) gp4[(size_t(warp) * G + g) * 32 + lane] = acc[g];
+    __syncthreads();
+    for (uint32_t o = tid; o < G * 32; o += blockDim.x) {
+        const uint32_t g = o / 32;
+        float4 r = gp4[o];
+        for (int w = 1; w < nw; ++w) {
+            const float4 q = gp4[size_t(w) * G * 32 + o];
+            r.x += q.x; r.y += q.y; r.z += q.z; r.w += q.w;
+        }
+        const float sum = sums[g];
+        const float inv = sum > 0.f ? 1.0f / sum : 0.f;
+        r.x *= inv; r.y *= inv; r.z *= inv; r.w *= inv;
+        reinterpret_cast<float4*>(a.attn_out + z * a.q_dim + size_t(kvh) * G * hd)[o] = r;
+    }
+}
+
 // End of a decode step on the device: append this step's token to the
 // history of sampler row 0, advance the position, and set the next uniform
 // draw (u_seq[pos % u_len], when given). One thread.

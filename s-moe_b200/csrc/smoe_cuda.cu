@@ -938,6 +938,22 @@ namespace {
 // Launch a trunk kernel with programmatic stream serialization: it may start
 // while its predecessor drains, and waits for it in pdl_wait().
 extern "C++" template <typename... KArgs, typename... Args>
+int pdl_launch_smem(SmoeCudaCtx* c, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, Args... args) {
+    cudaLaunchConfig_t lc{};
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.gridDim = grid;
+    lc.blockDim = block;
+    lc.dynamicSmemBytes = smem;
+    lc.stream = c->stream;
+    lc.attrs = at;
+    lc.numAttrs = 1;
+    c->dispatches += 1;
+    return cudaLaunchKernelEx(&lc, kern, KArgs(args)...) == cudaSuccess ? SMOE_OK : SMOE_ERR_CUDA;
+}
+
+extern "C++" template <typename... KArgs, typename... Args>
 int pdl_launch(SmoeCudaCtx* c, void (*kern)(KArgs...), dim3 grid, dim3 block, Args... args) {
     cudaLaunchConfig_t lc{};
     cudaLaunchAttribute at[1];
@@ -1067,26 +1083,29 @@ int smoe_cuda_attention_layer_async(SmoeCudaCtx* c, const SmoeCudaAttnLayerArgs*
     return gemv_set(c, o);
 }
 
-int smoe_cuda_gemm_bf16(SmoeCudaCtx* c, const uint16_t* w, const float* x, float* y, uint32_t rows,
-                        uint32_t cols, uint32_t batch) {
-    if (!c) { set_err("null context %s%ld", "", 0); return SMOE_ERR_ARG; }
-    if (batch == 1) return smoe_cuda_matvec_bf16(c, w, x, y, rows, cols);
-    if (!w || !x || !y || rows == 0 || cols == 0 || cols % 8 || batch == 0 || batch > c->cfg.max_batch ||
-        cols > c->cfg.max_d_model || !aligned16(w)) {
-        set_err("bad batched matvec arguments %s%ld", "", (long)batch);
+namespace {
+// X [batch x cols] fp32 -> the two bf16 planes in c->xsplit
+int split_planes(SmoeCudaCtx* c, const float* x, size_t n) {
+    const size_t blocks = (n + 1023) / 1024;
+    return pdl_launch(c, smoe::k_split_bf16, dim3(unsigned(blocks < 1184 ? blocks : 1184)), dim3(1024), x,
+                      c->xsplit, n);
+}
+
+// Y = W X over the planes already in c->xsplit (n = batch * cols).
+// cuBLAS is column-major: row-major W [rows x cols] is A = W^T (cols x rows,
+// ld cols), X [batch x cols] is B = X^T (cols x batch, ld cols) and Y [batch
+// x rows] is C = Y^T (rows x batch, ld rows); C = A^T B, hi plane then lo
+// plane accumulated.
+int gemm_planes(SmoeCudaCtx* c, const uint16_t* w, float* y, uint32_t rows, uint32_t cols, uint32_t batch) {
+    if (!w || !y || rows == 0 || !aligned16(w)) {
+        set_err("bad batched matvec operand %s%ld", "", (long)rows);
         return SMOE_ERR_ARG;
     }
-    const size_t n = size_t(batch) * cols;
-    int rc = pdl_launch(c, smoe::k_split_bf16, dim3(unsigned((n + 1023) / 1024 < 1184 ? (n + 1023) / 1024 : 1184)),
-                        dim3(1024), x, c->xsplit, n);
-    if (rc) return rc;
-    // cuBLAS is column-major: row-major W [rows x cols] is A = W^T (cols x
-    // rows, ld cols), X [batch x cols] is B = X^T (cols x batch, ld cols) and
-    // Y [batch x rows] is C = Y^T (rows x batch, ld rows); C = A^T B.
     if (cublasSetStream(c->blas, c->stream) != CUBLAS_STATUS_SUCCESS) {
         set_err("cuBLAS stream %s%ld", "", 0);
         return SMOE_ERR_CUDA;
     }
+    const size_t n = size_t(batch) * cols;
     const float one = 1.0f, zero = 0.0f;
     for (int plane = 0; plane < 2; ++plane) {
         const cublasStatus_t st = cublasGemmEx(
@@ -1102,6 +1121,24 @@ int smoe_cuda_gemm_bf16(SmoeCudaCtx* c, const uint16_t* w, const float* x, float
     return SMOE_OK;
 }
 
+bool gemm_shape_ok(const SmoeCudaCtx* c, const float* x, uint32_t cols, uint32_t batch) {
+    return x && cols && cols % 8 == 0 && batch && batch <= c->cfg.max_batch && cols <= c->cfg.max_d_model;
+}
+}  // namespace
+
+int smoe_cuda_gemm_bf16(SmoeCudaCtx* c, const uint16_t* w, const float* x, float* y, uint32_t rows,
+                        uint32_t cols, uint32_t batch) {
+    if (!c) { set_err("null context %s%ld", "", 0); return SMOE_ERR_ARG; }
+    if (batch == 1) return smoe_cuda_matvec_bf16(c, w, x, y, rows, cols);
+    if (!w || !y || rows == 0 || !aligned16(w) || !gemm_shape_ok(c, x, cols, batch)) {
+        set_err("bad batched matvec arguments %s%ld", "", (long)batch);
+        return SMOE_ERR_ARG;
+    }
+    int rc = split_planes(c, x, size_t(batch) * cols);
+    if (rc) return rc;
+    return gemm_planes(c, w, y, rows, cols, batch);
+}
+
 int smoe_cuda_attention_batch_async(SmoeCudaCtx* c, const SmoeCudaAttnLayerArgs* a, uint32_t batch,
                                     uint64_t kv_seq_stride, const uint32_t* pos) {
     if (!c || !a || !pos || batch == 0 || batch > 65535 || !a->w_q || !a->w_k || !a->w_v || !a->w_o ||
@@ -1115,9 +1152,20 @@ int smoe_cuda_attention_batch_async(SmoeCudaCtx* c, const SmoeCudaAttnLayerArgs*
         return SMOE_ERR_ARG;
     }
     int rc;
-    if ((rc = smoe_cuda_gemm_bf16(c, a->w_q, a->normed_in, a->qbuf, a->q_dim, a->d_model, batch))) return rc;
-    if ((rc = smoe_cuda_gemm_bf16(c, a->w_k, a->normed_in, a->kbuf, a->kv_dim, a->d_model, batch))) return rc;
-    if ((rc = smoe_cuda_gemm_bf16(c, a->w_v, a->normed_in, a->vbuf, a->kv_dim, a->d_model, batch))) return rc;
+    if (batch == 1) {
+        if ((rc = smoe_cuda_matvec_bf16(c, a->w_q, a->normed_in, a->qbuf, a->q_dim, a->d_model))) return rc;
+        if ((rc = smoe_cuda_matvec_bf16(c, a->w_k, a->normed_in, a->kbuf, a->kv_dim, a->d_model))) return rc;
+        if ((rc = smoe_cuda_matvec_bf16(c, a->w_v, a->normed_in, a->vbuf, a->kv_dim, a->d_model))) return rc;
+    } else {                             // the normed rows split into planes once for Q, K and V
+        if (!gemm_shape_ok(c, a->normed_in, a->d_model, batch) || !gemm_shape_ok(c, a->attn_out, a->q_dim, batch)) {
+            set_err("batched attention: batch or width above the context's limits %s%ld", "", (long)batch);
+            return SMOE_ERR_ARG;
+        }
+        if ((rc = split_planes(c, a->normed_in, size_t(batch) * a->d_model))) return rc;
+        if ((rc = gemm_planes(c, a->w_q, a->qbuf, a->q_dim, a->d_model, batch))) return rc;
+        if ((rc = gemm_planes(c, a->w_k, a->kbuf, a->kv_dim, a->d_model, batch))) return rc;
+        if ((rc = gemm_planes(c, a->w_v, a->vbuf, a->kv_dim, a->d_model, batch))) return rc;
+    }
     smoe::AttnArgs t{};
     t.q = a->qbuf; t.k = a->kbuf; t.v = a->vbuf;
     t.q_norm_w = a->q_norm_w; t.k_norm_w = a->k_norm_w;
@@ -1133,9 +1181,22 @@ int smoe_cuda_attention_batch_async(SmoeCudaCtx* c, const SmoeCudaAttnLayerArgs*
     t.part = c->attn_part;
     t.cnt = c->attn_cnt;
     t.kv_seq_stride = size_t(kv_seq_stride);
-    // batch x heads CTAs cover the GPU: one split per head (no partials)
-    const uint32_t splits = batch > 1 ? 1u : std::min<uint32_t>(smoe::kAttnSplits, (a->attn_ctx + 31) / 32);
-    rc = pdl_launch(c, smoe::k_attn_decode, dim3(a->num_heads, splits, batch), dim3(smoe::kAttnThreads), t);
+    // batch x heads CTAs cover the GPU: one split per head (no partials).
+    // Head groups whose ring is shared by several query heads take the
+    // GQA kernel (each ring read once per group) when its tiles fit.
+    const uint32_t G = a->num_heads / a->num_kv_heads;
+    const size_t gqa_smem = (size_t(G + 2) * a->head_dim + size_t(G) * a->attn_ctx +
+                             size_t(smoe::kAttnThreads / 32) * G * a->head_dim) * 4;
+    if (batch > 1 && a->head_dim == 128 && (size_t(G) * a->attn_ctx) % 4 == 0 &&   // float4 partials aligned
+        G <= uint32_t(smoe::kAttnGqaMaxG) && gqa_smem <= c->smem_optin && aligned16(a->k_cache) &&
+        aligned16(a->v_cache) && aligned16(a->qbuf) && aligned16(a->attn_out) && kv_seq_stride % 4 == 0) {
+        if ((rc = prep_kernel(c, smoe::k_attn_batch_gqa, gqa_smem))) return rc;
+        rc = pdl_launch_smem(c, smoe::k_attn_batch_gqa, dim3(a->num_kv_heads, batch), dim3(smoe::kAttnThreads),
+                             gqa_smem, t);
+    } else {
+        const uint32_t splits = batch > 1 ? 1u : std::min<uint32_t>(smoe::kAttnSplits, (a->attn_ctx + 31) / 32);
+        rc = pdl_launch(c, smoe::k_attn_decode, dim3(a->num_heads, splits, batch), dim3(smoe::kAttnThreads), t);
+    }
     if (rc) return rc;
     return smoe_cuda_gemm_bf16(c, a->w_o, a->attn_out, a->o_out, a->d_model, a->q_dim, batch);
 }

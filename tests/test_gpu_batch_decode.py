@@ -23,8 +23,10 @@ KERNEL_TOL = 5e-5
 LOGIT_TOL = 1e-3
 
 
-def small_shape(ctx_len=64):
+def small_shape(ctx_len=64, heads="30b"):
     from decode import Shape
+    if heads == "235b":                  # 64 query heads over 4 KV heads, d_model 4096
+        return Shape.qwen3_235b(layers=1, n_experts=16, top_k=4, vocab=512, attn_ctx=ctx_len)
     return Shape(layers=2, n_experts=16, top_k=4, vocab=512, attn_ctx=ctx_len)
 
 
@@ -44,12 +46,15 @@ def test_gemm_bf16_batch(ctx, batch, rows, cols):
         assert rel_err(got[b], ref[b]) < KERNEL_TOL
 
 
-@pytest.mark.parametrize("ctx_len,pos", [(64, 5), (64, 100), (256, 200)])
-def test_attention_batch(ctx, ctx_len, pos):
+@pytest.mark.parametrize("ctx_len,pos,heads", [(64, 5, "30b"), (64, 100, "30b"), (256, 200, "30b"), (4096, 300, "30b"),
+                                               (64, 100, "235b")])
+def test_attention_batch(ctx, ctx_len, pos, heads):
     """Three sequences with different pre-filled rings at one position (with
-    and without the ring wrapping): each against the restatement alone."""
+    and without the ring wrapping), 8 and 16 query heads per KV head (the
+    kernel reads each KV head's ring once for its group): each sequence
+    against the restatement alone."""
     B = 3
-    sh = small_shape(ctx_len)
+    sh = small_shape(ctx_len, heads)
     W = make_weights(sh, 5)
     ref = RefDecoder(W, sh)
     rng = np.random.default_rng(pos)
