@@ -430,11 +430,11 @@ def run_ours(args, rank, world, local):
             line["cpu_baseline"] = cpu["all"]
             line["cpu_baseline_1core"] = cpu["one"]
         if world == 1 and not args.no_extra:
-            line["config3_layer_1gpu"] = config3_leg(ctx, stream, args)
-            line["sampler"] = sampler_leg(ctx, stream)
-            line["decode_30b"] = decode_leg(ctx)
-            line["batch256"] = batch_leg(ctx, stream)
-            for key, fn in (("decode_b256", lambda: batched_decode_leg(ctx, "30b", 256, 45, 128)),
+            for key, fn in (("config3_layer_1gpu", lambda: config3_leg(ctx, stream, args)),
+                            ("sampler", lambda: sampler_leg(ctx, stream)),
+                            ("decode_30b", lambda: decode_leg(ctx)),
+                            ("batch256", lambda: batch_leg(ctx, stream)),
+                            ("decode_b256", lambda: batched_decode_leg(ctx, "30b", 256, 45, 128)),
                             ("decode_235b", lambda: decode_235b_leg(ctx)),
                             ("decode_235b_b32", lambda: batched_decode_leg(ctx, "235b", 32, 45, 32))):
                 try:                    # a side leg that fails leaves the headline line intact
@@ -612,6 +612,7 @@ def decode_leg(ctx, prompt=45, gen=256):
                        f"{gen} generated (random weights)", "tok_per_s": round(gen / t, 2),
            "ms_per_token": round(1e3 * t / gen, 4), "weight_bytes_per_token": per_tok,
            "achieved_gbs": round(per_tok * gen / t / 1e9, 1)}
+    out["prefill"] = prefill_timing(dec, pr)
     del dec, model
     torch.cuda.empty_cache()
     return out
@@ -633,6 +634,31 @@ def batched_decode_leg(ctx, shape, batch, prompt, gen):
     return out
 
 
+def prefill_timing(dec, prompt, gen=8):
+    """Time to first token with the layer-major prefill (the prompt's first
+    P - 1 tokens in one chunk, MoE by the layer kernel 4 tokens per launch,
+    captured as one graph), then the step on the last prompt token; against
+    feeding the prompt one token per step-graph replay."""
+    dec.run_prefill(prompt, gen)                         # capture + warm
+    _, ttft, _ = dec.run_prefill(prompt, gen)
+    dec.reset()
+    import torch
+    with torch.cuda.stream(dec.stream):
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(dec.stream)
+        for tok in prompt:
+            dec.token.fill_(int(tok))
+            dec.graph.replay()
+        e1.record(dec.stream)
+        torch.cuda.synchronize()
+    serial = e0.elapsed_time(e1) / 1e3
+    dec.reset()
+    return {"prompt_tokens": len(prompt), "ttft_ms": round(ttft * 1e3, 3),
+            "ttft_token_by_token_ms": round(serial * 1e3, 3),
+            "prefill_tok_per_s": round(len(prompt) / ttft, 1)}
+
+
 def decode_235b_leg(ctx, prompt=45, gen=64):
     """Config 3 at batch 1 on one GPU: the Qwen3-235B-A22B shape (94 layers,
     ~128 GB of tiled Q4 experts resident), one CUDA graph per token."""
@@ -652,10 +678,11 @@ def decode_235b_leg(ctx, prompt=45, gen=64):
     _, t = dec.run(pr, gen)
     ctx.synchronize()
     ptb = DEC.per_token_bytes(sh)
+    pf = prefill_timing(dec, pr)
     out = {"workload": f"config3 shape: Qwen3-235B-A22B decode, 94 layers, batch 1, 1 GPU, prompt {prompt}, "
                        f"{gen} generated (random weights)", "tok_per_s": round(gen / t, 2),
            "ms_per_token": round(1e3 * t / gen, 4), "weight_bytes_per_token": ptb,
-           "achieved_gbs": round(ptb * gen / t / 1e9, 1), "load_s": round(load, 1)}
+           "achieved_gbs": round(ptb * gen / t / 1e9, 1), "load_s": round(load, 1), "prefill": pf}
     del dec, model
     torch.cuda.empty_cache()
     return out

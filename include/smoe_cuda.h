@@ -392,6 +392,28 @@ int smoe_cuda_gemm_bf16(SmoeCudaCtx* ctx, const uint16_t* w, const float* x, flo
 int smoe_cuda_attention_batch_async(SmoeCudaCtx* ctx, const SmoeCudaAttnLayerArgs* args,
                                     uint32_t batch, uint64_t kv_seq_stride, const uint32_t* pos);
 
+/* ---- Layer-major prefill (prefill.cpp:82-465): the prompt's tokens, all
+ * but the last, go through each layer together, in chunks; the last prompt
+ * token then takes the normal decode step, which samples. */
+
+/* RoPE tables of n consecutive positions *pos + t (decode.cpp:113-118 per
+ * token): cos_out / sin_out [n x half]. */
+int smoe_cuda_rope_tables(SmoeCudaCtx* ctx, const uint32_t* pos, uint32_t n, const float* inv_freq,
+                          float* cos_out, float* sin_out, uint32_t half);
+
+/* The attention layer for a chunk of n_tokens of ONE sequence at positions
+ * *pos .. *pos + n_tokens - 1 (prefill.cpp:131-268): Q/K/V of all tokens,
+ * QK RMSNorm + RoPE at each token's position (rope_cos / rope_sin: [n_tokens
+ * x head_dim/2], smoe_cuda_rope_tables), every token's K/V appended to the
+ * ring, then causal attention (token t attends to the newest min(*pos + t +
+ * 1, attn_ctx) positions), O projection. Buffers as the batched entry
+ * ([n_tokens x width]); one ring (k_cache / v_cache). n_tokens <= max_batch
+ * and <= attn_ctx; head_dim 128 (else SMOE_ERR_UNSUPPORTED). As in the
+ * reference, a chunk that wraps the ring overwrites positions its earlier
+ * tokens would still see. slot/valid ignored. Asynchronous. */
+int smoe_cuda_attention_prefill_async(SmoeCudaCtx* ctx, const SmoeCudaAttnLayerArgs* args,
+                                      uint32_t n_tokens, const uint32_t* pos);
+
 /* End of a batched decode step: tokens[b] joins rows[b]'s history (history
  * [batch x hcap]), ++*pos, and rows[b].u = u_seq[(*pos * batch + b) % u_len]
  * when u_seq is given. batch <= 1024. */

@@ -216,6 +216,9 @@ struct AttnArgs {
     size_t kv_seq_stride;                // batched decode (gridDim.z sequences): floats between the
                                          // rings of consecutive sequences; q/k/v/qbuf/attn_out are
                                          // [sequences][q_dim or kv_dim] (one split per head then)
+    uint32_t prefill;                    // k_attn_batch_gqa: row z is token z of one sequence at
+                                         // position *pos + z, its K/V already in the ring
+                                         // (k_prefill_kv), RoPE tables [tokens][head_dim/2]
 };
 
 SMOE_DEVINL void attn_slot_valid(const AttnArgs& a, uint32_t& slot, uint32_t& valid) {
@@ -435,15 +438,24 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_batch_gqa(AttnArgs a) {
     float* gp = sc + size_t(G) * a.attn_ctx;
     pdl_trigger();
     pdl_wait();
-    uint32_t slot, valid;
-    attn_slot_valid(a, slot, valid);
     const size_t z = blockIdx.y;
+    const bool pf = a.prefill != 0;
+    uint32_t slot, valid;
+    if (pf) {                            // token z of the chunk (prefill.cpp:216-220)
+        const uint32_t p = *a.pos + uint32_t(z);
+        slot = p % a.attn_ctx;
+        valid = p + 1 < a.attn_ctx ? p + 1 : a.attn_ctx;
+        a.rope_cos += z * (hd / 2);
+        a.rope_sin += z * (hd / 2);
+    } else {
+        attn_slot_valid(a, slot, valid);
+    }
     const float* q = a.q + z * a.q_dim + size_t(kvh) * G * hd;
     float* k_cache = a.k_cache + z * a.kv_seq_stride;
     float* v_cache = a.v_cache + z * a.kv_seq_stride;
     // 1. norm + RoPE: rows 0..G-1 are the query heads, row G the K head
     const uint32_t per_lane = hd / 32, half = hd / 2;
-    for (uint32_t r = warp; r <= G; r += nw) {
+    for (uint32_t r = warp; r < G + (pf ? 0u : 1u); r += nw) {
         const float* src = r < G ? q + size_t(r) * hd : a.k + z * a.kv_dim + size_t(kvh) * hd;
         const uint16_t* nw_ = r < G ? a.q_norm_w : a.k_norm_w;
         float v[8];
@@ -483,22 +495,24 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_batch_gqa(AttnArgs a) {
                 if (uint32_t(j) < per_lane) qb[lane + 32 * j] = o[j];
         }
     }
-    for (uint32_t i = tid; i < hd; i += blockDim.x) vs[i] = a.v[z * a.kv_dim + size_t(kvh) * hd + i];
+    if (!pf)
+        for (uint32_t i = tid; i < hd; i += blockDim.x) vs[i] = a.v[z * a.kv_dim + size_t(kvh) * hd + i];
     __syncthreads();
-    for (uint32_t i = tid; i < hd; i += blockDim.x) {
-        k_cache[size_t(slot) * a.kv_dim + size_t(kvh) * hd + i] = ks[i];
-        v_cache[size_t(slot) * a.kv_dim + size_t(kvh) * hd + i] = vs[i];
-    }
-    // 2. scores: position i (0 = this step) at sc[g * ctx + i]
+    if (!pf)
+        for (uint32_t i = tid; i < hd; i += blockDim.x) {
+            k_cache[size_t(slot) * a.kv_dim + size_t(kvh) * hd + i] = ks[i];
+            v_cache[size_t(slot) * a.kv_dim + size_t(kvh) * hd + i] = vs[i];
+        }
+    // 2. scores: position i (0 = this step; from the ring in prefill) at sc[g * ctx + i]
     const uint32_t sub = lane & 3, q4 = hd / 16;                  // float4s per lane and position
     for (uint32_t base = warp * 8; base < valid; base += nw * 8) {
         const uint32_t i = base + (lane >> 2);
         float4 kk[16];
         if (i < valid) {
-            const float4* kr = i == 0 ? reinterpret_cast<const float4*>(ks) + sub * q4
-                                      : reinterpret_cast<const float4*>(
-                                            k_cache + size_t((slot + a.attn_ctx - i) % a.attn_ctx) * a.kv_dim +
-                                            size_t(kvh) * hd) + sub * q4;
+            const float4* kr = i == 0 && !pf ? reinterpret_cast<const float4*>(ks) + sub * q4
+                                             : reinterpret_cast<const float4*>(
+                                                   k_cache + size_t((slot + a.attn_ctx - i) % a.attn_ctx) * a.kv_dim +
+                                                   size_t(kvh) * hd) + sub * q4;
 #pragma unroll
             for (int j = 0; j < 16; ++j)
                 if (j < int(q4)) kk[j] = kr[j];
@@ -549,13 +563,13 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_batch_gqa(AttnArgs a) {
 #pragma unroll
     for (int g = 0; g < kAttnGqaMaxG; ++g) acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
     const float4* vb = reinterpret_cast<const float4*>(v_cache + size_t(kvh) * hd) + lane;
-    const float4 vnew = reinterpret_cast<const float4*>(vs)[lane];
+    const float4 vnew = pf ? make_float4(0.f, 0.f, 0.f, 0.f) : reinterpret_cast<const float4*>(vs)[lane];
     for (uint32_t i = warp; i < valid; i += 4 * nw) {
         float4 vv[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
             const uint32_t p = i + u * nw;
-            vv[u] = p == 0 ? vnew
+            vv[u] = p == 0 && !pf ? vnew
                   : p < valid ? vb[size_t((slot + a.attn_ctx - p) % a.attn_ctx) * (a.kv_dim / 4)]
                               : make_float4(0.f, 0.f, 0.f, 0.f);
         }
@@ -615,6 +629,63 @@ __global__ void k_decode_advance(SamplerRowDevMut* row, uint32_t* history, uint3
     const uint32_t p = *pos + 1;
     *pos = p;
     if (u_seq && u_len) row->u = u_seq[p % u_len];
+}
+
+// Prefill (prefill.cpp:165-203): token t of a chunk at position *pos + t:
+// K RMSNorm + half-split RoPE (table row t) of every KV head, K and V to the
+// ring slot (*pos + t) % ctx, before any token of the chunk attends (so
+// token t sees tokens 0..t of the chunk through the ring, as the reference's
+// causal loop does). Grid (num_kv_heads, tokens), one warp; head_dim % 64 ==
+// 0, <= 256.
+__global__ void k_prefill_kv(const float* k, const float* v, const uint16_t* k_norm_w, const float* rope_cos,
+                             const float* rope_sin, float* k_cache, float* v_cache, uint32_t kv_dim,
+                             uint32_t hd, uint32_t attn_ctx, const uint32_t* pos) {
+    pdl_trigger();
+    pdl_wait();
+    const uint32_t kvh = blockIdx.x, t = blockIdx.y, lane = threadIdx.x;
+    const uint32_t slot = (*pos + t) % attn_ctx, per_lane = hd / 32, jh = per_lane / 2, half = hd / 2;
+    const float* src = k + size_t(t) * kv_dim + size_t(kvh) * hd;
+    const float* cs = rope_cos + size_t(t) * half;
+    const float* sn = rope_sin + size_t(t) * half;
+    float x[8];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+        if (uint32_t(j) < per_lane) {
+            x[j] = src[lane + 32 * j];
+            ss = fmaf(x[j], x[j], ss);
+        }
+    if (k_norm_w) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float inv = 1.0f / sqrtf(ss / float(hd) + 1e-6f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (uint32_t(j) < per_lane) x[j] = (x[j] * inv) * bf16_bits_to_f32(k_norm_w[lane + 32 * j]);
+    }
+    float* kd = k_cache + size_t(slot) * kv_dim + size_t(kvh) * hd;
+    float* vd = v_cache + size_t(slot) * kv_dim + size_t(kvh) * hd;
+    const float* vs = v + size_t(t) * kv_dim + size_t(kvh) * hd;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+        if (uint32_t(j) < per_lane) {
+            const uint32_t i = lane + 32 * j, d = i < half ? i : i - half;
+            kd[i] = uint32_t(j) < jh ? x[j] * cs[d] - x[j + jh] * sn[d] : x[j - jh] * sn[d] + x[j] * cs[d];
+            vd[i] = vs[i];
+        }
+}
+
+// RoPE tables of `n` consecutive positions *pos + t (decode.cpp:113-118 per
+// token): cs / sn [n][half]. Grid (ceil(half / 128), n).
+__global__ void k_rope_tables(const uint32_t* pos, const float* inv_freq, float* cs, float* sn, uint32_t half) {
+    pdl_trigger();
+    pdl_wait();
+    const uint32_t i = threadIdx.x + blockIdx.x * blockDim.x, t = blockIdx.y;
+    if (i < half) {
+        const float a = float(*pos + t) * inv_freq[i];
+        cs[size_t(t) * half + i] = cosf(a);
+        sn[size_t(t) * half + i] = sinf(a);
+    }
 }
 
 // Batched decode (one position shared by `batch` sequences): sequence b's

@@ -1201,6 +1201,76 @@ int smoe_cuda_attention_batch_async(SmoeCudaCtx* c, const SmoeCudaAttnLayerArgs*
     return smoe_cuda_gemm_bf16(c, a->w_o, a->attn_out, a->o_out, a->d_model, a->q_dim, batch);
 }
 
+int smoe_cuda_rope_tables(SmoeCudaCtx* c, const uint32_t* pos, uint32_t n, const float* inv_freq, float* cos_out,
+                          float* sin_out, uint32_t half) {
+    if (!c || !pos || !inv_freq || !cos_out || !sin_out || half == 0 || n == 0 || n > 65535) {
+        set_err("bad rope table arguments %s%ld", "", (long)n);
+        return SMOE_ERR_ARG;
+    }
+    return pdl_launch(c, smoe::k_rope_tables, dim3((half + 127) / 128, n), dim3(128), pos, inv_freq, cos_out,
+                      sin_out, half);
+}
+
+int smoe_cuda_attention_prefill_async(SmoeCudaCtx* c, const SmoeCudaAttnLayerArgs* a, uint32_t n_tokens,
+                                      const uint32_t* pos) {
+    const uint32_t G = a && a->num_kv_heads ? a->num_heads / a->num_kv_heads : 0;
+    const size_t smem = a ? (size_t(G + 2) * a->head_dim + size_t(G) * a->attn_ctx +
+                             size_t(smoe::kAttnThreads / 32) * G * a->head_dim) * 4 : 0;
+    if (!c || !a || !pos || n_tokens == 0 || !a->w_q || !a->w_k || !a->w_v || !a->w_o || !a->rope_cos ||
+        !a->rope_sin || !a->normed_in || !a->qbuf || !a->kbuf || !a->vbuf || !a->k_cache || !a->v_cache ||
+        !a->attn_out || !a->o_out || a->num_kv_heads == 0 || a->num_heads % a->num_kv_heads ||
+        a->q_dim != a->num_heads * a->head_dim || a->kv_dim != a->num_kv_heads * a->head_dim ||
+        a->attn_ctx == 0 || a->attn_ctx > smoe::kAttnMaxCtx || n_tokens > a->attn_ctx) {
+        set_err("bad prefill attention arguments %s%ld", "", (long)n_tokens);
+        return SMOE_ERR_ARG;
+    }
+    if (a->head_dim != 128 || G > uint32_t(smoe::kAttnGqaMaxG) || (size_t(G) * a->attn_ctx) % 4 ||
+        smem > c->smem_optin || !aligned16(a->k_cache) || !aligned16(a->v_cache) || !aligned16(a->qbuf) ||
+        !aligned16(a->attn_out)) {
+        set_err("prefill attention needs head_dim 128, <= 16 query heads per KV head and aligned rings %s%ld", "",
+                (long)a->head_dim);
+        return SMOE_ERR_UNSUPPORTED;
+    }
+    int rc;
+    if (n_tokens == 1) {
+        if ((rc = smoe_cuda_matvec_bf16(c, a->w_q, a->normed_in, a->qbuf, a->q_dim, a->d_model))) return rc;
+        if ((rc = smoe_cuda_matvec_bf16(c, a->w_k, a->normed_in, a->kbuf, a->kv_dim, a->d_model))) return rc;
+        if ((rc = smoe_cuda_matvec_bf16(c, a->w_v, a->normed_in, a->vbuf, a->kv_dim, a->d_model))) return rc;
+    } else {
+        if (!gemm_shape_ok(c, a->normed_in, a->d_model, n_tokens) || !gemm_shape_ok(c, a->attn_out, a->q_dim, n_tokens)) {
+            set_err("prefill chunk or width above the context's limits %s%ld", "", (long)n_tokens);
+            return SMOE_ERR_ARG;
+        }
+        if ((rc = split_planes(c, a->normed_in, size_t(n_tokens) * a->d_model))) return rc;
+        if ((rc = gemm_planes(c, a->w_q, a->qbuf, a->q_dim, a->d_model, n_tokens))) return rc;
+        if ((rc = gemm_planes(c, a->w_k, a->kbuf, a->kv_dim, a->d_model, n_tokens))) return rc;
+        if ((rc = gemm_planes(c, a->w_v, a->vbuf, a->kv_dim, a->d_model, n_tokens))) return rc;
+    }
+    rc = pdl_launch(c, smoe::k_prefill_kv, dim3(a->num_kv_heads, n_tokens), dim3(32), (const float*)a->kbuf,
+                    (const float*)a->vbuf, a->k_norm_w, a->rope_cos, a->rope_sin, a->k_cache, a->v_cache, a->kv_dim,
+                    a->head_dim, a->attn_ctx, pos);
+    if (rc) return rc;
+    smoe::AttnArgs t{};
+    t.q = a->qbuf; t.k = a->kbuf; t.v = a->vbuf;
+    t.q_norm_w = a->q_norm_w; t.k_norm_w = a->k_norm_w;
+    t.rope_cos = a->rope_cos; t.rope_sin = a->rope_sin;
+    t.qbuf = a->qbuf; t.kbuf = a->kbuf; t.vbuf = a->vbuf;
+    t.k_cache = a->k_cache; t.v_cache = a->v_cache;
+    t.attn_out = a->attn_out;
+    t.q_dim = a->q_dim; t.kv_dim = a->kv_dim; t.head_dim = a->head_dim;
+    t.num_heads = a->num_heads; t.num_kv_heads = a->num_kv_heads;
+    t.attn_ctx = a->attn_ctx;
+    t.pos = pos;
+    t.scale = a->attn_scale;
+    t.kv_seq_stride = 0;                 // one sequence: every token's window is in the same ring
+    t.prefill = 1;
+    if ((rc = prep_kernel(c, smoe::k_attn_batch_gqa, smem))) return rc;
+    rc = pdl_launch_smem(c, smoe::k_attn_batch_gqa, dim3(a->num_kv_heads, n_tokens), dim3(smoe::kAttnThreads), smem,
+                         t);
+    if (rc) return rc;
+    return smoe_cuda_gemm_bf16(c, a->w_o, a->attn_out, a->o_out, a->d_model, a->q_dim, n_tokens);
+}
+
 int smoe_cuda_decode_advance_batch(SmoeCudaCtx* c, SmoeSamplerRow* rows, uint32_t* history, uint32_t hcap,
                                    const uint32_t* tokens, uint32_t batch, uint32_t* pos, const float* u_seq,
                                    uint32_t u_len) {

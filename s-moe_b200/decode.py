@@ -129,8 +129,9 @@ class Model:
             else:
                 varena, stride, off = self._random_experts(g)
             vault = S.make_layer(varena, stride, off, sh.n_experts, sh.d_model, sh.d_ff, sh.fmt, L["router"])
-            if layout == "vault":            # batched decode: the expert-grouped path reads the vault layout
+            if layout in ("vault", "both"):  # batched decode / prefill: the expert-grouped path reads it
                 L["vault"], L["vault_buf"] = vault, varena
+            if layout == "vault":
                 self.layers.append(L)
                 continue
             tb = torch.empty(sh.n_experts * tstride, dtype=torch.uint8, device=dev)
@@ -143,6 +144,7 @@ class Model:
             L["tiled_buf"] = tb
             del varena, vault
             self.layers.append(L)
+        self.layout = layout
         torch.cuda.synchronize()
 
     def _random_experts(self, g):
@@ -231,6 +233,117 @@ class Decoder:
         c.matvec_bf16(self.m.lm_head, self.normed, self.logits, sh.vocab, sh.d_model)
         c.sample(self.logits, sh.vocab, 1, self.row, self.history, self.hcap, self.token)
         c.decode_advance(self.row, self.history, self.hcap, self.token, self.pos, self.u_seq, self.u_seq.numel())
+
+    # ---- layer-major prefill (prefill.cpp:82-465, main.cpp:532-560)
+    def prefill_setup(self, max_chunk: int = 256):
+        """Buffers for prompt chunks of up to max_chunk tokens."""
+        sh = self.m.shape
+        C = max_chunk
+        f32 = dict(dtype=torch.float32, device="cuda")
+        self.pf_chunk = C
+        self.pf_hidden = torch.zeros(C, sh.d_model, **f32)
+        self.pf_normed = torch.zeros(C, sh.d_model, **f32)
+        self.pf_attn_o = torch.zeros(C, sh.d_model, **f32)
+        self.pf_ffn_out = torch.zeros(C, sh.d_model, **f32)
+        self.pf_q = torch.zeros(C, sh.q_dim, **f32)
+        self.pf_k = torch.zeros(C, sh.kv_dim, **f32)
+        self.pf_v = torch.zeros(C, sh.kv_dim, **f32)
+        self.pf_attn_out = torch.zeros(C, sh.q_dim, **f32)
+        self.pf_cos = torch.zeros(C, sh.head_dim // 2, **f32)
+        self.pf_sin = torch.zeros(C, sh.head_dim // 2, **f32)
+        self.pf_tokens = torch.zeros(C, dtype=torch.int32, device="cuda")
+        self.pf_pos = torch.zeros(1, dtype=torch.int32, device="cuda")
+        self.pf_args = []
+        for l, a0 in enumerate(self.args):
+            a = S.AttnLayerArgs.from_buffer_copy(a0)
+            a.rope_cos, a.rope_sin = self.pf_cos.data_ptr(), self.pf_sin.data_ptr()
+            a.normed_in = self.pf_normed.data_ptr()
+            a.qbuf, a.kbuf, a.vbuf = self.pf_q.data_ptr(), self.pf_k.data_ptr(), self.pf_v.data_ptr()
+            a.attn_out, a.o_out = self.pf_attn_out.data_ptr(), self.pf_attn_o.data_ptr()
+            self.pf_args.append(a)
+
+    def _prefill_chunk(self, n: int):
+        """Tokens pf_tokens[:n] at positions pf_pos.. through every layer
+        (their KV into the rings); the chunk's hidden states are not needed
+        afterwards (the last prompt token takes the normal step)."""
+        c, sh = self.ctx, self.m.shape
+        c.embed_bf16(self.m.embed, self.pf_tokens, n, sh.d_model, self.pf_hidden)
+        c.rope_tables(self.pf_pos, n, self.inv_freq, self.pf_cos, self.pf_sin, sh.head_dim // 2)
+        for l, L in enumerate(self.m.layers):
+            c.rms_norm(self.pf_hidden, self.pf_ffn_out if l > 0 else None, L["in_norm"], self.pf_normed, sh.d_model,
+                       rows=n)
+            c.attention_prefill(self.pf_args[l], n, self.pf_pos)
+            c.rms_norm(self.pf_hidden, self.pf_attn_o, L["post_norm"], self.pf_normed, sh.d_model, rows=n)
+            if "vault" in L and n > 4:       # expert-grouped path over the chunk's tokens
+                c.moe_layer(L["vault"], self.pf_normed, S.DTYPE_F32, n, sh.top_k, sh.norm_topk, self.pf_ffn_out,
+                            S.DTYPE_F32)
+            else:                            # the layer kernel, 4 tokens per launch
+                for i in range(0, n, 4):
+                    m = min(4, n - i)
+                    c.moe_layer(L["tiled"], self.pf_normed[i:i + m], S.DTYPE_F32, m, sh.top_k, sh.norm_topk,
+                                self.pf_ffn_out[i:i + m], S.DTYPE_F32)
+
+    def prefill(self, toks: torch.Tensor) -> None:
+        """All prompt tokens (device int32 [P]) but the last, layer-major in
+        chunks, then the device state for the last prompt token's step:
+        token, position P - 1, history = the prompt (the sampler's stream),
+        and that step's uniform. Device work only (capturable), on the
+        current stream."""
+        if not hasattr(self, "pf_chunk"):
+            self.prefill_setup()
+        P = toks.numel()
+        for b0 in range(0, P - 1, self.pf_chunk):
+            n = min(self.pf_chunk, P - 1 - b0)
+            self.pf_tokens[:n].copy_(toks[b0:b0 + n])
+            self.pf_pos.fill_(b0)
+            self._prefill_chunk(n)
+        self.token.copy_(toks[P - 1:P])
+        self.pos.fill_(P - 1)
+        n_hist = min(P, self.hcap)
+        self.history[:n_hist].copy_(toks[P - n_hist:])
+        self.row[5:6].fill_(n_hist)
+        self.row[4:5].copy_(self.u_seq[(P - 1) % self.u_seq.numel():(P - 1) % self.u_seq.numel() + 1].view(torch.int32))
+
+    def run_prefill(self, prompt: list[int], n_gen: int):
+        """Layer-major prefill of the prompt (one CUDA graph for its chunks),
+        then n_gen step-graph replays (the first processes the last prompt
+        token and samples the first generated one). Returns (generated ids,
+        seconds to the first generated token, seconds for all n_gen)."""
+        assert self.graph is not None
+        self.reset()
+        if not hasattr(self, "pf_chunk"):
+            self.prefill_setup()
+        new = torch.tensor([int(t) for t in prompt], dtype=torch.int32, device="cuda")
+        if getattr(self, "pf_graph_len", None) == len(prompt):
+            self.pf_prompt.copy_(new)                # the captured graph reads this buffer
+        else:
+            self.pf_prompt = new
+        torch.cuda.synchronize()
+        with torch.cuda.stream(self.stream):
+            if getattr(self, "pf_graph_len", None) != len(prompt):
+                self.prefill(self.pf_prompt)         # eager once (kernel attributes), then capture
+                torch.cuda.synchronize()
+                self.reset()
+                self.pf_graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(self.pf_graph, stream=self.stream):
+                    self.prefill(self.pf_prompt)
+                self.pf_graph_len = len(prompt)
+                torch.cuda.synchronize()
+                self.reset()
+            toks = torch.zeros(n_gen, dtype=torch.int32, device="cuda")
+            torch.cuda.synchronize()
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            ev[0].record(self.stream)
+            self.pf_graph.replay()
+            self.graph.replay()
+            toks[0:1].copy_(self.token)
+            ev[1].record(self.stream)
+            for i in range(1, n_gen):
+                self.graph.replay()
+                toks[i:i + 1].copy_(self.token)
+            ev[2].record(self.stream)
+            torch.cuda.synchronize()
+        return toks.cpu().numpy().tolist(), ev[0].elapsed_time(ev[1]) / 1e3, ev[0].elapsed_time(ev[2]) / 1e3
 
     def capture(self, stream: torch.cuda.Stream):
         self.stream = stream

@@ -41,6 +41,7 @@ EXPORTS = [
     "smoe_cuda_attention_layer", "smoe_cuda_attention_layer_async", "smoe_cuda_matvec_bf16",
     "smoe_cuda_rms_norm", "smoe_cuda_embed_bf16", "smoe_cuda_rope_table", "smoe_cuda_decode_advance",
     "smoe_cuda_gemm_bf16", "smoe_cuda_attention_batch_async", "smoe_cuda_decode_advance_batch",
+    "smoe_cuda_rope_tables", "smoe_cuda_attention_prefill_async",
 ]
 
 
@@ -170,6 +171,8 @@ def lib():
         L.smoe_cuda_gemm_bf16.argtypes = [vp, vp, vp, vp, u32, u32, u32]
         L.smoe_cuda_attention_batch_async.argtypes = [vp, C.POINTER(AttnLayerArgs), u32, u64, vp]
         L.smoe_cuda_decode_advance_batch.argtypes = [vp, vp, vp, u32, vp, u32, vp, vp, u32]
+        L.smoe_cuda_rope_tables.argtypes = [vp, vp, u32, vp, vp, vp, u32]
+        L.smoe_cuda_attention_prefill_async.argtypes = [vp, C.POINTER(AttnLayerArgs), u32, vp]
         L.smoe_cuda_ep_attach.argtypes = [vp, i32, i32, C.POINTER(EpHandle)]
         L.smoe_cuda_moe_layer_ep.argtypes = [vp, C.POINTER(MoeLayer), u32, u32, vp, i32, u32, u32, i32,
                                              vp, i32, vp, vp]
@@ -357,6 +360,14 @@ class Context:
     def attention_batch(self, args: AttnLayerArgs, batch, kv_seq_stride, pos):
         check(self.L.smoe_cuda_attention_batch_async(self.h, C.byref(args), batch, kv_seq_stride, ptr(pos)),
               "attention_batch")
+
+    def rope_tables(self, pos, n, inv_freq, cos_out, sin_out, half):
+        check(self.L.smoe_cuda_rope_tables(self.h, ptr(pos), n, ptr(inv_freq), ptr(cos_out), ptr(sin_out), half),
+              "rope_tables")
+
+    def attention_prefill(self, args: AttnLayerArgs, n_tokens, pos):
+        check(self.L.smoe_cuda_attention_prefill_async(self.h, C.byref(args), n_tokens, ptr(pos)),
+              "attention_prefill")
 
     def decode_advance_batch(self, rows, history, hcap, tokens, batch, pos, u_seq=None, u_len=0):
         check(self.L.smoe_cuda_decode_advance_batch(self.h, ptr(rows), ptr(history), hcap, ptr(tokens), batch,

@@ -115,3 +115,40 @@ def test_decode_steps_teacher_forced(ctx):
         assert e < TOL, f"pos {pos}: rel err {e:.2e}"
         assert int(dec.pos.item()) == pos + 1
     assert int(dec.token.item()) == int(np.argmax(got))     # greedy
+
+
+@pytest.mark.parametrize("layout,chunk", [("tiled", 256), ("both", 256), ("both", 4)])
+def test_prefill_then_step(ctx, layout, chunk):
+    """Layer-major prefill (prefill.cpp:82-465) of a 9-token prompt's first 8
+    tokens, then the normal step on the last prompt token: its logits
+    against the restatement stepped token by token (decode.cpp), and the
+    rings the prefill wrote against the restatement's. MoE over the chunk:
+    the layer kernel 4 tokens per launch ("tiled"), or the expert-grouped
+    path ("both"); chunk 4 splits the prompt in two chunks."""
+    from decode import Decoder, Model
+    sh = small_shape()
+    W = make_weights(sh, 21)
+    model = Model(ctx, sh, weights=W, layout=layout)
+    dec = Decoder(model, temperature=0.0, top_p=1.0, top_k=1, rep_penalty=1.0)
+    ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+    dec.prefill_setup(max_chunk=chunk)
+    prompt = [5, 400, 17, 17, 230, 88, 511, 3, 64]
+    dec.prefill(torch.tensor(prompt, dtype=torch.int32, device="cuda"))
+    torch.cuda.synchronize()
+    ctx.synchronize()
+    ref = RefDecoder(W, sh)
+    for pos, tok in enumerate(prompt[:-1]):
+        ref.step(tok, pos)
+    kv = dec.kv.cpu().numpy()
+    for l in range(sh.layers):
+        for m in range(2):
+            assert rel(kv[l, m, :len(prompt) - 1], ref.kv[l, m, :len(prompt) - 1]) < 1e-4
+    assert int(dec.pos.item()) == len(prompt) - 1
+    dec._step()
+    torch.cuda.synchronize()
+    ctx.synchronize()
+    got = dec.logits.cpu().numpy()
+    e = rel(got, ref.step(prompt[-1], len(prompt) - 1))
+    assert e < TOL, f"rel err {e:.2e}"
+    assert int(dec.token.item()) == int(np.argmax(got))
+    assert (dec.history.cpu().numpy()[:len(prompt)] == prompt).all()
