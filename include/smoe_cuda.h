@@ -200,6 +200,45 @@ uint64_t smoe_cuda_tiled_expert_bytes(uint32_t fmt, uint32_t d_model, uint32_t d
 int smoe_cuda_prepack_layer(SmoeCudaCtx* ctx, const SmoeMoeLayer* src, void* dst,
                             uint64_t dst_stride, SmoeMoeLayer* out);
 
+/* ---- .smoe vault (common.hpp:52-183, written by shatter_moe.py): the
+ * reader of main.cpp:96-198 and a device uploader. The vault is passed as
+ * host bytes (e.g. the caller's mmap); nothing here needs a GPU except the
+ * upload. */
+typedef struct {
+    uint32_t version, num_moe_layers, max_experts_per_layer, total_experts;
+    uint32_t group_size, bits, d_model, vocab_size, ffn_dim;
+    uint64_t table_offset, data_offset;
+    /* v2 arch block (has_arch 0 for a v1 vault) */
+    uint32_t has_arch, arch_flags, num_heads, num_kv_heads, head_dim, moe_top_k;
+    uint32_t moe_ffn_dim, dense_ffn_dim, shared_expert_ffn_dim, num_hidden_layers;
+    float    rope_theta, rms_norm_eps;
+    char     model_type[24];
+    /* expert layout from the first expert's descriptors (main.cpp:170-198) */
+    uint32_t gate_rows, gate_cols, up_rows, up_cols, down_rows, down_cols;
+    uint64_t gate_packed_offset, gate_scales_offset, up_packed_offset, up_scales_offset;
+    uint64_t down_packed_offset, down_scales_offset;
+    uint64_t max_raw_size;        /* largest expert blob, unpadded bytes */
+} SmoeVaultInfo;
+
+/* Header, arch block, tensor descriptors and table bounds (main.cpp:96-198:
+ * magic, version 1..2, a v2 vault's arch block valid, SiLU, top_k <= 16,
+ * head_dim <= 256, heads divisible). SMOE_OK or SMOE_ERR_ARG /
+ * SMOE_ERR_UNSUPPORTED with smoe_cuda_vault_last_error(). Host only. */
+int smoe_cuda_vault_parse(const void* vault, uint64_t size, SmoeVaultInfo* out);
+/* Byte offset and unpadded size of (layer, expert)'s blob. Host only. */
+int smoe_cuda_vault_expert(const void* vault, uint64_t size, uint32_t layer, uint32_t expert,
+                           uint64_t* offset, uint64_t* raw_size);
+/* Copy every expert blob of `layer` into the device arena dst (expert e at
+ * dst + e * dst_stride; dst_stride >= max_raw_size, 16-byte multiple), one
+ * cudaMemcpyAsync per expert on the context stream, and describe the result
+ * in *out (SMOE-Q4 vault layout, router_w stored as given). 4-bit group-64
+ * vaults only (a 2-bit vault: SMOE_ERR_UNSUPPORTED). The vault bytes must
+ * stay valid until the stream has run the copies. */
+int smoe_cuda_vault_upload_layer(SmoeCudaCtx* ctx, const void* vault, uint64_t size, uint32_t layer,
+                                 void* dst, uint64_t dst_stride, const uint16_t* router_w,
+                                 SmoeMoeLayer* out);
+const char* smoe_cuda_vault_last_error(void);
+
 /* Router of decode.cpp:280-303 for `batch` tokens: logits = W . x (bf16 W,
  * fp32 accumulate), softmax over n_experts, top-k by probability (lowest
  * index wins ties), renormalised over the k when norm_topk. Outputs (device):

@@ -17,7 +17,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 LIB = os.path.join(HERE, "libsmoe_cuda.so")
 LIB_TRACE = os.path.join(HERE, "libsmoe_cuda_trace.so")
-SOURCES = [os.path.join(HERE, "csrc", "smoe_cuda.cu"), os.path.join(HERE, "csrc", "smoe_noalloc.cu")]
+SOURCES = [os.path.join(HERE, "csrc", "smoe_cuda.cu"), os.path.join(HERE, "csrc", "smoe_noalloc.cu"),
+           os.path.join(HERE, "csrc", "smoe_vault.cpp")]
 DEPS = SOURCES + [os.path.join(HERE, "csrc", f) for f in os.listdir(os.path.join(HERE, "csrc"))] + [
     os.path.join(ROOT, "include", "smoe_cuda.h")]
 
@@ -57,5 +58,28 @@ def build(force: bool = False, verbose: bool = False, trace: bool = False) -> st
     return lib
 
 
+ENGINE = os.path.join(HERE, "smoe_engine")
+ENGINE_SRC = os.path.join(HERE, "engine", "smoe_engine.cu")
+
+
+def build_engine(force: bool = False, verbose: bool = False) -> str:
+    """The C++ engine binary (engine/smoe_engine.cu), linked against the
+    library beside it (rpath $ORIGIN)."""
+    lib = build(force=force, verbose=verbose)
+    if not force and os.path.exists(ENGINE) and os.path.getmtime(ENGINE) >= max(
+            os.path.getmtime(ENGINE_SRC), os.path.getmtime(lib), os.path.getmtime(os.path.join(ROOT, "include", "smoe_cuda.h"))):
+        return ENGINE
+    cmd = [nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17", ENGINE_SRC, "-o", ENGINE,
+           "-L" + HERE, "-lsmoe_cuda", "-Xlinker", "-rpath,$ORIGIN"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if verbose or r.returncode != 0:
+        sys.stderr.write(r.stdout + r.stderr)
+    if r.returncode != 0:
+        raise RuntimeError("nvcc failed building smoe_engine")
+    return ENGINE
+
+
 if __name__ == "__main__":
     print(build(force="--force" in sys.argv, verbose=True, trace="--trace" in sys.argv))
+    if "--trace" not in sys.argv:
+        print(build_engine(force="--force" in sys.argv))

@@ -216,6 +216,7 @@ struct AttnArgs {
     size_t kv_seq_stride;                // batched decode (gridDim.z sequences): floats between the
                                          // rings of consecutive sequences; q/k/v/qbuf/attn_out are
                                          // [sequences][q_dim or kv_dim] (one split per head then)
+    uint32_t blk;                        // k_attn_batch_gqa: positions per score block (shared memory)
     uint32_t prefill;                    // k_attn_batch_gqa: row z is token z of one sequence at
                                          // position *pos + z, its K/V already in the ring
                                          // (k_prefill_kv), RoPE tables [tokens][head_dim/2]
@@ -420,14 +421,18 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(AttnArgs a) {
 //  2. scores: 4 lanes per position (hd / 4 dims each, all loads issued
 //     before the dots), G dot products per K row, reduced over the 4 lanes;
 //  3. softmax per head (warp per head): max, exp, sum;
+//  steps 2-4 run over blocks of `blk` positions with the softmax carried
+//  from block to block (running max, sum and accumulators rescaled), so the
+//  scores held in shared memory are bounded whatever the ring size;
 //  4. out[g][d] = sum_i p[g][i] V[i][d] / sum_g: a warp takes every 8th
 //     position, a lane 4 dims of the row (one float4), G float4
 //     accumulators, 4 rows in flight; the warps' partials added through
 //     shared memory.
 // head_dim == 128. Dynamic shared memory (floats): q [G hd], k [hd], v [hd],
-// scores [G ctx], warp partials [8][G hd].
+// scores [G blk], warp partials [8][G hd].
 constexpr int kAttnGqaMaxG = 16;
-__global__ void __launch_bounds__(kAttnThreads) k_attn_batch_gqa(AttnArgs a) {
+template <int GM>      // query heads per KV head, at most (8 or 16): sizes the accumulators
+__global__ void __launch_bounds__(kAttnThreads, 2) k_attn_batch_gqa(AttnArgs a) {
     extern __shared__ __align__(16) float gqa_sm[];
     const uint32_t hd = a.head_dim, G = a.num_heads / a.num_kv_heads, kvh = blockIdx.x;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = kAttnThreads / 32;
@@ -435,7 +440,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_batch_gqa(AttnArgs a) {
     float* ks = qs + G * hd;
     float* vs = ks + hd;
     float* sc = vs + hd;
-    float* gp = sc + size_t(G) * a.attn_ctx;
+    float* gp = sc + size_t(G) * a.blk;
     pdl_trigger();
     pdl_wait();
     const size_t z = blockIdx.y;
@@ -503,94 +508,117 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_batch_gqa(AttnArgs a) {
             k_cache[size_t(slot) * a.kv_dim + size_t(kvh) * hd + i] = ks[i];
             v_cache[size_t(slot) * a.kv_dim + size_t(kvh) * hd + i] = vs[i];
         }
-    // 2. scores: position i (0 = this step; from the ring in prefill) at sc[g * ctx + i]
+    // 2-4 over blocks of a.blk positions, the softmax carried across blocks
+    // (running max per head; the sum and the accumulators rescaled by
+    // exp(old max - new max) when it grows)
+    __shared__ float sums[GM], mx[GM], alpha[GM];
+    if (uint32_t(tid) < G) {
+        sums[tid] = 0.f;
+        mx[tid] = -INFINITY;
+    }
+    float4 acc[GM];
+#pragma unroll
+    for (int g = 0; g < GM; ++g) acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
     const uint32_t sub = lane & 3, q4 = hd / 16;                  // float4s per lane and position
-    for (uint32_t base = warp * 8; base < valid; base += nw * 8) {
-        const uint32_t i = base + (lane >> 2);
-        float4 kk[16];
-        if (i < valid) {
-            const float4* kr = i == 0 && !pf ? reinterpret_cast<const float4*>(ks) + sub * q4
-                                             : reinterpret_cast<const float4*>(
-                                                   k_cache + size_t((slot + a.attn_ctx - i) % a.attn_ctx) * a.kv_dim +
-                                                   size_t(kvh) * hd) + sub * q4;
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-                if (j < int(q4)) kk[j] = kr[j];
-        }
-        for (uint32_t g = 0; g < G; ++g) {
-            const float4* qv = reinterpret_cast<const float4*>(qs + size_t(g) * hd) + sub * q4;
-            float s = 0.f;
-            if (i < valid) {
-#pragma unroll
-                for (int j = 0; j < 16; ++j)
-                    if (j < int(q4)) {
-                        const float4 qq = qv[j];
-                        s = fmaf(qq.x, kk[j].x, s);
-                        s = fmaf(qq.y, kk[j].y, s);
-                        s = fmaf(qq.z, kk[j].z, s);
-                        s = fmaf(qq.w, kk[j].w, s);
-                    }
-            }
-            s += __shfl_xor_sync(0xffffffffu, s, 1);
-            s += __shfl_xor_sync(0xffffffffu, s, 2);
-            if (sub == 0 && i < valid) sc[size_t(g) * a.attn_ctx + i] = s * a.scale;
-        }
-    }
-    __syncthreads();
-    // 3. softmax per head (a warp per head), the sums to shared memory
-    __shared__ float sums[kAttnGqaMaxG];
-    for (uint32_t g = warp; g < G; g += nw) {
-        float* sg = sc + size_t(g) * a.attn_ctx;
-        float m = -INFINITY;
-        for (uint32_t i = lane; i < valid; i += 32) m = fmaxf(m, sg[i]);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        float sum = 0.f;
-        for (uint32_t i = lane; i < valid; i += 32) {
-            const float e = expf(sg[i] - m);
-            sg[i] = e;
-            sum += e;
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        if (lane == 0) sums[g] = sum;
-    }
-    __syncthreads();
-    // 4. weighted V sum: warp w takes positions w, w + 8, ..., a lane the
-    //    float4 of dims 4 lane.. of each V row (hd == 128), 4 rows in flight;
-    //    the 8 warps' partials are added through shared memory
-    float4 acc[kAttnGqaMaxG];
-#pragma unroll
-    for (int g = 0; g < kAttnGqaMaxG; ++g) acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
     const float4* vb = reinterpret_cast<const float4*>(v_cache + size_t(kvh) * hd) + lane;
     const float4 vnew = pf ? make_float4(0.f, 0.f, 0.f, 0.f) : reinterpret_cast<const float4*>(vs)[lane];
-    for (uint32_t i = warp; i < valid; i += 4 * nw) {
-        float4 vv[4];
+    const uint32_t BL = a.blk;
+    for (uint32_t b0 = 0; b0 < valid; b0 += BL) {
+        const uint32_t b1 = min(valid, b0 + BL), nb = b1 - b0;
+        // 2. scores of positions [b0, b1) (0 = this step; from the ring in
+        //    prefill) at sc[g * BL + i - b0]
+        for (uint32_t base = b0 + warp * 8; base < b1; base += nw * 8) {
+            const uint32_t i = base + (lane >> 2);
+            float4 kk[8];                                 // hd == 128: 8 float4 per lane
+            if (i < b1) {
+                const float4* kr = i == 0 && !pf ? reinterpret_cast<const float4*>(ks) + sub * q4
+                                                 : reinterpret_cast<const float4*>(
+                                                       k_cache + size_t((slot + a.attn_ctx - i) % a.attn_ctx) *
+                                                                     a.kv_dim + size_t(kvh) * hd) + sub * q4;
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const uint32_t p = i + u * nw;
-            vv[u] = p == 0 && !pf ? vnew
-                  : p < valid ? vb[size_t((slot + a.attn_ctx - p) % a.attn_ctx) * (a.kv_dim / 4)]
-                              : make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int j = 0; j < 8; ++j) kk[j] = kr[j];
+            }
+            for (uint32_t g = 0; g < G; ++g) {
+                const float4* qv = reinterpret_cast<const float4*>(qs + size_t(g) * hd) + sub * q4;
+                float s = 0.f;
+                if (i < b1) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                            const float4 qq = qv[j];
+                            s = fmaf(qq.x, kk[j].x, s);
+                            s = fmaf(qq.y, kk[j].y, s);
+                            s = fmaf(qq.z, kk[j].z, s);
+                            s = fmaf(qq.w, kk[j].w, s);
+                        }
+                }
+                s += __shfl_xor_sync(0xffffffffu, s, 1);
+                s += __shfl_xor_sync(0xffffffffu, s, 2);
+                if (sub == 0 && i < b1) sc[size_t(g) * BL + (i - b0)] = s * a.scale;
+            }
         }
+        __syncthreads();
+        // 3. softmax terms per head (a warp per head)
+        for (uint32_t g = warp; g < G; g += nw) {
+            float* sg = sc + size_t(g) * BL;
+            float m = -INFINITY;
+            for (uint32_t i = lane; i < nb; i += 32) m = fmaxf(m, sg[i]);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const uint32_t p = i + u * nw;
-            if (p < valid)
+            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            const float m_old = mx[g], M = fmaxf(m_old, m);
+            float sum = 0.f;
+            for (uint32_t i = lane; i < nb; i += 32) {
+                const float e = expf(sg[i] - M);
+                sg[i] = e;
+                sum += e;
+            }
 #pragma unroll
-                for (int g = 0; g < kAttnGqaMaxG; ++g)
-                    if (uint32_t(g) < G) {
-                        const float w = sc[size_t(g) * a.attn_ctx + p];
-                        acc[g].x = fmaf(w, vv[u].x, acc[g].x);
-                        acc[g].y = fmaf(w, vv[u].y, acc[g].y);
-                        acc[g].z = fmaf(w, vv[u].z, acc[g].z);
-                        acc[g].w = fmaf(w, vv[u].w, acc[g].w);
-                    }
+            for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            if (lane == 0) {
+                const float al = m_old == -INFINITY ? 0.f : expf(m_old - M);
+                alpha[g] = al;
+                sums[g] = fmaf(sums[g], al, sum);
+                mx[g] = M;
+            }
         }
+        __syncthreads();
+        // 4. weighted V sum: warp w takes positions b0 + w, + 8, ..., a lane
+        //    the float4 of dims 4 lane.. of each V row (hd == 128), 4 rows in
+        //    flight
+#pragma unroll
+        for (int g = 0; g < GM; ++g)
+            if (uint32_t(g) < G) {
+                const float al = alpha[g];
+                acc[g].x *= al; acc[g].y *= al; acc[g].z *= al; acc[g].w *= al;
+            }
+        for (uint32_t i = b0 + warp; i < b1; i += 4 * nw) {
+            float4 vv[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const uint32_t p = i + u * nw;
+                vv[u] = p == 0 && !pf ? vnew
+                      : p < b1 ? vb[size_t((slot + a.attn_ctx - p) % a.attn_ctx) * (a.kv_dim / 4)]
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const uint32_t p = i + u * nw;
+                if (p < b1)
+#pragma unroll
+                    for (int g = 0; g < GM; ++g)
+                        if (uint32_t(g) < G) {
+                            const float w = sc[size_t(g) * BL + (p - b0)];
+                            acc[g].x = fmaf(w, vv[u].x, acc[g].x);
+                            acc[g].y = fmaf(w, vv[u].y, acc[g].y);
+                            acc[g].z = fmaf(w, vv[u].z, acc[g].z);
+                            acc[g].w = fmaf(w, vv[u].w, acc[g].w);
+                        }
+            }
+        }
+        __syncthreads();                 // the next block's scores overwrite sc
     }
     float4* gp4 = reinterpret_cast<float4*>(gp);                 // [8 warps][G][32 float4]
 #pragma unroll
-    for (int g = 0; g < kAttnGqaMaxG; ++g)
+    for (int g = 0; g < GM; ++g)
         if (uint32_t(g) < G) gp4[(size_t(warp) * G + g) * 32 + lane] = acc[g];
     __syncthreads();
     for (uint32_t o = tid; o < G * 32; o += blockDim.x) {

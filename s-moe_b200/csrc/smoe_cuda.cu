@@ -1126,6 +1126,15 @@ bool gemm_shape_ok(const SmoeCudaCtx* c, const float* x, uint32_t cols, uint32_t
 }
 }  // namespace
 
+namespace {
+// positions per score block of the GQA attention kernel (shared memory
+// [G][blk] floats): the whole ring up to 1024 positions
+uint32_t gqa_block(uint32_t attn_ctx) { return attn_ctx < 1024u ? attn_ctx : 1024u; }
+size_t gqa_smem_bytes(uint32_t G, uint32_t hd, uint32_t blk) {
+    return (size_t(G + 2) * hd + size_t(G) * blk + size_t(smoe::kAttnThreads / 32) * G * hd) * 4;
+}
+}  // namespace
+
 int smoe_cuda_gemm_bf16(SmoeCudaCtx* c, const uint16_t* w, const float* x, float* y, uint32_t rows,
                         uint32_t cols, uint32_t batch) {
     if (!c) { set_err("null context %s%ld", "", 0); return SMOE_ERR_ARG; }
@@ -1185,14 +1194,15 @@ int smoe_cuda_attention_batch_async(SmoeCudaCtx* c, const SmoeCudaAttnLayerArgs*
     // Head groups whose ring is shared by several query heads take the
     // GQA kernel (each ring read once per group) when its tiles fit.
     const uint32_t G = a->num_heads / a->num_kv_heads;
-    const size_t gqa_smem = (size_t(G + 2) * a->head_dim + size_t(G) * a->attn_ctx +
-                             size_t(smoe::kAttnThreads / 32) * G * a->head_dim) * 4;
-    if (batch > 1 && a->head_dim == 128 && (size_t(G) * a->attn_ctx) % 4 == 0 &&   // float4 partials aligned
+    const uint32_t blk = gqa_block(a->attn_ctx);
+    const size_t gqa_smem = gqa_smem_bytes(G, a->head_dim, blk);
+    t.blk = blk;
+    if (batch > 1 && a->head_dim == 128 && (size_t(G) * blk) % 4 == 0 &&   // float4 partials aligned
         G <= uint32_t(smoe::kAttnGqaMaxG) && gqa_smem <= c->smem_optin && aligned16(a->k_cache) &&
         aligned16(a->v_cache) && aligned16(a->qbuf) && aligned16(a->attn_out) && kv_seq_stride % 4 == 0) {
-        if ((rc = prep_kernel(c, smoe::k_attn_batch_gqa, gqa_smem))) return rc;
-        rc = pdl_launch_smem(c, smoe::k_attn_batch_gqa, dim3(a->num_kv_heads, batch), dim3(smoe::kAttnThreads),
-                             gqa_smem, t);
+        auto kern = G <= 8 ? smoe::k_attn_batch_gqa<8> : smoe::k_attn_batch_gqa<16>;
+        if ((rc = prep_kernel(c, kern, gqa_smem))) return rc;
+        rc = pdl_launch_smem(c, kern, dim3(a->num_kv_heads, batch), dim3(smoe::kAttnThreads), gqa_smem, t);
     } else {
         const uint32_t splits = batch > 1 ? 1u : std::min<uint32_t>(smoe::kAttnSplits, (a->attn_ctx + 31) / 32);
         rc = pdl_launch(c, smoe::k_attn_decode, dim3(a->num_heads, splits, batch), dim3(smoe::kAttnThreads), t);
@@ -1214,8 +1224,8 @@ int smoe_cuda_rope_tables(SmoeCudaCtx* c, const uint32_t* pos, uint32_t n, const
 int smoe_cuda_attention_prefill_async(SmoeCudaCtx* c, const SmoeCudaAttnLayerArgs* a, uint32_t n_tokens,
                                       const uint32_t* pos) {
     const uint32_t G = a && a->num_kv_heads ? a->num_heads / a->num_kv_heads : 0;
-    const size_t smem = a ? (size_t(G + 2) * a->head_dim + size_t(G) * a->attn_ctx +
-                             size_t(smoe::kAttnThreads / 32) * G * a->head_dim) * 4 : 0;
+    const uint32_t blk = a ? gqa_block(a->attn_ctx) : 0;
+    const size_t smem = a ? gqa_smem_bytes(G, a->head_dim, blk) : 0;
     if (!c || !a || !pos || n_tokens == 0 || !a->w_q || !a->w_k || !a->w_v || !a->w_o || !a->rope_cos ||
         !a->rope_sin || !a->normed_in || !a->qbuf || !a->kbuf || !a->vbuf || !a->k_cache || !a->v_cache ||
         !a->attn_out || !a->o_out || a->num_kv_heads == 0 || a->num_heads % a->num_kv_heads ||
@@ -1224,7 +1234,7 @@ int smoe_cuda_attention_prefill_async(SmoeCudaCtx* c, const SmoeCudaAttnLayerArg
         set_err("bad prefill attention arguments %s%ld", "", (long)n_tokens);
         return SMOE_ERR_ARG;
     }
-    if (a->head_dim != 128 || G > uint32_t(smoe::kAttnGqaMaxG) || (size_t(G) * a->attn_ctx) % 4 ||
+    if (a->head_dim != 128 || G > uint32_t(smoe::kAttnGqaMaxG) || (size_t(G) * blk) % 4 ||
         smem > c->smem_optin || !aligned16(a->k_cache) || !aligned16(a->v_cache) || !aligned16(a->qbuf) ||
         !aligned16(a->attn_out)) {
         set_err("prefill attention needs head_dim 128, <= 16 query heads per KV head and aligned rings %s%ld", "",
@@ -1264,9 +1274,10 @@ int smoe_cuda_attention_prefill_async(SmoeCudaCtx* c, const SmoeCudaAttnLayerArg
     t.scale = a->attn_scale;
     t.kv_seq_stride = 0;                 // one sequence: every token's window is in the same ring
     t.prefill = 1;
-    if ((rc = prep_kernel(c, smoe::k_attn_batch_gqa, smem))) return rc;
-    rc = pdl_launch_smem(c, smoe::k_attn_batch_gqa, dim3(a->num_kv_heads, n_tokens), dim3(smoe::kAttnThreads), smem,
-                         t);
+    t.blk = blk;
+    auto kern = G <= 8 ? smoe::k_attn_batch_gqa<8> : smoe::k_attn_batch_gqa<16>;
+    if ((rc = prep_kernel(c, kern, smem))) return rc;
+    rc = pdl_launch_smem(c, kern, dim3(a->num_kv_heads, n_tokens), dim3(smoe::kAttnThreads), smem, t);
     if (rc) return rc;
     return smoe_cuda_gemm_bf16(c, a->w_o, a->attn_out, a->o_out, a->d_model, a->q_dim, n_tokens);
 }

@@ -42,7 +42,23 @@ EXPORTS = [
     "smoe_cuda_rms_norm", "smoe_cuda_embed_bf16", "smoe_cuda_rope_table", "smoe_cuda_decode_advance",
     "smoe_cuda_gemm_bf16", "smoe_cuda_attention_batch_async", "smoe_cuda_decode_advance_batch",
     "smoe_cuda_rope_tables", "smoe_cuda_attention_prefill_async",
+    "smoe_cuda_vault_parse", "smoe_cuda_vault_expert", "smoe_cuda_vault_upload_layer", "smoe_cuda_vault_last_error",
 ]
+
+
+class VaultInfo(C.Structure):
+    """SmoeVaultInfo (a parsed .smoe vault header, arch block and layout)."""
+    _fields_ = [(n, C.c_uint32) for n in ("version", "num_moe_layers", "max_experts_per_layer", "total_experts",
+                                          "group_size", "bits", "d_model", "vocab_size", "ffn_dim")] + \
+              [("table_offset", C.c_uint64), ("data_offset", C.c_uint64)] + \
+              [(n, C.c_uint32) for n in ("has_arch", "arch_flags", "num_heads", "num_kv_heads", "head_dim",
+                                          "moe_top_k", "moe_ffn_dim", "dense_ffn_dim", "shared_expert_ffn_dim",
+                                          "num_hidden_layers")] + \
+              [("rope_theta", C.c_float), ("rms_norm_eps", C.c_float), ("model_type", C.c_char * 24)] + \
+              [(n, C.c_uint32) for n in ("gate_rows", "gate_cols", "up_rows", "up_cols", "down_rows", "down_cols")] + \
+              [(n, C.c_uint64) for n in ("gate_packed_offset", "gate_scales_offset", "up_packed_offset",
+                                          "up_scales_offset", "down_packed_offset", "down_scales_offset",
+                                          "max_raw_size")]
 
 
 class AttnLayerArgs(C.Structure):
@@ -172,6 +188,10 @@ def lib():
         L.smoe_cuda_attention_batch_async.argtypes = [vp, C.POINTER(AttnLayerArgs), u32, u64, vp]
         L.smoe_cuda_decode_advance_batch.argtypes = [vp, vp, vp, u32, vp, u32, vp, vp, u32]
         L.smoe_cuda_rope_tables.argtypes = [vp, vp, u32, vp, vp, vp, u32]
+        L.smoe_cuda_vault_parse.argtypes = [vp, u64, C.POINTER(VaultInfo)]
+        L.smoe_cuda_vault_expert.argtypes = [vp, u64, u32, u32, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]
+        L.smoe_cuda_vault_upload_layer.argtypes = [vp, vp, u64, u32, vp, u64, vp, C.POINTER(MoeLayer)]
+        L.smoe_cuda_vault_last_error.restype = C.c_char_p
         L.smoe_cuda_attention_prefill_async.argtypes = [vp, C.POINTER(AttnLayerArgs), u32, vp]
         L.smoe_cuda_ep_attach.argtypes = [vp, i32, i32, C.POINTER(EpHandle)]
         L.smoe_cuda_moe_layer_ep.argtypes = [vp, C.POINTER(MoeLayer), u32, u32, vp, i32, u32, u32, i32,
@@ -361,6 +381,16 @@ class Context:
         check(self.L.smoe_cuda_attention_batch_async(self.h, C.byref(args), batch, kv_seq_stride, ptr(pos)),
               "attention_batch")
 
+    def vault_upload_layer(self, vault, layer, dst, dst_stride, router_w) -> MoeLayer:
+        """Copy a vault layer's expert blobs into the device arena dst."""
+        p, n = _vault_bytes(vault)
+        out = MoeLayer()
+        rc = self.L.smoe_cuda_vault_upload_layer(self.h, p, n, layer, ptr(dst), dst_stride, ptr(router_w),
+                                                 C.byref(out))
+        if rc:
+            raise SmoeCudaError(f"vault_upload_layer: {STATUS.get(rc, rc)}: " + self.L.smoe_cuda_vault_last_error().decode())
+        return out
+
     def rope_tables(self, pos, n, inv_freq, cos_out, sin_out, half):
         check(self.L.smoe_cuda_rope_tables(self.h, ptr(pos), n, ptr(inv_freq), ptr(cos_out), ptr(sin_out), half),
               "rope_tables")
@@ -376,6 +406,33 @@ class Context:
     def sample(self, logits, vocab, batch, rows, history, history_stride, tokens):
         check(self.L.smoe_cuda_sample(self.h, ptr(logits), vocab, batch, ptr(rows), ptr(history),
                                       history_stride, ptr(tokens)), "sample")
+
+
+def _vault_bytes(vault):
+    """(pointer, size) of a vault held in host memory (numpy uint8 array or bytes)."""
+    import numpy as np
+    a = np.frombuffer(vault, np.uint8) if isinstance(vault, (bytes, bytearray, memoryview)) else vault
+    return a.ctypes.data, a.nbytes
+
+
+def vault_parse(vault) -> VaultInfo:
+    """Parse a .smoe vault (host bytes); raises SmoeCudaError with the reader's message."""
+    p, n = _vault_bytes(vault)
+    info = VaultInfo()
+    rc = lib().smoe_cuda_vault_parse(p, n, C.byref(info))
+    if rc:
+        raise SmoeCudaError(f"vault_parse: {STATUS.get(rc, rc)}: " + lib().smoe_cuda_vault_last_error().decode())
+    return info
+
+
+def vault_expert(vault, layer: int, expert: int):
+    """(byte offset, unpadded size) of one expert blob."""
+    p, n = _vault_bytes(vault)
+    off, raw = C.c_uint64(), C.c_uint64()
+    rc = lib().smoe_cuda_vault_expert(p, n, layer, expert, C.byref(off), C.byref(raw))
+    if rc:
+        raise SmoeCudaError(f"vault_expert: {STATUS.get(rc, rc)}: " + lib().smoe_cuda_vault_last_error().decode())
+    return off.value, raw.value
 
 
 def make_layer(base, stride, off, n_experts, d_model, d_ff, fmt, router_w) -> MoeLayer:

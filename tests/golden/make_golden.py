@@ -9,7 +9,7 @@ Sources of truth, all from the reference project itself:
     compiled unmodified into ``oracle/_ref/libsmoe_ref.so``.
 
 Usage:  python tests/golden/make_golden.py <reference-root>
-Writes: tests/golden/q4_expert.npz, sampler.npz, router.npz
+Writes: tests/golden/q4_expert.npz, vault.npz, sampler.npz, router.npz
 """
 from __future__ import annotations
 
@@ -55,6 +55,71 @@ def q4_fixture(ref_root: str):
     np.savez_compressed(os.path.join(HERE, "q4_expert.npz"), blob=blob, offsets=offs,
                         d=d, dff=dff, x=xs, y=np.array(ys), gate=dense[0].astype(np.float32),
                         up=dense[1].astype(np.float32), down=dense[2].astype(np.float32))
+
+
+def vault_fixture(ref_root: str):
+    """A two-layer, four-expert SMOE-Q4 vault (d_model 128, expert d_ff 64)
+    written with the reference writer's own pieces: ``build_expert_blob``
+    (quantise + blob layout), ``HEADER_FMT`` / ``EXPERT_ENTRY_FMT`` /
+    ``TENSOR_DESC_FMT`` records, ``build_arch_block``, the layout rules of its
+    ``main`` (table after the header, descriptors after the table, arch block
+    64-byte aligned after them, blobs from the next page, each padded to a
+    page), then accepted by the reference's ``validate_vault``. Stored with
+    the expected header / arch values and every blob's offset and size."""
+    sys.path.insert(0, os.path.join(ref_root, "scripts"))
+    import tempfile
+    import shatter_moe as S
+
+    L, E, d, dff = 2, 4, 128, 64
+    rng = np.random.default_rng(77)
+    blobs, metas = [], []
+    for l in range(L):
+        for e in range(E):
+            t = {"gate": rng.normal(0, 0.05, (dff, d)).astype(np.float32),
+                 "up": rng.normal(0, 0.05, (dff, d)).astype(np.float32),
+                 "down": rng.normal(0, 0.05, (d, dff)).astype(np.float32)}
+            blob, descs = S.build_expert_blob(t, 64, bits=4)
+            blobs.append(blob)
+            metas.append((l, e, descs))
+    n = len(blobs)
+    meta_bytes = S.HEADER_FMT.size + n * S.EXPERT_ENTRY_FMT.size + n * 3 * S.TENSOR_DESC_FMT.size
+    arch_offset = S._align_up(meta_bytes, 64)
+    data_offset = S._align_up(arch_offset + S.ARCH_FMT.size, S.PAGE_SIZE)
+    arch = {"norm_topk_prob": True, "has_qk_norm": True, "has_dense_layer_0": False, "rope_theta": 1e6,
+            "num_heads": 4, "num_kv_heads": 2, "head_dim": 32, "moe_top_k": 2, "moe_ffn_dim": dff,
+            "dense_ffn_dim": 0, "shared_expert_ffn_dim": 0, "activation": 0, "num_hidden_layers": L,
+            "rms_norm_eps": 1e-6, "model_type": "qwen3_moe"}
+    body, entries, cur = [], [], data_offset
+    for blob in blobs:
+        padded = S._align_up(len(blob), S.PAGE_SIZE)
+        entries.append((cur, len(blob), padded))
+        body.append(blob + b"\x00" * (padded - len(blob)))
+        cur += padded
+    head = bytearray(S.HEADER_FMT.pack(S.SMOE_MAGIC, S.SMOE_VERSION, L, E, n, S.HEADER_FMT.size, data_offset, 64,
+                                       4, d, 512, dff, arch_offset))
+    for (l, e, descs), (off, raw, pad) in zip(metas, entries):
+        groups = sum(td.num_groups for td in descs)
+        head += S.EXPERT_ENTRY_FMT.pack(l, e, off, raw, pad, 64, groups)
+    for (_, _, descs) in metas:
+        for td in descs:
+            head += S.TENSOR_DESC_FMT.pack(td.tensor_type, 2, td.rows, td.cols, td.packed_offset, td.packed_size,
+                                           td.scales_offset, td.scales_size)
+    head += b"\x00" * (arch_offset - len(head))
+    head += S.build_arch_block(arch)
+    head += b"\x00" * (data_offset - len(head))
+    vault = bytes(head) + b"".join(body)
+    with tempfile.TemporaryDirectory() as tmp:          # the reference's own reader accepts it
+        path = os.path.join(tmp, "fixture.smoe")
+        with open(path, "wb") as f:
+            f.write(vault)
+        S.validate_vault(S.Path(path))
+    d0 = metas[0][2]
+    np.savez_compressed(os.path.join(HERE, "vault.npz"), vault=np.frombuffer(vault, np.uint8),
+                        layers=L, experts=E, d_model=d, d_ff=dff, data_offset=data_offset, arch_offset=arch_offset,
+                        entries=np.array([(l, e, off, raw) for (l, e, _), (off, raw, _) in zip(metas, entries)],
+                                         np.int64),
+                        desc=np.array([[td.rows, td.cols, td.packed_offset, td.scales_offset] for td in d0],
+                                      np.int64))
 
 
 def sampler_fixture():
@@ -123,6 +188,7 @@ if __name__ == "__main__":
     assert ref_root and os.path.isdir(ref_root), "pass the reference project root"
     assert O.ref_available(), "build oracle/_ref first (make -C oracle REF_SRC=...)"
     q4_fixture(ref_root)
+    vault_fixture(ref_root)
     sampler_fixture()
     router_fixture()
     print("golden fixtures written to", HERE)

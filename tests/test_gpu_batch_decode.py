@@ -47,12 +47,13 @@ def test_gemm_bf16_batch(ctx, batch, rows, cols):
 
 
 @pytest.mark.parametrize("ctx_len,pos,heads", [(64, 5, "30b"), (64, 100, "30b"), (256, 200, "30b"), (4096, 300, "30b"),
-                                               (64, 100, "235b")])
+                                               (4096, 2500, "30b"), (64, 100, "235b"), (4096, 1500, "235b")])
 def test_attention_batch(ctx, ctx_len, pos, heads):
     """Three sequences with different pre-filled rings at one position (with
     and without the ring wrapping), 8 and 16 query heads per KV head (the
-    kernel reads each KV head's ring once for its group): each sequence
-    against the restatement alone."""
+    kernel reads each KV head's ring once for its group), windows of one and
+    of several 1024-position score blocks: each sequence against the
+    restatement alone."""
     B = 3
     sh = small_shape(ctx_len, heads)
     W = make_weights(sh, 5)
@@ -151,3 +152,46 @@ def test_batch_decode_teacher_forced(ctx):
     hist = dec.history.cpu().numpy()
     assert (dec.rows.cpu().numpy().view(np.uint32)[:, 5] == steps.shape[0]).all()
     assert (hist[:, steps.shape[0] - 1] == toks).all()
+
+
+@pytest.mark.parametrize("heads,ctx_len,pos0,n", [("30b", 64, 0, 7), ("30b", 4096, 1500, 5), ("235b", 4096, 1200, 6)])
+def test_attention_prefill_chunk(ctx, heads, ctx_len, pos0, n):
+    """smoe_cuda_attention_prefill_async: n tokens of one sequence at
+    positions pos0.. (prefill.cpp:131-268) against the restatement stepping
+    them one at a time: outputs, normed + roped Q, and the ring rows the
+    chunk appended."""
+    sh = small_shape(ctx_len, heads)
+    W = make_weights(sh, 6)
+    ref = RefDecoder(W, sh)
+    rng = np.random.default_rng(pos0 + n)
+    ring0 = rng.standard_normal(ref.kv[0].shape)
+    ref.kv[0] = ring0.copy()
+    normed = rng.standard_normal((n, sh.d_model))
+    f = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+    t = {k: dev(W[k][0]) for k in ("w_q", "w_k", "w_v", "w_o", "q_norm", "k_norm")}
+    kc, vc = f(ring0[0]), f(ring0[1])
+    bufs = {k: torch.zeros(n, c, device="cuda") for k, c in (("q", sh.q_dim), ("k", sh.kv_dim), ("v", sh.kv_dim),
+                                                              ("a", sh.q_dim), ("o", sh.d_model))}
+    ang = np.stack([(np.float32(pos0 + i) * ref.inv_freq).astype(np.float32) for i in range(n)]).astype(np.float64)
+    cs_d, sn_d, x_d = f(np.cos(ang)), f(np.sin(ang)), f(normed)
+    dpos = torch.tensor([pos0], dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    a = S.AttnLayerArgs()
+    a.w_q, a.w_k, a.w_v, a.w_o = (t[k].data_ptr() for k in ("w_q", "w_k", "w_v", "w_o"))
+    a.q_norm_w, a.k_norm_w = t["q_norm"].data_ptr(), t["k_norm"].data_ptr()
+    a.rope_cos, a.rope_sin, a.normed_in = cs_d.data_ptr(), sn_d.data_ptr(), x_d.data_ptr()
+    a.qbuf, a.kbuf, a.vbuf = bufs["q"].data_ptr(), bufs["k"].data_ptr(), bufs["v"].data_ptr()
+    a.k_cache, a.v_cache = kc.data_ptr(), vc.data_ptr()
+    a.attn_out, a.o_out = bufs["a"].data_ptr(), bufs["o"].data_ptr()
+    a.d_model, a.q_dim, a.kv_dim, a.head_dim = sh.d_model, sh.q_dim, sh.kv_dim, sh.head_dim
+    a.num_heads, a.num_kv_heads, a.attn_ctx = sh.num_heads, sh.num_kv_heads, sh.attn_ctx
+    a.attn_scale = 1.0 / math.sqrt(sh.head_dim)
+    ctx.attention_prefill(a, n, dpos)
+    ctx.synchronize()
+    for i in range(n):
+        o_ref, q_ref, k_ref = ref.attention(0, normed[i], pos0 + i)
+        slot = (pos0 + i) % sh.attn_ctx
+        assert rel_err(bufs["o"][i].cpu().numpy(), o_ref) < KERNEL_TOL
+        assert rel_err(bufs["q"][i].cpu().numpy(), q_ref.reshape(-1)) < KERNEL_TOL
+        assert rel_err(kc[slot].cpu().numpy(), k_ref.reshape(-1)) < KERNEL_TOL
+        assert rel_err(vc[slot].cpu().numpy(), ref.kv[0, 1, slot]) < KERNEL_TOL
