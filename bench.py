@@ -383,6 +383,13 @@ def run_ours(args, rank, world, local):
         del g1, d1, k1
         ctx1.close()
 
+    b32 = None
+    if ep:
+        try:
+            b32 = config3_b32_ep_leg(ctx, stream, rank, world, args)
+        except Exception as ex:  # noqa: BLE001  (the headline line stays intact)
+            b32 = {"error": f"{type(ex).__name__}: {ex}"[:300]}
+
     if rank == 0:
         peak, peak_kind = peaks()
         traffic = profile_traffic()
@@ -417,6 +424,8 @@ def run_ours(args, rank, world, local):
             "gpu_launches": int(steps),
             "clocks": ck,
         }
+        if b32:
+            line["config3_b32_ep"] = b32
         if single:
             line["single_gpu_same_layer"] = single
         if world == 1 and not args.no_cpu:
@@ -445,6 +454,79 @@ def run_ours(args, rank, world, local):
                     torch.cuda.empty_cache()
         print(json.dumps(line), flush=True)
     ctx.close()
+
+
+def config3_b32_ep_leg(ctx, stream, rank, world, args, B=32, nl=4, steps=20):
+    """BASELINE config 3's batched case at N > 1: the 235B layer for 32
+    tokens, experts sharded over the ranks (vault layout, expert-grouped path
+    on each rank's slots, smoe_cuda_moe_layer_shard) and the partial sums
+    combined by an NCCL reduce to rank 0; nl layers cycled. Max over ranks of
+    the device time; rank 0 also times the whole layer on its own GPU."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import oracle as O
+    import smoe_cuda as S
+    sh = SHAPES["235b"]
+    d, E, K, dff = sh["d"], sh["E"], sh["k"], sh["dff"]
+    import datetime
+    nccl = dist.new_group(backend="nccl", timeout=datetime.timedelta(seconds=120))   # a lost rank ends it
+    base, per = S.ep_partition(E, world, rank)
+    router = torch.from_numpy(O.normal_bf16(4242, 6, E * d, 0.0, 0.02).view(np.int16)).cuda()
+    shards, keep = [], []
+    for l in range(nl):
+        arena, stride, off = O.make_experts(O.FMT_AFFINE_Q4, per, d, dff, 5000 + l, first=base)
+        da = torch.from_numpy(arena).cuda()
+        keep.append(da)
+        shards.append(S.make_layer(da, stride, off, per, d, dff, O.FMT_AFFINE_Q4, router))
+    xs = torch.from_numpy(np.stack([O.normal_bf16(77 + i, 5, B * d) for i in range(4)]).view(np.int16)).cuda()
+    y = torch.zeros(B, d, dtype=torch.float32, device="cuda")
+    ids = torch.zeros(B, K, dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+
+    def step(i):
+        ctx.moe_layer_shard(shards[i % nl], E, base, xs[i % 4], S.DTYPE_BF16, B, K, True, y, ids)
+        dist.reduce(y, dst=0, group=nccl)
+
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, 3)):
+            step(i)
+        torch.cuda.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(steps):
+            step(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    touched = int((np.bincount(ids.cpu().numpy().reshape(-1), minlength=E) > 0).sum())
+    out = {"workload": f"config3 batched: Qwen3-235B-A22B MoE layer, batch {B}, experts over {world} GPUs "
+                       "(expert-grouped path per rank) + NCCL reduce to rank 0", "steps": steps,
+           "layer_us": round(ms / steps * 1e3, 2), "tokens_per_s_per_layer": round(B * steps / (ms * 1e-3)),
+           "experts_touched": touched}
+    if rank == 0:                               # the same layer on this GPU alone
+        full = []
+        for l in range(nl):
+            arena, stride, off = O.make_experts(O.FMT_AFFINE_Q4, E, d, dff, 5000 + l)
+            da = torch.from_numpy(arena).cuda()
+            keep.append(da)
+            full.append(S.make_layer(da, stride, off, E, d, dff, O.FMT_AFFINE_Q4, router))
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            for i in range(3):
+                ctx.moe_layer(full[i % nl], xs[i % 4], S.DTYPE_BF16, B, K, True, y, S.DTYPE_F32)
+            torch.cuda.synchronize()
+            e0.record(stream)
+            for i in range(steps):
+                ctx.moe_layer(full[i % nl], xs[i % 4], S.DTYPE_BF16, B, K, True, y, S.DTYPE_F32)
+            e1.record(stream)
+            torch.cuda.synchronize()
+        out["single_gpu_layer_us"] = round(e0.elapsed_time(e1) / steps * 1e3, 2)
+    barrier(world)
+    del keep
+    torch.cuda.empty_cache()
+    return out
 
 
 def config3_leg(ctx, stream, args):

@@ -239,6 +239,22 @@ int smoe_cuda_vault_upload_layer(SmoeCudaCtx* ctx, const void* vault, uint64_t s
                                  SmoeMoeLayer* out);
 const char* smoe_cuda_vault_last_error(void);
 
+/* Expert parallel for token batches (BASELINE config 3 at batch 32: the
+ * 235B layer's experts sharded over the GPUs, combined with NCCL). Every
+ * rank passes the same x and routes it over the whole router
+ * (shard->router_w: [n_experts_total x d_model]); shard holds experts
+ * [expert_base, expert_base + shard->n_experts) in the vault layout; the
+ * expert-grouped FFN runs only this rank's slots and y_partial [batch x
+ * d_model] fp32 receives their weighted sum in rank order (zero rows where
+ * no local expert was chosen). The layer output is the sum of the ranks'
+ * partials (an NCCL reduce or all-reduce of y_partial by the caller; sum
+ * order across ranks differs from the one-GPU rank order, ~1e-7
+ * relative). ids_out / w_out (optional, device): the routing. */
+int smoe_cuda_moe_layer_shard(SmoeCudaCtx* ctx, const SmoeMoeLayer* shard, uint32_t n_experts_total,
+                              uint32_t expert_base, const void* x, int x_dtype, uint32_t batch,
+                              uint32_t k, int norm, float* y_partial, uint32_t* ids_out,
+                              float* w_out);
+
 /* Router of decode.cpp:280-303 for `batch` tokens: logits = W . x (bf16 W,
  * fp32 accumulate), softmax over n_experts, top-k by probability (lowest
  * index wins ties), renormalised over the k when norm_topk. Outputs (device):

@@ -43,8 +43,11 @@ struct GroupedArgs {
 // over the slots in order (deterministic); ids are read 16 per lane, one
 // 512-slot round ahead of the ballots, so the scan is not a chain of loads.
 // Also clears the lo flag that the following k_build_tabs of x sets.
+// Expert-parallel shard (base > 0 or e_total > gridDim.x): the lists hold
+// the slots of experts [base, base + gridDim.x); other slots belong to
+// other ranks and are left out; ids >= e_total are errors.
 __global__ void k_group_slots(const uint32_t* ids, uint32_t nslots, uint32_t* list, uint32_t* count,
-                              uint32_t lcap, uint32_t* lo_flag, uint32_t* err) {
+                              uint32_t lcap, uint32_t* lo_flag, uint32_t* err, uint32_t base, uint32_t e_total) {
     const uint32_t e = blockIdx.x, lane = threadIdx.x;
     if (e == 0 && lane == 0 && lo_flag) *lo_flag = 0u;
     uint32_t n = 0;
@@ -65,8 +68,8 @@ __global__ void k_group_slots(const uint32_t* ids, uint32_t nslots, uint32_t* li
 #pragma unroll
         for (int q = 0; q < 16; ++q) {
             const uint32_t s = b0 + q * 32 + lane;
-            const bool mine = v[q] == e;
-            if (e == 0 && s < nslots && v[q] >= gridDim.x)   // an id past the layer's experts: no list takes it
+            const bool mine = v[q] - base == e;             // (unsigned: ids below base wrap past the shard)
+            if (e == 0 && s < nslots && v[q] >= e_total)      // an id past the layer's experts: no list takes it
                 atomicCAS(err, 0u, uint32_t(SMOE_DEVERR_BAD_EXPERT));
             const uint32_t m = __ballot_sync(0xffffffffu, mine);
             const uint32_t pos = n + __popc(m & ((1u << lane) - 1u));
@@ -618,13 +621,18 @@ __global__ void __launch_bounds__(256, 2) k_ffn_down_tc(GroupedArgs a) {
 
 // y[t] = sum_j w[t*k+j] * ys[t*k+j] in rank order j (axpy_f32: product, then
 // sum). grid (ceil(d/256), ntok).
+// ids (shard mode, else null): only slots of experts [base, base + e_local)
+// are added (this rank's partial sum; the ranks' partials are summed by the
+// caller's reduction).
 __global__ void k_combine_slots(const float* ys, const float* wts, uint32_t k, uint32_t d, void* y,
-                                int y_dtype) {
+                                int y_dtype, const uint32_t* ids, uint32_t base, uint32_t e_local) {
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x, t = blockIdx.y;
     if (i >= d) return;
     float acc = 0.f;
-    for (uint32_t j = 0; j < k; ++j)
+    for (uint32_t j = 0; j < k; ++j) {
+        if (ids && ids[t * k + j] - base >= e_local) continue;
         acc = __fadd_rn(acc, __fmul_rn(wts[t * k + j], ys[size_t(t * k + j) * d + i]));
+    }
     if (y_dtype == 0) static_cast<float*>(y)[size_t(t) * d + i] = acc;
     else static_cast<__nv_bfloat16*>(y)[size_t(t) * d + i] = __float2bfloat16_rn(acc);
 }

@@ -183,7 +183,11 @@ int check_ffn_dims(SmoeCudaCtx* c, uint32_t d, uint32_t dff) {
 // Launch gate_up then down/combine for a prepared FfnArgs.
 // Token batches (> 4 tokens) on the vault layout: the expert-grouped path,
 // each expert's weights read once per layer whatever its token count.
-int launch_grouped(SmoeCudaCtx* c, smoe::FfnArgs& a, int fmt, uint32_t E) {
+// base / e_total: an expert-parallel shard holds experts [base, base + E) of
+// e_total (0: the whole layer); its y is the partial sum over its experts.
+int launch_grouped(SmoeCudaCtx* c, smoe::FfnArgs& a, int fmt, uint32_t E, uint32_t base = 0, uint32_t e_total = 0) {
+    const bool shard = e_total != 0;
+    if (!shard) e_total = E;
     const uint32_t nslots = a.ntok * a.k, lcap = c->cfg.max_batch * 16u;
     if (nslots == 0) return SMOE_OK;
     if (nslots > lcap || E > c->cfg.max_experts || !a.ids) {
@@ -197,7 +201,8 @@ int launch_grouped(SmoeCudaCtx* c, smoe::FfnArgs& a, int fmt, uint32_t E) {
     int rc;
     uint32_t* lo_flag = c->g_count + c->cfg.max_experts;
     using namespace smoe;
-    smoe::k_group_slots<<<E, 32, 0, c->stream>>>(a.ids, nslots, c->g_list, c->g_count, lcap, lo_flag, c->err);
+    smoe::k_group_slots<<<E, 32, 0, c->stream>>>(a.ids, nslots, c->g_list, c->g_count, lcap, lo_flag, c->err,
+                                                 base, e_total);
     if ((rc = prep_kernel(c, k_build_tabs<kTabMma>, size_t(d / 4) * 8))) return rc;
     if ((rc = prep_kernel(c, k_build_tabs<kTabTc>, size_t(dff / 4) * 8))) return rc;
     k_build_tabs<kTabMma><<<a.ntok, 256, size_t(d / 4) * 8, c->stream>>>(a.x, a.x_dtype == 1, d, c->g_xtab, c->g_xgs,
@@ -235,7 +240,8 @@ int launch_grouped(SmoeCudaCtx* c, smoe::FfnArgs& a, int fmt, uint32_t E) {
                   : run(k_ffn_grouped<kFmtSmoe, 2, kRbGu, kWnGu, 0>, k_ffn_down_tc<kFmtSmoe>);
     if (rc) return rc;
     smoe::k_combine_slots<<<dim3((d + 255) / 256, a.ntok), 256, 0, c->stream>>>(c->g_ys, a.wts, a.k, d, a.y,
-                                                                               a.y_dtype);
+                                                                               a.y_dtype, shard ? a.ids : nullptr,
+                                                                               base, E);
     CK(cudaGetLastError());
     c->dispatches += 6;
     return SMOE_OK;
@@ -900,6 +906,40 @@ int smoe_cuda_moe_ffn(SmoeCudaCtx* c, const SmoeMoeLayer* L, const void* x, int 
     if (batch > uint32_t(smoe::kLMaxTok) && L->d_model % 128 == 0 && L->d_ff % 256 == 0 && L->d_ff <= 4096)
         return launch_grouped(c, a, fmt, L->n_experts);
     return launch_ffn(c, a, fmt);
+}
+
+int smoe_cuda_moe_layer_shard(SmoeCudaCtx* c, const SmoeMoeLayer* shard, uint32_t n_experts_total,
+                              uint32_t expert_base, const void* x, int x_dtype, uint32_t batch, uint32_t k,
+                              int norm, float* y_partial, uint32_t* ids_out, float* w_out) {
+    if (!c || !shard || !x || !y_partial) { set_err("null argument %s%ld", "", 0); return SMOE_ERR_ARG; }
+    smoe::FfnArgs a{};
+    int rc = layer_args(c, shard, a);
+    if (rc) return rc;
+    if ((shard->fmt & SMOE_LAYOUT_TILED) || !shard->router_w || shard->n_experts == 0 ||
+        expert_base + shard->n_experts > n_experts_total || k == 0 || k > SMOE_MAX_ACTIVE || batch == 0 ||
+        batch > c->cfg.max_batch || (x_dtype != 0 && x_dtype != 1) || shard->d_model % 128 ||
+        shard->d_ff % 256 || shard->d_ff > 4096) {
+        set_err("bad layer shard (vault layout, d_model %% 128, d_ff %% 256, experts within the layer) %s%ld", "",
+                (long)expert_base);
+        return SMOE_ERR_ARG;
+    }
+    uint32_t* ids = ids_out ? ids_out : c->ids;
+    float* wts = w_out ? w_out : c->wts;
+    // every rank routes over the whole router (identical ids on every rank)
+    if ((rc = smoe_cuda_router_topk(c, shard->router_w, x, x_dtype, n_experts_total, shard->d_model, batch, k, norm,
+                                    ids, wts, nullptr)))
+        return rc;
+    a.ids = ids;
+    a.wts = wts;
+    a.x = x;
+    a.x_dtype = x_dtype;
+    a.y = y_partial;
+    a.y_dtype = 0;
+    a.per_slot = 0;
+    a.k = k;
+    a.ntok = batch;
+    a.n_experts = n_experts_total;
+    return launch_grouped(c, a, int(shard->fmt), shard->n_experts, expert_base, n_experts_total);
 }
 
 int smoe_cuda_moe_layer(SmoeCudaCtx* c, const SmoeMoeLayer* L, const void* x, int x_dtype,

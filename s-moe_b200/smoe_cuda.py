@@ -43,6 +43,7 @@ EXPORTS = [
     "smoe_cuda_gemm_bf16", "smoe_cuda_attention_batch_async", "smoe_cuda_decode_advance_batch",
     "smoe_cuda_rope_tables", "smoe_cuda_attention_prefill_async",
     "smoe_cuda_vault_parse", "smoe_cuda_vault_expert", "smoe_cuda_vault_upload_layer", "smoe_cuda_vault_last_error",
+    "smoe_cuda_moe_layer_shard",
 ]
 
 
@@ -196,6 +197,8 @@ def lib():
         L.smoe_cuda_ep_attach.argtypes = [vp, i32, i32, C.POINTER(EpHandle)]
         L.smoe_cuda_moe_layer_ep.argtypes = [vp, C.POINTER(MoeLayer), u32, u32, vp, i32, u32, u32, i32,
                                              vp, i32, vp, vp]
+        L.smoe_cuda_moe_layer_shard.argtypes = [vp, C.POINTER(MoeLayer), u32, u32, vp, i32, u32, u32, i32, vp,
+                                                vp, vp]
         L.smoe_cuda_moe_ffn_noalloc.argtypes = [C.POINTER(MoeLayer), vp, i32, vp, vp, u32, u32, vp,
                                                 i32, vp]
         L.smoe_cuda_noalloc_last_error.restype = C.c_char_p
@@ -333,6 +336,12 @@ class Context:
         for r, b in enumerate(handles):
             C.memmove(arr[r].bytes, bytes(b), 64)
         check(self.L.smoe_cuda_ep_attach(self.h, rank, world, arr), "ep_attach")
+
+    def moe_layer_shard(self, shard: MoeLayer, n_experts_total, expert_base, x, x_dtype, batch, k, norm, y_partial,
+                        ids=None, w=None):
+        check(self.L.smoe_cuda_moe_layer_shard(self.h, C.byref(shard), n_experts_total, expert_base, ptr(x), x_dtype,
+                                               batch, k, int(norm), ptr(y_partial), ptr(ids), ptr(w)),
+              "moe_layer_shard")
 
     def moe_layer_ep(self, shard: MoeLayer, n_experts_total, expert_base, x, x_dtype, batch, k, norm,
                      y, y_dtype, ids=None, weights=None):

@@ -195,3 +195,38 @@ def test_attention_prefill_chunk(ctx, heads, ctx_len, pos0, n):
         assert rel_err(bufs["q"][i].cpu().numpy(), q_ref.reshape(-1)) < KERNEL_TOL
         assert rel_err(kc[slot].cpu().numpy(), k_ref.reshape(-1)) < KERNEL_TOL
         assert rel_err(vc[slot].cpu().numpy(), ref.kv[0, 1, slot]) < KERNEL_TOL
+
+
+@pytest.mark.parametrize("G,fmt", [(2, O.FMT_AFFINE_Q4), (4, O.FMT_SMOE_Q4)])
+def test_moe_layer_shards_sum_to_layer(ctx, G, fmt):
+    """smoe_cuda_moe_layer_shard on one GPU, once per shard of a 235B-shaped
+    layer (16 experts split over G shards), batch 32: the shards' partial
+    sums add up to the layer (what the ranks' NCCL reduce computes), routing
+    identical in every shard; against the oracle."""
+    B, E, d, dff, k = 32, 16, 4096, 1536, 8
+    arena, stride, off = O.make_experts(fmt, E, d, dff, 181)
+    router = O.normal_bf16(181, 6, E * d, 0.0, 0.02)
+    drouter = dev(router)
+    X = O.normal_bf16(182, 5, B * d)
+    dx = dev(X)
+    total = np.zeros((B, d), np.float64)
+    per = E // G
+    ids0 = None
+    for g in range(G):
+        da = dev(np.ascontiguousarray(arena[g * per:(g + 1) * per]))
+        shard = S.make_layer(da, stride, off, per, d, dff, fmt, drouter)
+        y = torch.zeros(B, d, dtype=torch.float32, device="cuda")
+        ids = torch.zeros(B, k, dtype=torch.int32, device="cuda")
+        torch.cuda.synchronize()
+        ctx.moe_layer_shard(shard, E, g * per, dx, S.DTYPE_BF16, B, k, True, y, ids)
+        ctx.synchronize()
+        total += y.cpu().numpy()
+        gid = ids.cpu().numpy()
+        if ids0 is None:
+            ids0 = gid
+        assert np.array_equal(gid, ids0)
+    for t in range(0, B, 3):
+        x = O.bf16_to_f32(X[t * d:(t + 1) * d])
+        ref, rids, _ = O.moe_layer(fmt, x, router, arena, stride, E, d, dff, k)
+        assert (ids0[t].view(np.uint32) == rids).all()
+        assert rel_err(total[t], ref) < 1e-4

@@ -1,7 +1,9 @@
 """GPU parity of the expert-parallel layer (smoe_cuda_moe_layer_ep): one
 process per GPU over 2, 4 and 8 GPUs (as many as present), both layer shapes
 (Qwen3-30B-A3B and Qwen3-235B-A22B), exchange inside the layer
-kernel over NVLink, results against the CPU oracle of the whole layer.
+kernel over NVLink, results against the CPU oracle of the whole layer; and
+the 235B layer at batch 32 (BASELINE config 3's batched case) as expert
+shards on the grouped path combined by an NCCL reduce.
 Skipped on a box with a single GPU (ranks that wait on each other never run
 as processes sharing one GPU)."""
 import os
@@ -27,7 +29,8 @@ def _free_port() -> int:
 
 
 @pytest.mark.parametrize("world,fmt,shape", [(2, 1, "30b"), (2, 0, "30b"), (4, 1, "30b"), (8, 1, "30b"),
-                                             (2, 1, "235b"), (4, 1, "235b"), (8, 1, "235b")])
+                                             (2, 1, "235b"), (4, 1, "235b"), (8, 1, "235b"),
+                                             (2, 1, "235b-b32"), (4, 0, "235b-b32"), (8, 1, "235b-b32")])
 def test_moe_layer_expert_parallel(world, fmt, shape):
     if _gpus() < world:
         pytest.skip(f"needs {world} GPUs")
