@@ -521,7 +521,19 @@ def per_token_bytes(sh: Shape) -> int:
                          + sh.n_experts * sh.d_model * 2) + sh.vocab * sh.d_model * 2)
 
 
-def run_batched(ctx, sh: Shape, batch: int, prompt: int, gen: int, seed: int = 11) -> dict:
+def profile_steps(dec, n: int = 1) -> None:
+    """n step-graph replays between cudaProfilerStart / Stop, for
+    `ncu --profile-from-start off` (the graph's kernels one by one)."""
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    with torch.cuda.stream(dec.stream):
+        for _ in range(n):
+            dec.graph.replay()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+
+
+def run_batched(ctx, sh: Shape, batch: int, prompt: int, gen: int, seed: int = 11, profile: bool = False) -> dict:
     t0 = time.time()
     model = Model(ctx, sh, layout="vault")
     t_load = time.time() - t0
@@ -534,6 +546,8 @@ def run_batched(ctx, sh: Shape, batch: int, prompt: int, gen: int, seed: int = 1
     dec.reset()
     toks, t = dec.run(prompts, gen)
     ctx.synchronize()
+    if profile:
+        profile_steps(dec)
     out = {"batch": batch, "tok_per_s": round(batch * gen / t, 1), "ms_per_step": round(1e3 * t / gen, 3),
            "load_s": round(t_load, 1), "first_tokens_seq0": toks[:8, 0].tolist()}
     del dec, model
@@ -549,6 +563,9 @@ def main():
     ap.add_argument("--ctx", type=int, default=4096, help="KV ring positions per sequence")
     ap.add_argument("--prompt", type=int, default=45)
     ap.add_argument("--gen", type=int, default=256)
+    ap.add_argument("--profile", action="store_true",
+                    help="after the timed run, one more step between cudaProfilerStart/Stop (ncu "
+                         "--profile-from-start off)")
     args = ap.parse_args()
     sh = Shape.qwen3_235b() if args.shape == "235b" else Shape()
     if args.layers:
@@ -557,7 +574,7 @@ def main():
     name = "Qwen3-235B-A22B" if args.shape == "235b" else "Qwen3-30B-A3B"
     ctx = S.Context(0)
     if args.batch > 1:
-        out = run_batched(ctx, sh, args.batch, args.prompt, args.gen)
+        out = run_batched(ctx, sh, args.batch, args.prompt, args.gen, profile=args.profile)
         out["workload"] = (f"{name}-shaped decode, {sh.layers} layers, batch {args.batch}, prompt {args.prompt}, "
                            f"{args.gen} generated per sequence (random weights)")
         print(json.dumps(out))
@@ -574,6 +591,8 @@ def main():
     dec.reset()
     toks, t = dec.run(prompt, args.gen)
     ctx.synchronize()
+    if args.profile:
+        profile_steps(dec)
     ptb = per_token_bytes(sh)
     print(json.dumps({"workload": f"{name}-shaped decode, {sh.layers} layers, batch 1, prompt "
                                   f"{args.prompt}, {args.gen} generated (random weights)",
