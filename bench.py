@@ -505,9 +505,9 @@ def config3_b32_ep_leg(ctx, stream, rank, world, args, B=32, nl=4, steps=20):
                        "(expert-grouped path per rank) + NCCL reduce to rank 0", "steps": steps,
            "layer_us": round(ms / steps * 1e3, 2), "tokens_per_s_per_layer": round(B * steps / (ms * 1e-3)),
            "experts_touched": touched}
-    if rank == 0:                               # the same layer on this GPU alone
-        full = []
-        for l in range(nl):
+    if rank == 0:                               # the same layer on this GPU alone (2 layers cycled,
+        full = []                               # 2.7 GB: beyond L2 all the same)
+        for l in range(2):
             arena, stride, off = O.make_experts(O.FMT_AFFINE_Q4, E, d, dff, 5000 + l)
             da = torch.from_numpy(arena).cuda()
             keep.append(da)
@@ -515,11 +515,11 @@ def config3_b32_ep_leg(ctx, stream, rank, world, args, B=32, nl=4, steps=20):
         torch.cuda.synchronize()
         with torch.cuda.stream(stream):
             for i in range(3):
-                ctx.moe_layer(full[i % nl], xs[i % 4], S.DTYPE_BF16, B, K, True, y, S.DTYPE_F32)
+                ctx.moe_layer(full[i % 2], xs[i % 4], S.DTYPE_BF16, B, K, True, y, S.DTYPE_F32)
             torch.cuda.synchronize()
             e0.record(stream)
             for i in range(steps):
-                ctx.moe_layer(full[i % nl], xs[i % 4], S.DTYPE_BF16, B, K, True, y, S.DTYPE_F32)
+                ctx.moe_layer(full[i % 2], xs[i % 4], S.DTYPE_BF16, B, K, True, y, S.DTYPE_F32)
             e1.record(stream)
             torch.cuda.synchronize()
         out["single_gpu_layer_us"] = round(e0.elapsed_time(e1) / steps * 1e3, 2)
