@@ -52,6 +52,15 @@ SMOE_DEVINL void samp_mark(unsigned long long* tr, int i) {
     }
 }
 
+// the same mark from a given thread (the workers' first thread)
+SMOE_DEVINL void samp_mark_w(unsigned long long* tr, int i) {
+    if (tr && blockIdx.y == 0) {
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        tr[blockIdx.x * 8 + i] = t;
+    }
+}
+
 constexpr int kSampCluster = 8;
 constexpr int kSampThreads = 1024;
 constexpr int kSampCand = 1024;
@@ -145,6 +154,72 @@ SMOE_DEVINL uint32_t block_exscan(uint32_t v, uint32_t* red, uint32_t* total) {
     return base + inc - v;
 }
 
+// ---- worker synchronisation while warp 0 of CTA 0 walks the exact sum:
+// the other warps of CTA 0 and every warp of the other CTAs ("workers")
+// synchronise among themselves only.
+// Within a CTA: named barrier 1 over its workers (992 or 1024 threads).
+SMOE_DEVINL void worker_bar(int nwork) {
+    asm volatile("bar.sync 1, %0;" :: "r"(nwork) : "memory");
+}
+// Across the cluster: every CTA's worker 0 arrives (release, cluster scope)
+// on the same mbarrier of all 8 CTAs, then every worker waits (acquire) for
+// its own CTA's barrier to complete the phase (8 arrivals). Two barriers
+// used alternately: a CTA can only arrive for sync k + 1 after every CTA
+// has arrived for sync k, so an arrival never lands in an older phase. The
+// wait is bounded (a %globaltimer deadline); running out lets the kernel
+// finish with a wrong token instead of hanging.
+struct WorkerClusterSync {
+    uint64_t* bars;            // [2] mbarriers in this CTA's shared memory, count kSampCluster
+    uint32_t par[2];
+    int use;
+    SMOE_DEVINL void sync(int wtid, int nwork) {
+        asm volatile("fence.acq_rel.cluster;" ::: "memory");
+        worker_bar(nwork);                                   // this CTA's workers are done writing
+        uint64_t* b = bars + use;
+        if (wtid == 0) {
+            const uint32_t a = smem_u32(b);
+#pragma unroll 1
+            for (uint32_t r = 0; r < uint32_t(kSampCluster); ++r)
+                asm volatile("{ .reg .b32 ra; mapa.shared::cluster.u32 ra, %0, %1;\n"
+                             " mbarrier.arrive.release.cluster.shared::cluster.b64 _, [ra]; }"
+                             :: "r"(a), "r"(r) : "memory");
+        }
+        const uint64_t deadline = gtimer() + SMOE_WAIT_NS_DEFAULT;
+#pragma unroll 1
+        for (uint32_t i = 0;; ++i) {
+            uint32_t ok;
+            asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+                         " selp.u32 %0, 1, 0, p; }"
+                         : "=r"(ok) : "r"(smem_u32(b)), "r"(par[use]) : "memory");
+            if (ok || ((i & 15) == 15 && gtimer() > deadline)) break;
+        }
+        par[use] ^= 1u;
+        use ^= 1;
+    }
+};
+
+// exclusive scan of a u32 over the workers of this CTA (nwork threads, worker
+// index wtid); *total = the sum over them
+SMOE_DEVINL uint32_t worker_exscan(uint32_t v, uint32_t* red, uint32_t* total, int wtid, int nwork) {
+    const int lane = wtid & 31, ww = wtid >> 5, nww = nwork >> 5;
+    uint32_t inc = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t t = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += t;
+    }
+    worker_bar(nwork);
+    if (lane == 31) red[ww] = inc;
+    worker_bar(nwork);
+    uint32_t base = 0, tot = 0;
+    for (int i = 0; i < nww; ++i) {
+        if (i < ww) base += red[i];
+        tot += red[i];
+    }
+    *total = tot;
+    return base + inc - v;
+}
+
 struct SampPub {            // per-CTA values read by the cluster
     float fval;
     uint32_t uidx;
@@ -164,6 +239,7 @@ k_sample(SamplerArgs a) {
     __shared__ SampPub pub;
     __shared__ SeqShared seqsh;
     __shared__ uint32_t sel_prefix, sel_krem;
+    __shared__ uint64_t wbars[2];
 
     cg::cluster_group cl = cg::this_cluster();
     const int rank = (int)cl.block_rank();
@@ -180,6 +256,11 @@ k_sample(SamplerArgs a) {
     float* lg = a.logits + size_t(row) * V;
 
     samp_mark(a.trace, 0);
+    if (tid == 0) {
+        mbar_init(&wbars[0], kSampCluster);
+        mbar_init(&wbars[1], kSampCluster);
+        fence_mbar_init();             // visible cluster-wide by the first cluster barrier below
+    }
     for (uint32_t i = tid; i < n; i += kSampThreads) s[i] = lg[lo + i];
     __syncthreads();
     samp_mark(a.trace, 1);
@@ -269,136 +350,152 @@ k_sample(SamplerArgs a) {
     }
     __syncthreads();
     samp_mark(a.trace, 2);
-    seq_sum_cluster(cl, s, n, L, V, C, &seqsh, a.trace);
-    samp_mark(a.trace, 3);
+    seq_summarise_cluster(cl, s, n, L, V, C, &seqsh, a.trace);
 
-    // ---- 4. radix select of the K-th largest score key
+    // From here warp 0 of CTA 0 walks the exact sum (43 us of serial work)
+    // while the other warps - the workers - select, collect and sort the
+    // top-K candidates; they meet again at the cluster barrier before the
+    // draw. The walker reads every CTA's e values and summaries remotely, so
+    // every CTA stays resident until that barrier.
     uint32_t K = P.top_k < 1u ? 1u : P.top_k;
     if (K > (uint32_t)kSampCand) K = kSampCand;
     if (K > V) K = V;
-    uint32_t prefix = 0, mask = 0, krem = K;
-    for (int pass = 0; pass < 4; ++pass) {
-        const int shift = 24 - 8 * pass;
-        uint32_t* hh = hist[pass & 1];
-        uint32_t* wh = whist[tid >> 5];
-        for (int b = tid & 31; b < 256; b += 32) wh[b] = 0;
-        __syncwarp();
-        for (uint32_t i = tid; i < n; i += kSampThreads) {
-            const uint32_t key = score_key(s[i]);
-            if ((key & mask) == prefix) atomicAdd(&wh[(key >> shift) & 255u], 1u);
-        }
-        __syncthreads();
-        if (tid < 256) {
-            uint32_t t = 0;
-            for (int w = 0; w < kSampThreads / 32; ++w) t += whist[w][tid];
-            hh[tid] = t;
-        }
-        cl.sync();
-        if (tid < 256) {
-            uint32_t t = 0;
-            for (int r = 0; r < kSampCluster; ++r) t += cl.map_shared_rank(hh, r)[tid];
-            tot[tid] = t;
-        }
-        __syncthreads();
-        if (tid < 32) {
-            // the highest bin b >= 1 whose count from bin 255 down reaches krem,
-            // else bin 0; cum = count above b. Lane l scans bins 255 - 8l ..
-            // 248 - 8l; the lane holding the answer walks its 8 bins.
-            const int lane = tid;
-            uint32_t v[8], sl = 0;
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                v[q] = tot[255 - 8 * lane - q];
-                sl += v[q];
+    if (rank == 0 && (tid >> 5) == 0) {
+        seq_walk(cl, s, L, V, C, &seqsh, a.trace);
+    } else {
+        const int wtid = rank == 0 ? tid - 32 : tid, nwork = rank == 0 ? kSampThreads - 32 : kSampThreads;
+        const int w0 = rank == 0 ? 1 : 0;                 // first worker warp of this CTA
+        WorkerClusterSync csync{wbars, {0u, 0u}, 0};
+        // ---- 4. radix select of the K-th largest score key
+        uint32_t prefix = 0, mask = 0, krem = K;
+        for (int pass = 0; pass < 4; ++pass) {
+            const int shift = 24 - 8 * pass;
+            uint32_t* hh = hist[pass & 1];
+            uint32_t* wh = whist[tid >> 5];
+            for (int b = tid & 31; b < 256; b += 32) wh[b] = 0;
+            __syncwarp();
+            for (uint32_t i = wtid; i < n; i += nwork) {
+                const uint32_t key = score_key(s[i]);
+                if ((key & mask) == prefix) atomicAdd(&wh[(key >> shift) & 255u], 1u);
             }
-            uint32_t incl = sl;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o) incl += y;
+            worker_bar(nwork);
+            if (wtid < 256) {
+                uint32_t t = 0;
+                for (int w = w0; w < kSampThreads / 32; ++w) t += whist[w][wtid];
+                hh[wtid] = t;
             }
-            const unsigned m = __ballot_sync(0xffffffffu, incl >= krem);
-            const int owner = m ? __ffs(m) - 1 : 31;
-            if (lane == owner) {
-                uint32_t cum = incl - sl;
-                int b = 0;
+            csync.sync(wtid, nwork);
+            if (wtid < 256) {
+                uint32_t t = 0;
+                for (int r = 0; r < kSampCluster; ++r) t += cl.map_shared_rank(hh, r)[wtid];
+                tot[wtid] = t;
+            }
+            worker_bar(nwork);
+            if (wtid < 32) {
+                // the highest bin b >= 1 whose count from bin 255 down reaches krem,
+                // else bin 0; cum = count above b. Lane l scans bins 255 - 8l ..
+                // 248 - 8l; the lane holding the answer walks its 8 bins.
+                const int lane = wtid;
+                uint32_t v[8], sl = 0;
 #pragma unroll
                 for (int q = 0; q < 8; ++q) {
-                    const int bin = 255 - 8 * lane - q;
-                    if (bin == 0) break;
-                    if (cum + v[q] >= krem) { b = bin; break; }
-                    cum += v[q];
+                    v[q] = tot[255 - 8 * lane - q];
+                    sl += v[q];
                 }
-                sel_krem = krem - cum;
-                sel_prefix = prefix | (uint32_t(b) << shift);
+                uint32_t incl = sl;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (lane >= o) incl += y;
+                }
+                const unsigned m = __ballot_sync(0xffffffffu, incl >= krem);
+                const int owner = m ? __ffs(m) - 1 : 31;
+                if (lane == owner) {
+                    uint32_t cum = incl - sl;
+                    int b = 0;
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        const int bin = 255 - 8 * lane - q;
+                        if (bin == 0) break;
+                        if (cum + v[q] >= krem) { b = bin; break; }
+                        cum += v[q];
+                    }
+                    sel_krem = krem - cum;
+                    sel_prefix = prefix | (uint32_t(b) << shift);
+                }
             }
+            worker_bar(nwork);
+            krem = sel_krem;
+            prefix = sel_prefix;
+            mask |= 255u << shift;
+            // (hist[pass & 1] is next written two passes later, after a
+            // cluster barrier that follows every CTA's reads of it)
         }
-        __syncthreads();
-        krem = sel_krem;
-        prefix = sel_prefix;
-        mask |= 255u << shift;
-    }
-    const uint32_t thr = prefix;   // key of the K-th largest; krem ties to take
-    samp_mark(a.trace, 4);
+        const uint32_t thr = prefix;   // key of the K-th largest; krem ties to take
+        if (wtid == 0) samp_mark_w(a.trace, 4);
 
-    // ---- collect candidates into CTA 0 (contiguous chunk per thread keeps
-    // the tie order = index order)
-    const uint32_t chunk = (n + kSampThreads - 1) / kSampThreads;
-    const uint32_t b0 = min(n, tid * chunk), b1 = min(n, b0 + chunk);
-    uint32_t ngt = 0, neq = 0;
-    for (uint32_t i = b0; i < b1; ++i) {
-        const uint32_t key = score_key(s[i]);
-        ngt += key > thr;
-        neq += key == thr;
-    }
-    uint32_t cta_gt, cta_eq;
-    const uint32_t off_gt = block_exscan(ngt, redu, &cta_gt);
-    const uint32_t off_eq = block_exscan(neq, redu, &cta_eq);
-    if (tid == 0) { pub.n_gt = cta_gt; pub.n_eq = cta_eq; }
-    cl.sync();
-    uint32_t all_gt = 0, gt_before = 0, eq_before = 0;
-    for (int r = 0; r < kSampCluster; ++r) {
-        const SampPub* o = cl.map_shared_rank(&pub, r);
-        all_gt += o->n_gt;
-        if (r < rank) { gt_before += o->n_gt; eq_before += o->n_eq; }
-    }
-    unsigned long long* cand0 = cl.map_shared_rank(cand, 0);
-    {
-        uint32_t pg = gt_before + off_gt, pe = eq_before + off_eq;
+        // ---- collect candidates into CTA 0 (contiguous chunk per worker keeps
+        // the tie order = index order)
+        const uint32_t chunk = (n + nwork - 1) / nwork;
+        const uint32_t b0 = min(n, wtid * chunk), b1 = min(n, b0 + chunk);
+        uint32_t ngt = 0, neq = 0;
         for (uint32_t i = b0; i < b1; ++i) {
             const uint32_t key = score_key(s[i]);
-            const unsigned long long packed =
-                (static_cast<unsigned long long>(key) << 32) | (~(lo + i) & 0xffffffffu);
-            if (key > thr) cand0[pg++] = packed;
-            else if (key == thr) {
-                if (pe < krem) cand0[all_gt + pe] = packed;
-                ++pe;
-            }
+            ngt += key > thr;
+            neq += key == thr;
         }
-    }
-    cl.sync();
-    samp_mark(a.trace, 5);
-    if (rank != 0) return;       // CTA 0's shared memory is no longer read remotely
-
-    // ---- 5. sort (score desc, index asc) and walk
-    uint32_t N2 = 1;
-    while (N2 < K) N2 <<= 1;
-    for (uint32_t i = K + tid; i < N2; i += kSampThreads) cand[i] = 0ull;
-    __syncthreads();
-    for (uint32_t size = 2; size <= N2; size <<= 1) {
-        for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
-            for (uint32_t i = tid; i < N2; i += kSampThreads) {
-                const uint32_t j = i ^ stride;
-                if (j > i) {
-                    const bool desc = (i & size) == 0;
-                    const unsigned long long x = cand[i], y = cand[j];
-                    if (desc ? (x < y) : (x > y)) { cand[i] = y; cand[j] = x; }
+        uint32_t cta_gt, cta_eq;
+        const uint32_t off_gt = worker_exscan(ngt, redu, &cta_gt, wtid, nwork);
+        const uint32_t off_eq = worker_exscan(neq, redu, &cta_eq, wtid, nwork);
+        if (wtid == 0) { pub.n_gt = cta_gt; pub.n_eq = cta_eq; }
+        csync.sync(wtid, nwork);
+        uint32_t all_gt = 0, gt_before = 0, eq_before = 0;
+        for (int r = 0; r < kSampCluster; ++r) {
+            const SampPub* o = cl.map_shared_rank(&pub, r);
+            all_gt += o->n_gt;
+            if (r < rank) { gt_before += o->n_gt; eq_before += o->n_eq; }
+        }
+        unsigned long long* cand0 = cl.map_shared_rank(cand, 0);
+        {
+            uint32_t pg = gt_before + off_gt, pe = eq_before + off_eq;
+            for (uint32_t i = b0; i < b1; ++i) {
+                const uint32_t key = score_key(s[i]);
+                const unsigned long long packed =
+                    (static_cast<unsigned long long>(key) << 32) | (~(lo + i) & 0xffffffffu);
+                if (key > thr) cand0[pg++] = packed;
+                else if (key == thr) {
+                    if (pe < krem) cand0[all_gt + pe] = packed;
+                    ++pe;
                 }
             }
-            __syncthreads();
+        }
+        csync.sync(wtid, nwork);
+        if (wtid == 0) samp_mark_w(a.trace, 5);
+
+        // ---- 5. sort (score desc, index asc), CTA 0's workers
+        if (rank == 0) {
+            uint32_t N2 = 1;
+            while (N2 < K) N2 <<= 1;
+            for (uint32_t i = K + wtid; i < N2; i += nwork) cand[i] = 0ull;
+            worker_bar(nwork);
+            for (uint32_t size = 2; size <= N2; size <<= 1) {
+                for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
+                    for (uint32_t i = wtid; i < N2; i += nwork) {
+                        const uint32_t j = i ^ stride;
+                        if (j > i) {
+                            const bool desc = (i & size) == 0;
+                            const unsigned long long x = cand[i], y = cand[j];
+                            if (desc ? (x < y) : (x > y)) { cand[i] = y; cand[j] = x; }
+                        }
+                    }
+                    worker_bar(nwork);
+                }
+            }
+            if (wtid == 0) samp_mark_w(a.trace, 6);
         }
     }
-    samp_mark(a.trace, 6);
+    cl.sync();                    // the walk is done and the candidates are sorted
+    if (rank != 0) return;        // no CTA's shared memory is read remotely any more
     const float inv_sum = __fdiv_rn(1.0f, seqsh.result);
     for (uint32_t i = tid; i < K; i += kSampThreads) {
         const float e = key_score(uint32_t(cand[i] >> 32));    // keys are the e values

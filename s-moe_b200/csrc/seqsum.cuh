@@ -68,8 +68,9 @@ struct SeqShared {            // per CTA
 };
 
 // Exact sequential fp32 sum of e[0..V) held in the cluster's shared memory
-// (e: this CTA's slice, n elements, slice length L, C per thread). All
-// threads of all CTAs call it; the result is in CTA 0's ss->result.
+// (e: this CTA's slice, n elements, slice length L, C per thread), part 1:
+// chunk totals, predicted binades and chunk summaries. All threads of all
+// CTAs call it; seq_walk (below) then produces the sum.
 SMOE_DEVINL void seq_mark(unsigned long long* tr, int i) {
     if (tr && threadIdx.x == 0 && blockIdx.y == 0) {
         unsigned long long t;
@@ -78,7 +79,7 @@ SMOE_DEVINL void seq_mark(unsigned long long* tr, int i) {
     }
 }
 
-SMOE_DEVINL void seq_sum_cluster(cooperative_groups::cluster_group& cl, const float* e, uint32_t n,
+SMOE_DEVINL void seq_summarise_cluster(cooperative_groups::cluster_group& cl, const float* e, uint32_t n,
                                  uint32_t L, uint32_t V, uint32_t C, SeqShared* ss,
                                  unsigned long long* tr = nullptr) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, rank = (int)cl.block_rank();
@@ -151,8 +152,17 @@ SMOE_DEVINL void seq_sum_cluster(cooperative_groups::cluster_group& cl, const fl
     }
     cl.sync();
     seq_mark(tr, 2);
-    // 4. CTA 0 warp 0 walks the chunks in order
-    if (rank == 0 && warp == 0) {
+}
+
+// 4. the walk: one warp (warp 0 of CTA 0) goes through the 256 summaries in
+// order, replaying only chunks that straddle a binade or hold a tie; reads
+// the other CTAs' e values and thread increments through distributed shared
+// memory, so they must stay resident (and leave them unchanged) until it
+// returns. The result is in CTA 0's ss->result.
+SMOE_DEVINL void seq_walk(cooperative_groups::cluster_group& cl, const float* e, uint32_t L, uint32_t V, uint32_t C,
+                          SeqShared* ss, unsigned long long* tr = nullptr) {
+    const int lane = threadIdx.x & 31;
+    {
         float s = 0.0f;
         for (int cb = 0; cb < kSeqChunks; cb += 32) {
             const int my_info = ss->sinfo[cb + lane];          // 32 summaries per load
@@ -226,7 +236,6 @@ SMOE_DEVINL void seq_sum_cluster(cooperative_groups::cluster_group& cl, const fl
         if (lane == 0) ss->result = s;
     }
     seq_mark(tr, 3);
-    cl.sync();
 }
 
 }  // namespace smoe
