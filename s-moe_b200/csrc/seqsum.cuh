@@ -164,24 +164,9 @@ SMOE_DEVINL void seq_walk(cooperative_groups::cluster_group& cl, const float* e,
     const int lane = threadIdx.x & 31;
     {
         float s = 0.0f;
-        for (int cb = 0; cb < kSeqChunks; cb += 32) {
-            const int my_info = ss->sinfo[cb + lane];          // 32 summaries per load
-            const long long my_inc = ss->sinc[cb + lane];
-            for (int j = 0; j < 32; ++j) {
-                const int c = cb + j;
-                const int info = __shfl_sync(0xffffffffu, my_info, j);
-                const long long cinc = __shfl_sync(0xffffffffu, my_inc, j);
-                const int ce = info & 0xffff;
-                const uint32_t cf = uint32_t(info) >> 16;
-                const int es = f32_expo(s);
-                if (cf == 0 && es == ce && es != 0) {
-                    const long long v = f32_units(s) + cinc;
-                    if (v < (1ll << 24)) {
-                        s = f32_from(es, v);
-                        continue;
-                    }
-                }
-                // replay: lane l stands for thread l of the chunk's warp
+        // replay of chunk c (predicted binade ce): lane l stands for thread l
+        // of the chunk's warp
+        auto replay = [&](int c, int ce) {
                 const int r = c >> 5, w = c & 31;
                 const SeqShared* sr = cl.map_shared_rank(ss, r);
                 const float* er = cl.map_shared_rank(e, r);
@@ -231,6 +216,41 @@ SMOE_DEVINL void seq_walk(cooperative_groups::cluster_group& cl, const float* e,
                     s = __shfl_sync(0xffffffffu, sv, evl);
                     ls = evl + 1;
                 }
+        };
+        // 32 chunks at a time (lane j: chunk cb + j): while the running sum
+        // stays in its binade, a clean chunk (no flag, predicted binade = the
+        // sum's) adds its increment to the sum's integer units - so the chunks
+        // from j0 up to the first one that is not clean or would carry the
+        // units to 2^24 are added at once through a prefix sum (increments
+        // are >= 0: the units only grow); that chunk is replayed, and the
+        // batch continues after it. The same result as chunk by chunk.
+        for (int cb = 0; cb < kSeqChunks; cb += 32) {
+            const int my_info = ss->sinfo[cb + lane];
+            const long long my_inc = ss->sinc[cb + lane];
+            const int my_ce = my_info & 0xffff;
+            const uint32_t my_cf = uint32_t(my_info) >> 16;
+            int j0 = 0;
+            while (j0 < 32) {
+                const int es = f32_expo(s);
+                const long long su = (es == 0 || es == 255) ? 0 : f32_units(s);
+                const bool act = lane >= j0;
+                long long incl = act ? my_inc : 0;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const long long y = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (lane >= o) incl += y;
+                }
+                const bool good = my_cf == 0 && my_ce == es && es != 0 && es != 255 && su + incl < (1ll << 24);
+                const unsigned bad = __ballot_sync(0xffffffffu, act && !good);
+                if (bad == 0) {
+                    s = f32_from(es, su + __shfl_sync(0xffffffffu, incl, 31));
+                    break;
+                }
+                const int fb = __ffs(bad) - 1;
+                const long long upto = __shfl_sync(0xffffffffu, incl, fb > 0 ? fb - 1 : 0);
+                if (fb > j0) s = f32_from(es, su + upto);
+                replay(cb + fb, __shfl_sync(0xffffffffu, my_ce, fb));
+                j0 = fb + 1;
             }
         }
         if (lane == 0) ss->result = s;
