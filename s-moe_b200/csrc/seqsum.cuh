@@ -182,6 +182,23 @@ SMOE_DEVINL void seq_walk(cooperative_groups::cluster_group& cl, const float* e,
                 int ls = 0;
                 while (ls < 32) {
                     const int ex = f32_expo(s);
+                    if (ex == 0 || ex == 255 || (ex != ce && ex != ce + 1)) {
+                        // no increment applies: the next lane with elements replays them
+                        // one by one (what the general step below does here, without its
+                        // prefix sum)
+                        const unsigned m = __ballot_sync(0xffffffffu, lane >= ls && cnt > 0);
+                        if (m == 0) break;
+                        const int evl = __ffs(m) - 1;
+                        float sv = s;
+                        if (lane == evl) {
+#pragma unroll
+                            for (int q = 0; q < kSeqMaxC; ++q)
+                                if (q < cnt) sv = __fadd_rn(sv, my_e[q]);
+                        }
+                        s = __shfl_sync(0xffffffffu, sv, evl);
+                        ls = evl + 1;
+                        continue;
+                    }
                     long long li = 0;
                     bool ev = false;
                     if (lane >= ls) {
