@@ -444,9 +444,12 @@ k_sample(SamplerArgs a) {
             ngt += key > thr;
             neq += key == thr;
         }
-        uint32_t cta_gt, cta_eq;
-        const uint32_t off_gt = worker_exscan(ngt, redu, &cta_gt, wtid, nwork);
-        const uint32_t off_eq = worker_exscan(neq, redu, &cta_eq, wtid, nwork);
+        // one scan of both counts, packed (each CTA total < 2^16: its slice
+        // holds at most 24,576 entries: vocab <= 8 x 1024 x kSeqMaxC)
+        uint32_t cta_both;
+        const uint32_t off_both = worker_exscan((ngt << 16) | neq, redu, &cta_both, wtid, nwork);
+        const uint32_t off_gt = off_both >> 16, off_eq = off_both & 0xffffu;
+        const uint32_t cta_gt = cta_both >> 16, cta_eq = cta_both & 0xffffu;
         if (wtid == 0) { pub.n_gt = cta_gt; pub.n_eq = cta_eq; }
         csync.sync(wtid, nwork);
         uint32_t all_gt = 0, gt_before = 0, eq_before = 0;
